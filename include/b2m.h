@@ -1,0 +1,238 @@
+/*
+ * b2m.h — C ABI of libb200mm.so, the B200 (sm_100a) backend for the
+ * MatMul-family operators of onnx_runtime_dart.
+ *
+ * The reference runtime executes these operators in pure Dart; its operator
+ * dispatch (OnnxGraphExecutor._dispatch, lib/src/onnx_graph.dart:1549) calls
+ *   MatMul        -> ops.opMatMul             lib/src/onnx_ops.dart:1710
+ *   Gemm          -> ops.opGemm (+ transB prepack)  onnx_ops.dart:2152, onnx_graph.dart:2156-2173
+ *   MatMulInteger -> ql.opMatMulInteger       lib/src/onnx_qlinear_ops.dart:32
+ *   QLinearMatMul -> ql.opQLinearMatMul       onnx_qlinear_ops.dart:85 (dispatch onnx_graph.dart:2902-2917)
+ *   MatMulNBits   -> ql.opMatMulNBits         onnx_qlinear_ops.dart:115 (dispatch onnx_graph.dart:2918-2934)
+ * Each b2m_* op below replaces one of those calls for device-resident
+ * operands; a dart:ffi binding (pattern: lib/src/ort/ort_backend.dart) calls
+ * them from the same dispatch cases.
+ *
+ * Conventions (mirroring the reference's native binding):
+ *   - Every entry point returns a b2m_status; 0 is success. On failure
+ *     b2m_last_error() returns a message for the calling thread (the ORT
+ *     binding reads GetErrorMessage the same way, ort_backend.dart:774-782).
+ *     Status codes map onto the reference's exceptions: INVALID_ARGUMENT ->
+ *     ArgumentError, UNSUPPORTED -> UnsupportedError, OUT_OF_MEMORY ->
+ *     OnnxMemoryLimitException, CANCELLED -> OnnxCancelledException.
+ *   - Nothing aborts the process; no entry point throws across the ABI.
+ *   - Tensors are row-major device buffers. Element types use ONNX
+ *     TensorProto.DataType codes (B2M_FLOAT = 1, ...), the codes the reference
+ *     already keys on (onnx_graph.dart:2903: elem type 3 = INT8).
+ *   - Op outputs: `y` is in/out. If *y is NULL the library allocates the
+ *     output tensor (the reference allocates fresh outputs, onnx_ops.dart:1741);
+ *     otherwise *y must already have the output's dtype and element count
+ *     and is written in place (no allocation on the hot path).
+ *   - Calls are enqueued on the context's current stream and return without
+ *     synchronising, except the b2m_*_host helpers and downloads, which
+ *     return after the result is in host memory.
+ *   - One b2m_ctx per thread / isolate and device; a context is not safe for
+ *     concurrent use from several threads (sessions are not shared across
+ *     isolates in the reference either, docs/native_backend.md:99-110).
+ */
+#ifndef B2M_H_
+#define B2M_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define B2M_API __attribute__((visibility("default")))
+#else
+#define B2M_API
+#endif
+
+#define B2M_ABI_VERSION 1
+
+typedef int32_t b2m_status;
+#define B2M_OK 0
+#define B2M_ERR_INVALID_ARGUMENT 1 /* Dart ArgumentError (onnx_qlinear_ops.dart:135,152,162,165) */
+#define B2M_ERR_UNSUPPORTED 2      /* Dart UnsupportedError (onnx_qlinear_ops.dart:38,89,127) */
+#define B2M_ERR_OUT_OF_MEMORY 3    /* device allocation failed or byte budget exceeded */
+#define B2M_ERR_CUDA 4             /* a CUDA runtime/driver call failed */
+#define B2M_ERR_TIMEOUT 5          /* a bounded device-side wait gave up */
+#define B2M_ERR_CANCELLED 6        /* the context's cancel flag was set before launch */
+#define B2M_ERR_NO_DEVICE 7        /* no CUDA device / unsupported device */
+
+/* Element types: ONNX TensorProto.DataType codes. */
+#define B2M_FLOAT 1
+#define B2M_UINT8 2
+#define B2M_INT8 3
+#define B2M_INT32 6
+#define B2M_INT64 7
+#define B2M_FLOAT16 10
+
+/* Arithmetic modes for the floating-point ops. */
+#define B2M_MODE_EXACT 0 /* bitwise identical to the reference Dart kernels */
+#define B2M_MODE_FAST 1  /* tensor cores; max|d|/max|ref| <= 1e-3, cosine >= 0.99999 */
+
+#define B2M_MAX_RANK 8
+
+typedef struct b2m_ctx b2m_ctx;
+typedef struct b2m_tensor b2m_tensor;
+typedef struct b2m_weight b2m_weight;
+
+/* ---- library / context ------------------------------------------------ */
+
+/* ABI version of the loaded library (B2M_ABI_VERSION it was built with). */
+B2M_API int32_t b2m_abi_version(void);
+
+/* Message for the last failing call on this thread ("" if none). Replaces
+ * the ORT status-message read (ort_backend.dart:774-782). */
+B2M_API const char *b2m_last_error(void);
+
+/* Number of visible CUDA devices. */
+B2M_API b2m_status b2m_device_count(int32_t *count);
+
+/* Opens a context on `device` (a CUDA ordinal). The context owns a
+ * non-blocking stream, a stream-ordered memory pool and scratch space.
+ * Replaces the session-level resource setup of OrtRuntime.load /
+ * OrtNativeSession._create (ort_backend.dart:83-111, 171-448). */
+B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx);
+
+/* Waits for outstanding work and frees the context. Tensors and weights made
+ * on the context must be freed first. */
+B2M_API b2m_status b2m_shutdown(b2m_ctx *ctx);
+
+/* Enqueue subsequent work on `stream` (a cudaStream_t of the context's
+ * device); NULL selects the context's own stream again. */
+B2M_API b2m_status b2m_set_stream(b2m_ctx *ctx, void *stream);
+
+/* Blocks until all work enqueued on the current stream has finished. */
+B2M_API b2m_status b2m_synchronize(b2m_ctx *ctx);
+
+/* Execution control, mirroring OnnxExecutionControl
+ * (lib/src/execution_control.dart:29-77): a host flag polled before every
+ * launch (non-zero -> B2M_ERR_CANCELLED, like checkpoint()), and a byte
+ * budget for library-allocated outputs (like checkAdditionalBytes;
+ * <= 0 disables). */
+B2M_API b2m_status b2m_set_cancel_flag(b2m_ctx *ctx, const volatile int32_t *flag);
+B2M_API b2m_status b2m_set_byte_budget(b2m_ctx *ctx, int64_t bytes);
+
+/* Device time of the last op, from CUDA events around its launches, when
+ * timing is on (default off; enabling costs one event pair per op). Replaces
+ * the per-node Stopwatch of ExecutionProfile (onnx_graph.dart:1246-1248). */
+B2M_API b2m_status b2m_enable_timing(b2m_ctx *ctx, int32_t on);
+B2M_API b2m_status b2m_last_kernel_ms(b2m_ctx *ctx, float *ms);
+
+/* ---- tensors (device-resident values; replace Tensor's typed lists,
+ *      lib/src/tensor.dart:16-30, for GPU operands) ----------------------- */
+
+B2M_API b2m_status b2m_tensor_alloc(b2m_ctx *ctx, int32_t dtype, const int64_t *shape, int32_t rank,
+                                    b2m_tensor **out);
+/* Borrows caller-owned device memory (not freed by b2m_tensor_free). */
+B2M_API b2m_status b2m_tensor_wrap(b2m_ctx *ctx, void *device_ptr, int32_t dtype, const int64_t *shape,
+                                   int32_t rank, b2m_tensor **out);
+/* Host <-> device copies of the whole tensor; `bytes` must equal its size.
+ * Both return after the copy has completed. */
+B2M_API b2m_status b2m_tensor_upload(b2m_ctx *ctx, b2m_tensor *t, const void *host, int64_t bytes);
+B2M_API b2m_status b2m_tensor_download(b2m_ctx *ctx, const b2m_tensor *t, void *host, int64_t bytes);
+B2M_API b2m_status b2m_tensor_free(b2m_tensor *t);
+/* dtype, rank, shape (B2M_MAX_RANK entries) and device pointer of `t`. */
+B2M_API b2m_status b2m_tensor_info(const b2m_tensor *t, int32_t *dtype, int32_t *rank, int64_t *shape,
+                                   void **device_ptr);
+
+/* ---- weight prepack (session load) ------------------------------------- */
+
+/* fp32 MatMul / Gemm initializer B. `rows x cols` host row-major; with
+ * trans != 0 the stored matrix is B^T (Gemm transB=1) and is transposed once
+ * here, as the reference caches opTranspose(B) per initializer
+ * (onnx_graph.dart:102-105, 2159-2161). The packed weight is logically
+ * [K, N]. */
+B2M_API b2m_status b2m_weight_prepack_f32(b2m_ctx *ctx, const float *host_b, int64_t rows, int64_t cols,
+                                          int32_t trans, b2m_weight **out);
+
+/* int8 / uint8 MatMulInteger / QLinearMatMul initializer B[K, N]
+ * (dtype B2M_INT8 or B2M_UINT8), stored K-major with per-column sums for the
+ * zero-point correction. */
+B2M_API b2m_status b2m_weight_prepack_i8(b2m_ctx *ctx, const void *host_b, int32_t dtype, int64_t k,
+                                         int64_t n, b2m_weight **out);
+
+/* MatMulNBits initializers: b_q uint8[N, ceil(K/block)/1, block/2] (low
+ * nibble first), scales float[N * nblocks], zero points either packed uint4
+ * uint8[N * ceil(nblocks/2)] (zp_dtype B2M_UINT8), float[N * nblocks]
+ * (B2M_FLOAT) or absent (zero_points NULL, zp_dtype 0; zero point 8).
+ * Validation mirrors opMatMulNBits (onnx_qlinear_ops.dart:126-166):
+ * bits != 4 -> UNSUPPORTED; K, N <= 0 or block not a power of two >= 16
+ * -> INVALID_ARGUMENT. */
+B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, const float *scales,
+                                            const void *zero_points, int32_t zp_dtype, int64_t k,
+                                            int64_t n, int32_t bits, int32_t block_size,
+                                            b2m_weight **out);
+B2M_API b2m_status b2m_weight_free(b2m_weight *w);
+
+/* ---- operators --------------------------------------------------------- */
+
+/* MatMul (opMatMul, onnx_ops.dart:1710-1766): numpy-broadcast batched
+ * A[..., M, K] . B[..., K, N]. Exactly one of `b` (device tensor) and
+ * `b_packed` (from b2m_weight_prepack_f32) is non-NULL. mode EXACT is
+ * bitwise identical to the reference's matmulKernel. */
+B2M_API b2m_status b2m_matmul_f32(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b,
+                                  const b2m_weight *b_packed, int32_t mode, b2m_tensor **y);
+
+/* Gemm (opGemm, onnx_ops.dart:2152-2173): alpha * A' . B' + beta * C with
+ * 2-D A, B; C (optional) broadcasts onto [M, N]. With `b_packed` the
+ * transpose was applied at prepack and trans_b must be 0. */
+B2M_API b2m_status b2m_gemm_f32(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b,
+                                const b2m_weight *b_packed, const b2m_tensor *c, float alpha, float beta,
+                                int32_t trans_a, int32_t trans_b, int32_t mode, b2m_tensor **y);
+
+/* MatMulInteger (opMatMulInteger, onnx_qlinear_ops.dart:32-81):
+ * Y int32 = (A - a_zp)(B - b_zp), A uint8/int8 [..., M, K], B uint8/int8
+ * [..., K, N] or prepacked. Zero points: NULL, scalar, per-row [M] (A) or
+ * per-column [N] (B), same dtype as their operand. Batches must match or be
+ * 1. Exact (the reference accumulates in int64; values outside int32 need
+ * K > 33025 and are rejected as UNSUPPORTED). */
+B2M_API b2m_status b2m_matmul_integer(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b,
+                                      const b2m_weight *b_packed, const b2m_tensor *a_zp,
+                                      const b2m_tensor *b_zp, b2m_tensor **y);
+
+/* QLinearMatMul (opQLinearMatMul, onnx_qlinear_ops.dart:85-108):
+ * per-tensor scales (host floats), zero-point tensors as above, y_zp scalar
+ * (NULL = 0); output dtype of y is uint8 if lo == 0, int8 if lo == -128
+ * (the reference picks lo/hi from y_zp's dtype, onnx_graph.dart:2903). */
+B2M_API b2m_status b2m_qlinear_matmul(b2m_ctx *ctx, const b2m_tensor *a, float a_scale,
+                                      const b2m_tensor *a_zp, const b2m_tensor *b,
+                                      const b2m_weight *b_packed, float b_scale, const b2m_tensor *b_zp,
+                                      float y_scale, int32_t y_zp, int32_t lo, int32_t hi,
+                                      b2m_tensor **y);
+
+/* MatMulNBits (opMatMulNBits, onnx_qlinear_ops.dart:115-228):
+ * Y[..., N] = A[..., K] . dequant(W)^T + bias, A float32, W from
+ * b2m_weight_prepack_nbits, bias float[N] or NULL. mode EXACT reproduces the
+ * reference bit for bit (double accumulation for one row, float32 tiles
+ * otherwise); FAST uses f16 tensor-core MMA with fp32 accumulation. */
+B2M_API b2m_status b2m_matmul_nbits(b2m_ctx *ctx, const b2m_tensor *a, const b2m_weight *w,
+                                    const b2m_tensor *bias, int32_t mode, b2m_tensor **y);
+
+/* Host-buffer convenience for callers without device tensors: copies A
+ * (m rows of K floats) and bias (N floats or NULL) to the device, runs
+ * b2m_matmul_nbits, copies Y (m x N floats) back, and returns when Y is in
+ * host memory. */
+B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int64_t m,
+                                         const b2m_weight *w, const float *bias_host, int32_t mode,
+                                         float *y_host);
+
+/* Raw device-pointer form of b2m_matmul_nbits for callers that manage their
+ * own device memory (a: m x K floats, bias: N floats or NULL, y: m x N
+ * floats), enqueued on the current stream. */
+B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m, const b2m_weight *w,
+                                        const float *bias, int32_t mode, float *y);
+
+/* Shape of a packed weight: K and N (logical B is [K, N]). */
+B2M_API b2m_status b2m_weight_info(const b2m_weight *w, int64_t *k, int64_t *n);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2M_H_ */

@@ -1,0 +1,203 @@
+// Internal types shared by the runtime (runtime.cu) and the kernel files.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/b2m.h"
+
+// ---------------------------------------------------------------------------
+// Errors: every ABI entry point converts a thrown B2mError into a status code
+// and a thread-local message; nothing escapes the C boundary.
+// ---------------------------------------------------------------------------
+struct B2mError {
+  b2m_status code;
+  std::string msg;
+};
+
+[[noreturn]] void b2m_throw(b2m_status code, const std::string &msg);
+
+#define B2M_CUDA(expr)                                                                     \
+  do {                                                                                     \
+    cudaError_t e__ = (expr);                                                              \
+    if (e__ != cudaSuccess) {                                                              \
+      (void)cudaGetLastError();                                                            \
+      b2m_throw(e__ == cudaErrorMemoryAllocation ? B2M_ERR_OUT_OF_MEMORY : B2M_ERR_CUDA,   \
+                std::string(#expr) + ": " + cudaGetErrorString(e__));                      \
+    }                                                                                      \
+  } while (0)
+
+#define B2M_REQUIRE(cond, code, msg) \
+  do {                               \
+    if (!(cond)) b2m_throw((code), (msg)); \
+  } while (0)
+
+// Device-side error codes written by kernels that contain bounded waits.
+#define B2M_DEVERR_NONE 0
+#define B2M_DEVERR_MBAR_TIMEOUT 1
+#define B2M_DEVERR_TMEM_TIMEOUT 2
+
+struct b2m_ctx {
+  int device = 0;
+  int sm_count = 0;
+  cudaStream_t own_stream = nullptr;
+  cudaStream_t stream = nullptr;
+  cudaMemPool_t pool = nullptr;
+  const volatile int32_t *cancel_flag = nullptr;
+  int64_t byte_budget = 0;
+  int64_t live_bytes = 0;
+  bool timing = false;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  bool timing_pending = false;
+  // Grow-only device workspace for op temporaries (transposes, converted
+  // operands). Stream-ordered: reused by the next op on the same stream.
+  void *scratch = nullptr;
+  size_t scratch_bytes = 0;
+  // Device word that kernels with bounded spin-waits set on timeout.
+  int32_t *dev_err = nullptr;
+  // Pinned staging for the host-buffer helpers.
+  void *pinned = nullptr;
+  size_t pinned_bytes = 0;
+};
+
+struct b2m_tensor {
+  b2m_ctx *ctx = nullptr;
+  void *data = nullptr;
+  int32_t dtype = 0;
+  int32_t rank = 0;
+  int64_t shape[B2M_MAX_RANK] = {0};
+  int64_t numel = 0;
+  bool owned = false;
+};
+
+enum WeightKind { W_F32 = 1, W_I8 = 2, W_NBITS = 3 };
+
+// Packed MatMulNBits weights (see prepack in runtime.cu):
+//   bq      [npad][kp/2] bytes; within every 16-byte (32-k) group the bytes are
+//           reordered so thread t of an MMA quad reads k in [4t,4t+4) and
+//           [16+4t,16+4t+4) with one 32-bit load: new[4t+0..3] =
+//           old[2t], old[2t+1], old[8+2t], old[9+2t].
+//   scales  [npad][nblocks] float
+//   zp_u8   [npad][zstride] packed uint4 (low nibble = even block), or
+//   zp_f32  [npad][nblocks] float, or neither (zero point 8).
+struct NbitsWeight {
+  uint8_t *bq = nullptr;
+  float *scales = nullptr;
+  uint8_t *zp_u8 = nullptr;
+  float *zp_f32 = nullptr;
+  int zp_kind = 0;  // 0 none, 1 packed uint4, 2 float
+  int block = 0;
+  int64_t nblocks = 0;
+  int64_t zstride = 0;
+  int64_t kp = 0;    // padded K (multiple of 64, >= nblocks*block)
+  int64_t npad = 0;  // padded N (multiple of 128)
+  float *wdeq = nullptr;  // exact-mode float32 W [N][K], made on first use
+};
+
+// Packed int8 / uint8 weights: bt[npad][kpad] (K-major), colsum[n] = sum_k b.
+struct I8Weight {
+  int8_t *bt = nullptr;
+  int32_t *colsum = nullptr;
+  int32_t dtype = 0;
+  int64_t kpad = 0, npad = 0;
+};
+
+struct b2m_weight {
+  b2m_ctx *ctx = nullptr;
+  int kind = 0;
+  int64_t k = 0, n = 0;
+  float *f32 = nullptr;  // W_F32: [K][N] row-major
+  I8Weight i8;
+  NbitsWeight nb;
+};
+
+// ---------------------------------------------------------------------------
+// Kernel launchers (implemented in k_*.cu)
+// ---------------------------------------------------------------------------
+
+// Epilogue kinds of the exact fp32 GEMM.
+enum F32Epi {
+  EPI_NONE = 0,
+  EPI_GEMM = 1,      // y = acc; y *= alpha (if has_alpha); y += (beta*)C
+  EPI_NBITS = 2,     // y = f32((double)acc + bias)   (tile path, :221-224)
+  EPI_NBITS_M1 = 3,  // y = f32(sum_double + bias)    (decode path, :203)
+};
+
+struct F32GemmArgs {
+  const float *A = nullptr;
+  const float *B = nullptr;
+  float *Y = nullptr;
+  int64_t M = 0, N = 0, K = 0;
+  int64_t sa_m = 0, sa_k = 0;  // A(i,k) = A[i*sa_m + k*sa_k]
+  int64_t sb_k = 0, sb_n = 0;  // B(k,j) = B[k*sb_k + j*sb_n]
+  int64_t ldy = 0;
+  // Broadcast batches: batch index decomposes over bdims (row-major); the
+  // operand offsets use per-dim strides (0 on broadcast dims).
+  int nbd = 0;
+  int64_t bdims[6] = {0};
+  int64_t a_bstride[6] = {0};
+  int64_t b_bstride[6] = {0};
+  int64_t y_bstride = 0;
+  int64_t batch = 1;
+  // Reference numerics: which columns accumulate in double.
+  int64_t m_eff = 0;   // row count the reference kernel saw (after batch collapse)
+  int64_t tile_w = 0;  // column tile width of the reference call (N, or 32 for NBits)
+  int all_double = 0;  // MatMulNBits single-row decode: every column in double
+  // Epilogue
+  int epi = EPI_NONE;
+  int has_alpha = 0;
+  float alpha = 1.f;
+  const float *C = nullptr;
+  int64_t c_rs = 0, c_cs = 0;
+  int has_beta = 0;
+  float beta = 1.f;
+  const float *bias = nullptr;
+};
+
+void launch_f32_exact(const F32GemmArgs &a, cudaStream_t s);
+
+// MatMulNBits
+struct NbitsArgs {
+  const float *A = nullptr;  // [M][K]
+  const NbitsWeight *w = nullptr;
+  const float *bias = nullptr;  // [N] or null
+  float *Y = nullptr;           // [M][N]
+  int64_t M = 0, K = 0, N = 0;
+  int32_t *dev_err = nullptr;
+};
+bool nbits_smallm_supported(const NbitsWeight &w, int64_t M);
+void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl);
+void launch_nbits_simt(const NbitsArgs &a, cudaStream_t s);
+void launch_nbits_dequant_f32(const NbitsWeight &w, int64_t K, int64_t N, float *out, cudaStream_t s);
+
+// MatMulInteger / QLinearMatMul
+struct I8GemmArgs {
+  const void *A = nullptr;  // [batch_a][M][K] uint8 or int8
+  int a_signed = 0;
+  int64_t a_bstride = 0;    // elements between A batches (0 = broadcast)
+  const int8_t *Bt = nullptr;  // [batch_b][npad][kpad] K-major
+  int b_signed = 0;
+  int64_t b_bstride = 0;
+  int64_t kpad = 0;
+  const int32_t *colsum = nullptr;  // [batch_b][n] (stride n)
+  int64_t colsum_bstride = 0;
+  const void *azp = nullptr;  // scalar or [M]; dtype of A
+  int64_t azp_len = 0;
+  const void *bzp = nullptr;  // scalar or [N]; dtype of B
+  int64_t bzp_len = 0;
+  int azp_signed = 0, bzp_signed = 0;
+  int64_t M = 0, N = 0, K = 0, batch = 1;
+  // output
+  int32_t *Y32 = nullptr;  // MatMulInteger
+  void *Yq = nullptr;      // QLinearMatMul (uint8 or int8)
+  int requant = 0;
+  double mult = 0.0;
+  int32_t y_zp = 0, lo = 0, hi = 0;
+};
+void launch_i8_gemm(const I8GemmArgs &a, cudaStream_t s);
+void launch_i8_pack(const void *B, int b_signed, int64_t batch, int64_t K, int64_t N, int8_t *bt,
+                    int64_t kpad, int64_t npad, int32_t *colsum, cudaStream_t s);

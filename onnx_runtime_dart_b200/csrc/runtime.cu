@@ -1,0 +1,1015 @@
+// C ABI of libb200mm.so (declared in include/b2m.h): contexts, device
+// tensors, weight prepack, operator validation and kernel dispatch.
+//
+// Validation mirrors the reference's operator functions so the same inputs
+// fail with the same class of error: opMatMul / opGemm
+// (lib/src/onnx_ops.dart:1710-1766, 2152-2173), opMatMulInteger /
+// opQLinearMatMul (lib/src/onnx_qlinear_ops.dart:32-108) and opMatMulNBits
+// (:115-228).
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "b2m_internal.cuh"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+template <class F>
+b2m_status guarded(F &&f) {
+  try {
+    f();
+    return B2M_OK;
+  } catch (const B2mError &e) {
+    g_last_error = e.msg;
+    return e.code;
+  } catch (const std::bad_alloc &) {
+    g_last_error = "host allocation failed";
+    return B2M_ERR_OUT_OF_MEMORY;
+  } catch (...) {
+    g_last_error = "unexpected internal error";
+    return B2M_ERR_CUDA;
+  }
+}
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) B2M_CUDA(cudaSetDevice(dev));
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+int64_t elem_size(int32_t dtype) {
+  switch (dtype) {
+    case B2M_FLOAT: return 4;
+    case B2M_UINT8: return 1;
+    case B2M_INT8: return 1;
+    case B2M_INT32: return 4;
+    case B2M_INT64: return 8;
+    case B2M_FLOAT16: return 2;
+    default: return 0;
+  }
+}
+
+int64_t round_up(int64_t x, int64_t m) { return (x + m - 1) / m * m; }
+
+std::string shape_str(const int64_t *s, int r) {
+  std::string o = "[";
+  for (int i = 0; i < r; i++) o += (i ? ", " : "") + std::to_string(s[i]);
+  return o + "]";
+}
+
+void check_ctx(b2m_ctx *ctx) { B2M_REQUIRE(ctx, B2M_ERR_INVALID_ARGUMENT, "null context"); }
+
+void check_cancel(b2m_ctx *ctx) {
+  if (ctx->cancel_flag && *ctx->cancel_flag) b2m_throw(B2M_ERR_CANCELLED, "operation cancelled");
+}
+
+void check_device_error(b2m_ctx *ctx) {
+  // Bounded device waits report through ctx->dev_err; read it lazily when the
+  // host synchronises anyway.
+  int32_t e = 0;
+  B2M_CUDA(cudaMemcpyAsync(&e, ctx->dev_err, sizeof(e), cudaMemcpyDeviceToHost, ctx->stream));
+  B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+  if (e != B2M_DEVERR_NONE) {
+    B2M_CUDA(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int32_t), ctx->stream));
+    b2m_throw(B2M_ERR_TIMEOUT, "a bounded device-side wait timed out (code " + std::to_string(e) + ")");
+  }
+}
+
+b2m_tensor *new_tensor(b2m_ctx *ctx, int32_t dtype, const int64_t *shape, int32_t rank) {
+  B2M_REQUIRE(rank >= 0 && rank <= B2M_MAX_RANK, B2M_ERR_INVALID_ARGUMENT, "tensor rank out of range");
+  B2M_REQUIRE(elem_size(dtype) > 0, B2M_ERR_INVALID_ARGUMENT, "unsupported tensor dtype");
+  int64_t numel = 1;
+  for (int i = 0; i < rank; i++) {
+    B2M_REQUIRE(shape[i] >= 0, B2M_ERR_INVALID_ARGUMENT, "negative dimension");
+    numel *= shape[i];
+  }
+  const int64_t bytes = numel * elem_size(dtype);
+  if (ctx->byte_budget > 0 && ctx->live_bytes + bytes > ctx->byte_budget)
+    b2m_throw(B2M_ERR_OUT_OF_MEMORY, "tensor byte budget exceeded (" + std::to_string(ctx->live_bytes + bytes) +
+                                         " > " + std::to_string(ctx->byte_budget) + ")");
+  b2m_tensor *t = new b2m_tensor();
+  t->ctx = ctx;
+  t->dtype = dtype;
+  t->rank = rank;
+  for (int i = 0; i < rank; i++) t->shape[i] = shape[i];
+  t->numel = numel;
+  t->owned = true;
+  if (bytes > 0) {
+    cudaError_t e = cudaMallocAsync(&t->data, (size_t)bytes, ctx->stream);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      delete t;
+      b2m_throw(B2M_ERR_OUT_OF_MEMORY, std::string("device allocation failed: ") + cudaGetErrorString(e));
+    }
+  }
+  ctx->live_bytes += bytes;
+  return t;
+}
+
+int64_t tensor_bytes(const b2m_tensor *t) { return t->numel * elem_size(t->dtype); }
+
+// Output handling: *y == NULL -> allocate; else check dtype / element count.
+b2m_tensor *prepare_output(b2m_ctx *ctx, b2m_tensor **y, int32_t dtype, const std::vector<int64_t> &shape) {
+  B2M_REQUIRE(y, B2M_ERR_INVALID_ARGUMENT, "null output pointer");
+  if (*y == nullptr) {
+    *y = new_tensor(ctx, dtype, shape.data(), (int32_t)shape.size());
+    return *y;
+  }
+  b2m_tensor *t = *y;
+  int64_t numel = 1;
+  for (int64_t d : shape) numel *= d;
+  B2M_REQUIRE(t->dtype == dtype && t->numel == numel, B2M_ERR_INVALID_ARGUMENT,
+              "output tensor has the wrong dtype or size for " + shape_str(shape.data(), (int)shape.size()));
+  t->rank = (int32_t)shape.size();
+  for (size_t i = 0; i < shape.size(); i++) t->shape[i] = shape[i];
+  return t;
+}
+
+// Bump allocator over the context workspace; reset at the start of each op.
+struct Scratch {
+  b2m_ctx *ctx;
+  size_t used = 0;
+  explicit Scratch(b2m_ctx *c, size_t need) : ctx(c) {
+    if (need > ctx->scratch_bytes) {
+      if (ctx->scratch) B2M_CUDA(cudaFreeAsync(ctx->scratch, ctx->stream));
+      ctx->scratch = nullptr;
+      ctx->scratch_bytes = 0;
+      const size_t sz = std::max(need, (size_t)1 << 20);
+      B2M_CUDA(cudaMallocAsync(&ctx->scratch, sz, ctx->stream));
+      ctx->scratch_bytes = sz;
+    }
+  }
+  void *take(size_t bytes) {
+    const size_t off = (used + 255) & ~(size_t)255;
+    B2M_REQUIRE(off + bytes <= ctx->scratch_bytes, B2M_ERR_CUDA, "internal: scratch overflow");
+    used = off + bytes;
+    return static_cast<char *>(ctx->scratch) + off;
+  }
+};
+
+struct OpTimer {
+  b2m_ctx *ctx;
+  explicit OpTimer(b2m_ctx *c) : ctx(c) {
+    if (ctx->timing) B2M_CUDA(cudaEventRecord(ctx->ev0, ctx->stream));
+  }
+  void done() {
+    if (ctx->timing) {
+      B2M_CUDA(cudaEventRecord(ctx->ev1, ctx->stream));
+      ctx->timing_pending = true;
+    }
+  }
+};
+
+void require_float(const b2m_tensor *t, const char *what) {
+  B2M_REQUIRE(t, B2M_ERR_INVALID_ARGUMENT, std::string(what) + " is null");
+  B2M_REQUIRE(t->dtype == B2M_FLOAT, B2M_ERR_INVALID_ARGUMENT, std::string(what) + " must be float32");
+}
+
+// ---------------------------------------------------------------------------
+// fp32 MatMul / Gemm
+// ---------------------------------------------------------------------------
+
+void matmul_f32_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const b2m_weight *bw, int32_t mode,
+                     b2m_tensor **y) {
+  require_float(a, "MatMul A");
+  B2M_REQUIRE((b == nullptr) != (bw == nullptr), B2M_ERR_INVALID_ARGUMENT, "MatMul: pass exactly one of b, b_packed");
+  B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT, "MatMul: bad mode");
+  int64_t bshape[B2M_MAX_RANK];
+  int brank;
+  const float *bptr;
+  if (b) {
+    require_float(b, "MatMul B");
+    brank = b->rank;
+    for (int i = 0; i < brank; i++) bshape[i] = b->shape[i];
+    bptr = static_cast<const float *>(b->data);
+  } else {
+    B2M_REQUIRE(bw->kind == W_F32, B2M_ERR_INVALID_ARGUMENT, "MatMul: b_packed is not an fp32 weight");
+    brank = 2;
+    bshape[0] = bw->k;
+    bshape[1] = bw->n;
+    bptr = bw->f32;
+  }
+  B2M_REQUIRE(a->rank >= 2 && brank >= 2, B2M_ERR_INVALID_ARGUMENT, "MatMul: operands must have rank >= 2");
+  const int64_t m = a->shape[a->rank - 2], k = a->shape[a->rank - 1];
+  const int64_t k2 = bshape[brank - 2], n = bshape[brank - 1];
+  B2M_REQUIRE(k == k2, B2M_ERR_INVALID_ARGUMENT,
+              "MatMul inner dims mismatch: " + std::to_string(k) + " vs " + std::to_string(k2));
+  // numpy broadcast of the batch dims (_broadcastShape, onnx_ops.dart:26-44)
+  const int ab = a->rank - 2, bb = brank - 2, rank = std::max(ab, bb);
+  B2M_REQUIRE(rank <= 6, B2M_ERR_UNSUPPORTED, "MatMul: more than 6 batch dims");
+  int64_t ap[6], bp[6], ob[6];
+  for (int d = 0; d < rank; d++) {
+    ap[d] = d < rank - ab ? 1 : a->shape[d - (rank - ab)];
+    bp[d] = d < rank - bb ? 1 : bshape[d - (rank - bb)];
+    if (ap[d] == bp[d]) ob[d] = ap[d];
+    else if (ap[d] == 1) ob[d] = bp[d];
+    else if (bp[d] == 1) ob[d] = ap[d];
+    else
+      b2m_throw(B2M_ERR_INVALID_ARGUMENT, "Cannot broadcast shapes " + shape_str(a->shape, ab) + " and " +
+                                              shape_str(bshape, bb));
+  }
+  std::vector<int64_t> oshape(ob, ob + rank);
+  oshape.push_back(m);
+  oshape.push_back(n);
+  int64_t batch = 1, bcount = 1;
+  for (int d = 0; d < rank; d++) batch *= ob[d];
+  for (int d = 0; d < bb; d++) bcount *= bshape[d];
+  check_cancel(ctx);
+  b2m_tensor *out = prepare_output(ctx, y, B2M_FLOAT, oshape);
+  if (batch * m * n == 0) return;
+  OpTimer timer(ctx);
+  F32GemmArgs p;
+  p.A = static_cast<const float *>(a->data);
+  p.B = bptr;
+  p.Y = static_cast<float *>(out->data);
+  p.K = k;
+  p.N = n;
+  p.sa_k = 1;
+  p.sa_m = k;
+  p.sb_k = n;
+  p.sb_n = 1;
+  p.ldy = n;
+  p.tile_w = n;
+  p.epi = EPI_NONE;
+  if (batch > 1 && bcount == 1) {
+    // Shared 2-D B: one GEMM over all batches' rows (onnx_ops.dart:1728-1735).
+    p.M = batch * m;
+    p.m_eff = batch * m;
+    p.batch = 1;
+  } else {
+    p.M = m;
+    p.m_eff = m;
+    p.batch = batch;
+    p.nbd = rank;
+    // Row-major strides over each operand's own batch dims.
+    int64_t sa = m * k, sb = k * n;
+    for (int d = rank - 1; d >= 0; d--) {
+      p.bdims[d] = ob[d];
+      p.a_bstride[d] = ap[d] == 1 ? 0 : sa;
+      p.b_bstride[d] = bp[d] == 1 ? 0 : sb;
+      sa *= ap[d];
+      sb *= bp[d];
+    }
+    p.y_bstride = m * n;
+  }
+  // FAST currently shares the exact kernel for fp32 MatMul (always within
+  // the fast-mode tolerance, since it is exact).
+  launch_f32_exact(p, ctx->stream);
+  timer.done();
+}
+
+void gemm_f32_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const b2m_weight *bw,
+                   const b2m_tensor *c, float alpha, float beta, int32_t ta, int32_t tb, int32_t mode,
+                   b2m_tensor **y) {
+  require_float(a, "Gemm A");
+  B2M_REQUIRE((b == nullptr) != (bw == nullptr), B2M_ERR_INVALID_ARGUMENT, "Gemm: pass exactly one of b, b_packed");
+  B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT, "Gemm: bad mode");
+  B2M_REQUIRE(a->rank == 2, B2M_ERR_INVALID_ARGUMENT, "Gemm: A must be 2-D");
+  int64_t br, bc;
+  const float *bptr;
+  if (b) {
+    require_float(b, "Gemm B");
+    B2M_REQUIRE(b->rank == 2, B2M_ERR_INVALID_ARGUMENT, "Gemm: B must be 2-D");
+    br = b->shape[0];
+    bc = b->shape[1];
+    bptr = static_cast<const float *>(b->data);
+  } else {
+    B2M_REQUIRE(bw->kind == W_F32, B2M_ERR_INVALID_ARGUMENT, "Gemm: b_packed is not an fp32 weight");
+    B2M_REQUIRE(!tb, B2M_ERR_INVALID_ARGUMENT, "Gemm: b_packed already holds B' (trans_b must be 0)");
+    br = bw->k;
+    bc = bw->n;
+    bptr = bw->f32;
+  }
+  const int64_t M = ta ? a->shape[1] : a->shape[0], K = ta ? a->shape[0] : a->shape[1];
+  const int64_t K2 = tb ? bc : br, N = tb ? br : bc;
+  B2M_REQUIRE(K == K2, B2M_ERR_INVALID_ARGUMENT,
+              "MatMul inner dims mismatch: " + std::to_string(K) + " vs " + std::to_string(K2));
+  int64_t crs = 0, ccs = 0;
+  if (c) {
+    require_float(c, "Gemm C");
+    int64_t cr = 1, cc = 1;
+    if (c->rank == 1) cc = c->shape[0];
+    else if (c->rank == 2) {
+      cr = c->shape[0];
+      cc = c->shape[1];
+    } else
+      B2M_REQUIRE(c->rank == 0, B2M_ERR_INVALID_ARGUMENT, "Gemm: C must have rank <= 2");
+    B2M_REQUIRE((cr == 1 || cr == M) && (cc == 1 || cc == N), B2M_ERR_INVALID_ARGUMENT,
+                "Cannot broadcast shapes [" + std::to_string(M) + ", " + std::to_string(N) + "] and " +
+                    shape_str(c->shape, c->rank));
+    crs = cr == 1 ? 0 : cc;
+    ccs = cc == 1 ? 0 : 1;
+  }
+  check_cancel(ctx);
+  b2m_tensor *out = prepare_output(ctx, y, B2M_FLOAT, {M, N});
+  if (M * N == 0) return;
+  OpTimer timer(ctx);
+  F32GemmArgs p;
+  p.A = static_cast<const float *>(a->data);
+  p.B = bptr;
+  p.Y = static_cast<float *>(out->data);
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  // A' / B' by strides: the reference's transposes are exact copies.
+  const int64_t acols = a->shape[1];
+  p.sa_m = ta ? 1 : acols;
+  p.sa_k = ta ? acols : 1;
+  p.sb_k = tb ? bc : bc;
+  p.sb_n = 1;
+  if (tb) {
+    p.sb_k = 1;
+    p.sb_n = bc;
+  } else {
+    p.sb_k = bc;
+    p.sb_n = 1;
+  }
+  p.ldy = N;
+  p.m_eff = M;
+  p.tile_w = N;
+  p.batch = 1;
+  p.epi = EPI_GEMM;
+  p.has_alpha = alpha != 1.0f;
+  p.alpha = alpha;
+  if (c) {
+    p.C = static_cast<const float *>(c->data);
+    p.c_rs = crs;
+    p.c_cs = ccs;
+    p.has_beta = beta != 1.0f;
+    p.beta = beta;
+  }
+  launch_f32_exact(p, ctx->stream);
+  timer.done();
+}
+
+// ---------------------------------------------------------------------------
+// MatMulInteger / QLinearMatMul
+// ---------------------------------------------------------------------------
+
+bool is_i8(int32_t dt) { return dt == B2M_UINT8 || dt == B2M_INT8; }
+
+void integer_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const b2m_weight *bw,
+                  const b2m_tensor *azp, const b2m_tensor *bzp, bool requant, double mult, int32_t yzp, int32_t lo,
+                  int32_t hi, b2m_tensor **y) {
+  const char *op = requant ? "QLinearMatMul" : "MatMulInteger";
+  B2M_REQUIRE(a && is_i8(a->dtype), B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": A must be uint8 or int8");
+  B2M_REQUIRE((b == nullptr) != (bw == nullptr), B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + ": pass exactly one of b, b_packed");
+  B2M_REQUIRE(a->rank >= 2, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": A must have rank >= 2");
+  const int64_t m = a->shape[a->rank - 2], k = a->shape[a->rank - 1];
+  int64_t n, kb, b_batch;
+  int32_t bdt;
+  if (b) {
+    B2M_REQUIRE(is_i8(b->dtype), B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": B must be uint8 or int8");
+    B2M_REQUIRE(b->rank >= 2, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": B must have rank >= 2");
+    n = b->shape[b->rank - 1];
+    kb = b->shape[b->rank - 2];
+    b_batch = (kb * n) ? b->numel / (kb * n) : 1;
+    bdt = b->dtype;
+  } else {
+    B2M_REQUIRE(bw->kind == W_I8, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": b_packed is not an int8 weight");
+    n = bw->n;
+    kb = bw->k;
+    b_batch = 1;
+    bdt = bw->i8.dtype;
+  }
+  B2M_REQUIRE(kb == k, B2M_ERR_INVALID_ARGUMENT, std::string(op) + " inner dim mismatch");
+  // Zero points: scalar, per-row [M] for A, per-column [N] for B (:37-40).
+  if ((azp && azp->numel != 1 && azp->numel != m) || (bzp && bzp->numel != 1 && bzp->numel != n))
+    b2m_throw(B2M_ERR_UNSUPPORTED,
+              "MatMulInteger: zero points must be scalar, per-row [M] for A or per-column [N] for B");
+  if (azp) B2M_REQUIRE(is_i8(azp->dtype), B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": a_zero_point dtype");
+  if (bzp) B2M_REQUIRE(is_i8(bzp->dtype), B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": b_zero_point dtype");
+  const int64_t a_batch = (m * k) ? a->numel / (m * k) : 1;
+  const int64_t batch = std::max(a_batch, b_batch);
+  B2M_REQUIRE((a_batch == batch || a_batch == 1) && (b_batch == batch || b_batch == 1), B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + " batch mismatch");
+  B2M_REQUIRE(k <= 33025, B2M_ERR_UNSUPPORTED, std::string(op) + ": K > 33025 may leave the int32 range");
+  std::vector<int64_t> oshape;
+  if (a_batch >= b_batch) oshape.assign(a->shape, a->shape + a->rank - 2);
+  else oshape.assign(b->shape, b->shape + b->rank - 2);
+  oshape.push_back(m);
+  oshape.push_back(n);
+  int32_t odt = B2M_INT32;
+  if (requant) {
+    B2M_REQUIRE((lo == 0 && hi == 255) || (lo == -128 && hi == 127), B2M_ERR_INVALID_ARGUMENT,
+                "QLinearMatMul: lo/hi must be [0,255] or [-128,127]");
+    odt = lo == 0 ? B2M_UINT8 : B2M_INT8;
+  }
+  check_cancel(ctx);
+  b2m_tensor *out = prepare_output(ctx, y, odt, oshape);
+  if (batch * m * n == 0) return;
+  OpTimer timer(ctx);
+  I8GemmArgs p;
+  p.A = a->data;
+  p.a_signed = a->dtype == B2M_INT8;
+  p.a_bstride = a_batch == 1 ? 0 : m * k;
+  p.b_signed = bdt == B2M_INT8;
+  p.M = m;
+  p.N = n;
+  p.K = k;
+  p.batch = batch;
+  if (bw) {
+    p.Bt = bw->i8.bt;
+    p.kpad = bw->i8.kpad;
+    p.colsum = bw->i8.colsum;
+    p.b_bstride = 0;
+    p.colsum_bstride = 0;
+  } else {
+    const int64_t kpad = round_up(std::max<int64_t>(k, 1), 64), npad = round_up(std::max<int64_t>(n, 1), 128);
+    Scratch sc(ctx, (size_t)(b_batch * npad * kpad + b_batch * n * 4 + 1024));
+    int8_t *bt = static_cast<int8_t *>(sc.take((size_t)(b_batch * npad * kpad)));
+    int32_t *cs = static_cast<int32_t *>(sc.take((size_t)(b_batch * n * 4)));
+    launch_i8_pack(b->data, p.b_signed, b_batch, k, n, bt, kpad, npad, cs, ctx->stream);
+    p.Bt = bt;
+    p.kpad = kpad;
+    p.colsum = cs;
+    p.b_bstride = b_batch == 1 ? 0 : npad * kpad;
+    p.colsum_bstride = b_batch == 1 ? 0 : n;
+  }
+  if (azp) {
+    p.azp = azp->data;
+    p.azp_len = azp->numel;
+    p.azp_signed = azp->dtype == B2M_INT8;
+  }
+  if (bzp) {
+    p.bzp = bzp->data;
+    p.bzp_len = bzp->numel;
+    p.bzp_signed = bzp->dtype == B2M_INT8;
+  }
+  if (requant) {
+    p.requant = 1;
+    p.mult = mult;
+    p.y_zp = yzp;
+    p.lo = lo;
+    p.hi = hi;
+    p.Yq = out->data;
+  } else {
+    p.Y32 = static_cast<int32_t *>(out->data);
+  }
+  launch_i8_gemm(p, ctx->stream);
+  timer.done();
+}
+
+// ---------------------------------------------------------------------------
+// MatMulNBits
+// ---------------------------------------------------------------------------
+
+void nbits_run(b2m_ctx *ctx, const float *A, int64_t m, const b2m_weight *w, const float *bias, int32_t mode,
+               float *Y) {
+  B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+  B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad mode");
+  if (m == 0) return;
+  const int64_t K = w->k, N = w->n;
+  if (mode == B2M_MODE_FAST) {
+    NbitsArgs p;
+    p.A = A;
+    p.w = &w->nb;
+    p.bias = bias;
+    p.Y = Y;
+    p.M = m;
+    p.K = K;
+    p.N = N;
+    p.dev_err = ctx->dev_err;
+    if (nbits_smallm_supported(w->nb, m)) launch_nbits_smallm(p, ctx->stream, true);
+    else launch_nbits_simt(p, ctx->stream);
+    return;
+  }
+  // EXACT: dequantize once (exactly as weight() does), then the exact GEMM.
+  NbitsWeight &nb = const_cast<b2m_weight *>(w)->nb;
+  if (!nb.wdeq) {
+    B2M_CUDA(cudaMalloc(&nb.wdeq, (size_t)(N * K * 4)));
+    launch_nbits_dequant_f32(nb, K, N, nb.wdeq, ctx->stream);
+  }
+  F32GemmArgs p;
+  p.A = A;
+  p.B = nb.wdeq;
+  p.Y = Y;
+  p.M = m;
+  p.N = N;
+  p.K = K;
+  p.sa_m = K;
+  p.sa_k = 1;
+  p.sb_k = 1;  // B(k, j) = W[j][k]
+  p.sb_n = K;
+  p.ldy = N;
+  p.batch = 1;
+  p.bias = bias;
+  if (m == 1) {
+    p.all_double = 1;  // decode path: double accumulation (:194-205)
+    p.m_eff = 1;
+    p.tile_w = 32;
+    p.epi = EPI_NBITS_M1;
+  } else {
+    p.m_eff = m;       // 32-column tiles through matmulKernel (:208-226)
+    p.tile_w = 32;
+    p.epi = EPI_NBITS;
+  }
+  launch_f32_exact(p, ctx->stream);
+}
+
+}  // namespace
+
+[[noreturn]] void b2m_throw(b2m_status code, const std::string &msg) { throw B2mError{code, msg}; }
+
+// ===========================================================================
+// Exported C ABI
+// ===========================================================================
+extern "C" {
+
+B2M_API int32_t b2m_abi_version(void) { return B2M_ABI_VERSION; }
+
+B2M_API const char *b2m_last_error(void) { return g_last_error.c_str(); }
+
+B2M_API b2m_status b2m_device_count(int32_t *count) {
+  return guarded([&] {
+    B2M_REQUIRE(count, B2M_ERR_INVALID_ARGUMENT, "null count");
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      n = 0;
+    }
+    *count = n;
+  });
+}
+
+B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx) {
+  return guarded([&] {
+    B2M_REQUIRE(out_ctx, B2M_ERR_INVALID_ARGUMENT, "null out_ctx");
+    *out_ctx = nullptr;
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+      (void)cudaGetLastError();
+      b2m_throw(B2M_ERR_NO_DEVICE, "no CUDA device available");
+    }
+    B2M_REQUIRE(device >= 0 && device < n, B2M_ERR_NO_DEVICE, "device ordinal out of range");
+    cudaDeviceProp prop;
+    B2M_CUDA(cudaGetDeviceProperties(&prop, device));
+    B2M_REQUIRE(prop.major == 10 && prop.minor == 0, B2M_ERR_NO_DEVICE,
+                std::string("libb200mm is built for sm_100a (B200); device is ") + prop.name);
+    DeviceGuard dg(device);
+    b2m_ctx *ctx = new b2m_ctx();
+    ctx->device = device;
+    ctx->sm_count = prop.multiProcessorCount;
+    B2M_CUDA(cudaStreamCreateWithFlags(&ctx->own_stream, cudaStreamNonBlocking));
+    ctx->stream = ctx->own_stream;
+    B2M_CUDA(cudaDeviceGetDefaultMemPool(&ctx->pool, device));
+    uint64_t thr = UINT64_MAX;
+    B2M_CUDA(cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &thr));
+    B2M_CUDA(cudaEventCreate(&ctx->ev0));
+    B2M_CUDA(cudaEventCreate(&ctx->ev1));
+    B2M_CUDA(cudaMalloc(&ctx->dev_err, sizeof(int32_t)));
+    B2M_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(int32_t)));
+    *out_ctx = ctx;
+  });
+}
+
+B2M_API b2m_status b2m_shutdown(b2m_ctx *ctx) {
+  return guarded([&] {
+    if (!ctx) return;
+    DeviceGuard dg(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->scratch) cudaFreeAsync(ctx->scratch, ctx->own_stream);
+    cudaStreamSynchronize(ctx->own_stream);
+    if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    cudaFree(ctx->dev_err);
+    cudaEventDestroy(ctx->ev0);
+    cudaEventDestroy(ctx->ev1);
+    cudaStreamDestroy(ctx->own_stream);
+    delete ctx;
+  });
+}
+
+B2M_API b2m_status b2m_set_stream(b2m_ctx *ctx, void *stream) {
+  return guarded([&] {
+    check_ctx(ctx);
+    ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  });
+}
+
+B2M_API b2m_status b2m_synchronize(b2m_ctx *ctx) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+    check_device_error(ctx);
+  });
+}
+
+B2M_API b2m_status b2m_set_cancel_flag(b2m_ctx *ctx, const volatile int32_t *flag) {
+  return guarded([&] {
+    check_ctx(ctx);
+    ctx->cancel_flag = flag;
+  });
+}
+
+B2M_API b2m_status b2m_set_byte_budget(b2m_ctx *ctx, int64_t bytes) {
+  return guarded([&] {
+    check_ctx(ctx);
+    ctx->byte_budget = bytes;
+  });
+}
+
+B2M_API b2m_status b2m_enable_timing(b2m_ctx *ctx, int32_t on) {
+  return guarded([&] {
+    check_ctx(ctx);
+    ctx->timing = on != 0;
+  });
+}
+
+B2M_API b2m_status b2m_last_kernel_ms(b2m_ctx *ctx, float *ms) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(ms, B2M_ERR_INVALID_ARGUMENT, "null ms");
+    DeviceGuard dg(ctx->device);
+    if (ctx->timing_pending) {
+      B2M_CUDA(cudaEventSynchronize(ctx->ev1));
+      B2M_CUDA(cudaEventElapsedTime(&ctx->last_ms, ctx->ev0, ctx->ev1));
+      ctx->timing_pending = false;
+    }
+    *ms = ctx->last_ms;
+  });
+}
+
+// ---- tensors --------------------------------------------------------------
+
+B2M_API b2m_status b2m_tensor_alloc(b2m_ctx *ctx, int32_t dtype, const int64_t *shape, int32_t rank,
+                                    b2m_tensor **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && (shape || rank == 0), B2M_ERR_INVALID_ARGUMENT, "null argument");
+    DeviceGuard dg(ctx->device);
+    *out = new_tensor(ctx, dtype, shape, rank);
+  });
+}
+
+B2M_API b2m_status b2m_tensor_wrap(b2m_ctx *ctx, void *device_ptr, int32_t dtype, const int64_t *shape,
+                                   int32_t rank, b2m_tensor **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && (shape || rank == 0), B2M_ERR_INVALID_ARGUMENT, "null argument");
+    B2M_REQUIRE(rank >= 0 && rank <= B2M_MAX_RANK, B2M_ERR_INVALID_ARGUMENT, "tensor rank out of range");
+    B2M_REQUIRE(elem_size(dtype) > 0, B2M_ERR_INVALID_ARGUMENT, "unsupported tensor dtype");
+    b2m_tensor *t = new b2m_tensor();
+    t->ctx = ctx;
+    t->data = device_ptr;
+    t->dtype = dtype;
+    t->rank = rank;
+    int64_t numel = 1;
+    for (int i = 0; i < rank; i++) {
+      t->shape[i] = shape[i];
+      numel *= shape[i];
+    }
+    t->numel = numel;
+    t->owned = false;
+    if (numel > 0 && !device_ptr) {
+      delete t;
+      b2m_throw(B2M_ERR_INVALID_ARGUMENT, "null device pointer for a non-empty tensor");
+    }
+    *out = t;
+  });
+}
+
+B2M_API b2m_status b2m_tensor_upload(b2m_ctx *ctx, b2m_tensor *t, const void *host, int64_t bytes) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(t && (host || bytes == 0), B2M_ERR_INVALID_ARGUMENT, "null argument");
+    B2M_REQUIRE(bytes == tensor_bytes(t), B2M_ERR_INVALID_ARGUMENT, "upload size does not match the tensor");
+    DeviceGuard dg(ctx->device);
+    if (bytes) B2M_CUDA(cudaMemcpyAsync(t->data, host, (size_t)bytes, cudaMemcpyHostToDevice, ctx->stream));
+    B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+  });
+}
+
+B2M_API b2m_status b2m_tensor_download(b2m_ctx *ctx, const b2m_tensor *t, void *host, int64_t bytes) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(t && (host || bytes == 0), B2M_ERR_INVALID_ARGUMENT, "null argument");
+    B2M_REQUIRE(bytes == tensor_bytes(t), B2M_ERR_INVALID_ARGUMENT, "download size does not match the tensor");
+    DeviceGuard dg(ctx->device);
+    if (bytes) B2M_CUDA(cudaMemcpyAsync(host, t->data, (size_t)bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+    check_device_error(ctx);
+  });
+}
+
+B2M_API b2m_status b2m_tensor_free(b2m_tensor *t) {
+  return guarded([&] {
+    if (!t) return;
+    if (t->owned && t->data) {
+      DeviceGuard dg(t->ctx->device);
+      B2M_CUDA(cudaFreeAsync(t->data, t->ctx->stream));
+      t->ctx->live_bytes -= tensor_bytes(t);
+    }
+    delete t;
+  });
+}
+
+B2M_API b2m_status b2m_tensor_info(const b2m_tensor *t, int32_t *dtype, int32_t *rank, int64_t *shape,
+                                   void **device_ptr) {
+  return guarded([&] {
+    B2M_REQUIRE(t, B2M_ERR_INVALID_ARGUMENT, "null tensor");
+    if (dtype) *dtype = t->dtype;
+    if (rank) *rank = t->rank;
+    if (shape)
+      for (int i = 0; i < B2M_MAX_RANK; i++) shape[i] = i < t->rank ? t->shape[i] : 0;
+    if (device_ptr) *device_ptr = t->data;
+  });
+}
+
+// ---- weights --------------------------------------------------------------
+
+B2M_API b2m_status b2m_weight_prepack_f32(b2m_ctx *ctx, const float *host_b, int64_t rows, int64_t cols,
+                                          int32_t trans, b2m_weight **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && host_b && rows > 0 && cols > 0, B2M_ERR_INVALID_ARGUMENT, "Gemm prepack: bad arguments");
+    DeviceGuard dg(ctx->device);
+    const int64_t K = trans ? cols : rows, N = trans ? rows : cols;
+    std::vector<float> packed;
+    const float *src = host_b;
+    if (trans) {  // opTranspose(B, [1, 0]) once (onnx_graph.dart:2159-2161)
+      packed.resize((size_t)(K * N));
+      for (int64_t r = 0; r < rows; r++)
+        for (int64_t c = 0; c < cols; c++) packed[(size_t)(c * N + r)] = host_b[r * cols + c];
+      src = packed.data();
+    }
+    b2m_weight *w = new b2m_weight();
+    w->ctx = ctx;
+    w->kind = W_F32;
+    w->k = K;
+    w->n = N;
+    cudaError_t e = cudaMalloc(&w->f32, (size_t)(K * N * 4));
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      delete w;
+      b2m_throw(B2M_ERR_OUT_OF_MEMORY, "weight allocation failed");
+    }
+    B2M_CUDA(cudaMemcpy(w->f32, src, (size_t)(K * N * 4), cudaMemcpyHostToDevice));
+    *out = w;
+  });
+}
+
+B2M_API b2m_status b2m_weight_prepack_i8(b2m_ctx *ctx, const void *host_b, int32_t dtype, int64_t k, int64_t n,
+                                         b2m_weight **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && host_b && k > 0 && n > 0, B2M_ERR_INVALID_ARGUMENT, "MatMulInteger prepack: bad arguments");
+    B2M_REQUIRE(is_i8(dtype), B2M_ERR_INVALID_ARGUMENT, "MatMulInteger prepack: dtype must be uint8 or int8");
+    DeviceGuard dg(ctx->device);
+    const int64_t kpad = round_up(k, 64), npad = round_up(n, 128);
+    std::vector<int8_t> bt((size_t)(npad * kpad), 0);
+    std::vector<int32_t> cs((size_t)n, 0);
+    const uint8_t *src = static_cast<const uint8_t *>(host_b);
+    for (int64_t kk = 0; kk < k; kk++)
+      for (int64_t j = 0; j < n; j++) {
+        const uint8_t v = src[kk * n + j];
+        bt[(size_t)(j * kpad + kk)] = (int8_t)v;
+        cs[(size_t)j] += dtype == B2M_INT8 ? (int32_t)(int8_t)v : (int32_t)v;
+      }
+    b2m_weight *w = new b2m_weight();
+    w->ctx = ctx;
+    w->kind = W_I8;
+    w->k = k;
+    w->n = n;
+    w->i8.dtype = dtype;
+    w->i8.kpad = kpad;
+    w->i8.npad = npad;
+    B2M_CUDA(cudaMalloc(&w->i8.bt, bt.size()));
+    B2M_CUDA(cudaMalloc(&w->i8.colsum, cs.size() * 4));
+    B2M_CUDA(cudaMemcpy(w->i8.bt, bt.data(), bt.size(), cudaMemcpyHostToDevice));
+    B2M_CUDA(cudaMemcpy(w->i8.colsum, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    *out = w;
+  });
+}
+
+B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, const float *scales,
+                                            const void *zero_points, int32_t zp_dtype, int64_t k, int64_t n,
+                                            int32_t bits, int32_t block_size, b2m_weight **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && b_q && scales, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits prepack: null argument");
+    // Same checks, same order, same error classes as opMatMulNBits (:126-135).
+    if (bits != 4) b2m_throw(B2M_ERR_UNSUPPORTED, "MatMulNBits: only bits=4 supported, got " + std::to_string(bits));
+    if (k <= 0 || n <= 0 || block_size < 16 || (block_size & (block_size - 1)) != 0)
+      b2m_throw(B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: invalid K, N, block_size or input shape");
+    B2M_REQUIRE(zp_dtype == 0 || zp_dtype == B2M_UINT8 || zp_dtype == B2M_FLOAT, B2M_ERR_INVALID_ARGUMENT,
+                "MatMulNBits: invalid zero_points");
+    B2M_REQUIRE((zp_dtype == 0) == (zero_points == nullptr), B2M_ERR_INVALID_ARGUMENT,
+                "MatMulNBits: invalid zero_points");
+    DeviceGuard dg(ctx->device);
+    const int64_t nb = (k + block_size - 1) / block_size;
+    const int64_t blob = block_size / 2;
+    const int64_t zs = (nb + 1) / 2;
+    const int64_t kp = round_up(nb * block_size, 64);
+    const int64_t npad = round_up(n, 128);
+    const int64_t row = kp / 2;
+    std::vector<uint8_t> bq((size_t)(npad * row), 0);
+    std::vector<uint8_t> tmp((size_t)row);
+    for (int64_t c = 0; c < n; c++) {
+      std::fill(tmp.begin(), tmp.end(), 0);
+      std::memcpy(tmp.data(), b_q + c * nb * blob, (size_t)(nb * blob));
+      uint8_t *dst = &bq[(size_t)(c * row)];
+      for (int64_t g = 0; g < row / 16; g++) {
+        const uint8_t *o = &tmp[(size_t)(g * 16)];
+        uint8_t *d = dst + g * 16;
+        for (int t = 0; t < 4; t++) {
+          d[4 * t + 0] = o[2 * t];
+          d[4 * t + 1] = o[2 * t + 1];
+          d[4 * t + 2] = o[8 + 2 * t];
+          d[4 * t + 3] = o[9 + 2 * t];
+        }
+      }
+    }
+    std::vector<float> sc((size_t)(npad * nb), 0.f);
+    std::memcpy(sc.data(), scales, (size_t)(n * nb * 4));
+    b2m_weight *w = new b2m_weight();
+    w->ctx = ctx;
+    w->kind = W_NBITS;
+    w->k = k;
+    w->n = n;
+    NbitsWeight &W = w->nb;
+    W.block = block_size;
+    W.nblocks = nb;
+    W.zstride = zs;
+    W.kp = kp;
+    W.npad = npad;
+    try {
+      B2M_CUDA(cudaMalloc(&W.bq, bq.size()));
+      B2M_CUDA(cudaMemcpy(W.bq, bq.data(), bq.size(), cudaMemcpyHostToDevice));
+      B2M_CUDA(cudaMalloc(&W.scales, sc.size() * 4));
+      B2M_CUDA(cudaMemcpy(W.scales, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice));
+      if (zp_dtype == B2M_UINT8) {
+        std::vector<uint8_t> z((size_t)(npad * zs), 0);
+        std::memcpy(z.data(), zero_points, (size_t)(n * zs));
+        W.zp_kind = 1;
+        B2M_CUDA(cudaMalloc(&W.zp_u8, z.size()));
+        B2M_CUDA(cudaMemcpy(W.zp_u8, z.data(), z.size(), cudaMemcpyHostToDevice));
+      } else if (zp_dtype == B2M_FLOAT) {
+        std::vector<float> z((size_t)(npad * nb), 0.f);
+        std::memcpy(z.data(), zero_points, (size_t)(n * nb * 4));
+        W.zp_kind = 2;
+        B2M_CUDA(cudaMalloc(&W.zp_f32, z.size() * 4));
+        B2M_CUDA(cudaMemcpy(W.zp_f32, z.data(), z.size() * 4, cudaMemcpyHostToDevice));
+      }
+    } catch (...) {
+      cudaFree(W.bq);
+      cudaFree(W.scales);
+      cudaFree(W.zp_u8);
+      cudaFree(W.zp_f32);
+      delete w;
+      throw;
+    }
+    *out = w;
+  });
+}
+
+B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
+  return guarded([&] {
+    if (!w) return;
+    DeviceGuard dg(w->ctx->device);
+    cudaStreamSynchronize(w->ctx->stream);
+    cudaFree(w->f32);
+    cudaFree(w->i8.bt);
+    cudaFree(w->i8.colsum);
+    cudaFree(w->nb.bq);
+    cudaFree(w->nb.scales);
+    cudaFree(w->nb.zp_u8);
+    cudaFree(w->nb.zp_f32);
+    cudaFree(w->nb.wdeq);
+    delete w;
+  });
+}
+
+B2M_API b2m_status b2m_weight_info(const b2m_weight *w, int64_t *k, int64_t *n) {
+  return guarded([&] {
+    B2M_REQUIRE(w, B2M_ERR_INVALID_ARGUMENT, "null weight");
+    if (k) *k = w->k;
+    if (n) *n = w->n;
+  });
+}
+
+// ---- operators ------------------------------------------------------------
+
+B2M_API b2m_status b2m_matmul_f32(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b,
+                                  const b2m_weight *b_packed, int32_t mode, b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    matmul_f32_impl(ctx, a, b, b_packed, mode, y);
+  });
+}
+
+B2M_API b2m_status b2m_gemm_f32(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b,
+                                const b2m_weight *b_packed, const b2m_tensor *c, float alpha, float beta,
+                                int32_t trans_a, int32_t trans_b, int32_t mode, b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    gemm_f32_impl(ctx, a, b, b_packed, c, alpha, beta, trans_a, trans_b, mode, y);
+  });
+}
+
+B2M_API b2m_status b2m_matmul_integer(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b,
+                                      const b2m_weight *b_packed, const b2m_tensor *a_zp, const b2m_tensor *b_zp,
+                                      b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    integer_impl(ctx, a, b, b_packed, a_zp, b_zp, false, 0.0, 0, 0, 0, y);
+  });
+}
+
+B2M_API b2m_status b2m_qlinear_matmul(b2m_ctx *ctx, const b2m_tensor *a, float a_scale, const b2m_tensor *a_zp,
+                                      const b2m_tensor *b, const b2m_weight *b_packed, float b_scale,
+                                      const b2m_tensor *b_zp, float y_scale, int32_t y_zp, int32_t lo, int32_t hi,
+                                      b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    // Requant multiplier exactly as the reference: f32(aS*bS), then f32(/yS),
+    // each step rounded to float32 (onnx_qlinear_ops.dart:95-99).
+    float f = (float)((double)a_scale * (double)b_scale);
+    f = (float)((double)f / (double)y_scale);
+    integer_impl(ctx, a, b, b_packed, a_zp, b_zp, true, (double)f, y_zp, lo, hi, y);
+  });
+}
+
+B2M_API b2m_status b2m_matmul_nbits(b2m_ctx *ctx, const b2m_tensor *a, const b2m_weight *w, const b2m_tensor *bias,
+                                    int32_t mode, b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+    require_float(a, "MatMulNBits A");
+    if (a->rank < 1 || a->shape[a->rank - 1] != w->k)
+      b2m_throw(B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: invalid K, N, block_size or input shape");
+    if (bias && (bias->dtype != B2M_FLOAT || bias->rank != 1 || bias->numel != w->n))
+      b2m_throw(B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bias must be floating point [N]");
+    const int64_t m = a->numel / w->k;
+    std::vector<int64_t> oshape(a->shape, a->shape + a->rank - 1);
+    oshape.push_back(w->n);
+    check_cancel(ctx);
+    b2m_tensor *out = prepare_output(ctx, y, B2M_FLOAT, oshape);
+    OpTimer timer(ctx);
+    nbits_run(ctx, static_cast<const float *>(a->data), m, w, bias ? static_cast<const float *>(bias->data) : nullptr,
+              mode, static_cast<float *>(out->data));
+    timer.done();
+  });
+}
+
+B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m, const b2m_weight *w,
+                                        const float *bias, int32_t mode, float *y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(m >= 0 && (a || m == 0) && (y || m == 0), B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad pointers");
+    check_cancel(ctx);
+    OpTimer timer(ctx);
+    nbits_run(ctx, a, m, w, bias, mode, y);
+    timer.done();
+  });
+}
+
+B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int64_t m, const b2m_weight *w,
+                                         const float *bias_host, int32_t mode, float *y_host) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+    B2M_REQUIRE(m >= 0 && (a_host || m == 0) && (y_host || m == 0), B2M_ERR_INVALID_ARGUMENT,
+                "MatMulNBits: bad host pointers");
+    check_cancel(ctx);
+    if (m == 0) return;
+    const size_t abytes = (size_t)(m * w->k * 4), ybytes = (size_t)(m * w->n * 4), bbytes = (size_t)(w->n * 4);
+    Scratch sc(ctx, abytes + ybytes + bbytes + 1024);
+    float *da = static_cast<float *>(sc.take(abytes));
+    float *dy = static_cast<float *>(sc.take(ybytes));
+    float *db = bias_host ? static_cast<float *>(sc.take(bbytes)) : nullptr;
+    B2M_CUDA(cudaMemcpyAsync(da, a_host, abytes, cudaMemcpyHostToDevice, ctx->stream));
+    if (db) B2M_CUDA(cudaMemcpyAsync(db, bias_host, bbytes, cudaMemcpyHostToDevice, ctx->stream));
+    OpTimer timer(ctx);
+    nbits_run(ctx, da, m, w, db, mode, dy);
+    timer.done();
+    B2M_CUDA(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, ctx->stream));
+    B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+    check_device_error(ctx);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,229 @@
+"""CPU oracle for the MatMul-family hot path — TEST INFRASTRUCTURE ONLY.
+
+A numpy/ctypes front end for ``b2m_oracle.c``, the C restatement of the
+reference Dart arithmetic (``lib/src/gemm_kernel_simd.dart``,
+``lib/src/onnx_ops.dart:1710-1766, 2152-2173``,
+``lib/src/onnx_qlinear_ops.dart:19-228``). Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline / reference arm may
+import this package; the product library never links or calls it.
+
+Pinning: the C restatement is checked against the ORT-generated golden vectors
+the reference's own fixture-parity test replays (``tests/golden/``, made by
+``tests/golden/make_golden.py`` from ``test/fixtures/*``), with the reference's
+tolerances (``test/fixture_parity_test.dart:21, 65-108``): integer outputs
+exact, float outputs max|d| <= max(2e-5, 2e-5*max|ref|) and cosine > 0.999999.
+The Dart VM itself cannot run here (no Dart SDK), so bitwise identity with the
+Dart VM rests on the restated rounding rules, not on a Dart run.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "liboracle.so")
+_lib = None
+
+_f32p = ctypes.POINTER(ctypes.c_float)
+_i32p = ctypes.POINTER(ctypes.c_int32)
+_i64p = ctypes.POINTER(ctypes.c_int64)
+_u8p = ctypes.POINTER(ctypes.c_uint8)
+_i64 = ctypes.c_int64
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc, no GPU needed)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def _load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(
+        os.path.join(_HERE, "b2m_oracle.c")
+    ):
+        build()
+    lib = ctypes.CDLL(_LIB_PATH)
+    lib.orc_matmul_kernel.argtypes = [_f32p, _f32p, _f32p, _i64, _i64, _i64, _i64, ctypes.c_int]
+    lib.orc_matmul_kernel.restype = None
+    lib.orc_matmul.argtypes = [_f32p, _i64p, ctypes.c_int, _f32p, _i64p, ctypes.c_int, _f32p, ctypes.c_int]
+    lib.orc_matmul.restype = ctypes.c_int
+    lib.orc_gemm.argtypes = [_f32p, _i64, _i64, _f32p, _i64, _i64, _f32p, _i64p, ctypes.c_int,
+                             ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_int, _f32p, ctypes.c_int]
+    lib.orc_gemm.restype = ctypes.c_int
+    mmi = [_i32p, _i64, _i64, _i64, _i32p, _i64, _i64, _i32p, _i64, _i32p, _i64]
+    lib.orc_matmul_integer.argtypes = mmi + [_i64p, ctypes.c_int]
+    lib.orc_matmul_integer.restype = ctypes.c_int
+    lib.orc_qlinear_matmul.argtypes = mmi + [ctypes.c_float, ctypes.c_float, ctypes.c_float,
+                                             ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, _i64p, ctypes.c_int]
+    lib.orc_qlinear_matmul.restype = ctypes.c_int
+    lib.orc_qlinear_multiplier.argtypes = [ctypes.c_float] * 3
+    lib.orc_qlinear_multiplier.restype = ctypes.c_float
+    lib.orc_round_even.argtypes = [ctypes.c_double]
+    lib.orc_round_even.restype = ctypes.c_int64
+    lib.orc_matmul_nbits.argtypes = [_f32p, _i64, _i64, _u8p, _f32p, _u8p, _f32p, _f32p, _i64, _i64, _f32p, ctypes.c_int]
+    lib.orc_matmul_nbits.restype = ctypes.c_int
+    lib.orc_nbits_dequant.argtypes = [_u8p, _f32p, _u8p, _f32p, _i64, _i64, _i64, _f32p]
+    lib.orc_nbits_dequant.restype = None
+    _lib = lib
+    return lib
+
+
+def _p(arr, typ):
+    return None if arr is None else arr.ctypes.data_as(typ)
+
+
+def _c(arr, dtype):
+    return None if arr is None else np.ascontiguousarray(arr, dtype=dtype)
+
+
+def matmul_kernel(a, b, m, k, n, nthreads=1):
+    """``matmulKernel`` on fresh zeroed output (gemm_kernel_simd.dart:32)."""
+    a = _c(a, np.float32)
+    b = _c(b, np.float32)
+    out = np.zeros(m * n, np.float32)
+    _load().orc_matmul_kernel(_p(a, _f32p), _p(b, _f32p), _p(out, _f32p), m, k, n, n, nthreads)
+    return out.reshape(m, n)
+
+
+def _broadcast(a_batch, b_batch):
+    rank = max(len(a_batch), len(b_batch))
+    ap = [1] * (rank - len(a_batch)) + list(a_batch)
+    bp = [1] * (rank - len(b_batch)) + list(b_batch)
+    out = []
+    for x, y in zip(ap, bp):
+        if x == y or y == 1:
+            out.append(x)
+        elif x == 1:
+            out.append(y)
+        else:
+            raise ValueError(f"Cannot broadcast shapes {a_batch} and {b_batch}")
+    return out
+
+
+def matmul(a, b, nthreads=1):
+    """``opMatMul`` (onnx_ops.dart:1710): numpy-broadcast batched fp32 MatMul."""
+    a = _c(a, np.float32)
+    b = _c(b, np.float32)
+    out_shape = _broadcast(a.shape[:-2], b.shape[:-2]) + [a.shape[-2], b.shape[-1]]
+    out = np.zeros(int(np.prod(out_shape)), np.float32)
+    ash = np.array(a.shape, np.int64)
+    bsh = np.array(b.shape, np.int64)
+    rc = _load().orc_matmul(_p(a, _f32p), _p(ash, _i64p), a.ndim, _p(b, _f32p), _p(bsh, _i64p), b.ndim,
+                            _p(out, _f32p), nthreads)
+    if rc:
+        raise ValueError("oracle matmul: bad shapes")
+    return out.reshape(out_shape)
+
+
+def gemm(a, b, c=None, alpha=1.0, beta=1.0, transA=False, transB=False, nthreads=1):
+    """``opGemm`` (onnx_ops.dart:2152-2173)."""
+    a = _c(a, np.float32)
+    b = _c(b, np.float32)
+    c = _c(c, np.float32)
+    M = a.shape[1] if transA else a.shape[0]
+    N = b.shape[0] if transB else b.shape[1]
+    y = np.zeros(M * N, np.float32)
+    csh = None if c is None else np.array(c.shape, np.int64)
+    rc = _load().orc_gemm(_p(a, _f32p), a.shape[0], a.shape[1], _p(b, _f32p), b.shape[0], b.shape[1],
+                          _p(c, _f32p), _p(csh, _i64p), 0 if c is None else c.ndim,
+                          float(np.float32(alpha)), float(np.float32(beta)), int(bool(transA)),
+                          int(bool(transB)), _p(y, _f32p), nthreads)
+    if rc:
+        raise ValueError("oracle gemm: bad shapes")
+    return y.reshape(M, N)
+
+
+def _int_operands(a, b, a_zp, b_zp):
+    a = np.asarray(a)
+    b = np.asarray(b)
+    m, k = a.shape[-2], a.shape[-1]
+    n = b.shape[-1]
+    a_batch = a.size // (m * k) if m * k else 1
+    b_batch = b.size // (k * n) if k * n else 1
+    a32 = _c(a.reshape(-1), np.int32)
+    b32 = _c(b.reshape(-1), np.int32)
+    az = None if a_zp is None else _c(np.asarray(a_zp).reshape(-1), np.int32)
+    bz = None if b_zp is None else _c(np.asarray(b_zp).reshape(-1), np.int32)
+    batch_shape = list(a.shape[:-2]) if a_batch >= b_batch else list(b.shape[:-2])
+    return a32, b32, az, bz, m, k, n, a_batch, b_batch, batch_shape
+
+
+def matmul_integer(a, b, a_zp=None, b_zp=None, nthreads=1):
+    """``opMatMulInteger`` (onnx_qlinear_ops.dart:32-81); int64 result."""
+    a32, b32, az, bz, m, k, n, ab, bb, bs = _int_operands(a, b, a_zp, b_zp)
+    out = np.zeros(max(ab, bb) * m * n, np.int64)
+    rc = _load().orc_matmul_integer(_p(a32, _i32p), ab, m, k, _p(b32, _i32p), bb, n, _p(az, _i32p),
+                                    0 if az is None else az.size, _p(bz, _i32p), 0 if bz is None else bz.size,
+                                    _p(out, _i64p), nthreads)
+    if rc:
+        raise ValueError("oracle matmul_integer: unsupported zero points or batch")
+    return out.reshape(bs + [m, n])
+
+
+def qlinear_multiplier(a_scale, b_scale, y_scale):
+    return np.float32(_load().orc_qlinear_multiplier(float(a_scale), float(b_scale), float(y_scale)))
+
+
+def round_even(v):
+    return int(_load().orc_round_even(float(v)))
+
+
+def qlinear_matmul(a, a_scale, a_zp, b, b_scale, b_zp, y_scale, y_zp, lo, hi, nthreads=1):
+    """``opQLinearMatMul`` (onnx_qlinear_ops.dart:85-108); int64 result."""
+    a32, b32, az, bz, m, k, n, ab, bb, bs = _int_operands(a, b, a_zp, b_zp)
+    out = np.zeros(max(ab, bb) * m * n, np.int64)
+    yz = 0 if y_zp is None else int(np.asarray(y_zp).reshape(-1)[0])
+    rc = _load().orc_qlinear_matmul(_p(a32, _i32p), ab, m, k, _p(b32, _i32p), bb, n, _p(az, _i32p),
+                                    0 if az is None else az.size, _p(bz, _i32p), 0 if bz is None else bz.size,
+                                    float(np.float32(a_scale)), float(np.float32(b_scale)),
+                                    float(np.float32(y_scale)), yz, lo, hi, _p(out, _i64p), nthreads)
+    if rc:
+        raise ValueError("oracle qlinear_matmul: unsupported zero points or batch")
+    return out.reshape(bs + [m, n])
+
+
+def matmul_nbits(a, b_q, scales, zero_points, k, n, block_size, bias=None, nthreads=1):
+    """``opMatMulNBits`` (onnx_qlinear_ops.dart:115-228), bits=4.
+
+    ``zero_points`` may be packed uint8 (uint4 pairs), float32, or None."""
+    a = _c(a, np.float32)
+    m = a.size // k
+    bq = _c(np.asarray(b_q).reshape(-1), np.uint8)
+    sc = _c(np.asarray(scales).reshape(-1), np.float32)
+    zu = zf = None
+    if zero_points is not None:
+        zp = np.asarray(zero_points)
+        if zp.dtype == np.uint8:
+            zu = _c(zp.reshape(-1), np.uint8)
+        else:
+            zf = _c(zp.reshape(-1), np.float32)
+    bi = None if bias is None else _c(np.asarray(bias).reshape(-1), np.float32)
+    out = np.zeros(m * n, np.float32)
+    rc = _load().orc_matmul_nbits(_p(a, _f32p), m, k, _p(bq, _u8p), _p(sc, _f32p), _p(zu, _u8p), _p(zf, _f32p),
+                                  _p(bi, _f32p), n, block_size, _p(out, _f32p), nthreads)
+    if rc:
+        raise ValueError("oracle matmul_nbits: invalid K, N or block_size")
+    return out.reshape(list(a.shape[:-1]) + [n])
+
+
+def nbits_dequant(b_q, scales, zero_points, k, n, block_size):
+    """Float32 weights W[n, k] exactly as the reference's ``weight()`` makes them."""
+    bq = _c(np.asarray(b_q).reshape(-1), np.uint8)
+    sc = _c(np.asarray(scales).reshape(-1), np.float32)
+    zu = zf = None
+    if zero_points is not None:
+        zp = np.asarray(zero_points)
+        if zp.dtype == np.uint8:
+            zu = _c(zp.reshape(-1), np.uint8)
+        else:
+            zf = _c(zp.reshape(-1), np.float32)
+    w = np.zeros(n * k, np.float32)
+    _load().orc_nbits_dequant(_p(bq, _u8p), _p(sc, _f32p), _p(zu, _u8p), _p(zf, _f32p), k, n, block_size,
+                              _p(w, _f32p))
+    return w.reshape(n, k)

@@ -1,0 +1,475 @@
+/*
+ * b2m_oracle.c — CPU restatement of the reference's MatMul-family arithmetic.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the checker that the CUDA kernels in
+ * onnx_runtime_dart_b200/csrc are compared against; it is also the timed CPU
+ * baseline of bench.py. Nothing in the product library links or calls it.
+ *
+ * What it restates (reference = onnx_runtime_dart, pure Dart):
+ *   - matmulKernel            lib/src/gemm_kernel_simd.dart:32-243 (+ _gemv :459-614,
+ *                             _matmulSmallM :616-677, _matmul4x16Direct :244-389)
+ *   - opMatMul                lib/src/onnx_ops.dart:1710-1766
+ *   - opGemm                  lib/src/onnx_ops.dart:2152-2173
+ *   - opMatMulInteger         lib/src/onnx_qlinear_ops.dart:32-81
+ *   - opQLinearMatMul         lib/src/onnx_qlinear_ops.dart:85-108 (+ _roundEven :19-26)
+ *   - opMatMulNBits           lib/src/onnx_qlinear_ops.dart:115-228
+ *
+ * Numerics. Dart's Float32x4 lanes multiply and add with separate float32
+ * rounding (SSE mulps/addps, no FMA), and scalar Dart `double` code rounds in
+ * binary64 and only narrows to float32 on a Float32List store. This file is
+ * compiled with -O2 -ffp-contract=off -fno-fast-math on x86-64 (SSE math,
+ * FLT_EVAL_METHOD 0), so `float` expressions here round exactly like a
+ * Float32x4 lane and `double` expressions like a Dart double.
+ *
+ * Parallelism. The reference's only parallel strategy is the isolate pool's
+ * output-column split (lib/src/parallel_pool.dart:236-260); every column is
+ * computed by exactly the same sequence of operations whichever worker owns
+ * it, so results are bitwise independent of `nthreads`. The same split is
+ * used here (pthreads) so the CPU baseline can use all host cores.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------------- */
+/* fp32 GEMM: matmulKernel                                                    */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * One output column j of out[m x n] = a[m x k] . b[k x n] (row-major).
+ *
+ * Which accumulator the reference uses for a column depends only on (m, n, j):
+ *   m >= 4          every column is a Float32x4 lane (4x16 direct tile :244,
+ *                   narrow tile :391 or packed 4x8 panel with zero-filled tail
+ *                   lanes :100-242) -> float acc, k order.
+ *   m == 1 / m < 4  columns below n & ~3 are Float32x4 lanes (_gemvAligned
+ *                   :480, _gemvScalar :543-600, _matmulSmallM :616-663);
+ *                   the n % 4 tail columns use a `double` accumulator
+ *                   (_gemvScalar :601-608, _matmulSmallM :665-672).
+ * Panel / tile widths never change the k order (the file comment at :12-15
+ * and the pool's bitwise-equality contract rely on this), so one column can be
+ * produced independently of its neighbours.
+ */
+static void gemm_column(const float *a, int64_t lda, const float *b, int64_t ldb,
+                        float *out, int64_t ldo, int64_t m, int64_t k, int64_t n,
+                        int64_t j) {
+  const int double_tail = (m < 4) && (j >= (n & ~(int64_t)3));
+  for (int64_t i = 0; i < m; i++) {
+    const float *ar = a + i * lda;
+    if (double_tail) {
+      double acc = 0.0;
+      for (int64_t kk = 0; kk < k; kk++) acc += (double)ar[kk] * (double)b[kk * ldb + j];
+      out[i * ldo + j] = (float)acc;
+    } else {
+      float acc = 0.0f;
+      for (int64_t kk = 0; kk < k; kk++) {
+        const float p = ar[kk] * b[kk * ldb + j];
+        acc = acc + p;
+      }
+      out[i * ldo + j] = acc;
+    }
+  }
+}
+
+typedef struct {
+  const float *a;
+  const float *b;
+  float *out;
+  int64_t m, k, n, ldo, j0, j1;
+} gemm_job;
+
+static void *gemm_worker(void *p) {
+  gemm_job *g = (gemm_job *)p;
+  for (int64_t j = g->j0; j < g->j1; j++)
+    gemm_column(g->a, g->k, g->b, g->n, g->out, g->ldo, g->m, g->k, g->n, j);
+  return NULL;
+}
+
+/* Column slices per worker: the pool's split (parallel_pool.dart:236-239). */
+static void run_column_split(void *(*fn)(void *), void *jobs, size_t job_size, int64_t n,
+                             int nthreads, void (*set_range)(void *, int64_t, int64_t)) {
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > n) nthreads = (int)(n > 0 ? n : 1);
+  pthread_t tid[256];
+  if (nthreads > 256) nthreads = 256;
+  int64_t base = n / nthreads, rem = n % nthreads, start = 0;
+  for (int t = 0; t < nthreads; t++) {
+    int64_t cnt = base + (t < rem ? 1 : 0);
+    void *job = (char *)jobs + (size_t)t * job_size;
+    set_range(job, start, start + cnt);
+    start += cnt;
+  }
+  if (nthreads == 1) {
+    fn(jobs);
+    return;
+  }
+  for (int t = 0; t < nthreads; t++) pthread_create(&tid[t], NULL, fn, (char *)jobs + (size_t)t * job_size);
+  for (int t = 0; t < nthreads; t++) pthread_join(tid[t], NULL);
+}
+
+static void gemm_set_range(void *p, int64_t j0, int64_t j1) {
+  ((gemm_job *)p)->j0 = j0;
+  ((gemm_job *)p)->j1 = j1;
+}
+
+/* matmulKernel(a, aOff, b, bOff, out, outOff, m, k, n, outStride: ldo). */
+ORC_API void orc_matmul_kernel(const float *a, const float *b, float *out, int64_t m, int64_t k,
+                               int64_t n, int64_t ldo, int nthreads) {
+  gemm_job jobs[256];
+  for (int t = 0; t < 256; t++) {
+    jobs[t].a = a;
+    jobs[t].b = b;
+    jobs[t].out = out;
+    jobs[t].m = m;
+    jobs[t].k = k;
+    jobs[t].n = n;
+    jobs[t].ldo = ldo;
+  }
+  run_column_split(gemm_worker, jobs, sizeof(gemm_job), n, nthreads, gemm_set_range);
+}
+
+/* ------------------------------------------------------------------------- */
+/* opMatMul: numpy-broadcast batches (onnx_ops.dart:1710-1766)                */
+/* ------------------------------------------------------------------------- */
+
+/* _flattenBroadcast (onnx_ops.dart:57-70): flat batch index of src for the
+ * output batch coordinates (leading dims of size 1 broadcast). */
+static int64_t flatten_broadcast(const int64_t *out_coords, int out_rank, const int64_t *src,
+                                 int src_rank) {
+  int64_t flat = 0, stride = 1;
+  for (int d = src_rank - 1; d >= 0; d--) {
+    int od = d + (out_rank - src_rank);
+    int64_t coord = src[d] == 1 ? 0 : out_coords[od];
+    flat += coord * stride;
+    stride *= src[d];
+  }
+  return flat;
+}
+
+/* Returns 0 on success, -1 if the batch shapes do not broadcast. */
+ORC_API int orc_matmul(const float *a, const int64_t *a_shape, int a_rank, const float *b,
+                       const int64_t *b_shape, int b_rank, float *out, int nthreads) {
+  if (a_rank < 2 || b_rank < 2 || a_rank > 16 || b_rank > 16) return -1;
+  const int64_t m = a_shape[a_rank - 2], k = a_shape[a_rank - 1];
+  const int64_t n = b_shape[b_rank - 1];
+  if (b_shape[b_rank - 2] != k) return -1;
+  const int ab = a_rank - 2, bb = b_rank - 2;
+  const int rank = ab > bb ? ab : bb;
+  int64_t out_batch[16], ap[16], bp[16];
+  for (int d = 0; d < rank; d++) {
+    ap[d] = d < rank - ab ? 1 : a_shape[d - (rank - ab)];
+    bp[d] = d < rank - bb ? 1 : b_shape[d - (rank - bb)];
+    if (ap[d] == bp[d]) out_batch[d] = ap[d];
+    else if (ap[d] == 1) out_batch[d] = bp[d];
+    else if (bp[d] == 1) out_batch[d] = ap[d];
+    else return -1;
+  }
+  int64_t batch_count = 1, b_count = 1;
+  for (int d = 0; d < rank; d++) batch_count *= out_batch[d];
+  for (int d = 0; d < bb; d++) b_count *= b_shape[d];
+  if (batch_count * m * n > 0) memset(out, 0, sizeof(float) * (size_t)(batch_count * m * n));
+  /* Shared 2-D B: collapse every batch of A into one GEMM (:1728-1735). This
+   * changes m (and so the kernel variant) and is part of the numerics. */
+  if (batch_count > 1 && b_count == 1) {
+    orc_matmul_kernel(a, b, out, batch_count * m, k, n, n, nthreads);
+    return 0;
+  }
+  int64_t coords[16];
+  for (int64_t batch = 0; batch < batch_count; batch++) {
+    int64_t rem = batch;
+    for (int d = rank - 1; d >= 0; d--) {
+      int64_t dim = out_batch[d] == 0 ? 1 : out_batch[d];
+      coords[d] = rem % dim;
+      rem /= dim;
+    }
+    int64_t af = flatten_broadcast(coords, rank, a_shape, ab);
+    int64_t bf = flatten_broadcast(coords, rank, b_shape, bb);
+    orc_matmul_kernel(a + af * m * k, b + bf * k * n, out + batch * m * n, m, k, n, n, nthreads);
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* opGemm (onnx_ops.dart:2152-2173; prepack onnx_graph.dart:2156-2161)        */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * y[M x N] = alpha * A' . B' + beta * C, A' = transA ? A^T : A (A stored
+ * [K x M] when transposed), B' likewise. The transposes are plain copies
+ * (opTranspose), the product goes through opMatMul (2-D, no batches), alpha
+ * multiplies in place only when != 1 (:2164-2168), beta scales C only when
+ * != 1 (:2170), and the add is opAdd with numpy broadcasting of C against
+ * [M, N] (C shape c_shape/c_rank; c == NULL means no C input).
+ */
+ORC_API int orc_gemm(const float *a, int64_t a_rows, int64_t a_cols, const float *b, int64_t b_rows,
+                     int64_t b_cols, const float *c, const int64_t *c_shape, int c_rank, float alpha,
+                     float beta, int trans_a, int trans_b, float *y, int nthreads) {
+  const int64_t M = trans_a ? a_cols : a_rows, K = trans_a ? a_rows : a_cols;
+  const int64_t K2 = trans_b ? b_cols : b_rows, N = trans_b ? b_rows : b_cols;
+  if (K != K2) return -1;
+  float *at = NULL, *bt = NULL;
+  const float *ap = a, *bp = b;
+  if (trans_a) {
+    at = (float *)malloc(sizeof(float) * (size_t)(M * K + 1));
+    for (int64_t i = 0; i < M; i++)
+      for (int64_t kk = 0; kk < K; kk++) at[i * K + kk] = a[kk * a_cols + i];
+    ap = at;
+  }
+  if (trans_b) {
+    bt = (float *)malloc(sizeof(float) * (size_t)(K * N + 1));
+    for (int64_t kk = 0; kk < K; kk++)
+      for (int64_t j = 0; j < N; j++) bt[kk * N + j] = b[j * b_cols + kk];
+    bp = bt;
+  }
+  int64_t as[2] = {M, K}, bs[2] = {K, N};
+  orc_matmul(ap, as, 2, bp, bs, 2, y, nthreads);
+  free(at);
+  free(bt);
+  if (alpha != 1.0f)
+    for (int64_t i = 0; i < M * N; i++) y[i] = y[i] * alpha;
+  if (c == NULL) return 0;
+  /* C broadcast onto [M, N]: rank <= 2, each dim 1 or equal. */
+  int64_t cr = 1, cc = 1;
+  if (c_rank == 1) cc = c_shape[0];
+  else if (c_rank == 2) {
+    cr = c_shape[0];
+    cc = c_shape[1];
+  } else if (c_rank != 0) return -1;
+  if ((cr != 1 && cr != M) || (cc != 1 && cc != N)) return -1;
+  for (int64_t i = 0; i < M; i++)
+    for (int64_t j = 0; j < N; j++) {
+      float cv = c[(cr == 1 ? 0 : i) * cc + (cc == 1 ? 0 : j)];
+      if (beta != 1.0f) cv = cv * beta;
+      y[i * N + j] = y[i * N + j] + cv;
+    }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* opMatMulInteger (onnx_qlinear_ops.dart:32-81)                              */
+/* ------------------------------------------------------------------------- */
+
+typedef struct {
+  const int32_t *a, *b, *azp, *bzp;
+  int64_t *out;
+  int64_t batch, a_batch, b_batch, m, k, n, azp_len, bzp_len, j0, j1;
+} mmi_job;
+
+static void *mmi_worker(void *p) {
+  mmi_job *g = (mmi_job *)p;
+  const int64_t m = g->m, k = g->k, n = g->n;
+  /* Zero-point rules (:41-44): scalar applies everywhere; a length-M (A) or
+   * length-N (B) vector applies per row / column unless M (N) is 1. */
+  const int64_t az = (g->azp && g->azp_len == 1) ? g->azp[0] : 0;
+  const int32_t *az_row = (g->azp && g->azp_len == m && m != 1) ? g->azp : NULL;
+  const int64_t bz = (g->bzp && g->bzp_len == 1) ? g->bzp[0] : 0;
+  const int32_t *bz_col = (g->bzp && g->bzp_len == n && n != 1) ? g->bzp : NULL;
+  for (int64_t bb = 0; bb < g->batch; bb++) {
+    const int64_t a_off = (g->a_batch == 1 ? 0 : bb) * m * k;
+    const int64_t b_off = (g->b_batch == 1 ? 0 : bb) * k * n;
+    const int64_t o_off = bb * m * n;
+    for (int64_t i = 0; i < m; i++) {
+      const int64_t azi = az_row ? az_row[i] : az;
+      for (int64_t kk = 0; kk < k; kk++) {
+        const int64_t av = (int64_t)g->a[a_off + i * k + kk] - azi;
+        if (av == 0) continue; /* exact skip (:61-62) */
+        const int32_t *brow = g->b + b_off + kk * n;
+        int64_t *orow = g->out + o_off + i * n;
+        for (int64_t j = g->j0; j < g->j1; j++)
+          orow[j] += av * ((int64_t)brow[j] - (bz_col ? (int64_t)bz_col[j] : bz));
+      }
+    }
+  }
+  return NULL;
+}
+
+static void mmi_set_range(void *p, int64_t j0, int64_t j1) {
+  ((mmi_job *)p)->j0 = j0;
+  ((mmi_job *)p)->j1 = j1;
+}
+
+/* Values of a and b are passed widened to int32 (uint8 / int8 sources).
+ * a is [a_batch, m, k], b is [b_batch, k, n]; out is [batch, m, n] int64.
+ * Returns -1 on a zero-point shape the reference rejects (:37-40) or a batch
+ * mismatch (:47-49). */
+ORC_API int orc_matmul_integer(const int32_t *a, int64_t a_batch, int64_t m, int64_t k,
+                               const int32_t *b, int64_t b_batch, int64_t n, const int32_t *azp,
+                               int64_t azp_len, const int32_t *bzp, int64_t bzp_len, int64_t *out,
+                               int nthreads) {
+  if ((azp && azp_len != 1 && azp_len != m) || (bzp && bzp_len != 1 && bzp_len != n)) return -1;
+  const int64_t batch = a_batch > b_batch ? a_batch : b_batch;
+  if ((a_batch != batch && a_batch != 1) || (b_batch != batch && b_batch != 1)) return -1;
+  if (batch * m * n > 0) memset(out, 0, sizeof(int64_t) * (size_t)(batch * m * n));
+  mmi_job jobs[256];
+  for (int t = 0; t < 256; t++) {
+    mmi_job g = {a, b, azp, bzp, out, batch, a_batch, b_batch, m, k, n, azp_len, bzp_len, 0, 0};
+    jobs[t] = g;
+  }
+  run_column_split(mmi_worker, jobs, sizeof(mmi_job), n, nthreads, mmi_set_range);
+  return 0;
+}
+
+/* _roundEven (onnx_qlinear_ops.dart:19-26): ties go to the even integer. */
+static int64_t round_even(double v) {
+  const double f = floor(v);
+  const double frac = v - f;
+  if (frac > 0.5) return (int64_t)f + 1;
+  if (frac < 0.5) return (int64_t)f;
+  const int64_t i = (int64_t)f;
+  return (i % 2 == 0) ? i : i + 1;
+}
+
+ORC_API int64_t orc_round_even(double v) { return round_even(v); }
+
+/* QLinearMatMul requant multiplier (:95-99): each step rounds to float32. */
+ORC_API float orc_qlinear_multiplier(float a_scale, float b_scale, float y_scale) {
+  float f = (float)((double)a_scale * (double)b_scale);
+  f = (float)((double)f / (double)y_scale);
+  return f;
+}
+
+/* opQLinearMatMul (:85-108): per-tensor scales; yzp scalar (or absent). */
+ORC_API int orc_qlinear_matmul(const int32_t *a, int64_t a_batch, int64_t m, int64_t k,
+                               const int32_t *b, int64_t b_batch, int64_t n, const int32_t *azp,
+                               int64_t azp_len, const int32_t *bzp, int64_t bzp_len, float a_scale,
+                               float b_scale, float y_scale, int32_t y_zp, int32_t lo, int32_t hi,
+                               int64_t *out, int nthreads) {
+  int rc = orc_matmul_integer(a, a_batch, m, k, b, b_batch, n, azp, azp_len, bzp, bzp_len, out,
+                              nthreads);
+  if (rc) return rc;
+  const double mult = (double)orc_qlinear_multiplier(a_scale, b_scale, y_scale);
+  const int64_t batch = a_batch > b_batch ? a_batch : b_batch;
+  for (int64_t i = 0; i < batch * m * n; i++) {
+    const float f = (float)((double)out[i] * mult); /* f32[0] = ai[i] * mult */
+    int64_t q = round_even((double)f) + y_zp;
+    out[i] = q < lo ? lo : (q > hi ? hi : q);
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* opMatMulNBits (onnx_qlinear_ops.dart:115-228)                              */
+/* ------------------------------------------------------------------------- */
+
+typedef struct {
+  const float *a;
+  const uint8_t *bq;
+  const float *scales;
+  const uint8_t *zp_u8; /* packed uint4 zero points, or NULL */
+  const float *zp_f32;  /* float zero points, or NULL */
+  const float *bias;    /* [n] or NULL */
+  float *out;
+  int64_t m, k, n, block, j0, j1;
+} nbits_job;
+
+/* weight(col, kk) (:177-191): nibble q (low nibble for even kk), zero point
+ * from the packed nibble (low for even block), the float zp, or 8; the
+ * product is formed in double and stored through a Float32List. */
+static inline float nbits_weight(const nbits_job *g, int64_t col, int64_t kk) {
+  const int64_t nblocks = (g->k + g->block - 1) / g->block;
+  const int64_t blob = g->block / 2;
+  const int64_t blk = kk / g->block;
+  const uint8_t byte = g->bq[(col * nblocks + blk) * blob + (kk % g->block) / 2];
+  const int q = (kk & 1) == 0 ? (byte & 15) : (byte >> 4);
+  double zp = 8.0;
+  if (g->zp_u8) {
+    const int64_t zstride = (nblocks + 1) / 2;
+    const uint8_t z = g->zp_u8[col * zstride + blk / 2];
+    zp = (double)((blk & 1) == 0 ? (z & 15) : (z >> 4));
+  } else if (g->zp_f32) {
+    zp = (double)g->zp_f32[col * nblocks + blk];
+  }
+  return (float)(((double)q - zp) * (double)g->scales[col * nblocks + blk]);
+}
+
+static void *nbits_worker(void *p) {
+  nbits_job *g = (nbits_job *)p;
+  const int64_t m = g->m, k = g->k, n = g->n;
+  if (m == 1) {
+    /* Token decode (:194-205): double accumulation straight from packed bytes. */
+    for (int64_t col = g->j0; col < g->j1; col++) {
+      double sum = 0.0;
+      for (int64_t kk = 0; kk < k; kk++) sum += (double)g->a[kk] * (double)nbits_weight(g, col, kk);
+      g->out[col] = (float)(sum + (g->bias ? (double)g->bias[col] : 0.0));
+    }
+    return NULL;
+  }
+  /* Prefill (:208-226): dequantize 32-column tiles to float, run matmulKernel
+   * on [m x k] . [k x columns], then add bias in double. Threads own whole
+   * tiles (j0/j1 are tile-aligned). */
+  const int64_t tile_cols = 32;
+  float *bt = (float *)malloc(sizeof(float) * (size_t)(k * tile_cols));
+  float *tile = (float *)malloc(sizeof(float) * (size_t)(m * tile_cols));
+  for (int64_t start = g->j0; start < g->j1; start += tile_cols) {
+    const int64_t columns = n - start < tile_cols ? n - start : tile_cols;
+    for (int64_t col = 0; col < columns; col++)
+      for (int64_t kk = 0; kk < k; kk++) bt[kk * columns + col] = nbits_weight(g, start + col, kk);
+    memset(tile, 0, sizeof(float) * (size_t)(m * columns));
+    for (int64_t j = 0; j < columns; j++) gemm_column(g->a, k, bt, columns, tile, columns, m, k, columns, j);
+    for (int64_t row = 0; row < m; row++)
+      for (int64_t col = 0; col < columns; col++)
+        g->out[row * n + start + col] =
+            (float)((double)tile[row * columns + col] + (g->bias ? (double)g->bias[start + col] : 0.0));
+  }
+  free(bt);
+  free(tile);
+  return NULL;
+}
+
+static void nbits_set_range(void *p, int64_t j0, int64_t j1) {
+  ((nbits_job *)p)->j0 = j0;
+  ((nbits_job *)p)->j1 = j1;
+}
+
+/* a: [m, k] fp32; bq: [n, ceil(k/block), block/2]; scales: [n*nblocks];
+ * zp_u8: [n * ceil(nblocks/2)] or NULL; zp_f32: [n*nblocks] or NULL;
+ * bias: [n] or NULL; out: [m, n]. Shape validation is the caller's (the host
+ * layer mirrors :126-166). */
+ORC_API int orc_matmul_nbits(const float *a, int64_t m, int64_t k, const uint8_t *bq,
+                             const float *scales, const uint8_t *zp_u8, const float *zp_f32,
+                             const float *bias, int64_t n, int64_t block, float *out, int nthreads) {
+  if (k <= 0 || n <= 0 || block < 16 || (block & (block - 1)) != 0) return -1;
+  if (m == 0) return 0;
+  nbits_job jobs[256];
+  for (int t = 0; t < 256; t++) {
+    nbits_job g = {a, bq, scales, zp_u8, zp_f32, bias, out, m, k, n, block, 0, 0};
+    jobs[t] = g;
+  }
+  if (m == 1) {
+    run_column_split(nbits_worker, jobs, sizeof(nbits_job), n, nthreads, nbits_set_range);
+    return 0;
+  }
+  /* Split whole 32-column tiles across workers. */
+  const int64_t tiles = (n + 31) / 32;
+  if (nthreads < 1) nthreads = 1;
+  if (nthreads > tiles) nthreads = (int)tiles;
+  if (nthreads > 256) nthreads = 256;
+  pthread_t tid[256];
+  int64_t base = tiles / nthreads, rem = tiles % nthreads, t0 = 0;
+  for (int t = 0; t < nthreads; t++) {
+    int64_t cnt = base + (t < rem ? 1 : 0);
+    jobs[t].j0 = t0 * 32;
+    jobs[t].j1 = (t0 + cnt) * 32 < n ? (t0 + cnt) * 32 : n;
+    t0 += cnt;
+  }
+  if (nthreads == 1) {
+    nbits_worker(&jobs[0]);
+    return 0;
+  }
+  for (int t = 0; t < nthreads; t++) pthread_create(&tid[t], NULL, nbits_worker, &jobs[t]);
+  for (int t = 0; t < nthreads; t++) pthread_join(tid[t], NULL);
+  return 0;
+}
+
+/* Dequantized weight matrix W[n, k] (float32, the values weight() returns);
+ * used by tests to build a float reference for the fast tensor-core mode. */
+ORC_API void orc_nbits_dequant(const uint8_t *bq, const float *scales, const uint8_t *zp_u8,
+                               const float *zp_f32, int64_t k, int64_t n, int64_t block, float *w) {
+  nbits_job g = {NULL, bq, scales, zp_u8, zp_f32, NULL, NULL, 0, k, n, block, 0, 0};
+  for (int64_t col = 0; col < n; col++)
+    for (int64_t kk = 0; kk < k; kk++) w[col * k + kk] = nbits_weight(&g, col, kk);
+}

@@ -1,0 +1,137 @@
+"""CPU-only checks of the C ABI library and the host-side operator layer.
+
+No compute runs here: the library must load without a GPU, export every
+entry point include/b2m.h declares, report "no device" cleanly, and the
+Python mirror of the reference's operator validation must raise the same
+error classes as the reference (onnx_qlinear_ops.dart:126-166) before any
+device work.
+"""
+import ctypes
+import os
+import re
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_symbols():
+    txt = open(os.path.join(ROOT, "include", "b2m.h")).read()
+    return sorted(set(re.findall(r"B2M_API\s+[^;(]*?\b(b2m_\w+)\s*\(", txt)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from onnx_runtime_dart_b200 import _native, build
+
+    if not os.path.exists(build.LIB):
+        build.build()
+    return _native.load()
+
+
+def test_header_symbols_all_exported(lib):
+    syms = header_symbols()
+    assert len(syms) >= 25
+    for s in syms:
+        assert hasattr(lib, s), f"libb200mm.so does not export {s}"
+
+
+def test_python_binding_covers_header(lib):
+    from onnx_runtime_dart_b200 import _native
+
+    assert sorted(_native.SIGNATURES) == header_symbols()
+
+
+def test_abi_version_and_no_device(lib):
+    from onnx_runtime_dart_b200 import _native
+
+    assert lib.b2m_abi_version() == 1
+    import torch
+
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    n = ctypes.c_int32(-1)
+    assert lib.b2m_device_count(ctypes.byref(n)) == 0
+    assert n.value == 0
+    h = ctypes.c_void_p()
+    st = lib.b2m_init(0, ctypes.byref(h))
+    assert st == _native.B2M_ERR_NO_DEVICE
+    assert b"no CUDA device" in lib.b2m_last_error()
+    with pytest.raises(_native.NoDeviceError):
+        _native.check(st)
+
+
+def test_null_arguments_are_rejected_not_crashing(lib):
+    from onnx_runtime_dart_b200 import _native
+
+    assert lib.b2m_matmul_f32(None, None, None, None, 0, None) == _native.B2M_ERR_INVALID_ARGUMENT
+    assert lib.b2m_tensor_free(None) == 0
+    assert lib.b2m_weight_free(None) == 0
+    assert lib.b2m_shutdown(None) == 0
+    assert lib.b2m_tensor_info(None, None, None, None, None) == _native.B2M_ERR_INVALID_ARGUMENT
+
+
+def test_nbits_prepack_validation_order(lib):
+    # bits check first (UnsupportedError), then K/N/block (ArgumentError) —
+    # the reference's order (onnx_qlinear_ops.dart:126-136). Context is NULL:
+    # the library rejects it before any device call.
+    from onnx_runtime_dart_b200 import _native
+
+    assert lib.b2m_weight_prepack_nbits(None, None, None, None, 0, 64, 8, 4, 32, None) == \
+        _native.B2M_ERR_INVALID_ARGUMENT
+
+
+def _nbits_args(k=64, n=8, block=32):
+    nb = (k + block - 1) // block
+    return (np.zeros((n, nb, block // 2), np.uint8), np.ones((n, nb), np.float32),
+            np.zeros((n, (nb + 1) // 2), np.uint8))
+
+
+def test_validate_nbits_mirrors_reference():
+    from onnx_runtime_dart_b200 import ArgumentError, UnsupportedError, validate_nbits
+
+    bq, sc, zp = _nbits_args()
+    validate_nbits([2, 64], np.float32, bq, sc, zp, None, 64, 8, 4, 32)
+    with pytest.raises(UnsupportedError, match="only bits=4"):
+        validate_nbits([2, 64], np.float32, bq, sc, zp, None, 64, 8, 8, 32)
+    for k, n, blk, shape in [(0, 8, 32, [2, 0]), (64, 0, 32, [2, 64]), (64, 8, 8, [2, 64]),
+                             (64, 8, 48, [2, 64]), (64, 8, 32, [2, 63]), (64, 8, 32, [])]:
+        with pytest.raises(ArgumentError, match="invalid K, N, block_size or input shape"):
+            validate_nbits(shape, np.float32, bq, sc, zp, None, k, n, 4, blk)
+    with pytest.raises(ArgumentError, match="invalid packed weights or scales"):
+        validate_nbits([2, 64], np.float32, bq.astype(np.int8), sc, zp, None, 64, 8, 4, 32)
+    with pytest.raises(ArgumentError, match="invalid packed weights or scales"):
+        validate_nbits([2, 64], np.int32, bq, sc, zp, None, 64, 8, 4, 32)
+    with pytest.raises(ArgumentError, match="invalid packed weights or scales"):
+        validate_nbits([2, 64], np.float32, bq, sc.reshape(2, 8), zp, None, 64, 8, 4, 32)
+    with pytest.raises(ArgumentError, match="invalid zero_points"):
+        validate_nbits([2, 64], np.float32, bq, sc, zp[:5], None, 64, 8, 4, 32)
+    with pytest.raises(ArgumentError, match="invalid zero_points"):
+        validate_nbits([2, 64], np.float32, bq, sc, np.zeros((8, 1), np.int32), None, 64, 8, 4, 32)
+    validate_nbits([2, 64], np.float32, bq, sc, np.zeros((8, 2), np.float32), None, 64, 8, 4, 32)
+    with pytest.raises(ArgumentError, match="bias must be floating point"):
+        validate_nbits([2, 64], np.float32, bq, sc, zp, np.zeros(8, np.int32), 64, 8, 4, 32)
+    with pytest.raises(ArgumentError, match="bias must be floating point"):
+        validate_nbits([2, 64], np.float32, bq, sc, zp, np.zeros((1, 8), np.float32), 64, 8, 4, 32)
+
+
+def test_dispatch_rejects_g_idx_before_device_work():
+    from onnx_runtime_dart_b200 import UnsupportedError
+    from onnx_runtime_dart_b200.dispatch import GpuDispatch
+
+    bq, sc, zp = _nbits_args()
+    d = GpuDispatch(ctx=None, initializers={"B": bq})
+    with pytest.raises(UnsupportedError, match="g_idx"):
+        d.dispatch("MatMulNBits", ["A", "B", "S", "", "G"], [np.zeros((1, 64), np.float32), bq, sc, None, None],
+                   {"K": 64, "N": 8, "block_size": 32})
+    assert d.dispatch("Relu", ["x"], [np.zeros(2)], {}) is None
+
+
+def test_product_path_has_no_oracle_or_cpu_fallback():
+    # The product package must not import the oracle (test infrastructure).
+    pkg = os.path.join(ROOT, "onnx_runtime_dart_b200")
+    for f in os.listdir(pkg):
+        if f.endswith(".py"):
+            src = open(os.path.join(pkg, f)).read()
+            assert not re.search(r"^\s*(import|from)\s+oracle\b", src, re.M), f

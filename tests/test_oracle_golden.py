@@ -1,0 +1,127 @@
+"""Pins the CPU oracle (oracle/b2m_oracle.c) to the reference's golden vectors.
+
+The vectors are the reference's ORT-generated fixtures (tests/golden/*.json,
+made by tests/golden/make_golden.py from test/fixtures/*) and its hand-computed
+known answers (test/gemm_prepack_test.dart:15-55,
+test/compact_tensor_test.dart:90-99, test/onnx_runtime_dart_test.dart:48-70).
+Tolerances are the reference test's own. CPU only.
+"""
+import numpy as np
+import pytest
+
+import oracle
+from tests.conftest import assert_fixture_close, golden_cases, load_golden
+
+
+def run_oracle(g):
+    op, x, at = g["op_type"], g["arrays"], g["attrs"]
+    if op == "MatMul":
+        return oracle.matmul(x[0], x[1])
+    if op == "Gemm":
+        return oracle.gemm(x[0], x[1], x[2] if len(x) > 2 else None, alpha=at.get("alpha", 1.0),
+                           beta=at.get("beta", 1.0), transA=bool(at.get("transA", 0)),
+                           transB=bool(at.get("transB", 0)))
+    if op == "MatMulInteger":
+        return oracle.matmul_integer(x[0], x[1], x[2] if len(x) > 2 else None, x[3] if len(x) > 3 else None)
+    if op == "QLinearMatMul":
+        # lo/hi from the y_zero_point's element type (onnx_graph.dart:2903, 2913-2914)
+        int8 = g["inputs"][7]["tensor"]["elem_type"] == 3
+        return oracle.qlinear_matmul(x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7],
+                                     -128 if int8 else 0, 127 if int8 else 255)
+    if op == "MatMulNBits":
+        return oracle.matmul_nbits(x[0], x[1], x[2], x[3] if len(x) > 3 else None, at["K"], at["N"],
+                                   at["block_size"], bias=x[5] if len(x) > 5 else None)
+    pytest.skip(f"{op} is not a MatMul-family op")
+
+
+@pytest.mark.parametrize("case", [c for c in golden_cases() if not c.startswith("dynamic")])
+def test_oracle_matches_reference_fixture(case):
+    g = load_golden(case)
+    got = run_oracle(g)
+    assert_fixture_close(got, g["expected_arrays"][g["outputs"][0]], case)
+
+
+def test_gemm_prepack_known_answer():
+    # test/gemm_prepack_test.dart:15-55: X[2x3] . W[4x3]^T + C[4]
+    w = np.arange(1, 13, dtype=np.float32).reshape(4, 3)
+    c = np.array([10, 20, 30, 40], np.float32)
+    x = np.arange(1, 7, dtype=np.float32).reshape(2, 3)
+    y = oracle.gemm(x, w, c, transB=True)
+    assert y.ravel().tolist() == [24.0, 52.0, 80.0, 108.0, 42.0, 97.0, 152.0, 207.0]
+
+
+def test_matmul_integer_compact_known_answer():
+    # test/compact_tensor_test.dart:90-99
+    a = np.array([[10, 130, 250]], np.uint8)
+    b = np.array([-1, 2, 3, -4, 5, 6], np.int8).reshape(3, 2)
+    assert oracle.matmul_integer(a, b, np.array(10), np.array(1)).ravel().tolist() == [1200, 600]
+
+
+def test_matmul_identity_known_answer():
+    # test/onnx_runtime_dart_test.dart:48-70
+    x = np.array([[5, 6], [7, 8]], np.float32)
+    assert oracle.matmul(x, np.eye(2, dtype=np.float32)).ravel().tolist() == [5, 6, 7, 8]
+
+
+@pytest.mark.parametrize("m", range(1, 7))
+def test_matmul_kernel_small_shapes_vs_double(m):
+    # test/gemm_kernel_test.dart:45-60: every m,k,n in 1..6 within 1e-5 of a
+    # double-accumulating naive loop.
+    rng = np.random.default_rng(11)
+    for k in range(1, 7):
+        for n in range(1, 7):
+            a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+            b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+            got = oracle.matmul_kernel(a, b, m, k, n)
+            want = (a.astype(np.float64) @ b.astype(np.float64)).astype(np.float32)
+            np.testing.assert_allclose(got, want, atol=1e-5, rtol=0)
+
+
+@pytest.mark.parametrize("mkn", [(1, 384, 384), (33, 65, 17), (7, 128, 5), (128, 64, 128), (5, 1, 9),
+                                 (64, 384, 1), (1, 40, 151), (1, 128, 19), (1, 896, 512)])
+def test_matmul_kernel_odd_shapes(mkn):
+    # test/gemm_kernel_test.dart:62-80
+    m, k, n = mkn
+    rng = np.random.default_rng(sum(mkn))
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    got = oracle.matmul_kernel(a, b, m, k, n)
+    want = a.astype(np.float64) @ b.astype(np.float64)
+    assert np.max(np.abs(got - want)) < 1e-4
+
+
+def test_float_lane_vs_double_tail_rules():
+    # m < 4 tail columns (n % 4) accumulate in double, everything else in
+    # float32 lanes (gemm_kernel_simd.dart:601-608, 665-672).
+    rng = np.random.default_rng(5)
+    m, k, n = 2, 257, 7
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    got = oracle.matmul_kernel(a, b, m, k, n)
+    f32 = np.zeros((m, n), np.float32)
+    for kk in range(k):
+        f32 = (f32 + (a[:, kk:kk + 1] * b[kk:kk + 1, :]).astype(np.float32)).astype(np.float32)
+    dbl = (a.astype(np.float64) @ b.astype(np.float64)).astype(np.float32)
+    np.testing.assert_array_equal(got[:, :4], f32[:, :4])
+    np.testing.assert_array_equal(got[:, 4:], dbl[:, 4:])
+
+
+def test_threads_are_bitwise_neutral():
+    # The pool's contract (parallel_pool.dart:7-8): column splits are bitwise identical.
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((9, 300)).astype(np.float32)
+    b = rng.standard_normal((300, 77)).astype(np.float32)
+    np.testing.assert_array_equal(oracle.matmul(a, b, nthreads=1), oracle.matmul(a, b, nthreads=5))
+    q = rng.integers(0, 256, (77, 10, 16), dtype=np.uint8)
+    s = np.abs(rng.standard_normal((77, 10))).astype(np.float32)
+    x = rng.standard_normal((5, 300)).astype(np.float32)
+    r1 = oracle.matmul_nbits(x, q, s, None, 300, 77, 32, nthreads=1)
+    r5 = oracle.matmul_nbits(x, q, s, None, 300, 77, 32, nthreads=5)
+    np.testing.assert_array_equal(r1, r5)
+
+
+def test_round_even_and_multiplier():
+    # _roundEven (onnx_qlinear_ops.dart:19-26)
+    assert [oracle.round_even(v) for v in (0.5, 1.5, 2.5, -0.5, -1.5, 2.4999, -2.6)] == [0, 2, 2, 0, -2, 2, -3]
+    m = oracle.qlinear_multiplier(0.02, 0.05, 0.1)
+    assert m == np.float32(np.float32(np.float32(0.02) * np.float32(0.05)) / np.float32(0.1))
