@@ -176,6 +176,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill"],
+                    help="run one phase only (for profiler captures); prints its device time")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -261,6 +263,21 @@ def main():
 
     hbm_peak, tc_peak, peak_src = peaks()
 
+    if args.case != "all":
+        m = {"decode1": 1, "decode8": 8, "prefill": 512}[args.case]
+        ms_c, _ = run_graph(m, R, args.steps, args.warmup)
+        if rank == 0:
+            print(json.dumps({"case": args.case, "M": m, "layers": R, "steps": args.steps,
+                              "us_per_launch": ms_c * 1e3 / (args.steps * R),
+                              "GBps": args.steps * R * launch_bytes(m) / (ms_c / 1e3) / 1e9,
+                              "TFLOPs": args.steps * R * 2 * m * K_DIM * N_DIM / (ms_c / 1e3) / 1e12}), flush=True)
+        for w in packed:
+            w.free()
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
     # Headline: M=1 decode over the full weight stack.
     ms, clocks = run_graph(1, R, args.steps, max(3, args.warmup))
     per_launch_s = ms / 1e3 / (args.steps * R)
@@ -301,11 +318,13 @@ def main():
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        layers = 8
-        gbs_c, dt_c = cpu_decode_gbs(2, 1, layers, threads)
+        # size the sample to ~10 s of CPU work from a short probe
+        probe_gbs, _ = cpu_decode_gbs(1, 1, 4, threads)
+        layers = max(8, int(10.0 * probe_gbs * 1e9 / launch_bytes(1)))
+        gbs_c, dt_c = cpu_decode_gbs(1, 0, layers, threads)
         cpu = {"value": round(gbs_c, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": f"oracle restatement of opMatMulNBits m==1, 2 x {layers} config-3 layers "
-                         f"({dt_c:.1f} s), column split over {threads} threads"}
+               "sample": f"oracle restatement of opMatMulNBits m==1 (double accumulation), {layers} config-3 "
+                         f"layers ({dt_c:.1f} s), column split over {threads} threads"}
 
     traffic = committed_traffic("nbits_decode_m1_k1024_n3072.md")
     line = {

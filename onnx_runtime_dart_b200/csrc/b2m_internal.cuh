@@ -59,6 +59,9 @@ struct b2m_ctx {
   size_t scratch_bytes = 0;
   // Device word that kernels with bounded spin-waits set on timeout.
   int32_t *dev_err = nullptr;
+  // Programmatic dependent launch for the decode kernels (env
+  // B2M_DISABLE_PDL=1 turns it off, e.g. to compare timelines).
+  bool pdl = true;
   // Pinned staging for the host-buffer helpers.
   void *pinned = nullptr;
   size_t pinned_bytes = 0;
@@ -77,10 +80,8 @@ struct b2m_tensor {
 enum WeightKind { W_F32 = 1, W_I8 = 2, W_NBITS = 3 };
 
 // Packed MatMulNBits weights (see prepack in runtime.cu):
-//   bq      [npad][kp/2] bytes; within every 16-byte (32-k) group the bytes are
-//           reordered so thread t of an MMA quad reads k in [4t,4t+4) and
-//           [16+4t,16+4t+4) with one 32-bit load: new[4t+0..3] =
-//           old[2t], old[2t+1], old[8+2t], old[9+2t].
+//   bq      npad*kp/2 bytes in the fragment-major layout of k_nbits.cu: one
+//           512-byte record per (16 columns, 64 k), 16 bytes per MMA lane.
 //   scales  [npad][nblocks] float
 //   zp_u8   [npad][zstride] packed uint4 (low nibble = even block), or
 //   zp_f32  [npad][nblocks] float, or neither (zero point 8).

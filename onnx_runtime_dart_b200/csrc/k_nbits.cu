@@ -1,15 +1,15 @@
 // MatMulNBits kernels (reference: opMatMulNBits, lib/src/onnx_qlinear_ops.dart:115-228).
 //
-//  * nbits_smallm_kernel  FAST mode, M <= 64 (token decode and small batches).
-//    HBM-bound GEMV: each CTA owns 32 output columns over all of K, pulls its
-//    packed nibbles, scales and zero points into shared memory with 1-D bulk
-//    copies issued BEFORE griddepcontrol.wait (weights never depend on the
-//    previous kernel, so under programmatic dependent launch the weight fetch
-//    of step i+1 overlaps the tail of step i), then runs warp-level
-//    m16n8k16 f16 MMAs with the weights as the 16-row operand (exact integers
-//    q - zp) and the activations (split into f16 hi + lo parts, so the product
-//    keeps ~22 bits of A) as the 8-column operand. The per-(column, block)
-//    scale multiplies the fp32 partial of each block, so scales stay fp32.
+//  * nbits_decode_kernel  FAST mode, M <= 32 (token decode and small batches).
+//    HBM-bound GEMV over the fragment-major packed layout (below): each lane
+//    issues one coalesced 16-byte weight load per 64-k chunk and converts the
+//    nibbles to f16 MMA fragments (exact integers q - zp) BEFORE
+//    griddepcontrol.wait — the weights never depend on the previous kernel, so
+//    under programmatic dependent launch the weight stream of step i+1
+//    overlaps step i. After the wait only the activations (split into f16
+//    hi + lo, keeping ~22 bits of A) are loaded and fed to warp-level
+//    m16n8k16 MMAs; the per-(column, block) scale multiplies each block's
+//    fp32 partial, so scales stay fp32.
 //  * nbits_simt_kernel    FAST mode fallback for shapes the other kernels do
 //    not take: dequantize a tile to fp32 in shared memory, fp32 FMA.
 //  * nbits_dequant_f32    EXACT mode: materialise W[N][K] float32 exactly as
@@ -21,27 +21,36 @@ namespace {
 
 using namespace b2m;
 
-constexpr int SM_COLS = 32;    // output columns per CTA (two m16 tiles)
-constexpr int SM_WARPS = 8;    // warps split K
-constexpr int SM_THREADS = SM_WARPS * 32;
-
-struct SmallmLayout {
-  uint32_t wq, sc, zp, red, bar, total;
-};
-
-__host__ __device__ inline SmallmLayout smallm_layout(const NbitsWeight &w, int mt) {
-  SmallmLayout L;
-  L.wq = 0;
-  L.sc = L.wq + (uint32_t)(SM_COLS * (w.kp / 2));
-  L.zp = L.sc + (uint32_t)(SM_COLS * w.nblocks * 4);
-  uint32_t zbytes = 0;
-  if (w.zp_kind == 1) zbytes = (uint32_t)(SM_COLS * w.zstride);
-  if (w.zp_kind == 2) zbytes = (uint32_t)(SM_COLS * w.nblocks * 4);
-  L.red = (L.zp + zbytes + 15u) & ~15u;
-  L.bar = L.red + (uint32_t)(SM_WARPS * 2 * mt * 32 * 4 * 4);
-  L.total = L.bar + 16;
-  return L;
+// ---------------------------------------------------------------------------
+// Packed layout ("fragment-major", written by the prepack in runtime.cu):
+// the weights of 16 output columns (a tile) and 64 consecutive k (a chunk)
+// form one 512-byte record; lane L = 4g + t of a warp owns bytes
+// [16L, 16L+16): four 32-bit words, (32-k group 0, column g), (group 0,
+// column g+8), (group 1, column g), (group 1, column g+8). Inside a word the
+// bytes are the column's original packed bytes 2t, 2t+1, 8+2t, 9+2t of that
+// 32-k group, i.e. k in [4t, 4t+4) and [16+4t, 16+4t+4). One coalesced 16-byte
+// load per lane therefore yields exactly the m16n8k16 A-fragments of two MMA
+// steps for two groups.
+// ---------------------------------------------------------------------------
+__host__ __device__ inline int64_t fm_byte(int64_t kp, int64_t col, int64_t k, int &nib_hi) {
+  const int64_t tile = col >> 4;
+  const int cc = (int)(col & 15), g = cc & 7, hi = cc >> 3;
+  const int64_t chunk = k >> 6;
+  const int grp = (int)((k >> 5) & 1);
+  const int kin = (int)(k & 31), kk = kin & 15, t = kk >> 2;
+  const int b = ((kin >> 4) << 1) + ((kk & 3) >> 1);
+  nib_hi = kk & 1;
+  return ((tile * (kp >> 6) + chunk) * 32 + (g * 4 + t)) * 16 + 4 * (2 * grp + hi) + b;
 }
+
+__device__ __forceinline__ int nib_at(const uint8_t *bq, int64_t kp, int64_t col, int64_t k) {
+  int h;
+  const uint8_t b = bq[fm_byte(kp, col, k, h)];
+  return h ? (b >> 4) : (b & 15);
+}
+
+constexpr int DEC_WARPS = 16;  // warps per CTA; each owns 64-k chunks
+constexpr bool DEC_LO = true;  // activations as f16 hi + lo (~22 bits)
 
 // Four activations of row `r`, k = k0..k0+3 (zero outside [0,M) x [0,K)).
 __device__ __forceinline__ float4 load_act4(const float *A, int64_t M, int64_t K, int64_t r, int64_t k0,
@@ -70,19 +79,19 @@ __device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_
 }
 
 template <int ZPK>
-__device__ __forceinline__ float zp_value(const uint8_t *zs, int64_t c, int64_t blk, const NbitsWeight &w) {
+__device__ __forceinline__ float zp_load(const NbitsWeight &w, int64_t col, int64_t blk) {
   if (ZPK == 1) {
-    const uint8_t z = reinterpret_cast<const uint8_t *>(zs)[c * w.zstride + (blk >> 1)];
+    const uint8_t z = __ldg(w.zp_u8 + col * w.zstride + (blk >> 1));
     return (float)((blk & 1) ? (z >> 4) : (z & 15));
   } else if (ZPK == 2) {
-    return reinterpret_cast<const float *>(zs)[c * w.nblocks + blk];
+    return __ldg(w.zp_f32 + col * w.nblocks + blk);
   }
   return 8.f;
 }
 
-// Weight fragment pair for one MMA step from the reordered 32-bit word:
-// selector picks bytes (b0,b1) for step 0 or (b2,b3) for step 1.
-// Returns half2(n_{4t}, n_{4t+2}) - zp and half2(n_{4t+1}, n_{4t+3}) - zp.
+// Weight fragment pair for one MMA step from one packed word: selector picks
+// bytes (b0,b1) for step 0 or (b2,b3) for step 1. Returns
+// half2(n_{4t} - zp, n_{4t+2} - zp) and half2(n_{4t+1} - zp, n_{4t+3} - zp).
 template <int ZPK>
 __device__ __forceinline__ void wfrag(uint32_t x, uint32_t sel, float zp, uint32_t &even, uint32_t &odd) {
   const uint32_t d = prmt(x, 0u, sel);
@@ -100,116 +109,116 @@ __device__ __forceinline__ void wfrag(uint32_t x, uint32_t sel, float zp, uint32
   }
 }
 
-template <int MT, int ZPK, bool BS16>
-__global__ void __launch_bounds__(SM_THREADS) nbits_smallm_kernel(const NbitsArgs p, const NbitsWeight w) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const SmallmLayout L = smallm_layout(w, MT);
-  uint8_t *s_wq = smem + L.wq;
-  float *s_sc = reinterpret_cast<float *>(smem + L.sc);
-  uint8_t *s_zp = smem + L.zp;
-  float *s_red = reinterpret_cast<float *>(smem + L.red);
-  uint64_t *bar = reinterpret_cast<uint64_t *>(smem + L.bar);
-
-  const int64_t col0 = (int64_t)blockIdx.x * SM_COLS;
+// Decode GEMV, M <= 8*MT. One CTA = 16 output columns (one m16 tile) over all
+// of K; warp w owns 64-k chunks w, w+NW, ... (at most CPW of them). Everything
+// that depends only on the weights — the coalesced 16-byte fragment loads,
+// nibble -> f16 conversion with the zero point subtracted (exact integers in
+// [-15, 15]), the scales — happens before griddepcontrol.wait, so under
+// programmatic dependent launch it overlaps the previous kernel. After the
+// wait: activation loads (f16 hi, plus the f16 residual lo when LO), MMAs,
+// per-block scaling, a fixed-order cross-warp reduction and the store.
+template <int MT, int ZPK, bool BS16, int CPW, int NW, bool LO>
+__global__ void __launch_bounds__(NW * 32) nbits_decode_kernel(const NbitsArgs p, const NbitsWeight w) {
+  extern __shared__ __align__(16) float s_red[];  // [NW][MT][32][4]
+  constexpr int SPS = BS16 ? 2 : 1;              // scales per 32-k group
+  const int tile = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
-  const int64_t row_bytes = w.kp / 2;
+  const int nchunks = (int)(w.kp >> 6);
+  const int nb = (int)w.nblocks;
+  const int groups = (int)((w.nblocks * w.block + 31) >> 5);  // 32-k groups holding real nibbles
+  const int c0 = tile * 16 + g, c1 = c0 + 8;
 
-  if (threadIdx.x == 0) {
-    mbar_init(bar, 1);
-    mbar_fence_init();
+  uint32_t af[CPW][2][2][4];  // [chunk][group][step][a0..a3]
+  float sc[CPW][2][SPS][2];   // [chunk][group][block][col g, col g+8]
+#pragma unroll
+  for (int i = 0; i < CPW; i++) {
+    const int c = warp + i * NW;
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (c < nchunks)
+      v = __ldg(reinterpret_cast<const uint4 *>(w.bq + (((size_t)tile * nchunks + c) * 32 + lane) * 16));
+#pragma unroll
+    for (int grp = 0; grp < 2; grp++) {
+      const int G = 2 * c + grp;
+      const uint32_t x0 = grp ? v.z : v.x, x1 = grp ? v.w : v.y;
+#pragma unroll
+      for (int s = 0; s < 2; s++) {
+        const int sb = BS16 ? s : 0;
+        int blk = BS16 ? (2 * G + s) : (G * 32) / w.block;
+        const bool valid = G < groups && blk < nb;
+        if (!valid) blk = 0;
+        const float z0 = zp_load<ZPK>(w, c0, blk), z1 = zp_load<ZPK>(w, c1, blk);
+        if (BS16 || s == 0) {
+          sc[i][grp][sb][0] = valid ? __ldg(w.scales + (size_t)c0 * nb + blk) : 0.f;
+          sc[i][grp][sb][1] = valid ? __ldg(w.scales + (size_t)c1 * nb + blk) : 0.f;
+        }
+        const uint32_t sel = s == 0 ? 0x4140u : 0x4342u;
+        wfrag<ZPK>(x0, sel, z0, af[i][grp][s][0], af[i][grp][s][2]);
+        wfrag<ZPK>(x1, sel, z1, af[i][grp][s][1], af[i][grp][s][3]);
+      }
+    }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const uint32_t wq_bytes = (uint32_t)(SM_COLS * row_bytes);
-    const uint32_t sc_bytes = (uint32_t)(SM_COLS * w.nblocks * 4);
-    uint32_t zp_bytes = 0;
-    if (ZPK == 1) zp_bytes = (uint32_t)(SM_COLS * w.zstride);
-    if (ZPK == 2) zp_bytes = (uint32_t)(SM_COLS * w.nblocks * 4);
-    mbar_arrive_expect_tx(bar, wq_bytes + sc_bytes + zp_bytes);
-    bulk_g2s(s_wq, w.bq + col0 * row_bytes, wq_bytes, bar);
-    bulk_g2s(s_sc, w.scales + col0 * w.nblocks, sc_bytes, bar);
-    if (ZPK == 1) bulk_g2s(s_zp, w.zp_u8 + col0 * w.zstride, zp_bytes, bar);
-    if (ZPK == 2) bulk_g2s(s_zp, w.zp_f32 + col0 * w.nblocks, zp_bytes, bar);
-  }
+
+  // Allow the next kernel in the stream to start its weight-only prologue
+  // now that ours is done (triggering earlier lets several future kernels
+  // crowd the SMs and measured slower); its griddepcontrol.wait still waits
+  // for this whole grid to complete.
   pdl_launch_dependents();
-  pdl_wait();  // activations / output buffer of the previous kernel are ready
+  pdl_wait();  // the previous kernel's results (our activations) are visible
 
   const bool vec_ok = ((p.K & 3) == 0) && ((reinterpret_cast<uintptr_t>(p.A) & 15) == 0);
-  const int64_t groups = w.kp / 32;
-  const int64_t g_begin = groups * warp / SM_WARPS, g_end = groups * (warp + 1) / SM_WARPS;
+  float acc[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[mt][e] = 0.f;
 
-  float acc[2][MT][4];
 #pragma unroll
-  for (int tt = 0; tt < 2; tt++)
+  for (int i = 0; i < CPW; i++) {
+    const int c = warp + i * NW;
+    if (c >= nchunks) break;
+    float4 av[2][2][MT];
 #pragma unroll
-    for (int mt = 0; mt < MT; mt++)
-#pragma unroll
-      for (int e = 0; e < 4; e++) acc[tt][mt][e] = 0.f;
-
-  const bool ok = mbar_wait_bounded(bar, 0, 1u << 24);
-  if (!ok) {
-    if (lane == 0 && p.dev_err) atomicExch(p.dev_err, B2M_DEVERR_MBAR_TIMEOUT);
-  } else {
-    for (int64_t gi = g_begin; gi < g_end; gi++) {
-      const int64_t kb = gi * 32;
-      // Activation fragments: both MMA steps, all row groups.
-      uint32_t bhi[2][MT][2], blo[2][MT][2];
+    for (int grp = 0; grp < 2; grp++)
 #pragma unroll
       for (int s = 0; s < 2; s++)
 #pragma unroll
-        for (int mt = 0; mt < MT; mt++) {
-          const float4 v = load_act4(p.A, p.M, p.K, mt * 8 + g, kb + 16 * s + 4 * t, vec_ok);
-          split_h2(v.x, v.z, bhi[s][mt][0], blo[s][mt][0]);
-          split_h2(v.y, v.w, bhi[s][mt][1], blo[s][mt][1]);
+        for (int mt = 0; mt < MT; mt++)
+          av[grp][s][mt] = load_act4(p.A, p.M, p.K, mt * 8 + g, c * 64 + grp * 32 + s * 16 + 4 * t, vec_ok);
+#pragma unroll
+    for (int grp = 0; grp < 2; grp++) {
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 2; s++) {
+          const float4 v = av[grp][s][mt];
+          uint32_t h0, l0, h1, l1;
+          if (LO) {
+            split_h2(v.x, v.z, h0, l0);
+            split_h2(v.y, v.w, h1, l1);
+          } else {
+            h0 = h2_as_u32(__floats2half2_rn(v.x, v.z));
+            h1 = h2_as_u32(__floats2half2_rn(v.y, v.w));
+          }
+          if (BS16) {
+            float e[4] = {0.f, 0.f, 0.f, 0.f};
+            mma_16816(e, af[i][grp][s], h0, h1, e);
+            if (LO) mma_16816(e, af[i][grp][s], l0, l1, e);
+            acc[mt][0] = fmaf(sc[i][grp][s % SPS][0], e[0], acc[mt][0]);
+            acc[mt][1] = fmaf(sc[i][grp][s % SPS][0], e[1], acc[mt][1]);
+            acc[mt][2] = fmaf(sc[i][grp][s % SPS][1], e[2], acc[mt][2]);
+            acc[mt][3] = fmaf(sc[i][grp][s % SPS][1], e[3], acc[mt][3]);
+          } else {
+            mma_16816(d, af[i][grp][s], h0, h1, d);
+            if (LO) mma_16816(d, af[i][grp][s], l0, l1, d);
+          }
         }
-#pragma unroll
-      for (int tt = 0; tt < 2; tt++) {
-        const int c0 = tt * 16 + g, c1 = c0 + 8;
-        const uint32_t x0 = *reinterpret_cast<const uint32_t *>(s_wq + c0 * row_bytes + kb / 2 + 4 * t);
-        const uint32_t x1 = *reinterpret_cast<const uint32_t *>(s_wq + c1 * row_bytes + kb / 2 + 4 * t);
-        if (BS16) {
-#pragma unroll
-          for (int s = 0; s < 2; s++) {
-            const int64_t blk = kb / 16 + s;
-            const float z0 = zp_value<ZPK>(s_zp, c0, blk, w), z1 = zp_value<ZPK>(s_zp, c1, blk, w);
-            const float sc0 = s_sc[c0 * w.nblocks + blk], sc1 = s_sc[c1 * w.nblocks + blk];
-            const uint32_t sel = s == 0 ? 0x4140u : 0x4342u;
-            uint32_t a[4];
-            wfrag<ZPK>(x0, sel, z0, a[0], a[2]);
-            wfrag<ZPK>(x1, sel, z1, a[1], a[3]);
-#pragma unroll
-            for (int mt = 0; mt < MT; mt++) {
-              float d[4] = {0.f, 0.f, 0.f, 0.f};
-              mma_16816(d, a, bhi[s][mt][0], bhi[s][mt][1], d);
-              mma_16816(d, a, blo[s][mt][0], blo[s][mt][1], d);
-              acc[tt][mt][0] = fmaf(sc0, d[0], acc[tt][mt][0]);
-              acc[tt][mt][1] = fmaf(sc0, d[1], acc[tt][mt][1]);
-              acc[tt][mt][2] = fmaf(sc1, d[2], acc[tt][mt][2]);
-              acc[tt][mt][3] = fmaf(sc1, d[3], acc[tt][mt][3]);
-            }
-          }
-        } else {
-          const int64_t blk = kb / w.block;
-          const float z0 = zp_value<ZPK>(s_zp, c0, blk, w), z1 = zp_value<ZPK>(s_zp, c1, blk, w);
-          const float sc0 = s_sc[c0 * w.nblocks + blk], sc1 = s_sc[c1 * w.nblocks + blk];
-          uint32_t a0[4], a1[4];
-          wfrag<ZPK>(x0, 0x4140u, z0, a0[0], a0[2]);
-          wfrag<ZPK>(x1, 0x4140u, z1, a0[1], a0[3]);
-          wfrag<ZPK>(x0, 0x4342u, z0, a1[0], a1[2]);
-          wfrag<ZPK>(x1, 0x4342u, z1, a1[1], a1[3]);
-#pragma unroll
-          for (int mt = 0; mt < MT; mt++) {
-            float d[4] = {0.f, 0.f, 0.f, 0.f};
-            mma_16816(d, a0, bhi[0][mt][0], bhi[0][mt][1], d);
-            mma_16816(d, a0, blo[0][mt][0], blo[0][mt][1], d);
-            mma_16816(d, a1, bhi[1][mt][0], bhi[1][mt][1], d);
-            mma_16816(d, a1, blo[1][mt][0], blo[1][mt][1], d);
-            acc[tt][mt][0] = fmaf(sc0, d[0], acc[tt][mt][0]);
-            acc[tt][mt][1] = fmaf(sc0, d[1], acc[tt][mt][1]);
-            acc[tt][mt][2] = fmaf(sc1, d[2], acc[tt][mt][2]);
-            acc[tt][mt][3] = fmaf(sc1, d[3], acc[tt][mt][3]);
-          }
+        if (!BS16) {
+          acc[mt][0] = fmaf(sc[i][grp][0][0], d[0], acc[mt][0]);
+          acc[mt][1] = fmaf(sc[i][grp][0][0], d[1], acc[mt][1]);
+          acc[mt][2] = fmaf(sc[i][grp][0][1], d[2], acc[mt][2]);
+          acc[mt][3] = fmaf(sc[i][grp][0][1], d[3], acc[mt][3]);
         }
       }
     }
@@ -217,37 +226,23 @@ __global__ void __launch_bounds__(SM_THREADS) nbits_smallm_kernel(const NbitsArg
 
   // Cross-warp reduction over the K split, in fixed warp order.
 #pragma unroll
-  for (int tt = 0; tt < 2; tt++)
-#pragma unroll
-    for (int mt = 0; mt < MT; mt++)
-      *reinterpret_cast<float4 *>(&s_red[(((warp * 2 + tt) * MT + mt) * 32 + lane) * 4]) =
-          make_float4(acc[tt][mt][0], acc[tt][mt][1], acc[tt][mt][2], acc[tt][mt][3]);
+  for (int mt = 0; mt < MT; mt++)
+    *reinterpret_cast<float4 *>(&s_red[((warp * MT + mt) * 32 + lane) * 4]) =
+        make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
   __syncthreads();
-  if (!ok) return;
-  constexpr int OUTS = 2 * MT * 32 * 4;
-  for (int o = threadIdx.x; o < OUTS; o += SM_THREADS) {
-    const int e = o & 3, ln = (o >> 2) & 31, mt = (o >> 7) % MT, tt = (o >> 7) / MT;
+  constexpr int OUTS = MT * 32 * 4;
+  for (int o = threadIdx.x; o < OUTS; o += NW * 32) {
+    const int e = o & 3, ln = (o >> 2) & 31, mt = o >> 7;
     float sum = 0.f;
 #pragma unroll
-    for (int wp = 0; wp < SM_WARPS; wp++) sum += s_red[(((wp * 2 + tt) * MT + mt) * 32 + ln) * 4 + e];
-    const int gg = ln >> 2, t4 = ln & 3;
-    const int64_t col = col0 + tt * 16 + gg + ((e & 2) ? 8 : 0);
-    const int64_t row = mt * 8 + 2 * t4 + (e & 1);
+    for (int wp = 0; wp < NW; wp++) sum += s_red[((wp * MT + mt) * 32 + ln) * 4 + e];
+    const int col = tile * 16 + (ln >> 2) + ((e & 2) ? 8 : 0);
+    const int row = mt * 8 + 2 * (ln & 3) + (e & 1);
     if (row < p.M && col < p.N) {
-      if (p.bias) sum += p.bias[col];
-      p.Y[row * p.N + col] = sum;
+      if (p.bias) sum += __ldg(p.bias + col);
+      p.Y[(size_t)row * p.N + col] = sum;
     }
   }
-}
-
-// Nibble of column row `wrow` (reordered layout) at logical k.
-__device__ __forceinline__ int nib_at(const uint8_t *wrow, int64_t k) {
-  const int64_t grp = k >> 5;
-  const int kin = (int)(k & 31);
-  const int kk = kin & 15;
-  const int byte = 4 * (kk >> 2) + ((kin >> 4) << 1) + ((kk & 3) >> 1);
-  const uint8_t b = wrow[grp * 16 + byte];
-  return (kk & 1) ? (b >> 4) : (b & 15);
 }
 
 // Generic fp32 tile kernel: Y[64 x 64] per CTA, K in steps of 32.
@@ -266,7 +261,7 @@ __global__ void __launch_bounds__(256) nbits_simt_kernel(const NbitsArgs p, cons
       float wv = 0.f;
       if (gj < p.N && gk < p.K) {
         const int64_t blk = gk / w.block;
-        const int q = nib_at(w.bq + gj * (w.kp / 2), gk);
+        const int q = nib_at(w.bq, w.kp, gj, gk);
         float zp = 8.f;
         if (w.zp_kind == 1) {
           const uint8_t z = w.zp_u8[gj * w.zstride + (blk >> 1)];
@@ -312,7 +307,7 @@ __global__ void nbits_dequant_kernel(const NbitsWeight w, int64_t K, int64_t N, 
   if (idx >= N * K) return;
   const int64_t n = idx / K, k = idx % K;
   const int64_t blk = k / w.block;
-  const int q = nib_at(w.bq + n * (w.kp / 2), k);
+  const int q = nib_at(w.bq, w.kp, n, k);
   const float s = w.scales[n * w.nblocks + blk];
   float v;
   if (w.zp_kind == 2) {
@@ -331,15 +326,15 @@ __global__ void nbits_dequant_kernel(const NbitsWeight w, int64_t K, int64_t N, 
   out[idx] = v;
 }
 
-template <int MT, int ZPK, bool BS16>
-void launch_smallm_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
-  const SmallmLayout L = smallm_layout(*a.w, MT);
-  auto kern = nbits_smallm_kernel<MT, ZPK, BS16>;
-  B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total));
+template <int MT, int ZPK, bool BS16, int CPW>
+void launch_decode_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
+  auto kern = nbits_decode_kernel<MT, ZPK, BS16, CPW, DEC_WARPS, DEC_LO>;
+  const int smem = DEC_WARPS * MT * 32 * 4 * (int)sizeof(float);
+  if (smem > 48 * 1024) B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)((a.N + SM_COLS - 1) / SM_COLS));
-  cfg.blockDim = dim3(SM_THREADS);
-  cfg.dynamicSmemBytes = L.total;
+  cfg.gridDim = dim3((unsigned)((a.N + 15) / 16));
+  cfg.blockDim = dim3(DEC_WARPS * 32);
+  cfg.dynamicSmemBytes = (size_t)smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -349,29 +344,49 @@ void launch_smallm_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, a, *a.w));
 }
 
-template <int MT>
-void launch_smallm_mt(const NbitsArgs &a, cudaStream_t s, bool pdl) {
+template <int MT, int CPW>
+void launch_decode_z(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   const bool bs16 = a.w->block == 16;
   switch (a.w->zp_kind) {
-    case 0: bs16 ? launch_smallm_t<MT, 0, true>(a, s, pdl) : launch_smallm_t<MT, 0, false>(a, s, pdl); break;
-    case 1: bs16 ? launch_smallm_t<MT, 1, true>(a, s, pdl) : launch_smallm_t<MT, 1, false>(a, s, pdl); break;
-    default: bs16 ? launch_smallm_t<MT, 2, true>(a, s, pdl) : launch_smallm_t<MT, 2, false>(a, s, pdl); break;
+    case 0: bs16 ? launch_decode_t<MT, 0, true, CPW>(a, s, pdl) : launch_decode_t<MT, 0, false, CPW>(a, s, pdl); break;
+    case 1: bs16 ? launch_decode_t<MT, 1, true, CPW>(a, s, pdl) : launch_decode_t<MT, 1, false, CPW>(a, s, pdl); break;
+    default: bs16 ? launch_decode_t<MT, 2, true, CPW>(a, s, pdl) : launch_decode_t<MT, 2, false, CPW>(a, s, pdl); break;
   }
+}
+
+int decode_cpw(const NbitsWeight &w) {
+  const int64_t chunks = w.kp / 64;
+  return (int)((chunks + DEC_WARPS - 1) / DEC_WARPS);
 }
 
 }  // namespace
 
+// Row groups x chunks per warp that the decode kernel is instantiated for
+// (register budget: weights of CPW chunks stay in registers across the wait).
 bool nbits_smallm_supported(const NbitsWeight &w, int64_t M) {
-  if (M < 1 || M > 64) return false;
-  const int mt = M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8;
-  return smallm_layout(w, mt).total <= 200 * 1024;
+  if (M < 1 || M > 32) return false;
+  const int cpw = decode_cpw(w);
+  const int mt = M <= 8 ? 1 : M <= 16 ? 2 : 4;
+  if (cpw <= 1) return true;
+  if (cpw <= 2) return mt <= 2;
+  if (cpw <= 4) return mt == 1;
+  return false;
 }
 
 void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl) {
-  if (a.M <= 8) launch_smallm_mt<1>(a, s, pdl);
-  else if (a.M <= 16) launch_smallm_mt<2>(a, s, pdl);
-  else if (a.M <= 32) launch_smallm_mt<4>(a, s, pdl);
-  else launch_smallm_mt<8>(a, s, pdl);
+  const int cpw = decode_cpw(*a.w);
+  const int mt = a.M <= 8 ? 1 : a.M <= 16 ? 2 : 4;
+  B2M_REQUIRE(nbits_smallm_supported(*a.w, a.M), B2M_ERR_CUDA, "internal: decode kernel shape not instantiated");
+  if (cpw <= 1) {
+    if (mt == 1) launch_decode_z<1, 1>(a, s, pdl);
+    else if (mt == 2) launch_decode_z<2, 1>(a, s, pdl);
+    else launch_decode_z<4, 1>(a, s, pdl);
+  } else if (cpw <= 2) {
+    if (mt == 1) launch_decode_z<1, 2>(a, s, pdl);
+    else launch_decode_z<2, 2>(a, s, pdl);
+  } else {
+    launch_decode_z<1, 4>(a, s, pdl);
+  }
 }
 
 void launch_nbits_simt(const NbitsArgs &a, cudaStream_t s) {

@@ -9,6 +9,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -484,7 +485,7 @@ void nbits_run(b2m_ctx *ctx, const float *A, int64_t m, const b2m_weight *w, con
     p.K = K;
     p.N = N;
     p.dev_err = ctx->dev_err;
-    if (nbits_smallm_supported(w->nb, m)) launch_nbits_smallm(p, ctx->stream, true);
+    if (nbits_smallm_supported(w->nb, m)) launch_nbits_smallm(p, ctx->stream, ctx->pdl);
     else launch_nbits_simt(p, ctx->stream);
     return;
   }
@@ -574,6 +575,8 @@ B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx) {
     B2M_CUDA(cudaEventCreate(&ctx->ev1));
     B2M_CUDA(cudaMalloc(&ctx->dev_err, sizeof(int32_t)));
     B2M_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(int32_t)));
+    const char *no_pdl = std::getenv("B2M_DISABLE_PDL");
+    ctx->pdl = !(no_pdl && no_pdl[0] == '1');
     *out_ctx = ctx;
   });
 }
@@ -819,20 +822,28 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
     const int64_t kp = round_up(nb * block_size, 64);
     const int64_t npad = round_up(n, 128);
     const int64_t row = kp / 2;
+    // Fragment-major layout (see k_nbits.cu): record (tile of 16 columns,
+    // chunk of 64 k) = 32 lanes x 16 bytes; lane 4g+t holds the words
+    // (group 0, col g), (group 0, col g+8), (group 1, col g), (group 1, col g+8),
+    // each word = original bytes 2t, 2t+1, 8+2t, 9+2t of that 32-k group.
+    const int64_t nchunks = kp / 64;
     std::vector<uint8_t> bq((size_t)(npad * row), 0);
     std::vector<uint8_t> tmp((size_t)row);
     for (int64_t c = 0; c < n; c++) {
       std::fill(tmp.begin(), tmp.end(), 0);
       std::memcpy(tmp.data(), b_q + c * nb * blob, (size_t)(nb * blob));
-      uint8_t *dst = &bq[(size_t)(c * row)];
-      for (int64_t g = 0; g < row / 16; g++) {
-        const uint8_t *o = &tmp[(size_t)(g * 16)];
-        uint8_t *d = dst + g * 16;
+      const int64_t tile = c / 16;
+      const int cc = (int)(c % 16), g = cc % 8, hi = cc / 8;
+      for (int64_t G = 0; G < kp / 32; G++) {
+        const uint8_t *o = &tmp[(size_t)(G * 16)];
+        const int64_t chunk = G / 2;
+        const int grp = (int)(G % 2);
         for (int t = 0; t < 4; t++) {
-          d[4 * t + 0] = o[2 * t];
-          d[4 * t + 1] = o[2 * t + 1];
-          d[4 * t + 2] = o[8 + 2 * t];
-          d[4 * t + 3] = o[9 + 2 * t];
+          uint8_t *d = &bq[(size_t)(((tile * nchunks + chunk) * 32 + (g * 4 + t)) * 16 + 4 * (2 * grp + hi))];
+          d[0] = o[2 * t];
+          d[1] = o[2 * t + 1];
+          d[2] = o[8 + 2 * t];
+          d[3] = o[9 + 2 * t];
         }
       }
     }
