@@ -97,6 +97,13 @@ struct NbitsWeight {
   int64_t kp = 0;    // padded K (multiple of 64, >= nblocks*block)
   int64_t npad = 0;  // padded N (multiple of 128)
   float *wdeq = nullptr;  // exact-mode float32 W [N][K], made on first use
+  // All scales are 0 or normal f16 numbers and zero points are integers, so
+  // the tensor-core dequant may scale in f16 (one rounding per weight).
+  bool f16_scales = false;
+  // Prefill scale records (block >= 32, integer zero points, f16-safe
+  // scales): [npad/16][kp/64][8] x 16 bytes, eight halves (s, 1024 + zp) for
+  // columns g / g+8 of the two 32-k groups of a chunk; null otherwise.
+  uint8_t *srec = nullptr;
 };
 
 // Packed int8 / uint8 weights: bt[npad][kpad] (K-major), colsum[n] = sum_k b.
@@ -174,6 +181,10 @@ bool nbits_smallm_supported(const NbitsWeight &w, int64_t M);
 void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl);
 void launch_nbits_simt(const NbitsArgs &a, cudaStream_t s);
 void launch_nbits_dequant_f32(const NbitsWeight &w, int64_t K, int64_t N, float *out, cudaStream_t s);
+// tcgen05 prefill GEMM; `a16` is scratch for A converted to f16, M x nbits_tc_k8(K).
+int64_t nbits_tc_k8(int64_t K);
+bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N);
+void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s);
 
 // MatMulInteger / QLinearMatMul
 struct I8GemmArgs {

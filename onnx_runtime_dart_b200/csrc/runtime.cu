@@ -9,6 +9,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <new>
@@ -144,7 +145,7 @@ struct Scratch {
   b2m_ctx *ctx;
   size_t used = 0;
   explicit Scratch(b2m_ctx *c, size_t need) : ctx(c) {
-    if (need > ctx->scratch_bytes) {
+    if (need > 0 && need > ctx->scratch_bytes) {
       if (ctx->scratch) B2M_CUDA(cudaFreeAsync(ctx->scratch, ctx->stream));
       ctx->scratch = nullptr;
       ctx->scratch_bytes = 0;
@@ -469,8 +470,15 @@ void integer_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const 
 // MatMulNBits
 // ---------------------------------------------------------------------------
 
-void nbits_run(b2m_ctx *ctx, const float *A, int64_t m, const b2m_weight *w, const float *bias, int32_t mode,
-               float *Y) {
+// Device scratch bytes nbits_run needs for an m-row call.
+size_t nbits_scratch_bytes(const b2m_weight *w, int64_t m, int32_t mode) {
+  if (mode != B2M_MODE_FAST || m == 0 || nbits_smallm_supported(w->nb, m)) return 0;
+  if (!nbits_tc_supported(w->nb, m, w->k, w->n)) return 0;
+  return (size_t)(m * nbits_tc_k8(w->k) * 2) + 256;
+}
+
+void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_weight *w, const float *bias,
+               int32_t mode, float *Y) {
   B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
   B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad mode");
   if (m == 0) return;
@@ -485,8 +493,14 @@ void nbits_run(b2m_ctx *ctx, const float *A, int64_t m, const b2m_weight *w, con
     p.K = K;
     p.N = N;
     p.dev_err = ctx->dev_err;
-    if (nbits_smallm_supported(w->nb, m)) launch_nbits_smallm(p, ctx->stream, ctx->pdl);
-    else launch_nbits_simt(p, ctx->stream);
+    if (nbits_smallm_supported(w->nb, m)) {
+      launch_nbits_smallm(p, ctx->stream, ctx->pdl);
+    } else if (nbits_tc_supported(w->nb, m, K, N)) {
+      __half *a16 = static_cast<__half *>(sc.take((size_t)(m * nbits_tc_k8(K) * 2)));
+      launch_nbits_tc(p, a16, ctx->stream);
+    } else {
+      launch_nbits_simt(p, ctx->stream);
+    }
     return;
   }
   // EXACT: dequantize once (exactly as weight() does), then the exact GEMM.
@@ -857,6 +871,38 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
     NbitsWeight &W = w->nb;
     W.block = block_size;
     W.nblocks = nb;
+    {
+      bool ok16 = zp_dtype != B2M_FLOAT;
+      for (int64_t i = 0; i < n * nb && ok16; i++) {
+        const float a = std::fabs(scales[i]);
+        ok16 = a == 0.f || (a >= 6.103515625e-05f && a <= 65504.f);
+      }
+      W.f16_scales = ok16;
+    }
+    std::vector<__half> srec;
+    if (W.f16_scales && block_size >= 32) {
+      const int64_t ntile = npad / 16;
+      srec.assign((size_t)(ntile * nchunks * 8 * 8), __float2half_rn(0.f));
+      for (int64_t tl = 0; tl < ntile; tl++)
+        for (int64_t ch = 0; ch < nchunks; ch++)
+          for (int g = 0; g < 8; g++)
+            for (int grp = 0; grp < 2; grp++)
+              for (int hi = 0; hi < 2; hi++) {
+                const int64_t col = tl * 16 + g + 8 * hi;
+                const int64_t blk = (ch * 64 + grp * 32) / block_size;
+                float sv = 0.f, zv = 8.f;
+                if (col < n && blk < nb) {
+                  sv = scales[col * nb + blk];
+                  if (zp_dtype == B2M_UINT8) {
+                    const uint8_t zb = static_cast<const uint8_t *>(zero_points)[col * zs + blk / 2];
+                    zv = (float)((blk & 1) ? (zb >> 4) : (zb & 15));
+                  }
+                }
+                const size_t o = (size_t)(((tl * nchunks + ch) * 8 + g) * 8 + grp * 4 + hi * 2);
+                srec[o] = __float2half_rn(sv);
+                srec[o + 1] = __float2half_rn(1024.f + zv);
+              }
+    }
     W.zstride = zs;
     W.kp = kp;
     W.npad = npad;
@@ -865,6 +911,10 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
       B2M_CUDA(cudaMemcpy(W.bq, bq.data(), bq.size(), cudaMemcpyHostToDevice));
       B2M_CUDA(cudaMalloc(&W.scales, sc.size() * 4));
       B2M_CUDA(cudaMemcpy(W.scales, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice));
+      if (!srec.empty()) {
+        B2M_CUDA(cudaMalloc(&W.srec, srec.size() * sizeof(__half)));
+        B2M_CUDA(cudaMemcpy(W.srec, srec.data(), srec.size() * sizeof(__half), cudaMemcpyHostToDevice));
+      }
       if (zp_dtype == B2M_UINT8) {
         std::vector<uint8_t> z((size_t)(npad * zs), 0);
         std::memcpy(z.data(), zero_points, (size_t)(n * zs));
@@ -883,6 +933,7 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
       cudaFree(W.scales);
       cudaFree(W.zp_u8);
       cudaFree(W.zp_f32);
+      cudaFree(W.srec);
       delete w;
       throw;
     }
@@ -903,6 +954,7 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     cudaFree(w->nb.zp_u8);
     cudaFree(w->nb.zp_f32);
     cudaFree(w->nb.wdeq);
+    cudaFree(w->nb.srec);
     delete w;
   });
 }
@@ -977,9 +1029,10 @@ B2M_API b2m_status b2m_matmul_nbits(b2m_ctx *ctx, const b2m_tensor *a, const b2m
     oshape.push_back(w->n);
     check_cancel(ctx);
     b2m_tensor *out = prepare_output(ctx, y, B2M_FLOAT, oshape);
+    Scratch sc(ctx, nbits_scratch_bytes(w, m, mode));
     OpTimer timer(ctx);
-    nbits_run(ctx, static_cast<const float *>(a->data), m, w, bias ? static_cast<const float *>(bias->data) : nullptr,
-              mode, static_cast<float *>(out->data));
+    nbits_run(ctx, sc, static_cast<const float *>(a->data), m, w,
+              bias ? static_cast<const float *>(bias->data) : nullptr, mode, static_cast<float *>(out->data));
     timer.done();
   });
 }
@@ -991,8 +1044,10 @@ B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m,
     DeviceGuard dg(ctx->device);
     B2M_REQUIRE(m >= 0 && (a || m == 0) && (y || m == 0), B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad pointers");
     check_cancel(ctx);
+    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+    Scratch sc(ctx, nbits_scratch_bytes(w, m, mode));
     OpTimer timer(ctx);
-    nbits_run(ctx, a, m, w, bias, mode, y);
+    nbits_run(ctx, sc, a, m, w, bias, mode, y);
     timer.done();
   });
 }
@@ -1008,14 +1063,14 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
     check_cancel(ctx);
     if (m == 0) return;
     const size_t abytes = (size_t)(m * w->k * 4), ybytes = (size_t)(m * w->n * 4), bbytes = (size_t)(w->n * 4);
-    Scratch sc(ctx, abytes + ybytes + bbytes + 1024);
+    Scratch sc(ctx, abytes + ybytes + bbytes + 1024 + nbits_scratch_bytes(w, m, mode));
     float *da = static_cast<float *>(sc.take(abytes));
     float *dy = static_cast<float *>(sc.take(ybytes));
     float *db = bias_host ? static_cast<float *>(sc.take(bbytes)) : nullptr;
     B2M_CUDA(cudaMemcpyAsync(da, a_host, abytes, cudaMemcpyHostToDevice, ctx->stream));
     if (db) B2M_CUDA(cudaMemcpyAsync(db, bias_host, bbytes, cudaMemcpyHostToDevice, ctx->stream));
     OpTimer timer(ctx);
-    nbits_run(ctx, da, m, w, db, mode, dy);
+    nbits_run(ctx, sc, da, m, w, db, mode, dy);
     timer.done();
     B2M_CUDA(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, ctx->stream));
     B2M_CUDA(cudaStreamSynchronize(ctx->stream));
