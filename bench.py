@@ -4,16 +4,14 @@
 Headline (one JSON line on rank 0): MatMulNBits int4 decode GEMV HBM
 throughput in GB/s, BASELINE config 3 at M=1 (K=1024, N=3072, block 32,
 packed uint4 zero points). One step = one decode token through a stack of
-`--layers` (default 256) distinct config-3 weight sets, launched back to back
-(captured in a CUDA graph; each kernel prefetches its weights under
-programmatic dependent launch), so the weights streamed per step (516 MB)
-exceed the 126 MB L2 and every timed byte comes from HBM. The same line
-carries the M=512 prefill TFLOP/s and M=8 decode GB/s (same config), the
-end-to-end number through the host-buffer C-ABI call, the roofline of the
+`--layers` x `--passes` config-3 layers (256 distinct weight sets, each reused
+every 516 MB of weight traffic, so the stream exceeds the 126 MB L2 and every
+timed byte comes from HBM), launched back to back (captured in a CUDA graph;
+each kernel prefetches its weights under programmatic dependent launch). The
+same line carries the M=512 prefill TFLOP/s and M=8 decode GB/s (same config),
+the end-to-end number through the host-buffer C-ABI call, the roofline of the
 dominant kernel, the CPU baseline (the oracle port of the reference's Dart
 kernel on the host cores) and SM clocks sampled during the timed region.
-
-  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
 N > 1 runs under torchrun: every rank drives its own GPU with its own weight
 stack (replicas: config 3 is a single op and shards no data; weak scaling),
@@ -92,7 +90,7 @@ class ClockSampler:
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -174,7 +172,9 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--layers", type=int, default=256)
+    ap.add_argument("--layers", type=int, default=256, help="distinct weight sets (516 MB for 256)")
+    ap.add_argument("--passes", type=int, default=64,
+                    help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill"],
                     help="run one phase only (for profiler captures); prints its device time")
@@ -221,7 +221,7 @@ def main():
     ws = make_weights(rng, R)
     packed = [ctx.prepack_nbits(bq, sc, zp, K_DIM, N_DIM, 4, BLOCK) for bq, sc, zp in ws]
 
-    def run_graph(m, layers, steps, warmup):
+    def run_graph(m, layers, steps, warmup, passes=1):
         a = torch.randn((m, K_DIM), device=dev, dtype=torch.float32)
         ys = [torch.empty((m, N_DIM), device=dev, dtype=torch.float32) for _ in range(layers)]
         torch.cuda.synchronize()
@@ -233,9 +233,10 @@ def main():
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g, stream=stream):
             ctx.set_stream(torch.cuda.current_stream().cuda_stream)
-            for i in range(layers):
-                N.check(lib.b2m_matmul_nbits_dev(ctx.handle, ctypes.c_void_p(a.data_ptr()), m, packed[i].handle,
-                                                 None, N.MODE_FAST, ctypes.c_void_p(ys[i].data_ptr())))
+            for _ in range(passes):
+                for i in range(layers):
+                    N.check(lib.b2m_matmul_nbits_dev(ctx.handle, ctypes.c_void_p(a.data_ptr()), m, packed[i].handle,
+                                                     None, N.MODE_FAST, ctypes.c_void_p(ys[i].data_ptr())))
         ctx.set_stream(stream.cuda_stream)
         with torch.cuda.stream(stream):
             for _ in range(warmup):
@@ -278,10 +279,11 @@ def main():
             dist.destroy_process_group()
         return
 
-    # Headline: M=1 decode over the full weight stack.
-    ms, clocks = run_graph(1, R, args.steps, max(3, args.warmup))
-    per_launch_s = ms / 1e3 / (args.steps * R)
-    value = world * args.steps * R * launch_bytes(1) / (ms / 1e3) / 1e9
+    # Headline: M=1 decode; one step = `passes` passes over the R weight sets.
+    P = args.passes
+    ms, clocks = run_graph(1, R, args.steps, max(3, args.warmup), passes=P)
+    per_launch_s = ms / 1e3 / (args.steps * R * P)
+    value = world * args.steps * R * P * launch_bytes(1) / (ms / 1e3) / 1e9
     achieved = launch_bytes(1) / per_launch_s / 1e9
 
     # M=8 decode (same rotation) and M=512 prefill (compute-bound).
@@ -318,9 +320,9 @@ def main():
     cpu = None
     if rank == 0 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        # size the sample to ~10 s of CPU work from a short probe
-        probe_gbs, _ = cpu_decode_gbs(1, 1, 4, threads)
-        layers = max(8, int(10.0 * probe_gbs * 1e9 / launch_bytes(1)))
+        # size the sample to ~15 s of CPU work from a short probe
+        probe_gbs, _ = cpu_decode_gbs(1, 1, 16, threads)
+        layers = max(8, int(15.0 * probe_gbs * 1e9 / launch_bytes(1)))
         gbs_c, dt_c = cpu_decode_gbs(1, 0, layers, threads)
         cpu = {"value": round(gbs_c, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": f"oracle restatement of opMatMulNBits m==1 (double accumulation), {layers} config-3 "
@@ -334,8 +336,9 @@ def main():
         "split f16 hi+lo, fp32 accumulate)", "data": "synthetic (seeded numpy default_rng)",
         "config": {"workload": "MatMulNBits int4 decode GEMV, BASELINE config 3 M=1 (K=1024 N=3072 block 32 "
                                "packed uint4 zp)", "M": 1, "K": K_DIM, "N": N_DIM, "block_size": BLOCK,
-                   "layers_per_step": R, "global_batch": world, "parallelism": f"replicas x{world}",
-                   "l2": f"weights rotated over {R * W_BYTES / 1e6:.0f} MB per step (> 126 MB L2)"},
+                   "layers_per_step": R * P, "distinct_weight_sets": R, "global_batch": world,
+                   "parallelism": f"replicas x{world}",
+                   "l2": f"weights rotated over {R * W_BYTES / 1e6:.0f} MB (> 126 MB L2) between reuses"},
         "secondary": {
             "decode_m8_gbs": None if gbs8 is None else round(gbs8, 2),
             "prefill_m512_tflops": round(tflops_p, 2),
@@ -350,7 +353,7 @@ def main():
                 "d2h_bytes_per_step": e2e_layers * N_DIM * 4,
                 "what": f"b2m_matmul_nbits_host per layer ({e2e_layers} layers per step): pinned A -> device, "
                         "kernel, Y -> pinned host, synchronise"},
-        "gpu_launches": args.steps * R,
+        "gpu_launches": args.steps * R * P,
         "clocks": clocks,
     }
     if cpu is not None:
