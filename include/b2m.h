@@ -228,6 +228,27 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
 B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m, const b2m_weight *w,
                                         const float *bias, int32_t mode, float *y);
 
+/* Allocation-free MatMulNBits. No counterpart in the reference: this entry
+ * point exists for callers that must not allocate device memory while they
+ * run an operator — a host application that has handed all device memory to
+ * its own pool, or an inference loop that must not risk an out-of-memory
+ * failure or the device-wide synchronisation cudaMalloc/cudaFree can cause.
+ * It runs the same tensor-core kernels as b2m_matmul_nbits (FAST numerics)
+ * on caller-owned device buffers (a: m x K floats, bias: N floats or NULL,
+ * y: m x N floats) and the prepacked weight `w`, on `stream` (a cudaStream_t
+ * of w's device; NULL = legacy default stream), and returns after Y is
+ * complete. Its only working memory is a fixed file-scope device array of
+ * B2M_NOALLOC_SCRATCH_BYTES (+256) bytes that every device loading the library
+ * holds until the process exits; calls needing more (m * roundup(K, 8) * 2
+ * bytes) fail with B2M_ERR_INVALID_ARGUMENT. The array is shared by all calls
+ * on a device and keeps the last call's contents, so calls that overlap on
+ * the GPU race; serialise them (one stream, or host-side ordering). The first
+ * call on a device resolves the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture. */
+#define B2M_NOALLOC_SCRATCH_BYTES (8u << 20)
+B2M_API b2m_status b2m_matmul_nbits_noalloc(const b2m_weight *w, const float *a, int64_t m, const float *bias,
+                                            float *y, void *stream);
+
 /* Shape of a packed weight: K and N (logical B is [K, N]). */
 B2M_API b2m_status b2m_weight_info(const b2m_weight *w, int64_t *k, int64_t *n);
 

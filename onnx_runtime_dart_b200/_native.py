@@ -37,6 +37,7 @@ MODE_EXACT = 0
 MODE_FAST = 1
 
 MAX_RANK = 8
+NOALLOC_SCRATCH_BYTES = 8 << 20
 
 
 class B2mError(RuntimeError):
@@ -127,6 +128,7 @@ SIGNATURES = {
     "b2m_matmul_nbits": (_i32, [_c_ctx, _c_tensor, _c_weight, _c_tensor, _i32, ctypes.POINTER(_c_tensor)]),
     "b2m_matmul_nbits_host": (_i32, [_c_ctx, _vp, _i64, _c_weight, _vp, _i32, _vp]),
     "b2m_matmul_nbits_dev": (_i32, [_c_ctx, _vp, _i64, _c_weight, _vp, _i32, _vp]),
+    "b2m_matmul_nbits_noalloc": (_i32, [_c_weight, _vp, _i64, _vp, _vp, _vp]),
 }
 
 _lib = None

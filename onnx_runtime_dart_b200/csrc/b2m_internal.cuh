@@ -19,6 +19,8 @@ struct B2mError {
 };
 
 [[noreturn]] void b2m_throw(b2m_status code, const std::string &msg);
+// Sets the message b2m_last_error() returns on this thread.
+void b2m_set_last_error(const std::string &msg);
 
 #define B2M_CUDA(expr)                                                                     \
   do {                                                                                     \

@@ -540,6 +540,8 @@ void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_w
 
 [[noreturn]] void b2m_throw(b2m_status code, const std::string &msg) { throw B2mError{code, msg}; }
 
+void b2m_set_last_error(const std::string &msg) { g_last_error = msg; }
+
 // ===========================================================================
 // Exported C ABI
 // ===========================================================================
