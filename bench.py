@@ -163,6 +163,65 @@ def run_reference(args, rank):
 
 
 # ---------------------------------------------------------------------------
+# BASELINE configs 1 and 2 (single ops, device-resident operands)
+# ---------------------------------------------------------------------------
+
+def _time_calls(torch, stream, fn, steps, warmup):
+    for _ in range(max(3, warmup)):
+        fn()
+    stream.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    stream.synchronize()
+    return e0.elapsed_time(e1) / steps  # ms per call
+
+
+def other_configs(ctx, lib, N, stream, dev, steps, warmup):
+    """Config 1: fp32 MatMul A[128,384] x B[384,1536] (B prepacked), EXACT and
+    FAST modes. Config 2: MatMulInteger u8[M,1024] x i8[1024,3072], aZp=128,
+    per-column bZp in [-4,4], M in {1, 64, 512}. Device-resident inputs,
+    calls enqueued back to back on one stream."""
+    import torch
+    rng = np.random.default_rng(0)
+    out = []
+    a = rng.standard_normal((128, 384)).astype(np.float32)
+    b = (rng.standard_normal((384, 1536)) / np.sqrt(384)).astype(np.float32)
+    wb = ctx.prepack_f32(b)
+    da = ctx.upload(a)
+    dy = ctx.empty((128, 1536))
+    for mode, name in ((N.MODE_EXACT, "exact"), (N.MODE_FAST, "fast")):
+        def call():
+            h = ctypes.c_void_p(dy.handle.value)
+            N.check(lib.b2m_matmul_f32(ctx.handle, da.handle, None, wb.handle, mode, ctypes.byref(h)))
+        ms = _time_calls(torch, stream, call, steps * 10, warmup)
+        flop = 2 * 128 * 384 * 1536
+        out.append({"case": f"config1_matmul_f32_{name}", "us_per_call": ms * 1e3,
+                    "TFLOPs": flop / (ms / 1e3) / 1e12, "GBps": 4 * (128 * 384 + 384 * 1536 + 128 * 1536) / (ms / 1e3) / 1e9})
+    bq = rng.integers(-127, 128, (1024, 3072)).astype(np.int8)
+    wi = ctx.prepack_i8(bq)
+    az = ctx.upload(np.array(128, np.uint8))
+    bz = ctx.upload(rng.integers(-4, 5, (3072,)).astype(np.int8))
+    for m in (1, 64, 512):
+        ai = ctx.upload(rng.integers(0, 256, (m, 1024)).astype(np.uint8))
+        yi = ctx.empty((m, 3072), np.int32)
+
+        def call():
+            h = ctypes.c_void_p(yi.handle.value)
+            N.check(lib.b2m_matmul_integer(ctx.handle, ai.handle, None, wi.handle, az.handle, bz.handle,
+                                           ctypes.byref(h)))
+        ms = _time_calls(torch, stream, call, steps * 10, warmup)
+        ops = 2 * m * 1024 * 3072
+        by = m * 1024 + 1024 * 3072 + 3072 + m * 3072 * 4
+        out.append({"case": f"config2_matmulinteger_m{m}", "us_per_call": ms * 1e3, "TOPs": ops / (ms / 1e3) / 1e12,
+                    "GBps": by / (ms / 1e3) / 1e9})
+    return out
+
+
+# ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
 
@@ -176,8 +235,9 @@ def main():
     ap.add_argument("--passes", type=int, default=64,
                     help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill"],
-                    help="run one phase only (for profiler captures); prints its device time")
+    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill", "ops"],
+                    help="run one phase only (for profiler captures); prints its device time. "
+                         "`ops` times BASELINE configs 1 and 2 (fp32 MatMul, MatMulInteger)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -263,6 +323,13 @@ def main():
         return ms, clocks
 
     hbm_peak, tc_peak, peak_src = peaks()
+
+    if args.case == "ops":
+        for line in other_configs(ctx, lib, N, stream, dev, args.steps, args.warmup):
+            if rank == 0:
+                print(json.dumps(line), flush=True)
+        ctx.close()
+        return
 
     if args.case != "all":
         m = {"decode1": 1, "decode8": 8, "prefill": 512}[args.case]

@@ -32,14 +32,19 @@ constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;           // one 128-byte swizzle row of f16
 constexpr uint32_t TC_WAIT_LIMIT = 1u << 26;
 
-template <int BN, int STAGES>
+// Shared-memory layout of one CTA: STAGES stages of KS 64-k chunks each, A
+// (activation, 128 rows) and B (weight, BN rows) sub-tiles per chunk, all in
+// the 128-byte swizzle, then the mbarriers.
+template <int BN, int STAGES, int KS>
 struct TcLayout {
-  static constexpr uint32_t A_STAGE = TC_BM * TC_BK * 2;  // 16 KB
-  static constexpr uint32_t B_STAGE = BN * TC_BK * 2;
+  static constexpr uint32_t A_CHUNK = TC_BM * TC_BK * 2;  // 16 KB
+  static constexpr uint32_t B_CHUNK = BN * TC_BK * 2;
+  static constexpr uint32_t A_STAGE = KS * A_CHUNK;
+  static constexpr uint32_t B_STAGE = KS * B_CHUNK;
   static constexpr uint32_t A_OFF = 0;
   static constexpr uint32_t B_OFF = A_OFF + STAGES * A_STAGE;
   static constexpr uint32_t BAR_OFF = B_OFF + STAGES * B_STAGE;
-  static constexpr uint32_t BARS = 3 * STAGES + 1;
+  static constexpr uint32_t BARS = 2 * STAGES + 1;
   static constexpr uint32_t SLOT_OFF = BAR_OFF + BARS * 8;
   static constexpr uint32_t FLAG_OFF = SLOT_OFF + 8;
   static constexpr uint32_t BYTES = FLAG_OFF + 8 + 1024;  // + alignment slack
@@ -186,36 +191,39 @@ __device__ __forceinline__ void store_recs(const RecS &r, uint8_t *b_stage, int 
   }
 }
 
-template <int BN, int STAGES, int ZPK, bool BS16, bool SREC, int DQG, int PF>
+template <int BN, int STAGES, int KS, int ZPK, bool BS16, bool SREC, int DQG, int PF>
 __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
     nbits_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const NbitsWeight w, const float *bias, float *Y,
                     int M, int N, int32_t *dev_err) {
-  using L = TcLayout<BN, STAGES>;
+  using L = TcLayout<BN, STAGES, KS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-  uint64_t *full_a = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-  uint64_t *full_b = full_a + STAGES;
-  uint64_t *empty = full_b + STAGES;
+  // One "full" barrier per stage completes when the activation TMA bytes have
+  // landed AND every dequant thread of the stage has arrived, so the MMA
+  // thread waits once per stage: each mbarrier wait stalls that thread for
+  // ~150 cycles in which it issues no MMA.
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+  uint64_t *empty = full + STAGES;
   uint64_t *accum = empty + STAGES;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG_OFF);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * BN, m0 = blockIdx.y * TC_BM;
-  const int nk = (int)(w.kp / TC_BK);
-  const int nchunks = nk;
+  const int nchunks = (int)(w.kp / TC_BK);
+  const int nst = (nchunks + KS - 1) / KS;
   const int nb = (int)w.nblocks;
   const int groups = (int)((w.nblocks * w.block + 31) >> 5);
   // CTAs sharing an M tile would otherwise request the same activation k-tile
-  // at the same moment and queue on the same L2 slices; each column tile
-  // walks K from its own starting point instead (the accumulation order is
-  // still fixed per output element, so results stay deterministic).
-  const int krot = (int)(((unsigned)blockIdx.x * 7u) % (unsigned)nk);
+  // at the same moment; each column tile walks K from its own starting stage
+  // (the accumulation order is still fixed per output element, so results
+  // stay deterministic).
+  const int krot = (int)(((unsigned)blockIdx.x * 7u) % (unsigned)nst);
+  auto stage_of = [&](int st) { return st + krot < nst ? st + krot : st + krot - nst; };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; s++) {
-      mbar_init(&full_a[s], 1);
-      mbar_init(&full_b[s], (BN / 16) * 32);
+      mbar_init(&full[s], 1 + (BN / 16) * 32);
       mbar_init(&empty[s], 1);
     }
     mbar_init(accum, 1);
@@ -232,37 +240,44 @@ __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
   if (warp == 0) {
     if (lane == 0) {
       int issued = 0;
-      for (int kb = 0; kb < nk; kb++) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+      for (int st = 0; st < nst; st++) {
+        const int s = st % STAGES;
+        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
         if (!wait_or_abort(&empty[s], ph ^ 1u, abort_flag, dev_err)) break;
-        mbar_arrive_expect_tx(&full_a[s], L::A_STAGE);
-        const int kt = kb + krot < nk ? kb + krot : kb + krot - nk;
-        tma_load_2d(smem + L::A_OFF + s * L::A_STAGE, &tmap_a, kt * TC_BK, m0, &full_a[s]);
-        issued = kb + 1;
+        const int rt = stage_of(st);
+        const int cnt = (rt * KS + KS <= nchunks) ? KS : nchunks - rt * KS;
+        mbar_arrive_expect_tx(&full[s], (uint32_t)cnt * L::A_CHUNK);
+        for (int c = 0; c < cnt; c++)
+          tma_load_2d(smem + L::A_OFF + s * L::A_STAGE + c * L::A_CHUNK, &tmap_a, (rt * KS + c) * TC_BK, m0,
+                      &full[s]);
+        issued = st + 1;
       }
       // Never leave a copy in flight into shared memory we are about to free.
       if (issued > 0) {
-        const int kb = issued - 1;
-        wait_or_abort(&full_a[kb % STAGES], (uint32_t)(kb / STAGES) & 1u, abort_flag, nullptr);
+        const int st = issued - 1;
+        wait_or_abort(&full[st % STAGES], (uint32_t)(st / STAGES) & 1u, abort_flag, nullptr);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc(TC_BM, BN, 1u, 0u, 0u);  // F32 <- F16 x F16
-      bool ok = true;
-      for (int kb = 0; kb < nk && ok; kb++) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-        ok = wait_or_abort(&full_a[s], ph, abort_flag, dev_err) && wait_or_abort(&full_b[s], ph, abort_flag, dev_err);
-        if (!ok) break;
+      for (int st = 0; st < nst; st++) {
+        const int s = st % STAGES;
+        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
+        if (!wait_or_abort(&full[s], ph, abort_flag, dev_err)) break;
         tc_fence_after();
+        const int rt = stage_of(st);
+        const int cnt = (rt * KS + KS <= nchunks) ? KS : nchunks - rt * KS;
         const uint32_t a_base = smem_u32(smem + L::A_OFF + s * L::A_STAGE);
         const uint32_t b_base = smem_u32(smem + L::B_OFF + s * L::B_STAGE);
 #pragma unroll
-        for (int kk = 0; kk < TC_BK / 16; kk++) {
-          umma_f16(tmem, sw128_kmajor_desc(a_base + kk * 32), sw128_kmajor_desc(b_base + kk * 32), idesc,
-                   (kb | kk) != 0 ? 1u : 0u);
+        for (int c = 0; c < KS; c++) {
+          if (c < cnt) {
+#pragma unroll
+            for (int kk = 0; kk < TC_BK / 16; kk++)
+              umma_f16(tmem, sw128_kmajor_desc(a_base + c * L::A_CHUNK + kk * 32),
+                       sw128_kmajor_desc(b_base + c * L::B_CHUNK + kk * 32), idesc, (st | c | kk) != 0 ? 1u : 0u);
+          }
         }
         umma_commit(&empty[s]);
       }
@@ -270,42 +285,54 @@ __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
     }
   } else {
     // Dequant producers: DQG groups of BN/16 warps; group gq handles the
-    // stages kb = gq, gq + DQG, ... and warp `rec` of a group owns record
-    // `rec` (16 columns x 64 k) of each of its stages. Every warp keeps its
-    // next PF stages' raw records in registers, so global-load latency
+    // stages gq, gq + DQG, ... and warp `rec` of a group owns record `rec`
+    // (16 columns x 64 k) of each chunk of its stages. Every warp keeps the
+    // raw records of its next PF stages in registers, so global-load latency
     // overlaps the dequantization of earlier stages.
     using RecT = typename std::conditional<SREC, RecS, Rec<BS16>>::type;
     const int dw = warp - 2;
     const int rec = dw % (BN / 16), gq = dw / (BN / 16);
-    auto load = [&](int kb) -> RecT {
-      const int kt = kb + krot < nk ? kb + krot : (kb + krot) % nk;
-      if constexpr (SREC) return load_recs(w, n0 / 16 + rec, kt, lane, nchunks);
-      else return load_rec<ZPK, BS16>(w, n0 / 16 + rec, kt, lane, nchunks, groups, nb);
+    auto load = [&](int st, int c) -> RecT {
+      const int ch = stage_of(st) * KS + c;
+      if constexpr (SREC) return load_recs(w, n0 / 16 + rec, ch < nchunks ? ch : 0, lane, nchunks);
+      else return load_rec<ZPK, BS16>(w, n0 / 16 + rec, ch < nchunks ? ch : 0, lane, nchunks, groups, nb);
     };
-    RecT ring[PF];
+    RecT ring[PF][KS];
 #pragma unroll
     for (int j = 0; j < PF; j++)
-      if (gq + j * DQG < nk) ring[j] = load(gq + j * DQG);
+#pragma unroll
+      for (int c = 0; c < KS; c++)
+        if (gq + j * DQG < nst) ring[j][c] = load(gq + j * DQG, c);
     bool alive = true;
-    for (int i0 = 0; gq + i0 * DQG < nk && alive; i0 += PF) {
+    for (int i0 = 0; gq + i0 * DQG < nst && alive; i0 += PF) {
 #pragma unroll
       for (int j = 0; j < PF; j++) {
-        const int kb = gq + (i0 + j) * DQG;
-        if (kb < nk && alive) {
-          const int s = kb % STAGES;
-          const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-          RecT nxt;
-          const int kn = kb + PF * DQG;
-          if (kn < nk) nxt = load(kn);
+        const int st = gq + (i0 + j) * DQG;
+        if (st < nst && alive) {
+          const int s = st % STAGES;
+          const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
+          RecT nxt[KS];
+          const int sn = st + PF * DQG;
+#pragma unroll
+          for (int c = 0; c < KS; c++)
+            if (sn < nst) nxt[c] = load(sn, c);
           if (!wait_or_abort(&empty[s], ph ^ 1u, abort_flag, dev_err)) {
             alive = false;
           } else {
+            const int rt = stage_of(st);
+            const int cnt = (rt * KS + KS <= nchunks) ? KS : nchunks - rt * KS;
             uint8_t *b_stage = smem + L::B_OFF + s * L::B_STAGE;
-            if constexpr (SREC) store_recs(ring[j], b_stage, rec * 16, lane);
-            else store_rec<BS16, false>(ring[j], b_stage, rec * 16, lane);
+#pragma unroll
+            for (int c = 0; c < KS; c++) {
+              if (c < cnt) {
+                if constexpr (SREC) store_recs(ring[j][c], b_stage + c * L::B_CHUNK, rec * 16, lane);
+                else store_rec<BS16, false>(ring[j][c], b_stage + c * L::B_CHUNK, rec * 16, lane);
+              }
+            }
             fence_proxy_async_smem();
-            mbar_arrive(&full_b[s]);
-            ring[j] = nxt;
+            mbar_arrive(&full[s]);
+#pragma unroll
+            for (int c = 0; c < KS; c++) ring[j][c] = nxt[c];
           }
         }
       }
@@ -400,27 +427,29 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-template <int BN, int STAGES, int ZPK, bool BS16, bool SREC, int DQG, int PF>
+template <int BN, int STAGES, int KS, int ZPK, bool BS16, bool SREC, int DQG, int PF>
 void launch_tc_t(const CUtensorMap &tm, const NbitsArgs &a, cudaStream_t s) {
-  using L = TcLayout<BN, STAGES>;
-  auto kern = nbits_tc_kernel<BN, STAGES, ZPK, BS16, SREC, DQG, PF>;
+  using L = TcLayout<BN, STAGES, KS>;
+  auto kern = nbits_tc_kernel<BN, STAGES, KS, ZPK, BS16, SREC, DQG, PF>;
   B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES));
   dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + TC_BM - 1) / TC_BM));
   kern<<<grid, (2 + DQG * (BN / 16)) * 32, L::BYTES, s>>>(tm, *a.w, a.bias, a.Y, (int)a.M, (int)a.N, a.dev_err);
   B2M_CUDA(cudaGetLastError());
 }
 
-template <int BN, int STAGES, int DQG, int PF>
+template <int BN, int STAGES, int KS, int DQG, int PF>
 void launch_tc_bn(const CUtensorMap &tm, const NbitsArgs &a, cudaStream_t s) {
   if (a.w->srec) {
-    launch_tc_t<BN, STAGES, 1, false, true, DQG, PF>(tm, a, s);
+    launch_tc_t<BN, STAGES, KS, 1, false, true, DQG, PF>(tm, a, s);
     return;
   }
+  // Generic records (fp32 scales, block 16, float zero points) are larger:
+  // a one-stage prefetch keeps them in registers.
   const bool bs16 = a.w->block == 16;
   switch (a.w->zp_kind) {
-    case 0: bs16 ? launch_tc_t<BN, STAGES, 0, true, false, DQG, PF>(tm, a, s) : launch_tc_t<BN, STAGES, 0, false, false, DQG, PF>(tm, a, s); break;
-    case 1: bs16 ? launch_tc_t<BN, STAGES, 1, true, false, DQG, PF>(tm, a, s) : launch_tc_t<BN, STAGES, 1, false, false, DQG, PF>(tm, a, s); break;
-    default: bs16 ? launch_tc_t<BN, STAGES, 2, true, false, DQG, PF>(tm, a, s) : launch_tc_t<BN, STAGES, 2, false, false, DQG, PF>(tm, a, s); break;
+    case 0: bs16 ? launch_tc_t<BN, STAGES, KS, 0, true, false, DQG, 1>(tm, a, s) : launch_tc_t<BN, STAGES, KS, 0, false, false, DQG, 1>(tm, a, s); break;
+    case 1: bs16 ? launch_tc_t<BN, STAGES, KS, 1, true, false, DQG, 1>(tm, a, s) : launch_tc_t<BN, STAGES, KS, 1, false, false, DQG, 1>(tm, a, s); break;
+    default: bs16 ? launch_tc_t<BN, STAGES, KS, 2, true, false, DQG, 1>(tm, a, s) : launch_tc_t<BN, STAGES, KS, 2, false, false, DQG, 1>(tm, a, s); break;
   }
 }
 
@@ -449,5 +478,5 @@ void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s) {
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
-  launch_tc_bn<128, 6, 2, 3>(tm, a, s);
+  launch_tc_bn<128, 3, 2, 2, 2>(tm, a, s);
 }
