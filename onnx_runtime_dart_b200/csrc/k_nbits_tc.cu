@@ -19,6 +19,7 @@
 // word and the CTA exits after releasing its TMEM.
 #include <cuda.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "b2m_internal.cuh"
@@ -193,8 +194,9 @@ __device__ __forceinline__ void store_recs(const RecS &r, uint8_t *b_stage, int 
 
 template <int BN, int STAGES, int KS, int ZPK, bool BS16, bool SREC, int DQG, int PF>
 __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
-    nbits_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const NbitsWeight w, const float *bias, float *Y,
-                    int M, int N, int32_t *dev_err) {
+    nbits_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_y,
+                    const NbitsWeight w, const float *bias, float *Y, int M, int N, int use_tma_store,
+                    int32_t *dev_err) {
   using L = TcLayout<BN, STAGES, KS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -239,6 +241,11 @@ __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      // The activation operand is written by the previous kernel (the f16
+      // conversion); everything before this point — TMEM, barriers, and the
+      // weight prefetch / dequant of the producer warps — overlaps it under
+      // programmatic dependent launch.
+      pdl_wait();
       int issued = 0;
       for (int st = 0; st < nst; st++) {
         const int s = st % STAGES;
@@ -342,37 +349,84 @@ __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
       const int q = warp & 3;
       const bool ok = wait_or_abort(accum, 0u, abort_flag, dev_err);
       tc_fence_after();
-      if (ok && !*abort_flag) {
-        const int row = m0 + q * 32 + lane;
-        const bool vec_store = (N & 3) == 0 && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) &&
-                               (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
+      pdl_wait();  // earlier kernels of the stream are complete before Y is written
+      const bool go = ok && !*abort_flag;
+      if (use_tma_store) {
+        if (go) {
+          // Stage 128 x 32 fp32 boxes in shared memory (the pipeline buffers
+          // are free once the accumulator is complete) in the 128-byte
+          // swizzle — conflict-free for one row per lane — and write each box
+          // with one TMA store; rows / columns past M, N are clipped.
+          uint8_t *stage_base = smem + L::A_OFF;
 #pragma unroll 1
-        for (int c = 0; c < BN / 16; c++) {
-          uint32_t r[16];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 16), r);
-          tmem_ld_wait();
-          if (row < M) {
-            float *yrow = Y + (size_t)row * N;
-            const int cb = n0 + c * 16;
-            if (vec_store && cb + 16 <= N) {
+          for (int cb = 0; cb < BN / 32; cb++) {
+            uint8_t *box = stage_base + cb * (TC_BM * 128);
+            const int r = q * 32 + lane;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              uint32_t v[16];
+              tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32 + h * 16), v);
+              tmem_ld_wait();
 #pragma unroll
               for (int j = 0; j < 16; j += 4) {
-                float4 o = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                                       __uint_as_float(r[j + 3]));
+                float4 o = make_float4(__uint_as_float(v[j]), __uint_as_float(v[j + 1]), __uint_as_float(v[j + 2]),
+                                       __uint_as_float(v[j + 3]));
+                const int col = n0 + cb * 32 + h * 16 + j;
                 if (bias) {
-                  const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + cb + j));
-                  o.x += b.x;
-                  o.y += b.y;
-                  o.z += b.z;
-                  o.w += b.w;
+                  o.x += col + 0 < N ? __ldg(bias + col + 0) : 0.f;
+                  o.y += col + 1 < N ? __ldg(bias + col + 1) : 0.f;
+                  o.z += col + 2 < N ? __ldg(bias + col + 2) : 0.f;
+                  o.w += col + 3 < N ? __ldg(bias + col + 3) : 0.f;
                 }
-                *reinterpret_cast<float4 *>(yrow + cb + j) = o;
+                const int chunk = (h * 16 + j) >> 2;  // 16-byte chunk of the 128-byte row
+                *reinterpret_cast<float4 *>(box + r * 128 + ((chunk ^ (r & 7)) << 4)) = o;
               }
-            } else {
+            }
+          }
+        }
+        // All four epilogue warps reach this barrier whatever their state.
+        fence_proxy_async_smem();
+        named_barrier_sync(1, 128);
+        if (go && warp == 2 && lane == 0) {
+          uint8_t *stage_base = smem + L::A_OFF;
+          for (int cb = 0; cb < BN / 32; cb++)
+            if (n0 + cb * 32 < N) tma_store_2d(&tmap_y, stage_base + cb * (TC_BM * 128), n0 + cb * 32, m0);
+          bulk_commit_group();
+          bulk_wait_group0();
+        }
+      } else if (go) {
+        const int row = m0 + q * 32 + lane;
+        {
+          const bool vec_store = (N & 3) == 0 && ((reinterpret_cast<uintptr_t>(Y) & 15) == 0) &&
+                                 (bias == nullptr || (reinterpret_cast<uintptr_t>(bias) & 15) == 0);
+#pragma unroll 1
+          for (int c = 0; c < BN / 16; c++) {
+            uint32_t r[16];
+            tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(c * 16), r);
+            tmem_ld_wait();
+            if (row < M) {
+              float *yrow = Y + (size_t)row * N;
+              const int cb = n0 + c * 16;
+              if (vec_store && cb + 16 <= N) {
 #pragma unroll
-              for (int j = 0; j < 16; j++) {
-                const int col = cb + j;
-                if (col < N) yrow[col] = __uint_as_float(r[j]) + (bias ? __ldg(bias + col) : 0.f);
+                for (int j = 0; j < 16; j += 4) {
+                  float4 o = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                                         __uint_as_float(r[j + 3]));
+                  if (bias) {
+                    const float4 b = __ldg(reinterpret_cast<const float4 *>(bias + cb + j));
+                    o.x += b.x;
+                    o.y += b.y;
+                    o.z += b.z;
+                    o.w += b.w;
+                  }
+                  *reinterpret_cast<float4 *>(yrow + cb + j) = o;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < 16; j++) {
+                  const int col = cb + j;
+                  if (col < N) yrow[col] = __uint_as_float(r[j]) + (bias ? __ldg(bias + col) : 0.f);
+                }
               }
             }
           }
@@ -391,24 +445,29 @@ __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
 // A[M][K] float32 -> A16[M][K8] f16 (zero padding up to K8, a multiple of 8);
 // with `perm`, k is permuted inside each aligned group of four as
 // (k0, k2, k1, k3), matching the dequantized weight tiles of store_recs.
-__global__ void f32_to_f16_rows(const float *A, __half *A16, int64_t M, int64_t K, int64_t K8, int perm) {
-  const int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-  if (idx >= M * K8) return;
-  const int64_t m = idx / K8, k = idx % K8;
-  float f[8];
-  const float *row = A + m * K;
+__global__ void __launch_bounds__(512) f32_to_f16_rows(const float *A, __half *A16, int64_t M, int64_t K, int64_t K8,
+                                                        int perm) {
+  pdl_launch_dependents();  // the GEMM may start its weight-side prologue now
+  pdl_wait();               // A (and the scratch we overwrite) are free to use
+  const int64_t total = M * K8;
+  for (int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x * 8) {
+    const int64_t m = idx / K8, k = idx % K8;
+    float f[8];
+    const float *row = A + m * K;
 #pragma unroll
-  for (int j = 0; j < 8; j++) f[j] = k + j < K ? row[k + j] : 0.f;
-  __align__(16) __half h[8];
-  if (perm) {
-    const int P[8] = {0, 2, 1, 3, 4, 6, 5, 7};
+    for (int j = 0; j < 8; j++) f[j] = k + j < K ? row[k + j] : 0.f;
+    __align__(16) __half h[8];
+    if (perm) {
+      const int P[8] = {0, 2, 1, 3, 4, 6, 5, 7};
 #pragma unroll
-    for (int j = 0; j < 8; j++) h[j] = __float2half_rn(f[P[j]]);
-  } else {
+      for (int j = 0; j < 8; j++) h[j] = __float2half_rn(f[P[j]]);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; j++) h[j] = __float2half_rn(f[j]);
+      for (int j = 0; j < 8; j++) h[j] = __float2half_rn(f[j]);
+    }
+    *reinterpret_cast<uint4 *>(A16 + idx) = *reinterpret_cast<const uint4 *>(h);
   }
-  *reinterpret_cast<uint4 *>(A16 + idx) = *reinterpret_cast<const uint4 *>(h);
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -428,28 +487,37 @@ EncodeTiledFn encode_fn() {
 }
 
 template <int BN, int STAGES, int KS, int ZPK, bool BS16, bool SREC, int DQG, int PF>
-void launch_tc_t(const CUtensorMap &tm, const NbitsArgs &a, cudaStream_t s) {
+void launch_tc_t(const CUtensorMap &tm, const CUtensorMap &ty, int use_ty, const NbitsArgs &a, cudaStream_t s) {
   using L = TcLayout<BN, STAGES, KS>;
   auto kern = nbits_tc_kernel<BN, STAGES, KS, ZPK, BS16, SREC, DQG, PF>;
   B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES));
   dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + TC_BM - 1) / TC_BM));
-  kern<<<grid, (2 + DQG * (BN / 16)) * 32, L::BYTES, s>>>(tm, *a.w, a.bias, a.Y, (int)a.M, (int)a.N, a.dev_err);
-  B2M_CUDA(cudaGetLastError());
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3((2 + DQG * (BN / 16)) * 32);
+  cfg.dynamicSmemBytes = L::BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, ty, *a.w, a.bias, a.Y, (int)a.M, (int)a.N, use_ty, a.dev_err));
 }
 
 template <int BN, int STAGES, int KS, int DQG, int PF>
-void launch_tc_bn(const CUtensorMap &tm, const NbitsArgs &a, cudaStream_t s) {
+void launch_tc_bn(const CUtensorMap &tm, const CUtensorMap &ty, int use_ty, const NbitsArgs &a, cudaStream_t s) {
   if (a.w->srec) {
-    launch_tc_t<BN, STAGES, KS, 1, false, true, DQG, PF>(tm, a, s);
+    launch_tc_t<BN, STAGES, KS, 1, false, true, DQG, PF>(tm, ty, use_ty, a, s);
     return;
   }
   // Generic records (fp32 scales, block 16, float zero points) are larger:
   // a one-stage prefetch keeps them in registers.
   const bool bs16 = a.w->block == 16;
   switch (a.w->zp_kind) {
-    case 0: bs16 ? launch_tc_t<BN, STAGES, KS, 0, true, false, DQG, 1>(tm, a, s) : launch_tc_t<BN, STAGES, KS, 0, false, false, DQG, 1>(tm, a, s); break;
-    case 1: bs16 ? launch_tc_t<BN, STAGES, KS, 1, true, false, DQG, 1>(tm, a, s) : launch_tc_t<BN, STAGES, KS, 1, false, false, DQG, 1>(tm, a, s); break;
-    default: bs16 ? launch_tc_t<BN, STAGES, KS, 2, true, false, DQG, 1>(tm, a, s) : launch_tc_t<BN, STAGES, KS, 2, false, false, DQG, 1>(tm, a, s); break;
+    case 0: bs16 ? launch_tc_t<BN, STAGES, KS, 0, true, false, DQG, 1>(tm, ty, use_ty, a, s) : launch_tc_t<BN, STAGES, KS, 0, false, false, DQG, 1>(tm, ty, use_ty, a, s); break;
+    case 1: bs16 ? launch_tc_t<BN, STAGES, KS, 1, true, false, DQG, 1>(tm, ty, use_ty, a, s) : launch_tc_t<BN, STAGES, KS, 1, false, false, DQG, 1>(tm, ty, use_ty, a, s); break;
+    default: bs16 ? launch_tc_t<BN, STAGES, KS, 2, true, false, DQG, 1>(tm, ty, use_ty, a, s) : launch_tc_t<BN, STAGES, KS, 2, false, false, DQG, 1>(tm, ty, use_ty, a, s); break;
   }
 }
 
@@ -465,9 +533,21 @@ bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N) {
 void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s) {
   const int64_t K8 = nbits_tc_k8(a.K);
   {
+    // At most one small CTA per SM, so the PDL-launched GEMM's CTAs find room
+    // and start their weight prologue while this kernel runs.
     const int64_t total = a.M * K8 / 8;
-    f32_to_f16_rows<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(a.A, a16, a.M, a.K, K8, a.w->srec ? 1 : 0);
-    B2M_CUDA(cudaGetLastError());
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(sms, (total + 511) / 512)));
+    cfg.blockDim = dim3(512);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_to_f16_rows, a.A, a16, a.M, a.K, K8, a.w->srec ? 1 : 0));
   }
   CUtensorMap tm;
   const cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)a.M};
@@ -478,5 +558,21 @@ void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s) {
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
-  launch_tc_bn<128, 3, 2, 2, 2>(tm, a, s);
+  // Output tensor map for the TMA-store epilogue (fp32 Y, 32 x 128 boxes,
+  // 128-byte swizzle); needs 16-byte aligned rows.
+  CUtensorMap ty;
+  int use_ty = 0;
+  if ((a.N % 4) == 0 && (reinterpret_cast<uintptr_t>(a.Y) & 15) == 0) {
+    const cuuint64_t ydims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+    const cuuint64_t ystr[1] = {(cuuint64_t)(a.N * 4)};
+    const cuuint32_t ybox[2] = {32, (cuuint32_t)TC_BM};
+    CUresult ry = encode_fn()(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.Y, ydims, ystr, ybox, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    B2M_REQUIRE(ry == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output");
+    use_ty = 1;
+  } else {
+    ty = tm;  // unused
+  }
+  launch_tc_bn<128, 3, 2, 2, 2>(tm, ty, use_ty, a, s);
 }

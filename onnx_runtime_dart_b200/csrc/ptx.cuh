@@ -104,6 +104,20 @@ __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, 
       : "memory");
 }
 
+// 2-D tiled TMA store shared -> global (bulk-group completion); coordinates
+// (innermost, outer) in elements. Out-of-range parts of the box are clipped.
+__device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the bulk stores committed by this thread have completed.
+__device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void *tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
