@@ -333,9 +333,9 @@ def main():
 
     if args.case != "all":
         m = {"decode1": 1, "decode8": 8, "prefill": 512}[args.case]
-        ms_c, _ = run_graph(m, R, args.steps, args.warmup)
+        ms_c, clk_c = run_graph(m, R, args.steps, args.warmup)
         if rank == 0:
-            print(json.dumps({"case": args.case, "M": m, "layers": R, "steps": args.steps,
+            print(json.dumps({"case": args.case, "M": m, "layers": R, "steps": args.steps, "clocks": clk_c,
                               "us_per_launch": ms_c * 1e3 / (args.steps * R),
                               "GBps": args.steps * R * launch_bytes(m) / (ms_c / 1e3) / 1e9,
                               "TFLOPs": args.steps * R * 2 * m * K_DIM * N_DIM / (ms_c / 1e3) / 1e12}), flush=True)

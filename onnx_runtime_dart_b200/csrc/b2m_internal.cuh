@@ -106,6 +106,13 @@ struct NbitsWeight {
   // scales): [npad/16][kp/64][8] x 16 bytes, eight halves (s, 1024 + zp) for
   // columns g / g+8 of the two 32-k groups of a chunk; null otherwise.
   uint8_t *srec = nullptr;
+  // TMEM-operand prefill layout (same eligibility as srec). tsq: per
+  // (128-column tile, 64-k chunk) two 128 x 16-byte planes; column c's 32
+  // bytes hold its 64 nibbles, word j = k 8j..8j+7 at bit offsets
+  // 0,16,4,20,8,24,12,28. tss: per (tile, chunk) 128 x 2 words, half2
+  // (s, 1024 + zp) of the chunk's two 32-k groups.
+  uint8_t *tsq = nullptr;
+  uint32_t *tss = nullptr;
 };
 
 // Packed int8 / uint8 weights: bt[npad][kpad] (K-major), colsum[n] = sum_k b.
@@ -187,6 +194,9 @@ void launch_nbits_dequant_f32(const NbitsWeight &w, int64_t K, int64_t N, float 
 int64_t nbits_tc_k8(int64_t K);
 bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N);
 void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s);
+// The TMEM-operand variant (weights with tsq/tss), called by launch_nbits_tc
+// after the activation conversion.
+void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s);
 
 // MatMulInteger / QLinearMatMul
 struct I8GemmArgs {

@@ -24,6 +24,7 @@
 
 #include "b2m_internal.cuh"
 #include "ptx.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
@@ -31,7 +32,6 @@ using namespace b2m;
 
 constexpr int TC_BM = 128;
 constexpr int TC_BK = 64;           // one 128-byte swizzle row of f16
-constexpr uint32_t TC_WAIT_LIMIT = 1u << 26;
 
 // Shared-memory layout of one CTA: STAGES stages of KS 64-k chunks each, A
 // (activation, 128 rows) and B (weight, BN rows) sub-tiles per chunk, all in
@@ -55,18 +55,6 @@ struct TcLayout {
 // Byte offset of (row, k) inside a 128-byte-swizzled K-major tile of f16.
 __device__ __forceinline__ uint32_t sw128_off(int row, int k) {
   return (uint32_t)(row * 128 + ((((k >> 3) ^ (row & 7))) << 4) + ((k & 7) << 1));
-}
-
-__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
-                                              int32_t *dev_err) {
-  for (uint32_t i = 0; i < TC_WAIT_LIMIT; i++) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 1023) == 1023 && *abort_flag) return false;
-    if (i > 256) __nanosleep(64);
-  }
-  *abort_flag = 1;
-  if (dev_err) atomicExch(dev_err, B2M_DEVERR_MBAR_TIMEOUT);
-  return false;
 }
 
 // One 16-column x 64-k record of packed weights with its scales / zero
@@ -446,7 +434,7 @@ __global__ void __launch_bounds__((2 + DQG * (BN / 16)) * 32, 1)
 // with `perm`, k is permuted inside each aligned group of four as
 // (k0, k2, k1, k3), matching the dequantized weight tiles of store_recs.
 __global__ void __launch_bounds__(512) f32_to_f16_rows(const float *A, __half *A16, int64_t M, int64_t K, int64_t K8,
-                                                        int perm) {
+                                                        int perm, int vec) {
   pdl_launch_dependents();  // the GEMM may start its weight-side prologue now
   pdl_wait();               // A (and the scratch we overwrite) are free to use
   const int64_t total = M * K8;
@@ -455,8 +443,14 @@ __global__ void __launch_bounds__(512) f32_to_f16_rows(const float *A, __half *A
     const int64_t m = idx / K8, k = idx % K8;
     float f[8];
     const float *row = A + m * K;
+    if (vec) {  // rows start 16-byte aligned and K % 4 == 0: two 16-byte loads
+      const float4 lo = __ldg(reinterpret_cast<const float4 *>(row + k));
+      const float4 hi = k + 4 < K ? __ldg(reinterpret_cast<const float4 *>(row + k + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      f[0] = lo.x, f[1] = lo.y, f[2] = lo.z, f[3] = lo.w, f[4] = hi.x, f[5] = hi.y, f[6] = hi.z, f[7] = hi.w;
+    } else {
 #pragma unroll
-    for (int j = 0; j < 8; j++) f[j] = k + j < K ? row[k + j] : 0.f;
+      for (int j = 0; j < 8; j++) f[j] = k + j < K ? row[k + j] : 0.f;
+    }
     __align__(16) __half h[8];
     if (perm) {
       const int P[8] = {0, 2, 1, 3, 4, 6, 5, 7};
@@ -468,22 +462,6 @@ __global__ void __launch_bounds__(512) f32_to_f16_rows(const float *A, __half *A
     }
     *reinterpret_cast<uint4 *>(A16 + idx) = *reinterpret_cast<const uint4 *>(h);
   }
-}
-
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
-                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
-                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void *p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    B2M_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
-    B2M_REQUIRE(p && q == cudaDriverEntryPointSuccess, B2M_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
-    fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
 }
 
 template <int BN, int STAGES, int KS, int ZPK, bool BS16, bool SREC, int DQG, int PF>
@@ -523,6 +501,41 @@ void launch_tc_bn(const CUtensorMap &tm, const CUtensorMap &ty, int use_ty, cons
 
 }  // namespace
 
+namespace b2m {
+
+EncodeTiledFn tensor_map_encoder() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    B2M_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q));
+    B2M_REQUIRE(p && q == cudaDriverEntryPointSuccess, B2M_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+void launch_f32_to_f16(const float *A, __half *A16, int64_t M, int64_t K, int64_t K8, int perm, cudaStream_t s) {
+  // At most one small CTA per SM, so the PDL-launched GEMM's CTAs find room
+  // and start their weight prologue while this kernel runs.
+  const int64_t total = M * K8 / 8;
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(sms, (total + 511) / 512)));
+  cfg.blockDim = dim3(512);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const int vec = (K % 4) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_to_f16_rows, A, A16, M, K, K8, perm, vec));
+}
+
+}  // namespace b2m
+
 int64_t nbits_tc_k8(int64_t K) { return (K + 7) / 8 * 8; }
 
 bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N) {
@@ -532,29 +545,18 @@ bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N) {
 
 void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s) {
   const int64_t K8 = nbits_tc_k8(a.K);
-  {
-    // At most one small CTA per SM, so the PDL-launched GEMM's CTAs find room
-    // and start their weight prologue while this kernel runs.
-    const int64_t total = a.M * K8 / 8;
-    int sms = 148;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(sms, (total + 511) / 512)));
-    cfg.blockDim = dim3(512);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_to_f16_rows, a.A, a16, a.M, a.K, K8, a.w->srec ? 1 : 0));
+  if (a.w->tsq) {
+    launch_f32_to_f16(a.A, a16, a.M, a.K, K8, 0, s);
+    launch_nbits_ts(a, a16, K8, s);
+    return;
   }
+  launch_f32_to_f16(a.A, a16, a.M, a.K, K8, a.w->srec ? 1 : 0, s);
   CUtensorMap tm;
   const cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)a.M};
   const cuuint64_t strides[1] = {(cuuint64_t)(K8 * 2)};
   const cuuint32_t box[2] = {(cuuint32_t)TC_BK, (cuuint32_t)TC_BM};
   const cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a16, dims, strides, box, estr,
+  CUresult r = tensor_map_encoder()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a16, dims, strides, box, estr,
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
@@ -566,7 +568,7 @@ void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s) {
     const cuuint64_t ydims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     const cuuint64_t ystr[1] = {(cuuint64_t)(a.N * 4)};
     const cuuint32_t ybox[2] = {32, (cuuint32_t)TC_BM};
-    CUresult ry = encode_fn()(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.Y, ydims, ystr, ybox, estr,
+    CUresult ry = tensor_map_encoder()(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.Y, ydims, ystr, ybox, estr,
                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     B2M_REQUIRE(ry == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output");

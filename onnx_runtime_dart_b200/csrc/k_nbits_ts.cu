@@ -1,0 +1,336 @@
+// MatMulNBits prefill GEMM with the dequantized weights as the TMEM operand,
+// reference: opMatMulNBits m > 1 path, lib/src/onnx_qlinear_ops.dart:208-226.
+//
+//   Y^T[N, M] = dequant(W)[N, K] . A[M, K]^T     (f16 operands, fp32 accumulate)
+//
+// One CTA owns 128 weight columns x BT tokens. The weight tile is the MMA's A
+// operand and lives in tensor memory: dequant warps turn the int4 nibbles into
+// f16 in registers and write them with tcgen05.st, so the weights never touch
+// shared memory. The activations (converted to f16 by the kernel launched
+// before this one) are the B operand, brought into 128-byte-swizzled shared
+// memory by TMA. Shared memory then carries only the activation stream (one
+// TMA write and one MMA read per byte), half of what a kernel with both
+// operands in shared memory moves per MMA cycle.
+//
+//   warp 0      TMA producer for the activation stages.
+//   warp 1      TMEM allocation; one thread issues tcgen05.mma (A from TMEM).
+//   warps 2-9   two dequant groups of four warps (one per TMEM lane quarter)
+//               taking alternate 128-k stages; each thread owns one weight
+//               column. After the main loop they are the epilogue: tcgen05.ld
+//               of the accumulator (lane = weight column, column = token), add
+//               bias, coalesced stores of Y rows.
+// Accumulator in TMEM columns [0, BT); A stages from column A_COL0 on, 64
+// columns per 128-k stage (two f16 per 32-bit column, k order).
+// Every mbarrier wait is bounded; a timeout sets the context's device error
+// word and the CTA exits after releasing its TMEM.
+#include <cuda.h>
+
+#include <algorithm>
+
+#include "b2m_internal.cuh"
+#include "ptx.cuh"
+#include "tc_common.cuh"
+
+namespace {
+
+using namespace b2m;
+
+constexpr int TS_THREADS = 320;
+constexpr uint32_t TS_TMEM_COLS = 512;
+
+// BT tokens per CTA; a pipeline stage is KSUB chunks of 64 k.
+template <int BT, int STAGES, int KSUB>
+struct TsLayout {
+  static constexpr uint32_t B_CHUNK = (uint32_t)BT * 128;  // 64 k x BT tokens of f16
+  static constexpr uint32_t B_STAGE = KSUB * B_CHUNK;
+  static constexpr uint32_t BAR_OFF = STAGES * B_STAGE;
+  static constexpr uint32_t SLOT_OFF = BAR_OFF + (2 * STAGES + 1) * 8;
+  static constexpr uint32_t FLAG_OFF = SLOT_OFF + 8;
+  static constexpr uint32_t BYTES = FLAG_OFF + 8 + 1024;  // + alignment slack
+  static constexpr uint32_t A_COL0 = (uint32_t)(BT + 31) / 32 * 32;
+  static constexpr uint32_t A_STAGE_COLS = KSUB * 32;
+  static_assert(BT % 32 == 0 && BT >= 32 && BT <= 256, "token tile: multiple of 32 in [32, 256]");
+  static_assert(KSUB == 2 || KSUB == 4, "stage: 128 or 256 k");
+  static_assert(A_COL0 + STAGES * A_STAGE_COLS <= TS_TMEM_COLS, "accumulator + weight stages exceed TMEM");
+  static_assert(BYTES <= 232448, "shared memory");
+};
+
+// The raw weights of one 64-k chunk for one column: 64 nibbles and the two
+// (s, 1024 + zp) pairs of its 32-k groups.
+struct TsRec {
+  uint4 v0, v1;
+  uint2 sz;
+};
+
+// Nibble word j holds k 8j .. 8j+7 at bit offsets 0,16,4,20,8,24,12,28, so
+// (x >> 4i) & 0x000F000F carries the pair (8j+2i, 8j+2i+1); OR-ing 0x6400
+// into each half gives the f16 numbers 1024 + q exactly, 1024 + q - (1024 +
+// zp) = q - zp is exact, and the product with the f16 scale rounds once.
+__device__ __forceinline__ void ts_dequant(const TsRec &r, uint32_t (&out)[32]) {
+  const uint32_t w[8] = {r.v0.x, r.v0.y, r.v0.z, r.v0.w, r.v1.x, r.v1.y, r.v1.z, r.v1.w};
+#pragma unroll
+  for (int g = 0; g < 2; g++) {
+    const uint32_t e = g ? r.sz.y : r.sz.x;
+    const __half2 ss = u32_as_h2(prmt(e, e, 0x1010u));
+    const __half2 zz = u32_as_h2(prmt(e, e, 0x3232u));
+#pragma unroll
+    for (int jj = 0; jj < 4; jj++) {
+      const uint32_t x = w[g * 4 + jj];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        const uint32_t p = ((x >> (4 * i)) & 0x000F000Fu) | 0x64006400u;
+        out[(g * 4 + jj) * 4 + i] = h2_as_u32(__hmul2(__hsub2(u32_as_h2(p), zz), ss));
+      }
+    }
+  }
+}
+
+template <int BT, int STAGES, int KSUB>
+__global__ void __launch_bounds__(TS_THREADS, 1)
+    nbits_ts_kernel(const __grid_constant__ CUtensorMap tmap_a, const uint4 *__restrict__ tsq,
+                    const uint2 *__restrict__ tss, const float *__restrict__ bias, float *__restrict__ Y, int M, int N,
+                    int nchunks, int32_t *dev_err) {
+  using L = TsLayout<BT, STAGES, KSUB>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+  // full[s]: the stage's activation bytes landed (TMA, one arrival + tx) and
+  // its weights are in TMEM (one arrival per dequant warp); empty[s]: the MMAs
+  // reading the stage completed; accum: the whole accumulator is final.
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+  uint64_t *empty = full + STAGES;
+  uint64_t *accum = empty + STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L::SLOT_OFF);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG_OFF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile = blockIdx.x;
+  const int n0 = tile * 128, t0 = blockIdx.y * BT;
+  const int nst = (nchunks + KSUB - 1) / KSUB;
+  // The CTAs of one token tile would otherwise request the same activation
+  // k-tile at the same moment; each weight tile walks K from its own starting
+  // stage (the summation order stays fixed per output element).
+  const int krot = (int)(((unsigned)blockIdx.x * 7u) % (unsigned)nst);
+  auto stage_of = [&](int st) { return st + krot < nst ? st + krot : st + krot - nst; };
+  auto chunks_of = [&](int rt) { return min(KSUB, nchunks - rt * KSUB); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      mbar_init(&full[s], 1 + 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(accum, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+    prefetch_tmap(&tmap_a);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TS_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // Every CTA is resident: the next kernel of the stream may launch and wait
+  // for this grid on the SMs' spare room.
+  pdl_launch_dependents();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // The activations are written by the conversion kernel launched just
+      // before; TMEM, barriers and the first weight stages overlap it.
+      pdl_wait();
+      int issued = 0;
+      for (int st = 0; st < nst; st++) {
+        const int s = st % STAGES;
+        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
+        if (!wait_or_abort(&empty[s], ph ^ 1u, abort_flag, dev_err)) break;
+        const int rt = stage_of(st);
+        const int cnt = chunks_of(rt);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)cnt * L::B_CHUNK);
+        for (int c = 0; c < cnt; c++)
+          tma_load_2d(smem + s * L::B_STAGE + c * L::B_CHUNK, &tmap_a, (rt * KSUB + c) * 64, t0, &full[s]);
+        issued = st + 1;
+      }
+      // Never leave a copy in flight into shared memory that is about to be freed.
+      if (issued > 0) {
+        const int st = issued - 1;
+        wait_or_abort(&full[st % STAGES], (uint32_t)(st / STAGES) & 1u, abort_flag, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc(128, BT, 1u, 0u, 0u);  // F32 <- F16 x F16, both K-major
+      // Descriptors are formed by adding 16-byte offsets to stage 0's (the
+      // start-address field cannot overflow below 256 KB of shared memory).
+      // Every readiness check in this thread stalls the MMA issue for about
+      // one MMA's time, so a stage carries 8 or 16 MMAs per check.
+      const uint64_t bdesc0 = sw128_kmajor_desc(smem_u32(smem));
+      for (int st = 0; st < nst; st++) {
+        const int s = st % STAGES;
+        const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
+        if (!wait_or_abort(&full[s], ph, abort_flag, dev_err)) break;
+        tc_fence_after();
+        const uint64_t bd = bdesc0 + (uint64_t)(((uint32_t)s * L::B_STAGE) >> 4);
+        const uint32_t a_col = tmem + L::A_COL0 + (uint32_t)s * L::A_STAGE_COLS;
+        const int cnt = chunks_of(stage_of(st));
+        if (cnt == KSUB) {
+#pragma unroll
+          for (int h = 0; h < KSUB / 2; h++)
+            umma_f16_ts_stage(tmem, a_col + h * 64, bd + h * (2 * L::B_CHUNK >> 4), L::B_CHUNK >> 4, idesc,
+                              (st | h) != 0 ? 1u : 0u);
+        } else {  // K tail: the last stage holds fewer chunks
+          for (int c = 0; c < cnt; c++)
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+              umma_f16_ts(tmem, a_col + (uint32_t)(c * 32 + kk * 8), bd + (uint64_t)(c * (L::B_CHUNK >> 4) + 2 * kk),
+                          idesc, (st | c | kk) != 0 ? 1u : 0u);
+        }
+        umma_commit(&empty[s]);
+      }
+      umma_commit(accum);
+    }
+  } else {
+    const int q = warp & 3;          // TMEM lane quarter this warp may access
+    const int gq = (warp - 2) >> 2;  // dequant group: stages gq, gq + 2, ...
+    const int cl = q * 32 + lane;    // weight column within the tile
+    const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
+    const uint4 *qcol = tsq + (size_t)tile * nchunks * 256 + cl;
+    const uint2 *scol = tss + (size_t)tile * nchunks * 128 + cl;
+    auto load = [&](int st, int c) -> TsRec {
+      int ch = stage_of(st) * KSUB + c;
+      if (ch >= nchunks) ch = nchunks - 1;  // K tail: loaded, never used
+      TsRec r;
+      r.v0 = __ldg(qcol + (size_t)(2 * ch) * 128);
+      r.v1 = __ldg(qcol + (size_t)(2 * ch + 1) * 128);
+      r.sz = __ldg(scol + (size_t)ch * 128);
+      return r;
+    };
+    // One stage of raw records per thread; chunk c of the group's next stage
+    // is requested as soon as chunk c of this one is dequantized, so every
+    // load has about two stages of time to arrive.
+    TsRec ring[KSUB];
+#pragma unroll
+    for (int c = 0; c < KSUB; c++)
+      if (gq < nst) ring[c] = load(gq, c);
+    for (int st = gq; st < nst; st += 2) {
+      const int s = st % STAGES;
+      const uint32_t ph = (uint32_t)(st / STAGES) & 1u;
+      if (!warp_wait_or_abort(&empty[s], ph ^ 1u, abort_flag, dev_err)) break;
+      tc_fence_after();
+      const int cnt = chunks_of(stage_of(st));
+      const bool more = st + 2 < nst;
+#pragma unroll
+      for (int c = 0; c < KSUB; c++) {
+        if (c < cnt) {
+          uint32_t o[32];
+          ts_dequant(ring[c], o);
+          tmem_st32(lane_base + L::A_COL0 + (uint32_t)(s * L::A_STAGE_COLS + c * 32), o);
+        }
+        if (more) ring[c] = load(st + 2, c);
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+    }
+    // Epilogue: group gq stores tokens [gq * BT/2, (gq + 1) * BT/2) of the tile.
+    const bool ok = warp_wait_or_abort(accum, 0u, abort_flag, dev_err);
+    tc_fence_after();
+    pdl_wait();  // earlier kernels of the stream are complete before Y is written
+    int go = ok && !*abort_flag;
+    go = __shfl_sync(0xffffffffu, go, 0);
+    if (go) {
+      const int col = n0 + cl;
+      const bool colok = col < N;
+      const float b = (bias && colok) ? __ldg(bias + col) : 0.f;
+      // All TMEM loads of a group of up to 64 tokens go out before one wait;
+      // a wait per 16 columns serializes the load latency.
+      constexpr int HALF = BT / 2;
+      constexpr int GRP = HALF % 64 == 0 ? 64 : HALF % 48 == 0 ? 48 : HALF % 32 == 0 ? 32 : 16;
+      static_assert(HALF % GRP == 0, "epilogue groups must tile the half tile");
+#pragma unroll 1
+      for (int c0 = gq * HALF; c0 < (gq + 1) * HALF; c0 += GRP) {
+        uint32_t v[GRP];
+#pragma unroll
+        for (int j = 0; j < GRP; j += 16)
+          tmem_ld16(lane_base + (uint32_t)(c0 + j), *reinterpret_cast<uint32_t(*)[16]>(&v[j]));
+        tmem_ld_wait();
+        if (colok) {
+          float *yc = Y + (size_t)(t0 + c0) * N + col;
+          const int lim = M - (t0 + c0);
+#pragma unroll
+          for (int j = 0; j < GRP; j++)
+            if (j < lim) yc[(size_t)j * N] = __uint_as_float(v[j]) + b;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TS_TMEM_COLS);
+  }
+}
+
+template <int BT, int STAGES, int KSUB>
+void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s) {
+  using L = TsLayout<BT, STAGES, KSUB>;
+  CUtensorMap tm;
+  const cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)a.M};
+  const cuuint64_t strides[1] = {(cuuint64_t)(K8 * 2)};
+  const cuuint32_t box[2] = {64u, (cuuint32_t)BT};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = tensor_map_encoder()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(a16), dims, strides,
+                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
+  auto kern = nbits_ts_kernel<BT, STAGES, KSUB>;
+  B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.w->npad / 128), (unsigned)((a.M + BT - 1) / BT));
+  cfg.blockDim = dim3(TS_THREADS);
+  cfg.dynamicSmemBytes = L::BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, reinterpret_cast<const uint4 *>(a.w->tsq),
+                              reinterpret_cast<const uint2 *>(a.w->tss), a.bias, a.Y, (int)a.M, (int)a.N,
+                              (int)(a.w->kp / 64), a.dev_err));
+}
+
+// Token-tile width. Per CTA: MMA time (a readiness check per stage caps the
+// issue rate at about one MMA per 64 cycles, so tiles under 128 tokens cost as
+// much per k-step as 128), the output burst (BT x 128 fp32, write throughput
+// per SM is the limit: about half a column-unit per token) and a fixed cost;
+// times the number of waves over the SMs.
+int nbits_ts_pick_bt(int64_t M, int64_t N, int sms) {
+  static const int cand[] = {256, 192, 128, 96};
+  const int64_t ntile = (N + 127) / 128;
+  int best = 128;
+  int64_t best_cost = -1;
+  for (int bt : cand) {
+    const int64_t ctas = ntile * ((M + bt - 1) / bt);
+    const int64_t waves = (ctas + sms - 1) / sms;
+    const int64_t cost = waves * (2 * std::max(bt, 128) + bt + 64);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      best = bt;
+    }
+  }
+  return best;
+}
+
+}  // namespace
+
+void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  switch (nbits_ts_pick_bt(a.M, a.N, sms)) {
+    case 256: launch_ts_t<256, 3, 2>(a, a16, K8, s); break;
+    case 192: launch_ts_t<192, 4, 2>(a, a16, K8, s); break;
+    case 128: launch_ts_t<128, 3, 4>(a, a16, K8, s); break;
+    default: launch_ts_t<96, 3, 4>(a, a16, K8, s); break;
+  }
+}

@@ -170,6 +170,45 @@ __device__ __forceinline__ void umma_f16(uint32_t tmem_d, uint64_t da, uint64_t 
       : "memory");
 }
 
+// A operand from TMEM (128 lanes = rows of A, K packed two f16 per 32-bit
+// column in k order), B from shared memory.
+__device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
+// One 128-k stage of TS MMAs (two 64-k chunks x four K=16 steps) as a single
+// asm statement: all addresses are formed before the first MMA issues, so the
+// eight tcgen05.mma go out back to back. `bd` is the stage's first B
+// descriptor; chunk c starts `b_chunk16` 16-byte units further, each K=16
+// step 2 units (32 bytes); the A operand advances 32 TMEM columns per chunk
+// and 8 per step. `accum` = 0 overwrites D with the first product.
+__device__ __forceinline__ void umma_f16_ts_stage(uint32_t tmem_d, uint32_t a, uint64_t bd, uint32_t b_chunk16,
+                                                  uint32_t idesc, uint32_t accum) {
+  const uint64_t c1 = bd + b_chunk16;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %18, 0;\n\t"
+      "setp.eq.b32 q, %17, %17;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %9, %17, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%2], %10, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%3], %11, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%4], %12, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%5], %13, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%6], %14, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%7], %15, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%8], %16, %17, q;\n\t"
+      "}" ::"r"(tmem_d),
+      "r"(a), "r"(a + 8), "r"(a + 16), "r"(a + 24), "r"(a + 32), "r"(a + 40), "r"(a + 48), "r"(a + 56),
+      "l"(bd), "l"(bd + 2), "l"(bd + 4), "l"(bd + 6), "l"(c1), "l"(c1 + 2), "l"(c1 + 4), "l"(c1 + 6),
+      "r"(idesc), "r"(accum)
+      : "memory");
+}
+
 __device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
@@ -194,6 +233,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
       : "r"(taddr)
       : "memory");
 }
+// 32 registers per thread -> 32 lanes x 32 consecutive 32-bit TMEM columns.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 }  // namespace b2m

@@ -905,6 +905,48 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
                 srec[o + 1] = __float2half_rn(1024.f + zv);
               }
     }
+    // TMEM-operand prefill layout (k_nbits_ts.cu), same eligibility.
+    std::vector<uint8_t> tsq;
+    std::vector<uint32_t> tss;
+    if (W.f16_scales && block_size >= 32) {
+      static const int pos[8] = {0, 16, 4, 20, 8, 24, 12, 28};
+      tsq.assign((size_t)(npad * kp / 2), 0);
+      tss.assign((size_t)(npad * nchunks * 2), 0u);
+      for (int64_t c = 0; c < npad; c++) {
+        const int64_t tile = c / 128, cl = c % 128;
+        const uint8_t *src = c < n ? b_q + c * nb * blob : nullptr;
+        for (int64_t ch = 0; ch < nchunks; ch++) {
+          for (int j = 0; j < 8; j++) {
+            uint32_t word = 0;
+            for (int i = 0; i < 8; i++) {
+              const int64_t kk = ch * 64 + 8 * j + i;
+              if (src && kk < nb * block_size) {
+                const uint8_t byte = src[kk / 2];
+                word |= (uint32_t)((kk & 1) ? (byte >> 4) : (byte & 15)) << pos[i];
+              }
+            }
+            const size_t off = ((size_t)((tile * nchunks + ch) * 2 + j / 4) * 128 + (size_t)cl) * 16 + (j % 4) * 4;
+            std::memcpy(&tsq[off], &word, 4);
+          }
+          for (int g = 0; g < 2; g++) {
+            const int64_t blk = (ch * 64 + g * 32) / block_size;
+            float sv = 0.f, zv = 8.f;
+            if (c < n && blk < nb) {
+              sv = scales[c * nb + blk];
+              if (zp_dtype == B2M_UINT8) {
+                const uint8_t zb = static_cast<const uint8_t *>(zero_points)[c * zs + blk / 2];
+                zv = (float)((blk & 1) ? (zb >> 4) : (zb & 15));
+              }
+            }
+            const __half hs = __float2half_rn(sv), hz = __float2half_rn(1024.f + zv);
+            uint16_t us, uz;
+            std::memcpy(&us, &hs, 2);
+            std::memcpy(&uz, &hz, 2);
+            tss[((size_t)(tile * nchunks + ch) * 128 + (size_t)cl) * 2 + g] = (uint32_t)us | ((uint32_t)uz << 16);
+          }
+        }
+      }
+    }
     W.zstride = zs;
     W.kp = kp;
     W.npad = npad;
@@ -916,6 +958,12 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
       if (!srec.empty()) {
         B2M_CUDA(cudaMalloc(&W.srec, srec.size() * sizeof(__half)));
         B2M_CUDA(cudaMemcpy(W.srec, srec.data(), srec.size() * sizeof(__half), cudaMemcpyHostToDevice));
+      }
+      if (!tsq.empty()) {
+        B2M_CUDA(cudaMalloc(&W.tsq, tsq.size()));
+        B2M_CUDA(cudaMemcpy(W.tsq, tsq.data(), tsq.size(), cudaMemcpyHostToDevice));
+        B2M_CUDA(cudaMalloc(&W.tss, tss.size() * 4));
+        B2M_CUDA(cudaMemcpy(W.tss, tss.data(), tss.size() * 4, cudaMemcpyHostToDevice));
       }
       if (zp_dtype == B2M_UINT8) {
         std::vector<uint8_t> z((size_t)(npad * zs), 0);
@@ -936,6 +984,8 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
       cudaFree(W.zp_u8);
       cudaFree(W.zp_f32);
       cudaFree(W.srec);
+      cudaFree(W.tsq);
+      cudaFree(W.tss);
       delete w;
       throw;
     }
@@ -957,6 +1007,8 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     cudaFree(w->nb.zp_f32);
     cudaFree(w->nb.wdeq);
     cudaFree(w->nb.srec);
+    cudaFree(w->nb.tsq);
+    cudaFree(w->nb.tss);
     delete w;
   });
 }

@@ -1,0 +1,51 @@
+// Pieces shared by the tcgen05 GEMM kernels: bounded mbarrier waits and the
+// driver's tensor-map encoder.
+#pragma once
+
+#include <cuda.h>
+
+#include "b2m_internal.cuh"
+#include "ptx.cuh"
+
+namespace b2m {
+
+constexpr uint32_t TC_WAIT_LIMIT = 1u << 26;
+
+// Waits for phase `parity` of `bar`. Gives up when another thread of the CTA
+// has raised `abort_flag`, or after TC_WAIT_LIMIT polls (then raises the flag
+// and records a timeout in the context's device error word).
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                              int32_t *dev_err) {
+  for (uint32_t i = 0; i < TC_WAIT_LIMIT; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023) == 1023 && *abort_flag) return false;
+    if (i > 256) __nanosleep(64);
+  }
+  *abort_flag = 1;
+  if (dev_err) atomicExch(dev_err, B2M_DEVERR_MBAR_TIMEOUT);
+  return false;
+}
+
+// Lane 0 waits, the warp follows its verdict: every lane then takes the same
+// path through the warp-wide (.sync.aligned) tcgen05 instructions.
+__device__ __forceinline__ bool warp_wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_flag,
+                                                   int32_t *dev_err) {
+  int ok = 0;
+  if ((threadIdx.x & 31) == 0) ok = wait_or_abort(bar, parity, abort_flag, dev_err) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda
+// link dependency).
+EncodeTiledFn tensor_map_encoder();
+
+// f16 copy of the activations for the tensor-core kernels: A[M][K] fp32 ->
+// A16[M][K8] (K8 = K rounded up to 8, zero padded); with `perm` k is permuted
+// inside each aligned group of four as (k0, k2, k1, k3).
+void launch_f32_to_f16(const float *A, __half *A16, int64_t M, int64_t K, int64_t K8, int perm, cudaStream_t s);
+
+}  // namespace b2m

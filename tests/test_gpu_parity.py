@@ -303,6 +303,20 @@ def test_nbits_config3(ctx, m):
     bits_equal(exact, want)
 
 
+@pytest.mark.parametrize("m,n", [(416, 6400), (288, 6400), (224, 6400), (512, 3072), (200, 300)])
+def test_nbits_prefill_token_tiles(ctx, m, n):
+    # Shapes that select each prefill token-tile width (256, 192, 128, 96
+    # tokens on a 148-SM part), partial token tiles and a partial weight-column
+    # tile.
+    rng = np.random.default_rng(7000 + m + n)
+    a, bq, sc, z = nbits_case(rng, m, 1024, n, 32, "packed")
+    bias = rng.standard_normal((n,)).astype(np.float32)
+    want = oracle.matmul_nbits(a, bq, sc, z, 1024, n, 32, bias=bias, nthreads=8)
+    w = ops.prepack_nbits(ctx, bq, sc, z, k=1024, n=n, bits=4, blockSize=32)
+    fast = ops.opMatMulNBits(a, w, k=1024, n=n, blockSize=32, bias=bias, ctx=ctx).numpy()
+    assert_fast_close(fast, want, f"prefill m={m} n={n}")
+
+
 def test_nbits_batched_leading_dims_and_empty(ctx):
     rng = np.random.default_rng(1)
     a, bq, sc, z = nbits_case(rng, 6, 64, 24)
