@@ -116,11 +116,16 @@ struct NbitsWeight {
 };
 
 // Packed int8 / uint8 weights: bt[npad][kpad] (K-major), colsum[n] = sum_k b.
+// ts8: TMEM-operand / GEMV layout, per (128-column tile, 128-k chunk) eight
+// planes of 128 columns x 16 bytes; plane p holds k 16p..16p+15 of the chunk
+// for each column (k128 = K rounded up to 128).
 struct I8Weight {
   int8_t *bt = nullptr;
   int32_t *colsum = nullptr;
   int32_t dtype = 0;
   int64_t kpad = 0, npad = 0;
+  uint8_t *ts8 = nullptr;
+  int64_t k128 = 0;
 };
 
 struct b2m_weight {
@@ -221,7 +226,14 @@ struct I8GemmArgs {
   int requant = 0;
   double mult = 0.0;
   int32_t y_zp = 0, lo = 0, hi = 0;
+  int32_t *dev_err = nullptr;
+  // Scratch for the tensor-core path's activation row sums (M int32), used
+  // when there are b zero points.
+  int32_t *rowsum = nullptr;
 };
 void launch_i8_gemm(const I8GemmArgs &a, cudaStream_t s);
+// Tensor-core / GEMV path for a prepacked weight with ts8 (batch 1): true if
+// it handled the call. Needs a.rowsum (M int32 of scratch) for M > 16.
+bool launch_i8_tc(const I8GemmArgs &a, const I8Weight &w, cudaStream_t s);
 void launch_i8_pack(const void *B, int b_signed, int64_t batch, int64_t K, int64_t N, int8_t *bt,
                     int64_t kpad, int64_t npad, int32_t *colsum, cudaStream_t s);

@@ -181,6 +181,38 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t tmem_d, uint32_t tmem_a, ui
       : "memory");
 }
 
+// Eight TS MMAs of kind::i8 (two 128-byte chunks x four K=32 steps), same
+// operand walk as umma_f16_ts_stage (32 bytes of K per MMA either way).
+__device__ __forceinline__ void umma_i8_ts_stage(uint32_t tmem_d, uint32_t a, uint64_t bd, uint32_t b_chunk16,
+                                                 uint32_t idesc, uint32_t accum) {
+  const uint64_t c1 = bd + b_chunk16;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.b32 p, %18, 0;\n\t"
+      "setp.eq.b32 q, %17, %17;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %9, %17, p;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%2], %10, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%3], %11, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%4], %12, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%5], %13, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%6], %14, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%7], %15, %17, q;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%8], %16, %17, q;\n\t"
+      "}" ::"r"(tmem_d),
+      "r"(a), "r"(a + 8), "r"(a + 16), "r"(a + 24), "r"(a + 32), "r"(a + 40), "r"(a + 48), "r"(a + 56),
+      "l"(bd), "l"(bd + 2), "l"(bd + 4), "l"(bd + 6), "l"(c1), "l"(c1 + 2), "l"(c1 + 4), "l"(c1 + 6),
+      "r"(idesc), "r"(accum)
+      : "memory");
+}
+__device__ __forceinline__ void umma_i8_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                           uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(accum)
+      : "memory");
+}
+
 // One 128-k stage of TS MMAs (two 64-k chunks x four K=16 steps) as a single
 // asm statement: all addresses are formed before the first MMA issues, so the
 // eight tcgen05.mma go out back to back. `bd` is the stage's first B

@@ -462,7 +462,14 @@ void integer_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const 
   } else {
     p.Y32 = static_cast<int32_t *>(out->data);
   }
-  launch_i8_gemm(p, ctx->stream);
+  p.dev_err = ctx->dev_err;
+  bool done = false;
+  if (bw && batch == 1) {
+    Scratch rs(ctx, (size_t)m * 4 + 256);
+    p.rowsum = static_cast<int32_t *>(rs.take((size_t)m * 4));
+    done = launch_i8_tc(p, bw->i8, ctx->stream);
+  }
+  if (!done) launch_i8_gemm(p, ctx->stream);
   timer.done();
 }
 
@@ -809,10 +816,32 @@ B2M_API b2m_status b2m_weight_prepack_i8(b2m_ctx *ctx, const void *host_b, int32
     w->i8.dtype = dtype;
     w->i8.kpad = kpad;
     w->i8.npad = npad;
-    B2M_CUDA(cudaMalloc(&w->i8.bt, bt.size()));
-    B2M_CUDA(cudaMalloc(&w->i8.colsum, cs.size() * 4));
-    B2M_CUDA(cudaMemcpy(w->i8.bt, bt.data(), bt.size(), cudaMemcpyHostToDevice));
-    B2M_CUDA(cudaMemcpy(w->i8.colsum, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    // ts8: per (128-column tile, 128-k chunk) eight planes of 128 columns x
+    // 16 bytes (k_int8_tc.cu); zero padded to npad x k128.
+    const int64_t k128 = round_up(k, 128), nch = k128 / 128;
+    std::vector<uint8_t> ts8((size_t)(npad * k128), 0);
+    for (int64_t kk = 0; kk < k; kk++) {
+      const int64_t ch = kk / 128, pl = (kk % 128) / 16, by = kk % 16;
+      for (int64_t j = 0; j < n; j++) {
+        const int64_t tile = j / 128, cl = j % 128;
+        ts8[(size_t)((((tile * nch + ch) * 8 + pl) * 128 + cl) * 16 + by)] = src[kk * n + j];
+      }
+    }
+    w->i8.k128 = k128;
+    try {
+      B2M_CUDA(cudaMalloc(&w->i8.bt, bt.size()));
+      B2M_CUDA(cudaMalloc(&w->i8.colsum, cs.size() * 4));
+      B2M_CUDA(cudaMalloc(&w->i8.ts8, ts8.size()));
+      B2M_CUDA(cudaMemcpy(w->i8.bt, bt.data(), bt.size(), cudaMemcpyHostToDevice));
+      B2M_CUDA(cudaMemcpy(w->i8.colsum, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+      B2M_CUDA(cudaMemcpy(w->i8.ts8, ts8.data(), ts8.size(), cudaMemcpyHostToDevice));
+    } catch (...) {
+      cudaFree(w->i8.bt);
+      cudaFree(w->i8.colsum);
+      cudaFree(w->i8.ts8);
+      delete w;
+      throw;
+    }
     *out = w;
   });
 }
@@ -1001,6 +1030,7 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     cudaFree(w->f32);
     cudaFree(w->i8.bt);
     cudaFree(w->i8.colsum);
+    cudaFree(w->i8.ts8);
     cudaFree(w->nb.bq);
     cudaFree(w->nb.scales);
     cudaFree(w->nb.zp_u8);

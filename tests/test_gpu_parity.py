@@ -247,6 +247,45 @@ def test_qlinear_matmul_bitwise(ctx, out_int8, m):
     bits_equal(got, oracle.qlinear_matmul(a, a_s, az, b, b_s, bz, y_s, yz, lo, hi))
 
 
+@pytest.mark.parametrize("adt,bdt", [(np.uint8, np.int8), (np.uint8, np.uint8), (np.int8, np.int8),
+                                     (np.int8, np.uint8)])
+@pytest.mark.parametrize("zp", ["none", "scalar", "row_col"])
+@pytest.mark.parametrize("m,k,n", [(1, 1024, 300), (7, 208, 130), (16, 70, 45), (17, 1024, 200),
+                                   (100, 208, 257), (300, 512, 640)])
+def test_matmul_integer_packed_tensor_core(ctx, adt, bdt, zp, m, k, n):
+    # Prepacked weights: M <= 16 runs the dp4a GEMV, larger M the tcgen05
+    # kind::i8 kernel (K % 16 == 0; K=70 exercises the fallback), with K
+    # tails inside a 128-k chunk and partial column / token tiles.
+    rng = np.random.default_rng(m * 7919 + k * 31 + n)
+    a, b = _int_case(rng, m, k, n, adt, bdt)
+    az = bz = None
+    if zp == "scalar":
+        az = np.array(rng.integers(0, 100), adt)
+        bz = np.array(rng.integers(0, 100), bdt)
+    elif zp == "row_col":
+        az = rng.integers(0, 100, (m,)).astype(adt)
+        bz = rng.integers(0, 100, (n,)).astype(bdt)
+    w = ctx.prepack_i8(b)
+    got = ops.opMatMulInteger(a, w, az, bz, ctx=ctx).numpy()
+    bits_equal(got, oracle.matmul_integer(a, b, az, bz, nthreads=8))
+
+
+@pytest.mark.parametrize("out_int8", [False, True])
+@pytest.mark.parametrize("m", [1, 9, 64, 200])
+def test_qlinear_matmul_packed_bitwise(ctx, out_int8, m):
+    rng = np.random.default_rng(500 + m + 10 * out_int8)
+    k, n = 256, 384
+    a = rng.integers(0, 256, (m, k)).astype(np.uint8)
+    b = rng.integers(-128, 128, (k, n)).astype(np.int8)
+    a_s, b_s, y_s = np.float32(0.02), np.float32(0.05), np.float32(3.7 if out_int8 else 9.0)
+    az, bz = np.array(113, np.uint8), np.array(-3, np.int8)
+    lo, hi = (-128, 127) if out_int8 else (0, 255)
+    yz = np.array(3, np.int8) if out_int8 else np.array(100, np.uint8)
+    w = ctx.prepack_i8(b)
+    got = ops.opQLinearMatMul(a, a_s, az, w, b_s, bz, y_s, yz, lo=lo, hi=hi, ctx=ctx).numpy()
+    bits_equal(got, oracle.qlinear_matmul(a, a_s, az, b, b_s, bz, y_s, yz, lo, hi))
+
+
 def test_qlinear_per_channel_scale_unsupported(ctx):
     a = np.zeros((2, 3), np.uint8)
     b = np.zeros((3, 2), np.uint8)
