@@ -180,44 +180,86 @@ def _time_calls(torch, stream, fn, steps, warmup):
     return e0.elapsed_time(e1) / steps  # ms per call
 
 
+def _time_graph(torch, ctx, stream, calls, steps, warmup):
+    """Device time per call of `calls` (a list of zero-argument launchers)
+    captured back to back in one CUDA graph, replayed `steps` times."""
+    for fn in calls:  # eager warm-up outside capture (kernel attributes, scratch growth)
+        fn()
+    stream.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+        for fn in calls:
+            fn()
+    ctx.set_stream(stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, warmup)):
+            g.replay()
+    stream.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(steps):
+            g.replay()
+        e1.record(stream)
+    stream.synchronize()
+    del g
+    return e0.elapsed_time(e1) / (steps * len(calls))
+
+
 def other_configs(ctx, lib, N, stream, dev, steps, warmup):
     """Config 1: fp32 MatMul A[128,384] x B[384,1536] (B prepacked), EXACT and
     FAST modes. Config 2: MatMulInteger u8[M,1024] x i8[1024,3072], aZp=128,
-    per-column bZp in [-4,4], M in {1, 64, 512}. Device-resident inputs,
-    calls enqueued back to back on one stream."""
+    per-column bZp in [-4,4], M in {1, 64, 512}. Device-resident inputs.
+    `us_per_call`: eager calls through the C ABI, back to back on one stream
+    (host overhead included, one weight set). `graph_us_per_call`: the same
+    calls over SETS distinct weight sets and outputs (more than L2 holds)
+    captured in one CUDA graph: device time per op."""
     import torch
+    SETS = 64
     rng = np.random.default_rng(0)
     out = []
     a = rng.standard_normal((128, 384)).astype(np.float32)
-    b = (rng.standard_normal((384, 1536)) / np.sqrt(384)).astype(np.float32)
-    wb = ctx.prepack_f32(b)
     da = ctx.upload(a)
-    dy = ctx.empty((128, 1536))
-    for mode, name in ((N.MODE_EXACT, "exact"), (N.MODE_FAST, "fast")):
+    wbs = [ctx.prepack_f32((rng.standard_normal((384, 1536)) / np.sqrt(384)).astype(np.float32)) for _ in range(SETS)]
+    dys = [ctx.empty((128, 1536)) for _ in range(SETS)]
+
+    def f32_call(i, mode):
         def call():
-            h = ctypes.c_void_p(dy.handle.value)
-            N.check(lib.b2m_matmul_f32(ctx.handle, da.handle, None, wb.handle, mode, ctypes.byref(h)))
-        ms = _time_calls(torch, stream, call, steps * 10, warmup)
+            h = ctypes.c_void_p(dys[i].handle.value)
+            N.check(lib.b2m_matmul_f32(ctx.handle, da.handle, None, wbs[i].handle, mode, ctypes.byref(h)))
+        return call
+    for mode, name in ((N.MODE_EXACT, "exact"), (N.MODE_FAST, "fast")):
+        ms = _time_calls(torch, stream, f32_call(0, mode), steps * 10, warmup)
+        gms = _time_graph(torch, ctx, stream, [f32_call(i, mode) for i in range(SETS)], steps, warmup)
         flop = 2 * 128 * 384 * 1536
-        out.append({"case": f"config1_matmul_f32_{name}", "us_per_call": ms * 1e3,
-                    "TFLOPs": flop / (ms / 1e3) / 1e12, "GBps": 4 * (128 * 384 + 384 * 1536 + 128 * 1536) / (ms / 1e3) / 1e9})
-    bq = rng.integers(-127, 128, (1024, 3072)).astype(np.int8)
-    wi = ctx.prepack_i8(bq)
+        out.append({"case": f"config1_matmul_f32_{name}", "us_per_call": ms * 1e3, "graph_us_per_call": gms * 1e3,
+                    "TFLOPs": flop / (gms / 1e3) / 1e12,
+                    "GBps": 4 * (128 * 384 + 384 * 1536 + 128 * 1536) / (gms / 1e3) / 1e9})
+    for w in wbs:
+        w.free()
+    wis = [ctx.prepack_i8(rng.integers(-127, 128, (1024, 3072)).astype(np.int8)) for _ in range(SETS)]
     az = ctx.upload(np.array(128, np.uint8))
     bz = ctx.upload(rng.integers(-4, 5, (3072,)).astype(np.int8))
     for m in (1, 64, 512):
         ai = ctx.upload(rng.integers(0, 256, (m, 1024)).astype(np.uint8))
-        yi = ctx.empty((m, 3072), np.int32)
+        yis = [ctx.empty((m, 3072), np.int32) for _ in range(SETS)]
 
-        def call():
-            h = ctypes.c_void_p(yi.handle.value)
-            N.check(lib.b2m_matmul_integer(ctx.handle, ai.handle, None, wi.handle, az.handle, bz.handle,
-                                           ctypes.byref(h)))
-        ms = _time_calls(torch, stream, call, steps * 10, warmup)
+        def i8_call(i):
+            def call():
+                h = ctypes.c_void_p(yis[i].handle.value)
+                N.check(lib.b2m_matmul_integer(ctx.handle, ai.handle, None, wis[i].handle, az.handle, bz.handle,
+                                               ctypes.byref(h)))
+            return call
+        ms = _time_calls(torch, stream, i8_call(0), steps * 10, warmup)
+        gms = _time_graph(torch, ctx, stream, [i8_call(i) for i in range(SETS)], steps, warmup)
         ops = 2 * m * 1024 * 3072
         by = m * 1024 + 1024 * 3072 + 3072 + m * 3072 * 4
-        out.append({"case": f"config2_matmulinteger_m{m}", "us_per_call": ms * 1e3, "TOPs": ops / (ms / 1e3) / 1e12,
-                    "GBps": by / (ms / 1e3) / 1e9})
+        out.append({"case": f"config2_matmulinteger_m{m}", "us_per_call": ms * 1e3, "graph_us_per_call": gms * 1e3,
+                    "TOPs": ops / (gms / 1e3) / 1e12, "GBps": by / (gms / 1e3) / 1e9})
+    for w in wis:
+        w.free()
     return out
 
 

@@ -85,13 +85,9 @@ __device__ __forceinline__ int dp4(uint32_t a, uint32_t w, int c) {
   return d;
 }
 
-// The zero-point correction and the output conversion of one element.
+// The output conversion of one corrected int32 element.
 template <bool REQ>
-__device__ __forceinline__ void i8_store(const I8Epi &e, int64_t idx, int32_t raw, int32_t az, int32_t cs,
-                                         int32_t bz, int32_t rs, int32_t K) {
-  const uint32_t y = (uint32_t)raw - (uint32_t)az * (uint32_t)cs - (uint32_t)bz * (uint32_t)rs +
-                     (uint32_t)K * (uint32_t)az * (uint32_t)bz;
-  const int32_t yi = (int32_t)y;
+__device__ __forceinline__ void i8_emit(const I8Epi &e, int64_t idx, int32_t yi) {
   if constexpr (!REQ) {
     e.Y32[idx] = yi;
   } else {
@@ -108,7 +104,8 @@ struct I8Layout {
   static constexpr uint32_t B_CHUNK = (uint32_t)BT * 128;  // 128 k x BT tokens, one byte each
   static constexpr uint32_t B_STAGE = I8_KSUB * B_CHUNK;
   static constexpr uint32_t BAR_OFF = STAGES * B_STAGE;
-  static constexpr uint32_t SLOT_OFF = BAR_OFF + (2 * STAGES + 1) * 8;
+  static constexpr uint32_t TOK_OFF = BAR_OFF + (2 * STAGES + 1) * 8;  // az[BT], u[BT] int32
+  static constexpr uint32_t SLOT_OFF = TOK_OFF + (uint32_t)BT * 8;
   static constexpr uint32_t FLAG_OFF = SLOT_OFF + 8;
   static constexpr uint32_t BYTES = FLAG_OFF + 8 + 1024;  // + alignment slack
   static constexpr uint32_t A_COL0 = (uint32_t)(BT + 31) / 32 * 32;
@@ -245,6 +242,27 @@ __global__ void __launch_bounds__(I8_THREADS, 1)
     const bool ok = warp_wait_or_abort(accum, 0u, abort_flag, dev_err);
     tc_fence_after();
     pdl_wait();  // the row sums (and anything Y aliases) come from earlier kernels
+    // Per-token terms of the correction, y = raw - az(t) cs(n) - bz(n) u(t)
+    // with u(t) = rowsum(t) - K az(t), staged once per CTA in shared memory
+    // (read per element from global memory they are reloaded after every
+    // store, which may alias them).
+    int32_t *tok_az = reinterpret_cast<int32_t *>(smem + L::TOK_OFF);
+    int32_t *tok_u = tok_az + BT;
+    {
+      const int i = threadIdx.x - 64;  // 256 epilogue threads
+      for (int r = i; r < BT; r += 256) {
+        const int t = t0 + r;
+        int32_t az = 0, u = 0;
+        if (t < M) {
+          az = az_at(e, t);
+          const int32_t rs = e.bz_mode != 0 ? __ldg(rowsum + t) : 0;
+          u = (int32_t)((uint32_t)rs - (uint32_t)K * (uint32_t)az);
+        }
+        tok_az[r] = az;
+        tok_u[r] = u;
+      }
+    }
+    named_barrier_sync(1, 256);
     int go = ok && !*abort_flag;
     go = __shfl_sync(0xffffffffu, go, 0);
     if (go) {
@@ -263,12 +281,12 @@ __global__ void __launch_bounds__(I8_THREADS, 1)
           tmem_ld16(lane_base + (uint32_t)(c0 + j), *reinterpret_cast<uint32_t(*)[16]>(&v[j]));
         tmem_ld_wait();
         if (nok) {
+          const int lim = M - (t0 + c0);
 #pragma unroll
           for (int j = 0; j < GRP; j++) {
-            const int t = t0 + c0 + j;
-            if (t < M) {
-              const int32_t rs = e.bz_mode != 0 ? __ldg(rowsum + t) : 0;
-              i8_store<REQ>(e, (int64_t)t * N + n, (int32_t)v[j], az_at(e, t), cs, bz, rs, K);
+            if (j < lim) {
+              const uint32_t y = v[j] - (uint32_t)tok_az[c0 + j] * (uint32_t)cs - (uint32_t)bz * (uint32_t)tok_u[c0 + j];
+              i8_emit<REQ>(e, (int64_t)(t0 + c0 + j) * N + n, (int32_t)y);
             }
           }
         }
@@ -393,9 +411,12 @@ __global__ void __launch_bounds__(GV_THREADS)
 #pragma unroll
     for (int w = 0; w < 8; w++) raw += part[(w * M + m) * 32 + c];
     const int n = tile * 128 + qc * 32 + c;
-    if (n < N)
-      i8_store<REQ>(e, (int64_t)m * N + n, raw, az_at(e, m), __ldg(colsum + n), bz_at(e, n),
-                    e.bz_mode != 0 ? rows[m] : 0, K);
+    if (n < N) {
+      const int32_t az = az_at(e, m), bz = bz_at(e, n), rs = e.bz_mode != 0 ? rows[m] : 0;
+      const uint32_t y = (uint32_t)raw - (uint32_t)az * (uint32_t)__ldg(colsum + n) - (uint32_t)bz * (uint32_t)rs +
+                         (uint32_t)K * (uint32_t)az * (uint32_t)bz;
+      i8_emit<REQ>(e, (int64_t)m * N + n, (int32_t)y);
+    }
   }
 }
 
@@ -429,7 +450,7 @@ void launch_ts(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaStrea
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the int8 activations");
   auto kern = i8_ts_kernel<BT, STAGES, AS, WS, REQ>;
-  B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES));
+  set_smem_limit_once<i8_ts_kernel<BT, STAGES, AS, WS, REQ>>((int)L::BYTES);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(w.npad / 128), (unsigned)((a.M + BT - 1) / BT));
   cfg.blockDim = dim3(I8_THREADS);
@@ -460,8 +481,7 @@ void launch_ts_bt(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaSt
     B2M_CUDA(cudaLaunchKernelEx(&cfg, i8_rowsum_kernel<AS>, reinterpret_cast<const uint8_t *>(a.A), a.rowsum,
                                 (int)a.M, (int)a.K));
   }
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  const int sms = device_sm_count();
   switch (i8_pick_bt(a.M, a.N, sms)) {
     case 256: launch_ts<256, 3, AS, WS, REQ>(a, w, e, s); break;
     case 192: launch_ts<192, 4, AS, WS, REQ>(a, w, e, s); break;
@@ -474,7 +494,7 @@ template <bool AS, bool WS, bool REQ>
 void launch_gemv(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaStream_t s) {
   const size_t smem = (size_t)a.M * w.k128 + (size_t)8 * a.M * 32 * 4 + (size_t)a.M * 4;
   auto kern = i8_gemv_kernel<AS, WS, REQ>;
-  B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  set_smem_limit_once<i8_gemv_kernel<AS, WS, REQ>>(232448);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(w.npad / 128 * 4));
   cfg.blockDim = dim3(GV_THREADS);

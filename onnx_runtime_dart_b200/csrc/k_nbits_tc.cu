@@ -468,7 +468,7 @@ template <int BN, int STAGES, int KS, int ZPK, bool BS16, bool SREC, int DQG, in
 void launch_tc_t(const CUtensorMap &tm, const CUtensorMap &ty, int use_ty, const NbitsArgs &a, cudaStream_t s) {
   using L = TcLayout<BN, STAGES, KS>;
   auto kern = nbits_tc_kernel<BN, STAGES, KS, ZPK, BS16, SREC, DQG, PF>;
-  B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES));
+  set_smem_limit_once<nbits_tc_kernel<BN, STAGES, KS, ZPK, BS16, SREC, DQG, PF>>((int)L::BYTES);
   dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + TC_BM - 1) / TC_BM));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
@@ -503,6 +503,19 @@ void launch_tc_bn(const CUtensorMap &tm, const CUtensorMap &ty, int use_ty, cons
 
 namespace b2m {
 
+int device_sm_count() {
+  static std::atomic<int> cache[64] = {};
+  int dev = 0;
+  B2M_CUDA(cudaGetDevice(&dev));
+  std::atomic<int> &slot = cache[dev & 63];
+  int v = slot.load(std::memory_order_relaxed);
+  if (v == 0) {
+    B2M_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev));
+    slot.store(v, std::memory_order_relaxed);
+  }
+  return v;
+}
+
 EncodeTiledFn tensor_map_encoder() {
   static EncodeTiledFn fn = nullptr;
   if (!fn) {
@@ -519,8 +532,7 @@ void launch_f32_to_f16(const float *A, __half *A16, int64_t M, int64_t K, int64_
   // At most one small CTA per SM, so the PDL-launched GEMM's CTAs find room
   // and start their weight prologue while this kernel runs.
   const int64_t total = M * K8 / 8;
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  const int sms = device_sm_count();
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(sms, (total + 511) / 512)));
   cfg.blockDim = dim3(512);

@@ -284,7 +284,7 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
   auto kern = nbits_ts_kernel<BT, STAGES, KSUB>;
-  B2M_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L::BYTES));
+  set_smem_limit_once<nbits_ts_kernel<BT, STAGES, KSUB>>((int)L::BYTES);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.w->npad / 128), (unsigned)((a.M + BT - 1) / BT));
   cfg.blockDim = dim3(TS_THREADS);
@@ -325,8 +325,7 @@ int nbits_ts_pick_bt(int64_t M, int64_t N, int sms) {
 }  // namespace
 
 void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s) {
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+  const int sms = device_sm_count();
   switch (nbits_ts_pick_bt(a.M, a.N, sms)) {
     case 256: launch_ts_t<256, 3, 2>(a, a16, K8, s); break;
     case 192: launch_ts_t<192, 4, 2>(a, a16, K8, s); break;

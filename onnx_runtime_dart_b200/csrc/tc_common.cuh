@@ -4,6 +4,8 @@
 
 #include <cuda.h>
 
+#include <atomic>
+
 #include "b2m_internal.cuh"
 #include "ptx.cuh"
 
@@ -34,6 +36,22 @@ __device__ __forceinline__ bool warp_wait_or_abort(uint64_t *bar, uint32_t parit
   if ((threadIdx.x & 31) == 0) ok = wait_or_abort(bar, parity, abort_flag, dev_err) ? 1 : 0;
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
+
+// Raises kernel Kern's dynamic shared-memory limit to `bytes` once per device
+// (the attribute persists for the process), keeping it off the per-call path.
+template <auto Kern>
+void set_smem_limit_once(int bytes) {
+  static std::atomic<uint64_t> done{0};
+  int dev = 0;
+  B2M_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (done.load(std::memory_order_acquire) & bit) return;
+  B2M_CUDA(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  done.fetch_or(bit, std::memory_order_acq_rel);
+}
+
+// SM count of the current device, cached.
+int device_sm_count();
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
