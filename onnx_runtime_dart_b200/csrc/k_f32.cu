@@ -116,6 +116,92 @@ __global__ void __launch_bounds__(256) f32_exact_gemm_kernel(const F32GemmArgs p
   }
 }
 
+// Small-tile variant for grids that would underfill the SMs with 64 x 64
+// tiles (e.g. 128 x 1536 outputs): 32 x 32 outputs per CTA, 64 threads with
+// 4 x 4 outputs each, and the next 32-k slab fetched into registers while the
+// current one is consumed. Same per-element k order as above.
+constexpr int SBM = 32, SBN = 32, SBK = 32;
+
+__global__ void __launch_bounds__(64) f32_exact_gemm_small_kernel(const F32GemmArgs p) {
+  __shared__ __align__(16) float As[SBK][SBM + 4];
+  __shared__ __align__(16) float Bs[SBK][SBN + 4];
+  int64_t aoff, boff;
+  batch_offsets(p, blockIdx.z, aoff, boff);
+  const float *A = p.A + aoff;
+  const float *B = p.B + boff;
+  const int64_t m0 = (int64_t)blockIdx.y * SBM, n0 = (int64_t)blockIdx.x * SBN;
+  const int tid = threadIdx.x, tx = tid & 7, ty = tid >> 3;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; i++)
+#pragma unroll
+    for (int j = 0; j < 4; j++) acc[i][j] = 0.f;
+  float ra[16], rb[16];
+  // Element e = tid + 64 r of a slab: A is walked k-fastest, B n-fastest, so
+  // row-major operands load coalesced.
+  auto fetch = [&](int64_t k0) {
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const int e = tid + 64 * r;
+      const int kk = e & 31, mm = e >> 5;
+      const int64_t gi = m0 + mm, gk = k0 + kk;
+      ra[r] = (gi < p.M && gk < p.K) ? __ldg(A + gi * p.sa_m + gk * p.sa_k) : 0.f;
+      const int nn = e & 31, kb = e >> 5;
+      const int64_t gj = n0 + nn, gkb = k0 + kb;
+      rb[r] = (gj < p.N && gkb < p.K) ? __ldg(B + gkb * p.sb_k + gj * p.sb_n) : 0.f;
+    }
+  };
+  fetch(0);
+  for (int64_t k0 = 0; k0 < p.K; k0 += SBK) {
+#pragma unroll
+    for (int r = 0; r < 16; r++) {
+      const int e = tid + 64 * r;
+      As[e & 31][e >> 5] = ra[r];
+      Bs[e >> 5][e & 31] = rb[r];
+    }
+    __syncthreads();
+    if (k0 + SBK < p.K) fetch(k0 + SBK);
+    const int kmax = (p.K - k0) < SBK ? (int)(p.K - k0) : SBK;
+    if (kmax == SBK) {
+#pragma unroll 8
+      for (int kk = 0; kk < SBK; kk++) {
+        const float4 av = *reinterpret_cast<const float4 *>(&As[kk][ty * 4]);
+        const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][tx * 4]);
+        const float a_[4] = {av.x, av.y, av.z, av.w};
+        const float b_[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a_[i], b_[j]));
+      }
+    } else {
+      for (int kk = 0; kk < kmax; kk++) {
+        const float4 av = *reinterpret_cast<const float4 *>(&As[kk][ty * 4]);
+        const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][tx * 4]);
+        const float a_[4] = {av.x, av.y, av.z, av.w};
+        const float b_[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+          for (int j = 0; j < 4; j++) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(a_[i], b_[j]));
+      }
+    }
+    __syncthreads();
+  }
+  float *Y = p.Y + (int64_t)blockIdx.z * p.y_bstride;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int64_t gi = m0 + ty * 4 + i;
+    if (gi >= p.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const int64_t gj = n0 + tx * 4 + j;
+      if (gj >= p.N) continue;
+      Y[gi * p.ldy + gj] = epilogue_f32(p, acc[i][j], gi, gj);
+    }
+  }
+}
+
 // Double-accumulated columns. One thread per (row, column) of the double set.
 __global__ void __launch_bounds__(128) f32_double_cols_kernel(const F32GemmArgs p) {
   const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -148,7 +234,15 @@ void launch_f32_exact(const F32GemmArgs &a, cudaStream_t s) {
   if (!a.all_double) {
     dim3 grid((unsigned)((a.N + BN - 1) / BN), (unsigned)((a.M + BM - 1) / BM), (unsigned)a.batch);
     B2M_REQUIRE(grid.y <= 65535, B2M_ERR_UNSUPPORTED, "MatMul: too many rows");
-    f32_exact_gemm_kernel<<<grid, 256, 0, s>>>(a);
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    if ((int64_t)grid.x * grid.y * grid.z < 2 * (int64_t)sms) {
+      dim3 sg((unsigned)((a.N + SBN - 1) / SBN), (unsigned)((a.M + SBM - 1) / SBM), (unsigned)a.batch);
+      B2M_REQUIRE(sg.y <= 65535, B2M_ERR_UNSUPPORTED, "MatMul: too many rows");
+      f32_exact_gemm_small_kernel<<<sg, 64, 0, s>>>(a);
+    } else {
+      f32_exact_gemm_kernel<<<grid, 256, 0, s>>>(a);
+    }
     B2M_CUDA(cudaGetLastError());
   }
   if (any_double) {

@@ -93,6 +93,17 @@ def test_matmul_odd_shapes_bitwise(ctx, mkn):
     bits_equal(ops.opMatMul(a, b, ctx=ctx).numpy(), oracle.matmul(a, b))
 
 
+@pytest.mark.parametrize("mkn", [(1024, 96, 1280), (640, 130, 1000)])
+def test_matmul_large_tiles_bitwise(ctx, mkn):
+    # Grids large enough for the 64 x 64 tile kernel (the small-tile kernel
+    # serves underfilled grids such as config 1).
+    m, k, n = mkn
+    rng = np.random.default_rng(sum(mkn))
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = rng.standard_normal((k, n)).astype(np.float32)
+    bits_equal(ops.opMatMul(a, b, ctx=ctx).numpy(), oracle.matmul(a, b, nthreads=8))
+
+
 @pytest.mark.parametrize("ash,bsh", [
     ((2, 3, 5, 7), (2, 3, 7, 4)),     # fixture matmul_batched
     ((4, 1, 3), (3, 6)),              # shared 2-D B collapse: m=1 rows -> one m=4 GEMM
