@@ -133,6 +133,9 @@ struct b2m_weight {
   int kind = 0;
   int64_t k = 0, n = 0;
   float *f32 = nullptr;  // W_F32: [K][N] row-major
+  // W_F32 FAST-mode planes for 3xTF32: K-major [N][roundup(K,32)], hi = w
+  // with the low 13 mantissa bits cleared, lo = w - hi.
+  float *tf_hi = nullptr, *tf_lo = nullptr;
   I8Weight i8;
   NbitsWeight nb;
 };
@@ -178,9 +181,15 @@ struct F32GemmArgs {
   int has_beta = 0;
   float beta = 1.f;
   const float *bias = nullptr;
+  int32_t *dev_err = nullptr;
 };
 
 void launch_f32_exact(const F32GemmArgs &a, cudaStream_t s);
+// FAST fp32 GEMM (3xTF32 on tcgen05) for a prepacked weight and contiguous A
+// rows; `a_split` is scratch for 2 x M x f32_tc_kp(K) floats.
+int64_t f32_tc_kp(int64_t K);
+bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w);
+void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, float *a_split, cudaStream_t s);
 
 // MatMulNBits
 struct NbitsArgs {

@@ -184,6 +184,19 @@ void require_float(const b2m_tensor *t, const char *what) {
 // fp32 MatMul / Gemm
 // ---------------------------------------------------------------------------
 
+// FAST with a prepacked weight and contiguous A rows runs 3xTF32 on the
+// tensor cores; everything else (and EXACT) runs the bit-exact kernels.
+void run_f32(b2m_ctx *ctx, F32GemmArgs &p, const b2m_weight *bw, int32_t mode) {
+  p.dev_err = ctx->dev_err;
+  if (mode == B2M_MODE_FAST && f32_tc_eligible(p, bw)) {
+    const size_t need = (size_t)(2 * p.M * f32_tc_kp(p.K) * 4);
+    Scratch sc(ctx, need + 256);
+    launch_f32_tc(p, *bw, static_cast<float *>(sc.take(need)), ctx->stream);
+    return;
+  }
+  launch_f32_exact(p, ctx->stream);
+}
+
 void matmul_f32_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const b2m_weight *bw, int32_t mode,
                      b2m_tensor **y) {
   require_float(a, "MatMul A");
@@ -267,9 +280,7 @@ void matmul_f32_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, con
     }
     p.y_bstride = m * n;
   }
-  // FAST currently shares the exact kernel for fp32 MatMul (always within
-  // the fast-mode tolerance, since it is exact).
-  launch_f32_exact(p, ctx->stream);
+  run_f32(ctx, p, bw, mode);
   timer.done();
 }
 
@@ -353,7 +364,7 @@ void gemm_f32_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const
     p.has_beta = beta != 1.0f;
     p.beta = beta;
   }
-  launch_f32_exact(p, ctx->stream);
+  run_f32(ctx, p, bw, mode);
   timer.done();
 }
 
@@ -787,6 +798,33 @@ B2M_API b2m_status b2m_weight_prepack_f32(b2m_ctx *ctx, const float *host_b, int
       b2m_throw(B2M_ERR_OUT_OF_MEMORY, "weight allocation failed");
     }
     B2M_CUDA(cudaMemcpy(w->f32, src, (size_t)(K * N * 4), cudaMemcpyHostToDevice));
+    // 3xTF32 planes for FAST mode (k_f32_tc.cu): K-major, K padded to 32.
+    {
+      const int64_t kp = round_up(K, 32);
+      std::vector<float> hi((size_t)(N * kp), 0.f), lo((size_t)(N * kp), 0.f);
+      for (int64_t kk = 0; kk < K; kk++)
+        for (int64_t j = 0; j < N; j++) {
+          const float v = src[kk * N + j];
+          uint32_t u;
+          std::memcpy(&u, &v, 4);
+          u &= 0xFFFFE000u;
+          float h;
+          std::memcpy(&h, &u, 4);
+          hi[(size_t)(j * kp + kk)] = h;
+          lo[(size_t)(j * kp + kk)] = v - h;
+        }
+      cudaError_t e1 = cudaMalloc(&w->tf_hi, hi.size() * 4);
+      cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&w->tf_lo, lo.size() * 4) : e1;
+      if (e1 != cudaSuccess || e2 != cudaSuccess) {
+        (void)cudaGetLastError();
+        cudaFree(w->f32);
+        cudaFree(w->tf_hi);
+        delete w;
+        b2m_throw(B2M_ERR_OUT_OF_MEMORY, "weight allocation failed");
+      }
+      B2M_CUDA(cudaMemcpy(w->tf_hi, hi.data(), hi.size() * 4, cudaMemcpyHostToDevice));
+      B2M_CUDA(cudaMemcpy(w->tf_lo, lo.data(), lo.size() * 4, cudaMemcpyHostToDevice));
+    }
     *out = w;
   });
 }
@@ -1028,6 +1066,8 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     DeviceGuard dg(w->ctx->device);
     cudaStreamSynchronize(w->ctx->stream);
     cudaFree(w->f32);
+    cudaFree(w->tf_hi);
+    cudaFree(w->tf_lo);
     cudaFree(w->i8.bt);
     cudaFree(w->i8.colsum);
     cudaFree(w->i8.ts8);

@@ -131,6 +131,45 @@ def test_matmul_config1_bitwise_with_prepack(ctx):
     bits_equal(ops.opMatMul(a, b, ctx=ctx).numpy(), want)
 
 
+@pytest.mark.parametrize("mkn", [(128, 384, 1536), (1, 64, 100), (300, 200, 130), (700, 96, 2048),
+                                 (1300, 64, 1792), (5, 7, 33)])
+def test_matmul_fast_tensor_core(ctx, mkn):
+    # FAST mode with a prepacked weight: 3xTF32 on tcgen05, against the exact
+    # reference within the fast-mode tolerance (column tiles 32/64/128, K and
+    # N tails, rows beyond a 128-row tile).
+    m, k, n = mkn
+    rng = np.random.default_rng(11 * m + k + n)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
+    w = ctx.prepack_f32(b)
+    got = ops.opMatMul(a, w, mode=ops.MODE_FAST, ctx=ctx).numpy()
+    assert_fast_close(got, oracle.matmul(a, b, nthreads=8), f"fast matmul {mkn}")
+
+
+def test_matmul_fast_batched_shared_weight(ctx):
+    rng = np.random.default_rng(12)
+    a = rng.standard_normal((2, 3, 50, 64)).astype(np.float32)
+    b = rng.standard_normal((64, 40)).astype(np.float32)
+    w = ctx.prepack_f32(b)
+    got = ops.opMatMul(a, w, mode=ops.MODE_FAST, ctx=ctx).numpy()
+    assert got.shape == (2, 3, 50, 40)
+    assert_fast_close(got, oracle.matmul(a, b), "fast batched matmul")
+
+
+@pytest.mark.parametrize("alpha,beta,cshape", [(1.0, 1.0, (96,)), (0.5, 2.0, (200, 96)), (-1.5, 1.0, (200, 1)),
+                                               (2.0, 3.0, ()), (1.0, 1.0, None)])
+def test_gemm_fast_tensor_core(ctx, alpha, beta, cshape):
+    rng = np.random.default_rng(13)
+    M, K, N = 200, 72, 96
+    a = rng.standard_normal((M, K)).astype(np.float32)
+    bt = rng.standard_normal((N, K)).astype(np.float32)  # transB initializer
+    c = None if cshape is None else rng.standard_normal(cshape).astype(np.float32)
+    w = ctx.prepack_f32(bt, trans=True)
+    got = ops.opGemm(a, w, c, alpha=alpha, beta=beta, mode=ops.MODE_FAST, ctx=ctx).numpy()
+    want = oracle.gemm(a, bt, c, alpha=alpha, beta=beta, transB=True)
+    assert_fast_close(got, want, f"fast gemm alpha={alpha} beta={beta} c={cshape}")
+
+
 @pytest.mark.parametrize("ta,tb,alpha,beta,cshape", [
     (False, True, 1.0, 1.0, (6,)),
     (False, False, 0.5, 2.0, (1, 6)),
