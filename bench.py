@@ -398,9 +398,13 @@ def main():
     # M=8 decode (same rotation) and M=512 prefill (compute-bound).
     ms8, _ = run_graph(8, R, max(1, args.steps // 2), 3)
     gbs8 = args.steps // 2 * R * launch_bytes(8) / (ms8 / 1e3) / 1e9 if args.steps // 2 else None
-    Rp = min(R, 64)
+    Rp = R  # 256 distinct weight sets: the prefill weights do not stay in L2 either
     msp, _ = run_graph(512, Rp, max(1, args.steps // 4), 3)
     tflops_p = max(1, args.steps // 4) * Rp * 2 * 512 * K_DIM * N_DIM / (msp / 1e3) / 1e12
+
+    # BASELINE configs 1 and 2 (fp32 MatMul, int8 MatMulInteger): device time
+    # per op over 64 weight sets in a CUDA graph.
+    ops_lines = other_configs(ctx, lib, N, stream, dev, max(1, args.steps // 4), 3)
 
     # End to end through the host-buffer C-ABI call (pinned host memory).
     e2e_layers = min(R, 64)
@@ -452,6 +456,8 @@ def main():
             "decode_m8_gbs": None if gbs8 is None else round(gbs8, 2),
             "prefill_m512_tflops": round(tflops_p, 2),
             "prefill_m512_frac_of_bf16_peak": round(tflops_p / tc_peak, 4),
+            "prefill_m512_us_per_op": round(msp * 1e3 / (max(1, args.steps // 4) * Rp), 3),
+            "configs_1_2_device_us_per_op": {o["case"]: round(o["graph_us_per_call"], 3) for o in ops_lines},
         },
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic,

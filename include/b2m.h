@@ -249,6 +249,75 @@ B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m,
 B2M_API b2m_status b2m_matmul_nbits_noalloc(const b2m_weight *w, const float *a, int64_t m, const float *bias,
                                             float *y, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Device-resident glue for the transformer chains (configs 4 and 5), so that
+ * a chain of MatMuls never round-trips through host memory. All pointers are
+ * device memory of the context's device; the ops are enqueued on the current
+ * stream and return at once. Rows are contiguous (row length = d).
+ * ---------------------------------------------------------------------- */
+
+/* RMSNorm over the last axis: s = x (+ skip when non-NULL; s is stored to
+ * sum_out when non-NULL), y = s * gamma / sqrt(mean(s^2) + eps), statistics in
+ * double. Replaces opRMSNorm (lib/src/onnx_ops.dart:1771) and the fused
+ * SkipSimplifiedLayerNormalization (lib/src/onnx_graph.dart:1793). */
+B2M_API b2m_status b2m_rmsnorm_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma, float *y,
+                                   float *sum_out, int64_t rows, int64_t d, double eps);
+
+/* RMSNorm of every head vector of [tokens][heads x head_dim] rows placed
+ * token_stride floats apart (per-head q / k norms read from a packed
+ * projection output; y may alias x, with the same layout). */
+B2M_API b2m_status b2m_rmsnorm_heads_dev(b2m_ctx *ctx, const float *x, const float *gamma, float *y, int64_t tokens,
+                                         int64_t heads, int64_t head_dim, int64_t token_stride, double eps);
+
+/* LayerNormalization over the last axis (mean / variance in double), with an
+ * optional residual as above; beta may be NULL. Replaces
+ * opLayerNormalization (lib/src/onnx_ops.dart:1666). */
+B2M_API b2m_status b2m_layernorm_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma,
+                                     const float *beta, float *y, float *sum_out, int64_t rows, int64_t d,
+                                     double eps);
+
+/* y[r][c] = silu(gate[r*gate_rs + c]) * up[r*up_rs + c] for c < d (the
+ * Sigmoid/Mul pair of a SwiGLU MLP; gate and up may be the two halves of one
+ * packed projection). */
+B2M_API b2m_status b2m_silu_mul_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gate_rs,
+                                    int64_t up_rs, float *y, int64_t rows, int64_t d);
+
+/* erf GELU, y = 0.5 x (1 + erf(x / sqrt 2)) (opGelu, lib/src/onnx_ops.dart:706). */
+B2M_API b2m_status b2m_gelu_dev(b2m_ctx *ctx, const float *x, float *y, int64_t n);
+
+/* y = a + b over rows x d; with b_broadcast, b is one row of d added to every
+ * row (bias). */
+B2M_API b2m_status b2m_add_dev(b2m_ctx *ctx, const float *a, const float *b, float *y, int64_t rows, int64_t d,
+                               int32_t b_broadcast);
+
+/* y[r][:] = table[ids[r]][:] (Gather of embedding rows; ids int64 in [0, v)). */
+B2M_API b2m_status b2m_gather_rows_dev(b2m_ctx *ctx, const float *table, const int64_t *ids, float *y,
+                                       int64_t rows, int64_t v, int64_t d);
+
+/* out[r] = argmax over the v entries of row r (first maximum wins; int64),
+ * as opArgMinMax with keepdims over the last axis. */
+B2M_API b2m_status b2m_argmax_dev(b2m_ctx *ctx, const float *x, int64_t *out, int64_t rows, int64_t v);
+
+/* GroupQueryAttention (lib/src/onnx_ops.dart:1844) over a caller-owned KV
+ * cache. q: [b][s] rows of h*head_dim floats (row stride q_rs), k / v: [b][s]
+ * rows of kvh*head_dim (row stride kv_rs). k_cache / v_cache:
+ * [b][kvh][cap][head_dim]. past[b] (int32, device memory) is the number of
+ * positions already cached for sequence b: this call writes its keys/values
+ * at past[b] .. past[b]+s-1 (rotary applied to K) and attends causally over
+ * [0, past[b] + i] for query i. cos / sin: [max_pos][rotary_half] caches or
+ * NULL (no rotary); rotary_dim <= head_dim, interleaved as the attribute.
+ * Scale <= 0 means 1/sqrt(head_dim). out: [b][s] rows of h*head_dim.
+ * head_dim <= 256, h a multiple of kvh. Reading `past` from device memory
+ * lets a decode step replay as a CUDA graph. */
+B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                               int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
+                               const float *cos_cache, const float *sin_cache, int32_t rotary_half,
+                               int32_t rotary_dim, int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h,
+                               int32_t kvh, int32_t head_dim, int32_t cap, float scale);
+
+/* past[i] += delta for i < n (int32 device counters of a decode loop). */
+B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta);
+
 /* Shape of a packed weight: K and N (logical B is [K, N]). */
 B2M_API b2m_status b2m_weight_info(const b2m_weight *w, int64_t *k, int64_t *n);
 

@@ -129,6 +129,17 @@ SIGNATURES = {
     "b2m_matmul_nbits_host": (_i32, [_c_ctx, _vp, _i64, _c_weight, _vp, _i32, _vp]),
     "b2m_matmul_nbits_dev": (_i32, [_c_ctx, _vp, _i64, _c_weight, _vp, _i32, _vp]),
     "b2m_matmul_nbits_noalloc": (_i32, [_c_weight, _vp, _i64, _vp, _vp, _vp]),
+    "b2m_rmsnorm_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_double]),
+    "b2m_rmsnorm_heads_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_double]),
+    "b2m_layernorm_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_double]),
+    "b2m_silu_mul_dev": (_i32, [_c_ctx, _vp, _vp, _i64, _i64, _vp, _i64, _i64]),
+    "b2m_gelu_dev": (_i32, [_c_ctx, _vp, _vp, _i64]),
+    "b2m_add_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i32]),
+    "b2m_gather_rows_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i64]),
+    "b2m_argmax_dev": (_i32, [_c_ctx, _vp, _vp, _i64, _i64]),
+    "b2m_gqa_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32,
+                           _i32, _i32, _i32, _i32, _i32, _f32]),
+    "b2m_advance_positions_dev": (_i32, [_c_ctx, _vp, _i32, _i32]),
 }
 
 _lib = None

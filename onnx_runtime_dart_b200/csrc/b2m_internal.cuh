@@ -212,6 +212,24 @@ void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s);
 // after the activation conversion.
 void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s);
 
+// Transformer glue (k_glue.cu)
+void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
+                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s);
+void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
+                      float *sum_out, int64_t rows, int D, double eps, cudaStream_t s);
+void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
+                     int64_t D, cudaStream_t s);
+void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s);
+void launch_add(const float *a, const float *b, float *y, int64_t rows, int64_t D, int b_bcast, cudaStream_t s);
+void launch_gather_rows(const float *table, const int64_t *ids, float *y, int64_t rows, int64_t V, int64_t D,
+                        int32_t *err, cudaStream_t s);
+void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, cudaStream_t s);
+void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
+                float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
+                int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
+                cudaStream_t s);
+void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s);
+
 // MatMulInteger / QLinearMatMul
 struct I8GemmArgs {
   const void *A = nullptr;  // [batch_a][M][K] uint8 or int8

@@ -1,0 +1,349 @@
+// Device-resident glue for the MatMul chains of a transformer layer, so a
+// chain never round-trips through host memory between its MatMuls:
+//   RMSNorm (+ fused residual add)   opRMSNorm, onnx_ops.dart:1771; fused
+//                                    SkipSimplifiedLayerNormalization,
+//                                    onnx_graph.dart:1793
+//   LayerNormalization (+ residual)  opLayerNormalization, onnx_ops.dart:1666
+//   SwiGLU silu(gate) * up           the Sigmoid/Mul pair of the MLP
+//   erf GELU                         opGelu, onnx_ops.dart:706
+//   Gather of embedding rows         opGather
+//   ArgMax over the last axis        opArgMinMax, onnx_ops.dart (first max wins)
+//   GroupQueryAttention              opGroupQueryAttention, onnx_ops.dart:1844
+//                                    with rotary (opRotaryEmbedding, :2659)
+// The reductions accumulate in double where the reference does (norm
+// statistics, softmax sums); elementwise math is fp32. The attention keeps its
+// K/V in a caller-owned cache [B][KVH][CAP][D] and reads the number of cached
+// positions from device memory, so a decode step replays as a CUDA graph.
+#include <cfloat>
+
+#include "b2m_internal.cuh"
+
+namespace {
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// One warp per row of length D. With `skip`, the row is x + skip (stored to
+// `sum_out` when given) before normalising: y = s * inv * gamma, inv =
+// 1/sqrt(mean(s^2) + eps) with the mean accumulated in double.
+// Rows are laid out as groups of `per` rows of D (offset g*gstride + i*D for
+// row r = g*per + i); contiguous rows have per = rows, gstride = 0.
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *skip, const float *__restrict__ gamma,
+                                                      float *y, float *sum_out, int64_t rows, int D, double eps,
+                                                      int64_t per, int64_t gstride) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  const int64_t off = (r / per) * gstride + (r % per) * D;
+  const float *xr = x + off;
+  const float *sr = skip ? skip + off : nullptr;
+  double ss = 0.0;
+  for (int j = lane; j < D; j += 32) {
+    const float v = sr ? xr[j] + sr[j] : xr[j];
+    ss += (double)v * (double)v;
+  }
+  ss = warp_sum_d(ss);
+  const double inv = 1.0 / sqrt(ss / D + eps);
+  for (int j = lane; j < D; j += 32) {
+    const float v = sr ? xr[j] + sr[j] : xr[j];
+    if (sum_out) sum_out[off + j] = v;
+    y[off + j] = (float)((double)v * inv * (double)gamma[j]);
+  }
+}
+
+// LayerNormalization over the last axis (mean and variance in double).
+__global__ void __launch_bounds__(256) layernorm_kernel(const float *__restrict__ x, const float *__restrict__ skip,
+                                                        const float *__restrict__ gamma, const float *__restrict__ beta,
+                                                        float *y, float *sum_out, int64_t rows, int D, double eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  const float *xr = x + r * D;
+  const float *sr = skip ? skip + r * D : nullptr;
+  double s1 = 0.0;
+  for (int j = lane; j < D; j += 32) s1 += (double)(sr ? xr[j] + sr[j] : xr[j]);
+  const double mean = warp_sum_d(s1) / D;
+  double s2 = 0.0;
+  for (int j = lane; j < D; j += 32) {
+    const double d = (double)(sr ? xr[j] + sr[j] : xr[j]) - mean;
+    s2 += d * d;
+  }
+  const double inv = 1.0 / sqrt(warp_sum_d(s2) / D + eps);
+  for (int j = lane; j < D; j += 32) {
+    const float v = sr ? xr[j] + sr[j] : xr[j];
+    if (sum_out) sum_out[r * D + j] = v;
+    y[r * D + j] = (float)(((double)v - mean) * inv * (double)gamma[j] + (beta ? (double)beta[j] : 0.0));
+  }
+}
+
+// y = silu(gate) * up, with gate / up either separate tensors or the two
+// halves of one [rows][2*D] tensor (a packed gate|up projection).
+__global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__restrict__ up, int64_t g_rs,
+                                int64_t u_rs, float *y, int64_t rows, int64_t D) {
+  const int64_t total = rows * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / D, c = i % D;
+    const float g = gate[r * g_rs + c];
+    const float s = g / (1.f + expf(-g));
+    y[i] = s * up[r * u_rs + c];
+  }
+}
+
+__global__ void gelu_kernel(const float *__restrict__ x, float *y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = x[i];
+    y[i] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+  }
+}
+
+// y = a + b, b broadcast over rows when b_rows == 1.
+__global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, float *y, int64_t rows, int64_t D,
+                           int b_bcast) {
+  const int64_t total = rows * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = a[i] + b[b_bcast ? i % D : i];
+}
+
+// y[r][:] = table[ids[r]][:] (ids int64); out-of-range ids write zeros and
+// raise the error word.
+__global__ void gather_rows_kernel(const float *__restrict__ table, const int64_t *__restrict__ ids, float *y,
+                                   int64_t rows, int64_t V, int64_t D, int32_t *err) {
+  const int64_t r = blockIdx.x;
+  if (r >= rows) return;
+  const int64_t id = ids[r];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && threadIdx.x == 0 && err) atomicExch(err, 4);
+  for (int64_t j = threadIdx.x; j < D; j += blockDim.x) y[r * D + j] = ok ? table[id * D + j] : 0.f;
+}
+
+// Row argmax (first maximum wins; NaN compares false). One CTA per row.
+__global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ x, int64_t *out, int64_t V) {
+  const int64_t r = blockIdx.x;
+  const float *xr = x + r * V;
+  float best = -FLT_MAX;
+  int64_t bi = V;
+  for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
+    const float v = xr[j];
+    if (v > best || (bi == V && v == best)) {
+      best = v;
+      bi = j;
+    }
+  }
+  __shared__ float sv[512];
+  __shared__ int64_t si[512];
+  sv[threadIdx.x] = best;
+  si[threadIdx.x] = bi;
+  __syncthreads();
+  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
+    if (threadIdx.x < s) {
+      const float ov = sv[threadIdx.x + s];
+      const int64_t oi = si[threadIdx.x + s];
+      if (ov > sv[threadIdx.x] || (ov == sv[threadIdx.x] && oi < si[threadIdx.x])) {
+        sv[threadIdx.x] = ov;
+        si[threadIdx.x] = oi;
+      }
+    }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) out[r] = si[0] < V ? si[0] : 0;
+}
+
+// Rotary of one head vector in place (non-interleaved: pairs (i, i + half);
+// interleaved: pairs (2i, 2i+1)), positions index the cos/sin rows.
+__device__ __forceinline__ void rotate_head(float *v, const float *cos, const float *sin, int64_t pos, int half,
+                                            int rot, int interleaved, int lane_lo, int lane_step) {
+  for (int i = lane_lo; i < rot / 2; i += lane_step) {
+    const float c = cos[pos * half + i], s = sin[pos * half + i];
+    const int i0 = interleaved ? 2 * i : i, i1 = interleaved ? 2 * i + 1 : i + rot / 2;
+    const float x0 = v[i0], x1 = v[i1];
+    v[i0] = x0 * c - x1 * s;
+    v[i1] = x1 * c + x0 * s;
+  }
+}
+
+struct GqaArgs {
+  const float *q, *k, *v;   // [B][S][H*D], [B][S][KVH*D] (row strides below)
+  int64_t q_rs, kv_rs;      // floats between consecutive tokens
+  float *kcache, *vcache;   // [B][KVH][CAP][D]
+  const int32_t *past;      // [B] positions already cached (device memory)
+  const float *cos, *sin;   // [max_pos][half] or null (no rotary)
+  int half, rot, interleaved;
+  float *out;               // [B][S][H*D]
+  int B, S, H, KVH, D, CAP;
+  float scale;
+  int32_t *err;
+};
+
+// Appends this call's keys / values to the cache (rotary on K), one warp per
+// (token, kv head).
+__global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * 8 + warp;
+  const int64_t total = (int64_t)a.B * a.S * a.KVH;
+  if (item >= total) return;
+  const int kvh = (int)(item % a.KVH);
+  const int64_t bs = item / a.KVH;
+  const int s = (int)(bs % a.S), b = (int)(bs / a.S);
+  const int past = a.past[b];
+  const int pos = past + s;
+  if (pos >= a.CAP) {
+    if (lane == 0 && a.err) atomicExch(a.err, 5);
+    return;
+  }
+  __shared__ float kbuf[8][256];
+  float *kv = kbuf[warp];
+  const float *ksrc = a.k + (int64_t)(b * a.S + s) * a.kv_rs + kvh * a.D;
+  const float *vsrc = a.v + (int64_t)(b * a.S + s) * a.kv_rs + kvh * a.D;
+  for (int d = lane; d < a.D; d += 32) kv[d] = ksrc[d];
+  __syncwarp();
+  if (a.cos) rotate_head(kv, a.cos, a.sin, pos, a.half, a.rot, a.interleaved, lane, 32);
+  __syncwarp();
+  const int64_t dst = (((int64_t)b * a.KVH + kvh) * a.CAP + pos) * a.D;
+  for (int d = lane; d < a.D; d += 32) {
+    a.kcache[dst + d] = kv[d];
+    a.vcache[dst + d] = vsrc[d];
+  }
+}
+
+// Causal attention of a tile of query tokens of one (batch, query head)
+// against the cache [0, past + s]. One warp per query token: q (rotated) in
+// registers across lanes, online softmax over the keys, fp32 accumulation of
+// P.V in registers (D <= 256, 8 values per lane).
+__global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int s = blockIdx.x * 8 + warp;
+  if (s >= a.S) return;
+  const int kvh = h / (a.H / a.KVH);
+  const int past = a.past[b];
+  const int pos = past + s;
+  __shared__ float qbuf[8][256];
+  float *qv = qbuf[warp];
+  const float *qsrc = a.q + (int64_t)(b * a.S + s) * a.q_rs + h * a.D;
+  for (int d = lane; d < a.D; d += 32) qv[d] = qsrc[d];
+  __syncwarp();
+  if (a.cos) rotate_head(qv, a.cos, a.sin, pos, a.half, a.rot, a.interleaved, lane, 32);
+  __syncwarp();
+  float qr[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) qr[i] = lane + 32 * i < a.D ? qv[lane + 32 * i] : 0.f;
+  const float *kc = a.kcache + ((int64_t)b * a.KVH + kvh) * a.CAP * a.D;
+  const float *vc = a.vcache + ((int64_t)b * a.KVH + kvh) * a.CAP * a.D;
+  float m = -INFINITY, l = 0.f;
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i] = 0.f;
+  const int last = pos < a.CAP ? pos : a.CAP - 1;
+  for (int j = 0; j <= last; j++) {
+    const float *kr = kc + (int64_t)j * a.D;
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (lane + 32 * i < a.D) part = fmaf(qr[i], kr[lane + 32 * i], part);
+    const float sc = warp_sum_f(part) * a.scale;
+    const float mn = fmaxf(m, sc);
+    const float corr = __expf(m - mn), p = __expf(sc - mn);
+    l = l * corr + p;
+    const float *vr = vc + (int64_t)j * a.D;
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (lane + 32 * i < a.D) acc[i] = fmaf(p, vr[lane + 32 * i], acc[i] * corr);
+    m = mn;
+  }
+  float *dst = a.out + (int64_t)(b * a.S + s) * (int64_t)a.H * a.D + h * a.D;
+  const float inv = 1.f / l;
+#pragma unroll
+  for (int i = 0; i < 8; i++)
+    if (lane + 32 * i < a.D) dst[lane + 32 * i] = acc[i] * inv;
+}
+
+__global__ void advance_kernel(int32_t *past, int n, int delta) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) past[i] += delta;
+}
+
+unsigned grid_for(int64_t n, int block) {
+  int64_t g = (n + block - 1) / block;
+  return (unsigned)std::max<int64_t>(1, std::min<int64_t>(g, 148 * 16));
+}
+
+}  // namespace
+
+void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
+                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s) {
+  if (rows <= 0) return;
+  rmsnorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
+                      float *sum_out, int64_t rows, int D, double eps, cudaStream_t s) {
+  if (rows <= 0) return;
+  layernorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
+                     int64_t D, cudaStream_t s) {
+  if (rows * D <= 0) return;
+  silu_mul_kernel<<<grid_for(rows * D, 256), 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s) {
+  if (n <= 0) return;
+  gelu_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_add(const float *a, const float *b, float *y, int64_t rows, int64_t D, int b_bcast, cudaStream_t s) {
+  if (rows * D <= 0) return;
+  add_kernel<<<grid_for(rows * D, 256), 256, 0, s>>>(a, b, y, rows, D, b_bcast);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_gather_rows(const float *table, const int64_t *ids, float *y, int64_t rows, int64_t V, int64_t D,
+                        int32_t *err, cudaStream_t s) {
+  if (rows <= 0) return;
+  gather_rows_kernel<<<(unsigned)rows, 256, 0, s>>>(table, ids, y, rows, V, D, err);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, cudaStream_t s) {
+  if (rows <= 0) return;
+  argmax_kernel<<<(unsigned)rows, 512, 0, s>>>(x, out, V);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
+                float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
+                int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
+                cudaStream_t s) {
+  GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
+            B, S, H, KVH, D, CAP, scale, err};
+  const int64_t items = (int64_t)B * S * KVH;
+  gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
+  B2M_CUDA(cudaGetLastError());
+  dim3 grid((unsigned)((S + 7) / 8), (unsigned)H, (unsigned)B);
+  gqa_attend_kernel<<<grid, 256, 0, s>>>(a);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s) {
+  if (n <= 0) return;
+  advance_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(past, n, delta);
+  B2M_CUDA(cudaGetLastError());
+}

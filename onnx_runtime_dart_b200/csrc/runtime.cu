@@ -1203,3 +1203,128 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Transformer glue (device pointers)
+// ---------------------------------------------------------------------------
+
+B2M_API b2m_status b2m_rmsnorm_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma, float *y,
+                                   float *sum_out, int64_t rows, int64_t d, double eps) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d > 0 && d <= (1 << 24) && (rows == 0 || (x && gamma && y)), B2M_ERR_INVALID_ARGUMENT,
+                "RMSNorm: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_rmsnorm(x, skip, gamma, y, sum_out, rows, (int)d, eps, std::max<int64_t>(rows, 1), 0, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_rmsnorm_heads_dev(b2m_ctx *ctx, const float *x, const float *gamma, float *y, int64_t tokens,
+                                         int64_t heads, int64_t head_dim, int64_t token_stride, double eps) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(tokens >= 0 && heads > 0 && head_dim > 0 && head_dim <= (1 << 24) &&
+                    token_stride >= heads * head_dim && (tokens == 0 || (x && gamma && y)),
+                B2M_ERR_INVALID_ARGUMENT, "RMSNorm heads: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_rmsnorm(x, nullptr, gamma, y, nullptr, tokens * heads, (int)head_dim, eps, heads, token_stride,
+                   ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_layernorm_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma,
+                                     const float *beta, float *y, float *sum_out, int64_t rows, int64_t d,
+                                     double eps) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d > 0 && d <= (1 << 24) && (rows == 0 || (x && gamma && y)), B2M_ERR_INVALID_ARGUMENT,
+                "LayerNormalization: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_layernorm(x, skip, gamma, beta, y, sum_out, rows, (int)d, eps, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_silu_mul_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gate_rs,
+                                    int64_t up_rs, float *y, int64_t rows, int64_t d) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d >= 0 && gate_rs >= d && up_rs >= d && (rows * d == 0 || (gate && up && y)),
+                B2M_ERR_INVALID_ARGUMENT, "SiLU*Mul: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_silu_mul(gate, up, gate_rs, up_rs, y, rows, d, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_gelu_dev(b2m_ctx *ctx, const float *x, float *y, int64_t n) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(n >= 0 && (n == 0 || (x && y)), B2M_ERR_INVALID_ARGUMENT, "Gelu: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_gelu(x, y, n, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_add_dev(b2m_ctx *ctx, const float *a, const float *b, float *y, int64_t rows, int64_t d,
+                               int32_t b_broadcast) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d >= 0 && (rows * d == 0 || (a && b && y)), B2M_ERR_INVALID_ARGUMENT,
+                "Add: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_add(a, b, y, rows, d, b_broadcast ? 1 : 0, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_gather_rows_dev(b2m_ctx *ctx, const float *table, const int64_t *ids, float *y,
+                                       int64_t rows, int64_t v, int64_t d) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && v > 0 && d > 0 && (rows == 0 || (table && ids && y)), B2M_ERR_INVALID_ARGUMENT,
+                "Gather: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_gather_rows(table, ids, y, rows, v, d, ctx->dev_err, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_argmax_dev(b2m_ctx *ctx, const float *x, int64_t *out, int64_t rows, int64_t v) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && v > 0 && (rows == 0 || (x && out)), B2M_ERR_INVALID_ARGUMENT, "ArgMax: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_argmax(x, out, rows, v, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                               int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
+                               const float *cos_cache, const float *sin_cache, int32_t rotary_half,
+                               int32_t rotary_dim, int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h,
+                               int32_t kvh, int32_t head_dim, int32_t cap, float scale) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(b >= 0 && s >= 0 && h > 0 && kvh > 0 && h % kvh == 0 && head_dim > 0 && head_dim <= 256 && cap > 0,
+                B2M_ERR_INVALID_ARGUMENT, "GroupQueryAttention: bad shape arguments");
+    B2M_REQUIRE(q_rs >= (int64_t)h * head_dim && kv_rs >= (int64_t)kvh * head_dim, B2M_ERR_INVALID_ARGUMENT,
+                "GroupQueryAttention: row strides too small");
+    B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && k_cache && v_cache && past && out), B2M_ERR_INVALID_ARGUMENT,
+                "GroupQueryAttention: null pointer");
+    const bool rot = cos_cache != nullptr;
+    B2M_REQUIRE(!rot || (sin_cache && rotary_half > 0 && rotary_dim > 0 && rotary_dim <= head_dim &&
+                         rotary_dim % 2 == 0 && rotary_dim / 2 <= rotary_half),
+                B2M_ERR_INVALID_ARGUMENT, "GroupQueryAttention: bad rotary arguments");
+    DeviceGuard dg(ctx->device);
+    if ((int64_t)b * s == 0) return;
+    const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
+    launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
+               interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(n >= 0 && (n == 0 || past), B2M_ERR_INVALID_ARGUMENT, "advance positions: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_advance_positions(past, n, delta, ctx->stream);
+  });
+}

@@ -1,0 +1,217 @@
+"""GPU tests of the device-resident glue ops (RMSNorm, LayerNorm, SiLU*Mul,
+GELU, Add, Gather, ArgMax, GroupQueryAttention with rotary and a KV cache)
+against the numpy restatement in oracle/glue.py, through the C ABI."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from oracle import glue
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import onnx_runtime_dart_b200 as b2m  # noqa: E402
+from onnx_runtime_dart_b200 import _native as N  # noqa: E402
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = b2m.Context(0)
+    yield c
+    c.synchronize()
+
+
+def _d(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def _close(got, want, rtol=1e-5, what=""):
+    got = np.asarray(got, np.float64)
+    want = np.asarray(want, np.float64)
+    scale = max(float(np.max(np.abs(want))), 1e-30)
+    err = float(np.max(np.abs(got - want))) / scale
+    assert err <= rtol, f"{what}: max rel err {err:.3e} > {rtol}"
+
+
+@pytest.mark.parametrize("rows,d,skip", [(7, 1024, False), (33, 128, True), (5, 100, True)])
+def test_rmsnorm_matches_reference(ctx, rows, d, skip):
+    rng = np.random.default_rng(rows + d)
+    x = rng.standard_normal((rows, d)).astype(np.float32)
+    s = rng.standard_normal((rows, d)).astype(np.float32) if skip else None
+    g = (1 + 0.1 * rng.standard_normal(d)).astype(np.float32)
+    want, wsum = glue.rmsnorm(x, g, 1e-6, skip=s)
+    dx, dg, dy = _d(x), _d(g), torch.empty_like(_d(x))
+    ds = _d(s) if skip else None
+    dsum = torch.empty_like(dx) if skip else None
+    N.check(ctx.lib.b2m_rmsnorm_dev(ctx.handle, _p(dx), _p(ds), _p(dg), _p(dy), _p(dsum), rows, d, 1e-6))
+    torch.cuda.synchronize()
+    _close(dy.cpu().numpy(), want, 2e-7, "rmsnorm")
+    if skip:
+        np.testing.assert_array_equal(dsum.cpu().numpy(), wsum)
+
+
+def test_rmsnorm_heads_in_place(ctx):
+    rng = np.random.default_rng(3)
+    tokens, heads, hd, stride = 6, 4, 32, 4 * 32 + 64
+    x = rng.standard_normal((tokens, stride)).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(hd)).astype(np.float32)
+    want = x.copy()
+    want[:, : heads * hd] = glue.rmsnorm(x[:, : heads * hd].reshape(tokens * heads, hd), g, 1e-6)[0].reshape(
+        tokens, heads * hd)
+    dx, dg = _d(x), _d(g)
+    N.check(ctx.lib.b2m_rmsnorm_heads_dev(ctx.handle, _p(dx), _p(dg), _p(dx), tokens, heads, hd, stride, 1e-6))
+    torch.cuda.synchronize()
+    _close(dx.cpu().numpy(), want, 2e-7, "rmsnorm heads")
+
+
+def test_layernorm_matches_reference(ctx):
+    rng = np.random.default_rng(4)
+    x = rng.standard_normal((9, 768)).astype(np.float32)
+    s = rng.standard_normal((9, 768)).astype(np.float32)
+    g = rng.standard_normal(768).astype(np.float32)
+    b = rng.standard_normal(768).astype(np.float32)
+    want, _ = glue.layernorm(x, g, b, 1e-12, skip=s)
+    dx, ds, dg, db = _d(x), _d(s), _d(g), _d(b)
+    dy = torch.empty_like(dx)
+    N.check(ctx.lib.b2m_layernorm_dev(ctx.handle, _p(dx), _p(ds), _p(dg), _p(db), _p(dy), None, 9, 768, 1e-12))
+    torch.cuda.synchronize()
+    _close(dy.cpu().numpy(), want, 2e-7, "layernorm")
+
+
+def test_elementwise_gather_argmax(ctx):
+    rng = np.random.default_rng(5)
+    gu = rng.standard_normal((10, 2 * 48)).astype(np.float32)
+    dgu = _d(gu)
+    dy = torch.empty((10, 48), device="cuda")
+    N.check(ctx.lib.b2m_silu_mul_dev(ctx.handle, _p(dgu), ctypes.c_void_p(dgu.data_ptr() + 48 * 4), 96, 96, _p(dy),
+                                     10, 48))
+    x = rng.standard_normal(1000).astype(np.float32)
+    dx = _d(x)
+    dgl = torch.empty_like(dx)
+    N.check(ctx.lib.b2m_gelu_dev(ctx.handle, _p(dx), _p(dgl), 1000))
+    a = rng.standard_normal((4, 8)).astype(np.float32)
+    b = rng.standard_normal(8).astype(np.float32)
+    da, db = _d(a), _d(b)
+    dsum = torch.empty_like(da)
+    N.check(ctx.lib.b2m_add_dev(ctx.handle, _p(da), _p(db), _p(dsum), 4, 8, 1))
+    table = rng.standard_normal((50, 16)).astype(np.float32)
+    ids = np.array([3, 0, 49, 7, 7], np.int64)
+    dt, di = _d(table), _d(ids)
+    drows = torch.empty((5, 16), device="cuda")
+    N.check(ctx.lib.b2m_gather_rows_dev(ctx.handle, _p(dt), _p(di), _p(drows), 5, 50, 16))
+    logits = rng.standard_normal((3, 151936)).astype(np.float32)
+    logits[1, 77] = logits[1, 99] = 50.0  # tie: the first index wins
+    dl = _d(logits)
+    dam = torch.empty(3, device="cuda", dtype=torch.int64)
+    N.check(ctx.lib.b2m_argmax_dev(ctx.handle, _p(dl), _p(dam), 3, 151936))
+    torch.cuda.synchronize()
+    _close(dy.cpu().numpy(), glue.silu_mul(gu[:, :48], gu[:, 48:]), 1e-6, "silu_mul")
+    _close(dgl.cpu().numpy(), glue.gelu(x), 1e-6, "gelu")
+    np.testing.assert_array_equal(dsum.cpu().numpy(), a + b)
+    np.testing.assert_array_equal(drows.cpu().numpy(), table[ids])
+    got = dam.cpu().numpy()
+    np.testing.assert_array_equal(got, glue.argmax(logits))
+    assert got[1] == 77
+
+
+@pytest.mark.parametrize("b,s,past,h,kvh,d,interleaved", [(2, 5, 0, 4, 2, 32, 0), (3, 1, 9, 16, 8, 128, 0),
+                                                           (1, 7, 3, 6, 3, 64, 1), (2, 40, 0, 8, 8, 96, 0)])
+def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
+    # Prefill-shaped and decode-shaped calls; `past` positions already cached.
+    rng = np.random.default_rng(b * 100 + s + past + d)
+    cap = past + s + 3
+    cos, sin = glue.rope_cache(cap, d // 2, 1e4)
+    q = rng.standard_normal((b, s, h * d)).astype(np.float32)
+    k = rng.standard_normal((b, s, kvh * d)).astype(np.float32)
+    v = rng.standard_normal((b, s, kvh * d)).astype(np.float32)
+    pk = rng.standard_normal((b, kvh, past, d)).astype(np.float32) if past else None
+    pv = rng.standard_normal((b, kvh, past, d)).astype(np.float32) if past else None
+    want, wk, wv = glue.gqa(q, k, v, h, kvh, pk, pv, cos, sin, interleaved=bool(interleaved))
+    kc = np.zeros((b, kvh, cap, d), np.float32)
+    vc = np.zeros((b, kvh, cap, d), np.float32)
+    if past:
+        kc[:, :, :past] = pk
+        vc[:, :, :past] = pv
+    dq, dk, dv, dkc, dvc = _d(q), _d(k), _d(v), _d(kc), _d(vc)
+    dpast = _d(np.full(b, past, np.int32))
+    dcos, dsin = _d(cos), _d(sin)
+    dout = torch.empty_like(dq)
+    N.check(ctx.lib.b2m_gqa_dev(ctx.handle, _p(dq), _p(dk), _p(dv), h * d, kvh * d, _p(dkc), _p(dvc), _p(dpast),
+                                _p(dcos), _p(dsin), d // 2, d, interleaved, _p(dout), b, s, h, kvh, d, cap, 0.0))
+    torch.cuda.synchronize()
+    _close(dout.cpu().numpy(), want, 2e-5, "gqa out")
+    _close(dkc.cpu().numpy()[:, :, : past + s], wk, 1e-6, "present key")
+    np.testing.assert_array_equal(dvc.cpu().numpy()[:, :, : past + s], wv)
+
+
+def _ref_decoder(dec, ids, past):
+    """numpy composition of the same chain: oracle MatMulNBits / MatMul and
+    the oracle/glue ops. `past` is a list of (k, v) per layer or None;
+    returns (last-token logits [B][V], new past)."""
+    c = dec.cfg
+    hst = dec.host
+    b, s = ids.shape
+    t = b * s
+    res = hst["emb"][ids.reshape(-1)]
+    p0 = 0 if past is None else past[0][0].shape[2]
+    cos, sin = glue.rope_cache(dec.cap, c.head_dim // 2, c.theta)
+    newp = []
+    down = None
+    for li in range(c.layers):
+        w = {n: hst[(li, n)] for n in ("qkv", "o", "gate_up", "down")}
+        if li == 0:
+            h, res = glue.rmsnorm(res, hst[(li, "attn_norm")], c.eps)
+        else:
+            h, res = glue.rmsnorm(down, hst[(li, "attn_norm")], c.eps, skip=res)
+        qkv = oracle.matmul_nbits(h, *w["qkv"], c.hidden, c.qkv_n, c.block, nthreads=8).reshape(t, c.qkv_n)
+        hd = c.head_dim
+        q = glue.rmsnorm(qkv[:, : c.heads * hd].reshape(-1, hd), hst[(li, "q_norm")], c.eps)[0].reshape(t, -1)
+        k = glue.rmsnorm(qkv[:, c.heads * hd:(c.heads + c.kv_heads) * hd].reshape(-1, hd), hst[(li, "k_norm")],
+                         c.eps)[0].reshape(t, -1)
+        v = qkv[:, (c.heads + c.kv_heads) * hd:]
+        pk, pv = (None, None) if past is None else past[li]
+        attn, nk, nv = glue.gqa(q.reshape(b, s, -1), k.reshape(b, s, -1), v.reshape(b, s, -1), c.heads,
+                                c.kv_heads, pk, pv, cos, sin)
+        newp.append((nk, nv))
+        o = oracle.matmul_nbits(attn.reshape(t, -1), *w["o"], c.heads * hd, c.hidden, c.block).reshape(t, -1)
+        h, res = glue.rmsnorm(o, hst[(li, "mlp_norm")], c.eps, skip=res)
+        gu = oracle.matmul_nbits(h, *w["gate_up"], c.hidden, 2 * c.inter, c.block).reshape(t, -1)
+        act = glue.silu_mul(gu[:, : c.inter], gu[:, c.inter:])
+        down = oracle.matmul_nbits(act, *w["down"], c.inter, c.hidden, c.block).reshape(t, -1)
+    hf, res = glue.rmsnorm(down, hst["final_norm"], c.eps, skip=res)
+    last = hf.reshape(b, s, -1)[:, -1]
+    return oracle.matmul(last, hst["lm_head"]), newp
+
+
+def test_tiny_decoder_chain_prefill_and_graph_decode(ctx):
+    from onnx_runtime_dart_b200.decoder import DecoderConfig, Int4Decoder
+    from tests.conftest import assert_fast_close
+
+    cfg = DecoderConfig.tiny()
+    b, s, steps = 2, 6, 3
+    dec = Int4Decoder(ctx, cfg, batch=b, cap=s + steps + 1, max_prefill=s, seed=21, keep_host=True)
+    rng = np.random.default_rng(22)
+    prompt = rng.integers(0, cfg.vocab, (b, s)).astype(np.int64)
+    dec.prefill(prompt)
+    torch.cuda.synchronize()
+    want, past = _ref_decoder(dec, prompt, None)
+    # Chain tolerance: FAST MatMulNBits rounds weights and activations to f16
+    # at every projection of the two layers.
+    assert_fast_close(dec.logits.cpu().numpy(), want, "prefill logits", max_rel=2e-2, min_cos=0.9995)
+    toks = dec.next_ids.cpu().numpy()
+    gen = dec.decode(steps).cpu().numpy()
+    cur = toks
+    for i in range(steps):
+        want, past = _ref_decoder(dec, cur.reshape(b, 1), past)
+        # the GPU's logits after the last replay correspond to step steps-1
+        if i == steps - 1:
+            assert_fast_close(dec.logits.cpu().numpy(), want, "decode logits", max_rel=2e-2, min_cos=0.9995)
+        cur = gen[i]
+    assert gen.shape == (steps, b)
+    assert np.all((gen >= 0) & (gen < cfg.vocab))
