@@ -263,6 +263,41 @@ def other_configs(ctx, lib, N, stream, dev, steps, warmup):
     return out
 
 
+def run_decoder(ctx, torch, stream, batch, prefill_len=512, steps=128, layers=None, seed=0):
+    """Qwen3-0.6B-shaped int4 decoder (random weights),
+    `batch` sequences, a `prefill_len`-token prompt, then `steps` greedy decode
+    steps replayed as one CUDA graph per step. Device time (CUDA events)."""
+    from onnx_runtime_dart_b200.decoder import DecoderConfig, Int4Decoder
+
+    cfg = DecoderConfig.qwen3_0_6b()
+    if layers:
+        cfg.layers = layers
+    dec = Int4Decoder(ctx, cfg, batch=batch, cap=prefill_len + steps + 8, max_prefill=prefill_len, seed=seed)
+    rng = np.random.default_rng(seed + 1)
+    prompt = rng.integers(0, cfg.vocab, (batch, prefill_len)).astype(np.int64)
+    with torch.cuda.stream(stream):
+        dec.prefill(prompt)  # warm-up (kernel attributes, scratch growth)
+        dec.decode(2)        # captures the decode graph
+        stream.synchronize()
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record(stream)
+        dec.prefill(prompt)
+        e1.record(stream)
+        gen = dec.decode(steps)
+        e2.record(stream)
+        stream.synchronize()
+    ms_p, ms_d = e0.elapsed_time(e1), e1.elapsed_time(e2)
+    ok = bool(((gen >= 0) & (gen < cfg.vocab)).all().item())
+    out = {"batch_per_gpu": batch, "prefill_len": prefill_len, "decode_steps": steps, "layers": cfg.layers,
+           "prefill_ms": round(ms_p, 3), "decode_ms": round(ms_d, 3),
+           "prefill_tokens_per_s": round(batch * prefill_len / (ms_p / 1e3), 1),
+           "decode_tokens_per_s": round(batch * steps / (ms_d / 1e3), 1),
+           "decode_ms_per_step": round(ms_d / steps, 4), "tokens_valid": ok}
+    del dec
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -277,9 +312,12 @@ def main():
     ap.add_argument("--passes", type=int, default=64,
                     help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill", "ops"],
+    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill", "ops", "decoder"],
                     help="run one phase only (for profiler captures); prints its device time. "
                          "`ops` times BASELINE configs 1 and 2 (fp32 MatMul, MatMulInteger)")
+    ap.add_argument("--dec-layers", type=int, default=None, help="decoder case: layers (default 28)")
+    ap.add_argument("--dec-steps", type=int, default=128, help="decoder case: greedy decode steps")
+    ap.add_argument("--dec-batch", type=int, default=None, help="decoder case: sequences per GPU (default 64/N)")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -317,6 +355,20 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.case == "decoder":
+        r = run_decoder(ctx, torch, stream, args.dec_batch or max(1, 64 // world), steps=args.dec_steps,
+                        layers=args.dec_layers)
+        t_p = max_over_ranks(r["prefill_ms"])
+        t_d = max_over_ranks(r["decode_ms"])
+        if rank == 0:
+            r["prefill_tokens_per_s_all_gpus"] = round(world * r["batch_per_gpu"] * r["prefill_len"] / (t_p / 1e3), 1)
+            r["decode_tokens_per_s_all_gpus"] = round(world * r["batch_per_gpu"] * r["decode_steps"] / (t_d / 1e3), 1)
+            print(json.dumps({"case": "decoder", **r}), flush=True)
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     rng = np.random.default_rng(1234 + rank)
     R = args.layers

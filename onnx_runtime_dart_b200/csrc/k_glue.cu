@@ -17,6 +17,7 @@
 #include <cfloat>
 
 #include "b2m_internal.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
@@ -270,6 +271,245 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
     if (lane + 32 * i < a.D) dst[lane + 32 * i] = acc[i] * inv;
 }
 
+// Flash-style attention for multi-token calls (prefill), fp32 on the CUDA
+// cores. CTA = (64-query tile, query head, batch), 256 threads. Each thread
+// owns 4 query rows x 4 keys of the 64 x 64 score tile and the same 4 rows x
+// D/16 columns of the output; the row statistics of the online softmax
+// (max, sum) are reduced over the 16 threads that share the rows. Q is
+// rotated and pre-scaled on load; K (rotated by gqa_append_kernel) and V come
+// from the cache. Key tiles past the last visible key are skipped.
+template <int D>
+__global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
+  constexpr int QT = 64, KT = 64, LD = 68, CPT = D / 16;
+  extern __shared__ __align__(16) float fsm[];
+  float *Qt = fsm;            // [D][LD], Qt[d][r]
+  float *Kt = Qt + D * LD;    // [D][LD], Kt[d][c]
+  float *Vs = Kt + D * LD;    // [KT][D]
+  float *Ps = Vs + KT * D;    // [QT][LD]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int h = blockIdx.y, b = blockIdx.z, q0 = blockIdx.x * QT;
+  const int kvh = h / (a.H / a.KVH);
+  const int past = a.past[b];
+  for (int i = tid; i < QT * D; i += 256) {
+    const int r = i / D, d = i % D;
+    const int s = q0 + r;
+    Qt[d * LD + r] = s < a.S ? a.q[(int64_t)(b * a.S + s) * a.q_rs + h * D + d] * a.scale : 0.f;
+  }
+  __syncthreads();
+  if (a.cos) {
+    const int npair = a.rot / 2;
+    for (int i = tid; i < QT * npair; i += 256) {
+      const int r = i / npair, pi = i % npair;
+      const int64_t pos = past + q0 + r;
+      if (q0 + r >= a.S || pos >= a.CAP) continue;
+      const float c = a.cos[pos * a.half + pi], sn = a.sin[pos * a.half + pi];
+      const int i0 = a.interleaved ? 2 * pi : pi, i1 = a.interleaved ? 2 * pi + 1 : pi + npair;
+      const float x0 = Qt[i0 * LD + r], x1 = Qt[i1 * LD + r];
+      Qt[i0 * LD + r] = x0 * c - x1 * sn;
+      Qt[i1 * LD + r] = x1 * c + x0 * sn;
+    }
+  }
+  const int last_q = min(q0 + QT, a.S) - 1;
+  const int max_key = min(past + last_q, a.CAP - 1);
+  const float *kc = a.kcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
+  const float *vc = a.vcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
+  float m[4], l[4], o[4][CPT];
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    m[i] = -INFINITY;
+    l[i] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPT; c++) o[i][c] = 0.f;
+  }
+  for (int j0 = 0; j0 <= max_key; j0 += KT) {
+    __syncthreads();
+    for (int i = tid; i < KT * D; i += 256) {
+      const int c = i / D, d = i % D;
+      const int j = j0 + c;
+      const bool ok = j <= max_key;
+      Kt[d * LD + c] = ok ? kc[(int64_t)j * D + d] : 0.f;
+      Vs[c * D + d] = ok ? vc[(int64_t)j * D + d] : 0.f;
+    }
+    __syncthreads();
+    float sc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+      for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll 4
+    for (int d = 0; d < D; d++) {
+      const float4 qv = *reinterpret_cast<const float4 *>(&Qt[d * LD + ty * 4]);
+      const float4 kv = *reinterpret_cast<const float4 *>(&Kt[d * LD + tx * 4]);
+      const float qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int j = 0; j < 4; j++) sc[i][j] = fmaf(qa[i], ka[j], sc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int qpos = past + q0 + ty * 4 + i;
+      float rmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (j0 + tx * 4 + j > qpos) sc[i][j] = -INFINITY;
+        rmax = fmaxf(rmax, sc[i][j]);
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, off));
+      const float mn = fmaxf(m[i], rmax);
+      const float corr = mn == -INFINITY ? 1.f : __expf(m[i] - mn);
+      float rsum = 0.f;
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float pv = mn == -INFINITY ? 0.f : __expf(sc[i][j] - mn);
+        Ps[(ty * 4 + i) * LD + tx * 4 + j] = pv;
+        rsum += pv;
+      }
+#pragma unroll
+      for (int off = 1; off < 16; off <<= 1) rsum += __shfl_xor_sync(0xffffffffu, rsum, off);
+      l[i] = l[i] * corr + rsum;
+      m[i] = mn;
+#pragma unroll
+      for (int c = 0; c < CPT; c++) o[i][c] *= corr;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int j = 0; j < KT; j++) {
+      float pj[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) pj[i] = Ps[(ty * 4 + i) * LD + j];
+      const float *vr = Vs + j * D + tx * CPT;
+#pragma unroll
+      for (int c = 0; c < CPT; c++) {
+        const float vv = vr[c];
+#pragma unroll
+        for (int i = 0; i < 4; i++) o[i][c] = fmaf(pj[i], vv, o[i][c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const int s = q0 + ty * 4 + i;
+    if (s >= a.S) continue;
+    float *dst = a.out + (int64_t)(b * a.S + s) * (int64_t)a.H * D + h * D + tx * CPT;
+    const float inv = 1.f / l[i];
+#pragma unroll
+    for (int c = 0; c < CPT; c++) dst[c] = o[i][c] * inv;
+  }
+}
+
+// Single-token attention (decode): CTA = (kv head, batch), 256 threads, the
+// G query heads of the group together so each cached K/V row is read once.
+// Warp w takes keys w*32 + 256*i + lane: a lane computes the G scores of its
+// key, the warp updates its online-softmax state, then the lanes switch to
+// head-dim columns for P.V (the key's weight broadcast by shuffle). The 8
+// warp states are merged in shared memory in fixed order.
+template <int D, int G>
+__global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a) {
+  constexpr int CPL = D / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int past = a.past[b];
+  const int nkeys = min(past + 1, a.CAP);
+  __shared__ __align__(16) float qs[G][D];
+  __shared__ float wm[8][G], wl[8][G];
+  __shared__ float wo[8][G][D];
+  for (int i = threadIdx.x; i < G * D; i += 256) {
+    const int g = i / D, d = i % D;
+    qs[g][d] = a.q[(int64_t)b * a.q_rs + (kvh * G + g) * D + d] * a.scale;
+  }
+  __syncthreads();
+  if (a.cos && past < a.CAP) {
+    const int npair = a.rot / 2;
+    for (int i = threadIdx.x; i < G * npair; i += 256) {
+      const int g = i / npair, pi = i % npair;
+      const float c = a.cos[(int64_t)past * a.half + pi], sn = a.sin[(int64_t)past * a.half + pi];
+      const int i0 = a.interleaved ? 2 * pi : pi, i1 = a.interleaved ? 2 * pi + 1 : pi + npair;
+      const float x0 = qs[g][i0], x1 = qs[g][i1];
+      qs[g][i0] = x0 * c - x1 * sn;
+      qs[g][i1] = x1 * c + x0 * sn;
+    }
+  }
+  __syncthreads();
+  const float *kc = a.kcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
+  const float *vc = a.vcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
+  float m[G], l[G], o[G][CPL];
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    m[g] = -INFINITY;
+    l[g] = 0.f;
+#pragma unroll
+    for (int c = 0; c < CPL; c++) o[g][c] = 0.f;
+  }
+  for (int c0 = warp * 32; c0 < nkeys; c0 += 256) {
+    const int j = c0 + lane;
+    const bool valid = j < nkeys;
+    float sc[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) sc[g] = 0.f;
+    if (valid) {
+      const float4 *kr = reinterpret_cast<const float4 *>(kc + (int64_t)j * D);
+#pragma unroll 8
+      for (int d4 = 0; d4 < D / 4; d4++) {
+        const float4 kv = kr[d4];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][d4 * 4]);
+          sc[g] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, sc[g]))));
+        }
+      }
+    }
+    float p[G];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      const float v = valid ? sc[g] : -INFINITY;
+      const float mn = fmaxf(m[g], warp_max_f(v));
+      const float corr = __expf(m[g] - mn);
+      p[g] = valid ? __expf(v - mn) : 0.f;
+      l[g] = l[g] * corr + warp_sum_f(p[g]);
+      m[g] = mn;
+#pragma unroll
+      for (int c = 0; c < CPL; c++) o[g][c] *= corr;
+    }
+    const int nj = min(32, nkeys - c0);
+    for (int jj = 0; jj < nj; jj++) {
+      const float *vr = vc + (int64_t)(c0 + jj) * D + lane * CPL;
+      float vv[CPL];
+#pragma unroll
+      for (int c = 0; c < CPL; c++) vv[c] = vr[c];
+#pragma unroll
+      for (int g = 0; g < G; g++) {
+        const float pj = __shfl_sync(0xffffffffu, p[g], jj);
+#pragma unroll
+        for (int c = 0; c < CPL; c++) o[g][c] = fmaf(pj, vv[c], o[g][c]);
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < G; g++) {
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wl[warp][g] = l[g];
+    }
+#pragma unroll
+    for (int c = 0; c < CPL; c++) wo[warp][g][lane * CPL + c] = o[g][c];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < G * D; i += 256) {
+    const int g = i / D, d = i % D;
+    float M = -INFINITY;
+    for (int w = 0; w < 8; w++) M = fmaxf(M, wm[w][g]);
+    float L = 0.f, O = 0.f;
+    for (int w = 0; w < 8; w++) {
+      const float f = wm[w][g] == -INFINITY ? 0.f : __expf(wm[w][g] - M);
+      L += wl[w][g] * f;
+      O += wo[w][g][d] * f;
+    }
+    a.out[(int64_t)b * (int64_t)a.H * D + (kvh * G + g) * D + d] = O / L;
+  }
+}
+
 __global__ void advance_kernel(int32_t *past, int n, int delta) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) past[i] += delta;
@@ -337,8 +577,42 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
   const int64_t items = (int64_t)B * S * KVH;
   gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
   B2M_CUDA(cudaGetLastError());
-  dim3 grid((unsigned)((S + 7) / 8), (unsigned)H, (unsigned)B);
-  gqa_attend_kernel<<<grid, 256, 0, s>>>(a);
+  const int G = H / KVH;
+  const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
+  if (S == 1 && dok && (G == 1 || G == 2 || G == 4 || G == 8)) {
+    dim3 grid((unsigned)KVH, (unsigned)B);
+#define B2M_DEC(DD, GG) \
+  if (D == DD && G == GG) gqa_decode_kernel<DD, GG><<<grid, 256, 0, s>>>(a);
+    B2M_DEC(32, 1) B2M_DEC(32, 2) B2M_DEC(32, 4) B2M_DEC(32, 8)
+    B2M_DEC(64, 1) B2M_DEC(64, 2) B2M_DEC(64, 4) B2M_DEC(64, 8)
+    B2M_DEC(96, 1) B2M_DEC(96, 2) B2M_DEC(96, 4) B2M_DEC(96, 8)
+    B2M_DEC(128, 1) B2M_DEC(128, 2) B2M_DEC(128, 4) B2M_DEC(128, 8)
+#undef B2M_DEC
+  } else if (dok) {
+    dim3 grid((unsigned)((S + 63) / 64), (unsigned)H, (unsigned)B);
+    const int smem = (2 * D * 68 + 64 * D + 64 * 68) * 4;
+    switch (D) {
+      case 32:
+        b2m::set_smem_limit_once<gqa_prefill_kernel<32>>(smem);
+        gqa_prefill_kernel<32><<<grid, 256, smem, s>>>(a);
+        break;
+      case 64:
+        b2m::set_smem_limit_once<gqa_prefill_kernel<64>>(smem);
+        gqa_prefill_kernel<64><<<grid, 256, smem, s>>>(a);
+        break;
+      case 96:
+        b2m::set_smem_limit_once<gqa_prefill_kernel<96>>(smem);
+        gqa_prefill_kernel<96><<<grid, 256, smem, s>>>(a);
+        break;
+      default:
+        b2m::set_smem_limit_once<gqa_prefill_kernel<128>>(smem);
+        gqa_prefill_kernel<128><<<grid, 256, smem, s>>>(a);
+        break;
+    }
+  } else {
+    dim3 grid((unsigned)((S + 7) / 8), (unsigned)H, (unsigned)B);
+    gqa_attend_kernel<<<grid, 256, 0, s>>>(a);
+  }
   B2M_CUDA(cudaGetLastError());
 }
 

@@ -121,7 +121,9 @@ def test_elementwise_gather_argmax(ctx):
 
 
 @pytest.mark.parametrize("b,s,past,h,kvh,d,interleaved", [(2, 5, 0, 4, 2, 32, 0), (3, 1, 9, 16, 8, 128, 0),
-                                                           (1, 7, 3, 6, 3, 64, 1), (2, 40, 0, 8, 8, 96, 0)])
+                                                           (1, 7, 3, 6, 3, 64, 1), (2, 40, 0, 8, 8, 96, 0),
+                                                           (2, 130, 20, 4, 2, 128, 0), (1, 1, 300, 16, 2, 128, 0),
+                                                           (2, 1, 0, 4, 4, 64, 1)])
 def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
     # Prefill-shaped and decode-shaped calls; `past` positions already cached.
     rng = np.random.default_rng(b * 100 + s + past + d)
