@@ -458,6 +458,16 @@ def main():
     # per op over 64 weight sets in a CUDA graph.
     ops_lines = other_configs(ctx, lib, N, stream, dev, max(1, args.steps // 4), 3)
 
+    # the int4 decoder chain, sequences sharded over ranks.
+    dec = run_decoder(ctx, torch, stream, max(1, 64 // world))
+    dec_tp = max_over_ranks(dec["prefill_ms"])
+    dec_td = max_over_ranks(dec["decode_ms"])
+    dec_line = {"prefill_tokens_per_s": round(world * dec["batch_per_gpu"] * dec["prefill_len"] / (dec_tp / 1e3), 1),
+                "decode_tokens_per_s": round(world * dec["batch_per_gpu"] * dec["decode_steps"] / (dec_td / 1e3), 1),
+                "sequences": world * dec["batch_per_gpu"], "prefill_len": dec["prefill_len"],
+                "decode_steps": dec["decode_steps"], "decode_ms_per_step": dec["decode_ms_per_step"],
+                "tokens_valid": dec["tokens_valid"]}
+
     # End to end through the host-buffer C-ABI call (pinned host memory).
     e2e_layers = min(R, 64)
     a_h = torch.randn((1, K_DIM), dtype=torch.float32).pin_memory()
@@ -510,6 +520,7 @@ def main():
             "prefill_m512_frac_of_bf16_peak": round(tflops_p / tc_peak, 4),
             "prefill_m512_us_per_op": round(msp * 1e3 / (max(1, args.steps // 4) * Rp), 3),
             "configs_1_2_device_us_per_op": {o["case"]: round(o["graph_us_per_call"], 3) for o in ops_lines},
+            "config5_decoder": dec_line,
         },
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
