@@ -298,6 +298,55 @@ def run_decoder(ctx, torch, stream, batch, prefill_len=512, steps=128, layers=No
     return out
 
 
+def run_bert(ctx, torch, stream, batch, seq=128, steps=10, warmup=3, layers=None, seed=0, exact=False):
+    """BERT-base-shaped fp32 encoder (random weights) over
+    `batch` sequences of `seq` tokens, all-ones attention mask. Device time of
+    one graph-replayed forward (CUDA events, mean over `steps`), and the same
+    forward end to end: ids from pinned host memory in, the last hidden state
+    back to pinned host memory."""
+    from onnx_runtime_dart_b200 import _native as N
+    from onnx_runtime_dart_b200.bert import BertConfig, BertEncoder
+
+    cfg = BertConfig.base()
+    if layers:
+        cfg.layers = layers
+    enc = BertEncoder(ctx, cfg, batch, seq, seed=seed, mode=N.MODE_EXACT if exact else N.MODE_FAST)
+    rng = np.random.default_rng(seed + 1)
+    ids = rng.integers(0, cfg.vocab, (batch, seq)).astype(np.int64)
+    ids_pin = torch.from_numpy(ids.reshape(-1)).pin_memory()
+    out_pin = torch.empty((batch * seq, cfg.hidden), dtype=torch.float32).pin_memory()
+    with torch.cuda.stream(stream):
+        enc.set_attention_mask(np.ones((batch, seq)))
+        enc.ids.copy_(ids_pin, non_blocking=True)
+        for _ in range(max(1, warmup)):
+            enc.forward_device(True)
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            enc.forward_device(True)
+        e1.record(stream)
+        stream.synchronize()
+        ms_dev = e0.elapsed_time(e1) / steps
+        e0.record(stream)
+        for _ in range(steps):
+            enc.ids.copy_(ids_pin, non_blocking=True)
+            enc.forward_device(True)
+            out_pin.copy_(enc.x, non_blocking=True)
+        e1.record(stream)
+        stream.synchronize()
+        ms_e2e = e0.elapsed_time(e1) / steps
+    finite = bool(np.isfinite(out_pin.numpy()).all())
+    flops = cfg.flops_per_token(seq) * batch * seq
+    out = {"batch_per_gpu": batch, "seq": seq, "layers": cfg.layers, "mode": "exact" if exact else "fast-3xtf32",
+           "forward_ms": round(ms_dev, 4), "e2e_forward_ms": round(ms_e2e, 4),
+           "flop_per_forward": flops, "tflops": round(flops / (ms_dev / 1e3) / 1e12, 2),
+           "h2d_bytes": int(ids.nbytes), "d2h_bytes": int(out_pin.numel() * 4), "finite": finite}
+    del enc
+    torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
@@ -312,12 +361,14 @@ def main():
     ap.add_argument("--passes", type=int, default=64,
                     help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill", "ops", "decoder"],
+    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill", "ops", "decoder", "bert"],
                     help="run one phase only (for profiler captures); prints its device time. "
                          "`ops` times BASELINE configs 1 and 2 (fp32 MatMul, MatMulInteger)")
     ap.add_argument("--dec-layers", type=int, default=None, help="decoder case: layers (default 28)")
     ap.add_argument("--dec-steps", type=int, default=128, help="decoder case: greedy decode steps")
     ap.add_argument("--dec-batch", type=int, default=None, help="decoder case: sequences per GPU (default 64/N)")
+    ap.add_argument("--bert-layers", type=int, default=None, help="bert case: layers (default 12)")
+    ap.add_argument("--bert-exact", action="store_true", help="bert case: fp32-exact MatMuls instead of 3xTF32")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))
@@ -355,6 +406,21 @@ def main():
         t = torch.tensor([x], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
+
+    if args.case == "bert":
+        r = run_bert(ctx, torch, stream, max(1, 32 // world), layers=args.bert_layers, exact=args.bert_exact,
+                     steps=args.steps, warmup=args.warmup)
+        t_f = max_over_ranks(r["forward_ms"])
+        t_e = max_over_ranks(r["e2e_forward_ms"])
+        if rank == 0:
+            tok = world * r["batch_per_gpu"] * r["seq"]
+            r["tokens_per_s_all_gpus"] = round(tok / (t_f / 1e3), 1)
+            r["e2e_tokens_per_s_all_gpus"] = round(tok / (t_e / 1e3), 1)
+            print(json.dumps({"case": "bert", **r}), flush=True)
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     if args.case == "decoder":
         r = run_decoder(ctx, torch, stream, args.dec_batch or max(1, 64 // world), steps=args.dec_steps,

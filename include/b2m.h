@@ -315,6 +315,21 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
                                int32_t rotary_dim, int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h,
                                int32_t kvh, int32_t head_dim, int32_t cap, float scale);
 
+/* MultiHeadAttention over projected rows (opMultiHeadAttention,
+ * lib/src/onnx_ops.dart:2019; the scale + mask + softmax between the two
+ * batched MatMuls of opFusedSDPA, :2106-2148). q: [b][s] rows of h*head_dim
+ * (row stride q_rs); k / v: [b][t] rows of kvh*head_dim (row stride kv_rs),
+ * h a multiple of kvh (query head i reads kv head i / (h / kvh)).
+ * mask: NULL or an additive per-key mask, row r = mask + r*mask_bs of t
+ * floats for batch r (mask_bs 0 broadcasts one row), added to the scaled
+ * scores before the softmax (the [batch, 1, 1, t] attention bias BERT-style
+ * graphs build from attention_mask). causal != 0 additionally hides keys
+ * j > i. Scale <= 0 means 1/sqrt(head_dim). out: [b][s] rows of h*head_dim.
+ * head_dim <= 256. */
+B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                               int64_t kv_rs, const float *mask, int64_t mask_bs, float *out, int32_t b, int32_t s,
+                               int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale, int32_t causal);
+
 /* past[i] += delta for i < n (int32 device counters of a decode loop). */
 B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta);
 

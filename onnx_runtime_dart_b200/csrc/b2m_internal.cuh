@@ -228,6 +228,9 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
                 cudaStream_t s);
+void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
+                int64_t mask_bs, float *out, int B, int S, int T, int H, int KVH, int D, float scale, int causal,
+                int32_t *err, cudaStream_t s);
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s);
 
 // MatMulInteger / QLinearMatMul

@@ -186,6 +186,15 @@ struct GqaArgs {
   int B, S, H, KVH, D, CAP;
   float scale;
   int32_t *err;
+  // Key / value addressing for the attend kernels: element (b, kvh, key j, d)
+  // sits at kcache[b*kc_bs + kvh*kc_hs + j*kc_rs + d] (same for vcache). The
+  // cache layout gives (KVH*CAP*D, CAP*D, D); MultiHeadAttention reads the
+  // projected [B][T][KVH*D] rows directly.
+  int64_t kc_bs, kc_hs, kc_rs;
+  int causal;               // 1: query i sees keys [0, past + i]; 0: keys [0, kv_len)
+  int kv_len;
+  const float *mask;        // additive per-key mask [B][kv_len] (row stride mask_bs; 0 broadcasts), or null
+  int64_t mask_bs;
 };
 
 // Appends this call's keys / values to the cache (rotary on K), one warp per
@@ -229,7 +238,7 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
   const int s = blockIdx.x * 8 + warp;
   if (s >= a.S) return;
   const int kvh = h / (a.H / a.KVH);
-  const int past = a.past[b];
+  const int past = a.past ? a.past[b] : 0;
   const int pos = past + s;
   __shared__ float qbuf[8][256];
   float *qv = qbuf[warp];
@@ -241,24 +250,27 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
   float qr[8];
 #pragma unroll
   for (int i = 0; i < 8; i++) qr[i] = lane + 32 * i < a.D ? qv[lane + 32 * i] : 0.f;
-  const float *kc = a.kcache + ((int64_t)b * a.KVH + kvh) * a.CAP * a.D;
-  const float *vc = a.vcache + ((int64_t)b * a.KVH + kvh) * a.CAP * a.D;
+  const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs : nullptr;
   float m = -INFINITY, l = 0.f;
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; i++) acc[i] = 0.f;
-  const int last = pos < a.CAP ? pos : a.CAP - 1;
+  const int last = a.causal ? (pos < a.CAP ? pos : a.CAP - 1) : a.kv_len - 1;
   for (int j = 0; j <= last; j++) {
-    const float *kr = kc + (int64_t)j * a.D;
+    const float *kr = kc + (int64_t)j * a.kc_rs;
     float part = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; i++)
       if (lane + 32 * i < a.D) part = fmaf(qr[i], kr[lane + 32 * i], part);
-    const float sc = warp_sum_f(part) * a.scale;
+    float sc = warp_sum_f(part) * a.scale;
+    if (mk) sc += mk[j];
     const float mn = fmaxf(m, sc);
+    if (mn == -INFINITY) continue;  // every key so far masked out
     const float corr = __expf(m - mn), p = __expf(sc - mn);
     l = l * corr + p;
-    const float *vr = vc + (int64_t)j * a.D;
+    const float *vr = vc + (int64_t)j * a.kc_rs;
 #pragma unroll
     for (int i = 0; i < 8; i++)
       if (lane + 32 * i < a.D) acc[i] = fmaf(p, vr[lane + 32 * i], acc[i] * corr);
@@ -289,7 +301,7 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int h = blockIdx.y, b = blockIdx.z, q0 = blockIdx.x * QT;
   const int kvh = h / (a.H / a.KVH);
-  const int past = a.past[b];
+  const int past = a.past ? a.past[b] : 0;
   for (int i = tid; i < QT * D; i += 256) {
     const int r = i / D, d = i % D;
     const int s = q0 + r;
@@ -310,9 +322,11 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
     }
   }
   const int last_q = min(q0 + QT, a.S) - 1;
-  const int max_key = min(past + last_q, a.CAP - 1);
-  const float *kc = a.kcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
-  const float *vc = a.vcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
+  const int max_key = a.causal ? min(past + last_q, a.CAP - 1) : a.kv_len - 1;
+  const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs : nullptr;
+  __shared__ float mrow[64];
   float m[4], l[4], o[4][CPT];
 #pragma unroll
   for (int i = 0; i < 4; i++) {
@@ -327,8 +341,12 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
       const int c = i / D, d = i % D;
       const int j = j0 + c;
       const bool ok = j <= max_key;
-      Kt[d * LD + c] = ok ? kc[(int64_t)j * D + d] : 0.f;
-      Vs[c * D + d] = ok ? vc[(int64_t)j * D + d] : 0.f;
+      Kt[d * LD + c] = ok ? kc[(int64_t)j * a.kc_rs + d] : 0.f;
+      Vs[c * D + d] = ok ? vc[(int64_t)j * a.kc_rs + d] : 0.f;
+    }
+    if (tid < KT) {
+      const int j = j0 + tid;
+      mrow[tid] = j > max_key ? -INFINITY : (mk ? mk[j] : 0.f);
     }
     __syncthreads();
     float sc[4][4];
@@ -352,7 +370,8 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
       float rmax = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        if (j0 + tx * 4 + j > qpos) sc[i][j] = -INFINITY;
+        sc[i][j] += mrow[tx * 4 + j];
+        if (a.causal && j0 + tx * 4 + j > qpos) sc[i][j] = -INFINITY;
         rmax = fmaxf(rmax, sc[i][j]);
       }
 #pragma unroll
@@ -432,8 +451,8 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a) {
     }
   }
   __syncthreads();
-  const float *kc = a.kcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
-  const float *vc = a.vcache + ((int64_t)b * a.KVH + kvh) * a.CAP * D;
+  const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
   float m[G], l[G], o[G][CPL];
 #pragma unroll
   for (int g = 0; g < G; g++) {
@@ -568,19 +587,15 @@ void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, cudaSt
   B2M_CUDA(cudaGetLastError());
 }
 
-void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
-                float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
-                int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                cudaStream_t s) {
-  GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
-            B, S, H, KVH, D, CAP, scale, err};
-  const int64_t items = (int64_t)B * S * KVH;
-  gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
-  B2M_CUDA(cudaGetLastError());
-  const int G = H / KVH;
+// Runs the attention proper (keys already in place) for the addressing in
+// `a`: the single-token decode kernel for cached causal calls of one query,
+// the tiled kernel for head dims 32..128 in steps of 32, the per-query-warp
+// kernel otherwise.
+static void launch_attend(const GqaArgs &a, cudaStream_t s) {
+  const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
-  if (S == 1 && dok && (G == 1 || G == 2 || G == 4 || G == 8)) {
-    dim3 grid((unsigned)KVH, (unsigned)B);
+  if (a.S == 1 && a.past && a.causal && !a.mask && dok && (G == 1 || G == 2 || G == 4 || G == 8)) {
+    dim3 grid((unsigned)a.KVH, (unsigned)a.B);
 #define B2M_DEC(DD, GG) \
   if (D == DD && G == GG) gqa_decode_kernel<DD, GG><<<grid, 256, 0, s>>>(a);
     B2M_DEC(32, 1) B2M_DEC(32, 2) B2M_DEC(32, 4) B2M_DEC(32, 8)
@@ -589,7 +604,7 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
     B2M_DEC(128, 1) B2M_DEC(128, 2) B2M_DEC(128, 4) B2M_DEC(128, 8)
 #undef B2M_DEC
   } else if (dok) {
-    dim3 grid((unsigned)((S + 63) / 64), (unsigned)H, (unsigned)B);
+    dim3 grid((unsigned)((a.S + 63) / 64), (unsigned)a.H, (unsigned)a.B);
     const int smem = (2 * D * 68 + 64 * D + 64 * 68) * 4;
     switch (D) {
       case 32:
@@ -610,10 +625,44 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
         break;
     }
   } else {
-    dim3 grid((unsigned)((S + 7) / 8), (unsigned)H, (unsigned)B);
+    dim3 grid((unsigned)((a.S + 7) / 8), (unsigned)a.H, (unsigned)a.B);
     gqa_attend_kernel<<<grid, 256, 0, s>>>(a);
   }
   B2M_CUDA(cudaGetLastError());
+}
+
+void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
+                float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
+                int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
+                cudaStream_t s) {
+  GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
+            B, S, H, KVH, D, CAP, scale, err};
+  a.kc_rs = D;
+  a.kc_hs = (int64_t)CAP * D;
+  a.kc_bs = (int64_t)KVH * CAP * D;
+  a.causal = 1;
+  a.kv_len = CAP;
+  a.mask = nullptr;
+  a.mask_bs = 0;
+  const int64_t items = (int64_t)B * S * KVH;
+  gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
+  B2M_CUDA(cudaGetLastError());
+  launch_attend(a, s);
+}
+
+void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
+                int64_t mask_bs, float *out, int B, int S, int T, int H, int KVH, int D, float scale, int causal,
+                int32_t *err, cudaStream_t s) {
+  GqaArgs a{q, k, v, q_rs, kv_rs, const_cast<float *>(k), const_cast<float *>(v), nullptr, nullptr, nullptr, 0, 0,
+            0, out, B, S, H, KVH, D, T, scale, err};
+  a.kc_rs = kv_rs;
+  a.kc_hs = D;
+  a.kc_bs = (int64_t)T * kv_rs;
+  a.causal = causal;
+  a.kv_len = T;
+  a.mask = mask;
+  a.mask_bs = mask_bs;
+  launch_attend(a, s);
 }
 
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s) {

@@ -1320,6 +1320,26 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
   });
 }
 
+B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                               int64_t kv_rs, const float *mask, int64_t mask_bs, float *out, int32_t b, int32_t s,
+                               int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale, int32_t causal) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(b >= 0 && s >= 0 && t > 0 && h > 0 && kvh > 0 && h % kvh == 0 && head_dim > 0 && head_dim <= 256,
+                B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: bad shape arguments");
+    B2M_REQUIRE(q_rs >= (int64_t)h * head_dim && kv_rs >= (int64_t)kvh * head_dim && mask_bs >= 0,
+                B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: row strides too small");
+    B2M_REQUIRE(!causal || s <= t, B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: causal needs s <= t");
+    B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && out), B2M_ERR_INVALID_ARGUMENT,
+                "MultiHeadAttention: null pointer");
+    DeviceGuard dg(ctx->device);
+    if ((int64_t)b * s == 0) return;
+    const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
+    launch_mha(q, k, v, q_rs, kv_rs, mask, mask_bs, out, b, s, t, h, kvh, head_dim, sc, causal ? 1 : 0,
+               ctx->dev_err, ctx->stream);
+  });
+}
+
 B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta) {
   return guarded([&] {
     check_ctx(ctx);

@@ -32,6 +32,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import _native as N
+from .runtime import torch_stream_scope
 
 
 @dataclass
@@ -147,6 +148,7 @@ class Int4Decoder:
         self.t_last = ctx.wrap(self.last.data_ptr(), (batch, c.hidden), np.float32)
         self.t_logits = ctx.wrap(self.logits.data_ptr(), (batch, c.vocab), np.float32)
         self.graph = None
+        self.stream = torch.cuda.Stream(device=dev)
 
     # -- one pass over the layers for `seq` new tokens per sequence -----------
     def _forward(self, seq: int):
@@ -208,11 +210,10 @@ class Int4Decoder:
         seq = ids.numel() // self.B
         if ids.numel() != self.B * seq or ids.numel() > self.max_tokens or seq > self.cap:
             raise N.ArgumentError("decoder prefill: prompt shape does not fit the decoder")
-        stream = torch.cuda.current_stream()
-        self.ctx.set_stream(stream.cuda_stream)
-        self.past.zero_()
-        self.ids[: ids.numel()].copy_(ids)
-        self._forward(seq)
+        with torch_stream_scope(self.ctx, torch, self.stream):
+            self.past.zero_()
+            self.ids[: ids.numel()].copy_(ids)
+            self._forward(seq)
 
     def _decode_body(self):
         self.ids[: self.B].copy_(self.next_ids)
@@ -222,31 +223,30 @@ class Int4Decoder:
         """Greedy decode `steps` tokens (device-resident loop); returns the
         generated ids as an int64 tensor [steps][B] on the device."""
         torch = self.torch
-        out = torch.empty((steps, self.B), device=self.dev, dtype=torch.int64)
-        stream = torch.cuda.current_stream()
-        self.ctx.set_stream(stream.cuda_stream)
-        if use_graph and self.graph is None:
-            # Capture one step; a warm-up step first so every kernel attribute
-            # and scratch size is settled outside the capture. The warm-up's
-            # cache writes and position advance are undone.
-            saved = self.past.clone()
-            self._decode_body()
-            self.past.copy_(saved)
-            self.next_ids.copy_(self.ids[: self.B])
-            g = torch.cuda.CUDAGraph()
-            cap_stream = torch.cuda.Stream(device=self.dev)
-            cap_stream.wait_stream(stream)
-            with torch.cuda.stream(cap_stream):
-                with torch.cuda.graph(g, stream=cap_stream):
-                    self.ctx.set_stream(torch.cuda.current_stream().cuda_stream)
-                    self._decode_body()
-            stream.wait_stream(cap_stream)
-            self.ctx.set_stream(stream.cuda_stream)
-            self.graph = g
-        for i in range(steps):
-            if use_graph:
-                self.graph.replay()
-            else:
+        with torch_stream_scope(self.ctx, torch, self.stream) as stream:
+            out = torch.empty((steps, self.B), device=self.dev, dtype=torch.int64)
+            if use_graph and self.graph is None:
+                # Capture one step; a warm-up step first so every kernel
+                # attribute and scratch size is settled outside the capture.
+                # The warm-up's cache writes and position advance are undone.
+                saved = self.past.clone()
                 self._decode_body()
-            out[i].copy_(self.next_ids)
+                self.past.copy_(saved)
+                self.next_ids.copy_(self.ids[: self.B])
+                g = torch.cuda.CUDAGraph()
+                cap_stream = torch.cuda.Stream(device=self.dev)
+                cap_stream.wait_stream(stream)
+                with torch.cuda.stream(cap_stream):
+                    with torch.cuda.graph(g, stream=cap_stream):
+                        self.ctx.set_stream(torch.cuda.current_stream().cuda_stream)
+                        self._decode_body()
+                stream.wait_stream(cap_stream)
+                self.ctx.set_stream(stream.cuda_stream)
+                self.graph = g
+            for i in range(steps):
+                if use_graph:
+                    self.graph.replay()
+                else:
+                    self._decode_body()
+                out[i].copy_(self.next_ids)
         return out

@@ -9,6 +9,7 @@ lib/src/onnx_graph.dart:102-105).
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import numpy as np
@@ -229,3 +230,25 @@ class PackedWeight:
                 self.handle = None
         except Exception:
             pass
+
+
+@contextlib.contextmanager
+def torch_stream_scope(ctx: Context, torch, own):
+    """Orders the enclosed library calls with torch's current stream.
+
+    b2m_set_stream(NULL) selects the context's own stream, so the legacy default
+    stream (handle 0) cannot be passed through; when it is current, the work
+    runs on `own` (a torch stream of the same device), which first waits for the
+    caller's stream and which the caller's stream waits for on exit."""
+    cur = torch.cuda.current_stream()
+    if cur.cuda_stream != 0:
+        ctx.set_stream(cur.cuda_stream)
+        yield cur
+        return
+    own.wait_stream(cur)
+    try:
+        with torch.cuda.stream(own):
+            ctx.set_stream(own.cuda_stream)
+            yield own
+    finally:
+        cur.wait_stream(own)

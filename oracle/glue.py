@@ -128,3 +128,37 @@ def gqa(q, k, v, num_heads, kv_heads, past_k=None, past_v=None, cos=None, sin=No
         probs = (e / e.sum(-1, keepdims=True)).astype(np.float32)
         out[:, hh] = np.einsum("bst,btd->bsd", probs.astype(np.float64), pv[:, kv].astype(np.float64))
     return out.transpose(0, 2, 1, 3).reshape(b, s, hid), pk, pv
+
+
+def mha(q, k, v, num_heads, kv_heads=None, mask=None, scale=None, causal=False):
+    """opFusedSDPA (lib/src/onnx_ops.dart:2106-2148) per head, as the
+    MultiHeadAttention of a BERT-style graph runs it: q [B][S][H*D], k / v
+    [B][T][KVH*D], mask None or additive [B][T] (a row per batch, broadcast over
+    heads and queries). Scores are a float32 MatMul; scale + mask, max, exp and
+    the sum run in double and the probabilities are stored float32; then the
+    float32 MatMul with V."""
+    q = np.asarray(q, np.float32)
+    k = np.asarray(k, np.float32)
+    v = np.asarray(v, np.float32)
+    b, s, hid = q.shape
+    t = k.shape[1]
+    kv_heads = kv_heads or num_heads
+    d = hid // num_heads
+    group = num_heads // kv_heads
+    sc = scale if scale else 1.0 / math.sqrt(d)
+    qh = q.reshape(b, s, num_heads, d).transpose(0, 2, 1, 3)
+    kh = k.reshape(b, t, kv_heads, d).transpose(0, 2, 1, 3)
+    vh = v.reshape(b, t, kv_heads, d).transpose(0, 2, 1, 3)
+    out = np.zeros((b, num_heads, s, d), np.float32)
+    for hh in range(num_heads):
+        kv = hh // group
+        scores = np.einsum("bsd,btd->bst", qh[:, hh].astype(np.float64), kh[:, kv].astype(np.float64))
+        val = scores.astype(np.float32).astype(np.float64) * sc
+        if mask is not None:
+            val = val + np.asarray(mask, np.float32).astype(np.float64).reshape(b, 1, t)
+        if causal:
+            val = np.where(np.arange(t)[None, None, :] > np.arange(s)[None, :, None], -np.inf, val)
+        e = np.exp(val - val.max(-1, keepdims=True))
+        probs = (e / e.sum(-1, keepdims=True)).astype(np.float32)
+        out[:, hh] = np.einsum("bst,btd->bsd", probs.astype(np.float64), vh[:, kv].astype(np.float64))
+    return out.transpose(0, 2, 1, 3).reshape(b, s, hid)

@@ -152,6 +152,59 @@ def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
     np.testing.assert_array_equal(dvc.cpu().numpy()[:, :, : past + s], wv)
 
 
+@pytest.mark.parametrize("b,s,t,h,kvh,d,mask_mode,causal,packed", [
+    (2, 128, 128, 12, 12, 64, "pad", 0, 1),   # BERT-base shaped, fused QKV rows, padded keys
+    (3, 5, 9, 4, 2, 32, "bcast", 0, 0),       # cross-attention shaped, one mask row for all batches
+    (1, 70, 70, 4, 4, 128, None, 1, 1),       # causal, two query tiles
+    (2, 33, 40, 2, 1, 48, "pad", 0, 0),       # head dim outside the tiled kernel's set
+    (2, 1, 17, 4, 4, 64, "inf", 0, 0),        # one query, -inf masked keys
+    (2, 130, 130, 8, 8, 96, None, 0, 1),      # ragged last tiles in both directions
+])
+def test_mha_additive_mask(ctx, b, s, t, h, kvh, d, mask_mode, causal, packed):
+    rng = np.random.default_rng(b * 1000 + s * 7 + t + d)
+    q = rng.standard_normal((b, s, h * d)).astype(np.float32)
+    k = rng.standard_normal((b, t, kvh * d)).astype(np.float32)
+    v = rng.standard_normal((b, t, kvh * d)).astype(np.float32)
+    mask = None
+    if mask_mode == "pad":
+        mask = np.zeros((b, t), np.float32)
+        for i in range(b):
+            mask[i, t - 1 - i * 3:] = -10000.0     # (1 - attention_mask) * -10000
+    elif mask_mode == "bcast":
+        mask = np.broadcast_to(rng.standard_normal(t).astype(np.float32), (b, t)).copy()
+    elif mask_mode == "inf":
+        mask = np.zeros((b, t), np.float32)
+        mask[:, 3::4] = -np.inf
+    want = glue.mha(q, k, v, h, kvh, mask, causal=bool(causal))
+    if packed:
+        # One [b][s][(h + 2 kvh) d] tensor as a fused QKV projection writes it.
+        assert s == t
+        qkv = np.concatenate([q, k, v], axis=-1)
+        dqkv = _d(qkv)
+        rs = qkv.shape[-1]
+        base = dqkv.data_ptr()
+        pq, pk, pv = (ctypes.c_void_p(base), ctypes.c_void_p(base + h * d * 4),
+                      ctypes.c_void_p(base + (h + kvh) * d * 4))
+        q_rs = kv_rs = rs
+    else:
+        dq, dk, dv = _d(q), _d(k), _d(v)
+        pq, pk, pv = _p(dq), _p(dk), _p(dv)
+        q_rs, kv_rs = h * d, kvh * d
+    dm = _d(mask[:1] if mask_mode == "bcast" else mask) if mask is not None else None
+    dout = torch.empty((b, s, h * d), dtype=torch.float32, device="cuda")
+    N.check(ctx.lib.b2m_mha_dev(ctx.handle, pq, pk, pv, q_rs, kv_rs, _p(dm),
+                                0 if mask_mode == "bcast" else t, _p(dout), b, s, t, h, kvh, d, 0.0, causal))
+    torch.cuda.synchronize()
+    _close(dout.cpu().numpy(), want, 2e-5, "mha out")
+
+
+def test_mha_rejects_bad_arguments(ctx):
+    assert ctx.lib.b2m_mha_dev(ctx.handle, None, None, None, 64, 64, None, 0, None, 1, 4, 3, 2, 2, 32, 0.0,
+                               1) == N.B2M_ERR_INVALID_ARGUMENT     # causal with s > t
+    assert ctx.lib.b2m_mha_dev(ctx.handle, None, None, None, 16, 64, None, 0, None, 1, 4, 4, 2, 2, 32, 0.0,
+                               0) == N.B2M_ERR_INVALID_ARGUMENT     # q row stride below h * head_dim
+
+
 def _ref_decoder(dec, ids, past):
     """numpy composition of the same chain: oracle MatMulNBits / MatMul and
     the oracle/glue ops. `past` is a list of (k, v) per layer or None;
@@ -217,3 +270,51 @@ def test_tiny_decoder_chain_prefill_and_graph_decode(ctx):
         cur = gen[i]
     assert gen.shape == (steps, b)
     assert np.all((gen >= 0) & (gen < cfg.vocab))
+
+
+def _ref_bert(enc, ids, mask01):
+    """numpy composition of the encoder chain: the oracle Gemm (the reference
+    fp32 kernel's operation order) and the oracle/glue ops."""
+    c, hst = enc.cfg, enc.host
+    b, s = ids.shape
+    t = b * s
+    pt = np.tile(hst["pos"][:s] + hst["typ"][0][None, :], (b, 1)).astype(np.float32)
+    x, _ = glue.layernorm(hst["word"][ids.reshape(-1)], hst["emb_g"], hst["emb_b"], c.eps, skip=pt)
+    addm = ((1.0 - mask01.astype(np.float32)) * -10000.0).astype(np.float32)
+    H = c.hidden
+    for li in range(c.layers):
+        wq, bq = hst[(li, "qkv")]
+        qkv = oracle.gemm(x, wq, bq, nthreads=8)
+        a = glue.mha(qkv[:, :H].reshape(b, s, H), qkv[:, H:2 * H].reshape(b, s, H), qkv[:, 2 * H:].reshape(b, s, H),
+                     c.heads, c.heads, addm).reshape(t, H)
+        wo, bo = hst[(li, "o")]
+        h1, _ = glue.layernorm(oracle.gemm(a, wo, bo, nthreads=8), *hst[(li, "ln1")], c.eps, skip=x)
+        w1, b1 = hst[(li, "ff1")]
+        f = glue.gelu(oracle.gemm(h1, w1, b1, nthreads=8))
+        w2, b2 = hst[(li, "ff2")]
+        x, _ = glue.layernorm(oracle.gemm(f, w2, b2, nthreads=8), *hst[(li, "ln2")], c.eps, skip=h1)
+    return x
+
+
+@pytest.mark.parametrize("mode", ["fast", "exact"])
+def test_tiny_bert_chain_matches_composition(ctx, mode):
+    from onnx_runtime_dart_b200.bert import BertConfig, BertEncoder
+
+    cfg = BertConfig.tiny()
+    b, s = 3, 40
+    enc = BertEncoder(ctx, cfg, b, s, seed=5, mode=N.MODE_FAST if mode == "fast" else N.MODE_EXACT, keep_host=True)
+    rng = np.random.default_rng(9)
+    ids = rng.integers(0, cfg.vocab, (b, s), dtype=np.int64)
+    mask01 = np.ones((b, s), np.int64)
+    mask01[1, 31:] = 0
+    want = _ref_bert(enc, ids, mask01)
+    eager = enc.forward(ids, mask01, use_graph=False)
+    graph = enc.forward(ids, mask01, use_graph=True)
+    np.testing.assert_array_equal(graph, eager)
+    got = graph.astype(np.float64)
+    err = float(np.max(np.abs(got - want))) / float(np.max(np.abs(want)))
+    cos = float((got * want).sum() / np.sqrt((got * got).sum() * (want.astype(np.float64) ** 2).sum()))
+    # Tolerance: each Gemm of the FAST chain is within 1e-3 of the exact one;
+    # attention / LayerNorm / GELU add float32 rounding-order differences.
+    assert err <= (1e-3 if mode == "fast" else 1e-4), f"bert chain max rel err {err:.3e}"
+    assert cos >= 0.99999, f"bert chain cosine {cos:.7f}"
