@@ -338,7 +338,7 @@ def run_bert(ctx, torch, stream, batch, seq=128, steps=10, warmup=3, layers=None
         ms_e2e = e0.elapsed_time(e1) / steps
     finite = bool(np.isfinite(out_pin.numpy()).all())
     flops = cfg.flops_per_token(seq) * batch * seq
-    out = {"batch_per_gpu": batch, "seq": seq, "layers": cfg.layers, "mode": "exact" if exact else "fast-3xtf32",
+    out = {"batch_per_gpu": batch, "seq": seq, "layers": cfg.layers, "mode": "exact" if exact else "fast-bf16x3",
            "forward_ms": round(ms_dev, 4), "e2e_forward_ms": round(ms_e2e, 4),
            "flop_per_forward": flops, "tflops": round(flops / (ms_dev / 1e3) / 1e12, 2),
            "h2d_bytes": int(ids.nbytes), "d2h_bytes": int(out_pin.numel() * 4), "finite": finite}
@@ -368,7 +368,7 @@ def main():
     ap.add_argument("--dec-steps", type=int, default=128, help="decoder case: greedy decode steps")
     ap.add_argument("--dec-batch", type=int, default=None, help="decoder case: sequences per GPU (default 64/N)")
     ap.add_argument("--bert-layers", type=int, default=None, help="bert case: layers (default 12)")
-    ap.add_argument("--bert-exact", action="store_true", help="bert case: fp32-exact MatMuls instead of 3xTF32")
+    ap.add_argument("--bert-exact", action="store_true", help="bert case: fp32-exact MatMuls instead of the FAST bf16-split tensor-core path")
     args = ap.parse_args()
 
     rank = int(os.environ.get("RANK", "0"))

@@ -65,7 +65,7 @@ def _ptr(t) -> ctypes.c_void_p:
 
 class BertEncoder:
     """Random-weight encoder of shape `cfg` for batches of `batch` sequences of
-    `seq` tokens. `mode` is the MatMul mode (N.MODE_FAST: 3xTF32 tensor cores;
+    `seq` tokens. `mode` is the MatMul mode (N.MODE_FAST: bf16-split products on the tensor cores;
     N.MODE_EXACT: the reference's fp32 operation order)."""
 
     def __init__(self, ctx, cfg: BertConfig, batch: int, seq: int, seed: int = 0, mode: int = N.MODE_FAST,

@@ -133,9 +133,9 @@ struct b2m_weight {
   int kind = 0;
   int64_t k = 0, n = 0;
   float *f32 = nullptr;  // W_F32: [K][N] row-major
-  // W_F32 FAST-mode planes for 3xTF32: K-major [N][roundup(K,32)], hi = w
-  // with the low 13 mantissa bits cleared, lo = w - hi.
-  float *tf_hi = nullptr, *tf_lo = nullptr;
+  // W_F32 FAST-mode planes: K-major bf16 [N][roundup(K,64)], hi = rn(w),
+  // lo = rn(w - hi).
+  uint16_t *bx_hi = nullptr, *bx_lo = nullptr;
   I8Weight i8;
   NbitsWeight nb;
 };
@@ -185,11 +185,12 @@ struct F32GemmArgs {
 };
 
 void launch_f32_exact(const F32GemmArgs &a, cudaStream_t s);
-// FAST fp32 GEMM (3xTF32 on tcgen05) for a prepacked weight and contiguous A
-// rows; `a_split` is scratch for 2 x M x f32_tc_kp(K) floats.
+// FAST fp32 GEMM (three bf16 products on tcgen05) for a prepacked weight and
+// contiguous A rows; `a_split` is scratch of f32_tc_scratch_bytes(M, K).
 int64_t f32_tc_kp(int64_t K);
+size_t f32_tc_scratch_bytes(int64_t M, int64_t K);
 bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w);
-void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, float *a_split, cudaStream_t s);
+void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cudaStream_t s);
 
 // MatMulNBits
 struct NbitsArgs {

@@ -184,14 +184,45 @@ void require_float(const b2m_tensor *t, const char *what) {
 // fp32 MatMul / Gemm
 // ---------------------------------------------------------------------------
 
-// FAST with a prepacked weight and contiguous A rows runs 3xTF32 on the
-// tensor cores; everything else (and EXACT) runs the bit-exact kernels.
+// Round-to-nearest-even fp32 -> bf16 bits (quiet NaN for NaN).
+uint16_t bf16_rn_host(float v) {
+  uint32_t u;
+  std::memcpy(&u, &v, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x007FFFFFu)) return (uint16_t)((u >> 16) | 0x40u);
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
+
+float bf16_to_float_host(uint16_t h) {
+  const uint32_t u = (uint32_t)h << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+// The device split (k_f32_tc.cu): x0 = rn(x) (truncated instead when rounding
+// would overflow a finite x), x1 = rn(x - x0), x1 = 0 for non-finite x.
+void split_bf16_host(float v, uint16_t &h, uint16_t &l) {
+  h = bf16_rn_host(v);
+  float hf = bf16_to_float_host(h);
+  const bool fin = std::isfinite(v);
+  if (std::isinf(hf) && fin) {
+    uint32_t u;
+    std::memcpy(&u, &v, 4);
+    h = (uint16_t)(u >> 16);
+    hf = bf16_to_float_host(h);
+  }
+  l = bf16_rn_host(fin ? v - hf : 0.f);
+}
+
+// FAST with a prepacked weight and contiguous A rows runs the bf16-split
+// product on the tensor cores; everything else (and EXACT) runs the bit-exact
+// kernels.
 void run_f32(b2m_ctx *ctx, F32GemmArgs &p, const b2m_weight *bw, int32_t mode) {
   p.dev_err = ctx->dev_err;
   if (mode == B2M_MODE_FAST && f32_tc_eligible(p, bw)) {
-    const size_t need = (size_t)(2 * p.M * f32_tc_kp(p.K) * 4);
+    const size_t need = f32_tc_scratch_bytes(p.M, p.K);
     Scratch sc(ctx, need + 256);
-    launch_f32_tc(p, *bw, static_cast<float *>(sc.take(need)), ctx->stream);
+    launch_f32_tc(p, *bw, sc.take(need), ctx->stream);
     return;
   }
   launch_f32_exact(p, ctx->stream);
@@ -798,32 +829,29 @@ B2M_API b2m_status b2m_weight_prepack_f32(b2m_ctx *ctx, const float *host_b, int
       b2m_throw(B2M_ERR_OUT_OF_MEMORY, "weight allocation failed");
     }
     B2M_CUDA(cudaMemcpy(w->f32, src, (size_t)(K * N * 4), cudaMemcpyHostToDevice));
-    // 3xTF32 planes for FAST mode (k_f32_tc.cu): K-major, K padded to 32.
+    // bf16 split planes for FAST mode (k_f32_tc.cu): x0 = rn(x), x1 = rn(x - x0),
+    // K-major, K padded to 64.
     {
-      const int64_t kp = round_up(K, 32);
-      std::vector<float> hi((size_t)(N * kp), 0.f), lo((size_t)(N * kp), 0.f);
+      const int64_t kp = f32_tc_kp(K);
+      std::vector<uint16_t> hi((size_t)(N * kp), 0), lo((size_t)(N * kp), 0);
       for (int64_t kk = 0; kk < K; kk++)
         for (int64_t j = 0; j < N; j++) {
-          const float v = src[kk * N + j];
-          uint32_t u;
-          std::memcpy(&u, &v, 4);
-          u &= 0xFFFFE000u;
-          float h;
-          std::memcpy(&h, &u, 4);
+          uint16_t h, l;
+          split_bf16_host(src[kk * N + j], h, l);
           hi[(size_t)(j * kp + kk)] = h;
-          lo[(size_t)(j * kp + kk)] = v - h;
+          lo[(size_t)(j * kp + kk)] = l;
         }
-      cudaError_t e1 = cudaMalloc(&w->tf_hi, hi.size() * 4);
-      cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&w->tf_lo, lo.size() * 4) : e1;
+      cudaError_t e1 = cudaMalloc(&w->bx_hi, hi.size() * 2);
+      cudaError_t e2 = e1 == cudaSuccess ? cudaMalloc(&w->bx_lo, lo.size() * 2) : e1;
       if (e1 != cudaSuccess || e2 != cudaSuccess) {
         (void)cudaGetLastError();
         cudaFree(w->f32);
-        cudaFree(w->tf_hi);
+        cudaFree(w->bx_hi);
         delete w;
         b2m_throw(B2M_ERR_OUT_OF_MEMORY, "weight allocation failed");
       }
-      B2M_CUDA(cudaMemcpy(w->tf_hi, hi.data(), hi.size() * 4, cudaMemcpyHostToDevice));
-      B2M_CUDA(cudaMemcpy(w->tf_lo, lo.data(), lo.size() * 4, cudaMemcpyHostToDevice));
+      B2M_CUDA(cudaMemcpy(w->bx_hi, hi.data(), hi.size() * 2, cudaMemcpyHostToDevice));
+      B2M_CUDA(cudaMemcpy(w->bx_lo, lo.data(), lo.size() * 2, cudaMemcpyHostToDevice));
     }
     *out = w;
   });
@@ -1066,8 +1094,8 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     DeviceGuard dg(w->ctx->device);
     cudaStreamSynchronize(w->ctx->stream);
     cudaFree(w->f32);
-    cudaFree(w->tf_hi);
-    cudaFree(w->tf_lo);
+    cudaFree(w->bx_hi);
+    cudaFree(w->bx_lo);
     cudaFree(w->i8.bt);
     cudaFree(w->i8.colsum);
     cudaFree(w->i8.ts8);

@@ -132,18 +132,23 @@ def test_matmul_config1_bitwise_with_prepack(ctx):
 
 
 @pytest.mark.parametrize("mkn", [(128, 384, 1536), (1, 64, 100), (300, 200, 130), (700, 96, 2048),
-                                 (1300, 64, 1792), (5, 7, 33)])
+                                 (1300, 64, 1792), (5, 7, 33), (4096, 256, 1280), (4100, 130, 1300)])
 def test_matmul_fast_tensor_core(ctx, mkn):
-    # FAST mode with a prepacked weight: 3xTF32 on tcgen05, against the exact
-    # reference within the fast-mode tolerance (column tiles 32/64/128, K and
-    # N tails, rows beyond a 128-row tile).
+    # FAST mode with a prepacked weight: three bf16 products on tcgen05,
+    # against the exact reference within the fast-mode tolerance (column tiles
+    # 32/64/128/256, K and N tails, rows beyond a 128-row tile, more tiles than
+    # SMs so each persistent CTA runs several with both accumulators).
     m, k, n = mkn
     rng = np.random.default_rng(11 * m + k + n)
     a = rng.standard_normal((m, k)).astype(np.float32)
     b = (rng.standard_normal((k, n)) / np.sqrt(k)).astype(np.float32)
     w = ctx.prepack_f32(b)
     got = ops.opMatMul(a, w, mode=ops.MODE_FAST, ctx=ctx).numpy()
-    assert_fast_close(got, oracle.matmul(a, b, nthreads=8), f"fast matmul {mkn}")
+    want = oracle.matmul(a, b, nthreads=8)
+    assert_fast_close(got, want, f"fast matmul {mkn}")
+    # The split keeps ~16 mantissa bits per operand: far inside the contract.
+    # A missing correction product would show up here as ~1e-3.
+    assert_fast_close(got, want, f"fast matmul {mkn} (split accuracy)", max_rel=5e-5)
 
 
 def test_matmul_fast_batched_shared_weight(ctx):
