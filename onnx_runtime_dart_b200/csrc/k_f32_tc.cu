@@ -18,12 +18,14 @@
 // f32_split_rows.
 //
 // Persistent kernel, one CTA per SM walking 128 x BN output tiles:
-//   warp 0      TMA producer: per 64-k chunk, A0 / A1 (128 x 64) and B0 / B1
-//               (BN x 64) boxes into 128-byte-swizzled shared memory.
-//   warp 1      TMEM allocation; one thread issues the 12 MMAs of a chunk
-//               (4 K=16 steps x 3 products) into one of two accumulators.
+//   warp 0      TMA producer: per BK-wide k chunk (32 or 64), A0 / A1
+//               (128 x BK) and B0 / B1 (BN x BK) boxes into swizzled shared
+//               memory (64- or 128-byte rows).
+//   warp 1      TMEM allocation; one thread issues the MMAs of a chunk
+//               (BK/16 K=16 steps x 3 products) into one of two accumulators.
 //   warps 2-5   epilogue of the other accumulator: tcgen05.ld (lane = row),
-//               alpha / beta*C, stores; it overlaps the next tile's MMAs.
+//               a 32 x 32 transpose through shared memory, alpha / beta*C and
+//               row-contiguous stores; it overlaps the next tile's MMAs.
 // Every wait is bounded; a timeout sets the device error word.
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -40,21 +42,41 @@ using namespace b2m;
 
 constexpr int FT_THREADS = 192;
 constexpr int FT_BM = 128;
-constexpr int FT_BK = 64;  // bf16 per 128-byte swizzle row
+constexpr int FT_KPAD = 64;  // K padding of the split planes
 
-template <int BN, int STAGES>
+// K-major shared-memory descriptor for BK-wide bf16 rows: 128-byte swizzle
+// for BK = 64, 64-byte swizzle for BK = 32 (8-row core groups, SBO = 8 rows).
+template <int BK>
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) {
+  if constexpr (BK == 64) {
+    return sw128_kmajor_desc(saddr);
+  } else {
+    static_assert(BK == 32, "chunk width");
+    uint64_t d = 0;
+    d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);  // start address, 16-byte units
+    d |= (uint64_t)1 << 16;                    // leading byte offset (unused when swizzled)
+    d |= (uint64_t)(512 >> 4) << 32;           // stride byte offset: 8 rows x 64 B
+    d |= (uint64_t)1 << 46;                    // descriptor version (sm_100)
+    d |= (uint64_t)4 << 61;                    // swizzle: 64-byte
+    return d;
+  }
+}
+
+template <int BN, int STAGES, int BK>
 struct FtLayout {
-  static constexpr uint32_t A_CHUNK = FT_BM * 128;  // 128 rows x 64 bf16
-  static constexpr uint32_t B_CHUNK = BN * 128;
+  static constexpr uint32_t A_CHUNK = FT_BM * BK * 2;  // 128 rows x BK bf16
+  static constexpr uint32_t B_CHUNK = BN * BK * 2;
   static constexpr uint32_t STAGE = 2 * A_CHUNK + 2 * B_CHUNK;  // x0, x1 of each
   static constexpr uint32_t BAR_OFF = STAGES * STAGE;
   // full[S], empty[S], acc_full[2], acc_empty[2], drain
   static constexpr uint32_t SLOT_OFF = BAR_OFF + (2 * STAGES + 5) * 8;
   static constexpr uint32_t FLAG_OFF = SLOT_OFF + 8;
-  static constexpr uint32_t BYTES = FLAG_OFF + 8 + 1024;
+  static constexpr uint32_t EPI_OFF = FLAG_OFF + 16;               // 4 warps x 32 x 33 floats
+  static constexpr uint32_t BYTES = EPI_OFF + 4 * 32 * 33 * 4 + 1024;
   static constexpr uint32_t ACC_COLS = BN;
   static constexpr uint32_t TMEM_COLS = 2 * BN <= 64 ? 64 : 2 * BN <= 128 ? 128 : 2 * BN <= 256 ? 256 : 512;
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "column tile");
+  static_assert(BK == 32 || BK == 64, "chunk width");
   static_assert(BYTES <= 232448, "shared memory");
 };
 
@@ -69,12 +91,12 @@ struct FtEpi {
   float beta;
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int BK>
 __global__ void __launch_bounds__(FT_THREADS, 1)
     f32_tc_kernel(const __grid_constant__ CUtensorMap ta0, const __grid_constant__ CUtensorMap ta1,
                   const __grid_constant__ CUtensorMap tb0, const __grid_constant__ CUtensorMap tb1,
                   const FtEpi e, int M, int N, int nchunks, int mtiles, int ntiles, int32_t *dev_err) {
-  using L = FtLayout<BN, STAGES>;
+  using L = FtLayout<BN, STAGES, BK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
@@ -127,10 +149,10 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
           }
           uint8_t *st = smem + s * L::STAGE;
           mbar_arrive_expect_tx(&full[s], L::STAGE);
-          tma_load_2d(st, &ta0, c * FT_BK, m0, &full[s]);
-          tma_load_2d(st + L::A_CHUNK, &ta1, c * FT_BK, m0, &full[s]);
-          tma_load_2d(st + 2 * L::A_CHUNK, &tb0, c * FT_BK, n0, &full[s]);
-          tma_load_2d(st + 2 * L::A_CHUNK + L::B_CHUNK, &tb1, c * FT_BK, n0, &full[s]);
+          tma_load_2d(st, &ta0, c * BK, m0, &full[s]);
+          tma_load_2d(st + L::A_CHUNK, &ta1, c * BK, m0, &full[s]);
+          tma_load_2d(st + 2 * L::A_CHUNK, &tb0, c * BK, n0, &full[s]);
+          tma_load_2d(st + 2 * L::A_CHUNK + L::B_CHUNK, &tb1, c * BK, n0, &full[s]);
         }
       }
       // Loads still in flight after an abort land before the CTA exits.
@@ -157,11 +179,11 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
           }
           tc_fence_after();
           const uint32_t base = smem_u32(smem + s * L::STAGE);
-          const uint64_t a0 = sw128_kmajor_desc(base), a1 = sw128_kmajor_desc(base + L::A_CHUNK);
-          const uint64_t b0 = sw128_kmajor_desc(base + 2 * L::A_CHUNK);
-          const uint64_t b1 = sw128_kmajor_desc(base + 2 * L::A_CHUNK + L::B_CHUNK);
+          const uint64_t a0 = kmajor_desc<BK>(base), a1 = kmajor_desc<BK>(base + L::A_CHUNK);
+          const uint64_t b0 = kmajor_desc<BK>(base + 2 * L::A_CHUNK);
+          const uint64_t b1 = kmajor_desc<BK>(base + 2 * L::A_CHUNK + L::B_CHUNK);
 #pragma unroll
-          for (int kk = 0; kk < 4; kk++) {  // K = 16 bf16 = 32 bytes per MMA
+          for (int kk = 0; kk < BK / 16; kk++) {  // K = 16 bf16 = 32 bytes per MMA
             const uint64_t o = (uint64_t)(2 * kk);
             umma_f16(d, a1 + o, b0 + o, idesc, (c | kk) != 0 ? 1u : 0u);
             umma_f16(d, a0 + o, b1 + o, idesc, 1u);
@@ -177,7 +199,10 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     }
   } else {
     const int q = warp & 3;  // TMEM lane quarter
-    const bool vec = (N & 3) == 0 && (e.ldy & 3) == 0 && (reinterpret_cast<uintptr_t>(e.Y) & 15) == 0;
+    // Per-warp 32 x 33 transpose buffer: the accumulator arrives one row per
+    // lane; it leaves one column per lane, so every store instruction writes
+    // 128 contiguous bytes of one output row.
+    float *tb = reinterpret_cast<float *>(smem + L::EPI_OFF) + (warp - 2) * (32 * 33);
     pdl_wait();  // Y may still be read by the kernels this one overlaps
     int local = 0;
     for (int t = blockIdx.x; t < ntile_total; t += gridDim.x, local++) {
@@ -186,43 +211,50 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
       if (!warp_wait_or_abort(&acc_full[buf], use & 1u, abort_flag, dev_err)) break;
       tc_fence_after();
       const int m0 = (t / ntiles) * FT_BM, n0 = (t % ntiles) * BN;
-      const int row = m0 + q * 32 + lane;
+      const int r0 = m0 + q * 32;
       const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * L::ACC_COLS);
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t v[16];
-        tmem_ld16(tbase + (uint32_t)c0, v);
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld16(tbase + (uint32_t)c0, *reinterpret_cast<uint32_t(*)[16]>(v));
+        tmem_ld16(tbase + (uint32_t)c0 + 16u, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
         tmem_ld_wait();
-        if (row < M && n0 + c0 < N) {
-          float y[16];
+        if (c0 + 32 == BN) {
+          // The accumulator is fully read: release it to the MMA warp early.
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[buf]);
+        }
+        if (n0 + c0 >= N || r0 >= M) continue;
 #pragma unroll
-          for (int j = 0; j < 16; j++) {
-            float tv = __uint_as_float(v[j]);
-            const int col = n0 + c0 + j;
+        for (int j = 0; j < 32; j++) tb[lane * 33 + j] = __uint_as_float(v[j]);
+        __syncwarp();
+        const int col = n0 + c0 + lane;
+        if (col < N) {
+          float cv_bcast = 0.f;
+          const bool bcast = e.C && e.c_rs == 0;
+          if (bcast) {
+            cv_bcast = e.C[(int64_t)col * e.c_cs];
+            if (e.has_beta) cv_bcast = cv_bcast * e.beta;
+          }
+          const int rows = min(32, M - r0);
+          float *yc = e.Y + (int64_t)r0 * e.ldy + col;
+#pragma unroll 4
+          for (int i = 0; i < rows; i++) {
+            float tv = tb[i * 33 + lane];
             if (e.has_alpha) tv = tv * e.alpha;
-            if (e.C && col < N) {
-              float cv = e.C[(int64_t)row * e.c_rs + (int64_t)col * e.c_cs];
+            if (bcast) {
+              tv = tv + cv_bcast;
+            } else if (e.C) {
+              float cv = e.C[(int64_t)(r0 + i) * e.c_rs + (int64_t)col * e.c_cs];
               if (e.has_beta) cv = cv * e.beta;
               tv = tv + cv;
             }
-            y[j] = tv;
-          }
-          float *yr = e.Y + (int64_t)row * e.ldy + n0 + c0;
-          if (vec && n0 + c0 + 16 <= N) {
-#pragma unroll
-            for (int j = 0; j < 16; j += 4)
-              *reinterpret_cast<float4 *>(yr + j) = make_float4(y[j], y[j + 1], y[j + 2], y[j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 16; j++)
-              if (n0 + c0 + j < N) yr[j] = y[j];
+            yc[(int64_t)i * e.ldy] = tv;
           }
         }
+        __syncwarp();
       }
-      // This warp's quarter of the accumulator is free for the tile after next.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();
@@ -272,25 +304,26 @@ __global__ void __launch_bounds__(256) f32_split_rows(const float *__restrict__ 
   }
 }
 
-CUtensorMap make_map(const void *base, int64_t rows, int64_t kp, int box_rows) {
+CUtensorMap make_map(const void *base, int64_t rows, int64_t kp, int box_rows, int bk) {
   CUtensorMap m;
   const cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)(kp * 2)};
-  const cuuint32_t box[2] = {(cuuint32_t)FT_BK, (cuuint32_t)box_rows};
+  const cuuint32_t box[2] = {(cuuint32_t)bk, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
-                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                    bk == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for a bf16 operand plane");
   return m;
 }
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int BK>
 void launch_ft(const F32GemmArgs &p, const b2m_weight &w, const __nv_bfloat16 *a0, const __nv_bfloat16 *a1,
                int64_t kp, cudaStream_t s) {
-  using L = FtLayout<BN, STAGES>;
-  const CUtensorMap t0 = make_map(a0, p.M, kp, FT_BM), t1 = make_map(a1, p.M, kp, FT_BM);
-  const CUtensorMap u0 = make_map(w.bx_hi, w.n, kp, BN), u1 = make_map(w.bx_lo, w.n, kp, BN);
+  using L = FtLayout<BN, STAGES, BK>;
+  const CUtensorMap t0 = make_map(a0, p.M, kp, FT_BM, BK), t1 = make_map(a1, p.M, kp, FT_BM, BK);
+  const CUtensorMap u0 = make_map(w.bx_hi, w.n, kp, BN, BK), u1 = make_map(w.bx_lo, w.n, kp, BN, BK);
   FtEpi e;
   e.Y = p.Y;
   e.ldy = p.ldy;
@@ -303,7 +336,7 @@ void launch_ft(const F32GemmArgs &p, const b2m_weight &w, const __nv_bfloat16 *a
   e.beta = p.beta;
   const int mt = (int)((p.M + FT_BM - 1) / FT_BM), nt = (int)((p.N + BN - 1) / BN);
   const int64_t tiles = (int64_t)mt * nt;
-  set_smem_limit_once<f32_tc_kernel<BN, STAGES>>((int)L::BYTES);
+  set_smem_limit_once<f32_tc_kernel<BN, STAGES, BK>>((int)L::BYTES);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)std::min<int64_t>(tiles, device_sm_count()));
   cfg.blockDim = dim3(FT_THREADS);
@@ -314,13 +347,13 @@ void launch_ft(const F32GemmArgs &p, const b2m_weight &w, const __nv_bfloat16 *a
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_tc_kernel<BN, STAGES>, t0, t1, u0, u1, e, (int)p.M, (int)p.N,
-                              (int)(kp / FT_BK), mt, nt, p.dev_err));
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_tc_kernel<BN, STAGES, BK>, t0, t1, u0, u1, e, (int)p.M, (int)p.N,
+                              (int)(kp / BK), mt, nt, p.dev_err));
 }
 
 }  // namespace
 
-int64_t f32_tc_kp(int64_t K) { return (K + FT_BK - 1) / FT_BK * FT_BK; }
+int64_t f32_tc_kp(int64_t K) { return (K + FT_KPAD - 1) / FT_KPAD * FT_KPAD; }
 
 size_t f32_tc_scratch_bytes(int64_t M, int64_t K) { return (size_t)(2 * M * f32_tc_kp(K) * 2); }
 
@@ -346,11 +379,29 @@ void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cud
     cfg.numAttrs = 1;
     B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_split_rows, p.A, p.sa_m, a0, a1, p.M, p.K, kp));
   }
-  // Column tile: 256 when that still gives every SM a tile, else narrower.
+  // Column tile by a makespan model: rounds of tiles over the SMs times the
+  // tile width, over a relative mainloop efficiency per width (narrow tiles
+  // re-read A more often per flop). 32-k stages keep four or more stages in
+  // flight at every width.
   const int sms = device_sm_count();
   const int64_t mt = (p.M + FT_BM - 1) / FT_BM;
-  if (mt * ((p.N + 255) / 256) >= sms) launch_ft<256, 2>(p, w, a0, a1, kp, s);
-  else if (mt * ((p.N + 127) / 128) >= sms / 2) launch_ft<128, 3>(p, w, a0, a1, kp, s);
-  else if (mt * ((p.N + 63) / 64) >= sms / 2) launch_ft<64, 4>(p, w, a0, a1, kp, s);
-  else launch_ft<32, 4>(p, w, a0, a1, kp, s);
+  static const int widths[5] = {256, 192, 128, 64, 32};
+  static const double eff[5] = {0.9, 0.88, 0.8, 0.6, 0.4};
+  int best = 0;
+  double best_cost = 0.0;
+  for (int i = 0; i < 5; i++) {
+    const int64_t tiles = mt * ((p.N + widths[i] - 1) / widths[i]);
+    const double cost = (double)((tiles + sms - 1) / sms) * widths[i] / eff[i];
+    if (i == 0 || cost < best_cost) {
+      best = i;
+      best_cost = cost;
+    }
+  }
+  switch (widths[best]) {
+    case 256: launch_ft<256, 4, 32>(p, w, a0, a1, kp, s); break;
+    case 192: launch_ft<192, 5, 32>(p, w, a0, a1, kp, s); break;
+    case 128: launch_ft<128, 6, 32>(p, w, a0, a1, kp, s); break;
+    case 64: launch_ft<64, 8, 32>(p, w, a0, a1, kp, s); break;
+    default: launch_ft<32, 8, 32>(p, w, a0, a1, kp, s); break;
+  }
 }

@@ -132,12 +132,14 @@ def test_matmul_config1_bitwise_with_prepack(ctx):
 
 
 @pytest.mark.parametrize("mkn", [(128, 384, 1536), (1, 64, 100), (300, 200, 130), (700, 96, 2048),
-                                 (1300, 64, 1792), (5, 7, 33), (4096, 256, 1280), (4100, 130, 1300)])
+                                 (1300, 64, 1792), (5, 7, 33), (4096, 256, 1280), (4100, 130, 1300),
+                                 (4096, 64, 3072), (4736, 96, 512), (1280, 80, 640)])
 def test_matmul_fast_tensor_core(ctx, mkn):
     # FAST mode with a prepacked weight: three bf16 products on tcgen05,
     # against the exact reference within the fast-mode tolerance (column tiles
-    # 32/64/128/256, K and N tails, rows beyond a 128-row tile, more tiles than
-    # SMs so each persistent CTA runs several with both accumulators).
+    # 32/64/128/192/256 by the launcher's cost model, K and N tails, rows beyond
+    # a 128-row tile, more tiles than SMs so each persistent CTA runs several
+    # with both accumulators).
     m, k, n = mkn
     rng = np.random.default_rng(11 * m + k + n)
     a = rng.standard_normal((m, k)).astype(np.float32)
