@@ -330,6 +330,14 @@ B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, con
                                int64_t kv_rs, const float *mask, int64_t mask_bs, float *out, int32_t b, int32_t s,
                                int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale, int32_t causal);
 
+/* DynamicQuantizeLinear (opDynamicQuantizeLinear, lib/src/onnx_ops.dart:3556):
+ * uint8 y[n] from float x[n] with the range's scale (float, written to
+ * *scale) and zero point (uint8, *zero_point), all device memory, bit-exact
+ * with the reference (scale and zero point in double then float32, round
+ * half to even). y / scale / zero_point feed b2m_matmul_integer directly. */
+B2M_API b2m_status b2m_dynamic_quantize_linear_dev(b2m_ctx *ctx, const float *x, int64_t n, uint8_t *y,
+                                                   float *scale, uint8_t *zero_point);
+
 /* past[i] += delta for i < n (int32 device counters of a decode loop). */
 B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta);
 

@@ -61,6 +61,8 @@ struct b2m_ctx {
   size_t scratch_bytes = 0;
   // Device word that kernels with bounded spin-waits set on timeout.
   int32_t *dev_err = nullptr;
+  // Self-resetting device counter (zero between calls), inside the same block.
+  uint32_t *dev_counter = nullptr;
   // Programmatic dependent launch for the decode kernels (env
   // B2M_DISABLE_PDL=1 turns it off, e.g. to compare timelines).
   bool pdl = true;
@@ -233,6 +235,13 @@ void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, in
                 int64_t mask_bs, float *out, int B, int S, int T, int H, int KVH, int D, float scale, int causal,
                 int32_t *err, cudaStream_t s);
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s);
+
+// DynamicQuantizeLinear (k_quant.cu): y = quantized x, scale / zp written to
+// device memory. `partial` holds dql_partial_floats() floats; `counter` is a
+// zeroed device word the kernel leaves zeroed.
+size_t dql_partial_floats();
+void launch_dynamic_quantize(const float *x, int64_t n, uint8_t *y, float *scale, uint8_t *zp, float *partial,
+                             uint32_t *counter, cudaStream_t s);
 
 // MatMulInteger / QLinearMatMul
 struct I8GemmArgs {

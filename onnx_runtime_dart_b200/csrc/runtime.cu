@@ -638,8 +638,11 @@ B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx) {
     B2M_CUDA(cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &thr));
     B2M_CUDA(cudaEventCreate(&ctx->ev0));
     B2M_CUDA(cudaEventCreate(&ctx->ev1));
-    B2M_CUDA(cudaMalloc(&ctx->dev_err, sizeof(int32_t)));
-    B2M_CUDA(cudaMemset(ctx->dev_err, 0, sizeof(int32_t)));
+    // One zeroed block: the error word, then counters that kernels reset
+    // themselves after use (the DynamicQuantizeLinear block counter).
+    B2M_CUDA(cudaMalloc(&ctx->dev_err, 256));
+    B2M_CUDA(cudaMemset(ctx->dev_err, 0, 256));
+    ctx->dev_counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(ctx->dev_err) + 128);
     const char *no_pdl = std::getenv("B2M_DISABLE_PDL");
     ctx->pdl = !(no_pdl && no_pdl[0] == '1');
     *out_ctx = ctx;
@@ -1365,6 +1368,20 @@ B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, con
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
     launch_mha(q, k, v, q_rs, kv_rs, mask, mask_bs, out, b, s, t, h, kvh, head_dim, sc, causal ? 1 : 0,
                ctx->dev_err, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_dynamic_quantize_linear_dev(b2m_ctx *ctx, const float *x, int64_t n, uint8_t *y,
+                                                   float *scale, uint8_t *zero_point) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(n >= 0 && scale && zero_point && (n == 0 || (x && y)), B2M_ERR_INVALID_ARGUMENT,
+                "DynamicQuantizeLinear: bad arguments");
+    DeviceGuard dg(ctx->device);
+    const size_t need = dql_partial_floats() * sizeof(float);
+    Scratch sc(ctx, need + 256);
+    launch_dynamic_quantize(x, n, y, scale, zero_point, static_cast<float *>(sc.take(need)), ctx->dev_counter,
+                            ctx->stream);
   });
 }
 

@@ -170,6 +170,29 @@ def opQLinearMatMul(a, aS, aZp, b, bS, bZp, yS, yZp, *, lo: int, hi: int, ctx: C
     return _wrap_out(ctx, y, out)
 
 
+def opDynamicQuantizeLinear(x, *, ctx: Context | None = None):
+    """opDynamicQuantizeLinear (lib/src/onnx_ops.dart:3556): returns
+    [y uint8 (x's shape), scale float32 scalar, zero point uint8 scalar], all
+    device tensors, bit-exact with the reference. y and the zero point feed
+    opMatMulInteger as A and aZp without leaving the device."""
+    ctx = _ctx(ctx)
+    if isinstance(x, DeviceTensor):
+        xt = x
+    else:
+        xt = ctx.upload(np.asarray(x, np.float32))
+    if xt.dtype != np.float32:
+        raise N.ArgumentError("DynamicQuantizeLinear: x must be float32")
+    shape = xt.shape
+    n = int(np.prod(shape)) if shape else 1
+    y = ctx.empty(shape, np.uint8)
+    scale = ctx.empty([], np.float32)
+    zp = ctx.empty([], np.uint8)
+    N.check(ctx.lib.b2m_dynamic_quantize_linear_dev(ctx.handle, ctypes.c_void_p(xt.data_ptr), n,
+                                                    ctypes.c_void_p(y.data_ptr), ctypes.c_void_p(scale.data_ptr),
+                                                    ctypes.c_void_p(zp.data_ptr)))
+    return [y, scale, zp]
+
+
 # ---------------------------------------------------------------------------
 # int4 MatMulNBits
 # ---------------------------------------------------------------------------

@@ -66,6 +66,8 @@ def _load():
     lib.orc_qlinear_multiplier.restype = ctypes.c_float
     lib.orc_round_even.argtypes = [ctypes.c_double]
     lib.orc_round_even.restype = ctypes.c_int64
+    lib.orc_dynamic_quantize_linear.argtypes = [_f32p, _i64, _u8p, ctypes.POINTER(ctypes.c_float)]
+    lib.orc_dynamic_quantize_linear.restype = ctypes.c_int64
     lib.orc_matmul_nbits.argtypes = [_f32p, _i64, _i64, _u8p, _f32p, _u8p, _f32p, _f32p, _i64, _i64, _f32p, ctypes.c_int]
     lib.orc_matmul_nbits.restype = ctypes.c_int
     lib.orc_nbits_dequant.argtypes = [_u8p, _f32p, _u8p, _f32p, _i64, _i64, _i64, _f32p]
@@ -172,6 +174,16 @@ def qlinear_multiplier(a_scale, b_scale, y_scale):
 
 def round_even(v):
     return int(_load().orc_round_even(float(v)))
+
+
+def dynamic_quantize_linear(x):
+    """``opDynamicQuantizeLinear`` (onnx_ops.dart:3556-3583): returns
+    (y uint8 of x's shape, scale float32, zero point int)."""
+    x = _c(x, np.float32)
+    y = np.zeros(x.size, np.uint8)
+    sc = ctypes.c_float()
+    zp = _load().orc_dynamic_quantize_linear(_p(x.reshape(-1), _f32p), x.size, _p(y, _u8p), ctypes.byref(sc))
+    return y.reshape(x.shape), np.float32(sc.value), int(zp)
 
 
 def qlinear_matmul(a, a_scale, a_zp, b, b_scale, b_zp, y_scale, y_zp, lo, hi, nthreads=1):

@@ -325,6 +325,37 @@ static int64_t round_even(double v) {
 
 ORC_API int64_t orc_round_even(double v) { return round_even(v); }
 
+/* opDynamicQuantizeLinear (lib/src/onnx_ops.dart:3556-3583): range spans 0;
+ * scale and zero point computed in double and stored as float32 where the
+ * reference stores through a Float32List; y = clamp(roundEven(f32(x/scale))
+ * + zp, 0, 255). Returns the zero point; *scale_out receives the scale. */
+ORC_API int64_t orc_dynamic_quantize_linear(const float *x, int64_t n, uint8_t *y, float *scale_out) {
+  double mn = 0, mx = 0;
+  for (int64_t i = 0; i < n; i++) {
+    const double v = x[i];
+    if (v < mn) mn = v;
+    if (v > mx) mx = v;
+  }
+  const float scale_f = (float)((mx - mn) / 255.0);
+  const double scale = scale_f;
+  const float zf32 = scale == 0 ? 0.0f : (float)(-mn / scale);
+  double zpf = zf32;
+  zpf = zpf < 0.0 ? 0.0 : (zpf > 255.0 ? 255.0 : zpf);
+  const int64_t zp = round_even(zpf);
+  for (int64_t i = 0; i < n; i++) {
+    int64_t q;
+    if (scale == 0) {
+      q = zp;
+    } else {
+      const float t = (float)((double)x[i] / scale);
+      q = round_even((double)t) + zp;
+    }
+    y[i] = (uint8_t)(q < 0 ? 0 : (q > 255 ? 255 : q));
+  }
+  *scale_out = scale_f;
+  return zp;
+}
+
 /* QLinearMatMul requant multiplier (:95-99): each step rounds to float32. */
 ORC_API float orc_qlinear_multiplier(float a_scale, float b_scale, float y_scale) {
   float f = (float)((double)a_scale * (double)b_scale);

@@ -125,3 +125,26 @@ def test_round_even_and_multiplier():
     assert [oracle.round_even(v) for v in (0.5, 1.5, 2.5, -0.5, -1.5, 2.4999, -2.6)] == [0, 2, 2, 0, -2, 2, -3]
     m = oracle.qlinear_multiplier(0.02, 0.05, 0.1)
     assert m == np.float32(np.float32(np.float32(0.02) * np.float32(0.05)) / np.float32(0.1))
+
+
+def test_dynamic_quantize_linear_fixture():
+    # test/fixtures/dynamicquantizelinear: [y, scale, zero point] bit-exact.
+    g = load_golden("dynamicquantizelinear")
+    y, scale, zp = oracle.dynamic_quantize_linear(g["arrays"][0])
+    exp = g["expected_arrays"]
+    assert y.astype(np.int64).tolist() == exp["out0"].tolist()
+    assert np.float32(scale) == np.float32(exp["out1"])
+    assert zp == int(exp["out2"])
+
+
+def test_dynamic_quantize_linear_edges():
+    # Range always spans 0; all-zero input gives scale 0, zp 0, y 0.
+    y, s, z = oracle.dynamic_quantize_linear(np.zeros(5, np.float32))
+    assert s == 0 and z == 0 and y.tolist() == [0] * 5
+    y, s, z = oracle.dynamic_quantize_linear(np.array([1.0, 2.0, 255.0], np.float32))
+    assert z == 0 and s == np.float32(1.0) and y.tolist() == [1, 2, 255]
+    y, s, z = oracle.dynamic_quantize_linear(np.array([-255.0, -1.0], np.float32))
+    assert z == 255 and y.tolist() == [0, 254]
+    # ties go to even: 0.5 / 1 and 2.5 / 1 with scale 1
+    y, s, z = oracle.dynamic_quantize_linear(np.array([0.5, 2.5, 255.0], np.float32))
+    assert y.tolist() == [0, 2, 255]
