@@ -320,15 +320,17 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
  * batched MatMuls of opFusedSDPA, :2106-2148). q: [b][s] rows of h*head_dim
  * (row stride q_rs); k / v: [b][t] rows of kvh*head_dim (row stride kv_rs),
  * h a multiple of kvh (query head i reads kv head i / (h / kvh)).
- * mask: NULL or an additive per-key mask, row r = mask + r*mask_bs of t
- * floats for batch r (mask_bs 0 broadcasts one row), added to the scaled
- * scores before the softmax (the [batch, 1, 1, t] attention bias BERT-style
- * graphs build from attention_mask). causal != 0 additionally hides keys
- * j > i. Scale <= 0 means 1/sqrt(head_dim). out: [b][s] rows of h*head_dim.
- * head_dim <= 256. */
+ * mask: NULL or an additive bias on the scaled scores, the element for
+ * (batch r, query head i, query row p, key j) at
+ * mask[r*mask_bs + i*mask_hs + p*mask_qs + j]; zero strides broadcast. A
+ * BERT-style key-padding mask [b][t] is (t, 0, 0); the reference's
+ * attention_bias [b][bias_heads][s][t] is (bias_heads*s*t, bias_heads == 1 ?
+ * 0 : s*t, t). causal != 0 additionally hides keys j > p. Scale <= 0 means
+ * 1/sqrt(head_dim). out: [b][s] rows of h*head_dim. head_dim <= 256. */
 B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
-                               int64_t kv_rs, const float *mask, int64_t mask_bs, float *out, int32_t b, int32_t s,
-                               int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale, int32_t causal);
+                               int64_t kv_rs, const float *mask, int64_t mask_bs, int64_t mask_hs, int64_t mask_qs,
+                               float *out, int32_t b, int32_t s, int32_t t, int32_t h, int32_t kvh, int32_t head_dim,
+                               float scale, int32_t causal);
 
 /* DynamicQuantizeLinear (opDynamicQuantizeLinear, lib/src/onnx_ops.dart:3556):
  * uint8 y[n] from float x[n] with the range's scale (float, written to
@@ -337,6 +339,18 @@ B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, con
  * half to even). y / scale / zero_point feed b2m_matmul_integer directly. */
 B2M_API b2m_status b2m_dynamic_quantize_linear_dev(b2m_ctx *ctx, const float *x, int64_t n, uint8_t *y,
                                                    float *scale, uint8_t *zero_point);
+
+/* RotaryEmbedding (opRotaryEmbedding, lib/src/onnx_ops.dart:2659-2717) over
+ * [b][s] rows of heads*head_dim floats (row strides x_rs / y_rs; y may be x).
+ * positions: int64 ids [b][s], or [s] shared by the batch when
+ * pos_per_batch is 0; cos_cache / sin_cache: [max_pos][half]. The first
+ * rotary_dim (even, <= 2*half) values of each head rotate, GPT-NeoX
+ * rotate-half or, with interleaved, GPT-J pairs; the rest pass through.
+ * head_dim <= 256. A position outside [0, max_pos) is a device error. */
+B2M_API b2m_status b2m_rotary_dev(b2m_ctx *ctx, const float *x, int64_t x_rs, const int64_t *positions,
+                                  int32_t pos_per_batch, const float *cos_cache, const float *sin_cache,
+                                  int32_t half, int32_t max_pos, float *y, int64_t y_rs, int32_t b, int32_t s,
+                                  int32_t heads, int32_t head_dim, int32_t rotary_dim, int32_t interleaved);
 
 /* past[i] += delta for i < n (int32 device counters of a decode loop). */
 B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta);

@@ -161,7 +161,7 @@ class BertEncoder:
         for lw in self.layers:
             self._gemm("x", lw, "qkv", "qkv")
             chk(lib.b2m_mha_dev(h, ctypes.c_void_p(qkv), ctypes.c_void_p(qkv + H * 4), ctypes.c_void_p(qkv + 2 * H * 4),
-                                3 * H, 3 * H, _ptr(self.mask), self.S, _ptr(self.attn), self.B, self.S, self.S,
+                                3 * H, 3 * H, _ptr(self.mask), self.S, 0, 0, _ptr(self.attn), self.B, self.S, self.S,
                                 c.heads, c.heads, D, ctypes.c_float(0.0), 0))
             self._gemm("attn", lw, "o", "o")
             chk(lib.b2m_layernorm_dev(h, _ptr(self.o), _ptr(self.x), _ptr(lw["ln1_g"]), _ptr(lw["ln1_b"]),

@@ -41,6 +41,8 @@ void b2m_set_last_error(const std::string &msg);
 #define B2M_DEVERR_NONE 0
 #define B2M_DEVERR_MBAR_TIMEOUT 1
 #define B2M_DEVERR_TMEM_TIMEOUT 2
+#define B2M_DEVERR_INDEX 4       // gather id / rotary position outside its table
+#define B2M_DEVERR_CACHE_FULL 5  // KV-cache append past its capacity
 
 struct b2m_ctx {
   int device = 0;
@@ -232,9 +234,12 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
                 cudaStream_t s);
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
-                int64_t mask_bs, float *out, int B, int S, int T, int H, int KVH, int D, float scale, int causal,
-                int32_t *err, cudaStream_t s);
+                int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
+                int D, float scale, int causal, int32_t *err, cudaStream_t s);
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s);
+void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,
+                   const float *sin, int half, int max_pos, float *y, int64_t y_rs, int B, int S, int heads, int D,
+                   int rot, int interleaved, int32_t *err, cudaStream_t s);
 
 // DynamicQuantizeLinear (k_quant.cu): y = quantized x, scale / zp written to
 // device memory. `partial` holds dql_partial_floats() floats; `counter` is a

@@ -126,7 +126,7 @@ __global__ void gather_rows_kernel(const float *__restrict__ table, const int64_
   if (r >= rows) return;
   const int64_t id = ids[r];
   const bool ok = id >= 0 && id < V;
-  if (!ok && threadIdx.x == 0 && err) atomicExch(err, 4);
+  if (!ok && threadIdx.x == 0 && err) atomicExch(err, B2M_DEVERR_INDEX);
   for (int64_t j = threadIdx.x; j < D; j += blockDim.x) y[r * D + j] = ok ? table[id * D + j] : 0.f;
 }
 
@@ -175,6 +175,37 @@ __device__ __forceinline__ void rotate_head(float *v, const float *cos, const fl
   }
 }
 
+// RotaryEmbedding of [B][S] rows of heads x D floats, one warp per (token,
+// head): the head is staged in shared memory, rotated in place, written out.
+// A position outside [0, max_pos) sets the device error word and passes the
+// head through unrotated.
+__global__ void __launch_bounds__(256) rotary_kernel(const float *__restrict__ x, int64_t x_rs,
+                                                     const int64_t *__restrict__ pos, int pos_per_batch,
+                                                     const float *cos, const float *sin, int half, int max_pos,
+                                                     float *y, int64_t y_rs, int B, int S, int heads, int D, int rot,
+                                                     int interleaved, int32_t *err) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t item = (int64_t)blockIdx.x * 8 + warp;
+  if (item >= (int64_t)B * S * heads) return;
+  const int h = (int)(item % heads);
+  const int64_t bs = item / heads;
+  const int s = (int)(bs % S), b = (int)(bs / S);
+  const int64_t p = pos[(pos_per_batch ? (int64_t)b * S : 0) + s];
+  __shared__ float hb[8][256];
+  float *v = hb[warp];
+  const float *src = x + bs * x_rs + (int64_t)h * D;
+  for (int d = lane; d < D; d += 32) v[d] = src[d];
+  __syncwarp();
+  if (p >= 0 && p < max_pos) {
+    rotate_head(v, cos, sin, p, half, rot, interleaved, lane, 32);
+  } else if (lane == 0 && err) {
+    atomicExch(err, B2M_DEVERR_INDEX);
+  }
+  __syncwarp();
+  float *dst = y + bs * y_rs + (int64_t)h * D;
+  for (int d = lane; d < D; d += 32) dst[d] = v[d];
+}
+
 struct GqaArgs {
   const float *q, *k, *v;   // [B][S][H*D], [B][S][KVH*D] (row strides below)
   int64_t q_rs, kv_rs;      // floats between consecutive tokens
@@ -193,8 +224,10 @@ struct GqaArgs {
   int64_t kc_bs, kc_hs, kc_rs;
   int causal;               // 1: query i sees keys [0, past + i]; 0: keys [0, kv_len)
   int kv_len;
-  const float *mask;        // additive per-key mask [B][kv_len] (row stride mask_bs; 0 broadcasts), or null
-  int64_t mask_bs;
+  // Additive score bias or null: element (b, query head h, query s, key j)
+  // at mask[b*mask_bs + h*mask_hs + s*mask_qs + j] (0 strides broadcast).
+  const float *mask;
+  int64_t mask_bs, mask_hs, mask_qs;
 };
 
 // Appends this call's keys / values to the cache (rotary on K), one warp per
@@ -210,7 +243,7 @@ __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
   const int past = a.past[b];
   const int pos = past + s;
   if (pos >= a.CAP) {
-    if (lane == 0 && a.err) atomicExch(a.err, 5);
+    if (lane == 0 && a.err) atomicExch(a.err, B2M_DEVERR_CACHE_FULL);
     return;
   }
   __shared__ float kbuf[8][256];
@@ -252,7 +285,8 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
   for (int i = 0; i < 8; i++) qr[i] = lane + 32 * i < a.D ? qv[lane + 32 * i] : 0.f;
   const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
   const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
-  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs : nullptr;
+  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs + (int64_t)h * a.mask_hs + (int64_t)s * a.mask_qs
+                           : nullptr;
   float m = -INFINITY, l = 0.f;
   float acc[8];
 #pragma unroll
@@ -325,7 +359,8 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
   const int max_key = a.causal ? min(past + last_q, a.CAP - 1) : a.kv_len - 1;
   const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
   const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
-  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs : nullptr;
+  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs + (int64_t)h * a.mask_hs : nullptr;
+  const bool per_query = mk && a.mask_qs != 0;  // else one bias row shared by all queries
   __shared__ float mrow[64];
   float m[4], l[4], o[4][CPT];
 #pragma unroll
@@ -346,7 +381,7 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
     }
     if (tid < KT) {
       const int j = j0 + tid;
-      mrow[tid] = j > max_key ? -INFINITY : (mk ? mk[j] : 0.f);
+      mrow[tid] = j > max_key ? -INFINITY : (mk && !per_query ? mk[j] : 0.f);
     }
     __syncthreads();
     float sc[4][4];
@@ -371,6 +406,8 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         sc[i][j] += mrow[tx * 4 + j];
+        if (per_query && q0 + ty * 4 + i < a.S && j0 + tx * 4 + j <= max_key)
+          sc[i][j] += mk[(int64_t)(q0 + ty * 4 + i) * a.mask_qs + j0 + tx * 4 + j];
         if (a.causal && j0 + tx * 4 + j > qpos) sc[i][j] = -INFINITY;
         rmax = fmaxf(rmax, sc[i][j]);
       }
@@ -643,7 +680,7 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
   a.causal = 1;
   a.kv_len = CAP;
   a.mask = nullptr;
-  a.mask_bs = 0;
+  a.mask_bs = a.mask_hs = a.mask_qs = 0;
   const int64_t items = (int64_t)B * S * KVH;
   gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
   B2M_CUDA(cudaGetLastError());
@@ -651,8 +688,8 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
 }
 
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
-                int64_t mask_bs, float *out, int B, int S, int T, int H, int KVH, int D, float scale, int causal,
-                int32_t *err, cudaStream_t s) {
+                int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
+                int D, float scale, int causal, int32_t *err, cudaStream_t s) {
   GqaArgs a{q, k, v, q_rs, kv_rs, const_cast<float *>(k), const_cast<float *>(v), nullptr, nullptr, nullptr, 0, 0,
             0, out, B, S, H, KVH, D, T, scale, err};
   a.kc_rs = kv_rs;
@@ -662,7 +699,19 @@ void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, in
   a.kv_len = T;
   a.mask = mask;
   a.mask_bs = mask_bs;
+  a.mask_hs = mask_hs;
+  a.mask_qs = mask_qs;
   launch_attend(a, s);
+}
+
+void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,
+                   const float *sin, int half, int max_pos, float *y, int64_t y_rs, int B, int S, int heads, int D,
+                   int rot, int interleaved, int32_t *err, cudaStream_t s) {
+  const int64_t items = (int64_t)B * S * heads;
+  if (items == 0) return;
+  rotary_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(x, x_rs, pos, pos_per_batch, cos, sin, half, max_pos, y,
+                                                            y_rs, B, S, heads, D, rot, interleaved, err);
+  B2M_CUDA(cudaGetLastError());
 }
 
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s) {

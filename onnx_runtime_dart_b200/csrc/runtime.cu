@@ -1352,22 +1352,25 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
 }
 
 B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
-                               int64_t kv_rs, const float *mask, int64_t mask_bs, float *out, int32_t b, int32_t s,
-                               int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale, int32_t causal) {
+                               int64_t kv_rs, const float *mask, int64_t mask_bs, int64_t mask_hs, int64_t mask_qs,
+                               float *out, int32_t b, int32_t s, int32_t t, int32_t h, int32_t kvh, int32_t head_dim,
+                               float scale, int32_t causal) {
   return guarded([&] {
     check_ctx(ctx);
     B2M_REQUIRE(b >= 0 && s >= 0 && t > 0 && h > 0 && kvh > 0 && h % kvh == 0 && head_dim > 0 && head_dim <= 256,
                 B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: bad shape arguments");
-    B2M_REQUIRE(q_rs >= (int64_t)h * head_dim && kv_rs >= (int64_t)kvh * head_dim && mask_bs >= 0,
-                B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: row strides too small");
+    B2M_REQUIRE(q_rs >= (int64_t)h * head_dim && kv_rs >= (int64_t)kvh * head_dim, B2M_ERR_INVALID_ARGUMENT,
+                "MultiHeadAttention: row strides too small");
+    B2M_REQUIRE(mask_bs >= 0 && mask_hs >= 0 && mask_qs >= 0, B2M_ERR_INVALID_ARGUMENT,
+                "MultiHeadAttention: negative mask strides");
     B2M_REQUIRE(!causal || s <= t, B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: causal needs s <= t");
     B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && out), B2M_ERR_INVALID_ARGUMENT,
                 "MultiHeadAttention: null pointer");
     DeviceGuard dg(ctx->device);
     if ((int64_t)b * s == 0) return;
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
-    launch_mha(q, k, v, q_rs, kv_rs, mask, mask_bs, out, b, s, t, h, kvh, head_dim, sc, causal ? 1 : 0,
-               ctx->dev_err, ctx->stream);
+    launch_mha(q, k, v, q_rs, kv_rs, mask, mask_bs, mask_hs, mask_qs, out, b, s, t, h, kvh, head_dim, sc,
+               causal ? 1 : 0, ctx->dev_err, ctx->stream);
   });
 }
 
@@ -1382,6 +1385,26 @@ B2M_API b2m_status b2m_dynamic_quantize_linear_dev(b2m_ctx *ctx, const float *x,
     Scratch sc(ctx, need + 256);
     launch_dynamic_quantize(x, n, y, scale, zero_point, static_cast<float *>(sc.take(need)), ctx->dev_counter,
                             ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_rotary_dev(b2m_ctx *ctx, const float *x, int64_t x_rs, const int64_t *positions,
+                                  int32_t pos_per_batch, const float *cos_cache, const float *sin_cache,
+                                  int32_t half, int32_t max_pos, float *y, int64_t y_rs, int32_t b, int32_t s,
+                                  int32_t heads, int32_t head_dim, int32_t rotary_dim, int32_t interleaved) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(b >= 0 && s >= 0 && heads > 0 && head_dim > 0 && head_dim <= 256 && half > 0 && max_pos > 0,
+                B2M_ERR_INVALID_ARGUMENT, "RotaryEmbedding: bad shape arguments");
+    B2M_REQUIRE(rotary_dim > 0 && rotary_dim % 2 == 0 && rotary_dim <= head_dim && rotary_dim / 2 <= half,
+                B2M_ERR_INVALID_ARGUMENT, "RotaryEmbedding: bad rotary_dim");
+    B2M_REQUIRE(x_rs >= (int64_t)heads * head_dim && y_rs >= (int64_t)heads * head_dim, B2M_ERR_INVALID_ARGUMENT,
+                "RotaryEmbedding: row strides too small");
+    B2M_REQUIRE((int64_t)b * s == 0 || (x && y && positions && cos_cache && sin_cache), B2M_ERR_INVALID_ARGUMENT,
+                "RotaryEmbedding: null pointer");
+    DeviceGuard dg(ctx->device);
+    launch_rotary(x, x_rs, positions, pos_per_batch ? 1 : 0, cos_cache, sin_cache, half, max_pos, y, y_rs, b, s,
+                  heads, head_dim, rotary_dim, interleaved ? 1 : 0, ctx->dev_err, ctx->stream);
   });
 }
 

@@ -130,13 +130,15 @@ def gqa(q, k, v, num_heads, kv_heads, past_k=None, past_v=None, cos=None, sin=No
     return out.transpose(0, 2, 1, 3).reshape(b, s, hid), pk, pv
 
 
-def mha(q, k, v, num_heads, kv_heads=None, mask=None, scale=None, causal=False):
-    """opFusedSDPA (lib/src/onnx_ops.dart:2106-2148) per head, as the
-    MultiHeadAttention of a BERT-style graph runs it: q [B][S][H*D], k / v
-    [B][T][KVH*D], mask None or additive [B][T] (a row per batch, broadcast over
-    heads and queries). Scores are a float32 MatMul; scale + mask, max, exp and
-    the sum run in double and the probabilities are stored float32; then the
-    float32 MatMul with V."""
+def mha(q, k, v, num_heads, kv_heads=None, mask=None, scale=None, causal=False, bias4d=None):
+    """opMultiHeadAttention (lib/src/onnx_ops.dart:2019-2098) / the scale +
+    mask + softmax of opFusedSDPA (:2106-2148) per head: q [B][S][H*D], k / v
+    [B][T][KVH*D]; mask None or additive [B][T] (a row per batch, broadcast over
+    heads and queries); bias4d None or the additive attention bias
+    [B][bias_heads][S][T], head h reading bias head h % bias_heads (:2062-2064).
+    Scores are a float32 MatMul; scale + bias, max, exp and the sum run in
+    double and the probabilities are stored float32; then the float32 MatMul
+    with V."""
     q = np.asarray(q, np.float32)
     k = np.asarray(k, np.float32)
     v = np.asarray(v, np.float32)
@@ -156,6 +158,10 @@ def mha(q, k, v, num_heads, kv_heads=None, mask=None, scale=None, causal=False):
         val = scores.astype(np.float32).astype(np.float64) * sc
         if mask is not None:
             val = val + np.asarray(mask, np.float32).astype(np.float64).reshape(b, 1, t)
+        if bias4d is not None:
+            bb = np.asarray(bias4d, np.float32)
+            val = val + bb[:, hh % bb.shape[1]].astype(np.float64)
+        val = val.astype(np.float32).astype(np.float64)  # the scores row is stored float32
         if causal:
             val = np.where(np.arange(t)[None, None, :] > np.arange(s)[None, :, None], -np.inf, val)
         e = np.exp(val - val.max(-1, keepdims=True))

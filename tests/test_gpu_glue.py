@@ -1,6 +1,9 @@
 """GPU tests of the device-resident glue ops (RMSNorm, LayerNorm, SiLU*Mul,
-GELU, Add, Gather, ArgMax, GroupQueryAttention with rotary and a KV cache)
-against the numpy restatement in oracle/glue.py, through the C ABI."""
+GELU, Add, Gather, ArgMax, RotaryEmbedding, GroupQueryAttention with rotary
+and a KV cache, MultiHeadAttention) through the C ABI: against the reference's
+own fixtures for these ops, and against the numpy restatement in
+oracle/glue.py (itself pinned to those fixtures) on larger seeded cases and on
+the BERT / decoder chains."""
 import ctypes
 
 import numpy as np
@@ -8,6 +11,8 @@ import pytest
 
 import oracle
 from oracle import glue
+from tests.conftest import assert_fixture_close, load_golden
+from tests.glue_fixtures import GLUE_CASES, run_case
 
 pytestmark = pytest.mark.gpu
 
@@ -159,6 +164,8 @@ def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
     (2, 33, 40, 2, 1, 48, "pad", 0, 0),       # head dim outside the tiled kernel's set
     (2, 1, 17, 4, 4, 64, "inf", 0, 0),        # one query, -inf masked keys
     (2, 130, 130, 8, 8, 96, None, 0, 1),      # ragged last tiles in both directions
+    (2, 70, 70, 4, 4, 64, "bias4d", 0, 0),    # attention_bias [b][h][s][t], per query row
+    (2, 9, 11, 4, 4, 48, "bias1h", 0, 0),     # attention_bias with one head, per-query-warp kernel
 ])
 def test_mha_additive_mask(ctx, b, s, t, h, kvh, d, mask_mode, causal, packed):
     rng = np.random.default_rng(b * 1000 + s * 7 + t + d)
@@ -175,7 +182,13 @@ def test_mha_additive_mask(ctx, b, s, t, h, kvh, d, mask_mode, causal, packed):
     elif mask_mode == "inf":
         mask = np.zeros((b, t), np.float32)
         mask[:, 3::4] = -np.inf
-    want = glue.mha(q, k, v, h, kvh, mask, causal=bool(causal))
+    bias4d = None
+    strides = (0 if mask_mode == "bcast" else t, 0, 0)
+    if mask_mode in ("bias4d", "bias1h"):
+        bh = h if mask_mode == "bias4d" else 1
+        bias4d = rng.standard_normal((b, bh, s, t)).astype(np.float32)
+        strides = (bh * s * t, s * t if bh > 1 else 0, t)
+    want = glue.mha(q, k, v, h, kvh, mask, causal=bool(causal), bias4d=bias4d)
     if packed:
         # One [b][s][(h + 2 kvh) d] tensor as a fused QKV projection writes it.
         assert s == t
@@ -191,17 +204,19 @@ def test_mha_additive_mask(ctx, b, s, t, h, kvh, d, mask_mode, causal, packed):
         pq, pk, pv = _p(dq), _p(dk), _p(dv)
         q_rs, kv_rs = h * d, kvh * d
     dm = _d(mask[:1] if mask_mode == "bcast" else mask) if mask is not None else None
+    if bias4d is not None:
+        dm = _d(bias4d)
     dout = torch.empty((b, s, h * d), dtype=torch.float32, device="cuda")
-    N.check(ctx.lib.b2m_mha_dev(ctx.handle, pq, pk, pv, q_rs, kv_rs, _p(dm),
-                                0 if mask_mode == "bcast" else t, _p(dout), b, s, t, h, kvh, d, 0.0, causal))
+    N.check(ctx.lib.b2m_mha_dev(ctx.handle, pq, pk, pv, q_rs, kv_rs, _p(dm), *strides, _p(dout), b, s, t, h, kvh, d,
+                                0.0, causal))
     torch.cuda.synchronize()
     _close(dout.cpu().numpy(), want, 2e-5, "mha out")
 
 
 def test_mha_rejects_bad_arguments(ctx):
-    assert ctx.lib.b2m_mha_dev(ctx.handle, None, None, None, 64, 64, None, 0, None, 1, 4, 3, 2, 2, 32, 0.0,
+    assert ctx.lib.b2m_mha_dev(ctx.handle, None, None, None, 64, 64, None, 0, 0, 0, None, 1, 4, 3, 2, 2, 32, 0.0,
                                1) == N.B2M_ERR_INVALID_ARGUMENT     # causal with s > t
-    assert ctx.lib.b2m_mha_dev(ctx.handle, None, None, None, 16, 64, None, 0, None, 1, 4, 4, 2, 2, 32, 0.0,
+    assert ctx.lib.b2m_mha_dev(ctx.handle, None, None, None, 16, 64, None, 0, 0, 0, None, 1, 4, 4, 2, 2, 32, 0.0,
                                0) == N.B2M_ERR_INVALID_ARGUMENT     # q row stride below h * head_dim
 
 
@@ -318,3 +333,99 @@ def test_tiny_bert_chain_matches_composition(ctx, mode):
     # attention / LayerNorm / GELU add float32 rounding-order differences.
     assert err <= (1e-3 if mode == "fast" else 1e-4), f"bert chain max rel err {err:.3e}"
     assert cos >= 0.99999, f"bert chain cosine {cos:.7f}"
+
+
+class _DeviceGlue:
+    """The device ops behind the fixture runner's interface (tests/glue_fixtures.py)."""
+
+    def __init__(self, ctx):
+        self.ctx, self.lib, self.h = ctx, ctx.lib, ctx.handle
+
+    def _run(self):
+        torch.cuda.synchronize()
+
+    def gelu(self, x):
+        dx = _d(x)
+        dy = torch.empty_like(dx)
+        N.check(self.lib.b2m_gelu_dev(self.h, _p(dx), _p(dy), dx.numel()))
+        self._run()
+        return dy.cpu().numpy()
+
+    def rmsnorm(self, x, gamma, eps, skip):
+        d = x.shape[-1]
+        dx, dg = _d(x), _d(np.asarray(gamma, np.float32))
+        ds = _d(skip) if skip is not None else None
+        dy, dsum = torch.empty_like(dx), torch.empty_like(dx)
+        N.check(self.lib.b2m_rmsnorm_dev(self.h, _p(dx), _p(ds), _p(dg), _p(dy), _p(dsum), dx.numel() // d, d,
+                                         ctypes.c_double(eps)))
+        self._run()
+        return dy.cpu().numpy(), (dsum.cpu().numpy() if skip is not None else None)
+
+    def argmax_last(self, x):
+        x = np.ascontiguousarray(x)
+        v = x.shape[-1]
+        dx = _d(x)
+        dout = torch.empty(x.size // v, dtype=torch.int64, device="cuda")
+        N.check(self.lib.b2m_argmax_dev(self.h, _p(dx), _p(dout), x.size // v, v))
+        self._run()
+        return dout.cpu().numpy().reshape(x.shape[:-1])
+
+    def rotary(self, x, pos, cos, sin, heads, interleaved):
+        b, s, hid = x.shape
+        dx, dp = _d(x), _d(np.asarray(pos, np.int64))
+        dc, dsn = _d(cos), _d(sin)
+        dy = torch.empty_like(dx)
+        half = cos.shape[-1]
+        hd = hid // heads
+        N.check(self.lib.b2m_rotary_dev(self.h, _p(dx), hid, _p(dp), int(np.asarray(pos).ndim == 2), _p(dc),
+                                        _p(dsn), half, cos.shape[0], _p(dy), hid, b, s, heads, hd, min(2 * half, hd),
+                                        int(interleaved)))
+        self._run()
+        return dy.cpu().numpy()
+
+    def gqa(self, q, k, v, h, kvh, pk, pv, cos, sin, scale):
+        b, s, _ = q.shape
+        d = q.shape[-1] // h
+        past = 0 if pk is None else pk.shape[2]
+        cap = past + s
+        kc = np.zeros((b, kvh, cap, d), np.float32)
+        vc = np.zeros((b, kvh, cap, d), np.float32)
+        if past:
+            kc[:, :, :past], vc[:, :, :past] = pk, pv
+        dq, dk, dv, dkc, dvc = _d(q), _d(k), _d(v), _d(kc), _d(vc)
+        dpast = _d(np.full(b, past, np.int32))
+        dc, dsn = (_d(cos), _d(sin)) if cos is not None else (None, None)
+        dout = torch.empty_like(dq)
+        half = cos.shape[-1] if cos is not None else 0
+        N.check(self.lib.b2m_gqa_dev(self.h, _p(dq), _p(dk), _p(dv), h * d, kvh * d, _p(dkc), _p(dvc), _p(dpast),
+                                     _p(dc), _p(dsn), half, 2 * half if cos is not None else 0, 0, _p(dout), b, s, h,
+                                     kvh, d, cap, ctypes.c_float(scale)))
+        self._run()
+        return dout.cpu().numpy(), dkc.cpu().numpy(), dvc.cpu().numpy()
+
+    def mha(self, q, k, v, h, bias, scale):
+        b, s, hid = q.shape
+        t = k.shape[1]
+        d = hid // h
+        dq, dk, dv = _d(q), _d(k), _d(v)
+        dm, strides = None, (0, 0, 0)
+        if bias is not None:
+            bh = bias.shape[1]
+            dm, strides = _d(bias), (bh * s * t, s * t if bh > 1 else 0, t)
+        dout = torch.empty_like(dq)
+        N.check(self.lib.b2m_mha_dev(self.h, _p(dq), _p(dk), _p(dv), hid, hid, _p(dm), *strides, _p(dout), b, s, t, h,
+                                     h, d, ctypes.c_float(scale), 0))
+        self._run()
+        return dout.cpu().numpy()
+
+
+@pytest.mark.parametrize("case", GLUE_CASES)
+def test_glue_device_matches_reference_fixture(ctx, case):
+    g = load_golden(case)
+    got = run_case(g, _DeviceGlue(ctx))
+    for name, arr in got.items():
+        want = g["expected_arrays"][name]
+        if want.dtype.kind in "iu":
+            assert np.asarray(arr).astype(np.int64).tolist() == want.tolist(), f"{case}:{name}"
+        else:
+            assert_fixture_close(arr, want, f"{case}:{name}")

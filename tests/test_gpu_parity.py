@@ -14,6 +14,7 @@ import pytest
 
 import oracle
 from tests.conftest import assert_fast_close, assert_fixture_close, golden_cases, load_golden
+from tests.glue_fixtures import GLUE_CASES
 
 pytestmark = pytest.mark.gpu
 
@@ -44,7 +45,7 @@ def bits_equal(a, b):
 # Golden fixtures through the dispatch hook
 # ---------------------------------------------------------------------------
 
-@pytest.mark.parametrize("case", [c for c in golden_cases() if not c.startswith("dynamic")])
+@pytest.mark.parametrize("case", [c for c in golden_cases() if not c.startswith("dynamic") and c not in GLUE_CASES])
 @pytest.mark.parametrize("nbits_mode", [ops.MODE_EXACT, ops.MODE_FAST])
 def test_golden_fixture_via_dispatch(ctx, case, nbits_mode):
     g = load_golden(case)

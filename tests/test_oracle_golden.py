@@ -10,7 +10,9 @@ import numpy as np
 import pytest
 
 import oracle
+from oracle import glue
 from tests.conftest import assert_fixture_close, golden_cases, load_golden
+from tests.glue_fixtures import GLUE_CASES, run_case
 
 
 def run_oracle(g):
@@ -34,7 +36,7 @@ def run_oracle(g):
     pytest.skip(f"{op} is not a MatMul-family op")
 
 
-@pytest.mark.parametrize("case", [c for c in golden_cases() if not c.startswith("dynamic")])
+@pytest.mark.parametrize("case", [c for c in golden_cases() if not c.startswith("dynamic") and c not in GLUE_CASES])
 def test_oracle_matches_reference_fixture(case):
     g = load_golden(case)
     got = run_oracle(g)
@@ -148,3 +150,43 @@ def test_dynamic_quantize_linear_edges():
     # ties go to even: 0.5 / 1 and 2.5 / 1 with scale 1
     y, s, z = oracle.dynamic_quantize_linear(np.array([0.5, 2.5, 255.0], np.float32))
     assert y.tolist() == [0, 2, 255]
+
+
+class _OracleGlue:
+    """oracle/glue.py behind the fixture runner's interface."""
+
+    @staticmethod
+    def gelu(x):
+        return glue.gelu(x)
+
+    @staticmethod
+    def rmsnorm(x, gamma, eps, skip):
+        return glue.rmsnorm(x, gamma, eps, skip=skip)
+
+    @staticmethod
+    def argmax_last(x):
+        return glue.argmax(x)
+
+    @staticmethod
+    def rotary(x, pos, cos, sin, heads, interleaved):
+        return glue.rotary(x, np.asarray(pos), cos, sin, heads, interleaved)
+
+    @staticmethod
+    def gqa(q, k, v, h, kvh, pk, pv, cos, sin, scale):
+        return glue.gqa(q, k, v, h, kvh, pk, pv, cos, sin, scale=scale or None)
+
+    @staticmethod
+    def mha(q, k, v, h, bias, scale):
+        return glue.mha(q, k, v, h, h, bias4d=bias, scale=scale or None)
+
+
+@pytest.mark.parametrize("case", GLUE_CASES)
+def test_glue_oracle_matches_reference_fixture(case):
+    g = load_golden(case)
+    got = run_case(g, _OracleGlue)
+    for name, arr in got.items():
+        want = g["expected_arrays"][name]
+        if want.dtype.kind in "iu":
+            assert np.asarray(arr).astype(np.int64).tolist() == want.tolist(), f"{case}:{name}"
+        else:
+            assert_fixture_close(arr, want, f"{case}:{name}")
