@@ -534,6 +534,17 @@ def main():
                 "decode_steps": dec["decode_steps"], "decode_ms_per_step": dec["decode_ms_per_step"],
                 "tokens_valid": dec["tokens_valid"]}
 
+    # the BERT-base fp32 chain, sequences sharded over ranks.
+    bert = run_bert(ctx, torch, stream, max(1, 32 // world), steps=5, warmup=3)
+    bert_tf = max_over_ranks(bert["forward_ms"])
+    bert_te = max_over_ranks(bert["e2e_forward_ms"])
+    bert_tok = world * bert["batch_per_gpu"] * bert["seq"]
+    bert_line = {"tokens_per_s": round(bert_tok / (bert_tf / 1e3), 1),
+                 "e2e_tokens_per_s": round(bert_tok / (bert_te / 1e3), 1),
+                 "forward_ms": bert["forward_ms"], "tflops_per_gpu": bert["tflops"],
+                 "sequences": world * bert["batch_per_gpu"], "seq": bert["seq"], "mode": bert["mode"],
+                 "finite": bert["finite"]}
+
     # End to end through the host-buffer C-ABI call (pinned host memory).
     e2e_layers = min(R, 64)
     a_h = torch.randn((1, K_DIM), dtype=torch.float32).pin_memory()
@@ -587,6 +598,7 @@ def main():
             "prefill_m512_us_per_op": round(msp * 1e3 / (max(1, args.steps // 4) * Rp), 3),
             "configs_1_2_device_us_per_op": {o["case"]: round(o["graph_us_per_call"], 3) for o in ops_lines},
             "config5_decoder": dec_line,
+            "config4_bert": bert_line,
         },
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
