@@ -44,6 +44,9 @@ void b2m_set_last_error(const std::string &msg);
 #define B2M_DEVERR_INDEX 4       // gather id / rotary position outside its table
 #define B2M_DEVERR_CACHE_FULL 5  // KV-cache append past its capacity
 
+// Device state block of a context: error word, counters (runtime.cu).
+#define B2M_DEV_STATE_BYTES 256
+
 struct b2m_ctx {
   int device = 0;
   int sm_count = 0;
@@ -63,7 +66,8 @@ struct b2m_ctx {
   size_t scratch_bytes = 0;
   // Device word that kernels with bounded spin-waits set on timeout.
   int32_t *dev_err = nullptr;
-  // Self-resetting device counter (zero between calls), inside the same block.
+  // Self-resetting device counter (zero between calls) in the same block,
+  // used by DynamicQuantizeLinear.
   uint32_t *dev_counter = nullptr;
   // Programmatic dependent launch for the decode kernels (env
   // B2M_DISABLE_PDL=1 turns it off, e.g. to compare timelines).
@@ -228,11 +232,18 @@ void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s);
 void launch_add(const float *a, const float *b, float *y, int64_t rows, int64_t D, int b_bcast, cudaStream_t s);
 void launch_gather_rows(const float *table, const int64_t *ids, float *y, int64_t rows, int64_t V, int64_t D,
                         int32_t *err, cudaStream_t s);
-void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, cudaStream_t s);
+// Row argmax in two passes; pv / pi hold rows x argmax_chunks(rows, V)
+// partial results.
+int argmax_chunks(int64_t rows, int64_t V);
+void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, float *pv, int64_t *pi, cudaStream_t s);
+// Decode calls (S == 1) split the cached keys over gqa_decode_splits(...)
+// CTAs per (kv head, sequence); split_part holds B*H*nsplit*(2 + D) floats
+// (null: no split).
+int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP);
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                cudaStream_t s);
+                float *split_part, int nsplit, cudaStream_t s);
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
                 int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
                 int D, float scale, int causal, int32_t *err, cudaStream_t s);

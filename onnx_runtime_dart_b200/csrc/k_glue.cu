@@ -14,6 +14,7 @@
 // statistics, softmax sums); elementwise math is fp32. The attention keeps its
 // K/V in a caller-owned cache [B][KVH][CAP][D] and reads the number of cached
 // positions from device memory, so a decode step replays as a CUDA graph.
+#include <algorithm>
 #include <cfloat>
 
 #include "b2m_internal.cuh"
@@ -42,6 +43,22 @@ __device__ __forceinline__ float warp_sum_f(float v) {
 // 1/sqrt(mean(s^2) + eps) with the mean accumulated in double.
 // Rows are laid out as groups of `per` rows of D (offset g*gstride + i*D for
 // row r = g*per + i); contiguous rows have per = rows, gstride = 0.
+// RMSNorm / LayerNorm, one warp per row. The reference reduces in double;
+// double arithmetic is a small fraction of the fp32 rate on this part, so the
+// row (VPL values per lane, all loads in flight together) is reduced in fp32
+// (per-lane partial sums, then a warp tree: relative error ~1e-6 for rows of
+// a few thousand) and only the per-row factor is formed in double. Outputs
+// may overwrite the input in place.
+template <int VPL>
+__device__ __forceinline__ void norm_load(const float *xr, const float *sr, int D, int lane, float (&v)[VPL]) {
+#pragma unroll
+  for (int i = 0; i < VPL; i++) {
+    const int j = lane + 32 * i;
+    v[i] = j < D ? (sr ? xr[j] + sr[j] : xr[j]) : 0.f;
+  }
+}
+
+template <int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *skip, const float *__restrict__ gamma,
                                                       float *y, float *sum_out, int64_t rows, int D, double eps,
                                                       int64_t per, int64_t gstride) {
@@ -49,44 +66,270 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
   const int64_t off = (r / per) * gstride + (r % per) * D;
-  const float *xr = x + off;
-  const float *sr = skip ? skip + off : nullptr;
-  double ss = 0.0;
-  for (int j = lane; j < D; j += 32) {
-    const float v = sr ? xr[j] + sr[j] : xr[j];
-    ss += (double)v * (double)v;
-  }
-  ss = warp_sum_d(ss);
-  const double inv = 1.0 / sqrt(ss / D + eps);
-  for (int j = lane; j < D; j += 32) {
-    const float v = sr ? xr[j] + sr[j] : xr[j];
-    if (sum_out) sum_out[off + j] = v;
-    y[off + j] = (float)((double)v * inv * (double)gamma[j]);
+  float v[VPL];
+  norm_load<VPL>(x + off, skip ? skip + off : nullptr, D, lane, v);
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; i++) ss = fmaf(v[i], v[i], ss);
+  ss = warp_sum_f(ss);
+  const float inv = (float)(1.0 / sqrt((double)ss / D + eps));
+#pragma unroll
+  for (int i = 0; i < VPL; i++) {
+    const int j = lane + 32 * i;
+    if (j < D) {
+      if (sum_out) sum_out[off + j] = v[i];
+      y[off + j] = v[i] * inv * gamma[j];
+    }
   }
 }
 
-// LayerNormalization over the last axis (mean and variance in double).
-__global__ void __launch_bounds__(256) layernorm_kernel(const float *__restrict__ x, const float *__restrict__ skip,
+template <int VPL>
+__global__ void __launch_bounds__(256) layernorm_kernel(const float *x, const float *skip,
                                                         const float *__restrict__ gamma, const float *__restrict__ beta,
                                                         float *y, float *sum_out, int64_t rows, int D, double eps) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
+  float v[VPL];
+  norm_load<VPL>(x + r * D, skip ? skip + r * D : nullptr, D, lane, v);
+  float s1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; i++) s1 += v[i];
+  const float mean = warp_sum_f(s1) / (float)D;
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < VPL; i++) {
+    const float d = lane + 32 * i < D ? v[i] - mean : 0.f;
+    s2 = fmaf(d, d, s2);
+  }
+  const float inv = (float)(1.0 / sqrt((double)warp_sum_f(s2) / D + eps));
+#pragma unroll
+  for (int i = 0; i < VPL; i++) {
+    const int j = lane + 32 * i;
+    if (j < D) {
+      if (sum_out) sum_out[r * D + j] = v[i];
+      y[r * D + j] = (v[i] - mean) * inv * gamma[j] + (beta ? beta[j] : 0.f);
+    }
+  }
+}
+
+// Warp per row with float4 loads (D % 4 == 0, 16-byte aligned rows): lane
+// takes float4 chunks lane + 32 i. Half the load instructions of the scalar
+// form and twice the bytes per request (BERT LayerNorm 4096 x 768: 6.5 us
+// against 12 us).
+template <int V4, bool LN>
+__global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const float *skip,
+                                                         const float *__restrict__ gamma,
+                                                         const float *__restrict__ beta, float *y, float *sum_out,
+                                                         int64_t rows, int D, double eps, int64_t per,
+                                                         int64_t gstride) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  const int64_t off = (r / per) * gstride + (r % per) * D;
+  const int d4 = D >> 2;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + off);
+  const float4 *sr = skip ? reinterpret_cast<const float4 *>(skip + off) : nullptr;
+  float4 v[V4];
+#pragma unroll
+  for (int i = 0; i < V4; i++) {
+    const int j = lane + 32 * i;
+    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < d4) {
+      v[i] = xr[j];
+      if (sr) {
+        const float4 t = sr[j];
+        v[i].x += t.x, v[i].y += t.y, v[i].z += t.z, v[i].w += t.w;
+      }
+    }
+  }
+  float mean = 0.f;
+  if (LN) {
+    float s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < V4; i++) s1 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    mean = warp_sum_f(s1) / (float)D;
+  }
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < V4; i++)
+    if (lane + 32 * i < d4) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      s2 = fmaf(a, a, fmaf(b, b, fmaf(c, c, fmaf(d, d, s2))));
+    }
+  const float inv = (float)(1.0 / sqrt((double)warp_sum_f(s2) / D + eps));
+  const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+  const float4 *b4 = beta ? reinterpret_cast<const float4 *>(beta) : nullptr;
+#pragma unroll
+  for (int i = 0; i < V4; i++) {
+    const int j = lane + 32 * i;
+    if (j < d4) {
+      if (sum_out) reinterpret_cast<float4 *>(sum_out + off)[j] = v[i];
+      const float4 g = g4[j];
+      const float4 bb = b4 ? b4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4 *>(y + off)[j] =
+          make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
+                      (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
+    }
+  }
+}
+
+// One CTA per row for few rows (a decode step's 64 tokens): float4 loads
+// spread over up to 256 threads instead of one warp walking the row, which
+// is what a handful of rows on a handful of SMs needs (64 x 1024: 1.7 us
+// against 8 us warp-per-row). Rows of D floats at offsets
+// (r / per) * gstride + (r % per) * D, D % 4 == 0 and 16-byte aligned
+// operands; NV4 float4 per thread (D <= 1024 * NV4).
+template <int NV4, bool LN>
+__global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const float *skip,
+                                                           const float *__restrict__ gamma,
+                                                           const float *__restrict__ beta, float *y, float *sum_out,
+                                                           int D, double eps, int64_t per, int64_t gstride) {
+  const int64_t r = blockIdx.x;
+  const int64_t off = (r / per) * gstride + (r % per) * D;
+  const int d4 = D >> 2, tid = threadIdx.x, nt = blockDim.x;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + off);
+  const float4 *sr = skip ? reinterpret_cast<const float4 *>(skip + off) : nullptr;
+  float4 v[NV4];
+#pragma unroll
+  for (int i = 0; i < NV4; i++) {
+    const int j = tid + nt * i;
+    v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (j < d4) {
+      v[i] = xr[j];
+      if (sr) {
+        const float4 t = sr[j];
+        v[i].x += t.x, v[i].y += t.y, v[i].z += t.z, v[i].w += t.w;
+      }
+    }
+  }
+  __shared__ float red[8];
+  auto block_sum = [&](float t) {
+    t = warp_sum_f(t);
+    __syncthreads();
+    if ((tid & 31) == 0) red[tid >> 5] = t;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < (nt + 31) / 32; w++) tot += red[w];
+    return tot;
+  };
+  float mean = 0.f;
+  if (LN) {
+    float s1 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV4; i++) s1 += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+    mean = block_sum(s1) / (float)D;
+  }
+  float s2 = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV4; i++)
+    if (tid + nt * i < d4) {
+      const float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+      s2 = fmaf(a, a, fmaf(b, b, fmaf(c, c, fmaf(d, d, s2))));
+    }
+  const float inv = (float)(1.0 / sqrt((double)block_sum(s2) / D + eps));
+  const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+  const float4 *b4 = beta ? reinterpret_cast<const float4 *>(beta) : nullptr;
+#pragma unroll
+  for (int i = 0; i < NV4; i++) {
+    const int j = tid + nt * i;
+    if (j < d4) {
+      if (sum_out) reinterpret_cast<float4 *>(sum_out + off)[j] = v[i];
+      const float4 g = g4[j];
+      const float4 bb = b4 ? b4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      reinterpret_cast<float4 *>(y + off)[j] =
+          make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
+                      (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
+    }
+  }
+}
+
+// Launches the CTA-per-row variant when the rows are few and the layout
+// allows float4; returns false otherwise.
+template <bool LN>
+bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
+                          float *sum_out, int64_t rows, int D, double eps, int64_t per, int64_t gstride,
+                          cudaStream_t s) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (D % 4 || gstride % 4 || D > 4096 || !al(x) || !al(skip) || !al(gamma) || !al(beta) || !al(y) ||
+      !al(sum_out))
+    return false;
+  if (rows > 4 * (int64_t)b2m::device_sm_count() || rows > 2147483647) {
+    // Many rows: a warp per row, float4 loads.
+    const unsigned g = (unsigned)((rows + 7) / 8);
+    const int v4 = (D / 4 + 31) / 32;
+#define B2M_NW4(N) \
+  norm_warp4_kernel<N, LN><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps, per, gstride)
+    if (v4 <= 1) B2M_NW4(1);
+    else if (v4 <= 2) B2M_NW4(2);
+    else if (v4 <= 4) B2M_NW4(4);
+    else if (v4 <= 6) B2M_NW4(6);
+    else if (v4 <= 8) B2M_NW4(8);
+    else if (v4 <= 16) B2M_NW4(16);
+    else return false;
+#undef B2M_NW4
+    B2M_CUDA(cudaGetLastError());
+    return true;
+  }
+  const int d4 = D / 4;
+  const int nt = std::min(256, (d4 + 31) / 32 * 32);
+  const int nv4 = (d4 + nt - 1) / nt;
+  const unsigned g = (unsigned)rows;
+#define B2M_NRC(N) norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride)
+  if (nv4 <= 1) B2M_NRC(1);
+  else if (nv4 <= 2) B2M_NRC(2);
+  else B2M_NRC(4);
+#undef B2M_NRC
+  B2M_CUDA(cudaGetLastError());
+  return true;
+}
+
+// Rows longer than 32 x 64 values: the same arithmetic streamed from memory.
+__global__ void __launch_bounds__(256) rmsnorm_long_kernel(const float *x, const float *skip,
+                                                           const float *__restrict__ gamma, float *y, float *sum_out,
+                                                           int64_t rows, int D, double eps, int64_t per,
+                                                           int64_t gstride) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  const int64_t off = (r / per) * gstride + (r % per) * D;
+  const float *xr = x + off;
+  const float *sr = skip ? skip + off : nullptr;
+  float ss = 0.f;
+  for (int j = lane; j < D; j += 32) {
+    const float v = sr ? xr[j] + sr[j] : xr[j];
+    ss = fmaf(v, v, ss);
+  }
+  const float inv = (float)(1.0 / sqrt((double)warp_sum_f(ss) / D + eps));
+  for (int j = lane; j < D; j += 32) {
+    const float v = sr ? xr[j] + sr[j] : xr[j];
+    if (sum_out) sum_out[off + j] = v;
+    y[off + j] = v * inv * gamma[j];
+  }
+}
+
+__global__ void __launch_bounds__(256) layernorm_long_kernel(const float *x, const float *skip,
+                                                             const float *__restrict__ gamma,
+                                                             const float *__restrict__ beta, float *y, float *sum_out,
+                                                             int64_t rows, int D, double eps) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
   const float *xr = x + r * D;
   const float *sr = skip ? skip + r * D : nullptr;
-  double s1 = 0.0;
-  for (int j = lane; j < D; j += 32) s1 += (double)(sr ? xr[j] + sr[j] : xr[j]);
-  const double mean = warp_sum_d(s1) / D;
-  double s2 = 0.0;
+  float s1 = 0.f;
+  for (int j = lane; j < D; j += 32) s1 += sr ? xr[j] + sr[j] : xr[j];
+  const float mean = warp_sum_f(s1) / (float)D;
+  float s2 = 0.f;
   for (int j = lane; j < D; j += 32) {
-    const double d = (double)(sr ? xr[j] + sr[j] : xr[j]) - mean;
-    s2 += d * d;
+    const float d = (sr ? xr[j] + sr[j] : xr[j]) - mean;
+    s2 = fmaf(d, d, s2);
   }
-  const double inv = 1.0 / sqrt(warp_sum_d(s2) / D + eps);
+  const float inv = (float)(1.0 / sqrt((double)warp_sum_f(s2) / D + eps));
   for (int j = lane; j < D; j += 32) {
     const float v = sr ? xr[j] + sr[j] : xr[j];
     if (sum_out) sum_out[r * D + j] = v;
-    y[r * D + j] = (float)(((double)v - mean) * inv * (double)gamma[j] + (beta ? (double)beta[j] : 0.0));
+    y[r * D + j] = (v - mean) * inv * gamma[j] + (beta ? beta[j] : 0.f);
   }
 }
 
@@ -131,35 +374,93 @@ __global__ void gather_rows_kernel(const float *__restrict__ table, const int64_
 }
 
 // Row argmax (first maximum wins; NaN compares false). One CTA per row.
-__global__ void __launch_bounds__(512) argmax_kernel(const float *__restrict__ x, int64_t *out, int64_t V) {
-  const int64_t r = blockIdx.x;
+__device__ __forceinline__ bool argmax_better(float v, int64_t i, float bv, int64_t bi) {
+  return v > bv || (v == bv && i < bi);
+}
+
+// Partial argmax of one chunk of a row: CTA (chunk c, row r) scans
+// [c*chunk, (c+1)*chunk) with float4 loads where the row allows, and writes
+// (value, index) of its best element (the smallest index among equal maxima;
+// NaN never wins; nothing above -FLT_MAX leaves index V).
+__global__ void __launch_bounds__(256) argmax_partial_kernel(const float *__restrict__ x, int64_t V, int64_t chunk,
+                                                             float *pv, int64_t *pi) {
+  const int64_t r = blockIdx.y, c = blockIdx.x;
   const float *xr = x + r * V;
+  const int64_t j0 = c * chunk, j1 = min(V, j0 + chunk);
   float best = -FLT_MAX;
   int64_t bi = V;
-  for (int64_t j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = xr[j];
-    if (v > best || (bi == V && v == best)) {
-      best = v;
-      bi = j;
+  const bool vec = ((V & 3) == 0) && ((reinterpret_cast<uintptr_t>(x) & 15) == 0) && ((chunk & 3) == 0);
+  if (vec) {
+    for (int64_t j = j0 + 4 * (int64_t)threadIdx.x; j < j1; j += 4 * 256) {
+      const float4 q = *reinterpret_cast<const float4 *>(xr + j);
+      const float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+        if (argmax_better(e[u], j + u, best, bi)) {
+          best = e[u];
+          bi = j + u;
+        }
     }
-  }
-  __shared__ float sv[512];
-  __shared__ int64_t si[512];
-  sv[threadIdx.x] = best;
-  si[threadIdx.x] = bi;
-  __syncthreads();
-  for (int s = blockDim.x / 2; s > 0; s >>= 1) {
-    if (threadIdx.x < s) {
-      const float ov = sv[threadIdx.x + s];
-      const int64_t oi = si[threadIdx.x + s];
-      if (ov > sv[threadIdx.x] || (ov == sv[threadIdx.x] && oi < si[threadIdx.x])) {
-        sv[threadIdx.x] = ov;
-        si[threadIdx.x] = oi;
+  } else {
+    for (int64_t j = j0 + threadIdx.x; j < j1; j += 256) {
+      const float v = xr[j];
+      if (argmax_better(v, j, best, bi)) {
+        best = v;
+        bi = j;
       }
     }
-    __syncthreads();
   }
-  if (threadIdx.x == 0) out[r] = si[0] < V ? si[0] : 0;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (argmax_better(ov, oi, best, bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  __shared__ float sv[8];
+  __shared__ int64_t si[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) {
+    sv[warp] = best;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < 8; w++)
+      if (argmax_better(sv[w], si[w], best, bi)) {
+        best = sv[w];
+        bi = si[w];
+      }
+    pv[r * gridDim.x + c] = best;
+    pi[r * gridDim.x + c] = bi;
+  }
+}
+
+// One warp per row combines the chunk results (order-independent rule).
+__global__ void __launch_bounds__(256) argmax_final_kernel(const float *pv, const int64_t *pi, int nchunk,
+                                                           int64_t *out, int64_t rows, int64_t V) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + warp;
+  if (r >= rows) return;
+  float best = -FLT_MAX;
+  int64_t bi = V;
+  for (int c = lane; c < nchunk; c += 32)
+    if (argmax_better(pv[r * nchunk + c], pi[r * nchunk + c], best, bi)) {
+      best = pv[r * nchunk + c];
+      bi = pi[r * nchunk + c];
+    }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, off);
+    const int64_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (argmax_better(ov, oi, best, bi)) {
+      best = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) out[r] = bi < V ? bi : 0;
 }
 
 // Rotary of one head vector in place (non-interleaved: pairs (i, i + half);
@@ -455,19 +756,53 @@ __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
   }
 }
 
-// Single-token attention (decode): CTA = (kv head, batch), 256 threads, the
-// G query heads of the group together so each cached K/V row is read once.
-// Warp w takes keys w*32 + 256*i + lane: a lane computes the G scores of its
-// key, the warp updates its online-softmax state, then the lanes switch to
-// head-dim columns for P.V (the key's weight broadcast by shuffle). The 8
-// warp states are merged in shared memory in fixed order.
+// Sums eight values over the warp and leaves all eight totals in every lane:
+// three reduce-scatter rounds (4 + 2 + 1 shuffles) leave value k summed over
+// lanes differing in bits 4..2 in lanes whose bits 4..2 spell k, two rounds
+// finish the sum, eight shuffles broadcast. 17 shuffles instead of 40.
+__device__ __forceinline__ void warp_allreduce8(float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  float t4[4], t2[2];
+  const bool h16 = lane & 16, h8 = lane & 8, h4 = lane & 4;
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    const float send = h16 ? v[i] : v[i + 4], keep = h16 ? v[i + 4] : v[i];
+    t4[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; i++) {
+    const float send = h8 ? t4[i] : t4[i + 2], keep = h8 ? t4[i + 2] : t4[i];
+    t2[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  float t1;
+  {
+    const float send = h4 ? t2[0] : t2[1], keep = h4 ? t2[1] : t2[0];
+    t1 = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 2);
+  t1 += __shfl_xor_sync(0xffffffffu, t1, 1);
+#pragma unroll
+  for (int k = 0; k < 8; k++) v[k] = __shfl_sync(0xffffffffu, t1, k << 2);
+}
+
+// Single-token attention (decode): CTA = (kv head, sequence, key split),
+// 256 threads, the G query heads of the group together so each cached K/V
+// row is read once. A warp takes 8/G keys per step: every lane loads its
+// D/32 values of each K and V row (512-byte coalesced rows for D = 128, all
+// the step's loads in flight together), the 8 partial dot products are
+// reduced together, and the warp's online-softmax state is updated. The 8
+// warp states merge in shared memory in fixed order; with key splits the
+// split states go to pm / pl / po and gqa_decode_combine_kernel merges them.
 template <int D, int G>
-__global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a) {
-  constexpr int CPL = D / 32;
+__global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float *pm, float *pl, float *po) {
+  constexpr int VPD = D / 32, KB = 8 / G;
+  static_assert(D % 32 == 0 && D <= 128 && KB * G == 8, "decode kernel shape");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kvh = blockIdx.x, b = blockIdx.y;
+  const int kvh = blockIdx.x, b = blockIdx.y, sp = blockIdx.z, nsplit = gridDim.z;
   const int past = a.past[b];
   const int nkeys = min(past + 1, a.CAP);
+  const int chunk = (nkeys + nsplit - 1) / nsplit;
+  const int jbeg = sp * chunk, jend = min(nkeys, jbeg + chunk);
   __shared__ __align__(16) float qs[G][D];
   __shared__ float wm[8][G], wl[8][G];
   __shared__ float wo[8][G][D];
@@ -488,58 +823,70 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a) {
     }
   }
   __syncthreads();
-  const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
-  const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
-  float m[G], l[G], o[G][CPL];
+  float q[G][VPD];
+#pragma unroll
+  for (int g = 0; g < G; g++)
+#pragma unroll
+    for (int c = 0; c < VPD; c++) q[g][c] = qs[g][lane * VPD + c];
+  const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs + lane * VPD;
+  const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs + lane * VPD;
+  float m[G], l[G], o[G][VPD];
 #pragma unroll
   for (int g = 0; g < G; g++) {
     m[g] = -INFINITY;
     l[g] = 0.f;
 #pragma unroll
-    for (int c = 0; c < CPL; c++) o[g][c] = 0.f;
+    for (int c = 0; c < VPD; c++) o[g][c] = 0.f;
   }
-  for (int c0 = warp * 32; c0 < nkeys; c0 += 256) {
-    const int j = c0 + lane;
-    const bool valid = j < nkeys;
-    float sc[G];
+  for (int j0 = jbeg + warp * KB; j0 < jend; j0 += 8 * KB) {
+    float kr[KB][VPD], vr[KB][VPD];
 #pragma unroll
-    for (int g = 0; g < G; g++) sc[g] = 0.f;
-    if (valid) {
-      const float4 *kr = reinterpret_cast<const float4 *>(kc + (int64_t)j * D);
-#pragma unroll 8
-      for (int d4 = 0; d4 < D / 4; d4++) {
-        const float4 kv = kr[d4];
+    for (int kb = 0; kb < KB; kb++) {
+      const bool ok = j0 + kb < jend;
+      const float *kp = kc + (int64_t)(j0 + kb) * a.kc_rs, *vp = vc + (int64_t)(j0 + kb) * a.kc_rs;
+      if constexpr (VPD == 4) {
+        const float4 k4 = ok ? *reinterpret_cast<const float4 *>(kp) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4 v4 = ok ? *reinterpret_cast<const float4 *>(vp) : make_float4(0.f, 0.f, 0.f, 0.f);
+        kr[kb][0] = k4.x, kr[kb][1] = k4.y, kr[kb][2] = k4.z, kr[kb][3] = k4.w;
+        vr[kb][0] = v4.x, vr[kb][1] = v4.y, vr[kb][2] = v4.z, vr[kb][3] = v4.w;
+      } else {
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-          const float4 qv = *reinterpret_cast<const float4 *>(&qs[g][d4 * 4]);
-          sc[g] = fmaf(qv.x, kv.x, fmaf(qv.y, kv.y, fmaf(qv.z, kv.z, fmaf(qv.w, kv.w, sc[g]))));
+        for (int c = 0; c < VPD; c++) {
+          kr[kb][c] = ok ? kp[c] : 0.f;
+          vr[kb][c] = ok ? vp[c] : 0.f;
         }
       }
     }
-    float p[G];
+    float s[8];
 #pragma unroll
-    for (int g = 0; g < G; g++) {
-      const float v = valid ? sc[g] : -INFINITY;
-      const float mn = fmaxf(m[g], warp_max_f(v));
-      const float corr = __expf(m[g] - mn);
-      p[g] = valid ? __expf(v - mn) : 0.f;
-      l[g] = l[g] * corr + warp_sum_f(p[g]);
-      m[g] = mn;
-#pragma unroll
-      for (int c = 0; c < CPL; c++) o[g][c] *= corr;
-    }
-    const int nj = min(32, nkeys - c0);
-    for (int jj = 0; jj < nj; jj++) {
-      const float *vr = vc + (int64_t)(c0 + jj) * D + lane * CPL;
-      float vv[CPL];
-#pragma unroll
-      for (int c = 0; c < CPL; c++) vv[c] = vr[c];
+    for (int kb = 0; kb < KB; kb++)
 #pragma unroll
       for (int g = 0; g < G; g++) {
-        const float pj = __shfl_sync(0xffffffffu, p[g], jj);
+        float t = 0.f;
 #pragma unroll
-        for (int c = 0; c < CPL; c++) o[g][c] = fmaf(pj, vv[c], o[g][c]);
+        for (int c = 0; c < VPD; c++) t = fmaf(q[g][c], kr[kb][c], t);
+        s[kb * G + g] = t;
       }
+    warp_allreduce8(s);
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+      float mx = m[g];
+#pragma unroll
+      for (int kb = 0; kb < KB; kb++)
+        if (j0 + kb < jend) mx = fmaxf(mx, s[kb * G + g]);
+      const float corr = __expf(m[g] - mx);
+      float psum = 0.f;
+#pragma unroll
+      for (int c = 0; c < VPD; c++) o[g][c] *= corr;
+#pragma unroll
+      for (int kb = 0; kb < KB; kb++) {
+        const float p = j0 + kb < jend ? __expf(s[kb * G + g] - mx) : 0.f;
+        psum += p;
+#pragma unroll
+        for (int c = 0; c < VPD; c++) o[g][c] = fmaf(p, vr[kb][c], o[g][c]);
+      }
+      l[g] = l[g] * corr + psum;
+      m[g] = mx;
     }
   }
 #pragma unroll
@@ -549,7 +896,7 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a) {
       wl[warp][g] = l[g];
     }
 #pragma unroll
-    for (int c = 0; c < CPL; c++) wo[warp][g][lane * CPL + c] = o[g][c];
+    for (int c = 0; c < VPD; c++) wo[warp][g][lane * VPD + c] = o[g][c];
   }
   __syncthreads();
   for (int i = threadIdx.x; i < G * D; i += 256) {
@@ -562,7 +909,35 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a) {
       L += wl[w][g] * f;
       O += wo[w][g][d] * f;
     }
-    a.out[(int64_t)b * (int64_t)a.H * D + (kvh * G + g) * D + d] = O / L;
+    const int h = kvh * G + g;
+    if (nsplit == 1) {
+      a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = O / L;
+    } else {
+      const int64_t slot = ((int64_t)b * a.H + h) * nsplit + sp;
+      if (d == 0) {
+        pm[slot] = M;
+        pl[slot] = L;
+      }
+      po[slot * D + d] = O;
+    }
+  }
+}
+
+// Merges the key-split states of gqa_decode_kernel in split order.
+__global__ void gqa_decode_combine_kernel(const float *pm, const float *pl, const float *po, float *out, int H, int D,
+                                          int nsplit) {
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int64_t base = ((int64_t)b * H + h) * nsplit;
+  float M = -INFINITY;
+  for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, pm[base + sp]);
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float L = 0.f, O = 0.f;
+    for (int sp = 0; sp < nsplit; sp++) {
+      const float f = pm[base + sp] == -INFINITY ? 0.f : __expf(pm[base + sp] - M);
+      L += pl[base + sp] * f;
+      O += po[(base + sp) * D + d] * f;
+    }
+    out[((int64_t)b * H + h) * D + d] = O / L;
   }
 }
 
@@ -581,14 +956,36 @@ unsigned grid_for(int64_t n, int block) {
 void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
                     int D, double eps, int64_t per, int64_t gstride, cudaStream_t s) {
   if (rows <= 0) return;
-  rmsnorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride);
+  if (launch_norm_rows_cta<false>(x, skip, gamma, nullptr, y, sum_out, rows, D, eps, per, gstride, s)) return;
+  const unsigned g = (unsigned)((rows + 7) / 8);
+  const int vpl = (D + 31) / 32;
+#define B2M_RMS(V) rmsnorm_kernel<V><<<g, 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride)
+  if (vpl <= 4) B2M_RMS(4);
+  else if (vpl <= 8) B2M_RMS(8);
+  else if (vpl <= 16) B2M_RMS(16);
+  else if (vpl <= 24) B2M_RMS(24);
+  else if (vpl <= 32) B2M_RMS(32);
+  else if (vpl <= 64) B2M_RMS(64);
+  else rmsnorm_long_kernel<<<g, 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride);
+#undef B2M_RMS
   B2M_CUDA(cudaGetLastError());
 }
 
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                       float *sum_out, int64_t rows, int D, double eps, cudaStream_t s) {
   if (rows <= 0) return;
-  layernorm_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps);
+  if (launch_norm_rows_cta<true>(x, skip, gamma, beta, y, sum_out, rows, D, eps, rows, 0, s)) return;
+  const unsigned g = (unsigned)((rows + 7) / 8);
+  const int vpl = (D + 31) / 32;
+#define B2M_LN(V) layernorm_kernel<V><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps)
+  if (vpl <= 4) B2M_LN(4);
+  else if (vpl <= 8) B2M_LN(8);
+  else if (vpl <= 16) B2M_LN(16);
+  else if (vpl <= 24) B2M_LN(24);
+  else if (vpl <= 32) B2M_LN(32);
+  else if (vpl <= 64) B2M_LN(64);
+  else layernorm_long_kernel<<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps);
+#undef B2M_LN
   B2M_CUDA(cudaGetLastError());
 }
 
@@ -618,9 +1015,19 @@ void launch_gather_rows(const float *table, const int64_t *ids, float *y, int64_
   B2M_CUDA(cudaGetLastError());
 }
 
-void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, cudaStream_t s) {
+int argmax_chunks(int64_t rows, int64_t V) {
+  const int64_t want = (4 * (int64_t)b2m::device_sm_count() + rows - 1) / std::max<int64_t>(rows, 1);
+  const int64_t by_len = (V + 4095) / 4096;
+  return (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(want, by_len), 1024));
+}
+
+void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, float *pv, int64_t *pi, cudaStream_t s) {
   if (rows <= 0) return;
-  argmax_kernel<<<(unsigned)rows, 512, 0, s>>>(x, out, V);
+  const int nchunk = argmax_chunks(rows, V);
+  const int64_t chunk = ((V + nchunk - 1) / nchunk + 3) / 4 * 4;
+  argmax_partial_kernel<<<dim3((unsigned)nchunk, (unsigned)rows), 256, 0, s>>>(x, V, chunk, pv, pi);
+  B2M_CUDA(cudaGetLastError());
+  argmax_final_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(pv, pi, nchunk, out, rows, V);
   B2M_CUDA(cudaGetLastError());
 }
 
@@ -628,18 +1035,31 @@ void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, cudaSt
 // `a`: the single-token decode kernel for cached causal calls of one query,
 // the tiled kernel for head dims 32..128 in steps of 32, the per-query-warp
 // kernel otherwise.
-static void launch_attend(const GqaArgs &a, cudaStream_t s) {
+static bool decode_shape(const GqaArgs &a) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
-  if (a.S == 1 && a.past && a.causal && !a.mask && dok && (G == 1 || G == 2 || G == 4 || G == 8)) {
-    dim3 grid((unsigned)a.KVH, (unsigned)a.B);
+  return a.S == 1 && a.past && a.causal && !a.mask && dok && (G == 1 || G == 2 || G == 4 || G == 8);
+}
+
+static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaStream_t s) {
+  const int D = a.D, G = a.H / a.KVH;
+  const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
+  if (decode_shape(a)) {
+    if (!split_part) nsplit = 1;
+    dim3 grid((unsigned)a.KVH, (unsigned)a.B, (unsigned)nsplit);
+    const int64_t slots = (int64_t)a.B * a.H * nsplit;
+    float *pm = split_part, *pl = pm ? pm + slots : nullptr, *po = pm ? pl + slots : nullptr;
 #define B2M_DEC(DD, GG) \
-  if (D == DD && G == GG) gqa_decode_kernel<DD, GG><<<grid, 256, 0, s>>>(a);
+  if (D == DD && G == GG) gqa_decode_kernel<DD, GG><<<grid, 256, 0, s>>>(a, pm, pl, po);
     B2M_DEC(32, 1) B2M_DEC(32, 2) B2M_DEC(32, 4) B2M_DEC(32, 8)
     B2M_DEC(64, 1) B2M_DEC(64, 2) B2M_DEC(64, 4) B2M_DEC(64, 8)
     B2M_DEC(96, 1) B2M_DEC(96, 2) B2M_DEC(96, 4) B2M_DEC(96, 8)
     B2M_DEC(128, 1) B2M_DEC(128, 2) B2M_DEC(128, 4) B2M_DEC(128, 8)
 #undef B2M_DEC
+    B2M_CUDA(cudaGetLastError());
+    if (nsplit > 1) {
+      gqa_decode_combine_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, 0, s>>>(pm, pl, po, a.out, a.H, D, nsplit);
+    }
   } else if (dok) {
     dim3 grid((unsigned)((a.S + 63) / 64), (unsigned)a.H, (unsigned)a.B);
     const int smem = (2 * D * 68 + 64 * D + 64 * 68) * 4;
@@ -668,10 +1088,18 @@ static void launch_attend(const GqaArgs &a, cudaStream_t s) {
   B2M_CUDA(cudaGetLastError());
 }
 
+// Key splits of the decode kernel: enough CTAs for two per SM, at least 128
+// cache positions per split. Partial-state floats: B*H*nsplit*(2 + D).
+int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP) {
+  if (S != 1 || B * KVH <= 0) return 1;
+  const int want = (2 * b2m::device_sm_count() + B * KVH - 1) / (B * KVH);
+  return std::max(1, std::min(want, (CAP + 127) / 128));
+}
+
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                cudaStream_t s) {
+                float *split_part, int nsplit, cudaStream_t s) {
   GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
             B, S, H, KVH, D, CAP, scale, err};
   a.kc_rs = D;
@@ -684,7 +1112,7 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
   const int64_t items = (int64_t)B * S * KVH;
   gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
   B2M_CUDA(cudaGetLastError());
-  launch_attend(a, s);
+  launch_attend(a, split_part, nsplit, s);
 }
 
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
@@ -701,7 +1129,7 @@ void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, in
   a.mask_bs = mask_bs;
   a.mask_hs = mask_hs;
   a.mask_qs = mask_qs;
-  launch_attend(a, s);
+  launch_attend(a, nullptr, 1, s);
 }
 
 void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,

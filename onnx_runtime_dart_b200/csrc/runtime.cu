@@ -85,7 +85,8 @@ void check_device_error(b2m_ctx *ctx) {
   B2M_CUDA(cudaMemcpyAsync(&e, ctx->dev_err, sizeof(e), cudaMemcpyDeviceToHost, ctx->stream));
   B2M_CUDA(cudaStreamSynchronize(ctx->stream));
   if (e != B2M_DEVERR_NONE) {
-    B2M_CUDA(cudaMemsetAsync(ctx->dev_err, 0, sizeof(int32_t), ctx->stream));
+    // An aborted kernel may leave counters mid-count: clear the whole block.
+    B2M_CUDA(cudaMemsetAsync(ctx->dev_err, 0, B2M_DEV_STATE_BYTES, ctx->stream));
     b2m_throw(B2M_ERR_TIMEOUT, "a bounded device-side wait timed out (code " + std::to_string(e) + ")");
   }
 }
@@ -546,6 +547,7 @@ void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_w
       launch_nbits_smallm(p, ctx->stream, ctx->pdl);
     } else if (nbits_tc_supported(w->nb, m, K, N)) {
       __half *a16 = static_cast<__half *>(sc.take((size_t)(m * nbits_tc_k8(K) * 2)));
+
       launch_nbits_tc(p, a16, ctx->stream);
     } else {
       launch_nbits_simt(p, ctx->stream);
@@ -640,9 +642,10 @@ B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx) {
     B2M_CUDA(cudaEventCreate(&ctx->ev1));
     // One zeroed block: the error word, then counters that kernels reset
     // themselves after use (the DynamicQuantizeLinear block counter).
-    B2M_CUDA(cudaMalloc(&ctx->dev_err, 256));
-    B2M_CUDA(cudaMemset(ctx->dev_err, 0, 256));
+    B2M_CUDA(cudaMalloc(&ctx->dev_err, B2M_DEV_STATE_BYTES));
+    B2M_CUDA(cudaMemset(ctx->dev_err, 0, B2M_DEV_STATE_BYTES));
     ctx->dev_counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(ctx->dev_err) + 128);
+
     const char *no_pdl = std::getenv("B2M_DISABLE_PDL");
     ctx->pdl = !(no_pdl && no_pdl[0] == '1');
     *out_ctx = ctx;
@@ -1322,7 +1325,12 @@ B2M_API b2m_status b2m_argmax_dev(b2m_ctx *ctx, const float *x, int64_t *out, in
     check_ctx(ctx);
     B2M_REQUIRE(rows >= 0 && v > 0 && (rows == 0 || (x && out)), B2M_ERR_INVALID_ARGUMENT, "ArgMax: bad arguments");
     DeviceGuard dg(ctx->device);
-    launch_argmax(x, out, rows, v, ctx->stream);
+    if (rows == 0) return;
+    const size_t np = (size_t)(rows * argmax_chunks(rows, v));
+    Scratch sc(ctx, np * 12 + 512);
+    float *pv = static_cast<float *>(sc.take(np * 4));
+    int64_t *pi = static_cast<int64_t *>(sc.take(np * 8));
+    launch_argmax(x, out, rows, v, pv, pi, ctx->stream);
   });
 }
 
@@ -1346,8 +1354,12 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
     DeviceGuard dg(ctx->device);
     if ((int64_t)b * s == 0) return;
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
+    const int nsplit = gqa_decode_splits(b, s, h, kvh, head_dim, cap);
+    float *part = nullptr;
+    Scratch scr(ctx, nsplit > 1 ? (size_t)b * h * nsplit * (2 + head_dim) * 4 + 256 : 0);
+    if (nsplit > 1) part = static_cast<float *>(scr.take((size_t)b * h * nsplit * (2 + head_dim) * 4));
     launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
-               interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, ctx->stream);
+               interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit, ctx->stream);
   });
 }
 

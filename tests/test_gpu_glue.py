@@ -128,7 +128,9 @@ def test_elementwise_gather_argmax(ctx):
 @pytest.mark.parametrize("b,s,past,h,kvh,d,interleaved", [(2, 5, 0, 4, 2, 32, 0), (3, 1, 9, 16, 8, 128, 0),
                                                            (1, 7, 3, 6, 3, 64, 1), (2, 40, 0, 8, 8, 96, 0),
                                                            (2, 130, 20, 4, 2, 128, 0), (1, 1, 300, 16, 2, 128, 0),
-                                                           (2, 1, 0, 4, 4, 64, 1)])
+                                                           (2, 1, 0, 4, 4, 64, 1), (8, 1, 576, 16, 8, 128, 0),
+                                                           (2, 1, 1000, 16, 4, 32, 0), (3, 1, 700, 8, 8, 96, 1),
+                                                           (64, 1, 40, 16, 8, 128, 0)])
 def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
     # Prefill-shaped and decode-shaped calls; `past` positions already cached.
     rng = np.random.default_rng(b * 100 + s + past + d)
@@ -429,3 +431,24 @@ def test_glue_device_matches_reference_fixture(ctx, case):
             assert np.asarray(arr).astype(np.int64).tolist() == want.tolist(), f"{case}:{name}"
         else:
             assert_fixture_close(arr, want, f"{case}:{name}")
+
+
+@pytest.mark.parametrize("rows,v", [(64, 151936), (3, 1000), (1, 7), (130, 4099)])
+def test_argmax_chunked_ties_nan(ctx, rows, v):
+    # Two-pass argmax over row chunks: the smallest index among equal maxima
+    # wins across chunk boundaries, NaN never wins, an all -inf row gives 0.
+    rng = np.random.default_rng(rows + v)
+    x = rng.standard_normal((rows, v)).astype(np.float32)
+    x[0, [v // 3, v - 1, 5 % v]] = 50.0                     # ties in different chunks
+    if rows > 1:
+        x[1] = -np.inf
+    if rows > 2:
+        x[2, ::3] = np.nan
+    dx = _d(x)
+    dout = torch.empty(rows, dtype=torch.int64, device="cuda")
+    N.check(ctx.lib.b2m_argmax_dev(ctx.handle, _p(dx), _p(dout), rows, v))
+    torch.cuda.synchronize()
+    vals = np.where(np.isnan(x), -np.inf, x)
+    mx = vals.max(axis=1)
+    want = np.where(mx >= -np.finfo(np.float32).max, np.argmax(vals == mx[:, None], axis=1), 0)
+    np.testing.assert_array_equal(dout.cpu().numpy(), want)

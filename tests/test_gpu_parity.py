@@ -414,6 +414,24 @@ def test_nbits_prefill_token_tiles(ctx, m, n):
     assert_fast_close(fast, want, f"prefill m={m} n={n}")
 
 
+@pytest.mark.parametrize("m,k,n", [(64, 2048, 1024), (64, 3072, 1024), (64, 1024, 4096), (64, 1024, 6144),
+                                   (33, 1000, 1100), (100, 4096, 256), (40, 256, 640)])
+def test_nbits_prefill_small_grids(ctx, m, k, n):
+    # Tensor-core shapes whose grids underfill the SMs: decoder projections at
+    # 64 sequences (o / down / qkv / gate_up), a K tail with a partial column
+    # tile, long K on two column tiles; repeated calls are bitwise stable.
+    rng = np.random.default_rng(9000 + m + k + n)
+    a, bq, sc, z = nbits_case(rng, m, k, n, 32, "packed")
+    bias = rng.standard_normal((n,)).astype(np.float32)
+    want = oracle.matmul_nbits(a, bq, sc, z, k, n, 32, bias=bias, nthreads=8)
+    w = ops.prepack_nbits(ctx, bq, sc, z, k=k, n=n, bits=4, blockSize=32)
+    first = ops.opMatMulNBits(a, w, k=k, n=n, blockSize=32, bias=bias, ctx=ctx).numpy()
+    assert_fast_close(first, want, f"small grid m={m} k={k} n={n}")
+    for _ in range(2):
+        again = ops.opMatMulNBits(a, w, k=k, n=n, blockSize=32, bias=bias, ctx=ctx).numpy()
+        bits_equal(again, first)
+
+
 def test_nbits_batched_leading_dims_and_empty(ctx):
     rng = np.random.default_rng(1)
     a, bq, sc, z = nbits_case(rng, 6, 64, 24)
