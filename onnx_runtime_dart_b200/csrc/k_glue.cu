@@ -838,8 +838,10 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
 #pragma unroll
     for (int c = 0; c < VPD; c++) o[g][c] = 0.f;
   }
-  for (int j0 = jbeg + warp * KB; j0 < jend; j0 += 8 * KB) {
-    float kr[KB][VPD], vr[KB][VPD];
+  // The next step's K / V rows are requested before this step's arithmetic,
+  // so a warp always has two steps of loads in flight.
+  float kn[KB][VPD], vn[KB][VPD];
+  auto load_step = [&](int j0) {
 #pragma unroll
     for (int kb = 0; kb < KB; kb++) {
       const bool ok = j0 + kb < jend;
@@ -847,16 +849,28 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
       if constexpr (VPD == 4) {
         const float4 k4 = ok ? *reinterpret_cast<const float4 *>(kp) : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4 v4 = ok ? *reinterpret_cast<const float4 *>(vp) : make_float4(0.f, 0.f, 0.f, 0.f);
-        kr[kb][0] = k4.x, kr[kb][1] = k4.y, kr[kb][2] = k4.z, kr[kb][3] = k4.w;
-        vr[kb][0] = v4.x, vr[kb][1] = v4.y, vr[kb][2] = v4.z, vr[kb][3] = v4.w;
+        kn[kb][0] = k4.x, kn[kb][1] = k4.y, kn[kb][2] = k4.z, kn[kb][3] = k4.w;
+        vn[kb][0] = v4.x, vn[kb][1] = v4.y, vn[kb][2] = v4.z, vn[kb][3] = v4.w;
       } else {
 #pragma unroll
         for (int c = 0; c < VPD; c++) {
-          kr[kb][c] = ok ? kp[c] : 0.f;
-          vr[kb][c] = ok ? vp[c] : 0.f;
+          kn[kb][c] = ok ? kp[c] : 0.f;
+          vn[kb][c] = ok ? vp[c] : 0.f;
         }
       }
     }
+  };
+  if (jbeg + warp * KB < jend) load_step(jbeg + warp * KB);
+  for (int j0 = jbeg + warp * KB; j0 < jend; j0 += 8 * KB) {
+    float kr[KB][VPD], vr[KB][VPD];
+#pragma unroll
+    for (int kb = 0; kb < KB; kb++)
+#pragma unroll
+      for (int c = 0; c < VPD; c++) {
+        kr[kb][c] = kn[kb][c];
+        vr[kb][c] = vn[kb][c];
+      }
+    if (j0 + 8 * KB < jend) load_step(j0 + 8 * KB);
     float s[8];
 #pragma unroll
     for (int kb = 0; kb < KB; kb++)
