@@ -18,7 +18,8 @@
 //               taking alternate 128-k stages; each thread owns one weight
 //               column. After the main loop they are the epilogue: tcgen05.ld
 //               of the accumulator (lane = weight column, column = token), add
-//               bias, coalesced stores of Y rows.
+//               bias, stage the half tile in shared memory, one TMA store
+//               (or, for unaligned outputs, coalesced stores of Y rows).
 // Accumulator in TMEM columns [0, BT); A stages from column A_COL0 on, 64
 // columns per 128-k stage (two f16 per 32-bit column, k order).
 // Every mbarrier wait is bounded; a timeout sets the context's device error
@@ -53,6 +54,7 @@ struct TsLayout {
   static_assert(KSUB == 2 || KSUB == 4, "stage: 128 or 256 k");
   static_assert(A_COL0 + STAGES * A_STAGE_COLS <= TS_TMEM_COLS, "accumulator + weight stages exceed TMEM");
   static_assert(BYTES <= 232448, "shared memory");
+  static_assert((uint32_t)BT * 128 * 4 <= STAGES * B_STAGE, "the output tile is staged in the activation stages");
 };
 
 // The raw weights of one 64-k chunk for one column: 64 nibbles and the two
@@ -87,9 +89,10 @@ __device__ __forceinline__ void ts_dequant(const TsRec &r, uint32_t (&out)[32]) 
 
 template <int BT, int STAGES, int KSUB>
 __global__ void __launch_bounds__(TS_THREADS, 1)
-    nbits_ts_kernel(const __grid_constant__ CUtensorMap tmap_a, const uint4 *__restrict__ tsq,
-                    const uint2 *__restrict__ tss, const float *__restrict__ bias, float *__restrict__ Y, int M, int N,
-                    int nchunks, int32_t *dev_err) {
+    nbits_ts_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_y,
+                    int use_tma_y, const uint4 *__restrict__ tsq, const uint2 *__restrict__ tss,
+                    const float *__restrict__ bias, float *__restrict__ Y, int M, int N, int nchunks,
+                    int32_t *dev_err) {
   using L = TsLayout<BT, STAGES, KSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -246,6 +249,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       constexpr int HALF = BT / 2;
       constexpr int GRP = HALF % 64 == 0 ? 64 : HALF % 48 == 0 ? 48 : HALF % 32 == 0 ? 32 : 16;
       static_assert(HALF % GRP == 0, "epilogue groups must tile the half tile");
+      // With an output tensor map the group's half tile goes through shared
+      // memory (the activation stages, idle once the accumulator is final:
+      // every stage's TMA landed before its MMAs ran) as a row-major
+      // [HALF tokens][128 columns] box, written by one TMA store; a lane's
+      // direct stores are 4-byte column slices, 48 per token group, and the
+      // write burst of a tile took ~2.5 us that way.
+      float *stage_out = reinterpret_cast<float *>(smem) + (size_t)gq * HALF * 128;
 #pragma unroll 1
       for (int c0 = gq * HALF; c0 < (gq + 1) * HALF; c0 += GRP) {
         uint32_t v[GRP];
@@ -253,6 +263,11 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         for (int j = 0; j < GRP; j += 16)
           tmem_ld16(lane_base + (uint32_t)(c0 + j), *reinterpret_cast<uint32_t(*)[16]>(&v[j]));
         tmem_ld_wait();
+        if (use_tma_y) {
+#pragma unroll
+          for (int j = 0; j < GRP; j++) stage_out[(c0 - gq * HALF + j) * 128 + cl] = __uint_as_float(v[j]) + b;
+          continue;
+        }
         if (colok) {
           float *yc = Y + (size_t)(t0 + c0) * N + col;
           const int lim = M - (t0 + c0);
@@ -260,6 +275,16 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
           for (int j = 0; j < GRP; j++)
             if (j < lim) yc[(size_t)j * N] = __uint_as_float(v[j]) + b;
         }
+      }
+    }
+    if (use_tma_y) {
+      // Every epilogue warp takes the group barrier, aborted or not.
+      fence_proxy_async_smem();
+      named_barrier_sync(2 + gq, 128);
+      if (go && warp == 2 + 4 * gq && lane == 0) {
+        tma_store_2d(&tmap_y, reinterpret_cast<float *>(smem) + (size_t)gq * (BT / 2) * 128, n0, t0 + gq * (BT / 2));
+        bulk_commit_group();
+        bulk_wait_group0();
       }
     }
   }
@@ -283,6 +308,20 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t
                                     box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   B2M_REQUIRE(r == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the activation operand");
+  // Output map for the TMA-store epilogue: [M][N] fp32 rows, boxes of 128
+  // columns x BT/2 tokens (needs 16-byte aligned rows; otherwise direct stores).
+  CUtensorMap ty = tm;
+  int use_ty = 0;
+  if ((a.N % 4) == 0 && (reinterpret_cast<uintptr_t>(a.Y) & 15) == 0) {
+    const cuuint64_t ydims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
+    const cuuint64_t ystr[1] = {(cuuint64_t)(a.N * 4)};
+    const cuuint32_t ybox[2] = {128u, (cuuint32_t)(BT / 2)};
+    CUresult ry = tensor_map_encoder()(&ty, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.Y, ydims, ystr, ybox, estr,
+                                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                       CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    B2M_REQUIRE(ry == CUDA_SUCCESS, B2M_ERR_CUDA, "cuTensorMapEncodeTiled failed for the output");
+    use_ty = 1;
+  }
   auto kern = nbits_ts_kernel<BT, STAGES, KSUB>;
   set_smem_limit_once<nbits_ts_kernel<BT, STAGES, KSUB>>((int)L::BYTES);
   cudaLaunchConfig_t cfg = {};
@@ -295,7 +334,7 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, reinterpret_cast<const uint4 *>(a.w->tsq),
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, ty, use_ty, reinterpret_cast<const uint4 *>(a.w->tsq),
                               reinterpret_cast<const uint2 *>(a.w->tss), a.bias, a.Y, (int)a.M, (int)a.N,
                               (int)(a.w->kp / 64), a.dev_err));
 }

@@ -415,7 +415,7 @@ def test_nbits_prefill_token_tiles(ctx, m, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(64, 2048, 1024), (64, 3072, 1024), (64, 1024, 4096), (64, 1024, 6144),
-                                   (33, 1000, 1100), (100, 4096, 256), (40, 256, 640)])
+                                   (33, 1000, 1100), (100, 4096, 256), (40, 256, 640), (96, 512, 1030)])
 def test_nbits_prefill_small_grids(ctx, m, k, n):
     # Tensor-core shapes whose grids underfill the SMs: decoder projections at
     # 64 sequences (o / down / qkv / gate_up), a K tail with a partial column
