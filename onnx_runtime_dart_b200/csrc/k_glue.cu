@@ -17,6 +17,8 @@
 #include <algorithm>
 #include <cfloat>
 
+#include <cuda_bf16.h>
+
 #include "b2m_internal.cuh"
 #include "tc_common.cuh"
 
@@ -955,6 +957,260 @@ __global__ void gqa_decode_combine_kernel(const float *pm, const float *pl, cons
   }
 }
 
+// ---------------------------------------------------------------------------
+// MultiHeadAttention on the tensor cores for one (query head, sequence) of at
+// most 128 queries x 128 keys, head_dim 64 (the BERT-base shape). Scores and
+// P.V are fp32 products of bf16-split operands (x = x0 + x1, three
+// kind::f16 MMAs per product, ~1e-5 relative), the softmax runs in fp32 on
+// the accumulator rows.
+//
+//   smem (bytes, 128-byte-swizzled K-major [rows][64 bf16] blocks):
+//     [0, 64K)    Q hi, Q lo, K hi, K lo (16 KB each); later P hi / lo
+//                 ([128 queries][128 keys], two 64-key blocks each), later
+//                 the output staging
+//     [64K, 96K)  V^T hi, V^T lo: [64 dims][128 keys], two 64-key blocks
+//     [96K, ...)  bias row (128 floats), barriers, TMEM slot
+//   TMEM: scores in columns [0, 128), output in [128, 192).
+// ---------------------------------------------------------------------------
+using b2m::fence_proxy_async_smem;
+using b2m::mbar_fence_init;
+using b2m::mbar_init;
+using b2m::smem_u32;
+using b2m::sw128_kmajor_desc;
+using b2m::tc_fence_after;
+using b2m::tc_fence_before;
+using b2m::tmem_alloc;
+using b2m::tmem_dealloc;
+using b2m::tmem_ld16;
+using b2m::tmem_ld_wait;
+using b2m::umma_commit;
+using b2m::umma_f16;
+using b2m::umma_idesc;
+using b2m::warp_wait_or_abort;
+
+constexpr int MTC_D = 64, MTC_T = 128;
+constexpr uint32_t MTC_QH = 0, MTC_QL = 16384, MTC_KH = 32768, MTC_KL = 49152;
+constexpr uint32_t MTC_PH = 0, MTC_PL = 32768;
+constexpr uint32_t MTC_VH = 65536, MTC_VL = 81920;
+constexpr uint32_t MTC_MASK = 98304, MTC_BAR = MTC_MASK + 512, MTC_SLOT = MTC_BAR + 16;
+constexpr uint32_t MTC_BYTES = MTC_SLOT + 16 + 1024;
+
+// Byte offset of bf16 element (row r, k) in a [rows][64] SW128 K-major block.
+__device__ __forceinline__ uint32_t sw128_elem(int r, int k) {
+  return (uint32_t)(r * 128 + ((((k >> 3) ^ (r & 7)) << 4) | ((k & 7) << 1)));
+}
+
+// x = x0 + x1 in bf16 (x0 = rn(x), truncated if rounding would overflow a
+// finite x; x1 = rn(x - x0), 0 for non-finite x).
+__device__ __forceinline__ void split2_bf16(float x, __nv_bfloat16 &h, __nv_bfloat16 &l) {
+  h = __float2bfloat16_rn(x);
+  float hf = __bfloat162float(h);
+  if (isinf(hf) && isfinite(x)) {
+    h = __float2bfloat16_rz(x);
+    hf = __bfloat162float(h);
+  }
+  l = __float2bfloat16_rn(isfinite(x) ? x - hf : 0.f);
+}
+
+// Stages one [128][64] fp32 operand (row r of 64 floats at base + r * rs,
+// rows >= n are zero) as bf16 hi / lo SW128 blocks; thread = row.
+__device__ __forceinline__ void mtc_stage_rows(uint8_t *smem, uint32_t off_h, uint32_t off_l, const float *base,
+                                               int64_t rs, int n) {
+  const int r = threadIdx.x;
+  const float *src = base + (int64_t)r * rs;
+#pragma unroll
+  for (int c = 0; c < 8; c++) {
+    float x[8];
+    if (r < n) {
+      const float4 a = *reinterpret_cast<const float4 *>(src + 8 * c);
+      const float4 b = *reinterpret_cast<const float4 *>(src + 8 * c + 4);
+      x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) x[j] = 0.f;
+    }
+    __align__(16) __nv_bfloat16 h[8], l[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) split2_bf16(x[j], h[j], l[j]);
+    *reinterpret_cast<uint4 *>(smem + off_h + sw128_elem(r, 8 * c)) = *reinterpret_cast<const uint4 *>(h);
+    *reinterpret_cast<uint4 *>(smem + off_l + sw128_elem(r, 8 * c)) = *reinterpret_cast<const uint4 *>(l);
+  }
+}
+
+__global__ void __launch_bounds__(128) mha_tc_kernel(const GqaArgs a) {
+  extern __shared__ uint8_t mtc_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(mtc_raw) + 1023) & ~(uintptr_t)1023);
+  float *mrow = reinterpret_cast<float *>(smem + MTC_MASK);
+  uint64_t *bar_s = reinterpret_cast<uint64_t *>(smem + MTC_BAR), *bar_o = bar_s + 1;
+  uint32_t *slot = reinterpret_cast<uint32_t *>(smem + MTC_SLOT);
+  __shared__ int abort_flag_s;
+  volatile int *abort_flag = &abort_flag_s;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int h = blockIdx.x, b = blockIdx.y;
+  const int kvh = h / (a.H / a.KVH);
+  const int S = a.S, T = a.kv_len;
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    abort_flag_s = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) tmem_alloc(slot, 256);
+  // Operands: Q rows, K rows, V^T (thread i packs keys 2p, 2p+1 of dims
+  // 32 (i / 64) .. +32 as bf16 pairs).
+  mtc_stage_rows(smem, MTC_QH, MTC_QL, a.q + (int64_t)b * S * a.q_rs + h * MTC_D, a.q_rs, S);
+  const float *kb0 = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *vb0 = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  mtc_stage_rows(smem, MTC_KH, MTC_KL, kb0, a.kc_rs, T);
+  {
+    const int pr = tid & 63, d0 = (tid >> 6) * 32;
+    const int t0 = 2 * pr;
+    const float *v0 = vb0 + (int64_t)t0 * a.kc_rs + d0, *v1 = v0 + a.kc_rs;
+    const uint32_t blk = (uint32_t)(t0 >> 6) * 8192u;
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
+      if (t0 < T) x0 = *reinterpret_cast<const float4 *>(v0 + 4 * c);
+      if (t0 + 1 < T) x1 = *reinterpret_cast<const float4 *>(v1 + 4 * c);
+      const float e0[4] = {x0.x, x0.y, x0.z, x0.w}, e1[4] = {x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int d = d0 + 4 * c + j;
+        __nv_bfloat16 h0, l0, h1, l1;
+        split2_bf16(e0[j], h0, l0);
+        split2_bf16(e1[j], h1, l1);
+        const uint32_t o = blk + sw128_elem(d, t0 & 63);
+        *reinterpret_cast<__nv_bfloat162 *>(smem + MTC_VH + o) = __halves2bfloat162(h0, h1);
+        *reinterpret_cast<__nv_bfloat162 *>(smem + MTC_VL + o) = __halves2bfloat162(l0, l1);
+      }
+    }
+  }
+  const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs + (int64_t)h * a.mask_hs : nullptr;
+  const bool per_query = mk && a.mask_qs != 0;
+  mrow[tid] = tid >= T ? -INFINITY : (mk && !per_query ? mk[tid] : 0.f);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *slot;
+  if (tid == 0) {
+    constexpr uint32_t idesc_s = umma_idesc(128, 128, 1u, 1u, 1u);
+    const uint32_t base = smem_u32(smem);
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const uint32_t o = (uint32_t)kk * 32u;
+      const uint64_t qh = sw128_kmajor_desc(base + MTC_QH + o), ql = sw128_kmajor_desc(base + MTC_QL + o);
+      const uint64_t kh = sw128_kmajor_desc(base + MTC_KH + o), kl = sw128_kmajor_desc(base + MTC_KL + o);
+      umma_f16(tmem, ql, kh, idesc_s, kk ? 1u : 0u);
+      umma_f16(tmem, qh, kl, idesc_s, 1u);
+      umma_f16(tmem, qh, kh, idesc_s, 1u);
+    }
+    umma_commit(bar_s);
+  }
+  const bool ok_s = warp_wait_or_abort(bar_s, 0u, abort_flag, a.err);
+  tc_fence_after();
+  // Softmax of query row r = tid over the 128 key columns (fp32); P
+  // (unnormalised, <= 1) goes back to shared memory as bf16 hi / lo.
+  const int r = tid;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  const float *mq = per_query && r < S ? mk + (int64_t)r * a.mask_qs : nullptr;
+  auto score = [&](float raw, int t) {
+    float v = raw * a.scale + mrow[t];
+    if (mq && t < T) v += mq[t];
+    if (a.causal && t > r) v = -INFINITY;
+    return v;
+  };
+  float mx = -INFINITY;
+  if (ok_s) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < MTC_T; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(trow + (uint32_t)c0, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; j++) mx = fmaxf(mx, score(__uint_as_float(v[j]), c0 + j));
+    }
+  }
+  float lsum = 0.f;
+  __syncthreads();  // every warp has read its S rows before P overwrites Q / K
+  if (ok_s) {
+#pragma unroll 1
+    for (int c0 = 0; c0 < MTC_T; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(trow + (uint32_t)c0, v);
+      tmem_ld_wait();
+      __align__(16) __nv_bfloat16 ph[16], pl[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const float sc = score(__uint_as_float(v[j]), c0 + j);
+        const float e = mx == -INFINITY ? 0.f : __expf(sc - mx);
+        lsum += e;
+        split2_bf16(e, ph[j], pl[j]);
+      }
+      const uint32_t blk = (uint32_t)(c0 >> 6) * 16384u;
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        const uint32_t o = blk + sw128_elem(r, (c0 & 63) + 8 * hh);
+        *reinterpret_cast<uint4 *>(smem + MTC_PH + o) = *reinterpret_cast<const uint4 *>(ph + 8 * hh);
+        *reinterpret_cast<uint4 *>(smem + MTC_PL + o) = *reinterpret_cast<const uint4 *>(pl + 8 * hh);
+      }
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0 && ok_s) {
+    constexpr uint32_t idesc_o = umma_idesc(128, 64, 1u, 1u, 1u);
+    const uint32_t base = smem_u32(smem);
+#pragma unroll
+    for (int kk = 0; kk < 8; kk++) {
+      const uint32_t o = (uint32_t)(kk & 3) * 32u;
+      const uint64_t ph = sw128_kmajor_desc(base + MTC_PH + (kk >> 2) * 16384u + o);
+      const uint64_t pl = sw128_kmajor_desc(base + MTC_PL + (kk >> 2) * 16384u + o);
+      const uint64_t vh = sw128_kmajor_desc(base + MTC_VH + (kk >> 2) * 8192u + o);
+      const uint64_t vl = sw128_kmajor_desc(base + MTC_VL + (kk >> 2) * 8192u + o);
+      umma_f16(tmem + 128, pl, vh, idesc_o, kk ? 1u : 0u);
+      umma_f16(tmem + 128, ph, vl, idesc_o, 1u);
+      umma_f16(tmem + 128, ph, vh, idesc_o, 1u);
+    }
+  }
+  if (tid == 0) umma_commit(bar_o);  // also when skipped, so every wait ends
+  const bool ok_o = warp_wait_or_abort(bar_o, 0u, abort_flag, a.err) && ok_s;
+  tc_fence_after();
+  __syncthreads();  // P reads by the MMAs are complete: the staging may reuse it
+  // Output: O / l through a per-warp 32 x 65 transpose so each store writes a
+  // contiguous 256-byte row segment.
+  float *st = reinterpret_cast<float *>(smem) + warp * (32 * 65);
+  if (ok_o) {
+    const float inv = 1.f / lsum;
+#pragma unroll
+    for (int c0 = 0; c0 < MTC_D; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(trow + 128u + (uint32_t)c0, v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; j++) st[lane * 65 + c0 + j] = __uint_as_float(v[j]) * inv;
+    }
+  }
+  __syncwarp();
+  if (ok_o) {
+    for (int i = 0; i < 32; i++) {
+      const int q = warp * 32 + i;
+      if (q >= S) break;
+      float *dst = a.out + ((int64_t)b * S + q) * (int64_t)a.H * MTC_D + h * MTC_D;
+      dst[lane] = st[i * 65 + lane];
+      dst[lane + 32] = st[i * 65 + lane + 32];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 __global__ void advance_kernel(int32_t *past, int n, int delta) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) past[i] += delta;
@@ -1055,6 +1311,14 @@ static bool decode_shape(const GqaArgs &a) {
   return a.S == 1 && a.past && a.causal && !a.mask && dok && (G == 1 || G == 2 || G == 4 || G == 8);
 }
 
+// The tensor-core kernel: MultiHeadAttention (keys from the projected rows)
+// of head_dim 64 with at most 128 queries and keys, 16-byte aligned rows.
+static bool mha_tc_shape(const GqaArgs &a) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return !a.past && a.D == 64 && a.S >= 1 && a.S <= 128 && a.kv_len >= 1 && a.kv_len <= 128 && a.q_rs % 4 == 0 &&
+         a.kc_rs % 4 == 0 && a.kc_bs % 4 == 0 && a.kc_hs % 4 == 0 && al(a.q) && al(a.kcache) && al(a.vcache);
+}
+
 static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaStream_t s) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
@@ -1074,6 +1338,9 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaS
     if (nsplit > 1) {
       gqa_decode_combine_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, 0, s>>>(pm, pl, po, a.out, a.H, D, nsplit);
     }
+  } else if (mha_tc_shape(a)) {
+    b2m::set_smem_limit_once<mha_tc_kernel>((int)MTC_BYTES);
+    mha_tc_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, MTC_BYTES, s>>>(a);
   } else if (dok) {
     dim3 grid((unsigned)((a.S + 63) / 64), (unsigned)a.H, (unsigned)a.B);
     const int smem = (2 * D * 68 + 64 * D + 64 * 68) * 4;

@@ -168,6 +168,8 @@ def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
     (2, 130, 130, 8, 8, 96, None, 0, 1),      # ragged last tiles in both directions
     (2, 70, 70, 4, 4, 64, "bias4d", 0, 0),    # attention_bias [b][h][s][t], per query row
     (2, 9, 11, 4, 4, 48, "bias1h", 0, 0),     # attention_bias with one head, per-query-warp kernel
+    (2, 100, 100, 4, 2, 64, None, 1, 0),      # causal, grouped kv heads, tensor-core kernel
+    (3, 128, 77, 2, 2, 64, "pad", 0, 0),      # cross-attention with ragged keys, tensor-core kernel
 ])
 def test_mha_additive_mask(ctx, b, s, t, h, kvh, d, mask_mode, causal, packed):
     rng = np.random.default_rng(b * 1000 + s * 7 + t + d)
@@ -313,11 +315,13 @@ def _ref_bert(enc, ids, mask01):
     return x
 
 
-@pytest.mark.parametrize("mode", ["fast", "exact"])
-def test_tiny_bert_chain_matches_composition(ctx, mode):
+@pytest.mark.parametrize("mode,heads", [("fast", 4), ("exact", 4), ("fast", 2)])
+def test_tiny_bert_chain_matches_composition(ctx, mode, heads):
+    # heads=2 gives head_dim 64: the tensor-core attention kernel.
     from onnx_runtime_dart_b200.bert import BertConfig, BertEncoder
 
     cfg = BertConfig.tiny()
+    cfg.heads = heads
     b, s = 3, 40
     enc = BertEncoder(ctx, cfg, b, s, seed=5, mode=N.MODE_FAST if mode == "fast" else N.MODE_EXACT, keep_host=True)
     rng = np.random.default_rng(9)
