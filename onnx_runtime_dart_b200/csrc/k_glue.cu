@@ -1013,17 +1013,18 @@ __device__ __forceinline__ void split2_bf16(float x, __nv_bfloat16 &h, __nv_bflo
 }
 
 // Stages one [128][64] fp32 operand (row r of 64 floats at base + r * rs,
-// rows >= n are zero) as bf16 hi / lo SW128 blocks; thread = row.
+// rows >= n are zero) as bf16 hi / lo SW128 blocks. Item (row, 8-float
+// chunk), 1024 per operand over the CTA's threads: a warp reads four 256-byte
+// row segments.
 __device__ __forceinline__ void mtc_stage_rows(uint8_t *smem, uint32_t off_h, uint32_t off_l, const float *base,
                                                int64_t rs, int n) {
-  const int r = threadIdx.x;
-  const float *src = base + (int64_t)r * rs;
-#pragma unroll
-  for (int c = 0; c < 8; c++) {
+  for (int it = threadIdx.x; it < 128 * 8; it += blockDim.x) {
+    const int r = it >> 3, c = it & 7;
     float x[8];
     if (r < n) {
-      const float4 a = *reinterpret_cast<const float4 *>(src + 8 * c);
-      const float4 b = *reinterpret_cast<const float4 *>(src + 8 * c + 4);
+      const float *src = base + (int64_t)r * rs + 8 * c;
+      const float4 a = *reinterpret_cast<const float4 *>(src);
+      const float4 b = *reinterpret_cast<const float4 *>(src + 4);
       x[0] = a.x, x[1] = a.y, x[2] = a.z, x[3] = a.w, x[4] = b.x, x[5] = b.y, x[6] = b.z, x[7] = b.w;
     } else {
 #pragma unroll
@@ -1037,15 +1038,20 @@ __device__ __forceinline__ void mtc_stage_rows(uint8_t *smem, uint32_t off_h, ui
   }
 }
 
-__global__ void __launch_bounds__(128) mha_tc_kernel(const GqaArgs a) {
+// 512 threads. Warp w reads TMEM lane quarter w % 4 (query rows) and owns
+// column block w / 4: 32 of the 128 score columns, 16 of the 64 output
+// columns; row max and sum combine the four column blocks in shared memory.
+__global__ void __launch_bounds__(512) mha_tc_kernel(const GqaArgs a) {
   extern __shared__ uint8_t mtc_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(mtc_raw) + 1023) & ~(uintptr_t)1023);
   float *mrow = reinterpret_cast<float *>(smem + MTC_MASK);
   uint64_t *bar_s = reinterpret_cast<uint64_t *>(smem + MTC_BAR), *bar_o = bar_s + 1;
   uint32_t *slot = reinterpret_cast<uint32_t *>(smem + MTC_SLOT);
   __shared__ int abort_flag_s;
+  __shared__ float red[4][128];
   volatile int *abort_flag = &abort_flag_s;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int q4 = warp & 3, cb = warp >> 2;
   const int h = blockIdx.x, b = blockIdx.y;
   const int kvh = h / (a.H / a.KVH);
   const int S = a.S, T = a.kv_len;
@@ -1056,38 +1062,40 @@ __global__ void __launch_bounds__(128) mha_tc_kernel(const GqaArgs a) {
     mbar_fence_init();
   }
   if (warp == 0) tmem_alloc(slot, 256);
-  // Operands: Q rows, K rows, V^T (thread i packs keys 2p, 2p+1 of dims
-  // 32 (i / 64) .. +32 as bf16 pairs).
   mtc_stage_rows(smem, MTC_QH, MTC_QL, a.q + (int64_t)b * S * a.q_rs + h * MTC_D, a.q_rs, S);
   const float *kb0 = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
   const float *vb0 = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
   mtc_stage_rows(smem, MTC_KH, MTC_KL, kb0, a.kc_rs, T);
   {
-    const int pr = tid & 63, d0 = (tid >> 6) * 32;
+    // V^T: thread packs keys 2p, 2p+1 of dims 8g .. 8g+7 as bf16 pairs.
+    const int pr = tid & 63, g = tid >> 6;
     const int t0 = 2 * pr;
-    const float *v0 = vb0 + (int64_t)t0 * a.kc_rs + d0, *v1 = v0 + a.kc_rs;
+    const float *v0 = vb0 + (int64_t)t0 * a.kc_rs + 8 * g, *v1 = v0 + a.kc_rs;
+    float e0[8], e1[8];
+#pragma unroll
+    for (int j = 0; j < 8; j++) e0[j] = e1[j] = 0.f;
+    if (t0 < T) {
+      const float4 x = *reinterpret_cast<const float4 *>(v0), y = *reinterpret_cast<const float4 *>(v0 + 4);
+      e0[0] = x.x, e0[1] = x.y, e0[2] = x.z, e0[3] = x.w, e0[4] = y.x, e0[5] = y.y, e0[6] = y.z, e0[7] = y.w;
+    }
+    if (t0 + 1 < T) {
+      const float4 x = *reinterpret_cast<const float4 *>(v1), y = *reinterpret_cast<const float4 *>(v1 + 4);
+      e1[0] = x.x, e1[1] = x.y, e1[2] = x.z, e1[3] = x.w, e1[4] = y.x, e1[5] = y.y, e1[6] = y.z, e1[7] = y.w;
+    }
     const uint32_t blk = (uint32_t)(t0 >> 6) * 8192u;
 #pragma unroll
-    for (int c = 0; c < 8; c++) {
-      float4 x0 = make_float4(0.f, 0.f, 0.f, 0.f), x1 = x0;
-      if (t0 < T) x0 = *reinterpret_cast<const float4 *>(v0 + 4 * c);
-      if (t0 + 1 < T) x1 = *reinterpret_cast<const float4 *>(v1 + 4 * c);
-      const float e0[4] = {x0.x, x0.y, x0.z, x0.w}, e1[4] = {x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const int d = d0 + 4 * c + j;
-        __nv_bfloat16 h0, l0, h1, l1;
-        split2_bf16(e0[j], h0, l0);
-        split2_bf16(e1[j], h1, l1);
-        const uint32_t o = blk + sw128_elem(d, t0 & 63);
-        *reinterpret_cast<__nv_bfloat162 *>(smem + MTC_VH + o) = __halves2bfloat162(h0, h1);
-        *reinterpret_cast<__nv_bfloat162 *>(smem + MTC_VL + o) = __halves2bfloat162(l0, l1);
-      }
+    for (int j = 0; j < 8; j++) {
+      __nv_bfloat16 h0, l0, h1, l1;
+      split2_bf16(e0[j], h0, l0);
+      split2_bf16(e1[j], h1, l1);
+      const uint32_t o = blk + sw128_elem(8 * g + j, t0 & 63);
+      *reinterpret_cast<__nv_bfloat162 *>(smem + MTC_VH + o) = __halves2bfloat162(h0, h1);
+      *reinterpret_cast<__nv_bfloat162 *>(smem + MTC_VL + o) = __halves2bfloat162(l0, l1);
     }
   }
   const float *mk = a.mask ? a.mask + (int64_t)b * a.mask_bs + (int64_t)h * a.mask_hs : nullptr;
   const bool per_query = mk && a.mask_qs != 0;
-  mrow[tid] = tid >= T ? -INFINITY : (mk && !per_query ? mk[tid] : 0.f);
+  if (tid < 128) mrow[tid] = tid >= T ? -INFINITY : (mk && !per_query ? mk[tid] : 0.f);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
@@ -1109,57 +1117,55 @@ __global__ void __launch_bounds__(128) mha_tc_kernel(const GqaArgs a) {
   }
   const bool ok_s = warp_wait_or_abort(bar_s, 0u, abort_flag, a.err);
   tc_fence_after();
-  // Softmax of query row r = tid over the 128 key columns (fp32); P
-  // (unnormalised, <= 1) goes back to shared memory as bf16 hi / lo.
-  const int r = tid;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  // Softmax of query row r over this warp's 32 key columns (fp32); P
+  // (unnormalised, <= 1) goes to shared memory as bf16 hi / lo.
+  const int r = q4 * 32 + lane, c0 = cb * 32;
+  const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
   const float *mq = per_query && r < S ? mk + (int64_t)r * a.mask_qs : nullptr;
-  auto score = [&](float raw, int t) {
-    float v = raw * a.scale + mrow[t];
-    if (mq && t < T) v += mq[t];
-    if (a.causal && t > r) v = -INFINITY;
-    return v;
-  };
+  float sv[32];
   float mx = -INFINITY;
   if (ok_s) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < MTC_T; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(trow + (uint32_t)c0, v);
-      tmem_ld_wait();
+    uint32_t v[32];
+    tmem_ld16(trow + (uint32_t)c0, *reinterpret_cast<uint32_t(*)[16]>(v));
+    tmem_ld16(trow + (uint32_t)c0 + 16u, *reinterpret_cast<uint32_t(*)[16]>(v + 16));
+    tmem_ld_wait();
 #pragma unroll
-      for (int j = 0; j < 16; j++) mx = fmaxf(mx, score(__uint_as_float(v[j]), c0 + j));
+    for (int j = 0; j < 32; j++) {
+      const int t = c0 + j;
+      float x = __uint_as_float(v[j]) * a.scale + mrow[t];
+      if (mq && t < T) x += mq[t];
+      if (a.causal && t > r) x = -INFINITY;
+      sv[j] = x;
+      mx = fmaxf(mx, x);
     }
   }
-  float lsum = 0.f;
-  __syncthreads();  // every warp has read its S rows before P overwrites Q / K
+  red[cb][r] = mx;
+  __syncthreads();  // also: every S read is done before P overwrites Q / K
+  mx = fmaxf(fmaxf(red[0][r], red[1][r]), fmaxf(red[2][r], red[3][r]));
+  float psum = 0.f;
   if (ok_s) {
-#pragma unroll 1
-    for (int c0 = 0; c0 < MTC_T; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(trow + (uint32_t)c0, v);
-      tmem_ld_wait();
-      __align__(16) __nv_bfloat16 ph[16], pl[16];
+    __align__(16) __nv_bfloat16 ph[32], pl[32];
 #pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const float sc = score(__uint_as_float(v[j]), c0 + j);
-        const float e = mx == -INFINITY ? 0.f : __expf(sc - mx);
-        lsum += e;
-        split2_bf16(e, ph[j], pl[j]);
-      }
-      const uint32_t blk = (uint32_t)(c0 >> 6) * 16384u;
+    for (int j = 0; j < 32; j++) {
+      const float e = mx == -INFINITY ? 0.f : __expf(sv[j] - mx);
+      psum += e;
+      split2_bf16(e, ph[j], pl[j]);
+    }
+    const uint32_t blk = (uint32_t)(c0 >> 6) * 16384u;
 #pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        const uint32_t o = blk + sw128_elem(r, (c0 & 63) + 8 * hh);
-        *reinterpret_cast<uint4 *>(smem + MTC_PH + o) = *reinterpret_cast<const uint4 *>(ph + 8 * hh);
-        *reinterpret_cast<uint4 *>(smem + MTC_PL + o) = *reinterpret_cast<const uint4 *>(pl + 8 * hh);
-      }
+    for (int hh = 0; hh < 4; hh++) {
+      const uint32_t o = blk + sw128_elem(r, (c0 & 63) + 8 * hh);
+      *reinterpret_cast<uint4 *>(smem + MTC_PH + o) = *reinterpret_cast<const uint4 *>(ph + 8 * hh);
+      *reinterpret_cast<uint4 *>(smem + MTC_PL + o) = *reinterpret_cast<const uint4 *>(pl + 8 * hh);
     }
   }
+  __syncthreads();  // every thread has read red[][] (max) before it is reused
+  red[cb][r] = psum;
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  const float lsum = (red[0][r] + red[1][r]) + (red[2][r] + red[3][r]);
   if (tid == 0 && ok_s) {
     constexpr uint32_t idesc_o = umma_idesc(128, 64, 1u, 1u, 1u);
     const uint32_t base = smem_u32(smem);
@@ -1178,29 +1184,23 @@ __global__ void __launch_bounds__(128) mha_tc_kernel(const GqaArgs a) {
   if (tid == 0) umma_commit(bar_o);  // also when skipped, so every wait ends
   const bool ok_o = warp_wait_or_abort(bar_o, 0u, abort_flag, a.err) && ok_s;
   tc_fence_after();
-  __syncthreads();  // P reads by the MMAs are complete: the staging may reuse it
-  // Output: O / l through a per-warp 32 x 65 transpose so each store writes a
-  // contiguous 256-byte row segment.
-  float *st = reinterpret_cast<float *>(smem) + warp * (32 * 65);
+  __syncthreads();  // the MMAs' P reads are complete: the staging may reuse it
+  // Output O / l: this warp's 16 columns of its 32 rows into a [128][65]
+  // staging block, then row-contiguous stores by all threads.
+  float *st = reinterpret_cast<float *>(smem);
   if (ok_o) {
     const float inv = 1.f / lsum;
+    uint32_t v[16];
+    tmem_ld16(trow + 128u + (uint32_t)(cb * 16), v);
+    tmem_ld_wait();
 #pragma unroll
-    for (int c0 = 0; c0 < MTC_D; c0 += 16) {
-      uint32_t v[16];
-      tmem_ld16(trow + 128u + (uint32_t)c0, v);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 16; j++) st[lane * 65 + c0 + j] = __uint_as_float(v[j]) * inv;
-    }
+    for (int j = 0; j < 16; j++) st[r * 65 + cb * 16 + j] = __uint_as_float(v[j]) * inv;
   }
-  __syncwarp();
+  __syncthreads();
   if (ok_o) {
-    for (int i = 0; i < 32; i++) {
-      const int q = warp * 32 + i;
-      if (q >= S) break;
-      float *dst = a.out + ((int64_t)b * S + q) * (int64_t)a.H * MTC_D + h * MTC_D;
-      dst[lane] = st[i * 65 + lane];
-      dst[lane + 32] = st[i * 65 + lane + 32];
+    for (int it = tid; it < 128 * MTC_D; it += 512) {
+      const int q = it >> 6, d = it & 63;
+      if (q < S) a.out[((int64_t)b * S + q) * (int64_t)a.H * MTC_D + h * MTC_D + d] = st[q * 65 + d];
     }
   }
   tc_fence_before();
@@ -1340,7 +1340,7 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaS
     }
   } else if (mha_tc_shape(a)) {
     b2m::set_smem_limit_once<mha_tc_kernel>((int)MTC_BYTES);
-    mha_tc_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, MTC_BYTES, s>>>(a);
+    mha_tc_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 512, MTC_BYTES, s>>>(a);
   } else if (dok) {
     dim3 grid((unsigned)((a.S + 63) / 64), (unsigned)a.H, (unsigned)a.B);
     const int smem = (2 * D * 68 + 64 * D + 64 * 68) * 4;
