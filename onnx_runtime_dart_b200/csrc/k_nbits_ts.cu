@@ -27,6 +27,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <atomic>
 
 #include "b2m_internal.cuh"
 #include "ptx.cuh"
@@ -35,6 +36,25 @@
 namespace {
 
 using namespace b2m;
+
+// Thread-block cluster helpers for the split-K reduction through
+// distributed shared memory.
+__device__ __forceinline__ uint32_t dsmem_map(uint32_t saddr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+  return d;
+}
+__device__ __forceinline__ float4 dsmem_ld4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
 
 constexpr int TS_THREADS = 320;
 constexpr uint32_t TS_TMEM_COLS = 512;
@@ -108,12 +128,18 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x;
   const int n0 = tile * 128, t0 = blockIdx.y * BT;
-  const int nst = (nchunks + KSUB - 1) / KSUB;
+  // Split-K over a cluster of gridDim.z CTAs: CTA z sums the stages
+  // [sbeg, sbeg + nst); the partial tiles are added through distributed
+  // shared memory at the end.
+  const int nst_all = (nchunks + KSUB - 1) / KSUB;
+  const int splits = gridDim.z, zr = blockIdx.z;
+  const int sbeg = (int)((int64_t)nst_all * zr / splits);
+  const int nst = (int)((int64_t)nst_all * (zr + 1) / splits) - sbeg;
   // The CTAs of one token tile would otherwise request the same activation
-  // k-tile at the same moment; each weight tile walks K from its own starting
-  // stage (the summation order stays fixed per output element).
+  // k-tile at the same moment; each weight tile walks its K range from its own
+  // starting stage (the summation order stays fixed per output element).
   const int krot = (int)(((unsigned)blockIdx.x * 7u) % (unsigned)nst);
-  auto stage_of = [&](int st) { return st + krot < nst ? st + krot : st + krot - nst; };
+  auto stage_of = [&](int st) { return sbeg + (st + krot < nst ? st + krot : st + krot - nst); };
   auto chunks_of = [&](int rt) { return min(KSUB, nchunks - rt * KSUB); };
 
   if (threadIdx.x == 0) {
@@ -243,7 +269,10 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     if (go) {
       const int col = n0 + cl;
       const bool colok = col < N;
-      const float b = (bias && colok) ? __ldg(bias + col) : 0.f;
+      // With K split, the raw partial tile is staged (no bias) for the
+      // cluster reduction below.
+      const bool stage = use_tma_y || splits > 1;
+      const float b = (bias && colok && splits == 1) ? __ldg(bias + col) : 0.f;
       // All TMEM loads of a group of up to 64 tokens go out before one wait;
       // a wait per 16 columns serializes the load latency.
       constexpr int HALF = BT / 2;
@@ -263,7 +292,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         for (int j = 0; j < GRP; j += 16)
           tmem_ld16(lane_base + (uint32_t)(c0 + j), *reinterpret_cast<uint32_t(*)[16]>(&v[j]));
         tmem_ld_wait();
-        if (use_tma_y) {
+        if (stage) {
 #pragma unroll
           for (int j = 0; j < GRP; j++) stage_out[(c0 - gq * HALF + j) * 128 + cl] = __uint_as_float(v[j]) + b;
           continue;
@@ -277,7 +306,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         }
       }
     }
-    if (use_tma_y) {
+    if (use_tma_y && splits == 1) {
       // Every epilogue warp takes the group barrier, aborted or not.
       fence_proxy_async_smem();
       named_barrier_sync(2 + gq, 128);
@@ -288,6 +317,46 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       }
     }
   }
+  if (splits > 1) {
+    // Every thread of every CTA of the cluster takes both cluster barriers,
+    // aborted or not. CTA z adds the staged partial tiles of all ranks, in
+    // rank order, for its share of the tile's token rows.
+    __syncwarp();
+    pdl_wait();  // (returns at once) every thread that writes Y has waited on the prior grid
+    cluster_sync_all();
+    const int per = (BT + splits - 1) / splits;
+    const int rb = zr * per, re = min(BT, rb + per);
+    const uint32_t sbase = smem_u32(smem);
+    const bool vec = (N & 3) == 0 && (reinterpret_cast<uintptr_t>(Y) & 15) == 0;
+    if (!*abort_flag) {
+      for (int it = threadIdx.x; it < (re - rb) * 32; it += TS_THREADS) {
+        const int row = rb + (it >> 5), c4 = (it & 31) * 4;
+        const int t = t0 + row, col = n0 + c4;
+        if (t >= M || col >= N) continue;
+        const uint32_t off = (uint32_t)(row * 128 + c4) * 4u;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int rk = 0; rk < splits; rk++) {
+          const float4 p = dsmem_ld4(dsmem_map(sbase + off, (uint32_t)rk));
+          acc.x += p.x, acc.y += p.y, acc.z += p.z, acc.w += p.w;
+        }
+        const float o[4] = {acc.x, acc.y, acc.z, acc.w};
+        float *yr = Y + (size_t)t * N + col;
+        if (vec && col + 4 <= N) {
+          float4 w4;
+          w4.x = o[0] + (bias ? __ldg(bias + col) : 0.f);
+          w4.y = o[1] + (bias ? __ldg(bias + col + 1) : 0.f);
+          w4.z = o[2] + (bias ? __ldg(bias + col + 2) : 0.f);
+          w4.w = o[3] + (bias ? __ldg(bias + col + 3) : 0.f);
+          *reinterpret_cast<float4 *>(yr) = w4;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; j++)
+            if (col + j < N) yr[j] = o[j] + (bias ? __ldg(bias + col + j) : 0.f);
+        }
+      }
+    }
+    cluster_sync_all();  // the peers have read this CTA's partial tile
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -297,7 +366,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 }
 
 template <int BT, int STAGES, int KSUB>
-void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s) {
+void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, cudaStream_t s) {
   using L = TsLayout<BT, STAGES, KSUB>;
   CUtensorMap tm;
   const cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)a.M};
@@ -325,15 +394,19 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t
   auto kern = nbits_ts_kernel<BT, STAGES, KSUB>;
   set_smem_limit_once<nbits_ts_kernel<BT, STAGES, KSUB>>((int)L::BYTES);
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(a.w->npad / 128), (unsigned)((a.M + BT - 1) / BT));
+  cfg.gridDim = dim3((unsigned)(a.w->npad / 128), (unsigned)((a.M + BT - 1) / BT), (unsigned)splits);
   cfg.blockDim = dim3(TS_THREADS);
   cfg.dynamicSmemBytes = L::BYTES;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = (unsigned)splits;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = splits > 1 ? 2 : 1;
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, ty, use_ty, reinterpret_cast<const uint4 *>(a.w->tsq),
                               reinterpret_cast<const uint2 *>(a.w->tss), a.bias, a.Y, (int)a.M, (int)a.N,
                               (int)(a.w->kp / 64), a.dev_err));
@@ -363,12 +436,60 @@ int nbits_ts_pick_bt(int64_t M, int64_t N, int sms) {
 
 }  // namespace
 
+namespace {
+
+// Split-K: only when the output tiles leave three quarters of the SMs idle
+// (the decoder's projections at 64 tokens); then the smallest cluster that
+// reaches the fewest stages per CTA (<= 8 CTAs, at least one 128/256-k stage
+// each) and still fits, checked once per tile width with the occupancy API.
+template <int BT, int STAGES, int KSUB>
+int ts_splits(const NbitsArgs &a, int sms) {
+  const int64_t ctas = (a.w->npad / 128) * ((a.M + BT - 1) / BT);
+  if (ctas * 4 > sms) return 1;
+  const int64_t nst = (a.w->kp / 64 + KSUB - 1) / KSUB;
+  const int64_t lim = std::min<int64_t>({(int64_t)8, nst, sms / ctas});
+  // The fewest CTAs that reach the smallest stage count per CTA.
+  const int64_t per = (nst + lim - 1) / lim;
+  int want = (int)((nst + per - 1) / per);
+  static std::atomic<int> max_ok{0};
+  if (max_ok.load() == 0) {
+    using L = TsLayout<BT, STAGES, KSUB>;
+    set_smem_limit_once<nbits_ts_kernel<BT, STAGES, KSUB>>((int)L::BYTES);
+    int best = 1;
+    for (int c = 2; c <= 8; c++) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(1, 1, (unsigned)c);
+      cfg.blockDim = dim3(TS_THREADS);
+      cfg.dynamicSmemBytes = L::BYTES;
+      cudaLaunchAttribute at[1];
+      at[0].id = cudaLaunchAttributeClusterDimension;
+      at[0].val.clusterDim.x = 1;
+      at[0].val.clusterDim.y = 1;
+      at[0].val.clusterDim.z = (unsigned)c;
+      cfg.attrs = at;
+      cfg.numAttrs = 1;
+      int n = 0;
+      if (cudaOccupancyMaxActiveClusters(&n, nbits_ts_kernel<BT, STAGES, KSUB>, &cfg) == cudaSuccess && n > 0) best = c;
+      else (void)cudaGetLastError();
+    }
+    max_ok.store(best);
+  }
+  return std::max(1, std::min(want, max_ok.load()));
+}
+
+template <int BT, int STAGES, int KSUB>
+void launch_ts_split(const NbitsArgs &a, const __half *a16, int64_t K8, int sms, cudaStream_t s) {
+  launch_ts_t<BT, STAGES, KSUB>(a, a16, K8, ts_splits<BT, STAGES, KSUB>(a, sms), s);
+}
+
+}  // namespace
+
 void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s) {
   const int sms = device_sm_count();
   switch (nbits_ts_pick_bt(a.M, a.N, sms)) {
-    case 256: launch_ts_t<256, 3, 2>(a, a16, K8, s); break;
-    case 192: launch_ts_t<192, 4, 2>(a, a16, K8, s); break;
-    case 128: launch_ts_t<128, 3, 4>(a, a16, K8, s); break;
-    default: launch_ts_t<96, 3, 4>(a, a16, K8, s); break;
+    case 256: launch_ts_split<256, 3, 2>(a, a16, K8, sms, s); break;
+    case 192: launch_ts_split<192, 4, 2>(a, a16, K8, sms, s); break;
+    case 128: launch_ts_split<128, 3, 4>(a, a16, K8, sms, s); break;
+    default: launch_ts_split<96, 3, 4>(a, a16, K8, sms, s); break;
   }
 }
