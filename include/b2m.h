@@ -355,6 +355,17 @@ B2M_API b2m_status b2m_rotary_dev(b2m_ctx *ctx, const float *x, int64_t x_rs, co
 /* past[i] += delta for i < n (int32 device counters of a decode loop). */
 B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta);
 
+/* Serialises a packed weight (its device layouts, as prepacked) into buf, for
+ * an on-disk prepack cache: *needed receives the byte size; with buf NULL
+ * only the size is returned. The blob is tied to this library's
+ * B2M_ABI_VERSION. */
+B2M_API b2m_status b2m_weight_export(const b2m_weight *w, void *buf, size_t capacity, size_t *needed);
+
+/* Recreates a packed weight on ctx's device from a b2m_weight_export blob,
+ * without redoing the host-side layout work. UNSUPPORTED for a blob of
+ * another library version, INVALID_ARGUMENT for a malformed one. */
+B2M_API b2m_status b2m_weight_import(b2m_ctx *ctx, const void *buf, size_t size, b2m_weight **out);
+
 /* Shape of a packed weight: K and N (logical B is [K, N]). */
 B2M_API b2m_status b2m_weight_info(const b2m_weight *w, int64_t *k, int64_t *n);
 

@@ -145,6 +145,8 @@ SIGNATURES = {
     "b2m_rotary_dev": (_i32, [_c_ctx, _vp, _i64, _vp, _i32, _vp, _vp, _i32, _i32, _vp, _i64, _i32, _i32, _i32,
                               _i32, _i32, _i32]),
     "b2m_advance_positions_dev": (_i32, [_c_ctx, _vp, _i32, _i32]),
+    "b2m_weight_export": (_i32, [_c_weight, _vp, ctypes.c_size_t, ctypes.POINTER(ctypes.c_size_t)]),
+    "b2m_weight_import": (_i32, [_c_ctx, _vp, ctypes.c_size_t, ctypes.POINTER(_c_weight)]),
 }
 
 _lib = None

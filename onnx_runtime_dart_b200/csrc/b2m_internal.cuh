@@ -136,10 +136,17 @@ struct I8Weight {
   int64_t k128 = 0;
 };
 
+// Device buffers of a packed weight, for b2m_weight_export / import.
+enum WeightSegment {
+  SEG_F32, SEG_BX_HI, SEG_BX_LO, SEG_I8_BT, SEG_I8_COLSUM, SEG_I8_TS8, SEG_NB_BQ, SEG_NB_SCALES, SEG_NB_ZP_U8,
+  SEG_NB_ZP_F32, SEG_NB_SREC, SEG_NB_TSQ, SEG_NB_TSS, SEG_COUNT
+};
+
 struct b2m_weight {
   b2m_ctx *ctx = nullptr;
   int kind = 0;
   int64_t k = 0, n = 0;
+  size_t seg_bytes[SEG_COUNT] = {0};  // allocation size of each device buffer
   float *f32 = nullptr;  // W_F32: [K][N] row-major
   // W_F32 FAST-mode planes: K-major bf16 [N][roundup(K,64)], hi = rn(w),
   // lo = rn(w - hi).

@@ -829,6 +829,7 @@ B2M_API b2m_status b2m_weight_prepack_f32(b2m_ctx *ctx, const float *host_b, int
     w->k = K;
     w->n = N;
     cudaError_t e = cudaMalloc(&w->f32, (size_t)(K * N * 4));
+    w->seg_bytes[SEG_F32] = (size_t)(K * N * 4);
     if (e != cudaSuccess) {
       (void)cudaGetLastError();
       delete w;
@@ -856,6 +857,8 @@ B2M_API b2m_status b2m_weight_prepack_f32(b2m_ctx *ctx, const float *host_b, int
         delete w;
         b2m_throw(B2M_ERR_OUT_OF_MEMORY, "weight allocation failed");
       }
+      w->seg_bytes[SEG_BX_HI] = hi.size() * 2;
+      w->seg_bytes[SEG_BX_LO] = lo.size() * 2;
       B2M_CUDA(cudaMemcpy(w->bx_hi, hi.data(), hi.size() * 2, cudaMemcpyHostToDevice));
       B2M_CUDA(cudaMemcpy(w->bx_lo, lo.data(), lo.size() * 2, cudaMemcpyHostToDevice));
     }
@@ -904,6 +907,9 @@ B2M_API b2m_status b2m_weight_prepack_i8(b2m_ctx *ctx, const void *host_b, int32
       B2M_CUDA(cudaMalloc(&w->i8.bt, bt.size()));
       B2M_CUDA(cudaMalloc(&w->i8.colsum, cs.size() * 4));
       B2M_CUDA(cudaMalloc(&w->i8.ts8, ts8.size()));
+      w->seg_bytes[SEG_I8_BT] = bt.size();
+      w->seg_bytes[SEG_I8_COLSUM] = cs.size() * 4;
+      w->seg_bytes[SEG_I8_TS8] = ts8.size();
       B2M_CUDA(cudaMemcpy(w->i8.bt, bt.data(), bt.size(), cudaMemcpyHostToDevice));
       B2M_CUDA(cudaMemcpy(w->i8.colsum, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
       B2M_CUDA(cudaMemcpy(w->i8.ts8, ts8.data(), ts8.size(), cudaMemcpyHostToDevice));
@@ -1053,17 +1059,22 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
     W.npad = npad;
     try {
       B2M_CUDA(cudaMalloc(&W.bq, bq.size()));
+      w->seg_bytes[SEG_NB_BQ] = bq.size();
       B2M_CUDA(cudaMemcpy(W.bq, bq.data(), bq.size(), cudaMemcpyHostToDevice));
       B2M_CUDA(cudaMalloc(&W.scales, sc.size() * 4));
+      w->seg_bytes[SEG_NB_SCALES] = sc.size() * 4;
       B2M_CUDA(cudaMemcpy(W.scales, sc.data(), sc.size() * 4, cudaMemcpyHostToDevice));
       if (!srec.empty()) {
         B2M_CUDA(cudaMalloc(&W.srec, srec.size() * sizeof(__half)));
+        w->seg_bytes[SEG_NB_SREC] = srec.size() * sizeof(__half);
         B2M_CUDA(cudaMemcpy(W.srec, srec.data(), srec.size() * sizeof(__half), cudaMemcpyHostToDevice));
       }
       if (!tsq.empty()) {
         B2M_CUDA(cudaMalloc(&W.tsq, tsq.size()));
+        w->seg_bytes[SEG_NB_TSQ] = tsq.size();
         B2M_CUDA(cudaMemcpy(W.tsq, tsq.data(), tsq.size(), cudaMemcpyHostToDevice));
         B2M_CUDA(cudaMalloc(&W.tss, tss.size() * 4));
+        w->seg_bytes[SEG_NB_TSS] = tss.size() * 4;
         B2M_CUDA(cudaMemcpy(W.tss, tss.data(), tss.size() * 4, cudaMemcpyHostToDevice));
       }
       if (zp_dtype == B2M_UINT8) {
@@ -1071,12 +1082,14 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
         std::memcpy(z.data(), zero_points, (size_t)(n * zs));
         W.zp_kind = 1;
         B2M_CUDA(cudaMalloc(&W.zp_u8, z.size()));
+        w->seg_bytes[SEG_NB_ZP_U8] = z.size();
         B2M_CUDA(cudaMemcpy(W.zp_u8, z.data(), z.size(), cudaMemcpyHostToDevice));
       } else if (zp_dtype == B2M_FLOAT) {
         std::vector<float> z((size_t)(npad * nb), 0.f);
         std::memcpy(z.data(), zero_points, (size_t)(n * nb * 4));
         W.zp_kind = 2;
         B2M_CUDA(cudaMalloc(&W.zp_f32, z.size() * 4));
+        w->seg_bytes[SEG_NB_ZP_F32] = z.size() * 4;
         B2M_CUDA(cudaMemcpy(W.zp_f32, z.data(), z.size() * 4, cudaMemcpyHostToDevice));
       }
     } catch (...) {
@@ -1114,6 +1127,146 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     cudaFree(w->nb.tsq);
     cudaFree(w->nb.tss);
     delete w;
+  });
+}
+
+}  // extern "C"
+
+namespace {
+
+// Serialised packed weight: a fixed header, the scalar fields, the byte size
+// of every device buffer, then the buffers in segment order.
+constexpr uint32_t WEIGHT_MAGIC = 0x574d3242u;  // "B2MW"
+constexpr uint32_t WEIGHT_FORMAT = 1;
+constexpr int WEIGHT_FIELDS = 13;
+
+void **segment_slot(b2m_weight *w, int id) {
+  switch (id) {
+    case SEG_F32: return reinterpret_cast<void **>(&w->f32);
+    case SEG_BX_HI: return reinterpret_cast<void **>(&w->bx_hi);
+    case SEG_BX_LO: return reinterpret_cast<void **>(&w->bx_lo);
+    case SEG_I8_BT: return reinterpret_cast<void **>(&w->i8.bt);
+    case SEG_I8_COLSUM: return reinterpret_cast<void **>(&w->i8.colsum);
+    case SEG_I8_TS8: return reinterpret_cast<void **>(&w->i8.ts8);
+    case SEG_NB_BQ: return reinterpret_cast<void **>(&w->nb.bq);
+    case SEG_NB_SCALES: return reinterpret_cast<void **>(&w->nb.scales);
+    case SEG_NB_ZP_U8: return reinterpret_cast<void **>(&w->nb.zp_u8);
+    case SEG_NB_ZP_F32: return reinterpret_cast<void **>(&w->nb.zp_f32);
+    case SEG_NB_SREC: return reinterpret_cast<void **>(&w->nb.srec);
+    case SEG_NB_TSQ: return reinterpret_cast<void **>(&w->nb.tsq);
+    default: return reinterpret_cast<void **>(&w->nb.tss);
+  }
+}
+
+void weight_fields(const b2m_weight *w, int64_t (&f)[WEIGHT_FIELDS]) {
+  const int64_t v[WEIGHT_FIELDS] = {w->k, w->n, w->i8.dtype, w->i8.kpad, w->i8.npad, w->i8.k128, w->nb.zp_kind,
+                                    w->nb.block, w->nb.nblocks, w->nb.zstride, w->nb.kp, w->nb.npad,
+                                    w->nb.f16_scales ? 1 : 0};
+  for (int i = 0; i < WEIGHT_FIELDS; i++) f[i] = v[i];
+}
+
+size_t weight_blob_bytes(const b2m_weight *w) {
+  size_t n = 4 * sizeof(uint32_t) + WEIGHT_FIELDS * sizeof(int64_t) + SEG_COUNT * sizeof(uint64_t);
+  for (int i = 0; i < SEG_COUNT; i++) n += w->seg_bytes[i];
+  return n;
+}
+
+}  // namespace
+
+extern "C" {
+
+B2M_API b2m_status b2m_weight_export(const b2m_weight *w, void *buf, size_t capacity, size_t *needed) {
+  return guarded([&] {
+    B2M_REQUIRE(w && needed, B2M_ERR_INVALID_ARGUMENT, "weight export: null argument");
+    const size_t total = weight_blob_bytes(w);
+    *needed = total;
+    if (!buf) return;
+    B2M_REQUIRE(capacity >= total, B2M_ERR_INVALID_ARGUMENT, "weight export: buffer too small");
+    DeviceGuard dg(w->ctx->device);
+    B2M_CUDA(cudaStreamSynchronize(w->ctx->stream));
+    uint8_t *p = static_cast<uint8_t *>(buf);
+    const uint32_t hdr[4] = {WEIGHT_MAGIC, WEIGHT_FORMAT, (uint32_t)B2M_ABI_VERSION, (uint32_t)w->kind};
+    std::memcpy(p, hdr, sizeof(hdr));
+    p += sizeof(hdr);
+    int64_t f[WEIGHT_FIELDS];
+    weight_fields(w, f);
+    std::memcpy(p, f, sizeof(f));
+    p += sizeof(f);
+    for (int i = 0; i < SEG_COUNT; i++) {
+      const uint64_t b = w->seg_bytes[i];
+      std::memcpy(p, &b, sizeof(b));
+      p += sizeof(b);
+    }
+    for (int i = 0; i < SEG_COUNT; i++) {
+      if (!w->seg_bytes[i]) continue;
+      void *dev = *segment_slot(const_cast<b2m_weight *>(w), i);
+      B2M_REQUIRE(dev, B2M_ERR_CUDA, "weight export: missing device buffer");
+      B2M_CUDA(cudaMemcpy(p, dev, w->seg_bytes[i], cudaMemcpyDeviceToHost));
+      p += w->seg_bytes[i];
+    }
+  });
+}
+
+B2M_API b2m_status b2m_weight_import(b2m_ctx *ctx, const void *buf, size_t size, b2m_weight **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(buf && out, B2M_ERR_INVALID_ARGUMENT, "weight import: null argument");
+    const size_t head = 4 * sizeof(uint32_t) + WEIGHT_FIELDS * sizeof(int64_t) + SEG_COUNT * sizeof(uint64_t);
+    B2M_REQUIRE(size >= head, B2M_ERR_INVALID_ARGUMENT, "weight import: truncated header");
+    const uint8_t *p = static_cast<const uint8_t *>(buf);
+    uint32_t hdr[4];
+    std::memcpy(hdr, p, sizeof(hdr));
+    p += sizeof(hdr);
+    B2M_REQUIRE(hdr[0] == WEIGHT_MAGIC && hdr[1] == WEIGHT_FORMAT, B2M_ERR_INVALID_ARGUMENT,
+                "weight import: not a packed-weight blob");
+    B2M_REQUIRE(hdr[2] == (uint32_t)B2M_ABI_VERSION, B2M_ERR_UNSUPPORTED,
+                "weight import: blob written by another library version");
+    B2M_REQUIRE(hdr[3] == W_F32 || hdr[3] == W_I8 || hdr[3] == W_NBITS, B2M_ERR_INVALID_ARGUMENT,
+                "weight import: unknown weight kind");
+    int64_t f[WEIGHT_FIELDS];
+    std::memcpy(f, p, sizeof(f));
+    p += sizeof(f);
+    uint64_t segb[SEG_COUNT];
+    std::memcpy(segb, p, sizeof(segb));
+    p += sizeof(segb);
+    size_t total = head;
+    for (int i = 0; i < SEG_COUNT; i++) {
+      B2M_REQUIRE(segb[i] <= size, B2M_ERR_INVALID_ARGUMENT, "weight import: bad segment size");
+      total += segb[i];
+    }
+    B2M_REQUIRE(total == size, B2M_ERR_INVALID_ARGUMENT, "weight import: size mismatch");
+    DeviceGuard dg(ctx->device);
+    b2m_weight *w = new b2m_weight();
+    w->ctx = ctx;
+    w->kind = (int)hdr[3];
+    w->k = f[0];
+    w->n = f[1];
+    w->i8.dtype = (int32_t)f[2];
+    w->i8.kpad = f[3];
+    w->i8.npad = f[4];
+    w->i8.k128 = f[5];
+    w->nb.zp_kind = (int)f[6];
+    w->nb.block = (int)f[7];
+    w->nb.nblocks = f[8];
+    w->nb.zstride = f[9];
+    w->nb.kp = f[10];
+    w->nb.npad = f[11];
+    w->nb.f16_scales = f[12] != 0;
+    try {
+      for (int i = 0; i < SEG_COUNT; i++) {
+        if (!segb[i]) continue;
+        void **slot = segment_slot(w, i);
+        B2M_CUDA(cudaMalloc(slot, segb[i]));
+        w->seg_bytes[i] = segb[i];
+        B2M_CUDA(cudaMemcpy(*slot, p, segb[i], cudaMemcpyHostToDevice));
+        p += segb[i];
+      }
+    } catch (...) {
+      for (int i = 0; i < SEG_COUNT; i++) cudaFree(*segment_slot(w, i));
+      delete w;
+      throw;
+    }
+    *out = w;
   });
 }
 
