@@ -72,6 +72,16 @@ def _load():
     lib.orc_matmul_nbits.restype = ctypes.c_int
     lib.orc_nbits_dequant.argtypes = [_u8p, _f32p, _u8p, _f32p, _i64, _i64, _i64, _f32p]
     lib.orc_nbits_dequant.restype = None
+    lib.orc_conv_f32.argtypes = [_f32p, _i64p, ctypes.c_int, _f32p, _i64p, _i64, _f32p, _i64p, _i64p, _i64p, _i64,
+                                 _f32p]
+    lib.orc_conv_f32.restype = ctypes.c_int
+    lib.orc_conv_int_acc.argtypes = [_i32p, _i64, _i64, _i64, _i64, _i32p, _i64, _i64, _i64, _i64, ctypes.c_int32,
+                                     _i32p] + [_i64] * 9 + [_i64p]
+    lib.orc_conv_int_acc.restype = None
+    lib.orc_qlinear_conv_requant.argtypes = [_i64p, _i64, _i64, _i64, ctypes.c_double,
+                                             ctypes.POINTER(ctypes.c_double), _i64, ctypes.c_double, _i64, _i64p,
+                                             _i64, _i64, _i64p]
+    lib.orc_qlinear_conv_requant.restype = None
     _lib = lib
     return lib
 
@@ -239,3 +249,110 @@ def nbits_dequant(b_q, scales, zero_points, k, n, block_size):
     _load().orc_nbits_dequant(_p(bq, _u8p), _p(sc, _f32p), _p(zu, _u8p), _p(zf, _f32p), k, n, block_size,
                               _p(w, _f32p))
     return w.reshape(n, k)
+
+
+# ---------------------------------------------------------------------------
+# Conv / ConvInteger / QLinearConv
+# ---------------------------------------------------------------------------
+
+def resolve_pads(in_sp, kernel, strides, dilations, auto_pad="NOTSET", pads=None):
+    """``_resolvePads`` (lib/src/onnx_nn_ops.dart:38-88) without ceil mode:
+    (pads [begin..., end...], output spatial dims)."""
+    nd = len(in_sp)
+    p, out = [0] * (2 * nd), [0] * nd
+    for k in range(nd):
+        window = dilations[k] * (kernel[k] - 1) + 1
+        if auto_pad in ("SAME_UPPER", "SAME_LOWER"):
+            out[k] = (in_sp[k] + strides[k] - 1) // strides[k]
+            total = max(0, (out[k] - 1) * strides[k] + window - in_sp[k])
+            small = total // 2
+            p[k] = small if auto_pad == "SAME_UPPER" else total - small
+            p[nd + k] = total - p[k]
+        elif auto_pad == "VALID":
+            out[k] = (in_sp[k] - window) // strides[k] + 1
+        else:
+            p[k] = 0 if pads is None else int(pads[k])
+            p[nd + k] = 0 if pads is None else int(pads[nd + k])
+            out[k] = (in_sp[k] + p[k] + p[nd + k] - window) // strides[k] + 1
+    return p, out
+
+
+def conv_f32(x, w, bias=None, strides=None, pads=None, dilations=None, group=1, auto_pad="NOTSET"):
+    """``opConv`` (lib/src/onnx_nn_ops.dart:179-545) outside its Winograd
+    branch: im2col + matmulKernel for 1-D / 2-D, double accumulation for
+    depthwise 2-D and for 3-D."""
+    x = _c(x, np.float32)
+    w = _c(w, np.float32)
+    bias = _c(bias, np.float32)
+    nd = x.ndim - 2
+    kernel = list(w.shape[2:])
+    s = list(strides) if strides is not None else [1] * nd
+    d = list(dilations) if dilations is not None else [1] * nd
+    p, osp = resolve_pads(list(x.shape[2:]), kernel, s, d, auto_pad, pads)
+    out = np.zeros([x.shape[0], w.shape[0]] + osp, np.float32)
+    arr = lambda v: np.array(v, np.int64)
+    xs, ks, ss, ps, ds = arr(x.shape), arr(kernel), arr(s), arr(p), arr(d)
+    rc = _load().orc_conv_f32(_p(x, _f32p), _p(xs, _i64p), nd, _p(w, _f32p), _p(ks, _i64p), w.shape[0],
+                              _p(bias, _f32p), _p(ss, _i64p), _p(ps, _i64p), _p(ds, _i64p), int(group),
+                              _p(out, _f32p))
+    if rc:
+        raise ValueError(f"oracle conv: bad arguments ({rc})")
+    return out
+
+
+def _conv_int(x, w, x_zp, w_zp, strides, pads, dilations, group):
+    """``_convIntAcc`` with opConvInteger's 1-D reshape (:305-320)."""
+    x = np.asarray(x)
+    w = np.asarray(w)
+    if x.ndim == 3:
+        x = x.reshape(x.shape[0], x.shape[1], 1, x.shape[2])
+        w = w.reshape(w.shape[0], w.shape[1], 1, w.shape[2])
+        strides = [1, 1 if strides is None else strides[0]]
+        pads = None if pads is None else [0, pads[0], 0, pads[1]]
+        dilations = [1, 1 if dilations is None else dilations[0]]
+        one_d = True
+    else:
+        one_d = False
+    s = strides or [1, 1]
+    p = pads or [0, 0, 0, 0]
+    d = dilations or [1, 1]
+    m = w.shape[0]
+    osp = [(x.shape[2 + a] + p[a] + p[2 + a] - (d[a] * (w.shape[2 + a] - 1) + 1)) // s[a] + 1 for a in range(2)]
+    wz = np.zeros(m, np.int32) if w_zp is None else np.broadcast_to(
+        np.asarray(w_zp).astype(np.int32).ravel()[:1] if np.asarray(w_zp).size == 1 else
+        np.asarray(w_zp).astype(np.int32).ravel(), (m,)).copy()
+    xz = 0 if x_zp is None else int(np.asarray(x_zp).ravel()[0])
+    xi = np.ascontiguousarray(x, dtype=np.int32)
+    wi = np.ascontiguousarray(w, dtype=np.int32)
+    acc = np.zeros([x.shape[0], m] + osp, np.int64)
+    _load().orc_conv_int_acc(_p(xi, _i32p), x.shape[0], x.shape[1], x.shape[2], x.shape[3], _p(wi, _i32p), m,
+                             w.shape[1], w.shape[2], w.shape[3], xz, _p(wz, _i32p), s[0], s[1], d[0], d[1], p[0],
+                             p[1], int(group), osp[0], osp[1], _p(acc, _i64p))
+    return acc, one_d
+
+
+def conv_integer(x, w, x_zp=None, w_zp=None, strides=None, pads=None, dilations=None, group=1):
+    """``opConvInteger`` (lib/src/onnx_qlinear_ops.dart:305-338): int32-exact
+    accumulators (int64 here, as in the reference)."""
+    if w_zp is not None and np.asarray(w_zp).size not in (1, np.asarray(w).shape[0]):
+        raise NotImplementedError("ConvInteger: weight zero point must be scalar or per-output-channel")
+    acc, one_d = _conv_int(x, w, x_zp, w_zp, strides, pads, dilations, group)
+    return acc.reshape(acc.shape[0], acc.shape[1], acc.shape[3]) if one_d else acc
+
+
+def qlinear_conv(x, x_scale, x_zp, w, w_scale, w_zp, y_scale, y_zp, bias=None, strides=None, pads=None,
+                 dilations=None, group=1, lo=0, hi=255):
+    """``opQLinearConv`` (lib/src/onnx_qlinear_ops.dart:341-382), 2-D."""
+    acc, _ = _conv_int(x, w, x_zp, w_zp, strides, pads, dilations, group)
+    n, m = acc.shape[0], acc.shape[1]
+    spn = int(np.prod(acc.shape[2:]))
+    ws = np.ascontiguousarray(np.asarray(w_scale, np.float32).astype(np.float64).ravel())
+    b = None if bias is None else np.ascontiguousarray(np.asarray(bias).astype(np.int64).ravel())
+    yz = 0 if y_zp is None else int(np.asarray(y_zp).ravel()[0])
+    out = np.zeros(acc.shape, np.int64)
+    acc = np.ascontiguousarray(acc)
+    _load().orc_qlinear_conv_requant(_p(acc, _i64p), n, m, spn, float(np.float32(np.asarray(x_scale).ravel()[0])),
+                                     ws.ctypes.data_as(ctypes.POINTER(ctypes.c_double)), ws.size,
+                                     float(np.float32(np.asarray(y_scale).ravel()[0])), yz, _p(b, _i64p), lo, hi,
+                                     _p(out, _i64p))
+    return out

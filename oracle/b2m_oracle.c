@@ -504,3 +504,211 @@ ORC_API void orc_nbits_dequant(const uint8_t *bq, const float *scales, const uin
   for (int64_t col = 0; col < n; col++)
     for (int64_t kk = 0; kk < k; kk++) w[col * k + kk] = nbits_weight(&g, col, kk);
 }
+
+/* ------------------------------------------------------------------------- */
+/* Conv (opConv, lib/src/onnx_nn_ops.dart:179-545), without the Winograd      */
+/* branch (:241-277), which only the executor selects for initializer 3x3     */
+/* stride-1 kernels with >= 1024 output pixels (:779-812).                    */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * x [n][cin][sp...] with nd = 1..3 spatial dims, w [m][cpg][k...], bias [m]
+ * or NULL, pads resolved (begin[nd], end[nd]), out [n][m][osp...].
+ *
+ * nd == 1 runs as 2-D with a unit height (:200-215). 2-D:
+ *   depthwise (cpg == 1 && m / group == 1): each channel is copied into a
+ *     zero-padded plane and every tap, padding included, accumulates in
+ *     double from the bias (:423-483);
+ *   otherwise im2col in chunks of output rows (chunkRows = (8 << 20) floats /
+ *     (colRows * ow), at least 1, at most oh; :313-323 with the executor's
+ *     workspace rule onnx_graph.dart:1509-1546), matmulKernel(W_g, cols) per
+ *     chunk with the chunk as the call's columns (gemm_column above), then the
+ *     bias added in float32 (:406-418). A pointwise conv reads x directly
+ *     (:293-306); its chunks are addressed here with the channel stride h*w.
+ * 3-D walks the kernel taps in order, skipping taps outside the input, and
+ * accumulates in double from the bias (:485-530).
+ */
+static void conv2d_f32(const float *x, int64_t n, int64_t cin, int64_t h, int64_t wd, const float *w,
+                       int64_t m, int64_t cpg, int64_t kh, int64_t kw, const float *bias, int64_t sh, int64_t sw,
+                       int64_t dh, int64_t dw, int64_t ph, int64_t pw, int64_t pb, int64_t pr, int64_t group,
+                       int64_t oh, int64_t ow, float *out) {
+  const int64_t mpg = m / group;
+  if (cpg == 1 && mpg == 1) {
+    const int64_t hp = h + ph + pb, wp = wd + pw + pr;
+    double *xpad = (double *)malloc(sizeof(double) * (size_t)(hp * wp));
+    for (int64_t b = 0; b < n; b++) {
+      for (int64_t om = 0; om < m; om++) {
+        for (int64_t i = 0; i < hp * wp; i++) xpad[i] = 0.0;
+        const float *xc = x + (b * cin + om) * h * wd;
+        for (int64_t yy = 0; yy < h; yy++)
+          for (int64_t xx = 0; xx < wd; xx++) xpad[(yy + ph) * wp + pw + xx] = (double)xc[yy * wd + xx];
+        const double acc0 = bias ? (double)bias[om] : 0.0;
+        const float *wc = w + om * kh * kw;
+        float *oc = out + (b * m + om) * oh * ow;
+        for (int64_t oy = 0; oy < oh; oy++) {
+          for (int64_t ox = 0; ox < ow; ox++) {
+            double acc = acc0;
+            const int64_t i0 = oy * sh * wp + ox * sw;
+            for (int64_t ky = 0; ky < kh; ky++)
+              for (int64_t kx = 0; kx < kw; kx++) acc += xpad[i0 + ky * dh * wp + kx * dw] * (double)wc[ky * kw + kx];
+            oc[oy * ow + ox] = (float)acc;
+          }
+        }
+      }
+    }
+    free(xpad);
+    return;
+  }
+  const int64_t col_rows = cpg * kh * kw, col_n = oh * ow;
+  int64_t chunk_rows = ((int64_t)8 << 20) / (col_rows * ow);
+  if (chunk_rows < 1) chunk_rows = 1;
+  if (chunk_rows > oh) chunk_rows = oh;
+  float *cols = (float *)malloc(sizeof(float) * (size_t)(col_rows * chunk_rows * ow));
+  for (int64_t b = 0; b < n; b++) {
+    for (int64_t g = 0; g < group; g++) {
+      const float *xg = x + (b * cin + g * cpg) * h * wd;
+      const float *wg = w + g * mpg * col_rows;
+      float *og = out + (b * m + g * mpg) * col_n;
+      for (int64_t row0 = 0; row0 < oh; row0 += chunk_rows) {
+        const int64_t rows = row0 + chunk_rows <= oh ? chunk_rows : oh - row0;
+        const int64_t chunk_n = rows * ow;
+        for (int64_t r = 0; r < col_rows; r++) {
+          const int64_t c = r / (kh * kw), ky = (r / kw) % kh, kx = r % kw;
+          for (int64_t oyl = 0; oyl < rows; oyl++) {
+            const int64_t iy = (row0 + oyl) * sh - ph + ky * dh;
+            for (int64_t ox = 0; ox < ow; ox++) {
+              const int64_t ix = ox * sw - pw + kx * dw;
+              const int inside = iy >= 0 && iy < h && ix >= 0 && ix < wd;
+              cols[r * chunk_n + oyl * ow + ox] = inside ? xg[c * h * wd + iy * wd + ix] : 0.0f;
+            }
+          }
+        }
+        for (int64_t j = 0; j < chunk_n; j++)
+          gemm_column(wg, col_rows, cols, chunk_n, og + row0 * ow, col_n, mpg, col_rows, chunk_n, j);
+      }
+    }
+  }
+  free(cols);
+  if (bias) {
+    for (int64_t b = 0; b < n; b++)
+      for (int64_t om = 0; om < m; om++)
+        for (int64_t k = 0; k < col_n; k++) {
+          float *o = out + (b * m + om) * col_n + k;
+          *o = *o + bias[om];
+        }
+  }
+}
+
+ORC_API int orc_conv_f32(const float *x, const int64_t *xshape, int nd, const float *w, const int64_t *kshape,
+                         int64_t m, const float *bias, const int64_t *strides, const int64_t *pads,
+                         const int64_t *dil, int64_t group, float *out) {
+  if (nd < 1 || nd > 3) return -1;
+  const int64_t n = xshape[0], cin = xshape[1];
+  if (group < 1 || cin % group || m % group) return -2;
+  const int64_t cpg = cin / group, mpg = m / group;
+  int64_t osp[3];
+  for (int a = 0; a < nd; a++) {
+    const int64_t window = dil[a] * (kshape[a] - 1) + 1;
+    osp[a] = (xshape[2 + a] + pads[a] + pads[nd + a] - window) / strides[a] + 1;
+    if (osp[a] < 1) return -3;
+  }
+  if (nd == 1) {
+    conv2d_f32(x, n, cin, 1, xshape[2], w, m, cpg, 1, kshape[0], bias, 1, strides[0], 1, dil[0], 0, pads[0], 0,
+               pads[1], group, 1, osp[0], out);
+    return 0;
+  }
+  if (nd == 2) {
+    conv2d_f32(x, n, cin, xshape[2], xshape[3], w, m, cpg, kshape[0], kshape[1], bias, strides[0], strides[1],
+               dil[0], dil[1], pads[0], pads[1], pads[2], pads[3], group, osp[0], osp[1], out);
+    return 0;
+  }
+  const int64_t in_n = xshape[2] * xshape[3] * xshape[4];
+  const int64_t k_n = kshape[0] * kshape[1] * kshape[2];
+  const int64_t out_n = osp[0] * osp[1] * osp[2];
+  for (int64_t b = 0; b < n; b++) {
+    for (int64_t om = 0; om < m; om++) {
+      const int64_t g = om / mpg;
+      const double acc0 = bias ? (double)bias[om] : 0.0;
+      for (int64_t oi = 0; oi < out_n; oi++) {
+        const int64_t oc[3] = {oi / (osp[1] * osp[2]), (oi / osp[2]) % osp[1], oi % osp[2]};
+        double acc = acc0;
+        for (int64_t c = 0; c < cpg; c++) {
+          const float *xc = x + (b * cin + g * cpg + c) * in_n;
+          const float *wc = w + (om * cpg + c) * k_n;
+          for (int64_t ki = 0; ki < k_n; ki++) {
+            const int64_t kc[3] = {ki / (kshape[1] * kshape[2]), (ki / kshape[2]) % kshape[1], ki % kshape[2]};
+            int64_t off = 0;
+            int inside = 1;
+            for (int a = 0; a < 3; a++) {
+              const int64_t ia = oc[a] * strides[a] - pads[a] + kc[a] * dil[a];
+              if (ia < 0 || ia >= xshape[2 + a]) {
+                inside = 0;
+                break;
+              }
+              off = off * xshape[2 + a] + ia;
+            }
+            if (inside) acc += (double)xc[off] * (double)wc[ki];
+          }
+        }
+        out[(b * m + om) * out_n + oi] = (float)acc;
+      }
+    }
+  }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* ConvInteger / QLinearConv (lib/src/onnx_qlinear_ops.dart:230-382)          */
+/* ------------------------------------------------------------------------- */
+
+/* _convIntAcc (:232-291): acc[n,m,oy,ox] = sum over in-range taps of
+ * (x - xZp)(w - wZp[m]), exact (int64). 2-D; 1-D callers pass h = kh = 1. */
+ORC_API void orc_conv_int_acc(const int32_t *x, int64_t n, int64_t cin, int64_t h, int64_t wd, const int32_t *w,
+                              int64_t m, int64_t cpg, int64_t kh, int64_t kw, int32_t xzp, const int32_t *wzp,
+                              int64_t sh, int64_t sw, int64_t dh, int64_t dw, int64_t ph, int64_t pw, int64_t group,
+                              int64_t oh, int64_t ow, int64_t *out) {
+  const int64_t mpg = m / group;
+  for (int64_t b = 0; b < n; b++) {
+    for (int64_t om = 0; om < m; om++) {
+      const int64_t g = om / mpg;
+      const int64_t wz = wzp[om];
+      for (int64_t oy = 0; oy < oh; oy++) {
+        for (int64_t ox = 0; ox < ow; ox++) {
+          int64_t acc = 0;
+          for (int64_t c = 0; c < cpg; c++) {
+            const int32_t *xc = x + (b * cin + g * cpg + c) * h * wd;
+            const int32_t *wc = w + (om * cpg + c) * kh * kw;
+            for (int64_t ky = 0; ky < kh; ky++) {
+              const int64_t iy = oy * sh - ph + ky * dh;
+              if (iy < 0 || iy >= h) continue;
+              for (int64_t kx = 0; kx < kw; kx++) {
+                const int64_t ix = ox * sw - pw + kx * dw;
+                if (ix < 0 || ix >= wd) continue;
+                acc += (int64_t)(xc[iy * wd + ix] - xzp) * (int64_t)(wc[ky * kw + kx] - wz);
+              }
+            }
+          }
+          out[((b * m + om) * oh + oy) * ow + ox] = acc;
+        }
+      }
+    }
+  }
+}
+
+/* QLinearConv's requantisation (:361-380): mult = xs * ws[om] / ys in double,
+ * q = roundEven((acc + bias[om]) * mult) + yz, clamped to [lo, hi]. */
+ORC_API void orc_qlinear_conv_requant(const int64_t *acc, int64_t n, int64_t m, int64_t spn, double xs,
+                                      const double *ws, int64_t ws_len, double ys, int64_t yz, const int64_t *bias,
+                                      int64_t lo, int64_t hi, int64_t *out) {
+  for (int64_t b = 0; b < n; b++) {
+    for (int64_t om = 0; om < m; om++) {
+      const double mult = xs * ws[ws_len == 1 ? 0 : om] / ys;
+      const int64_t bv = bias ? bias[om] : 0;
+      const int64_t base = (b * m + om) * spn;
+      for (int64_t k = 0; k < spn; k++) {
+        const int64_t q = round_even((double)(acc[base + k] + bv) * mult) + yz;
+        out[base + k] = q < lo ? lo : (q > hi ? hi : q);
+      }
+    }
+  }
+}

@@ -33,6 +33,17 @@ def run_oracle(g):
     if op == "MatMulNBits":
         return oracle.matmul_nbits(x[0], x[1], x[2], x[3] if len(x) > 3 else None, at["K"], at["N"],
                                    at["block_size"], bias=x[5] if len(x) > 5 else None)
+    if op == "Conv":
+        return oracle.conv_f32(x[0], x[1], x[2] if len(x) > 2 else None, at.get("strides"), at.get("pads"),
+                               at.get("dilations"), at.get("group", 1), at.get("auto_pad", "NOTSET"))
+    if op == "ConvInteger":
+        return oracle.conv_integer(x[0], x[1], x[2] if len(x) > 2 else None, x[3] if len(x) > 3 else None,
+                                   at.get("strides"), at.get("pads"), at.get("dilations"), at.get("group", 1))
+    if op == "QLinearConv":
+        int8 = g["inputs"][7]["tensor"]["elem_type"] == 3
+        return oracle.qlinear_conv(x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7], x[8] if len(x) > 8 else None,
+                                   at.get("strides"), at.get("pads"), at.get("dilations"), at.get("group", 1),
+                                   -128 if int8 else 0, 127 if int8 else 255)
     pytest.skip(f"{op} is not a MatMul-family op")
 
 
@@ -190,3 +201,66 @@ def test_glue_oracle_matches_reference_fixture(case):
             assert np.asarray(arr).astype(np.int64).tolist() == want.tolist(), f"{case}:{name}"
         else:
             assert_fixture_close(arr, want, f"{case}:{name}")
+
+
+def _conv_naive_double(x, w, bias, s, p, d, group):
+    """Direct 2-D convolution in float64 (test-only cross-check)."""
+    n, cin, h, wd = x.shape
+    m, cpg, kh, kw = w.shape
+    oh = (h + p[0] + p[2] - (d[0] * (kh - 1) + 1)) // s[0] + 1
+    ow = (wd + p[1] + p[3] - (d[1] * (kw - 1) + 1)) // s[1] + 1
+    xp = np.zeros((n, cin, h + p[0] + p[2], wd + p[1] + p[3]))
+    xp[:, :, p[0]:p[0] + h, p[1]:p[1] + wd] = x
+    out = np.zeros((n, m, oh, ow))
+    mpg = m // group
+    for om in range(m):
+        g = om // mpg
+        for ky in range(kh):
+            for kx in range(kw):
+                patch = xp[:, g * cpg:(g + 1) * cpg, ky * d[0]:ky * d[0] + s[0] * (oh - 1) + 1:s[0],
+                           kx * d[1]:kx * d[1] + s[1] * (ow - 1) + 1:s[1]]
+                out[:, om] += np.einsum("nchw,c->nhw", patch, w[om, :, ky, kx].astype(np.float64))
+        if bias is not None:
+            out[:, om] += bias[om]
+    return out
+
+
+@pytest.mark.parametrize("cfg", [
+    # (n, cin, h, w, m, kh, kw, stride, pad, dil, group)
+    (2, 3, 9, 11, 8, 3, 3, 1, 1, 1, 1),
+    (1, 4, 8, 8, 2, 3, 3, 2, 0, 1, 1),      # m < 4: double tail pixels
+    (1, 6, 7, 9, 6, 3, 2, 1, 1, 2, 3),      # groups, 2 outputs per group
+    (2, 8, 5, 5, 16, 1, 1, 1, 0, 1, 1),     # pointwise
+    (1, 4, 10, 10, 4, 5, 5, 1, 2, 1, 4),    # depthwise
+])
+def test_conv_oracle_vs_float64(cfg):
+    n, cin, h, wd, m, kh, kw, st, pd, dl, grp = cfg
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((n, cin, h, wd)).astype(np.float32)
+    w = (rng.standard_normal((m, cin // grp, kh, kw)) / np.sqrt(cin // grp * kh * kw)).astype(np.float32)
+    b = rng.standard_normal(m).astype(np.float32)
+    got = oracle.conv_f32(x, w, b, [st, st], [pd] * 4, [dl, dl], grp)
+    want = _conv_naive_double(x, w, b, [st, st], [pd] * 4, [dl, dl], grp)
+    assert got.shape == want.shape
+    assert np.max(np.abs(got - want)) <= 1e-5 * max(1.0, np.max(np.abs(want)))
+
+
+def test_conv_oracle_chunking_is_per_row():
+    """Chunking the im2col panel over output rows (onnx_nn_ops.dart:313-323)
+    leaves every element's k order alone: with m >= 4 a conv too large for one
+    chunk equals the row-by-row direct fp32 evaluation in k order."""
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((1, 64, 40, 1100)).astype(np.float32)   # colRows*ow = 576*1100 > (8<<20)/16
+    w = (rng.standard_normal((4, 64, 3, 3)) * 0.05).astype(np.float32)
+    got = oracle.conv_f32(x, w, None, [1, 1], [1, 1, 1, 1], [1, 1], 1)
+    # Reference per element: float acc += float(a*b) in (c, ky, kx) order.
+    xp = np.zeros((64, 42, 1102), np.float32)
+    xp[:, 1:41, 1:1101] = x[0]
+    oy, ox = 17, 1099
+    for om in range(4):
+        acc = np.float32(0)
+        for c in range(64):
+            for ky in range(3):
+                for kx in range(3):
+                    acc = np.float32(acc + np.float32(w[om, c, ky, kx] * xp[c, oy + ky, ox + kx]))
+        assert got[0, om, oy, ox] == acc
