@@ -355,6 +355,71 @@ B2M_API b2m_status b2m_rotary_dev(b2m_ctx *ctx, const float *x, int64_t x_rs, co
 /* past[i] += delta for i < n (int32 device counters of a decode loop). */
 B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_t n, int32_t delta);
 
+/* ---- convolutions through the GEMM cores --------------------------------
+ * The reference's other matmulKernel callers: opConv
+ * (lib/src/onnx_nn_ops.dart:179-545; dispatch lib/src/onnx_graph.dart:2436-2490)
+ * and the integer convolutions opConvInteger / opQLinearConv
+ * (lib/src/onnx_qlinear_ops.dart:230-382; dispatch onnx_graph.dart:2889-2901,
+ * 2935-2956). Each runs as an im2col panel on the device feeding the fp32 or
+ * int8 GEMM kernels above; outputs are NC[D]HW. */
+
+/* auto_pad attribute values (the attribute's strings, _resolvePads
+ * onnx_nn_ops.dart:38-88). */
+#define B2M_AUTO_PAD_NOTSET 0
+#define B2M_AUTO_PAD_SAME_UPPER 1
+#define B2M_AUTO_PAD_SAME_LOWER 2
+#define B2M_AUTO_PAD_VALID 3
+
+/* Conv / ConvInteger / QLinearConv weight [m][C/group][kernel...] (host,
+ * row-major, viewed as m rows of k = C/group * kernel volume) packed as the
+ * GEMM operand: dtype B2M_FLOAT -> an fp32 weight holding W^T [k][m] (the
+ * layout b2m_weight_prepack_f32 makes with trans = 1); B2M_UINT8 / B2M_INT8
+ * -> an int8 weight holding W^T with k zero-padded to a multiple of 16 (so
+ * the tensor-core path takes it). Replaces the per-call weight reads of the
+ * reference's convolutions. */
+B2M_API b2m_status b2m_weight_prepack_conv(b2m_ctx *ctx, const void *host_w, int32_t dtype, int64_t m, int64_t k,
+                                           b2m_weight **out);
+
+/* Conv (opConv): x float [n][C][spatial...] with 1-3 spatial dims, w from
+ * b2m_weight_prepack_conv (B2M_FLOAT), kernel_shape[nd] (the weight's spatial
+ * dims), strides[nd] / dilations[nd] or NULL (all 1), pads[2 nd]
+ * (begin..., end...) or NULL (all 0; ignored unless auto_pad is NOTSET),
+ * group >= 1, bias float[m] or NULL. y: [n][m][out spatial...].
+ * mode EXACT reproduces the reference's arithmetic: the im2col panel times
+ * matmulKernel's per-element k order (double tails for fewer than four
+ * outputs per group), the bias added in float32 afterwards; depthwise 1-D /
+ * 2-D and every 3-D conv accumulate in double from the bias. The reference
+ * switches to Winograd F(2x2, 3x3) for initializer 3x3 stride-1 group-1
+ * convs with >= 1024 output pixels; EXACT follows the im2col arithmetic
+ * there, which the Winograd path only matches within rounding.
+ * mode FAST runs the im2col panel as bf16 split planes through the tcgen05
+ * FAST GEMM (tolerance contract; depthwise and 3-D as in EXACT). */
+B2M_API b2m_status b2m_conv_f32(b2m_ctx *ctx, const b2m_tensor *x, const b2m_weight *w, const b2m_tensor *bias,
+                                const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
+                                const int64_t *dilations, int32_t group, int32_t auto_pad, int32_t mode,
+                                b2m_tensor **y);
+
+/* ConvInteger (opConvInteger): x uint8 / int8 [n][C][W] or [n][C][H][W]
+ * (1-D or 2-D, as the reference), x_zp (first element used) or NULL, w from
+ * b2m_weight_prepack_conv (int8 kinds), w_zp NULL, scalar or per output
+ * channel [m] (else UNSUPPORTED, :322-326), same dtype as the weight. No
+ * auto_pad (the dispatch passes none). y int32 [n][m][out...], exact. */
+B2M_API b2m_status b2m_conv_integer(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *x_zp, const b2m_weight *w,
+                                    const b2m_tensor *w_zp, const int64_t *kernel_shape, const int64_t *strides,
+                                    const int64_t *pads, const int64_t *dilations, int32_t group, b2m_tensor **y);
+
+/* QLinearConv (opQLinearConv), 2-D: ConvInteger's accumulator, then per
+ * output channel q = roundEven((acc + bias) * (x_scale * w_scale[c] /
+ * y_scale)) + y_zp in double, clamped to [lo, hi] (0..255 -> uint8 y,
+ * -128..127 -> int8 y; the reference picks them from y_zp's dtype,
+ * onnx_graph.dart:2936). w_scale: host floats, 1 or m of them; bias int32
+ * [m] or NULL. */
+B2M_API b2m_status b2m_qlinear_conv(b2m_ctx *ctx, const b2m_tensor *x, float x_scale, const b2m_tensor *x_zp,
+                                    const b2m_weight *w, const float *w_scale, int64_t n_w_scale,
+                                    const b2m_tensor *w_zp, float y_scale, int32_t y_zp, const b2m_tensor *bias,
+                                    const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
+                                    const int64_t *dilations, int32_t group, int32_t lo, int32_t hi, b2m_tensor **y);
+
 /* Serialises a packed weight (its device layouts, as prepacked) into buf, for
  * an on-disk prepack cache: *needed receives the byte size; with buf NULL
  * only the size is returned. The blob is tied to this library's

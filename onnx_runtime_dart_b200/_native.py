@@ -52,6 +52,13 @@ class ArgumentError(B2mError, ValueError):
     status = B2M_ERR_INVALID_ARGUMENT
 
 
+class StateError(B2mError):
+    """Dart StateError: the executor's node-level consistency checks (e.g.
+    Conv's kernel_shape against the weight, onnx_graph.dart:2440-2446)."""
+
+    status = B2M_ERR_INVALID_ARGUMENT
+
+
 class UnsupportedError(B2mError, NotImplementedError):
     """Dart UnsupportedError: a valid but unsupported feature."""
 
@@ -117,6 +124,13 @@ SIGNATURES = {
     "b2m_weight_prepack_nbits": (_i32, [_c_ctx, _vp, _vp, _vp, _i32, _i64, _i64, _i32, _i32,
                                         ctypes.POINTER(_c_weight)]),
     "b2m_weight_free": (_i32, [_c_weight]),
+    "b2m_weight_prepack_conv": (_i32, [_c_ctx, _vp, _i32, _i64, _i64, ctypes.POINTER(_c_weight)]),
+    "b2m_conv_f32": (_i32, [_c_ctx, _c_tensor, _c_weight, _c_tensor, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                            ctypes.POINTER(_c_tensor)]),
+    "b2m_conv_integer": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_weight, _c_tensor, _vp, _vp, _vp, _vp, _i32,
+                                ctypes.POINTER(_c_tensor)]),
+    "b2m_qlinear_conv": (_i32, [_c_ctx, _c_tensor, _f32, _c_tensor, _c_weight, _vp, _i64, _c_tensor, _f32, _i32,
+                                _c_tensor, _vp, _vp, _vp, _vp, _i32, _i32, _i32, ctypes.POINTER(_c_tensor)]),
     "b2m_weight_info": (_i32, [_c_weight, _i64p, _i64p]),
     "b2m_matmul_f32": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_weight, _i32, ctypes.POINTER(_c_tensor)]),
     "b2m_gemm_f32": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_weight, _c_tensor, _f32, _f32, _i32, _i32, _i32,

@@ -206,6 +206,50 @@ int64_t f32_tc_kp(int64_t K);
 size_t f32_tc_scratch_bytes(int64_t M, int64_t K);
 bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w);
 void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cudaStream_t s);
+// The same GEMM on operands already split into bf16 planes: A planes (x0 then
+// x1, each [M][f32_tc_kp(K)]) and B planes [b_rows][f32_tc_kp(K)]; p.Y, p.ldy
+// and the Gemm epilogue fields as above. cm_P > 0 selects the channel-major
+// output of a convolution: Y(i, j) at Y[(i / cm_P) * cm_bs + j * cm_P + i % cm_P].
+void launch_f32_tc_planes(const F32GemmArgs &p, const void *b_hi, const void *b_lo, int64_t b_rows,
+                          const void *a_planes, int64_t cm_P, int64_t cm_bs, cudaStream_t s);
+
+// Convolution (Conv / ConvInteger / QLinearConv) as GEMMs over an im2col
+// panel. Geometry with 1-3 spatial dims carried as three (leading unit dims).
+struct ConvGeom {
+  int64_t n = 0, cin = 0, m = 0, group = 1, cpg = 0, mpg = 0;
+  int64_t in[3] = {1, 1, 1};   // D, H, W
+  int64_t k[3] = {1, 1, 1};    // kernel D, H, W
+  int64_t st[3] = {1, 1, 1};   // strides
+  int64_t dil[3] = {1, 1, 1};  // dilations
+  int64_t pad[3] = {0, 0, 0};  // leading pads (the trailing ones only shape the output)
+  int64_t out[3] = {1, 1, 1};  // output D, H, W
+  int64_t K = 0;               // cpg * kernel volume: the GEMM's reduction length
+  int64_t P = 0;               // output pixels per image
+};
+// im2col of group `grp` for images [b0, b0 + nb): fp32 [nb][K][P] (the
+// reference's panel, pixels contiguous), zero at padded taps.
+void launch_conv_im2col_f32(const float *x, const ConvGeom &g, int64_t grp, int64_t b0, int64_t nb, float *cols,
+                            cudaStream_t s);
+// The same panel as rows [nb * P][kp] of bf16 split planes (hi, then lo),
+// pixel-major, k zero-padded to kp (a multiple of 64): the FAST GEMM's A.
+void launch_conv_im2col_planes(const float *x, const ConvGeom &g, int64_t grp, int64_t b0, int64_t nb, int64_t kp,
+                               void *hi, void *lo, cudaStream_t s);
+// int8 / uint8 rows [nb * P][kg] (kg >= K): padded taps and k >= K hold the
+// input zero point (*xzp, or 0), so (x - xzp) vanishes there.
+void launch_conv_im2col_i8(const void *x, const ConvGeom &g, int64_t grp, int64_t b0, int64_t nb, int64_t kg,
+                           const void *xzp, uint8_t *rows, cudaStream_t s);
+// Direct convolution, one output per thread, accumulated in double from the
+// bias over the taps in (c, kd, kh, kw) order and rounded once (the
+// reference's depthwise and N-D paths). wt: [K][m] (the prepacked layout).
+// pad_taps != 0 also adds the zero products of padded taps.
+void launch_conv_direct_double(const float *x, const float *wt, const float *bias, const ConvGeom &g, int pad_taps,
+                               float *y, cudaStream_t s);
+// z [nb * P][mpg] int32 -> y[b][grp * mpg + j][p]: int32 (y32) or, with yq,
+// QLinearConv's requantisation q = roundEven((z + bias) * mult[ch]) + y_zp
+// clamped to [lo, hi] (mult in double, per output channel).
+void launch_conv_scatter(const int32_t *z, const ConvGeom &g, int64_t grp, int64_t b0, int64_t nb, int32_t *y32,
+                         void *yq, const double *mult, const int32_t *bias, int32_t y_zp, int32_t lo, int32_t hi,
+                         cudaStream_t s);
 
 // MatMulNBits
 struct NbitsArgs {

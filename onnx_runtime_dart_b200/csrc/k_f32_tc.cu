@@ -89,6 +89,12 @@ struct FtEpi {
   int64_t c_rs, c_cs;
   int has_beta;
   float beta;
+  // Channel-major output (convolution): when cm_P > 0, row i of the GEMM is
+  // pixel i % cm_P of image i / cm_P, and Y(i, j) lands at
+  // Y[(i / cm_P) * cm_bs + j * cm_P + i % cm_P], the NC[D]HW layout. Lane =
+  // row in TMEM, so each store instruction of a warp writes 32 consecutive
+  // pixels of one channel.
+  int64_t cm_P, cm_bs;
 };
 
 template <int BN, int STAGES, int BK>
@@ -226,6 +232,28 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
           if (lane == 0) mbar_arrive(&acc_empty[buf]);
         }
         if (n0 + c0 >= N || r0 >= M) continue;
+        if (e.cm_P > 0) {
+          const int row = r0 + lane;
+          if (row < M) {
+            const int64_t img = row / e.cm_P, pix = row - img * e.cm_P;
+            float *yb = e.Y + img * e.cm_bs + pix;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+              const int col = n0 + c0 + j;
+              if (col < N) {
+                float tv = __uint_as_float(v[j]);
+                if (e.has_alpha) tv = tv * e.alpha;
+                if (e.C) {
+                  float cv = e.C[(int64_t)col * e.c_cs];
+                  if (e.has_beta) cv = cv * e.beta;
+                  tv = tv + cv;
+                }
+                yb[(int64_t)col * e.cm_P] = tv;
+              }
+            }
+          }
+          continue;
+        }
 #pragma unroll
         for (int j = 0; j < 32; j++) tb[lane * 33 + j] = __uint_as_float(v[j]);
         __syncwarp();
@@ -263,18 +291,6 @@ __global__ void __launch_bounds__(FT_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, L::TMEM_COLS);
   }
-}
-
-// x -> (x0, x1) = (rn_bf16(x), rn_bf16(x - x0)). A finite x whose rounding
-// overflows bf16 keeps its truncation as x0; a non-finite x passes through x0.
-__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &h, __nv_bfloat16 &l) {
-  h = __float2bfloat16_rn(x);
-  float hf = __bfloat162float(h);
-  if (isinf(hf) && isfinite(x)) {
-    h = __float2bfloat16_rz(x);
-    hf = __bfloat162float(h);
-  }
-  l = __float2bfloat16_rn(isfinite(x) ? x - hf : 0.f);
 }
 
 // A[M][K] (row stride lda) -> x0 / x1 bf16 planes [M][Kp] (zero padded to Kp,
@@ -318,13 +334,23 @@ CUtensorMap make_map(const void *base, int64_t rows, int64_t kp, int box_rows, i
   return m;
 }
 
+// B operand planes (K-major bf16 [b_rows][kp]) and the output layout of one
+// launch.
+struct FtOperandB {
+  const void *hi, *lo;
+  int64_t rows;
+  int64_t cm_P = 0, cm_bs = 0;
+};
+
 template <int BN, int STAGES, int BK>
-void launch_ft(const F32GemmArgs &p, const b2m_weight &w, const __nv_bfloat16 *a0, const __nv_bfloat16 *a1,
+void launch_ft(const F32GemmArgs &p, const FtOperandB &b, const __nv_bfloat16 *a0, const __nv_bfloat16 *a1,
                int64_t kp, cudaStream_t s) {
   using L = FtLayout<BN, STAGES, BK>;
   const CUtensorMap t0 = make_map(a0, p.M, kp, FT_BM, BK), t1 = make_map(a1, p.M, kp, FT_BM, BK);
-  const CUtensorMap u0 = make_map(w.bx_hi, w.n, kp, BN, BK), u1 = make_map(w.bx_lo, w.n, kp, BN, BK);
+  const CUtensorMap u0 = make_map(b.hi, b.rows, kp, BN, BK), u1 = make_map(b.lo, b.rows, kp, BN, BK);
   FtEpi e;
+  e.cm_P = b.cm_P;
+  e.cm_bs = b.cm_bs;
   e.Y = p.Y;
   e.ldy = p.ldy;
   e.has_alpha = p.epi == EPI_GEMM ? p.has_alpha : 0;
@@ -363,6 +389,52 @@ bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w) {
          p.epi != EPI_NBITS && p.epi != EPI_NBITS_M1;
 }
 
+namespace {
+
+// Column tile by a makespan model: rounds of tiles over the SMs times the
+// tile width, over a relative mainloop efficiency per width (narrow tiles
+// re-read A more often per flop). 32-k stages keep four or more stages in
+// flight at every width.
+void launch_ft_any(const F32GemmArgs &p, const FtOperandB &b, const __nv_bfloat16 *a0, const __nv_bfloat16 *a1,
+                   int64_t kp, cudaStream_t s) {
+  const int sms = device_sm_count();
+  const int64_t mt = (p.M + FT_BM - 1) / FT_BM;
+  static const int widths[5] = {256, 192, 128, 64, 32};
+  static const double eff[5] = {0.9, 0.88, 0.8, 0.6, 0.4};
+  int best = 0;
+  double best_cost = 0.0;
+  for (int i = 0; i < 5; i++) {
+    const int64_t tiles = mt * ((p.N + widths[i] - 1) / widths[i]);
+    const double cost = (double)((tiles + sms - 1) / sms) * widths[i] / eff[i];
+    if (i == 0 || cost < best_cost) {
+      best = i;
+      best_cost = cost;
+    }
+  }
+  switch (widths[best]) {
+    case 256: launch_ft<256, 4, 32>(p, b, a0, a1, kp, s); break;
+    case 192: launch_ft<192, 5, 32>(p, b, a0, a1, kp, s); break;
+    case 128: launch_ft<128, 6, 32>(p, b, a0, a1, kp, s); break;
+    case 64: launch_ft<64, 8, 32>(p, b, a0, a1, kp, s); break;
+    default: launch_ft<32, 8, 32>(p, b, a0, a1, kp, s); break;
+  }
+}
+
+}  // namespace
+
+void launch_f32_tc_planes(const F32GemmArgs &p, const void *b_hi, const void *b_lo, int64_t b_rows,
+                          const void *a_planes, int64_t cm_P, int64_t cm_bs, cudaStream_t s) {
+  const int64_t kp = f32_tc_kp(p.K);
+  const __nv_bfloat16 *a0 = static_cast<const __nv_bfloat16 *>(a_planes), *a1 = a0 + p.M * kp;
+  FtOperandB b;
+  b.hi = b_hi;
+  b.lo = b_lo;
+  b.rows = b_rows;
+  b.cm_P = cm_P;
+  b.cm_bs = cm_bs;
+  launch_ft_any(p, b, a0, a1, kp, s);
+}
+
 void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cudaStream_t s) {
   const int64_t kp = f32_tc_kp(p.K);
   __nv_bfloat16 *a0 = static_cast<__nv_bfloat16 *>(a_split), *a1 = a0 + p.M * kp;
@@ -379,29 +451,9 @@ void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cud
     cfg.numAttrs = 1;
     B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_split_rows, p.A, p.sa_m, a0, a1, p.M, p.K, kp));
   }
-  // Column tile by a makespan model: rounds of tiles over the SMs times the
-  // tile width, over a relative mainloop efficiency per width (narrow tiles
-  // re-read A more often per flop). 32-k stages keep four or more stages in
-  // flight at every width.
-  const int sms = device_sm_count();
-  const int64_t mt = (p.M + FT_BM - 1) / FT_BM;
-  static const int widths[5] = {256, 192, 128, 64, 32};
-  static const double eff[5] = {0.9, 0.88, 0.8, 0.6, 0.4};
-  int best = 0;
-  double best_cost = 0.0;
-  for (int i = 0; i < 5; i++) {
-    const int64_t tiles = mt * ((p.N + widths[i] - 1) / widths[i]);
-    const double cost = (double)((tiles + sms - 1) / sms) * widths[i] / eff[i];
-    if (i == 0 || cost < best_cost) {
-      best = i;
-      best_cost = cost;
-    }
-  }
-  switch (widths[best]) {
-    case 256: launch_ft<256, 4, 32>(p, w, a0, a1, kp, s); break;
-    case 192: launch_ft<192, 5, 32>(p, w, a0, a1, kp, s); break;
-    case 128: launch_ft<128, 6, 32>(p, w, a0, a1, kp, s); break;
-    case 64: launch_ft<64, 8, 32>(p, w, a0, a1, kp, s); break;
-    default: launch_ft<32, 8, 32>(p, w, a0, a1, kp, s); break;
-  }
+  FtOperandB b;
+  b.hi = w.bx_hi;
+  b.lo = w.bx_lo;
+  b.rows = w.n;
+  launch_ft_any(p, b, a0, a1, kp, s);
 }

@@ -58,8 +58,11 @@ __global__ void __launch_bounds__(256) i8_gemm_kernel(const I8GemmArgs p, const 
         }
       }
       As[r][w] = v;
-      const int64_t gj = n0 + r;  // packed B rows are zero-padded to npad x kpad
-      Bs[r][w] = *reinterpret_cast<const uint32_t *>(Bt + gj * p.kpad + k0 + w * 4);
+      // Packed B rows are zero-padded to npad x kpad; a column slice of a
+      // packed weight (a convolution group) may end before its last tile, so
+      // rows past N read as zero.
+      const int64_t gj = n0 + r;
+      Bs[r][w] = gj < p.N ? *reinterpret_cast<const uint32_t *>(Bt + gj * p.kpad + k0 + w * 4) : 0u;
     }
     __syncthreads();
 #pragma unroll

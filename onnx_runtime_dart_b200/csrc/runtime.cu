@@ -1581,3 +1581,371 @@ B2M_API b2m_status b2m_advance_positions_dev(b2m_ctx *ctx, int32_t *past, int32_
     launch_advance_positions(past, n, delta, ctx->stream);
   });
 }
+
+// ---------------------------------------------------------------------------
+// Conv / ConvInteger / QLinearConv: im2col panels on the device feeding the
+// fp32 and int8 GEMM kernels (opConv, lib/src/onnx_nn_ops.dart:179-545;
+// opConvInteger / opQLinearConv, lib/src/onnx_qlinear_ops.dart:230-382).
+// ---------------------------------------------------------------------------
+
+namespace {
+
+// Bytes of im2col panel (or GEMM output) one pass may hold; images beyond it
+// run in further passes over the same scratch.
+constexpr int64_t CONV_PANEL_BYTES = (int64_t)512 << 20;
+
+// Spatial attributes of one call, resolved as _resolvePads
+// (onnx_nn_ops.dart:38-88, no ceil mode) into a ConvGeom.
+ConvGeom conv_geometry(const b2m_tensor *x, int64_t m, int64_t wk, const int64_t *kernel_shape,
+                       const int64_t *strides, const int64_t *pads, const int64_t *dilations, int32_t group,
+                       int32_t auto_pad, const char *op) {
+  const int nd = x->rank - 2;
+  B2M_REQUIRE(kernel_shape, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": kernel_shape is required");
+  B2M_REQUIRE(group >= 1, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": group must be >= 1");
+  B2M_REQUIRE(auto_pad >= B2M_AUTO_PAD_NOTSET && auto_pad <= B2M_AUTO_PAD_VALID, B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + ": bad auto_pad");
+  ConvGeom g;
+  g.n = x->shape[0];
+  g.cin = x->shape[1];
+  g.m = m;
+  g.group = group;
+  int64_t kvol = 1;
+  for (int a = 0; a < nd; a++) {
+    B2M_REQUIRE(kernel_shape[a] >= 1, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": bad kernel_shape");
+    kvol *= kernel_shape[a];
+  }
+  B2M_REQUIRE(wk % kvol == 0, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": weight does not match kernel_shape");
+  g.cpg = wk / kvol;
+  B2M_REQUIRE(g.cin == g.cpg * group, B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + " channel mismatch: input C=" + std::to_string(g.cin) +
+                  ", weight C/g=" + std::to_string(g.cpg) + ", group=" + std::to_string(group));
+  B2M_REQUIRE(m % group == 0, B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + ": output channels " + std::to_string(m) + " not divisible by group");
+  g.mpg = m / group;
+  g.K = wk;
+  g.P = 1;
+  const int off = 3 - nd;  // spatial axis a of the call is axis off + a of the geometry
+  for (int a = 0; a < nd; a++) {
+    const int64_t in = x->shape[2 + a], k = kernel_shape[a];
+    const int64_t s = strides ? strides[a] : 1, d = dilations ? dilations[a] : 1;
+    B2M_REQUIRE(s >= 1 && d >= 1, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": strides / dilations must be >= 1");
+    const int64_t window = d * (k - 1) + 1;
+    int64_t pb = 0, out = 0;
+    if (auto_pad == B2M_AUTO_PAD_SAME_UPPER || auto_pad == B2M_AUTO_PAD_SAME_LOWER) {
+      out = (in + s - 1) / s;
+      const int64_t total = std::max<int64_t>(0, (out - 1) * s + window - in);
+      const int64_t small = total / 2;
+      pb = auto_pad == B2M_AUTO_PAD_SAME_UPPER ? small : total - small;
+    } else if (auto_pad == B2M_AUTO_PAD_VALID) {
+      out = in >= window ? (in - window) / s + 1 : 0;
+    } else {
+      pb = pads ? pads[a] : 0;
+      const int64_t pe = pads ? pads[nd + a] : 0;
+      B2M_REQUIRE(pb >= 0 && pe >= 0, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": pads must be >= 0");
+      const int64_t span = in + pb + pe - window;
+      out = span >= 0 ? span / s + 1 : 0;
+    }
+    B2M_REQUIRE(out >= 1, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": empty output along a spatial axis");
+    g.in[off + a] = in;
+    g.k[off + a] = k;
+    g.st[off + a] = s;
+    g.dil[off + a] = d;
+    g.pad[off + a] = pb;
+    g.out[off + a] = out;
+    g.P *= out;
+  }
+  const int64_t lim = INT32_MAX;
+  B2M_REQUIRE(g.K < lim && g.P < lim && g.cin < lim && g.m < lim && g.in[0] * g.in[1] * g.in[2] < lim,
+              B2M_ERR_UNSUPPORTED, std::string(op) + ": dimensions beyond 2^31");
+  return g;
+}
+
+std::vector<int64_t> conv_out_shape(const ConvGeom &g, int nd) {
+  std::vector<int64_t> s = {g.n, g.m};
+  for (int a = 3 - nd; a < 3; a++) s.push_back(g.out[a]);
+  return s;
+}
+
+// Images per pass so that `bytes_per_image` x images stays within the panel
+// budget (at least one).
+int64_t images_per_pass(const ConvGeom &g, int64_t bytes_per_image, int64_t max_rows_per_image = 0) {
+  int64_t nb = std::max<int64_t>(1, CONV_PANEL_BYTES / std::max<int64_t>(1, bytes_per_image));
+  if (max_rows_per_image > 0) nb = std::min<int64_t>(nb, std::max<int64_t>(1, ((int64_t)1 << 21) / max_rows_per_image));
+  return std::min<int64_t>(nb, g.n);
+}
+
+void conv_f32_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_weight *w, const b2m_tensor *bias,
+                   const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads, const int64_t *dilations,
+                   int32_t group, int32_t auto_pad, int32_t mode, b2m_tensor **y) {
+  require_float(x, "Conv input");
+  B2M_REQUIRE(x->rank >= 3 && x->rank <= 5, B2M_ERR_UNSUPPORTED,
+              "Conv supports 1-3 spatial dims, got rank " + std::to_string(x->rank));
+  B2M_REQUIRE(w && w->kind == W_F32, B2M_ERR_INVALID_ARGUMENT, "Conv: w is not an fp32 conv weight");
+  B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT, "Conv: bad mode");
+  const int nd = x->rank - 2;
+  const ConvGeom g = conv_geometry(x, w->n, w->k, kernel_shape, strides, pads, dilations, group, auto_pad, "Conv");
+  if (bias) {
+    require_float(bias, "Conv bias");
+    B2M_REQUIRE(bias->numel == g.m, B2M_ERR_INVALID_ARGUMENT, "Conv: bias must have one value per output channel");
+  }
+  check_cancel(ctx);
+  b2m_tensor *out = prepare_output(ctx, y, B2M_FLOAT, conv_out_shape(g, nd));
+  if (out->numel == 0) return;
+  OpTimer timer(ctx);
+  const float *xd = static_cast<const float *>(x->data);
+  const float *bd = bias ? static_cast<const float *>(bias->data) : nullptr;
+  float *yd = static_cast<float *>(out->data);
+  // The reference's direct double paths: depthwise 1-D / 2-D (padded taps
+  // included, onnx_nn_ops.dart:423-483) and every 3-D conv (:485-530).
+  const bool depthwise = nd <= 2 && g.cpg == 1 && g.mpg == 1;
+  if (nd == 3 || depthwise) {
+    launch_conv_direct_double(xd, w->f32, bd, g, depthwise ? 1 : 0, yd, ctx->stream);
+    timer.done();
+    return;
+  }
+  const int64_t plane = g.in[0] * g.in[1] * g.in[2];
+  if (mode == B2M_MODE_FAST && w->bx_hi) {
+    const int64_t kp = f32_tc_kp(g.K);
+    const int64_t nb = images_per_pass(g, g.P * kp * 4, g.P);
+    Scratch sc(ctx, (size_t)(nb * g.P * kp * 4) + 512);
+    void *planes = sc.take((size_t)(nb * g.P * kp * 4));
+    const uint16_t *hi_planes = w->bx_hi, *lo_planes = w->bx_lo;
+    for (int64_t b0 = 0; b0 < g.n; b0 += nb) {
+      const int64_t cnt = std::min(nb, g.n - b0);
+      for (int64_t grp = 0; grp < g.group; grp++) {
+        void *hi = planes;
+        void *lo = static_cast<uint16_t *>(planes) + cnt * g.P * kp;
+        launch_conv_im2col_planes(xd, g, grp, b0, cnt, kp, hi, lo, ctx->stream);
+        F32GemmArgs p;
+        p.M = cnt * g.P;
+        p.N = g.mpg;
+        p.K = g.K;
+        p.Y = yd + (b0 * g.m + grp * g.mpg) * g.P;
+        p.ldy = g.P;
+        p.epi = EPI_GEMM;
+        if (bd) {
+          p.C = bd + grp * g.mpg;
+          p.c_rs = 0;
+          p.c_cs = 1;
+        }
+        p.dev_err = ctx->dev_err;
+        launch_f32_tc_planes(p, hi_planes + grp * g.mpg * kp, lo_planes + grp * g.mpg * kp, g.mpg, planes, g.P,
+                             g.m * g.P, ctx->stream);
+      }
+    }
+    timer.done();
+    return;
+  }
+  // EXACT: Y_g[mpg][P] = W_g[mpg][K] . panel[K][P] per image, the reference's
+  // matmulKernel(W_g, cols) with the chunk of output rows as the call's
+  // columns (chunkRows = (8 << 20) floats / (K * ow), onnx_nn_ops.dart:313-323),
+  // then the bias in float32 (:406-418).
+  const int64_t ow = g.out[2], oh = g.out[1] * g.out[0];
+  const int64_t chunk_rows = std::min<int64_t>(oh, std::max<int64_t>(1, ((int64_t)8 << 20) / (g.K * ow)));
+  const bool pointwise = nd <= 2 && g.K == g.cpg && g.st[1] == 1 && g.st[2] == 1 && g.pad[1] == 0 &&
+                         g.pad[2] == 0 && g.out[1] == g.in[1] && g.out[2] == g.in[2];
+  const int64_t nb = pointwise ? g.n : std::min<int64_t>(images_per_pass(g, g.K * g.P * 4), 65535);
+  Scratch sc(ctx, pointwise ? 0 : (size_t)(nb * g.K * g.P * 4) + 256);
+  float *cols = pointwise ? nullptr : static_cast<float *>(sc.take((size_t)(nb * g.K * g.P * 4)));
+  for (int64_t b0 = 0; b0 < g.n; b0 += nb) {
+    const int64_t cnt = std::min(nb, g.n - b0);
+    for (int64_t grp = 0; grp < g.group; grp++) {
+      F32GemmArgs p;
+      p.A = w->f32 + grp * g.mpg;  // W_g(i, k) = W^T[k][grp * mpg + i]
+      p.sa_m = 1;
+      p.sa_k = g.m;
+      if (pointwise) {
+        p.B = xd + (b0 * g.cin + grp * g.cpg) * plane;
+        p.b_bstride[0] = g.cin * plane;
+      } else {
+        launch_conv_im2col_f32(xd, g, grp, b0, cnt, cols, ctx->stream);
+        p.B = cols;
+        p.b_bstride[0] = g.K * g.P;
+      }
+      p.sb_k = g.P;
+      p.sb_n = 1;
+      p.Y = yd + (b0 * g.m + grp * g.mpg) * g.P;
+      p.ldy = g.P;
+      p.M = g.mpg;
+      p.N = g.P;
+      p.K = g.K;
+      p.nbd = 1;
+      p.bdims[0] = cnt;
+      p.a_bstride[0] = 0;
+      p.y_bstride = g.m * g.P;
+      p.batch = cnt;
+      p.m_eff = g.mpg;
+      p.tile_w = chunk_rows * ow;
+      p.epi = EPI_GEMM;
+      if (bd) {
+        p.C = bd + grp * g.mpg;
+        p.c_rs = 1;
+        p.c_cs = 0;
+      }
+      p.dev_err = ctx->dev_err;
+      launch_f32_exact(p, ctx->stream);
+    }
+  }
+  timer.done();
+}
+
+void conv_int_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *xzp, const b2m_weight *w,
+                   const b2m_tensor *wzp, const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
+                   const int64_t *dilations, int32_t group, bool requant, double xs, const float *ws, int64_t nws,
+                   double ys, int32_t yzp, const b2m_tensor *bias, int32_t lo, int32_t hi, b2m_tensor **y) {
+  const char *op = requant ? "QLinearConv" : "ConvInteger";
+  B2M_REQUIRE(x && is_i8(x->dtype), B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": x must be uint8 or int8");
+  if (requant)
+    B2M_REQUIRE(x->rank == 4, B2M_ERR_UNSUPPORTED, "QLinearConv implemented for 2-D convs");
+  else
+    B2M_REQUIRE(x->rank == 3 || x->rank == 4, B2M_ERR_UNSUPPORTED, "ConvInteger implemented for 1-D/2-D convs");
+  B2M_REQUIRE(w && w->kind == W_I8, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": w is not an int8 conv weight");
+  const int nd = x->rank - 2;
+  int64_t kvol = 1;
+  B2M_REQUIRE(kernel_shape, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": kernel_shape is required");
+  for (int a = 0; a < nd; a++) kvol *= std::max<int64_t>(1, kernel_shape[a]);
+  B2M_REQUIRE(group >= 1 && x->shape[1] % group == 0, B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + ": input channels not divisible by group");
+  const int64_t K = x->shape[1] / group * kvol;
+  B2M_REQUIRE(w->k == K || w->k == round_up(K, 16), B2M_ERR_INVALID_ARGUMENT,
+              std::string(op) + ": weight does not match the input channels and kernel_shape");
+  const ConvGeom g = conv_geometry(x, w->n, K, kernel_shape, strides, pads, dilations, group, B2M_AUTO_PAD_NOTSET, op);
+  if (wzp && wzp->numel != 1 && wzp->numel != g.m)
+    b2m_throw(B2M_ERR_UNSUPPORTED, "ConvInteger: weight zero point must be scalar or per-output-channel");
+  if (wzp) B2M_REQUIRE(wzp->dtype == w->i8.dtype, B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": w_zero_point dtype");
+  if (xzp) B2M_REQUIRE(xzp->dtype == x->dtype && xzp->numel >= 1, B2M_ERR_INVALID_ARGUMENT,
+                       std::string(op) + ": x_zero_point dtype");
+  B2M_REQUIRE(w->k <= 33025, B2M_ERR_UNSUPPORTED, std::string(op) + ": a reduction beyond 33025 may leave int32");
+  int32_t odt = B2M_INT32;
+  if (requant) {
+    B2M_REQUIRE((lo == 0 && hi == 255) || (lo == -128 && hi == 127), B2M_ERR_INVALID_ARGUMENT,
+                "QLinearConv: lo/hi must be [0,255] or [-128,127]");
+    B2M_REQUIRE(ws && (nws == 1 || nws == g.m), B2M_ERR_INVALID_ARGUMENT,
+                "QLinearConv: w_scale must have 1 or M values");
+    if (bias)
+      B2M_REQUIRE(bias->dtype == B2M_INT32 && bias->numel == g.m, B2M_ERR_INVALID_ARGUMENT,
+                  "QLinearConv: bias must be int32 with one value per output channel");
+    odt = lo == 0 ? B2M_UINT8 : B2M_INT8;
+  }
+  check_cancel(ctx);
+  b2m_tensor *out = prepare_output(ctx, y, odt, conv_out_shape(g, nd));
+  if (out->numel == 0) return;
+  OpTimer timer(ctx);
+  const int64_t kg = w->k;
+  const int64_t nb = images_per_pass(g, g.P * (kg + 4 * g.mpg + 4), g.P);
+  const size_t rows_b = (size_t)(nb * g.P * kg), z_b = (size_t)(nb * g.P * g.mpg * 4), rs_b = (size_t)(nb * g.P * 4);
+  const size_t mult_b = requant ? (size_t)g.m * 8 : 0;
+  Scratch sc(ctx, rows_b + z_b + rs_b + mult_b + 4 * 256);
+  uint8_t *rows = static_cast<uint8_t *>(sc.take(rows_b));
+  int32_t *z = static_cast<int32_t *>(sc.take(z_b));
+  int32_t *rowsum = static_cast<int32_t *>(sc.take(rs_b));
+  double *mult = nullptr;
+  if (requant) {
+    // mult = x_scale * w_scale[c] / y_scale in double (onnx_qlinear_ops.dart:370).
+    std::vector<double> hm((size_t)g.m);
+    for (int64_t c = 0; c < g.m; c++) hm[(size_t)c] = xs * (double)ws[nws == 1 ? 0 : c] / ys;
+    mult = static_cast<double *>(sc.take(mult_b));
+    B2M_CUDA(cudaMemcpyAsync(mult, hm.data(), mult_b, cudaMemcpyHostToDevice, ctx->stream));
+    B2M_CUDA(cudaStreamSynchronize(ctx->stream));  // hm leaves scope below
+  }
+  const bool per_channel = wzp && wzp->numel == g.m && g.m != 1;
+  for (int64_t b0 = 0; b0 < g.n; b0 += nb) {
+    const int64_t cnt = std::min(nb, g.n - b0);
+    for (int64_t grp = 0; grp < g.group; grp++) {
+      launch_conv_im2col_i8(x->data, g, grp, b0, cnt, kg, xzp ? xzp->data : nullptr, rows, ctx->stream);
+      I8GemmArgs p;
+      p.A = rows;
+      p.a_signed = x->dtype == B2M_INT8;
+      p.Bt = w->i8.bt + grp * g.mpg * w->i8.kpad;
+      p.b_signed = w->i8.dtype == B2M_INT8;
+      p.kpad = w->i8.kpad;
+      p.colsum = w->i8.colsum + grp * g.mpg;
+      if (xzp) {
+        p.azp = xzp->data;
+        p.azp_len = 1;
+        p.azp_signed = xzp->dtype == B2M_INT8;
+      }
+      if (wzp) {
+        p.bzp = static_cast<const uint8_t *>(wzp->data) + (per_channel ? grp * g.mpg : 0);
+        p.bzp_len = per_channel ? g.mpg : 1;
+        p.bzp_signed = wzp->dtype == B2M_INT8;
+      }
+      p.M = cnt * g.P;
+      p.N = g.mpg;
+      p.K = kg;
+      p.batch = 1;
+      p.Y32 = z;
+      p.rowsum = rowsum;
+      p.dev_err = ctx->dev_err;
+      const bool done = g.group == 1 && launch_i8_tc(p, w->i8, ctx->stream);
+      if (!done) launch_i8_gemm(p, ctx->stream);
+      launch_conv_scatter(z, g, grp, b0, cnt, requant ? nullptr : static_cast<int32_t *>(out->data),
+                          requant ? out->data : nullptr, mult, bias ? static_cast<const int32_t *>(bias->data) : nullptr,
+                          yzp, lo, hi, ctx->stream);
+    }
+  }
+  timer.done();
+}
+
+}  // namespace
+
+extern "C" {
+
+B2M_API b2m_status b2m_weight_prepack_conv(b2m_ctx *ctx, const void *host_w, int32_t dtype, int64_t m, int64_t k,
+                                           b2m_weight **out) {
+  if (dtype == B2M_FLOAT) return b2m_weight_prepack_f32(ctx, static_cast<const float *>(host_w), m, k, 1, out);
+  b2m_status st = guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && host_w && m > 0 && k > 0, B2M_ERR_INVALID_ARGUMENT, "Conv prepack: bad arguments");
+    B2M_REQUIRE(is_i8(dtype), B2M_ERR_INVALID_ARGUMENT, "Conv prepack: dtype must be float, uint8 or int8");
+  });
+  if (st != B2M_OK) return st;
+  // W [m][k] -> W^T [kg][m], k zero-padded to a multiple of 16.
+  const int64_t kg = (k + 15) / 16 * 16;
+  std::vector<uint8_t> bt;
+  st = guarded([&] {
+    bt.assign((size_t)(kg * m), 0);
+    const uint8_t *src = static_cast<const uint8_t *>(host_w);
+    for (int64_t j = 0; j < m; j++)
+      for (int64_t kk = 0; kk < k; kk++) bt[(size_t)(kk * m + j)] = src[j * k + kk];
+  });
+  if (st != B2M_OK) return st;
+  return b2m_weight_prepack_i8(ctx, bt.data(), dtype, kg, m, out);
+}
+
+B2M_API b2m_status b2m_conv_f32(b2m_ctx *ctx, const b2m_tensor *x, const b2m_weight *w, const b2m_tensor *bias,
+                                const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
+                                const int64_t *dilations, int32_t group, int32_t auto_pad, int32_t mode,
+                                b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    conv_f32_impl(ctx, x, w, bias, kernel_shape, strides, pads, dilations, group, auto_pad, mode, y);
+  });
+}
+
+B2M_API b2m_status b2m_conv_integer(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *x_zp, const b2m_weight *w,
+                                    const b2m_tensor *w_zp, const int64_t *kernel_shape, const int64_t *strides,
+                                    const int64_t *pads, const int64_t *dilations, int32_t group, b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    conv_int_impl(ctx, x, x_zp, w, w_zp, kernel_shape, strides, pads, dilations, group, false, 0.0, nullptr, 0, 0.0,
+                  0, nullptr, 0, 0, y);
+  });
+}
+
+B2M_API b2m_status b2m_qlinear_conv(b2m_ctx *ctx, const b2m_tensor *x, float x_scale, const b2m_tensor *x_zp,
+                                    const b2m_weight *w, const float *w_scale, int64_t n_w_scale,
+                                    const b2m_tensor *w_zp, float y_scale, int32_t y_zp, const b2m_tensor *bias,
+                                    const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
+                                    const int64_t *dilations, int32_t group, int32_t lo, int32_t hi, b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    conv_int_impl(ctx, x, x_zp, w, w_zp, kernel_shape, strides, pads, dilations, group, true, (double)x_scale,
+                  w_scale, n_w_scale, (double)y_scale, y_zp, bias, lo, hi, y);
+  });
+}
+
+}  // extern "C"

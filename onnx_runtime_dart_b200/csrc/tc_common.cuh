@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include <atomic>
 
@@ -48,6 +49,19 @@ void set_smem_limit_once(int bytes) {
   if (done.load(std::memory_order_acquire) & bit) return;
   B2M_CUDA(cudaFuncSetAttribute(Kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
   done.fetch_or(bit, std::memory_order_acq_rel);
+}
+
+// x -> (x0, x1) = (rn_bf16(x), rn_bf16(x - x0)), the two-term split of the
+// FAST fp32 GEMM's operands. A finite x whose rounding overflows bf16 keeps
+// its truncation as x0; a non-finite x passes through x0.
+__device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &h, __nv_bfloat16 &l) {
+  h = __float2bfloat16_rn(x);
+  float hf = __bfloat162float(h);
+  if (isinf(hf) && isfinite(x)) {
+    h = __float2bfloat16_rz(x);
+    hf = __bfloat162float(h);
+  }
+  l = __float2bfloat16_rn(isfinite(x) ? x - hf : 0.f);
 }
 
 // SM count of the current device, cached.

@@ -8,6 +8,9 @@ reference's cases line for line:
   'MatMulInteger' onnx_graph.dart:2880-2888
   'QLinearMatMul' onnx_graph.dart:2902-2917  (lo/hi from y_zero_point's elem type)
   'MatMulNBits'   onnx_graph.dart:2918-2934  (g_idx rejected)
+  'Conv'          onnx_graph.dart:2436-2490  (kernel_shape checked against the weight)
+  'ConvInteger'   onnx_graph.dart:2889-2901
+  'QLinearConv'   onnx_graph.dart:2935-2956  (lo/hi from y_zero_point's elem type)
 Initializer weights are prepacked on first use and cached by initializer name
 (the reference's `_prepackedGemmB`, onnx_graph.dart:102-105); the graph itself
 is unchanged. Ops outside the family return None, leaving the reference's own
@@ -23,7 +26,8 @@ from .runtime import Context, DeviceTensor
 
 
 class GpuDispatch:
-    HANDLED = ("MatMul", "Gemm", "MatMulInteger", "QLinearMatMul", "MatMulNBits")
+    HANDLED = ("MatMul", "Gemm", "MatMulInteger", "QLinearMatMul", "MatMulNBits", "Conv", "ConvInteger",
+               "QLinearConv")
 
     def __init__(self, ctx: Context, initializers: dict, initializer_elem_types: dict | None = None,
                  f32_mode: int = ops.MODE_EXACT, nbits_mode: int = ops.MODE_FAST):
@@ -86,6 +90,8 @@ class GpuDispatch:
                 b = self._packed_for(("i8", input_names[3]), lambda: ctx.prepack_i8(np.asarray(b)))
             return [ops.opQLinearMatMul(need(0), need(1), opt(2), b, need(4), opt(5), need(6), opt(7),
                                         lo=-128 if int8 else 0, hi=127 if int8 else 255, ctx=ctx)]
+        if op_type in ("Conv", "ConvInteger", "QLinearConv"):
+            return [self._conv(op_type, input_names, need, opt, attrs)]
         # MatMulNBits
         if len(input_names) > 4 and input_names[4]:
             raise N.UnsupportedError("MatMulNBits: g_idx input not supported")
@@ -107,3 +113,25 @@ class GpuDispatch:
             w = ops.prepack_nbits(ctx, need(1), need(2), zp, k=k, n=n, bits=bits, blockSize=block)
         return [ops.opMatMulNBits(a, w, k=k, n=n, bits=bits, blockSize=block, bias=bias, mode=self.nbits_mode,
                                   ctx=ctx)]
+
+    def _conv(self, op_type, input_names, need, opt, attrs):
+        ctx = self.ctx
+        wi = 3 if op_type == "QLinearConv" else 1
+        w = need(wi)
+        if op_type == "Conv":
+            declared = attrs.get("kernel_shape")
+            kernel = [int(v) for v in (w.shape if hasattr(w, "shape") else np.shape(w))[2:]]
+            if declared is not None and [int(v) for v in declared] != kernel:
+                raise N.StateError(f"Conv kernel_shape {list(declared)} does not match weight shape {kernel}.")
+        if self._is_init(input_names[wi]) and not isinstance(w, DeviceTensor):
+            w = self._packed_for(("conv", input_names[wi]), lambda: ctx.prepack_conv(np.asarray(w)))
+        spatial = dict(strides=attrs.get("strides"), pads=attrs.get("pads"), dilations=attrs.get("dilations"),
+                       group=int(attrs.get("group", 1)))
+        if op_type == "Conv":
+            return ops.opConv(need(0), w, opt(2), autoPad=attrs.get("auto_pad", "NOTSET") or "NOTSET",
+                              mode=self.f32_mode, ctx=ctx, **spatial)
+        if op_type == "ConvInteger":
+            return ops.opConvInteger(need(0), w, opt(2), opt(3), ctx=ctx, **spatial)
+        int8 = self.elem_types.get(input_names[7] if len(input_names) > 7 else "", 0) == 3
+        return ops.opQLinearConv(need(0), need(1), opt(2), w, need(4), opt(5), need(6), opt(7), opt(8),
+                                 lo=-128 if int8 else 0, hi=127 if int8 else 255, ctx=ctx, **spatial)

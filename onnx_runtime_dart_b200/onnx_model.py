@@ -330,7 +330,8 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
     """A dispatch.GpuDispatch for `model` with every MatMul-family initializer
     weight packed now (MatMul / Gemm fp32 B, Gemm transB applied at pack time,
     MatMulInteger / QLinearMatMul int8 B, MatMulNBits b_q + scales + zero
-    points), under the keys the dispatch uses. Returns (dispatch, stats)."""
+    points, Conv / ConvInteger / QLinearConv weights), under the keys the
+    dispatch uses. Returns (dispatch, stats)."""
     from . import ops
     from .dispatch import GpuDispatch
 
@@ -344,8 +345,13 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
         if cache is None:
             disp._packed[key] = make()
         else:
-            disp._packed[key] = cache.get_or_make(_cache_key(kind, parts, arrays), make,
-                                                  "f32" if kind in ("f32", "gemm") else kind)
+            pk = "f32" if kind in ("f32", "gemm") else kind
+            if kind == "conv":
+                pk = "f32" if arrays[0].dtype == np.float32 else "i8"
+            w = cache.get_or_make(_cache_key(kind, parts, arrays), make, pk)
+            if kind == "conv":  # an imported blob does not carry the ONNX weight shape
+                w.shape = tuple(int(d) for d in arrays[0].shape)
+            disp._packed[key] = w
 
     for nd in model.nodes:
         ins = nd.inputs
@@ -362,6 +368,12 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
                     and inits[ins[bi]].dtype in (np.int8, np.uint8):
                 b = inits[ins[bi]]
                 packed(("i8", ins[bi]), "i8", (), [b], lambda b=b: ctx.prepack_i8(b))
+        elif nd.op_type in ("Conv", "ConvInteger", "QLinearConv"):
+            wi = 3 if nd.op_type == "QLinearConv" else 1
+            if len(ins) > wi and ins[wi] in inits and inits[ins[wi]].ndim >= 3 \
+                    and inits[ins[wi]].dtype in (np.float32, np.int8, np.uint8):
+                wt = inits[ins[wi]]
+                packed(("conv", ins[wi]), "conv", (), [wt], lambda wt=wt: ctx.prepack_conv(wt))
         elif nd.op_type == "MatMulNBits" and len(ins) > 2 and ins[1] in inits and ins[2] in inits:
             k, n = int(nd.attrs["K"]), int(nd.attrs["N"])
             bits, block = int(nd.attrs.get("bits", 4)), int(nd.attrs["block_size"])

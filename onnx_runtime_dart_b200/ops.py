@@ -6,6 +6,9 @@ Same names, argument meaning and error behaviour as
   opMatMulInteger  lib/src/onnx_qlinear_ops.dart:32-81
   opQLinearMatMul  lib/src/onnx_qlinear_ops.dart:85-108
   opMatMulNBits    lib/src/onnx_qlinear_ops.dart:115-228
+  opConv           lib/src/onnx_nn_ops.dart:179-545
+  opConvInteger    lib/src/onnx_qlinear_ops.dart:305-338
+  opQLinearConv    lib/src/onnx_qlinear_ops.dart:341-382
 but executed by libb200mm.so on the GPU. Operands may be numpy arrays (host
 values, uploaded for the call), DeviceTensor (device-resident, e.g. the output
 of a previous op), or — for the weight operand — a PackedWeight prepared once
@@ -269,4 +272,121 @@ def opMatMulNBits(a, bQ, scales=None, zeroPoints=None, *, k: int, n: int, bits: 
     bh, _b = _dev(ctx, bias, np.float32)
     y = _out(out)
     N.check(ctx.lib.b2m_matmul_nbits(ctx.handle, ah, w.handle, bh, int(mode), ctypes.byref(y)))
+    return _wrap_out(ctx, y, out)
+
+
+# ---------------------------------------------------------------------------
+# Convolutions through the GEMM cores
+# ---------------------------------------------------------------------------
+
+AUTO_PAD = {"NOTSET": 0, "SAME_UPPER": 1, "SAME_LOWER": 2, "VALID": 3}
+
+
+def _i64_array(v, count=None, what=""):
+    if v is None:
+        return None, None
+    arr = np.ascontiguousarray(np.asarray(v, np.int64).ravel())
+    if count is not None and arr.size != count:
+        raise N.ArgumentError(f"Conv: {what} must have {count} values, got {arr.size}")
+    return arr, arr.ctypes.data_as(ctypes.c_void_p)
+
+
+def _spatial_attrs(pw, strides, pads, dilations):
+    """kernel_shape / strides / pads / dilations arrays of the lengths the
+    C ABI reads (nd, nd, 2 nd, nd)."""
+    nd = len(pw.shape) - 2
+    return (_i64_array(pw.shape[2:]), _i64_array(strides, nd, "strides"), _i64_array(pads, 2 * nd, "pads"),
+            _i64_array(dilations, nd, "dilations"))
+
+
+def _conv_weight(ctx, w):
+    if isinstance(w, PackedWeight):
+        if w.shape is None:
+            raise N.ArgumentError("Conv: the packed weight was not made by prepack_conv")
+        return w, None
+    pw = ctx.prepack_conv(np.asarray(w.numpy() if isinstance(w, DeviceTensor) else w))
+    return pw, pw
+
+
+def _check_conv_rank(x, pw, lo, hi):
+    """The weight's spatial rank must match the input's (opConv asserts
+    w.rank == x.rank, onnx_nn_ops.dart:197); ranks outside [lo, hi] are left
+    to the library, which rejects them as unsupported."""
+    xr = len(x.shape) if hasattr(x, "shape") else np.ndim(x)
+    if lo <= xr <= hi and len(pw.shape) != xr:
+        raise N.ArgumentError("Conv weight rank must match input rank")
+
+
+def opConv(x, w, bias=None, *, strides=None, pads=None, dilations=None, group: int = 1, autoPad: str = "NOTSET",
+           mode: int = MODE_EXACT, ctx: Context | None = None, out: DeviceTensor | None = None):
+    """Conv over 1-3 spatial dims: x [N][C][spatial...], w [M][C/group][kernel...]
+    (a PackedWeight from Context.prepack_conv, or a host array packed for the
+    call), bias [M]. Pads are [begin..., end...] as the ONNX attribute."""
+    ctx = _ctx(ctx)
+    if autoPad not in AUTO_PAD:
+        raise N.ArgumentError(f"Conv: unknown auto_pad {autoPad!r}")
+    pw, tmp = _conv_weight(ctx, w)
+    _check_conv_rank(x, pw, 3, 5)
+    xh, _x = _dev(ctx, x, np.float32)
+    bh, _b = _dev(ctx, bias, np.float32)
+    (ks, ksp), (st, stp), (pd, pdp), (dl, dlp) = _spatial_attrs(pw, strides, pads, dilations)
+    y = _out(out)
+    try:
+        N.check(ctx.lib.b2m_conv_f32(ctx.handle, xh, pw.handle, bh, ksp, stp, pdp, dlp, int(group), AUTO_PAD[autoPad],
+                                     int(mode), ctypes.byref(y)))
+    finally:
+        if tmp is not None:
+            ctx.synchronize()
+            tmp.free()
+    return _wrap_out(ctx, y, out)
+
+
+def opConvInteger(x, w, xZp=None, wZp=None, *, strides=None, pads=None, dilations=None, group: int = 1,
+                  ctx: Context | None = None, out: DeviceTensor | None = None):
+    """ConvInteger (1-D / 2-D): int32 y = sum over taps of (x - xZp)(w - wZp[m])."""
+    ctx = _ctx(ctx)
+    pw, tmp = _conv_weight(ctx, w)
+    _check_conv_rank(x, pw, 3, 4)
+    xh, _x = _int_operand(ctx, x)
+    xzh, _xz = _int_operand(ctx, xZp)
+    wzh, _wz = _int_operand(ctx, wZp)
+    (ks, ksp), (st, stp), (pd, pdp), (dl, dlp) = _spatial_attrs(pw, strides, pads, dilations)
+    y = _out(out)
+    try:
+        N.check(ctx.lib.b2m_conv_integer(ctx.handle, xh, xzh, pw.handle, wzh, ksp, stp, pdp, dlp, int(group),
+                                         ctypes.byref(y)))
+    finally:
+        if tmp is not None:
+            ctx.synchronize()
+            tmp.free()
+    return _wrap_out(ctx, y, out)
+
+
+def opQLinearConv(x, xS, xZp, w, wS, wZp, yS, yZp, bias=None, *, strides=None, pads=None, dilations=None,
+                  group: int = 1, lo: int, hi: int, ctx: Context | None = None, out: DeviceTensor | None = None):
+    """QLinearConv (2-D): ConvInteger's accumulator plus the int32 bias,
+    requantized per output channel with xS * wS[c] / yS in double, rounded half
+    to even, shifted by yZp and clamped to [lo, hi] (from yZp's dtype)."""
+    ctx = _ctx(ctx)
+    pw, tmp = _conv_weight(ctx, w)
+    _check_conv_rank(x, pw, 4, 4)
+    host = lambda v: np.asarray(v.numpy() if isinstance(v, DeviceTensor) else v)
+    xs = float(np.float32(host(xS).reshape(-1)[0]))
+    ys = float(np.float32(host(yS).reshape(-1)[0]))
+    ws = np.ascontiguousarray(host(wS).astype(np.float32).reshape(-1))
+    yz = 0 if yZp is None else int(host(yZp).reshape(-1)[0])
+    xh, _x = _int_operand(ctx, x)
+    xzh, _xz = _int_operand(ctx, xZp)
+    wzh, _wz = _int_operand(ctx, wZp)
+    bh, _b = _dev(ctx, bias, np.int32)
+    (ks, ksp), (st, stp), (pd, pdp), (dl, dlp) = _spatial_attrs(pw, strides, pads, dilations)
+    y = _out(out)
+    try:
+        N.check(ctx.lib.b2m_qlinear_conv(ctx.handle, xh, xs, xzh, pw.handle, ws.ctypes.data_as(ctypes.c_void_p),
+                                         ws.size, wzh, ys, yz, bh, ksp, stp, pdp, dlp, int(group), int(lo), int(hi),
+                                         ctypes.byref(y)))
+    finally:
+        if tmp is not None:
+            ctx.synchronize()
+            tmp.free()
     return _wrap_out(ctx, y, out)

@@ -130,6 +130,22 @@ class Context:
                                                b.shape[0], b.shape[1], ctypes.byref(h)))
         return PackedWeight(self, h, "i8")
 
+    def prepack_conv(self, w) -> "PackedWeight":
+        """Conv / ConvInteger / QLinearConv weight [M][C/group][kernel...]
+        (float32, uint8 or int8) packed as the GEMM operand; the result keeps
+        the ONNX weight shape in `.shape`."""
+        w = np.ascontiguousarray(w)
+        if w.ndim < 3 or w.dtype not in (np.float32, np.uint8, np.int8):
+            raise N.ArgumentError("Conv prepack: weight must be [M][C/group][kernel...] float32, uint8 or int8")
+        m = int(w.shape[0])
+        k = int(np.prod(w.shape[1:]))
+        h = ctypes.c_void_p()
+        N.check(self.lib.b2m_weight_prepack_conv(self.handle, w.ctypes.data_as(ctypes.c_void_p), b2m_dtype(w.dtype),
+                                                 m, k, ctypes.byref(h)))
+        pw = PackedWeight(self, h, "f32" if w.dtype == np.float32 else "i8")
+        pw.shape = tuple(int(d) for d in w.shape)
+        return pw
+
     def prepack_nbits(self, b_q, scales, zero_points, k: int, n: int, bits: int, block_size: int) -> "PackedWeight":
         bq = np.ascontiguousarray(b_q, np.uint8)
         sc = np.ascontiguousarray(scales, np.float32)
@@ -211,6 +227,7 @@ class PackedWeight:
         self.ctx = ctx
         self.handle = handle
         self.kind = kind
+        self.shape = None  # ONNX weight shape of a convolution weight
 
     @property
     def kn(self):
