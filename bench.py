@@ -351,6 +351,61 @@ def run_bert(ctx, torch, stream, batch, seq=128, steps=10, warmup=3, layers=None
 # our arm
 # ---------------------------------------------------------------------------
 
+def conv_configs(ctx, lib, N, stream, steps, warmup):
+    """Convolutions through the GEMM cores on a ResNet-style 3x3 layer
+    (x [32, 64, 56, 56], w [64, 64, 3, 3], pads 1, bias): Conv FAST (bf16
+    split planes on tcgen05) and EXACT (fp32, the reference's k order), and
+    QLinearConv u8 x i8 -> u8. Four distinct inputs / weights / outputs per
+    CUDA graph (the FAST im2col panel, 231 MB per call, exceeds L2).
+    Device time per call; FLOP = 2 * n * P * M * K (useful work)."""
+    import torch
+    SETS = 4
+    n, c, hw, m, k = 32, 64, 56, 64, 3
+    rng = np.random.default_rng(2)
+    xs = [ctx.upload(rng.standard_normal((n, c, hw, hw)).astype(np.float32)) for _ in range(SETS)]
+    ws = [ctx.prepack_conv((rng.standard_normal((m, c, k, k)) / np.sqrt(c * k * k)).astype(np.float32))
+          for _ in range(SETS)]
+    bs = [ctx.upload(rng.standard_normal(m).astype(np.float32)) for _ in range(SETS)]
+    ys = [ctx.empty((n, m, hw, hw)) for _ in range(SETS)]
+    flop = 2 * n * hw * hw * m * c * k * k
+    ks = np.array([k, k], np.int64)
+    pads = np.array([1, 1, 1, 1], np.int64)
+    vp = lambda a: a.ctypes.data_as(ctypes.c_void_p)
+    out = {"shape": f"x[{n},{c},{hw},{hw}] w[{m},{c},{k},{k}] pads 1"}
+
+    def f32_call(i, mode):
+        def call():
+            h = ctypes.c_void_p(ys[i].handle.value)
+            N.check(lib.b2m_conv_f32(ctx.handle, xs[i].handle, ws[i].handle, bs[i].handle, vp(ks), None, vp(pads),
+                                     None, 1, 0, mode, ctypes.byref(h)))
+        return call
+    for mode, name in ((N.MODE_FAST, "fast"), (N.MODE_EXACT, "exact")):
+        gms = _time_graph(torch, ctx, stream, [f32_call(i, mode) for i in range(SETS)], steps, warmup)
+        out[f"conv_{name}_us"] = round(gms * 1e3, 2)
+        out[f"conv_{name}_tflops"] = round(flop / (gms / 1e3) / 1e12, 2)
+    xq = [ctx.upload(rng.integers(0, 256, (n, c, hw, hw)).astype(np.uint8)) for _ in range(SETS)]
+    wq = [ctx.prepack_conv(rng.integers(-127, 128, (m, c, k, k)).astype(np.int8)) for _ in range(SETS)]
+    xz = ctx.upload(np.array(128, np.uint8))
+    wz = ctx.upload(np.array(0, np.int8))
+    bq = ctx.upload(rng.integers(-1000, 1000, m).astype(np.int32))
+    wscale = ctx.upload(np.full(m, 0.004, np.float32))
+    yq = [ctx.empty((n, m, hw, hw), np.uint8) for _ in range(SETS)]
+
+    def q_call(i):
+        def call():
+            h = ctypes.c_void_p(yq[i].handle.value)
+            N.check(lib.b2m_qlinear_conv(ctx.handle, xq[i].handle, 0.02, xz.handle, wq[i].handle, wscale.handle,
+                                         wz.handle, 0.5, 128, bq.handle, vp(ks), None, vp(pads), None, 1, 0, 255,
+                                         ctypes.byref(h)))
+        return call
+    gms = _time_graph(torch, ctx, stream, [q_call(i) for i in range(SETS)], steps, warmup)
+    out["qlinearconv_us"] = round(gms * 1e3, 2)
+    out["qlinearconv_tops"] = round(flop / (gms / 1e3) / 1e12, 2)
+    for w in ws + wq:
+        w.free()
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -361,9 +416,11 @@ def main():
     ap.add_argument("--passes", type=int, default=64,
                     help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--case", default="all", choices=["all", "decode1", "decode8", "prefill", "ops", "decoder", "bert"],
+    ap.add_argument("--case", default="all",
+                    choices=["all", "decode1", "decode8", "prefill", "ops", "decoder", "bert", "conv"],
                     help="run one phase only (for profiler captures); prints its device time. "
-                         "`ops` times BASELINE configs 1 and 2 (fp32 MatMul, MatMulInteger)")
+                         "`ops` times BASELINE configs 1 and 2 (fp32 MatMul, MatMulInteger); `conv` the "
+                         "convolutions through the GEMM cores")
     ap.add_argument("--dec-layers", type=int, default=None, help="decoder case: layers (default 28)")
     ap.add_argument("--dec-steps", type=int, default=128, help="decoder case: greedy decode steps")
     ap.add_argument("--dec-batch", type=int, default=None, help="decoder case: sequences per GPU (default 64/N)")
@@ -431,6 +488,15 @@ def main():
             r["prefill_tokens_per_s_all_gpus"] = round(world * r["batch_per_gpu"] * r["prefill_len"] / (t_p / 1e3), 1)
             r["decode_tokens_per_s_all_gpus"] = round(world * r["batch_per_gpu"] * r["decode_steps"] / (t_d / 1e3), 1)
             print(json.dumps({"case": "decoder", **r}), flush=True)
+        ctx.close()
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    if args.case == "conv":
+        r = conv_configs(ctx, lib, N, stream, args.steps, args.warmup)
+        if rank == 0:
+            print(json.dumps({"case": "conv", **r}), flush=True)
         ctx.close()
         if world > 1:
             dist.destroy_process_group()
@@ -523,6 +589,7 @@ def main():
     # BASELINE configs 1 and 2 (fp32 MatMul, int8 MatMulInteger): device time
     # per op over 64 weight sets in a CUDA graph.
     ops_lines = other_configs(ctx, lib, N, stream, dev, max(1, args.steps // 4), 3)
+    conv_line = conv_configs(ctx, lib, N, stream, max(1, args.steps // 4), 3)
 
     # the int4 decoder chain, sequences sharded over ranks.
     dec = run_decoder(ctx, torch, stream, max(1, 64 // world))
@@ -597,6 +664,7 @@ def main():
             "prefill_m512_frac_of_bf16_peak": round(tflops_p / tc_peak, 4),
             "prefill_m512_us_per_op": round(msp * 1e3 / (max(1, args.steps // 4) * Rp), 3),
             "configs_1_2_device_us_per_op": {o["case"]: round(o["graph_us_per_call"], 3) for o in ops_lines},
+            "conv_through_gemm_cores": conv_line,
             "config5_decoder": dec_line,
             "config4_bert": bert_line,
         },

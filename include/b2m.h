@@ -412,10 +412,10 @@ B2M_API b2m_status b2m_conv_integer(b2m_ctx *ctx, const b2m_tensor *x, const b2m
  * output channel q = roundEven((acc + bias) * (x_scale * w_scale[c] /
  * y_scale)) + y_zp in double, clamped to [lo, hi] (0..255 -> uint8 y,
  * -128..127 -> int8 y; the reference picks them from y_zp's dtype,
- * onnx_graph.dart:2936). w_scale: host floats, 1 or m of them; bias int32
- * [m] or NULL. */
+ * onnx_graph.dart:2936). w_scale: float device tensor of 1 or m values;
+ * bias int32 [m] or NULL. No host buffer is read after the call returns. */
 B2M_API b2m_status b2m_qlinear_conv(b2m_ctx *ctx, const b2m_tensor *x, float x_scale, const b2m_tensor *x_zp,
-                                    const b2m_weight *w, const float *w_scale, int64_t n_w_scale,
+                                    const b2m_weight *w, const b2m_tensor *w_scale,
                                     const b2m_tensor *w_zp, float y_scale, int32_t y_zp, const b2m_tensor *bias,
                                     const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
                                     const int64_t *dilations, int32_t group, int32_t lo, int32_t hi, b2m_tensor **y);

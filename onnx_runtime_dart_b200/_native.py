@@ -129,7 +129,7 @@ SIGNATURES = {
                             ctypes.POINTER(_c_tensor)]),
     "b2m_conv_integer": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_weight, _c_tensor, _vp, _vp, _vp, _vp, _i32,
                                 ctypes.POINTER(_c_tensor)]),
-    "b2m_qlinear_conv": (_i32, [_c_ctx, _c_tensor, _f32, _c_tensor, _c_weight, _vp, _i64, _c_tensor, _f32, _i32,
+    "b2m_qlinear_conv": (_i32, [_c_ctx, _c_tensor, _f32, _c_tensor, _c_weight, _c_tensor, _c_tensor, _f32, _i32,
                                 _c_tensor, _vp, _vp, _vp, _vp, _i32, _i32, _i32, ctypes.POINTER(_c_tensor)]),
     "b2m_weight_info": (_i32, [_c_weight, _i64p, _i64p]),
     "b2m_matmul_f32": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_weight, _i32, ctypes.POINTER(_c_tensor)]),

@@ -244,12 +244,19 @@ void launch_conv_im2col_i8(const void *x, const ConvGeom &g, int64_t grp, int64_
 // pad_taps != 0 also adds the zero products of padded taps.
 void launch_conv_direct_double(const float *x, const float *wt, const float *bias, const ConvGeom &g, int pad_taps,
                                float *y, cudaStream_t s);
-// z [nb * P][mpg] int32 -> y[b][grp * mpg + j][p]: int32 (y32) or, with yq,
-// QLinearConv's requantisation q = roundEven((z + bias) * mult[ch]) + y_zp
-// clamped to [lo, hi] (mult in double, per output channel).
+// QLinearConv's requantisation: q = roundEven((z + bias[ch]) * mult) + y_zp
+// clamped to [lo, hi], mult = x_scale * w_scale[ch or 0] / y_scale in double.
+struct ConvRequant {
+  double xs = 0.0, ys = 1.0;
+  const float *ws = nullptr;
+  int64_t ws_len = 1;
+  const int32_t *bias = nullptr;
+  int32_t y_zp = 0, lo = 0, hi = 255;
+};
+// z [nb * P][mpg] int32 -> y[b][grp * mpg + j][p]: int32 (y32), or requantized
+// bytes (yq with rq).
 void launch_conv_scatter(const int32_t *z, const ConvGeom &g, int64_t grp, int64_t b0, int64_t nb, int32_t *y32,
-                         void *yq, const double *mult, const int32_t *bias, int32_t y_zp, int32_t lo, int32_t hi,
-                         cudaStream_t s);
+                         void *yq, const ConvRequant &rq, cudaStream_t s);
 
 // MatMulNBits
 struct NbitsArgs {

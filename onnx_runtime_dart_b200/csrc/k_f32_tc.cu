@@ -31,6 +31,7 @@
 #include <cuda_bf16.h>
 
 #include <algorithm>
+#include <climits>
 
 #include "b2m_internal.cuh"
 #include "ptx.cuh"
@@ -301,8 +302,17 @@ __global__ void __launch_bounds__(256) f32_split_rows(const float *__restrict__ 
   pdl_wait();
   const int64_t groups = Kp >> 3, total = M * groups;
   const bool vec = (lda & 3) == 0 && (reinterpret_cast<uintptr_t>(A) & 15) == 0;
+  const bool narrow = total < INT32_MAX;  // 32-bit index division
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t m = i / groups, k = (i % groups) * 8;
+    int64_t m, k;
+    if (narrow) {
+      const int q = (int)i / (int)groups;
+      m = q;
+      k = ((int)i - q * (int)groups) * 8;
+    } else {
+      m = i / groups;
+      k = (i % groups) * 8;
+    }
     const float *src = A + m * lda + k;
     float x[8];
     if (vec && k + 8 <= K) {
@@ -312,11 +322,13 @@ __global__ void __launch_bounds__(256) f32_split_rows(const float *__restrict__ 
 #pragma unroll
       for (int j = 0; j < 8; j++) x[j] = k + j < K ? src[j] : 0.f;
     }
-    __align__(16) __nv_bfloat16 h[8], l[8];
-#pragma unroll
-    for (int j = 0; j < 8; j++) split_bf16(x[j], h[j], l[j]);
-    *reinterpret_cast<uint4 *>(p0 + m * Kp + k) = *reinterpret_cast<const uint4 *>(h);
-    *reinterpret_cast<uint4 *>(p1 + m * Kp + k) = *reinterpret_cast<const uint4 *>(l);
+    uint4 h, l;
+    split_bf16x2(x[0], x[1], h.x, l.x);
+    split_bf16x2(x[2], x[3], h.y, l.y);
+    split_bf16x2(x[4], x[5], h.z, l.z);
+    split_bf16x2(x[6], x[7], h.w, l.w);
+    *reinterpret_cast<uint4 *>(p0 + m * Kp + k) = h;
+    *reinterpret_cast<uint4 *>(p1 + m * Kp + k) = l;
   }
 }
 

@@ -1655,8 +1655,8 @@ ConvGeom conv_geometry(const b2m_tensor *x, int64_t m, int64_t wk, const int64_t
     g.P *= out;
   }
   const int64_t lim = INT32_MAX;
-  B2M_REQUIRE(g.K < lim && g.P < lim && g.cin < lim && g.m < lim && g.in[0] * g.in[1] * g.in[2] < lim,
-              B2M_ERR_UNSUPPORTED, std::string(op) + ": dimensions beyond 2^31");
+  B2M_REQUIRE(g.K < lim && g.P < lim && g.cin < lim && g.m < lim && g.cpg * g.in[0] * g.in[1] * g.in[2] < lim,
+              B2M_ERR_UNSUPPORTED, std::string(op) + ": dimensions beyond 2^31 (per image and group)");
   return g;
 }
 
@@ -1791,7 +1791,7 @@ void conv_f32_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_weight *w, const
 
 void conv_int_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *xzp, const b2m_weight *w,
                    const b2m_tensor *wzp, const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
-                   const int64_t *dilations, int32_t group, bool requant, double xs, const float *ws, int64_t nws,
+                   const int64_t *dilations, int32_t group, bool requant, double xs, const b2m_tensor *ws,
                    double ys, int32_t yzp, const b2m_tensor *bias, int32_t lo, int32_t hi, b2m_tensor **y) {
   const char *op = requant ? "QLinearConv" : "ConvInteger";
   B2M_REQUIRE(x && is_i8(x->dtype), B2M_ERR_INVALID_ARGUMENT, std::string(op) + ": x must be uint8 or int8");
@@ -1820,8 +1820,8 @@ void conv_int_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *xzp, con
   if (requant) {
     B2M_REQUIRE((lo == 0 && hi == 255) || (lo == -128 && hi == 127), B2M_ERR_INVALID_ARGUMENT,
                 "QLinearConv: lo/hi must be [0,255] or [-128,127]");
-    B2M_REQUIRE(ws && (nws == 1 || nws == g.m), B2M_ERR_INVALID_ARGUMENT,
-                "QLinearConv: w_scale must have 1 or M values");
+    B2M_REQUIRE(ws && ws->dtype == B2M_FLOAT && (ws->numel == 1 || ws->numel == g.m), B2M_ERR_INVALID_ARGUMENT,
+                "QLinearConv: w_scale must be float with 1 or M values");
     if (bias)
       B2M_REQUIRE(bias->dtype == B2M_INT32 && bias->numel == g.m, B2M_ERR_INVALID_ARGUMENT,
                   "QLinearConv: bias must be int32 with one value per output channel");
@@ -1834,19 +1834,20 @@ void conv_int_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *xzp, con
   const int64_t kg = w->k;
   const int64_t nb = images_per_pass(g, g.P * (kg + 4 * g.mpg + 4), g.P);
   const size_t rows_b = (size_t)(nb * g.P * kg), z_b = (size_t)(nb * g.P * g.mpg * 4), rs_b = (size_t)(nb * g.P * 4);
-  const size_t mult_b = requant ? (size_t)g.m * 8 : 0;
-  Scratch sc(ctx, rows_b + z_b + rs_b + mult_b + 4 * 256);
+  Scratch sc(ctx, rows_b + z_b + rs_b + 3 * 256);
   uint8_t *rows = static_cast<uint8_t *>(sc.take(rows_b));
   int32_t *z = static_cast<int32_t *>(sc.take(z_b));
   int32_t *rowsum = static_cast<int32_t *>(sc.take(rs_b));
-  double *mult = nullptr;
+  ConvRequant rq;
   if (requant) {
-    // mult = x_scale * w_scale[c] / y_scale in double (onnx_qlinear_ops.dart:370).
-    std::vector<double> hm((size_t)g.m);
-    for (int64_t c = 0; c < g.m; c++) hm[(size_t)c] = xs * (double)ws[nws == 1 ? 0 : c] / ys;
-    mult = static_cast<double *>(sc.take(mult_b));
-    B2M_CUDA(cudaMemcpyAsync(mult, hm.data(), mult_b, cudaMemcpyHostToDevice, ctx->stream));
-    B2M_CUDA(cudaStreamSynchronize(ctx->stream));  // hm leaves scope below
+    rq.xs = xs;
+    rq.ys = ys;
+    rq.ws = static_cast<const float *>(ws->data);
+    rq.ws_len = ws->numel;
+    rq.bias = bias ? static_cast<const int32_t *>(bias->data) : nullptr;
+    rq.y_zp = yzp;
+    rq.lo = lo;
+    rq.hi = hi;
   }
   const bool per_channel = wzp && wzp->numel == g.m && g.m != 1;
   for (int64_t b0 = 0; b0 < g.n; b0 += nb) {
@@ -1880,8 +1881,7 @@ void conv_int_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *xzp, con
       const bool done = g.group == 1 && launch_i8_tc(p, w->i8, ctx->stream);
       if (!done) launch_i8_gemm(p, ctx->stream);
       launch_conv_scatter(z, g, grp, b0, cnt, requant ? nullptr : static_cast<int32_t *>(out->data),
-                          requant ? out->data : nullptr, mult, bias ? static_cast<const int32_t *>(bias->data) : nullptr,
-                          yzp, lo, hi, ctx->stream);
+                          requant ? out->data : nullptr, rq, ctx->stream);
     }
   }
   timer.done();
@@ -1930,13 +1930,13 @@ B2M_API b2m_status b2m_conv_integer(b2m_ctx *ctx, const b2m_tensor *x, const b2m
   return guarded([&] {
     check_ctx(ctx);
     DeviceGuard dg(ctx->device);
-    conv_int_impl(ctx, x, x_zp, w, w_zp, kernel_shape, strides, pads, dilations, group, false, 0.0, nullptr, 0, 0.0,
-                  0, nullptr, 0, 0, y);
+    conv_int_impl(ctx, x, x_zp, w, w_zp, kernel_shape, strides, pads, dilations, group, false, 0.0, nullptr, 1.0, 0,
+                  nullptr, 0, 0, y);
   });
 }
 
 B2M_API b2m_status b2m_qlinear_conv(b2m_ctx *ctx, const b2m_tensor *x, float x_scale, const b2m_tensor *x_zp,
-                                    const b2m_weight *w, const float *w_scale, int64_t n_w_scale,
+                                    const b2m_weight *w, const b2m_tensor *w_scale,
                                     const b2m_tensor *w_zp, float y_scale, int32_t y_zp, const b2m_tensor *bias,
                                     const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
                                     const int64_t *dilations, int32_t group, int32_t lo, int32_t hi, b2m_tensor **y) {
@@ -1944,7 +1944,7 @@ B2M_API b2m_status b2m_qlinear_conv(b2m_ctx *ctx, const b2m_tensor *x, float x_s
     check_ctx(ctx);
     DeviceGuard dg(ctx->device);
     conv_int_impl(ctx, x, x_zp, w, w_zp, kernel_shape, strides, pads, dilations, group, true, (double)x_scale,
-                  w_scale, n_w_scale, (double)y_scale, y_zp, bias, lo, hi, y);
+                  w_scale, (double)y_scale, y_zp, bias, lo, hi, y);
   });
 }
 

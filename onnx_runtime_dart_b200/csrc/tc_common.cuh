@@ -64,6 +64,26 @@ __device__ __forceinline__ void split_bf16(float x, __nv_bfloat16 &h, __nv_bfloa
   l = __float2bfloat16_rn(isfinite(x) ? x - hf : 0.f);
 }
 
+// split_bf16 of two values at once, packed as bf16x2 words (a in the low
+// half). Finite values below 3.38e38 in magnitude (every value whose bf16
+// rounding stays finite, with margin) take two packed conversions; anything
+// else goes through split_bf16, so the results are identical.
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t &hi, uint32_t &lo) {
+  if (fabsf(a) < 3.38e38f && fabsf(b) < 3.38e38f) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    const float2 hf = __bfloat1622float2(h);
+    const __nv_bfloat162 l = __floats2bfloat162_rn(a - hf.x, b - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+    return;
+  }
+  __nv_bfloat16 h0, l0, h1, l1;
+  split_bf16(a, h0, l0);
+  split_bf16(b, h1, l1);
+  hi = (uint32_t)__bfloat16_as_ushort(h0) | ((uint32_t)__bfloat16_as_ushort(h1) << 16);
+  lo = (uint32_t)__bfloat16_as_ushort(l0) | ((uint32_t)__bfloat16_as_ushort(l1) << 16);
+}
+
 // SM count of the current device, cached.
 int device_sm_count();
 

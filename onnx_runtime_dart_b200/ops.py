@@ -373,8 +373,8 @@ def opQLinearConv(x, xS, xZp, w, wS, wZp, yS, yZp, bias=None, *, strides=None, p
     host = lambda v: np.asarray(v.numpy() if isinstance(v, DeviceTensor) else v)
     xs = float(np.float32(host(xS).reshape(-1)[0]))
     ys = float(np.float32(host(yS).reshape(-1)[0]))
-    ws = np.ascontiguousarray(host(wS).astype(np.float32).reshape(-1))
     yz = 0 if yZp is None else int(host(yZp).reshape(-1)[0])
+    wsh, _ws = _dev(ctx, wS, np.float32)
     xh, _x = _int_operand(ctx, x)
     xzh, _xz = _int_operand(ctx, xZp)
     wzh, _wz = _int_operand(ctx, wZp)
@@ -382,8 +382,7 @@ def opQLinearConv(x, xS, xZp, w, wS, wZp, yS, yZp, bias=None, *, strides=None, p
     (ks, ksp), (st, stp), (pd, pdp), (dl, dlp) = _spatial_attrs(pw, strides, pads, dilations)
     y = _out(out)
     try:
-        N.check(ctx.lib.b2m_qlinear_conv(ctx.handle, xh, xs, xzh, pw.handle, ws.ctypes.data_as(ctypes.c_void_p),
-                                         ws.size, wzh, ys, yz, bh, ksp, stp, pdp, dlp, int(group), int(lo), int(hi),
+        N.check(ctx.lib.b2m_qlinear_conv(ctx.handle, xh, xs, xzh, pw.handle, wsh, wzh, ys, yz, bh, ksp, stp, pdp, dlp, int(group), int(lo), int(hi),
                                          ctypes.byref(y)))
     finally:
         if tmp is not None:
