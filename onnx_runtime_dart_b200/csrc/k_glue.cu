@@ -976,6 +976,7 @@ using b2m::fence_proxy_async_smem;
 using b2m::mbar_fence_init;
 using b2m::mbar_init;
 using b2m::smem_u32;
+using b2m::split_bf16x2;
 using b2m::sw128_kmajor_desc;
 using b2m::tc_fence_after;
 using b2m::tc_fence_before;
@@ -1211,6 +1212,279 @@ __global__ void __launch_bounds__(512) mha_tc_kernel(const GqaArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Causal GroupQueryAttention prefill on the tensor cores (head_dim 64 or
+// 128, keys from the KV cache): flash-style, one CTA of 512 threads per
+// (128-query tile, query head, sequence), 64-key tiles with an online
+// softmax. Per key tile:
+//   * all threads stage K (64 x D) and V^T (D x 64) as bf16 hi / lo planes in
+//     128-byte swizzled shared memory;
+//   * one thread issues S = Q.K^T as three kind::f16 products (the bf16
+//     split Q0.K0 + Q0.K1 + Q1.K0, as the FAST GEMM) into TMEM columns 0-63;
+//   * warp w reads lane quarter w % 4 (query rows) and 16 of the 64 score
+//     columns, applies the causal limit (key j visible to query i when
+//     j <= past + i), and the four column warps of a row agree on the running
+//     max and sum through shared memory; P = exp(s - max) is split into
+//     bf16 hi / lo in shared memory;
+//   * one thread issues P.V (three products, fresh accumulator in TMEM
+//     columns 64 .. 64 + D); each thread adds its D / 4 output columns into
+//     registers as O = O * corr + PV.
+// Q (scaled, then rotated as the SIMT prefill kernel does) is staged once.
+// Every wait is bounded; a timeout records the device error and the CTA
+// leaves the loop.
+// ---------------------------------------------------------------------------
+template <int D>
+struct FaLayout {
+  static constexpr int ND = D / 64;                       // 64-dim SW128 blocks of Q / K
+  static constexpr uint32_t QH = 0, QL = ND * 16384;      // [128][64] blocks
+  static constexpr uint32_t R = 2 * ND * 16384;           // K / V / P region (Q staging scratch first)
+  static constexpr uint32_t KH = R, KL = KH + ND * 8192;  // [64][64] blocks
+  static constexpr uint32_t VH = KL + ND * 8192, VL = VH + D * 128;  // [D][64] blocks
+  static constexpr uint32_t PH = VL + D * 128, PL = PH + 16384;      // [128][64]
+  static constexpr uint32_t RED = PL + 16384;             // red_m[4][128], red_l[4][128]
+  static constexpr uint32_t BAR = RED + 2 * 4 * 128 * 4;  // bar_s, bar_o
+  static constexpr uint32_t SLOT = BAR + 16;
+  static constexpr uint32_t FLAG = SLOT + 8;
+  static constexpr uint32_t BYTES = FLAG + 8 + 1024;      // + alignment slack
+  static_assert(128 * D * 4 <= PL + 16384 - R, "Q staging fits the K / V / P region");
+  static_assert(BYTES <= 232448, "shared memory");
+};
+
+template <int D>
+__global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
+  using L = FaLayout<D>;
+  constexpr int DW = D / 4;  // output columns per thread
+  extern __shared__ uint8_t fa_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(fa_raw) + 1023) & ~(uintptr_t)1023);
+  float *red_m = reinterpret_cast<float *>(smem + L::RED), *red_l = red_m + 4 * 128;
+  uint64_t *bar_s = reinterpret_cast<uint64_t *>(smem + L::BAR), *bar_o = bar_s + 1;
+  uint32_t *slot = reinterpret_cast<uint32_t *>(smem + L::SLOT);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + L::FLAG);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int q4 = warp & 3, cb = warp >> 2;
+  const int q0 = blockIdx.x * 128, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (a.H / a.KVH);
+  const int past = a.past[b];
+  if (tid == 0) {
+    mbar_init(bar_s, 1);
+    mbar_init(bar_o, 1);
+    *abort_flag = 0;
+    mbar_fence_init();
+  }
+  if (warp == 0) tmem_alloc(slot, 256);
+
+  // Q tile: scaled fp32 rows in the K / V / P region, rotated, then split.
+  float *qf = reinterpret_cast<float *>(smem + L::R);  // [128][D]
+  for (int it = tid; it < 128 * (D / 4); it += 512) {
+    const int r = it / (D / 4), c = it % (D / 4);
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (q0 + r < a.S)
+      v = *reinterpret_cast<const float4 *>(a.q + (int64_t)(b * a.S + q0 + r) * a.q_rs + h * D + 4 * c);
+    v.x *= a.scale, v.y *= a.scale, v.z *= a.scale, v.w *= a.scale;
+    *reinterpret_cast<float4 *>(qf + r * D + 4 * c) = v;
+  }
+  __syncthreads();
+  if (a.cos) {
+    const int npair = a.rot / 2;
+    for (int i = tid; i < 128 * npair; i += 512) {
+      const int r = i / npair, pi = i % npair;
+      const int64_t pos = past + q0 + r;
+      if (q0 + r >= a.S || pos >= a.CAP) continue;
+      const float c = a.cos[pos * a.half + pi], sn = a.sin[pos * a.half + pi];
+      const int i0 = a.interleaved ? 2 * pi : pi, i1 = a.interleaved ? 2 * pi + 1 : pi + npair;
+      const float x0 = qf[r * D + i0], x1 = qf[r * D + i1];
+      qf[r * D + i0] = x0 * c - x1 * sn;
+      qf[r * D + i1] = x1 * c + x0 * sn;
+    }
+  }
+  __syncthreads();
+  for (int it = tid; it < 128 * (D / 8); it += 512) {
+    const int r = it / (D / 8), c = it % (D / 8);
+    const float *src = qf + r * D + 8 * c;
+    uint4 hv, lv;
+    split_bf16x2(src[0], src[1], hv.x, lv.x);
+    split_bf16x2(src[2], src[3], hv.y, lv.y);
+    split_bf16x2(src[4], src[5], hv.z, lv.z);
+    split_bf16x2(src[6], src[7], hv.w, lv.w);
+    const uint32_t o = (uint32_t)(c >> 3) * 16384u + sw128_elem(r, (8 * c) & 63);
+    *reinterpret_cast<uint4 *>(smem + L::QH + o) = hv;
+    *reinterpret_cast<uint4 *>(smem + L::QL + o) = lv;
+  }
+  __syncthreads();  // the Q staging scratch is consumed before K / V reuse it
+
+  const int nkeys = min(past + a.S, a.CAP);
+  const int kend = min(nkeys, past + min(q0 + 128, a.S));  // keys any row of the tile sees
+  const float *kc = a.kcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const float *vc = a.vcache + (int64_t)b * a.kc_bs + (int64_t)kvh * a.kc_hs;
+  const uint32_t tmem = *slot;
+  const int r = q4 * 32 + lane;
+  const int vis = past + q0 + r;  // last key this row sees
+  const uint32_t trow = tmem + ((uint32_t)(q4 * 32) << 16);
+  float m = -INFINITY, l = 0.f;
+  float o[DW];
+#pragma unroll
+  for (int c = 0; c < DW; c++) o[c] = 0.f;
+  bool ok = true;
+  int it = 0;
+  for (int j0 = 0; j0 < kend && ok; j0 += 64, it++) {
+    // K tile: (key t, 8-dim chunk) items.
+    for (int e = tid; e < 64 * (D / 8); e += 512) {
+      const int t = e / (D / 8), c = e % (D / 8);
+      float x[8];
+      if (j0 + t < kend) {
+        const float *src = kc + (int64_t)(j0 + t) * a.kc_rs + 8 * c;
+        const float4 u = *reinterpret_cast<const float4 *>(src), w = *reinterpret_cast<const float4 *>(src + 4);
+        x[0] = u.x, x[1] = u.y, x[2] = u.z, x[3] = u.w, x[4] = w.x, x[5] = w.y, x[6] = w.z, x[7] = w.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) x[j] = 0.f;
+      }
+      uint4 hv, lv;
+      split_bf16x2(x[0], x[1], hv.x, lv.x);
+      split_bf16x2(x[2], x[3], hv.y, lv.y);
+      split_bf16x2(x[4], x[5], hv.z, lv.z);
+      split_bf16x2(x[6], x[7], hv.w, lv.w);
+      const uint32_t ob = (uint32_t)(c >> 3) * 8192u + sw128_elem(t, (8 * c) & 63);
+      *reinterpret_cast<uint4 *>(smem + L::KH + ob) = hv;
+      *reinterpret_cast<uint4 *>(smem + L::KL + ob) = lv;
+    }
+    // V^T tile: keys 2p, 2p+1 of dims 8g .. 8g+7 as bf16 pairs.
+    for (int e = tid; e < 32 * (D / 8); e += 512) {
+      const int pr = e % 32, g = e / 32, t0 = 2 * pr;
+      float e0[8], e1[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) e0[j] = e1[j] = 0.f;
+      const float *v0 = vc + (int64_t)(j0 + t0) * a.kc_rs + 8 * g;
+      if (j0 + t0 < kend) {
+        const float4 u = *reinterpret_cast<const float4 *>(v0), w = *reinterpret_cast<const float4 *>(v0 + 4);
+        e0[0] = u.x, e0[1] = u.y, e0[2] = u.z, e0[3] = u.w, e0[4] = w.x, e0[5] = w.y, e0[6] = w.z, e0[7] = w.w;
+      }
+      if (j0 + t0 + 1 < kend) {
+        const float *v1 = v0 + a.kc_rs;
+        const float4 u = *reinterpret_cast<const float4 *>(v1), w = *reinterpret_cast<const float4 *>(v1 + 4);
+        e1[0] = u.x, e1[1] = u.y, e1[2] = u.z, e1[3] = u.w, e1[4] = w.x, e1[5] = w.y, e1[6] = w.z, e1[7] = w.w;
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        uint32_t hw, lw;
+        split_bf16x2(e0[j], e1[j], hw, lw);
+        const uint32_t ov = sw128_elem(8 * g + j, t0);
+        *reinterpret_cast<uint32_t *>(smem + L::VH + ov) = hw;
+        *reinterpret_cast<uint32_t *>(smem + L::VL + ov) = lw;
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      constexpr uint32_t idesc_s = umma_idesc(128, 64, 1u, 1u, 1u);
+      const uint32_t base = smem_u32(smem);
+#pragma unroll
+      for (int kk = 0; kk < D / 16; kk++) {
+        const uint32_t o16 = (uint32_t)(kk & 3) * 32u;
+        const uint64_t qh = sw128_kmajor_desc(base + L::QH + (kk >> 2) * 16384u + o16);
+        const uint64_t ql = sw128_kmajor_desc(base + L::QL + (kk >> 2) * 16384u + o16);
+        const uint64_t kh = sw128_kmajor_desc(base + L::KH + (kk >> 2) * 8192u + o16);
+        const uint64_t kl = sw128_kmajor_desc(base + L::KL + (kk >> 2) * 8192u + o16);
+        umma_f16(tmem, ql, kh, idesc_s, kk ? 1u : 0u);
+        umma_f16(tmem, qh, kl, idesc_s, 1u);
+        umma_f16(tmem, qh, kh, idesc_s, 1u);
+      }
+      umma_commit(bar_s);
+    }
+    const bool ok_s = warp_wait_or_abort(bar_s, (uint32_t)(it & 1), abort_flag, a.err);
+    tc_fence_after();
+    float sv[16];
+    float tmax = -INFINITY;
+    if (ok_s) {
+      uint32_t v[16];
+      tmem_ld16(trow + (uint32_t)(cb * 16), v);
+      tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const int t = j0 + cb * 16 + j;
+        const float x = (t <= vis && t < kend) ? __uint_as_float(v[j]) : -INFINITY;
+        sv[j] = x;
+        tmax = fmaxf(tmax, x);
+      }
+    }
+    red_m[cb * 128 + r] = tmax;
+    __syncthreads();
+    const float mnew = fmaxf(m, fmaxf(fmaxf(red_m[r], red_m[128 + r]), fmaxf(red_m[256 + r], red_m[384 + r])));
+    float psum = 0.f;
+    {
+      uint32_t ph[8], pl[8];
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) {
+        const float e0 = (ok_s && mnew != -INFINITY) ? __expf(sv[j] - mnew) : 0.f;
+        const float e1 = (ok_s && mnew != -INFINITY) ? __expf(sv[j + 1] - mnew) : 0.f;
+        psum += e0 + e1;
+        split_bf16x2(e0, e1, ph[j / 2], pl[j / 2]);
+      }
+#pragma unroll
+      for (int hh = 0; hh < 2; hh++) {
+        const uint32_t op = sw128_elem(r, cb * 16 + 8 * hh);
+        *reinterpret_cast<uint4 *>(smem + L::PH + op) = make_uint4(ph[4 * hh], ph[4 * hh + 1], ph[4 * hh + 2], ph[4 * hh + 3]);
+        *reinterpret_cast<uint4 *>(smem + L::PL + op) = make_uint4(pl[4 * hh], pl[4 * hh + 1], pl[4 * hh + 2], pl[4 * hh + 3]);
+      }
+    }
+    red_l[cb * 128 + r] = psum;
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const float corr = m == -INFINITY ? 0.f : __expf(m - mnew);
+    l = l * corr + ((red_l[r] + red_l[128 + r]) + (red_l[256 + r] + red_l[384 + r]));
+    m = mnew;
+    if (tid == 0) {
+      if (ok_s) {
+        constexpr uint32_t idesc_o = umma_idesc(128, D, 1u, 1u, 1u);
+        const uint32_t base = smem_u32(smem);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+          const uint32_t o16 = (uint32_t)kk * 32u;
+          const uint64_t ph = sw128_kmajor_desc(base + L::PH + o16), pl = sw128_kmajor_desc(base + L::PL + o16);
+          const uint64_t vh = sw128_kmajor_desc(base + L::VH + o16), vl = sw128_kmajor_desc(base + L::VL + o16);
+          umma_f16(tmem + 64, pl, vh, idesc_o, kk ? 1u : 0u);
+          umma_f16(tmem + 64, ph, vl, idesc_o, 1u);
+          umma_f16(tmem + 64, ph, vh, idesc_o, 1u);
+        }
+      }
+      umma_commit(bar_o);  // also when skipped, so every wait ends
+    }
+    const bool ok_o = warp_wait_or_abort(bar_o, (uint32_t)(it & 1), abort_flag, a.err) && ok_s;
+    tc_fence_after();
+    if (ok_o) {
+#pragma unroll
+      for (int c0 = 0; c0 < DW; c0 += 16) {
+        uint32_t v[16];
+        tmem_ld16(trow + 64u + (uint32_t)(cb * DW + c0), v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; j++) o[c0 + j] = fmaf(o[c0 + j], corr, __uint_as_float(v[j]));
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // P / K / V and both TMEM regions are free for the next tile
+    tc_fence_after();
+    ok = !*abort_flag;
+  }
+  if (ok && q0 + r < a.S) {
+    const float inv = 1.f / l;
+    float *dst = a.out + (int64_t)(b * a.S + q0 + r) * a.H * D + h * D + cb * DW;
+#pragma unroll
+    for (int c = 0; c < DW; c += 4)
+      *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 __global__ void advance_kernel(int32_t *past, int n, int delta) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) past[i] += delta;
@@ -1319,6 +1593,16 @@ static bool mha_tc_shape(const GqaArgs &a) {
          a.kc_rs % 4 == 0 && a.kc_bs % 4 == 0 && a.kc_hs % 4 == 0 && al(a.q) && al(a.kcache) && al(a.vcache);
 }
 
+// The tensor-core flash kernel: causal GroupQueryAttention over the KV cache
+// (prefill or chunked prefill, more than one query), head_dim 64 or 128,
+// 16-byte aligned rows, no additive bias.
+static bool fa_tc_shape(const GqaArgs &a) {
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  return a.past && a.causal && !a.mask && (a.D == 64 || a.D == 128) && a.S >= 2 && a.H % a.KVH == 0 &&
+         a.q_rs % 4 == 0 && a.kc_rs % 4 == 0 && a.kc_bs % 4 == 0 && a.kc_hs % 4 == 0 && (int64_t)a.H * a.D % 4 == 0 &&
+         al(a.q) && al(a.kcache) && al(a.vcache) && al(a.out) && (a.rot == 0 || !a.cos || a.rot <= a.D);
+}
+
 static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaStream_t s) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
@@ -1337,6 +1621,16 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaS
     B2M_CUDA(cudaGetLastError());
     if (nsplit > 1) {
       gqa_decode_combine_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, 0, s>>>(pm, pl, po, a.out, a.H, D, nsplit);
+    }
+  } else if (fa_tc_shape(a)) {
+    if (D == 128) {
+      b2m::set_smem_limit_once<fa_tc_kernel<128>>((int)FaLayout<128>::BYTES);
+      fa_tc_kernel<128><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)a.H, (unsigned)a.B), 512,
+                          FaLayout<128>::BYTES, s>>>(a);
+    } else {
+      b2m::set_smem_limit_once<fa_tc_kernel<64>>((int)FaLayout<64>::BYTES);
+      fa_tc_kernel<64><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)a.H, (unsigned)a.B), 512,
+                         FaLayout<64>::BYTES, s>>>(a);
     }
   } else if (mha_tc_shape(a)) {
     b2m::set_smem_limit_once<mha_tc_kernel>((int)MTC_BYTES);

@@ -130,7 +130,8 @@ def test_elementwise_gather_argmax(ctx):
                                                            (2, 130, 20, 4, 2, 128, 0), (1, 1, 300, 16, 2, 128, 0),
                                                            (2, 1, 0, 4, 4, 64, 1), (8, 1, 576, 16, 8, 128, 0),
                                                            (2, 1, 1000, 16, 4, 32, 0), (3, 1, 700, 8, 8, 96, 1),
-                                                           (64, 1, 40, 16, 8, 128, 0)])
+                                                           (64, 1, 40, 16, 8, 128, 0), (2, 300, 0, 16, 8, 128, 0),
+                                                           (1, 129, 70, 4, 1, 64, 1), (3, 64, 5, 8, 4, 128, 1)])
 def test_gqa_cache_rotary(ctx, b, s, past, h, kvh, d, interleaved):
     # Prefill-shaped and decode-shaped calls; `past` positions already cached.
     rng = np.random.default_rng(b * 100 + s + past + d)
