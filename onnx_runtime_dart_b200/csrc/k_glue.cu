@@ -1326,51 +1326,68 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
   for (int c = 0; c < DW; c++) o[c] = 0.f;
   bool ok = true;
   int it = 0;
-  for (int j0 = 0; j0 < kend && ok; j0 += 64, it++) {
-    // K tile: (key t, 8-dim chunk) items.
-    for (int e = tid; e < 64 * (D / 8); e += 512) {
-      const int t = e / (D / 8), c = e % (D / 8);
-      float x[8];
-      if (j0 + t < kend) {
+  // The next key tile's K / V values are loaded into registers while the
+  // current tile's MMAs and softmax run, and written to shared memory (split)
+  // once the tile's P.V has consumed the previous ones.
+  constexpr int KI = (64 * (D / 8) + 511) / 512;  // K items (key, 8-dim chunk) per thread
+  float kx[KI][8], vx[2][8];
+  auto load_tile = [&](int j0) {
+#pragma unroll
+    for (int i = 0; i < KI; i++) {
+      const int e = tid + 512 * i, t = e / (D / 8), c = e % (D / 8);
+      if (e < 64 * (D / 8) && j0 + t < kend) {
         const float *src = kc + (int64_t)(j0 + t) * a.kc_rs + 8 * c;
         const float4 u = *reinterpret_cast<const float4 *>(src), w = *reinterpret_cast<const float4 *>(src + 4);
-        x[0] = u.x, x[1] = u.y, x[2] = u.z, x[3] = u.w, x[4] = w.x, x[5] = w.y, x[6] = w.z, x[7] = w.w;
+        kx[i][0] = u.x, kx[i][1] = u.y, kx[i][2] = u.z, kx[i][3] = u.w;
+        kx[i][4] = w.x, kx[i][5] = w.y, kx[i][6] = w.z, kx[i][7] = w.w;
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; j++) x[j] = 0.f;
+        for (int j = 0; j < 8; j++) kx[i][j] = 0.f;
       }
-      uint4 hv, lv;
-      split_bf16x2(x[0], x[1], hv.x, lv.x);
-      split_bf16x2(x[2], x[3], hv.y, lv.y);
-      split_bf16x2(x[4], x[5], hv.z, lv.z);
-      split_bf16x2(x[6], x[7], hv.w, lv.w);
-      const uint32_t ob = (uint32_t)(c >> 3) * 8192u + sw128_elem(t, (8 * c) & 63);
-      *reinterpret_cast<uint4 *>(smem + L::KH + ob) = hv;
-      *reinterpret_cast<uint4 *>(smem + L::KL + ob) = lv;
+    }
+    const int pr = tid % 32, g = tid / 32, t0 = 2 * pr;
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+      const float *src = vc + (int64_t)(j0 + t0 + q) * a.kc_rs + 8 * g;
+      if (g < D / 8 && j0 + t0 + q < kend) {
+        const float4 u = *reinterpret_cast<const float4 *>(src), w = *reinterpret_cast<const float4 *>(src + 4);
+        vx[q][0] = u.x, vx[q][1] = u.y, vx[q][2] = u.z, vx[q][3] = u.w;
+        vx[q][4] = w.x, vx[q][5] = w.y, vx[q][6] = w.z, vx[q][7] = w.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; j++) vx[q][j] = 0.f;
+      }
+    }
+  };
+  if (kend > 0) load_tile(0);
+  for (int j0 = 0; j0 < kend && ok; j0 += 64, it++) {
+    // K tile: (key t, 8-dim chunk) items, split into the hi / lo planes.
+#pragma unroll
+    for (int i = 0; i < KI; i++) {
+      const int e = tid + 512 * i, t = e / (D / 8), c = e % (D / 8);
+      if (e < 64 * (D / 8)) {
+        uint4 hv, lv;
+        split_bf16x2(kx[i][0], kx[i][1], hv.x, lv.x);
+        split_bf16x2(kx[i][2], kx[i][3], hv.y, lv.y);
+        split_bf16x2(kx[i][4], kx[i][5], hv.z, lv.z);
+        split_bf16x2(kx[i][6], kx[i][7], hv.w, lv.w);
+        const uint32_t ob = (uint32_t)(c >> 3) * 8192u + sw128_elem(t, (8 * c) & 63);
+        *reinterpret_cast<uint4 *>(smem + L::KH + ob) = hv;
+        *reinterpret_cast<uint4 *>(smem + L::KL + ob) = lv;
+      }
     }
     // V^T tile: keys 2p, 2p+1 of dims 8g .. 8g+7 as bf16 pairs.
-    for (int e = tid; e < 32 * (D / 8); e += 512) {
-      const int pr = e % 32, g = e / 32, t0 = 2 * pr;
-      float e0[8], e1[8];
+    {
+      const int pr = tid % 32, g = tid / 32, t0 = 2 * pr;
+      if (g < D / 8) {
 #pragma unroll
-      for (int j = 0; j < 8; j++) e0[j] = e1[j] = 0.f;
-      const float *v0 = vc + (int64_t)(j0 + t0) * a.kc_rs + 8 * g;
-      if (j0 + t0 < kend) {
-        const float4 u = *reinterpret_cast<const float4 *>(v0), w = *reinterpret_cast<const float4 *>(v0 + 4);
-        e0[0] = u.x, e0[1] = u.y, e0[2] = u.z, e0[3] = u.w, e0[4] = w.x, e0[5] = w.y, e0[6] = w.z, e0[7] = w.w;
-      }
-      if (j0 + t0 + 1 < kend) {
-        const float *v1 = v0 + a.kc_rs;
-        const float4 u = *reinterpret_cast<const float4 *>(v1), w = *reinterpret_cast<const float4 *>(v1 + 4);
-        e1[0] = u.x, e1[1] = u.y, e1[2] = u.z, e1[3] = u.w, e1[4] = w.x, e1[5] = w.y, e1[6] = w.z, e1[7] = w.w;
-      }
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        uint32_t hw, lw;
-        split_bf16x2(e0[j], e1[j], hw, lw);
-        const uint32_t ov = sw128_elem(8 * g + j, t0);
-        *reinterpret_cast<uint32_t *>(smem + L::VH + ov) = hw;
-        *reinterpret_cast<uint32_t *>(smem + L::VL + ov) = lw;
+        for (int j = 0; j < 8; j++) {
+          uint32_t hw, lw;
+          split_bf16x2(vx[0][j], vx[1][j], hw, lw);
+          const uint32_t ov = sw128_elem(8 * g + j, t0);
+          *reinterpret_cast<uint32_t *>(smem + L::VH + ov) = hw;
+          *reinterpret_cast<uint32_t *>(smem + L::VL + ov) = lw;
+        }
       }
     }
     fence_proxy_async_smem();
@@ -1393,6 +1410,7 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
       }
       umma_commit(bar_s);
     }
+    if (j0 + 64 < kend) load_tile(j0 + 64);  // in flight under this tile's MMAs and softmax
     const bool ok_s = warp_wait_or_abort(bar_s, (uint32_t)(it & 1), abort_flag, a.err);
     tc_fence_after();
     float sv[16];
