@@ -263,18 +263,23 @@ def other_configs(ctx, lib, N, stream, dev, steps, warmup):
     return out
 
 
-def run_decoder(ctx, torch, stream, batch, prefill_len=512, steps=128, layers=None, seed=0):
-    """Qwen3-0.6B-shaped int4 decoder (random weights),
-    `batch` sequences, a `prefill_len`-token prompt, then `steps` greedy decode
-    steps replayed as one CUDA graph per step. Device time (CUDA events)."""
+def run_decoder(ctx, torch, stream, global_batch, prefill_len=512, steps=128, layers=None, seed=0, world=1, rank=0):
+    """Qwen3-0.6B-shaped int4 decoder (random weights,
+    replicated on every rank). This rank runs its slice of the
+    `global_batch` sequences (a seeded global prompt of `prefill_len` tokens
+    each), then `steps` greedy decode steps replayed as one CUDA graph per
+    step. Device time (CUDA events)."""
+    from onnx_runtime_dart_b200 import sharding
     from onnx_runtime_dart_b200.decoder import DecoderConfig, Int4Decoder
 
     cfg = DecoderConfig.qwen3_0_6b()
     if layers:
         cfg.layers = layers
-    dec = Int4Decoder(ctx, cfg, batch=batch, cap=prefill_len + steps + 8, max_prefill=prefill_len, seed=seed)
     rng = np.random.default_rng(seed + 1)
-    prompt = rng.integers(0, cfg.vocab, (batch, prefill_len)).astype(np.int64)
+    prompt_all = rng.integers(0, cfg.vocab, (global_batch, prefill_len)).astype(np.int64)
+    prompt = sharding.local_slice(prompt_all, world, rank)
+    batch = len(prompt)
+    dec = Int4Decoder(ctx, cfg, batch=batch, cap=prefill_len + steps + 8, max_prefill=prefill_len, seed=seed)
     with torch.cuda.stream(stream):
         dec.prefill(prompt)  # warm-up (kernel attributes, scratch growth)
         dec.decode(2)        # captures the decode graph
@@ -298,21 +303,25 @@ def run_decoder(ctx, torch, stream, batch, prefill_len=512, steps=128, layers=No
     return out
 
 
-def run_bert(ctx, torch, stream, batch, seq=128, steps=10, warmup=3, layers=None, seed=0, exact=False):
-    """BERT-base-shaped fp32 encoder (random weights) over
-    `batch` sequences of `seq` tokens, all-ones attention mask. Device time of
-    one graph-replayed forward (CUDA events, mean over `steps`), and the same
+def run_bert(ctx, torch, stream, global_batch, seq=128, steps=10, warmup=3, layers=None, seed=0, exact=False,
+             world=1, rank=0):
+    """BERT-base-shaped fp32 encoder (random weights,
+    replicated on every rank) over this rank's slice of `global_batch`
+    sequences of `seq` tokens, all-ones attention mask. Device time of one
+    graph-replayed forward (CUDA events, mean over `steps`), and the same
     forward end to end: ids from pinned host memory in, the last hidden state
     back to pinned host memory."""
     from onnx_runtime_dart_b200 import _native as N
+    from onnx_runtime_dart_b200 import sharding
     from onnx_runtime_dart_b200.bert import BertConfig, BertEncoder
 
     cfg = BertConfig.base()
     if layers:
         cfg.layers = layers
-    enc = BertEncoder(ctx, cfg, batch, seq, seed=seed, mode=N.MODE_EXACT if exact else N.MODE_FAST)
     rng = np.random.default_rng(seed + 1)
-    ids = rng.integers(0, cfg.vocab, (batch, seq)).astype(np.int64)
+    ids = sharding.local_slice(rng.integers(0, cfg.vocab, (global_batch, seq)).astype(np.int64), world, rank)
+    batch = len(ids)
+    enc = BertEncoder(ctx, cfg, batch, seq, seed=seed, mode=N.MODE_EXACT if exact else N.MODE_FAST)
     ids_pin = torch.from_numpy(ids.reshape(-1)).pin_memory()
     out_pin = torch.empty((batch * seq, cfg.hidden), dtype=torch.float32).pin_memory()
     with torch.cuda.stream(stream):
@@ -423,7 +432,8 @@ def main():
                          "convolutions through the GEMM cores")
     ap.add_argument("--dec-layers", type=int, default=None, help="decoder case: layers (default 28)")
     ap.add_argument("--dec-steps", type=int, default=128, help="decoder case: greedy decode steps")
-    ap.add_argument("--dec-batch", type=int, default=None, help="decoder case: sequences per GPU (default 64/N)")
+    ap.add_argument("--dec-batch", type=int, default=None,
+                    help="decoder case: sequences of the whole job, split over the ranks (default 64)")
     ap.add_argument("--bert-layers", type=int, default=None, help="bert case: layers (default 12)")
     ap.add_argument("--bert-exact", action="store_true", help="bert case: fp32-exact MatMuls instead of the FAST bf16-split tensor-core path")
     args = ap.parse_args()
@@ -441,6 +451,7 @@ def main():
 
     import onnx_runtime_dart_b200 as b2m
     from onnx_runtime_dart_b200 import _native as N
+    from onnx_runtime_dart_b200 import sharding
 
     if world > 1:
         import datetime
@@ -458,19 +469,15 @@ def main():
             dist.barrier()
 
     def max_over_ranks(x):
-        if world == 1:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return sharding.max_over_ranks(x, dist if world > 1 else None, dev)
 
     if args.case == "bert":
-        r = run_bert(ctx, torch, stream, max(1, 32 // world), layers=args.bert_layers, exact=args.bert_exact,
+        r = run_bert(ctx, torch, stream, 32, layers=args.bert_layers, exact=args.bert_exact, world=world, rank=rank,
                      steps=args.steps, warmup=args.warmup)
         t_f = max_over_ranks(r["forward_ms"])
         t_e = max_over_ranks(r["e2e_forward_ms"])
         if rank == 0:
-            tok = world * r["batch_per_gpu"] * r["seq"]
+            tok = 32 * r["seq"]  # the global batch, split over the ranks
             r["tokens_per_s_all_gpus"] = round(tok / (t_f / 1e3), 1)
             r["e2e_tokens_per_s_all_gpus"] = round(tok / (t_e / 1e3), 1)
             print(json.dumps({"case": "bert", **r}), flush=True)
@@ -480,13 +487,14 @@ def main():
         return
 
     if args.case == "decoder":
-        r = run_decoder(ctx, torch, stream, args.dec_batch or max(1, 64 // world), steps=args.dec_steps,
+        r = run_decoder(ctx, torch, stream, args.dec_batch or 64, steps=args.dec_steps, world=world, rank=rank,
                         layers=args.dec_layers)
         t_p = max_over_ranks(r["prefill_ms"])
         t_d = max_over_ranks(r["decode_ms"])
         if rank == 0:
-            r["prefill_tokens_per_s_all_gpus"] = round(world * r["batch_per_gpu"] * r["prefill_len"] / (t_p / 1e3), 1)
-            r["decode_tokens_per_s_all_gpus"] = round(world * r["batch_per_gpu"] * r["decode_steps"] / (t_d / 1e3), 1)
+            gb = args.dec_batch or 64
+            r["prefill_tokens_per_s_all_gpus"] = round(gb * r["prefill_len"] / (t_p / 1e3), 1)
+            r["decode_tokens_per_s_all_gpus"] = round(gb * r["decode_steps"] / (t_d / 1e3), 1)
             print(json.dumps({"case": "decoder", **r}), flush=True)
         ctx.close()
         if world > 1:
@@ -592,24 +600,24 @@ def main():
     conv_line = conv_configs(ctx, lib, N, stream, max(1, args.steps // 4), 3)
 
     # the int4 decoder chain, sequences sharded over ranks.
-    dec = run_decoder(ctx, torch, stream, max(1, 64 // world))
+    dec = run_decoder(ctx, torch, stream, 64, world=world, rank=rank)
     dec_tp = max_over_ranks(dec["prefill_ms"])
     dec_td = max_over_ranks(dec["decode_ms"])
-    dec_line = {"prefill_tokens_per_s": round(world * dec["batch_per_gpu"] * dec["prefill_len"] / (dec_tp / 1e3), 1),
-                "decode_tokens_per_s": round(world * dec["batch_per_gpu"] * dec["decode_steps"] / (dec_td / 1e3), 1),
-                "sequences": world * dec["batch_per_gpu"], "prefill_len": dec["prefill_len"],
+    dec_line = {"prefill_tokens_per_s": round(64 * dec["prefill_len"] / (dec_tp / 1e3), 1),
+                "decode_tokens_per_s": round(64 * dec["decode_steps"] / (dec_td / 1e3), 1),
+                "sequences": 64, "prefill_len": dec["prefill_len"],
                 "decode_steps": dec["decode_steps"], "decode_ms_per_step": dec["decode_ms_per_step"],
                 "tokens_valid": dec["tokens_valid"]}
 
     # the BERT-base fp32 chain, sequences sharded over ranks.
-    bert = run_bert(ctx, torch, stream, max(1, 32 // world), steps=5, warmup=3)
+    bert = run_bert(ctx, torch, stream, 32, steps=5, warmup=3, world=world, rank=rank)
     bert_tf = max_over_ranks(bert["forward_ms"])
     bert_te = max_over_ranks(bert["e2e_forward_ms"])
-    bert_tok = world * bert["batch_per_gpu"] * bert["seq"]
+    bert_tok = 32 * bert["seq"]
     bert_line = {"tokens_per_s": round(bert_tok / (bert_tf / 1e3), 1),
                  "e2e_tokens_per_s": round(bert_tok / (bert_te / 1e3), 1),
                  "forward_ms": bert["forward_ms"], "tflops_per_gpu": bert["tflops"],
-                 "sequences": world * bert["batch_per_gpu"], "seq": bert["seq"], "mode": bert["mode"],
+                 "sequences": 32, "seq": bert["seq"], "mode": bert["mode"],
                  "finite": bert["finite"]}
 
     # End to end through the host-buffer C-ABI call (pinned host memory).
