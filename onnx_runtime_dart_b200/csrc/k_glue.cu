@@ -337,14 +337,26 @@ __global__ void __launch_bounds__(256) layernorm_long_kernel(const float *x, con
 
 // y = silu(gate) * up, with gate / up either separate tensors or the two
 // halves of one [rows][2*D] tensor (a packed gate|up projection).
+__device__ __forceinline__ float silu_times(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
+// Rows over blockIdx.y, columns over x (float4 when VEC: D, both row strides
+// and the three pointers 16-byte aligned); no per-element index division.
+template <bool VEC>
 __global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__restrict__ up, int64_t g_rs,
                                 int64_t u_rs, float *y, int64_t rows, int64_t D) {
-  const int64_t total = rows * D;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / D, c = i % D;
-    const float g = gate[r * g_rs + c];
-    const float s = g / (1.f + expf(-g));
-    y[i] = s * up[r * u_rs + c];
+  const int64_t step = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const float *gr = gate + r * g_rs, *ur = up + r * u_rs;
+    float *yr = y + r * D;
+    if (VEC) {
+      for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < D / 4; c += step) {
+        const float4 g = reinterpret_cast<const float4 *>(gr)[c], u = reinterpret_cast<const float4 *>(ur)[c];
+        reinterpret_cast<float4 *>(yr)[c] =
+            make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z), silu_times(g.w, u.w));
+      }
+    } else {
+      for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < D; c += step) yr[c] = silu_times(gr[c], ur[c]);
+    }
   }
 }
 
@@ -1554,7 +1566,12 @@ void launch_layernorm(const float *x, const float *skip, const float *gamma, con
 void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
                      int64_t D, cudaStream_t s) {
   if (rows * D <= 0) return;
-  silu_mul_kernel<<<grid_for(rows * D, 256), 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D);
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const bool vec = D % 4 == 0 && g_rs % 4 == 0 && u_rs % 4 == 0 && al(gate) && al(up) && al(y);
+  const int64_t cols = vec ? D / 4 : D;
+  const dim3 grid((unsigned)std::min<int64_t>((cols + 255) / 256, 64), (unsigned)std::min<int64_t>(rows, 65535));
+  if (vec) silu_mul_kernel<true><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D);
+  else silu_mul_kernel<false><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D);
   B2M_CUDA(cudaGetLastError());
 }
 
