@@ -75,6 +75,9 @@ struct b2m_ctx {
   // Pinned staging for the host-buffer helpers.
   void *pinned = nullptr;
   size_t pinned_bytes = 0;
+  // Pinned copy of the device error word: a host-buffer call enqueues its
+  // read with the output copy and checks it after its one synchronisation.
+  int32_t *err_host = nullptr;
 };
 
 struct b2m_tensor {

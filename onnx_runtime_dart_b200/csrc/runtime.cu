@@ -91,6 +91,21 @@ void check_device_error(b2m_ctx *ctx) {
   }
 }
 
+// The same check for a caller that synchronises anyway: enqueue_error_read
+// before its cudaStreamSynchronize, raise_enqueued_error after it.
+void enqueue_error_read(b2m_ctx *ctx) {
+  B2M_CUDA(cudaMemcpyAsync(ctx->err_host, ctx->dev_err, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+}
+
+void raise_enqueued_error(b2m_ctx *ctx) {
+  const int32_t e = *ctx->err_host;
+  if (e != B2M_DEVERR_NONE) {
+    B2M_CUDA(cudaMemsetAsync(ctx->dev_err, 0, B2M_DEV_STATE_BYTES, ctx->stream));
+    *ctx->err_host = B2M_DEVERR_NONE;
+    b2m_throw(B2M_ERR_TIMEOUT, "a bounded device-side wait timed out (code " + std::to_string(e) + ")");
+  }
+}
+
 b2m_tensor *new_tensor(b2m_ctx *ctx, int32_t dtype, const int64_t *shape, int32_t rank) {
   B2M_REQUIRE(rank >= 0 && rank <= B2M_MAX_RANK, B2M_ERR_INVALID_ARGUMENT, "tensor rank out of range");
   B2M_REQUIRE(elem_size(dtype) > 0, B2M_ERR_INVALID_ARGUMENT, "unsupported tensor dtype");
@@ -645,6 +660,8 @@ B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx) {
     B2M_CUDA(cudaMalloc(&ctx->dev_err, B2M_DEV_STATE_BYTES));
     B2M_CUDA(cudaMemset(ctx->dev_err, 0, B2M_DEV_STATE_BYTES));
     ctx->dev_counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(ctx->dev_err) + 128);
+    B2M_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&ctx->err_host), sizeof(int32_t), cudaHostAllocDefault));
+    *ctx->err_host = B2M_DEVERR_NONE;
 
     const char *no_pdl = std::getenv("B2M_DISABLE_PDL");
     ctx->pdl = !(no_pdl && no_pdl[0] == '1');
@@ -661,6 +678,7 @@ B2M_API b2m_status b2m_shutdown(b2m_ctx *ctx) {
     if (ctx->scratch) cudaFreeAsync(ctx->scratch, ctx->own_stream);
     cudaStreamSynchronize(ctx->own_stream);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
+    if (ctx->err_host) cudaFreeHost(ctx->err_host);
     cudaFree(ctx->dev_err);
     cudaEventDestroy(ctx->ev0);
     cudaEventDestroy(ctx->ev1);
@@ -1384,8 +1402,9 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
     nbits_run(ctx, sc, da, m, w, db, mode, dy);
     timer.done();
     B2M_CUDA(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, ctx->stream));
+    enqueue_error_read(ctx);  // one synchronisation for Y and the error word
     B2M_CUDA(cudaStreamSynchronize(ctx->stream));
-    check_device_error(ctx);
+    raise_enqueued_error(ctx);
   });
 }
 
