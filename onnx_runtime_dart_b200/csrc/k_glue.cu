@@ -24,16 +24,6 @@
 
 namespace {
 
-__device__ __forceinline__ double warp_sum_d(double v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max_f(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
 __device__ __forceinline__ float warp_sum_f(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -1001,7 +991,7 @@ using b2m::umma_f16;
 using b2m::umma_idesc;
 using b2m::warp_wait_or_abort;
 
-constexpr int MTC_D = 64, MTC_T = 128;
+constexpr int MTC_D = 64;
 constexpr uint32_t MTC_QH = 0, MTC_QL = 16384, MTC_KH = 32768, MTC_KL = 49152;
 constexpr uint32_t MTC_PH = 0, MTC_PL = 32768;
 constexpr uint32_t MTC_VH = 65536, MTC_VL = 81920;
