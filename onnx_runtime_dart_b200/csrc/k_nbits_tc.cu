@@ -20,6 +20,7 @@
 #include <cuda.h>
 
 #include <algorithm>
+#include <climits>
 #include <type_traits>
 
 #include "b2m_internal.cuh"
@@ -438,9 +439,18 @@ __global__ void __launch_bounds__(512) f32_to_f16_rows(const float *A, __half *A
   pdl_launch_dependents();  // the GEMM may start its weight-side prologue now
   pdl_wait();               // A (and the scratch we overwrite) are free to use
   const int64_t total = M * K8;
+  const bool narrow = total < INT32_MAX;  // 32-bit index division
   for (int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x * 8) {
-    const int64_t m = idx / K8, k = idx % K8;
+    int64_t m, k;
+    if (narrow) {
+      const int q = (int)idx / (int)K8;
+      m = q;
+      k = (int)idx - q * (int)K8;
+    } else {
+      m = idx / K8;
+      k = idx % K8;
+    }
     float f[8];
     const float *row = A + m * K;
     if (vec) {  // rows start 16-byte aligned and K % 4 == 0: two 16-byte loads
@@ -451,14 +461,16 @@ __global__ void __launch_bounds__(512) f32_to_f16_rows(const float *A, __half *A
 #pragma unroll
       for (int j = 0; j < 8; j++) f[j] = k + j < K ? row[k + j] : 0.f;
     }
-    __align__(16) __half h[8];
+    // Two values per conversion (the same round-to-nearest as one at a time).
+    __align__(16) __half2 h[4];
     if (perm) {
-      const int P[8] = {0, 2, 1, 3, 4, 6, 5, 7};
-#pragma unroll
-      for (int j = 0; j < 8; j++) h[j] = __float2half_rn(f[P[j]]);
+      h[0] = __floats2half2_rn(f[0], f[2]);
+      h[1] = __floats2half2_rn(f[1], f[3]);
+      h[2] = __floats2half2_rn(f[4], f[6]);
+      h[3] = __floats2half2_rn(f[5], f[7]);
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; j++) h[j] = __float2half_rn(f[j]);
+      for (int j = 0; j < 4; j++) h[j] = __floats2half2_rn(f[2 * j], f[2 * j + 1]);
     }
     *reinterpret_cast<uint4 *>(A16 + idx) = *reinterpret_cast<const uint4 *>(h);
   }
