@@ -71,6 +71,10 @@ def attr_int(name, v):
     return f_bytes(1, name) + f_varint(3, v) + f_varint(20, 2)
 
 
+def attr_ints(name, values):
+    return f_bytes(1, name) + f_bytes(8, b"".join(_varint(int(v)) for v in values)) + f_varint(20, 7)
+
+
 def attr_float(name, v):
     return f_bytes(1, name) + f_float(2, v) + f_varint(20, 1)
 

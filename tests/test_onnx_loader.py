@@ -35,35 +35,44 @@ def build_model(tmp_path):
     c2 = rng.standard_normal(8).astype(np.float32)
     wq = rng.integers(-127, 128, (16, 12)).astype(np.int8)
     bq, sc, zp = _nbits_operands(rng, 64, 40, 32)
+    wc = (rng.standard_normal((4, 3, 3, 3)) * 0.2).astype(np.float32)   # Conv weight
+    bc = rng.standard_normal(4).astype(np.float32)
+    wi = rng.integers(-127, 128, (5, 2, 3, 3)).astype(np.int8)          # ConvInteger weight
     pad = b"\0" * 24
     ext = pad + w2.tobytes()
     inits = [W.tensor("w1", w1, "raw"),
              W.tensor("w2", w2, "external", external=("w.bin", len(pad), w2.nbytes)),
              W.tensor("c2", c2, "typed"),
              W.tensor("wq", wq, "typed"),
-             W.tensor("bq", bq, "raw"), W.tensor("sc", sc, "raw"), W.tensor("zp", zp, "raw")]
+             W.tensor("bq", bq, "raw"), W.tensor("sc", sc, "raw"), W.tensor("zp", zp, "raw"),
+             W.tensor("wc", wc, "raw"), W.tensor("bc", bc, "typed"), W.tensor("wi", wi, "raw")]
     nodes = [W.node("MatMul", ["x", "w1"], ["y1"]),
              W.node("Gemm", ["x24", "w2", "c2"], ["y2"], [W.attr_int("transB", 1), W.attr_float("alpha", 0.5)]),
              W.node("MatMulInteger", ["xq", "wq"], ["y3"]),
              W.node("MatMulNBits", ["x64", "bq", "sc", "zp"], ["y4"],
                     [W.attr_int("K", 64), W.attr_int("N", 40), W.attr_int("bits", 4), W.attr_int("block_size", 32)],
-                    domain="com.microsoft")]
-    path = _write(tmp_path, "m.onnx", nodes, inits, ["x", "x24", "xq", "x64"], ["y1", "y2", "y3", "y4"],
-                  {"w.bin": ext})
-    return path, dict(w1=w1, w2=w2, c2=c2, wq=wq, bq=bq, sc=sc, zp=zp)
+                    domain="com.microsoft"),
+             W.node("Conv", ["xc", "wc", "bc"], ["y5"], [W.attr_ints("pads", [1, 1, 1, 1]),
+                                                       W.attr_ints("kernel_shape", [3, 3])]),
+             W.node("ConvInteger", ["xi", "wi"], ["y6"], [W.attr_ints("strides", [2, 1])])]
+    path = _write(tmp_path, "m.onnx", nodes, inits, ["x", "x24", "xq", "x64", "xc", "xi"],
+                  ["y1", "y2", "y3", "y4", "y5", "y6"], {"w.bin": ext})
+    return path, dict(w1=w1, w2=w2, c2=c2, wq=wq, bq=bq, sc=sc, zp=zp, wc=wc, bc=bc, wi=wi)
 
 
 def test_reads_graph_initializers_and_external_data(tmp_path):
     path, ref = build_model(tmp_path)
     m = om.load_model(path)
-    assert [n.op_type for n in m.nodes] == ["MatMul", "Gemm", "MatMulInteger", "MatMulNBits"]
+    assert [n.op_type for n in m.nodes] == ["MatMul", "Gemm", "MatMulInteger", "MatMulNBits", "Conv", "ConvInteger"]
     assert m.nodes[1].attrs["transB"] == 1 and abs(m.nodes[1].attrs["alpha"] - 0.5) < 1e-7
     assert m.nodes[3].domain == "com.microsoft" and m.nodes[3].attrs["block_size"] == 32
+    assert m.nodes[4].attrs["pads"] == [1, 1, 1, 1] and m.nodes[5].attrs["strides"] == [2, 1]
     for k, v in ref.items():
         np.testing.assert_array_equal(m.initializers[k], v)
         assert m.initializers[k].dtype == v.dtype
     assert m.elem_types["wq"] == om.INT8 and m.elem_types["w2"] == om.FLOAT
-    assert m.inputs == ["x", "x24", "xq", "x64"] and m.outputs == ["y1", "y2", "y3", "y4"]
+    assert m.inputs == ["x", "x24", "xq", "x64", "xc", "xi"]
+    assert m.outputs == ["y1", "y2", "y3", "y4", "y5", "y6"]
 
 
 def test_tensor_decoding_rules():
@@ -116,7 +125,9 @@ def test_load_time_prepack_and_cache_match_first_use_packing(tmp_path):
     feeds = {"x": rng.standard_normal((5, 16)).astype(np.float32),
              "x24": rng.standard_normal((6, 24)).astype(np.float32),
              "xq": rng.integers(0, 256, (7, 16), dtype=np.uint8),
-             "x64": rng.standard_normal((9, 64)).astype(np.float32)}
+             "x64": rng.standard_normal((9, 64)).astype(np.float32),
+             "xc": rng.standard_normal((2, 3, 9, 9)).astype(np.float32),
+             "xi": rng.integers(0, 256, (1, 2, 7, 7), dtype=np.uint8)}
 
     def run(disp):
         out = []
@@ -128,16 +139,19 @@ def test_load_time_prepack_and_cache_match_first_use_packing(tmp_path):
 
     lazy = run(GpuDispatch(ctx, m.initializers, m.elem_types))
     eager, st0 = om.prepack_session(ctx, m)
-    assert st0["packed"] == 4
+    assert st0["packed"] == 6
     first = run(eager)
     cache = str(tmp_path / "cache")
     d1, st1 = om.prepack_session(ctx, m, cache_dir=cache)
-    assert st1["cache_misses"] == 4 and st1["cache_hits"] == 0
+    assert st1["cache_misses"] == 6 and st1["cache_hits"] == 0
     d2, st2 = om.prepack_session(ctx, m, cache_dir=cache)
-    assert st2["cache_hits"] == 4 and st2["cache_misses"] == 0
+    assert st2["cache_hits"] == 6 and st2["cache_misses"] == 0
     for a, b_, c, d in zip(lazy, first, run(d1), run(d2)):
         np.testing.assert_array_equal(a, b_)
         np.testing.assert_array_equal(a, c)
         np.testing.assert_array_equal(a, d)
+    import oracle
+    np.testing.assert_array_equal(lazy[4], oracle.conv_f32(feeds["xc"], ref["wc"], ref["bc"], None, [1, 1, 1, 1]))
+    np.testing.assert_array_equal(lazy[5].astype(np.int64), oracle.conv_integer(feeds["xi"], ref["wi"], strides=[2, 1]))
     np.testing.assert_array_equal(lazy[2].astype(np.int64),
                                   ops.as_reference_int64(ops.opMatMulInteger(feeds["xq"], ref["wq"], ctx=ctx)))
