@@ -1362,7 +1362,7 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
     }
   };
   if (kend > 0) load_tile(0);
-  for (int j0 = 0; j0 < kend && ok; j0 += 64, it++) {
+  for (int j0 = 0; j0 < kend; j0 += 64, it++) {
     // K tile: (key t, 8-dim chunk) items, split into the hi / lo planes.
 #pragma unroll
     for (int i = 0; i < KI; i++) {
@@ -1396,6 +1396,10 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if (*abort_flag) {  // read by every thread after the same barrier: a uniform exit
+      ok = false;
+      break;
+    }
     if (tid == 0) {
       constexpr uint32_t idesc_s = umma_idesc(128, 64, 1u, 1u, 1u);
       const uint32_t base = smem_u32(smem);
@@ -1485,10 +1489,9 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
         for (int j = 0; j < 16; j++) o[c0 + j] = fmaf(o[c0 + j], corr, __uint_as_float(v[j]));
       }
     }
-    tc_fence_before();
-    __syncthreads();  // P / K / V and both TMEM regions are free for the next tile
-    tc_fence_after();
-    ok = !*abort_flag;
+    // No barrier here: every thread has passed this tile's P.V completion
+    // (so K, V and P are free) and the next tile's first barrier orders the
+    // rest.
   }
   if (ok && q0 + r < a.S) {
     const float inv = 1.f / l;
