@@ -135,3 +135,25 @@ def test_product_path_has_no_oracle_or_cpu_fallback():
         if f.endswith(".py"):
             src = open(os.path.join(pkg, f)).read()
             assert not re.search(r"^\s*(import|from)\s+oracle\b", src, re.M), f
+
+
+def test_conv_spatial_attributes_are_length_checked():
+    # The C ABI reads kernel_shape[nd], strides[nd], pads[2 nd], dilations[nd];
+    # the Python layer rejects arrays of other lengths before any call.
+    from types import SimpleNamespace
+
+    from onnx_runtime_dart_b200 import _native as N
+    from onnx_runtime_dart_b200 import ops
+
+    pw = SimpleNamespace(shape=(8, 4, 3, 3))
+    (ks, _), (st, _), (pd, _), (dl, _) = ops._spatial_attrs(pw, [1, 2], [1, 1, 0, 0], None)
+    assert ks.tolist() == [3, 3] and st.tolist() == [1, 2] and pd.tolist() == [1, 1, 0, 0] and dl is None
+    with pytest.raises(N.ArgumentError, match="pads"):
+        ops._spatial_attrs(pw, None, [1, 1], None)
+    with pytest.raises(N.ArgumentError, match="strides"):
+        ops._spatial_attrs(pw, [1], None, None)
+    with pytest.raises(N.ArgumentError, match="dilations"):
+        ops._spatial_attrs(pw, None, None, [1, 1, 1])
+    with pytest.raises(N.ArgumentError, match="rank"):
+        ops._check_conv_rank(np.zeros((1, 4, 5)), pw, 3, 5)
+    assert ops.AUTO_PAD == {"NOTSET": 0, "SAME_UPPER": 1, "SAME_LOWER": 2, "VALID": 3}
