@@ -82,6 +82,9 @@ def _load():
                                              ctypes.POINTER(ctypes.c_double), _i64, ctypes.c_double, _i64, _i64p,
                                              _i64, _i64, _i64p]
     lib.orc_qlinear_conv_requant.restype = None
+    lib.orc_conv_transpose_f32.argtypes = [_f32p, _i64p, ctypes.c_int, _f32p, _i64p, _i64, _i64, _f32p, _i64p,
+                                           _i64p, _i64p, _i64p, _i64p, _f32p, _i64p]
+    lib.orc_conv_transpose_f32.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -356,3 +359,33 @@ def qlinear_conv(x, x_scale, x_zp, w, w_scale, w_zp, y_scale, y_zp, bias=None, s
                                      float(np.float32(np.asarray(y_scale).ravel()[0])), yz, _p(b, _i64p), lo, hi,
                                      _p(out, _i64p))
     return out
+
+
+def conv_transpose_f32(x, w, bias=None, strides=None, pads=None, dilations=None, output_padding=None,
+                       output_shape=None, group=1):
+    """``opConvTranspose`` (lib/src/onnx_nn_ops.dart:815-1060): the GEMM +
+    overlap-add path for one image of 1-D / 2-D without output_shape, the
+    generic double-product scatter otherwise."""
+    x = _c(x, np.float32)
+    w = _c(w, np.float32)
+    bias = _c(bias, np.float32)
+    nd = x.ndim - 2
+    arr = lambda v: np.array(v, np.int64)
+    ks = arr(w.shape[2:])
+    st = arr(strides if strides is not None else [1] * nd)
+    dl = arr(dilations if dilations is not None else [1] * nd)
+    op = arr(output_padding if output_padding is not None else [0] * nd)
+    pd = None if pads is None else arr(pads)
+    osh = None if output_shape is None else arr(list(output_shape)[-nd:])
+    mpg = w.shape[1]
+    out = np.zeros(x.shape[0] * mpg * group * 4 * int(np.prod([
+        (x.shape[2 + a] - 1) * st[a] + dl[a] * (ks[a] - 1) + 1 + op[a] for a in range(nd)])) + 16, np.float32)
+    osp = np.zeros(3, np.int64)
+    xs = arr(x.shape)
+    rc = _load().orc_conv_transpose_f32(_p(x, _f32p), _p(xs, _i64p), nd, _p(w, _f32p), _p(ks, _i64p), mpg,
+                                        int(group), _p(bias, _f32p), _p(st, _i64p), _p(pd, _i64p), _p(dl, _i64p),
+                                        _p(op, _i64p), _p(osh, _i64p), _p(out, _f32p), _p(osp, _i64p))
+    if rc:
+        raise ValueError(f"oracle conv_transpose: bad arguments ({rc})")
+    shape = [x.shape[0], mpg * group] + [int(v) for v in osp[:nd]]
+    return out[:int(np.prod(shape))].reshape(shape).copy()

@@ -712,3 +712,127 @@ ORC_API void orc_qlinear_conv_requant(const int64_t *acc, int64_t n, int64_t m, 
     }
   }
 }
+
+/* ------------------------------------------------------------------------- */
+/* ConvTranspose (opConvTranspose, lib/src/onnx_nn_ops.dart:815-1060)         */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * x [n][cin][sp...] (nd = 1..3), w [cin][mpg][k...], bias [m] or NULL, pads
+ * [begin..., end...], out_shape: the requested spatial output dims or NULL.
+ * With n == 1, nd <= 2 and no output_shape the reference takes its GEMM path
+ * (:850-963): per group, prod[mpg*kvol][H*W] = matmulKernel(W_g^T, X_g) (the
+ * gemm_column rule with m = mpg*kvol, k = cin/group, n = H*W), then an
+ * overlap-add of each (mm, kh, kw) plane into the float32 output (loop order
+ * mm, kh, kw, ih, iw) and the bias added in float32. Otherwise the generic
+ * scatter (:965-1050): for b, c, input position ii, tap ki (ascending), every
+ * non-zero input adds v * w in double onto the float32 output element, which
+ * is stored back as float32; then the bias. output_shape recomputes the pads
+ * (total = full - requested; end = total / 2, begin = total - end).
+ */
+ORC_API int orc_conv_transpose_f32(const float *x, const int64_t *xshape, int nd, const float *w,
+                                   const int64_t *kshape, int64_t mpg, int64_t group, const float *bias,
+                                   const int64_t *strides, const int64_t *pads_in, const int64_t *dil,
+                                   const int64_t *outpad, const int64_t *out_shape, float *out, int64_t *osp_out) {
+  if (nd < 1 || nd > 3) return -1;
+  const int64_t n = xshape[0], cin = xshape[1];
+  if (group < 1 || cin % group) return -2;
+  const int64_t cpg = cin / group, m = mpg * group;
+  int64_t p[6], osp[3];
+  for (int a = 0; a < 2 * nd; a++) p[a] = pads_in ? pads_in[a] : 0;
+  for (int a = 0; a < nd; a++) {
+    const int64_t full = (xshape[2 + a] - 1) * strides[a] + dil[a] * (kshape[a] - 1) + 1 + outpad[a];
+    if (out_shape) {
+      osp[a] = out_shape[a];
+      const int64_t total = full - osp[a];
+      p[nd + a] = total / 2;
+      p[a] = total - p[nd + a];
+    } else {
+      osp[a] = full - p[a] - p[nd + a];
+    }
+    if (osp[a] < 1) return -3;
+    osp_out[a] = osp[a];
+  }
+  int64_t in_n = 1, k_n = 1, out_n = 1;
+  for (int a = 0; a < nd; a++) {
+    in_n *= xshape[2 + a];
+    k_n *= kshape[a];
+    out_n *= osp[a];
+  }
+  for (int64_t i = 0; i < n * m * out_n; i++) out[i] = 0.0f;
+  if (nd <= 2 && !out_shape && n == 1) {
+    const int64_t H = nd == 2 ? xshape[2] : 1, W = xshape[1 + nd], kH = nd == 2 ? kshape[0] : 1,
+                  kW = kshape[nd - 1];
+    const int64_t sH = nd == 2 ? strides[0] : 1, sW = strides[nd - 1], dH = nd == 2 ? dil[0] : 1,
+                  dW = dil[nd - 1];
+    const int64_t pT = nd == 2 ? p[0] : 0, pL = nd == 2 ? p[1] : p[0];
+    const int64_t oH = nd == 2 ? osp[0] : 1, oW = osp[nd - 1];
+    const int64_t hw = H * W, mk = mpg * k_n;
+    float *wt = (float *)malloc(sizeof(float) * (size_t)(mk * cpg));
+    float *prod = (float *)malloc(sizeof(float) * (size_t)(mk * hw));
+    for (int64_t g = 0; g < group; g++) {
+      for (int64_t c = 0; c < cpg; c++)
+        for (int64_t idx = 0; idx < mk; idx++) wt[idx * cpg + c] = w[(g * cpg + c) * mk + idx];
+      for (int64_t j = 0; j < hw; j++) gemm_column(wt, cpg, x + g * cpg * hw, hw, prod, hw, mk, cpg, hw, j);
+      for (int64_t mm = 0; mm < mpg; mm++) {
+        float *ob = out + (g * mpg + mm) * oH * oW;
+        for (int64_t kh = 0; kh < kH; kh++)
+          for (int64_t kw = 0; kw < kW; kw++) {
+            const float *pb = prod + ((mm * kH + kh) * kW + kw) * hw;
+            for (int64_t ih = 0; ih < H; ih++) {
+              const int64_t oh = ih * sH + kh * dH - pT;
+              if (oh < 0 || oh >= oH) continue;
+              for (int64_t iw = 0; iw < W; iw++) {
+                const int64_t ow = iw * sW + kw * dW - pL;
+                if (ow >= 0 && ow < oW) ob[oh * oW + ow] = ob[oh * oW + ow] + pb[ih * W + iw];
+              }
+            }
+          }
+      }
+    }
+    free(wt);
+    free(prod);
+  } else {
+    int64_t ostr[3] = {1, 1, 1};
+    for (int a = nd - 2; a >= 0; a--) ostr[a] = ostr[a + 1] * osp[a + 1];
+    for (int64_t b = 0; b < n; b++)
+      for (int64_t c = 0; c < cin; c++) {
+        const int64_t g = c / cpg;
+        for (int64_t ii = 0; ii < in_n; ii++) {
+          const float v = x[(b * cin + c) * in_n + ii];
+          if (v == 0.0f) continue;
+          int64_t ic[3], rem = ii;
+          for (int a = nd - 1; a >= 0; a--) {
+            ic[a] = rem % xshape[2 + a];
+            rem /= xshape[2 + a];
+          }
+          for (int64_t ki = 0; ki < k_n; ki++) {
+            int64_t kc[3], kr = ki, off = 0;
+            for (int a = nd - 1; a >= 0; a--) {
+              kc[a] = kr % kshape[a];
+              kr /= kshape[a];
+            }
+            int inside = 1;
+            for (int a = 0; a < nd; a++) {
+              const int64_t oa = ic[a] * strides[a] + kc[a] * dil[a] - p[a];
+              if (oa < 0 || oa >= osp[a]) {
+                inside = 0;
+                break;
+              }
+              off += oa * ostr[a];
+            }
+            if (!inside) continue;
+            for (int64_t mm = 0; mm < mpg; mm++) {
+              float *o = out + (b * m + g * mpg + mm) * out_n + off;
+              *o = (float)((double)*o + (double)v * (double)w[(c * mpg + mm) * k_n + ki]);
+            }
+          }
+        }
+      }
+  }
+  if (bias)
+    for (int64_t b = 0; b < n; b++)
+      for (int64_t om = 0; om < m; om++)
+        for (int64_t k = 0; k < out_n; k++) out[(b * m + om) * out_n + k] = out[(b * m + om) * out_n + k] + bias[om];
+  return 0;
+}

@@ -44,6 +44,10 @@ def run_oracle(g):
         return oracle.qlinear_conv(x[0], x[1], x[2], x[3], x[4], x[5], x[6], x[7], x[8] if len(x) > 8 else None,
                                    at.get("strides"), at.get("pads"), at.get("dilations"), at.get("group", 1),
                                    -128 if int8 else 0, 127 if int8 else 255)
+    if op == "ConvTranspose":
+        return oracle.conv_transpose_f32(x[0], x[1], x[2] if len(x) > 2 else None, at.get("strides"), at.get("pads"),
+                                         at.get("dilations"), at.get("output_padding"), at.get("output_shape"),
+                                         at.get("group", 1))
     pytest.skip(f"{op} is not a MatMul-family op")
 
 
@@ -264,3 +268,44 @@ def test_conv_oracle_chunking_is_per_row():
                 for kx in range(3):
                     acc = np.float32(acc + np.float32(w[om, c, ky, kx] * xp[c, oy + ky, ox + kx]))
         assert got[0, om, oy, ox] == acc
+
+
+def _conv_transpose_f64(x, w, bias, s, p, d, op, group):
+    n, cin = x.shape[:2]
+    nd = x.ndim - 2
+    mpg = w.shape[1]
+    ks = w.shape[2:]
+    osp = [(x.shape[2 + a] - 1) * s[a] + d[a] * (ks[a] - 1) + 1 + op[a] - p[a] - p[nd + a] for a in range(nd)]
+    out = np.zeros([n, mpg * group] + osp)
+    cpg = cin // group
+    for idx in np.ndindex(*x.shape[2:]):
+        for kidx in np.ndindex(*ks):
+            o = [idx[a] * s[a] + kidx[a] * d[a] - p[a] for a in range(nd)]
+            if any(o[a] < 0 or o[a] >= osp[a] for a in range(nd)):
+                continue
+            for g in range(group):
+                xs = x[(slice(None), slice(g * cpg, (g + 1) * cpg)) + idx].astype(np.float64)   # [n, cpg]
+                ws = w[(slice(g * cpg, (g + 1) * cpg), slice(None)) + kidx].astype(np.float64)  # [cpg, mpg]
+                out[(slice(None), slice(g * mpg, (g + 1) * mpg)) + tuple(o)] += xs @ ws
+    if bias is not None:
+        out += bias.reshape([1, -1] + [1] * nd)
+    return out
+
+
+@pytest.mark.parametrize("cfg", [
+    # (n, cin, spatial, mpg, kernel, strides, pads, dilations, output_padding, group)
+    (1, 4, (6, 7), 3, (3, 2), (2, 1), (1, 0, 0, 1), (1, 2), (1, 0), 2),   # GEMM + overlap-add path
+    (2, 3, (5, 5), 2, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1), (0, 0), 1),   # generic scatter (two images)
+    (1, 2, (9,), 4, (5,), (3,), (2, 1), (1,), (2,), 1),                   # 1-D GEMM path
+    (1, 2, (3, 4, 3), 2, (2, 2, 2), (1, 2, 1), (0, 0, 0, 0, 1, 0), (1, 1, 1), (0, 0, 0), 1),  # 3-D
+])
+def test_conv_transpose_oracle_vs_float64(cfg):
+    n, cin, sp, mpg, ks, s, p, d, op, grp = cfg
+    rng = np.random.default_rng(len(sp) + cin)
+    x = rng.standard_normal((n, cin, *sp)).astype(np.float32)
+    w = (rng.standard_normal((cin, mpg, *ks)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(mpg * grp).astype(np.float32)
+    got = oracle.conv_transpose_f32(x, w, b, s, p, d, op, None, grp)
+    want = _conv_transpose_f64(x, w, b, s, p, d, op, grp)
+    assert got.shape == want.shape
+    assert np.max(np.abs(got - want)) <= 1e-5 * max(1.0, np.max(np.abs(want)))
