@@ -420,6 +420,21 @@ B2M_API b2m_status b2m_qlinear_conv(b2m_ctx *ctx, const b2m_tensor *x, float x_s
                                     const int64_t *kernel_shape, const int64_t *strides, const int64_t *pads,
                                     const int64_t *dilations, int32_t group, int32_t lo, int32_t hi, b2m_tensor **y);
 
+/* ConvTranspose (opConvTranspose, lib/src/onnx_nn_ops.dart:815-1060; dispatch
+ * onnx_graph.dart:2491-2515): x float [n][C][spatial...] (1-3 spatial dims),
+ * w float [C][M/group][kernel...] (a device tensor, read as is), bias
+ * float[M] or NULL; strides / dilations / output_padding [nd] or NULL
+ * (1 / 1 / 0), pads [2 nd] or NULL, output_shape [nd] (the spatial dims) or
+ * NULL. y: [n][M][out...]. The reference's arithmetic in every call: for one
+ * image of 1-D / 2-D without output_shape, the exact GEMM W_g^T . X_g (the
+ * matmulKernel rule) and an overlap-add in float32; otherwise its scatter,
+ * each non-zero input adding x * w in double onto the float32 output, in
+ * the reference's order; then the bias in float32. */
+B2M_API b2m_status b2m_conv_transpose_f32(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *w,
+                                          const b2m_tensor *bias, const int64_t *strides, const int64_t *pads,
+                                          const int64_t *dilations, const int64_t *output_padding,
+                                          const int64_t *output_shape, int32_t group, b2m_tensor **y);
+
 /* Serialises a packed weight (its device layouts, as prepacked) into buf, for
  * an on-disk prepack cache: *needed receives the byte size; with buf NULL
  * only the size is returned. The blob is tied to this library's

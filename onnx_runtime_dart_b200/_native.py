@@ -125,6 +125,8 @@ SIGNATURES = {
                                         ctypes.POINTER(_c_weight)]),
     "b2m_weight_free": (_i32, [_c_weight]),
     "b2m_weight_prepack_conv": (_i32, [_c_ctx, _vp, _i32, _i64, _i64, ctypes.POINTER(_c_weight)]),
+    "b2m_conv_transpose_f32": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_tensor, _vp, _vp, _vp, _vp, _vp, _i32,
+                                      ctypes.POINTER(_c_tensor)]),
     "b2m_conv_f32": (_i32, [_c_ctx, _c_tensor, _c_weight, _c_tensor, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                             ctypes.POINTER(_c_tensor)]),
     "b2m_conv_integer": (_i32, [_c_ctx, _c_tensor, _c_tensor, _c_weight, _c_tensor, _vp, _vp, _vp, _vp, _i32,

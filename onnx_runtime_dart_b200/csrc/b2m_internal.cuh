@@ -247,6 +247,25 @@ void launch_conv_im2col_i8(const void *x, const ConvGeom &g, int64_t grp, int64_
 // pad_taps != 0 also adds the zero products of padded taps.
 void launch_conv_direct_double(const float *x, const float *wt, const float *bias, const ConvGeom &g, int pad_taps,
                                float *y, cudaStream_t s);
+// ConvTranspose geometry (1-3 spatial dims carried as three): input [n][cin]
+// [in...], weight [cin][mpg][k...], output [n][m][out...]; pad = leading pads
+// (after output_shape has been resolved).
+struct ConvTGeom {
+  int64_t n = 0, cin = 0, m = 0, group = 1, cpg = 0, mpg = 0;
+  int64_t in[3] = {1, 1, 1}, k[3] = {1, 1, 1}, st[3] = {1, 1, 1}, dil[3] = {1, 1, 1}, pad[3] = {0, 0, 0};
+  int64_t out[3] = {1, 1, 1};
+};
+// Overlap-add of one group's GEMM planes prod[mpg * kvol][in_h * in_w] (one
+// image, depth 1) into y [m][out_h][out_w]: each output element sums its
+// planes in (kh, kw) order in float32, then adds the bias.
+void launch_conv_transpose_col2im(const float *prod, const ConvTGeom &g, int64_t grp, const float *bias, float *y,
+                                  cudaStream_t s);
+// The reference's generic scatter, gathered per output element: over input
+// channels of the group, then input positions in ascending order, each
+// non-zero input adds x * w in double onto the float32 value; then the bias.
+void launch_conv_transpose_scatter(const float *x, const float *w, const float *bias, const ConvTGeom &g, float *y,
+                                   cudaStream_t s);
+
 // QLinearConv's requantisation: q = roundEven((z + bias[ch]) * mult) + y_zp
 // clamped to [lo, hi], mult = x_scale * w_scale[ch or 0] / y_scale in double.
 struct ConvRequant {

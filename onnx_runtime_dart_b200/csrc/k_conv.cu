@@ -337,6 +337,84 @@ __global__ void __launch_bounds__(256) conv_scatter_kernel(const int32_t *__rest
   }
 }
 
+// ConvTranspose, GEMM path: one thread per output element of the group.
+__global__ void __launch_bounds__(256) conv_transpose_col2im_kernel(const float *__restrict__ prod, const ConvTGeom g,
+                                                                    int64_t grp, const float *__restrict__ bias,
+                                                                    float *__restrict__ y) {
+  const int64_t out_hw = g.out[1] * g.out[2], in_hw = g.in[1] * g.in[2];
+  const int64_t total = g.mpg * out_hw;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t mm = i / out_hw, r = i - mm * out_hw;
+    const int64_t oh = r / g.out[2], ow = r - oh * g.out[2];
+    float acc = 0.f;
+    for (int64_t kh = 0; kh < g.k[1]; kh++) {
+      const int64_t nh = oh + g.pad[1] - kh * g.dil[1];
+      if (nh < 0 || nh % g.st[1]) continue;
+      const int64_t ih = nh / g.st[1];
+      if (ih >= g.in[1]) continue;
+      for (int64_t kw = 0; kw < g.k[2]; kw++) {
+        const int64_t nw = ow + g.pad[2] - kw * g.dil[2];
+        if (nw < 0 || nw % g.st[2]) continue;
+        const int64_t iw = nw / g.st[2];
+        if (iw >= g.in[2]) continue;
+        acc = __fadd_rn(acc, __ldg(prod + ((mm * g.k[1] + kh) * g.k[2] + kw) * in_hw + ih * g.in[2] + iw));
+      }
+    }
+    const int64_t om = grp * g.mpg + mm;
+    if (bias) acc = __fadd_rn(acc, __ldg(bias + om));
+    y[om * out_hw + r] = acc;
+  }
+}
+
+// ConvTranspose, generic path: one thread per output element (b, om, o).
+// For a fixed output, input position i along an axis pairs with the single
+// tap k = (o + pad - i * stride) / dilation, so walking k downwards walks i
+// upwards: the loops visit (c, i0, i1, i2) in the reference's order.
+__global__ void __launch_bounds__(256) conv_transpose_scatter_kernel(const float *__restrict__ x,
+                                                                     const float *__restrict__ w,
+                                                                     const float *__restrict__ bias, const ConvTGeom g,
+                                                                     float *__restrict__ y) {
+  const int64_t out_n = g.out[0] * g.out[1] * g.out[2];
+  const int64_t kvol = g.k[0] * g.k[1] * g.k[2];
+  const int64_t total = g.n * g.m * out_n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i % out_n, bm = i / out_n;
+    const int64_t om = bm % g.m, b = bm / g.m;
+    const int64_t grp = om / g.mpg, mm = om - grp * g.mpg;
+    const int64_t o2 = r % g.out[2], o1 = (r / g.out[2]) % g.out[1], o0 = r / (g.out[1] * g.out[2]);
+    float acc = 0.f;
+    for (int64_t c = grp * g.cpg; c < (grp + 1) * g.cpg; c++) {
+      const float *xc = x + (b * g.cin + c) * g.in[0] * g.in[1] * g.in[2];
+      const float *wc = w + (c * g.mpg + mm) * kvol;
+      for (int64_t k0 = g.k[0] - 1; k0 >= 0; k0--) {
+        const int64_t n0 = o0 + g.pad[0] - k0 * g.dil[0];
+        if (n0 < 0 || n0 % g.st[0]) continue;
+        const int64_t i0 = n0 / g.st[0];
+        if (i0 >= g.in[0]) continue;
+        for (int64_t k1 = g.k[1] - 1; k1 >= 0; k1--) {
+          const int64_t n1 = o1 + g.pad[1] - k1 * g.dil[1];
+          if (n1 < 0 || n1 % g.st[1]) continue;
+          const int64_t i1 = n1 / g.st[1];
+          if (i1 >= g.in[1]) continue;
+          for (int64_t k2 = g.k[2] - 1; k2 >= 0; k2--) {
+            const int64_t n2 = o2 + g.pad[2] - k2 * g.dil[2];
+            if (n2 < 0 || n2 % g.st[2]) continue;
+            const int64_t i2 = n2 / g.st[2];
+            if (i2 >= g.in[2]) continue;
+            const float v = __ldg(xc + (i0 * g.in[1] + i1) * g.in[2] + i2);
+            if (v == 0.f) continue;
+            // float x float is exact in double; one double add, then float32.
+            const double p = __dmul_rn((double)v, (double)__ldg(wc + (k0 * g.k[1] + k1) * g.k[2] + k2));
+            acc = __double2float_rn(__dadd_rn((double)acc, p));
+          }
+        }
+      }
+    }
+    if (bias) acc = __fadd_rn(acc, __ldg(bias + om));
+    y[i] = acc;
+  }
+}
+
 unsigned grid_for(int64_t total) {
   const int64_t want = (total + 255) / 256;
   return (unsigned)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)device_sm_count() * 16));
@@ -398,5 +476,21 @@ void launch_conv_scatter(const int32_t *z, const ConvGeom &g, int64_t grp, int64
   if (!yq) conv_scatter_kernel<false, false><<<grid, 256, 0, s>>>(z, g32, grp, b0, rows, y32, q, rq);
   else if (rq.lo < 0) conv_scatter_kernel<true, true><<<grid, 256, 0, s>>>(z, g32, grp, b0, rows, y32, q, rq);
   else conv_scatter_kernel<true, false><<<grid, 256, 0, s>>>(z, g32, grp, b0, rows, y32, q, rq);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_conv_transpose_col2im(const float *prod, const ConvTGeom &g, int64_t grp, const float *bias, float *y,
+                                  cudaStream_t s) {
+  const int64_t total = g.mpg * g.out[1] * g.out[2];
+  if (total <= 0) return;
+  conv_transpose_col2im_kernel<<<grid_for(total), 256, 0, s>>>(prod, g, grp, bias, y);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_conv_transpose_scatter(const float *x, const float *w, const float *bias, const ConvTGeom &g, float *y,
+                                   cudaStream_t s) {
+  const int64_t total = g.n * g.m * g.out[0] * g.out[1] * g.out[2];
+  if (total <= 0) return;
+  conv_transpose_scatter_kernel<<<grid_for(total), 256, 0, s>>>(x, w, bias, g, y);
   B2M_CUDA(cudaGetLastError());
 }

@@ -1906,9 +1906,115 @@ void conv_int_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *xzp, con
   timer.done();
 }
 
+// ConvTranspose (opConvTranspose, onnx_nn_ops.dart:815-1060): the
+// reference's two arithmetics, in EXACT terms for every call.
+void conv_transpose_impl(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *w, const b2m_tensor *bias,
+                         const int64_t *strides, const int64_t *pads, const int64_t *dilations,
+                         const int64_t *output_padding, const int64_t *output_shape, int32_t group, b2m_tensor **y) {
+  require_float(x, "ConvTranspose input");
+  require_float(w, "ConvTranspose weight");
+  B2M_REQUIRE(x->rank >= 3 && x->rank <= 5, B2M_ERR_UNSUPPORTED,
+              "ConvTranspose supports 1-3 spatial dims, got rank " + std::to_string(x->rank));
+  B2M_REQUIRE(w->rank == x->rank, B2M_ERR_INVALID_ARGUMENT, "ConvTranspose weight rank must match input rank");
+  const int nd = x->rank - 2;
+  B2M_REQUIRE(group >= 1 && x->shape[1] % group == 0 && w->shape[0] == x->shape[1], B2M_ERR_INVALID_ARGUMENT,
+              "ConvTranspose channel mismatch: input C=" + std::to_string(x->shape[1]) + ", weight C=" +
+                  std::to_string(w->shape[0]) + ", group=" + std::to_string(group));
+  ConvTGeom g;
+  g.n = x->shape[0];
+  g.cin = x->shape[1];
+  g.group = group;
+  g.cpg = g.cin / group;
+  g.mpg = w->shape[1];
+  g.m = g.mpg * group;
+  const int off = 3 - nd;
+  for (int a = 0; a < nd; a++) {
+    const int64_t in = x->shape[2 + a], k = w->shape[2 + a];
+    const int64_t s = strides ? strides[a] : 1, d = dilations ? dilations[a] : 1;
+    const int64_t op = output_padding ? output_padding[a] : 0;
+    B2M_REQUIRE(s >= 1 && d >= 1 && op >= 0 && k >= 1, B2M_ERR_INVALID_ARGUMENT,
+                "ConvTranspose: strides / dilations must be >= 1, output_padding >= 0");
+    const int64_t full = (in - 1) * s + d * (k - 1) + 1 + op;
+    int64_t pb = pads ? pads[a] : 0, pe = pads ? pads[nd + a] : 0, out;
+    if (output_shape) {
+      // The spec's split of the difference, the larger half at the start.
+      out = output_shape[a];
+      const int64_t total = full - out;
+      pe = total / 2;
+      pb = total - pe;
+    } else {
+      B2M_REQUIRE(pb >= 0 && pe >= 0, B2M_ERR_INVALID_ARGUMENT, "ConvTranspose: pads must be >= 0");
+      out = full - pb - pe;
+    }
+    B2M_REQUIRE(out >= 1, B2M_ERR_INVALID_ARGUMENT, "ConvTranspose: empty output along a spatial axis");
+    g.in[off + a] = in;
+    g.k[off + a] = k;
+    g.st[off + a] = s;
+    g.dil[off + a] = d;
+    g.pad[off + a] = pb;
+    g.out[off + a] = out;
+  }
+  if (bias) {
+    require_float(bias, "ConvTranspose bias");
+    B2M_REQUIRE(bias->numel == g.m, B2M_ERR_INVALID_ARGUMENT,
+                "ConvTranspose: bias must have one value per output channel");
+  }
+  check_cancel(ctx);
+  std::vector<int64_t> oshape = {g.n, g.m};
+  for (int a = off; a < 3; a++) oshape.push_back(g.out[a]);
+  b2m_tensor *out = prepare_output(ctx, y, B2M_FLOAT, oshape);
+  if (out->numel == 0) return;
+  OpTimer timer(ctx);
+  const float *xd = static_cast<const float *>(x->data), *wd = static_cast<const float *>(w->data);
+  const float *bd = bias ? static_cast<const float *>(bias->data) : nullptr;
+  float *yd = static_cast<float *>(out->data);
+  if (nd <= 2 && !output_shape && g.n == 1) {
+    // GEMM path (:850-963): prod[mpg*kvol][H*W] = W_g^T . X_g, then overlap-add.
+    const int64_t kvol = g.k[1] * g.k[2], mk = g.mpg * kvol, hw = g.in[1] * g.in[2];
+    B2M_REQUIRE(mk <= 65535, B2M_ERR_UNSUPPORTED, "ConvTranspose: too many output planes per group");
+    Scratch sc(ctx, (size_t)(mk * hw * 4) + 256);
+    float *prod = static_cast<float *>(sc.take((size_t)(mk * hw * 4)));
+    for (int64_t grp = 0; grp < g.group; grp++) {
+      F32GemmArgs p;
+      p.A = wd + grp * g.cpg * mk;  // A(i, c) = W[grp * cpg + c][i]
+      p.sa_m = 1;
+      p.sa_k = mk;
+      p.B = xd + grp * g.cpg * hw;
+      p.sb_k = hw;
+      p.sb_n = 1;
+      p.Y = prod;
+      p.ldy = hw;
+      p.M = mk;
+      p.N = hw;
+      p.K = g.cpg;
+      p.batch = 1;
+      p.m_eff = mk;
+      p.tile_w = hw;
+      p.epi = EPI_NONE;
+      p.dev_err = ctx->dev_err;
+      launch_f32_exact(p, ctx->stream);
+      launch_conv_transpose_col2im(prod, g, grp, bd, yd, ctx->stream);
+    }
+  } else {
+    launch_conv_transpose_scatter(xd, wd, bd, g, yd, ctx->stream);
+  }
+  timer.done();
+}
+
 }  // namespace
 
 extern "C" {
+
+B2M_API b2m_status b2m_conv_transpose_f32(b2m_ctx *ctx, const b2m_tensor *x, const b2m_tensor *w,
+                                          const b2m_tensor *bias, const int64_t *strides, const int64_t *pads,
+                                          const int64_t *dilations, const int64_t *output_padding,
+                                          const int64_t *output_shape, int32_t group, b2m_tensor **y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    conv_transpose_impl(ctx, x, w, bias, strides, pads, dilations, output_padding, output_shape, group, y);
+  });
+}
 
 B2M_API b2m_status b2m_weight_prepack_conv(b2m_ctx *ctx, const void *host_w, int32_t dtype, int64_t m, int64_t k,
                                            b2m_weight **out) {

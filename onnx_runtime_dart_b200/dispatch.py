@@ -11,6 +11,7 @@ reference's cases line for line:
   'Conv'          onnx_graph.dart:2436-2490  (kernel_shape checked against the weight)
   'ConvInteger'   onnx_graph.dart:2889-2901
   'QLinearConv'   onnx_graph.dart:2935-2956  (lo/hi from y_zero_point's elem type)
+  'ConvTranspose' onnx_graph.dart:2491-2515  (kernel_shape checked against the weight)
 Initializer weights are prepacked on first use and cached by initializer name
 (the reference's `_prepackedGemmB`, onnx_graph.dart:102-105); the graph itself
 is unchanged. Ops outside the family return None, leaving the reference's own
@@ -27,7 +28,7 @@ from .runtime import Context, DeviceTensor
 
 class GpuDispatch:
     HANDLED = ("MatMul", "Gemm", "MatMulInteger", "QLinearMatMul", "MatMulNBits", "Conv", "ConvInteger",
-               "QLinearConv")
+               "QLinearConv", "ConvTranspose")
 
     def __init__(self, ctx: Context, initializers: dict, initializer_elem_types: dict | None = None,
                  f32_mode: int = ops.MODE_EXACT, nbits_mode: int = ops.MODE_FAST):
@@ -92,6 +93,19 @@ class GpuDispatch:
                                         lo=-128 if int8 else 0, hi=127 if int8 else 255, ctx=ctx)]
         if op_type in ("Conv", "ConvInteger", "QLinearConv"):
             return [self._conv(op_type, input_names, need, opt, attrs)]
+        if op_type == "ConvTranspose":
+            w = need(1)
+            declared = attrs.get("kernel_shape")
+            kernel = [int(v) for v in (w.shape if hasattr(w, "shape") else np.shape(w))[2:]]
+            if declared is not None and [int(v) for v in declared] != kernel:
+                raise N.StateError(f"ConvTranspose kernel_shape {list(declared)} does not match weight shape "
+                                   f"{kernel}.")
+            if self._is_init(input_names[1]) and not isinstance(w, DeviceTensor):
+                w = self._packed_for(("convT", input_names[1]), lambda: ctx.upload(np.asarray(w, np.float32)))
+            return [ops.opConvTranspose(need(0), w, opt(2), strides=attrs.get("strides"), pads=attrs.get("pads"),
+                                        dilations=attrs.get("dilations"), outputPadding=attrs.get("output_padding"),
+                                        outputShape=attrs.get("output_shape"), group=int(attrs.get("group", 1)),
+                                        ctx=ctx)]
         # MatMulNBits
         if len(input_names) > 4 and input_names[4]:
             raise N.UnsupportedError("MatMulNBits: g_idx input not supported")

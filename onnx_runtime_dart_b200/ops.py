@@ -9,6 +9,7 @@ Same names, argument meaning and error behaviour as
   opConv           lib/src/onnx_nn_ops.dart:179-545
   opConvInteger    lib/src/onnx_qlinear_ops.dart:305-338
   opQLinearConv    lib/src/onnx_qlinear_ops.dart:341-382
+  opConvTranspose  lib/src/onnx_nn_ops.dart:815-1060
 but executed by libb200mm.so on the GPU. Operands may be numpy arrays (host
 values, uploaded for the call), DeviceTensor (device-resident, e.g. the output
 of a previous op), or — for the weight operand — a PackedWeight prepared once
@@ -388,4 +389,30 @@ def opQLinearConv(x, xS, xZp, w, wS, wZp, yS, yZp, bias=None, *, strides=None, p
         if tmp is not None:
             ctx.synchronize()
             tmp.free()
+    return _wrap_out(ctx, y, out)
+
+
+def opConvTranspose(x, w, bias=None, *, strides=None, pads=None, dilations=None, outputPadding=None,
+                    outputShape=None, group: int = 1, ctx: Context | None = None, out: DeviceTensor | None = None):
+    """ConvTranspose over 1-3 spatial dims: x [N][C][spatial...], w
+    [C][M/group][kernel...] (host array or DeviceTensor), bias [M]. Pads are
+    [begin..., end...]; output_shape lists the spatial dims (or the full
+    N, C, spatial shape, of which the last nd entries are used)."""
+    ctx = _ctx(ctx)
+    xh, _x = _dev(ctx, x, np.float32)
+    wh, _w = _dev(ctx, w, np.float32)
+    bh, _b = _dev(ctx, bias, np.float32)
+    xr = len(x.shape) if hasattr(x, "shape") else np.ndim(x)
+    nd = xr - 2
+    if 1 <= nd <= 3:
+        st, stp = _i64_array(strides, nd, "strides")
+        pd, pdp = _i64_array(pads, 2 * nd, "pads")
+        dl, dlp = _i64_array(dilations, nd, "dilations")
+        op, opp = _i64_array(outputPadding, nd, "output_padding")
+        osh, oshp = _i64_array(None if outputShape is None else list(outputShape)[-nd:], nd, "output_shape")
+    else:
+        stp = pdp = dlp = opp = oshp = None
+    y = _out(out)
+    N.check(ctx.lib.b2m_conv_transpose_f32(ctx.handle, xh, wh, bh, stp, pdp, dlp, opp, oshp, int(group),
+                                           ctypes.byref(y)))
     return _wrap_out(ctx, y, out)

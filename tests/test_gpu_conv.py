@@ -172,3 +172,45 @@ def test_conv_integer_errors(ctx):
     with pytest.raises(N.UnsupportedError, match="2-D"):
         ops.opQLinearConv(x.reshape(1, 2, 25), 0.1, None, pw, np.float32([0.1]), None, 0.1, None, lo=0, hi=255,
                           ctx=ctx)
+
+
+# (n, cin, spatial, mpg, kernel, strides, pads, dilations, output_padding, output_shape, group)
+CT_CASES = [
+    (1, 4, (6, 7), 3, (3, 2), (2, 1), (1, 0, 0, 1), (1, 2), (1, 0), None, 2),      # GEMM + overlap-add
+    (1, 16, (14, 14), 8, (4, 4), (2, 2), (1, 1, 1, 1), (1, 1), (0, 0), None, 1),  # decoder-style upsampling
+    (1, 2, (9,), 4, (5,), (3,), (2, 1), (1,), (2,), None, 1),                     # 1-D GEMM path
+    (1, 2, (5,), 1, (3,), (1,), (0, 0), (1,), (0,), None, 1),                     # 3 planes: double tails
+    (2, 3, (5, 5), 2, (3, 3), (2, 2), (1, 1, 1, 1), (1, 1), (0, 0), None, 1),     # two images: scatter
+    (1, 2, (5, 5), 3, (3, 3), (2, 2), None, (1, 1), (0, 0), (10, 10), 1),         # output_shape: scatter
+    (1, 2, (3, 4, 3), 2, (2, 2, 2), (1, 2, 1), (0, 0, 0, 0, 1, 0), (1, 1, 1), (0, 0, 0), None, 1),  # 3-D
+]
+
+
+@pytest.mark.parametrize("case", CT_CASES, ids=[f"cfg{i}" for i in range(len(CT_CASES))])
+def test_conv_transpose_bitwise(ctx, case):
+    n, cin, sp, mpg, ks, st, pd, dl, op, osh, grp = case
+    rng = np.random.default_rng(cin * 10 + len(sp))
+    x = rng.standard_normal((n, cin, *sp)).astype(np.float32)
+    x[x > 1.5] = 0.0  # zero inputs, which the reference's scatter skips
+    w = (rng.standard_normal((cin, mpg, *ks)) * 0.3).astype(np.float32)
+    b = rng.standard_normal(mpg * grp).astype(np.float32)
+    want = oracle.conv_transpose_f32(x, w, b, st, pd, dl, op, osh, grp)
+    got = ops.opConvTranspose(x, w, b, strides=st, pads=pd, dilations=dl, outputPadding=op, outputShape=osh,
+                              group=grp, ctx=ctx).numpy()
+    assert got.shape == want.shape
+    np.testing.assert_array_equal(got, want)
+
+
+def test_conv_transpose_errors(ctx):
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((1, 4, 5, 5)).astype(np.float32)
+    w = rng.standard_normal((4, 2, 3, 3)).astype(np.float32)
+    with pytest.raises(N.ArgumentError, match="channel mismatch"):
+        ops.opConvTranspose(x, w[:3], ctx=ctx)
+    with pytest.raises(N.ArgumentError, match="rank"):
+        ops.opConvTranspose(x, w[:, :, :, 0], ctx=ctx)
+    with pytest.raises(N.ArgumentError, match="bias"):
+        ops.opConvTranspose(x, w, np.zeros(3, np.float32), ctx=ctx)
+    d = GpuDispatch(ctx, {"w": w}, {})
+    with pytest.raises(N.StateError, match="kernel_shape"):
+        d.dispatch("ConvTranspose", ["x", "w"], [x, w], {"kernel_shape": [2, 2]})
