@@ -330,8 +330,9 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
     """A dispatch.GpuDispatch for `model` with every MatMul-family initializer
     weight packed now (MatMul / Gemm fp32 B, Gemm transB applied at pack time,
     MatMulInteger / QLinearMatMul int8 B, MatMulNBits b_q + scales + zero
-    points, Conv / ConvInteger / QLinearConv weights), under the keys the
-    dispatch uses. Returns (dispatch, stats)."""
+    points, Conv / ConvInteger / QLinearConv weights; ConvTranspose weights
+    are uploaded as they are), under the keys the dispatch uses. Returns
+    (dispatch, stats)."""
     from . import ops
     from .dispatch import GpuDispatch
 
@@ -374,6 +375,10 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
                     and inits[ins[wi]].dtype in (np.float32, np.int8, np.uint8):
                 wt = inits[ins[wi]]
                 packed(("conv", ins[wi]), "conv", (), [wt], lambda wt=wt: ctx.prepack_conv(wt))
+        elif nd.op_type == "ConvTranspose" and len(ins) > 1 and ins[1] in inits \
+                and inits[ins[1]].dtype == np.float32 and ("convT", ins[1]) not in disp._packed:
+            # Read as is by the kernels: uploaded once, nothing to pack or cache.
+            disp._packed[("convT", ins[1])] = ctx.upload(np.ascontiguousarray(inits[ins[1]]))
         elif nd.op_type == "MatMulNBits" and len(ins) > 2 and ins[1] in inits and ins[2] in inits:
             k, n = int(nd.attrs["K"]), int(nd.attrs["N"])
             bits, block = int(nd.attrs.get("bits", 4)), int(nd.attrs["block_size"])

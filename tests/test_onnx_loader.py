@@ -38,6 +38,7 @@ def build_model(tmp_path):
     wc = (rng.standard_normal((4, 3, 3, 3)) * 0.2).astype(np.float32)   # Conv weight
     bc = rng.standard_normal(4).astype(np.float32)
     wi = rng.integers(-127, 128, (5, 2, 3, 3)).astype(np.int8)          # ConvInteger weight
+    wt = (rng.standard_normal((3, 2, 2, 2)) * 0.5).astype(np.float32)   # ConvTranspose weight
     pad = b"\0" * 24
     ext = pad + w2.tobytes()
     inits = [W.tensor("w1", w1, "raw"),
@@ -45,7 +46,8 @@ def build_model(tmp_path):
              W.tensor("c2", c2, "typed"),
              W.tensor("wq", wq, "typed"),
              W.tensor("bq", bq, "raw"), W.tensor("sc", sc, "raw"), W.tensor("zp", zp, "raw"),
-             W.tensor("wc", wc, "raw"), W.tensor("bc", bc, "typed"), W.tensor("wi", wi, "raw")]
+             W.tensor("wc", wc, "raw"), W.tensor("bc", bc, "typed"), W.tensor("wi", wi, "raw"),
+             W.tensor("wt", wt, "raw")]
     nodes = [W.node("MatMul", ["x", "w1"], ["y1"]),
              W.node("Gemm", ["x24", "w2", "c2"], ["y2"], [W.attr_int("transB", 1), W.attr_float("alpha", 0.5)]),
              W.node("MatMulInteger", ["xq", "wq"], ["y3"]),
@@ -54,16 +56,18 @@ def build_model(tmp_path):
                     domain="com.microsoft"),
              W.node("Conv", ["xc", "wc", "bc"], ["y5"], [W.attr_ints("pads", [1, 1, 1, 1]),
                                                        W.attr_ints("kernel_shape", [3, 3])]),
-             W.node("ConvInteger", ["xi", "wi"], ["y6"], [W.attr_ints("strides", [2, 1])])]
-    path = _write(tmp_path, "m.onnx", nodes, inits, ["x", "x24", "xq", "x64", "xc", "xi"],
-                  ["y1", "y2", "y3", "y4", "y5", "y6"], {"w.bin": ext})
-    return path, dict(w1=w1, w2=w2, c2=c2, wq=wq, bq=bq, sc=sc, zp=zp, wc=wc, bc=bc, wi=wi)
+             W.node("ConvInteger", ["xi", "wi"], ["y6"], [W.attr_ints("strides", [2, 1])]),
+             W.node("ConvTranspose", ["xt", "wt"], ["y7"], [W.attr_ints("strides", [2, 2])])]
+    path = _write(tmp_path, "m.onnx", nodes, inits, ["x", "x24", "xq", "x64", "xc", "xi", "xt"],
+                  ["y1", "y2", "y3", "y4", "y5", "y6", "y7"], {"w.bin": ext})
+    return path, dict(w1=w1, w2=w2, c2=c2, wq=wq, bq=bq, sc=sc, zp=zp, wc=wc, bc=bc, wi=wi, wt=wt)
 
 
 def test_reads_graph_initializers_and_external_data(tmp_path):
     path, ref = build_model(tmp_path)
     m = om.load_model(path)
-    assert [n.op_type for n in m.nodes] == ["MatMul", "Gemm", "MatMulInteger", "MatMulNBits", "Conv", "ConvInteger"]
+    assert [n.op_type for n in m.nodes] == ["MatMul", "Gemm", "MatMulInteger", "MatMulNBits", "Conv", "ConvInteger",
+                                            "ConvTranspose"]
     assert m.nodes[1].attrs["transB"] == 1 and abs(m.nodes[1].attrs["alpha"] - 0.5) < 1e-7
     assert m.nodes[3].domain == "com.microsoft" and m.nodes[3].attrs["block_size"] == 32
     assert m.nodes[4].attrs["pads"] == [1, 1, 1, 1] and m.nodes[5].attrs["strides"] == [2, 1]
@@ -71,8 +75,8 @@ def test_reads_graph_initializers_and_external_data(tmp_path):
         np.testing.assert_array_equal(m.initializers[k], v)
         assert m.initializers[k].dtype == v.dtype
     assert m.elem_types["wq"] == om.INT8 and m.elem_types["w2"] == om.FLOAT
-    assert m.inputs == ["x", "x24", "xq", "x64", "xc", "xi"]
-    assert m.outputs == ["y1", "y2", "y3", "y4", "y5", "y6"]
+    assert m.inputs == ["x", "x24", "xq", "x64", "xc", "xi", "xt"]
+    assert m.outputs == ["y1", "y2", "y3", "y4", "y5", "y6", "y7"]
 
 
 def test_tensor_decoding_rules():
@@ -127,7 +131,8 @@ def test_load_time_prepack_and_cache_match_first_use_packing(tmp_path):
              "xq": rng.integers(0, 256, (7, 16), dtype=np.uint8),
              "x64": rng.standard_normal((9, 64)).astype(np.float32),
              "xc": rng.standard_normal((2, 3, 9, 9)).astype(np.float32),
-             "xi": rng.integers(0, 256, (1, 2, 7, 7), dtype=np.uint8)}
+             "xi": rng.integers(0, 256, (1, 2, 7, 7), dtype=np.uint8),
+             "xt": rng.standard_normal((1, 3, 4, 5)).astype(np.float32)}
 
     def run(disp):
         out = []
@@ -139,11 +144,11 @@ def test_load_time_prepack_and_cache_match_first_use_packing(tmp_path):
 
     lazy = run(GpuDispatch(ctx, m.initializers, m.elem_types))
     eager, st0 = om.prepack_session(ctx, m)
-    assert st0["packed"] == 6
+    assert st0["packed"] == 7
     first = run(eager)
     cache = str(tmp_path / "cache")
     d1, st1 = om.prepack_session(ctx, m, cache_dir=cache)
-    assert st1["cache_misses"] == 6 and st1["cache_hits"] == 0
+    assert st1["cache_misses"] == 6 and st1["cache_hits"] == 0  # the ConvTranspose weight is uploaded, not cached
     d2, st2 = om.prepack_session(ctx, m, cache_dir=cache)
     assert st2["cache_hits"] == 6 and st2["cache_misses"] == 0
     for a, b_, c, d in zip(lazy, first, run(d1), run(d2)):
@@ -153,5 +158,6 @@ def test_load_time_prepack_and_cache_match_first_use_packing(tmp_path):
     import oracle
     np.testing.assert_array_equal(lazy[4], oracle.conv_f32(feeds["xc"], ref["wc"], ref["bc"], None, [1, 1, 1, 1]))
     np.testing.assert_array_equal(lazy[5].astype(np.int64), oracle.conv_integer(feeds["xi"], ref["wi"], strides=[2, 1]))
+    np.testing.assert_array_equal(lazy[6], oracle.conv_transpose_f32(feeds["xt"], ref["wt"], None, [2, 2]))
     np.testing.assert_array_equal(lazy[2].astype(np.int64),
                                   ops.as_reference_int64(ops.opMatMulInteger(feeds["xq"], ref["wq"], ctx=ctx)))
