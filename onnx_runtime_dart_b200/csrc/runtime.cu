@@ -535,9 +535,21 @@ void integer_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const 
 // MatMulNBits
 // ---------------------------------------------------------------------------
 
+// FAST route for m rows: the decode GEMV serves m <= 32, except that from 17
+// rows on (four m16 tiles per CTA) the tensor-core kernel is faster once the
+// GEMV grid (16 columns per CTA) passes 256 CTAs. Measured per op, K = 1024,
+// GEMV against tensor cores: N = 4096: m = 24 7.47 / 7.48 us, m = 32 8.16 /
+// 7.57 us; N = 6144: m = 24 11.06 / 8.37 us, m = 32 12.00 / 8.19 us; N = 1024
+// stays with the GEMV (3.54 / 6.79 us at m = 32). The comparison holds for
+// weights with the prefill scale records (tsq); others keep the GEMV.
+static bool nbits_use_smallm(const NbitsWeight &w, int64_t m, int64_t K, int64_t N) {
+  if (!nbits_smallm_supported(w, m)) return false;
+  return !(m > 16 && w.npad >= 4096 && w.tsq && nbits_tc_supported(w, m, K, N));
+}
+
 // Device scratch bytes nbits_run needs for an m-row call.
 size_t nbits_scratch_bytes(const b2m_weight *w, int64_t m, int32_t mode) {
-  if (mode != B2M_MODE_FAST || m == 0 || nbits_smallm_supported(w->nb, m)) return 0;
+  if (mode != B2M_MODE_FAST || m == 0 || nbits_use_smallm(w->nb, m, w->k, w->n)) return 0;
   if (!nbits_tc_supported(w->nb, m, w->k, w->n)) return 0;
   return (size_t)(m * nbits_tc_k8(w->k) * 2) + 256;
 }
@@ -558,7 +570,7 @@ void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_w
     p.K = K;
     p.N = N;
     p.dev_err = ctx->dev_err;
-    if (nbits_smallm_supported(w->nb, m)) {
+    if (nbits_use_smallm(w->nb, m, K, N)) {
       launch_nbits_smallm(p, ctx->stream, ctx->pdl);
     } else if (nbits_tc_supported(w->nb, m, K, N)) {
       __half *a16 = static_cast<__half *>(sc.take((size_t)(m * nbits_tc_k8(K) * 2)));

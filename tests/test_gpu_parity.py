@@ -415,11 +415,14 @@ def test_nbits_prefill_token_tiles(ctx, m, n):
 
 
 @pytest.mark.parametrize("m,k,n", [(64, 2048, 1024), (64, 3072, 1024), (64, 1024, 4096), (64, 1024, 6144),
-                                   (33, 1000, 1100), (100, 4096, 256), (40, 256, 640), (96, 512, 1030)])
+                                   (33, 1000, 1100), (100, 4096, 256), (40, 256, 640), (96, 512, 1030),
+                                   (17, 1024, 4096), (24, 1024, 6144), (32, 1024, 4100)])
 def test_nbits_prefill_small_grids(ctx, m, k, n):
     # Tensor-core shapes whose grids underfill the SMs: decoder projections at
     # 64 sequences (o / down / qkv / gate_up), a K tail with a partial column
-    # tile, long K on two column tiles; repeated calls are bitwise stable.
+    # tile, long K on two column tiles, and the 17-32 row calls on wide
+    # weights that leave the GEMV for the tensor cores; repeated calls are
+    # bitwise stable.
     rng = np.random.default_rng(9000 + m + k + n)
     a, bq, sc, z = nbits_case(rng, m, k, n, 32, "packed")
     bias = rng.standard_normal((n,)).astype(np.float32)
