@@ -74,6 +74,14 @@ typedef int32_t b2m_status;
 /* Arithmetic modes for the floating-point ops. */
 #define B2M_MODE_EXACT 0 /* bitwise identical to the reference Dart kernels */
 #define B2M_MODE_FAST 1  /* tensor cores; max|d|/max|ref| <= 1e-3, cosine >= 0.99999 */
+/* MatMulNBits only: tensor cores on weights dequantized exactly as the
+ * reference's weight() and split, with the activations, into two bf16 terms
+ * (three products, ~1e-5 relative per op), or the decode GEMV (exact integer
+ * weights, fp32 scales, f16 hi + lo activations) where it serves the row
+ * count. For chains of many layers whose end result must stay within the
+ * FAST tolerance of the reference: single-f16 weights and activations
+ * compound to several 1e-3 over 28 layers. */
+#define B2M_MODE_PRECISE 2
 
 #define B2M_MAX_RANK 8
 
@@ -117,6 +125,14 @@ B2M_API b2m_status b2m_synchronize(b2m_ctx *ctx);
  * <= 0 disables). */
 B2M_API b2m_status b2m_set_cancel_flag(b2m_ctx *ctx, const volatile int32_t *flag);
 B2M_API b2m_status b2m_set_byte_budget(b2m_ctx *ctx, int64_t bytes);
+
+/* Numerics of the attention entry points (b2m_gqa_dev, b2m_mha_dev) on this
+ * context. FAST (default): tcgen05 kernels with bf16-split products where the
+ * shape allows, and key splits for decode steps of few sequences. EXACT:
+ * fp32 CUDA-core kernels and no key splits, so a sequence's result does not
+ * depend on the other sequences of the batch — the property the reference's
+ * pool guarantees for its partitioned MatMuls (parallel_pool.dart:7-8). */
+B2M_API b2m_status b2m_set_attention_mode(b2m_ctx *ctx, int32_t mode);
 
 /* Device time of the last op, from CUDA events around its launches, when
  * timing is on (default off; enabling costs one event pair per op). Replaces

@@ -7,13 +7,13 @@ for the executor hook.
 """
 from ._native import (ArgumentError, B2mError, DeviceTimeoutError, NoDeviceError, OnnxCancelledException,
                       OnnxMemoryLimitException, UnsupportedError)
-from .ops import (MODE_EXACT, MODE_FAST, opDynamicQuantizeLinear, opGemm, opMatMul, opMatMulInteger, opMatMulNBits,
-                  opQLinearMatMul, prepack_nbits, validate_nbits)
+from .ops import (MODE_EXACT, MODE_FAST, MODE_PRECISE, opDynamicQuantizeLinear, opGemm, opMatMul, opMatMulInteger,
+                  opMatMulNBits, opQLinearMatMul, prepack_nbits, validate_nbits)
 from .runtime import Context, DeviceTensor, PackedWeight
 
 __all__ = [
     "ArgumentError", "B2mError", "DeviceTimeoutError", "NoDeviceError", "OnnxCancelledException",
-    "OnnxMemoryLimitException", "UnsupportedError", "MODE_EXACT", "MODE_FAST", "opDynamicQuantizeLinear", "opGemm",
-    "opMatMul", "opMatMulInteger", "opMatMulNBits", "opQLinearMatMul", "prepack_nbits", "validate_nbits", "Context",
-    "DeviceTensor", "PackedWeight",
+    "OnnxMemoryLimitException", "UnsupportedError", "MODE_EXACT", "MODE_FAST", "MODE_PRECISE",
+    "opDynamicQuantizeLinear", "opGemm", "opMatMul", "opMatMulInteger", "opMatMulNBits", "opQLinearMatMul",
+    "prepack_nbits", "validate_nbits", "Context", "DeviceTensor", "PackedWeight",
 ]

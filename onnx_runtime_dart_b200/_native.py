@@ -1,8 +1,7 @@
 """ctypes binding of libb200mm.so (include/b2m.h).
 
 This is the Python counterpart of the dart:ffi binding a Dart caller would
-use (INTEGRATION.md shows that binding): it opens the library, declares the
-entry points, and turns status codes into the exception classes the reference
+use: it opens the library, declares the entry points, and turns status codes into the exception classes the reference
 throws (ArgumentError, UnsupportedError, OnnxMemoryLimitException,
 OnnxCancelledException — lib/src/onnx_qlinear_ops.dart:127-165,
 lib/src/execution_control.dart). Library discovery follows the reference's
@@ -35,6 +34,7 @@ B2M_FLOAT16 = 10
 
 MODE_EXACT = 0
 MODE_FAST = 1
+MODE_PRECISE = 2  # MatMulNBits: bf16-split products on exactly dequantized weights
 
 MAX_RANK = 8
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -111,6 +111,7 @@ SIGNATURES = {
     "b2m_synchronize": (_i32, [_c_ctx]),
     "b2m_set_cancel_flag": (_i32, [_c_ctx, _i32p]),
     "b2m_set_byte_budget": (_i32, [_c_ctx, _i64]),
+    "b2m_set_attention_mode": (_i32, [_c_ctx, _i32]),
     "b2m_enable_timing": (_i32, [_c_ctx, _i32]),
     "b2m_last_kernel_ms": (_i32, [_c_ctx, ctypes.POINTER(_f32)]),
     "b2m_tensor_alloc": (_i32, [_c_ctx, _i32, _i64p, _i32, ctypes.POINTER(_c_tensor)]),

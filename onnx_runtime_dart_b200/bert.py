@@ -66,7 +66,8 @@ def _ptr(t) -> ctypes.c_void_p:
 class BertEncoder:
     """Random-weight encoder of shape `cfg` for batches of `batch` sequences of
     `seq` tokens. `mode` is the MatMul mode (N.MODE_FAST: bf16-split products on the tensor cores;
-    N.MODE_EXACT: the reference's fp32 operation order)."""
+    N.MODE_EXACT: the reference's fp32 operation order, with the attention on
+    the fp32 CUDA-core kernels)."""
 
     def __init__(self, ctx, cfg: BertConfig, batch: int, seq: int, seed: int = 0, mode: int = N.MODE_FAST,
                  keep_host: bool = False):
@@ -152,6 +153,14 @@ class BertEncoder:
                                       self.mode, ctypes.byref(yh)))
 
     def _forward(self):
+        # EXACT mode also runs the attention on the fp32 CUDA-core kernels.
+        self.ctx.set_attention_mode(N.MODE_EXACT if self.mode == N.MODE_EXACT else N.MODE_FAST)
+        try:
+            self._layers()
+        finally:
+            self.ctx.set_attention_mode(N.MODE_FAST)
+
+    def _layers(self):
         c, lib, h, chk = self.cfg, self.lib, self.ctx.handle, N.check
         T, H, I, D = self.T, c.hidden, c.inter, c.head_dim
         chk(lib.b2m_gather_rows_dev(h, _ptr(self.word), _ptr(self.ids), _ptr(self.o), T, c.vocab, H))

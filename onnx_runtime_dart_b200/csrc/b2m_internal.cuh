@@ -72,6 +72,9 @@ struct b2m_ctx {
   // Programmatic dependent launch for the decode kernels (env
   // B2M_DISABLE_PDL=1 turns it off, e.g. to compare timelines).
   bool pdl = true;
+  // Attention numerics (b2m_set_attention_mode): fp32 CUDA-core kernels and
+  // no key splits when set.
+  bool attn_exact = false;
   // Pinned staging for the host-buffer helpers.
   void *pinned = nullptr;
   size_t pinned_bytes = 0;
@@ -110,6 +113,10 @@ struct NbitsWeight {
   int64_t kp = 0;    // padded K (multiple of 64, >= nblocks*block)
   int64_t npad = 0;  // padded N (multiple of 128)
   float *wdeq = nullptr;  // exact-mode float32 W [N][K], made on first use
+  // PRECISE-mode operand of the FAST fp32 GEMM: the exactly dequantized W
+  // split into bf16 hi / lo planes [N][f32_tc_kp(K)] (K-major), made on first
+  // use.
+  uint16_t *px_hi = nullptr, *px_lo = nullptr;
   // All scales are 0 or normal f16 numbers and zero points are integers, so
   // the tensor-core dequant may scale in f16 (one rounding per weight).
   bool f16_scales = false;
@@ -209,6 +216,10 @@ int64_t f32_tc_kp(int64_t K);
 size_t f32_tc_scratch_bytes(int64_t M, int64_t K);
 bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w);
 void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cudaStream_t s);
+// The same with the B planes given directly ([b_rows][f32_tc_kp(K)] each).
+void launch_f32_tc_b(const F32GemmArgs &p, const void *b_hi, const void *b_lo, int64_t b_rows, void *a_split,
+                     cudaStream_t s);
+bool f32_tc_shape_ok(const F32GemmArgs &p);
 // The same GEMM on operands already split into bf16 planes: A planes (x0 then
 // x1, each [M][f32_tc_kp(K)]) and B planes [b_rows][f32_tc_kp(K)]; p.Y, p.ldy
 // and the Gemm epilogue fields as above. cm_P > 0 selects the channel-major
@@ -293,6 +304,10 @@ bool nbits_smallm_supported(const NbitsWeight &w, int64_t M);
 void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl);
 void launch_nbits_simt(const NbitsArgs &a, cudaStream_t s);
 void launch_nbits_dequant_f32(const NbitsWeight &w, int64_t K, int64_t N, float *out, cudaStream_t s);
+// W dequantized exactly (as nbits_dequant_f32) and split into bf16 hi / lo
+// planes [N][kp], zero for k >= K.
+void launch_nbits_split_planes(const NbitsWeight &w, int64_t K, int64_t N, int64_t kp, uint16_t *hi, uint16_t *lo,
+                               cudaStream_t s);
 // tcgen05 prefill GEMM; `a16` is scratch for A converted to f16, M x nbits_tc_k8(K).
 int64_t nbits_tc_k8(int64_t K);
 bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N);
@@ -323,10 +338,12 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP);
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, cudaStream_t s);
+                float *split_part, int nsplit, bool exact, cudaStream_t s);
+// `exact`: the fp32 CUDA-core attention kernels only (no bf16-split tensor-core
+// kernels); with nsplit = 1 every sequence's result is independent of the batch.
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
                 int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
-                int D, float scale, int causal, int32_t *err, cudaStream_t s);
+                int D, float scale, int causal, int32_t *err, bool exact, cudaStream_t s);
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s);
 void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,
                    const float *sin, int half, int max_pos, float *y, int64_t y_rs, int B, int S, int heads, int D,

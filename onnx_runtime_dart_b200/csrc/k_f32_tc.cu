@@ -395,11 +395,13 @@ int64_t f32_tc_kp(int64_t K) { return (K + FT_KPAD - 1) / FT_KPAD * FT_KPAD; }
 
 size_t f32_tc_scratch_bytes(int64_t M, int64_t K) { return (size_t)(2 * M * f32_tc_kp(K) * 2); }
 
-bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w) {
-  return w && w->bx_hi && p.batch == 1 && p.sa_k == 1 && p.sa_m == p.K && p.M >= 1 && p.N >= 1 &&
+bool f32_tc_shape_ok(const F32GemmArgs &p) {
+  return p.batch == 1 && p.sa_k == 1 && p.sa_m == p.K && p.M >= 1 && p.N >= 1 &&
          (p.M + FT_BM - 1) / FT_BM * ((p.N + 31) / 32) <= ((int64_t)1 << 31) - 1 && p.K <= ((int64_t)1 << 30) &&
          p.epi != EPI_NBITS && p.epi != EPI_NBITS_M1;
 }
+
+bool f32_tc_eligible(const F32GemmArgs &p, const b2m_weight *w) { return w && w->bx_hi && f32_tc_shape_ok(p); }
 
 namespace {
 
@@ -448,6 +450,11 @@ void launch_f32_tc_planes(const F32GemmArgs &p, const void *b_hi, const void *b_
 }
 
 void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cudaStream_t s) {
+  launch_f32_tc_b(p, w.bx_hi, w.bx_lo, w.n, a_split, s);
+}
+
+void launch_f32_tc_b(const F32GemmArgs &p, const void *b_hi, const void *b_lo, int64_t b_rows, void *a_split,
+                     cudaStream_t s) {
   const int64_t kp = f32_tc_kp(p.K);
   __nv_bfloat16 *a0 = static_cast<__nv_bfloat16 *>(a_split), *a1 = a0 + p.M * kp;
   {
@@ -464,8 +471,8 @@ void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cud
     B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_split_rows, p.A, p.sa_m, a0, a1, p.M, p.K, kp));
   }
   FtOperandB b;
-  b.hi = w.bx_hi;
-  b.lo = w.bx_lo;
-  b.rows = w.n;
+  b.hi = b_hi;
+  b.lo = b_lo;
+  b.rows = b_rows;
   launch_ft_any(p, b, a0, a1, kp, s);
 }

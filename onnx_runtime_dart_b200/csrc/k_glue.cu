@@ -1631,7 +1631,7 @@ static bool fa_tc_shape(const GqaArgs &a) {
          al(a.q) && al(a.kcache) && al(a.vcache) && al(a.out) && (a.rot == 0 || !a.cos || a.rot <= a.D);
 }
 
-static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaStream_t s) {
+static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool exact, cudaStream_t s) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
   if (decode_shape(a)) {
@@ -1650,7 +1650,7 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaS
     if (nsplit > 1) {
       gqa_decode_combine_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, 0, s>>>(pm, pl, po, a.out, a.H, D, nsplit);
     }
-  } else if (fa_tc_shape(a)) {
+  } else if (!exact && fa_tc_shape(a)) {
     if (D == 128) {
       b2m::set_smem_limit_once<fa_tc_kernel<128>>((int)FaLayout<128>::BYTES);
       fa_tc_kernel<128><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)a.H, (unsigned)a.B), 512,
@@ -1660,7 +1660,7 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, cudaS
       fa_tc_kernel<64><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)a.H, (unsigned)a.B), 512,
                          FaLayout<64>::BYTES, s>>>(a);
     }
-  } else if (mha_tc_shape(a)) {
+  } else if (!exact && mha_tc_shape(a)) {
     b2m::set_smem_limit_once<mha_tc_kernel>((int)MTC_BYTES);
     mha_tc_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 512, MTC_BYTES, s>>>(a);
   } else if (dok) {
@@ -1702,7 +1702,7 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP) {
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, cudaStream_t s) {
+                float *split_part, int nsplit, bool exact, cudaStream_t s) {
   GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
             B, S, H, KVH, D, CAP, scale, err};
   a.kc_rs = D;
@@ -1715,12 +1715,12 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
   const int64_t items = (int64_t)B * S * KVH;
   gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
   B2M_CUDA(cudaGetLastError());
-  launch_attend(a, split_part, nsplit, s);
+  launch_attend(a, split_part, nsplit, exact, s);
 }
 
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
                 int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
-                int D, float scale, int causal, int32_t *err, cudaStream_t s) {
+                int D, float scale, int causal, int32_t *err, bool exact, cudaStream_t s) {
   GqaArgs a{q, k, v, q_rs, kv_rs, const_cast<float *>(k), const_cast<float *>(v), nullptr, nullptr, nullptr, 0, 0,
             0, out, B, S, H, KVH, D, T, scale, err};
   a.kc_rs = kv_rs;
@@ -1732,7 +1732,7 @@ void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, in
   a.mask_bs = mask_bs;
   a.mask_hs = mask_hs;
   a.mask_qs = mask_qs;
-  launch_attend(a, nullptr, 1, s);
+  launch_attend(a, nullptr, 1, exact, s);
 }
 
 void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,

@@ -16,6 +16,7 @@
 //    the reference's weight() (:177-191) does, for the exact fp32 GEMM.
 #include "b2m_internal.cuh"
 #include "ptx.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
@@ -326,6 +327,42 @@ __global__ void nbits_dequant_kernel(const NbitsWeight w, int64_t K, int64_t N, 
   out[idx] = v;
 }
 
+// PRECISE-mode weight planes: the exact weight (as nbits_dequant_kernel makes
+// it) split into bf16 hi = rn(w), lo = rn(w - hi), K-major [N][kp], zero for
+// k >= K. Two consecutive k per thread.
+__global__ void nbits_split_planes_kernel(const NbitsWeight w, int64_t K, int64_t N, int64_t kp, uint32_t *hi,
+                                          uint32_t *lo) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // pair index
+  const int64_t half = kp >> 1;
+  if (idx >= N * half) return;
+  const int64_t n = idx / half, k0 = (idx - n * half) * 2;
+  float v[2];
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    const int64_t k = k0 + j;
+    v[j] = 0.f;
+    if (k < K) {
+      const int64_t blk = k / w.block;
+      const int q = nib_at(w.bq, w.kp, n, k);
+      const float sc = w.scales[n * w.nblocks + blk];
+      if (w.zp_kind == 2) {
+        v[j] = __double2float_rn(__dmul_rn(__dsub_rn((double)q, (double)w.zp_f32[n * w.nblocks + blk]), (double)sc));
+      } else {
+        int zp = 8;
+        if (w.zp_kind == 1) {
+          const uint8_t z = w.zp_u8[n * w.zstride + (blk >> 1)];
+          zp = (blk & 1) ? (z >> 4) : (z & 15);
+        }
+        v[j] = __fmul_rn((float)(q - zp), sc);
+      }
+    }
+  }
+  uint32_t h, l;
+  split_bf16x2(v[0], v[1], h, l);
+  hi[idx] = h;
+  lo[idx] = l;
+}
+
 template <int MT, int ZPK, bool BS16, int CPW>
 void launch_decode_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   auto kern = nbits_decode_kernel<MT, ZPK, BS16, CPW, DEC_WARPS, DEC_LO>;
@@ -393,6 +430,14 @@ void launch_nbits_simt(const NbitsArgs &a, cudaStream_t s) {
   dim3 grid((unsigned)((a.N + 63) / 64), (unsigned)((a.M + 63) / 64));
   B2M_REQUIRE(grid.y <= 65535, B2M_ERR_UNSUPPORTED, "MatMulNBits: too many rows");
   nbits_simt_kernel<<<grid, 256, 0, s>>>(a, *a.w);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_nbits_split_planes(const NbitsWeight &w, int64_t K, int64_t N, int64_t kp, uint16_t *hi, uint16_t *lo,
+                               cudaStream_t s) {
+  const int64_t pairs = N * (kp / 2);
+  nbits_split_planes_kernel<<<(unsigned)((pairs + 255) / 256), 256, 0, s>>>(
+      w, K, N, kp, reinterpret_cast<uint32_t *>(hi), reinterpret_cast<uint32_t *>(lo));
   B2M_CUDA(cudaGetLastError());
 }
 

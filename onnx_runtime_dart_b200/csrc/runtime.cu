@@ -547,9 +547,38 @@ static bool nbits_use_smallm(const NbitsWeight &w, int64_t m, int64_t K, int64_t
   return !(m > 16 && w.npad >= 4096 && w.tsq && nbits_tc_supported(w, m, K, N));
 }
 
+// PRECISE mode: the decode GEMV wherever it serves the row count (exact
+// integer weights, fp32 scales, f16 hi + lo activations), otherwise the FAST
+// fp32 GEMM (three bf16 products) over the exactly dequantized weight split
+// into bf16 planes.
+static bool nbits_precise_gemv(const NbitsWeight &w, int64_t m) { return nbits_smallm_supported(w, m); }
+
+static F32GemmArgs nbits_precise_args(const float *A, int64_t m, int64_t K, int64_t N, const float *bias, float *Y) {
+  F32GemmArgs p;
+  p.A = A;
+  p.Y = Y;
+  p.M = m;
+  p.N = N;
+  p.K = K;
+  p.sa_m = K;
+  p.sa_k = 1;
+  p.ldy = N;
+  p.batch = 1;
+  p.epi = EPI_GEMM;  // y = acc + bias[col]
+  p.C = bias;
+  p.c_rs = 0;
+  p.c_cs = 1;
+  return p;
+}
+
 // Device scratch bytes nbits_run needs for an m-row call.
 size_t nbits_scratch_bytes(const b2m_weight *w, int64_t m, int32_t mode) {
-  if (mode != B2M_MODE_FAST || m == 0 || nbits_use_smallm(w->nb, m, w->k, w->n)) return 0;
+  if (m == 0) return 0;
+  if (mode == B2M_MODE_PRECISE) {
+    if (nbits_precise_gemv(w->nb, m)) return 0;
+    return f32_tc_scratch_bytes(m, w->k) + 256;
+  }
+  if (mode != B2M_MODE_FAST || nbits_use_smallm(w->nb, m, w->k, w->n)) return 0;
   if (!nbits_tc_supported(w->nb, m, w->k, w->n)) return 0;
   return (size_t)(m * nbits_tc_k8(w->k) * 2) + 256;
 }
@@ -557,9 +586,45 @@ size_t nbits_scratch_bytes(const b2m_weight *w, int64_t m, int32_t mode) {
 void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_weight *w, const float *bias,
                int32_t mode, float *Y) {
   B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
-  B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad mode");
+  B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST || mode == B2M_MODE_PRECISE,
+              B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad mode");
   if (m == 0) return;
   const int64_t K = w->k, N = w->n;
+  if (mode == B2M_MODE_PRECISE) {
+    if (nbits_precise_gemv(w->nb, m)) {
+      NbitsArgs p;
+      p.A = A;
+      p.w = &w->nb;
+      p.bias = bias;
+      p.Y = Y;
+      p.M = m;
+      p.K = K;
+      p.N = N;
+      p.dev_err = ctx->dev_err;
+      launch_nbits_smallm(p, ctx->stream, ctx->pdl);
+      return;
+    }
+    F32GemmArgs p = nbits_precise_args(A, m, K, N, bias, Y);
+    p.dev_err = ctx->dev_err;
+    B2M_REQUIRE(f32_tc_shape_ok(p), B2M_ERR_UNSUPPORTED, "MatMulNBits: shape not supported in PRECISE mode");
+    NbitsWeight &nb = const_cast<b2m_weight *>(w)->nb;
+    if (!nb.px_hi) {
+      const int64_t kp = f32_tc_kp(K);
+      const size_t bytes = (size_t)(N * kp * 2);
+      uint16_t *hi = nullptr, *lo = nullptr;
+      B2M_CUDA(cudaMalloc(&hi, bytes));
+      const cudaError_t e = cudaMalloc(&lo, bytes);
+      if (e != cudaSuccess) {
+        cudaFree(hi);
+        B2M_CUDA(e);
+      }
+      launch_nbits_split_planes(nb, K, N, kp, hi, lo, ctx->stream);
+      nb.px_hi = hi;
+      nb.px_lo = lo;
+    }
+    launch_f32_tc_b(p, nb.px_hi, nb.px_lo, N, sc.take(f32_tc_scratch_bytes(m, K)), ctx->stream);
+    return;
+  }
   if (mode == B2M_MODE_FAST) {
     NbitsArgs p;
     p.A = A;
@@ -703,6 +768,15 @@ B2M_API b2m_status b2m_set_stream(b2m_ctx *ctx, void *stream) {
   return guarded([&] {
     check_ctx(ctx);
     ctx->stream = stream ? static_cast<cudaStream_t>(stream) : ctx->own_stream;
+  });
+}
+
+B2M_API b2m_status b2m_set_attention_mode(b2m_ctx *ctx, int32_t mode) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST, B2M_ERR_INVALID_ARGUMENT,
+                "attention mode must be EXACT or FAST");
+    ctx->attn_exact = mode == B2M_MODE_EXACT;
   });
 }
 
@@ -1153,6 +1227,8 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     cudaFree(w->nb.zp_u8);
     cudaFree(w->nb.zp_f32);
     cudaFree(w->nb.wdeq);
+    cudaFree(w->nb.px_hi);
+    cudaFree(w->nb.px_lo);
     cudaFree(w->nb.srec);
     cudaFree(w->nb.tsq);
     cudaFree(w->nb.tss);
@@ -1538,12 +1614,13 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
     DeviceGuard dg(ctx->device);
     if ((int64_t)b * s == 0) return;
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
-    const int nsplit = gqa_decode_splits(b, s, h, kvh, head_dim, cap);
+    const int nsplit = ctx->attn_exact ? 1 : gqa_decode_splits(b, s, h, kvh, head_dim, cap);
     float *part = nullptr;
     Scratch scr(ctx, nsplit > 1 ? (size_t)b * h * nsplit * (2 + head_dim) * 4 + 256 : 0);
     if (nsplit > 1) part = static_cast<float *>(scr.take((size_t)b * h * nsplit * (2 + head_dim) * 4));
     launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
-               interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit, ctx->stream);
+               interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit,
+               ctx->attn_exact, ctx->stream);
   });
 }
 
@@ -1566,7 +1643,7 @@ B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, con
     if ((int64_t)b * s == 0) return;
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
     launch_mha(q, k, v, q_rs, kv_rs, mask, mask_bs, mask_hs, mask_qs, out, b, s, t, h, kvh, head_dim, sc,
-               causal ? 1 : 0, ctx->dev_err, ctx->stream);
+               causal ? 1 : 0, ctx->dev_err, ctx->attn_exact, ctx->stream);
   });
 }
 

@@ -81,9 +81,15 @@ class Int4Decoder:
     cache of `cap` positions; prompts up to `max_prefill` tokens."""
 
     def __init__(self, ctx, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int, seed: int = 0,
-                 keep_host: bool = False):
+                 keep_host: bool = False, mode: int = N.MODE_FAST):
         import torch
 
+        if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
+            raise N.ArgumentError("decoder: mode must be FAST, PRECISE or EXACT")
+        # MatMulNBits numerics of every projection; the lm_head MatMul runs
+        # EXACT in EXACT mode and FAST (bf16-split products) otherwise, and the
+        # attention runs the fp32 CUDA-core kernels in EXACT mode.
+        self.mode = mode
         self.torch = torch
         self.ctx, self.cfg, self.B, self.cap = ctx, cfg, batch, cap
         self.lib = ctx.lib
@@ -157,8 +163,14 @@ class Int4Decoder:
         sequence's last token in self.logits and its argmax in self.next_ids,
         and advances past by seq. Everything is enqueued on the context's
         stream."""
+        self.ctx.set_attention_mode(N.MODE_EXACT if self.mode == N.MODE_EXACT else N.MODE_FAST)
+        try:
+            self._layers(seq, self.B * seq)
+        finally:
+            self.ctx.set_attention_mode(N.MODE_FAST)
+
+    def _layers(self, seq: int, T: int):
         c, lib, h = self.cfg, self.lib, self.ctx.handle
-        T = self.B * seq
         H, D = c.hidden, c.head_dim
         chk = N.check
         chk(lib.b2m_gather_rows_dev(h, _ptr(self.emb), _ptr(self.ids), _ptr(self.res), T, c.vocab, H))
@@ -171,7 +183,7 @@ class Int4Decoder:
             else:  # residual of the previous layer's MLP, then the attention norm
                 chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(lw["attn_norm"]), _ptr(self.h),
                                         _ptr(self.res), T, H, c.eps))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["qkv"].handle, None, N.MODE_FAST, _ptr(self.qkv)))
+            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["qkv"].handle, None, self.mode, _ptr(self.qkv)))
             chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qkv + q_off), _ptr(lw["q_norm"]),
                                           ctypes.c_void_p(qkv + q_off), T, c.heads, D, c.qkv_n, c.eps))
             chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qkv + k_off), _ptr(lw["k_norm"]),
@@ -180,15 +192,15 @@ class Int4Decoder:
                                 ctypes.c_void_p(qkv + v_off), c.qkv_n, c.qkv_n, _ptr(self.kcache[li]),
                                 _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D, 0,
                                 _ptr(self.attn), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, N.MODE_FAST, _ptr(self.o)))
+            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, self.mode, _ptr(self.o)))
             chk(lib.b2m_rmsnorm_dev(h, _ptr(self.o), _ptr(self.res), _ptr(lw["mlp_norm"]), _ptr(self.h),
                                     _ptr(self.res), T, H, c.eps))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["gate_up"].handle, None, N.MODE_FAST,
+            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["gate_up"].handle, None, self.mode,
                                          _ptr(self.gu)))
             gu = self.gu.data_ptr()
             chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gu), ctypes.c_void_p(gu + c.inter * 4), 2 * c.inter,
                                      2 * c.inter, _ptr(self.act), T, c.inter))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, N.MODE_FAST,
+            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
                                          _ptr(self.down)))
         chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(self.final_norm), _ptr(self.h),
                                 _ptr(self.res), T, H, c.eps))
@@ -198,7 +210,8 @@ class Int4Decoder:
             self.last_idx[seq] = idx
         chk(lib.b2m_gather_rows_dev(h, _ptr(self.h), _ptr(idx), _ptr(self.last), self.B, T, H))
         y = ctypes.c_void_p(self.t_logits.handle.value)
-        chk(lib.b2m_matmul_f32(h, self.t_last.handle, None, self.lm_head.handle, N.MODE_FAST, ctypes.byref(y)))
+        lm_mode = N.MODE_EXACT if self.mode == N.MODE_EXACT else N.MODE_FAST
+        chk(lib.b2m_matmul_f32(h, self.t_last.handle, None, self.lm_head.handle, lm_mode, ctypes.byref(y)))
         chk(lib.b2m_argmax_dev(h, _ptr(self.logits), _ptr(self.next_ids), self.B, c.vocab))
         chk(lib.b2m_advance_positions_dev(h, _ptr(self.past), self.B, seq))
 

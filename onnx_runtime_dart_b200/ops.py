@@ -32,6 +32,7 @@ from .runtime import Context, DeviceTensor, PackedWeight
 
 MODE_EXACT = N.MODE_EXACT
 MODE_FAST = N.MODE_FAST
+MODE_PRECISE = N.MODE_PRECISE
 
 _default = {}
 _lock = threading.Lock()
@@ -249,8 +250,10 @@ def opMatMulNBits(a, bQ, scales=None, zeroPoints=None, *, k: int, n: int, bits: 
 
     `bQ` is the packed uint8 [N, ceil(K/block), block/2] initializer (with
     `scales` and optional `zeroPoints`), or a PackedWeight from
-    `prepack_nbits`. mode FAST (default) runs the tensor-core kernels; mode
-    EXACT reproduces the reference bit for bit."""
+    `prepack_nbits`. mode FAST (default) runs the tensor-core kernels on f16
+    weights and activations; mode PRECISE splits both into two bf16 terms
+    (three tensor-core products, ~1e-5 relative) for long chains; mode EXACT
+    reproduces the reference bit for bit."""
     ctx = _ctx(ctx)
     a_shape = _shape(a)
     a_dtype = a.dtype

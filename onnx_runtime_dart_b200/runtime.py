@@ -83,6 +83,12 @@ class Context:
     def set_byte_budget(self, nbytes: int):
         N.check(self.lib.b2m_set_byte_budget(self.handle, int(nbytes)))
 
+    def set_attention_mode(self, mode: int):
+        """N.MODE_EXACT: fp32 CUDA-core attention with no key splits (each
+        sequence's result independent of the batch); N.MODE_FAST (default):
+        the tensor-core kernels."""
+        N.check(self.lib.b2m_set_attention_mode(self.handle, int(mode)))
+
     def enable_timing(self, on: bool = True):
         N.check(self.lib.b2m_enable_timing(self.handle, 1 if on else 0))
 

@@ -119,14 +119,14 @@ def gqa(q, k, v, num_heads, kv_heads, past_k=None, past_v=None, cos=None, sin=No
     out = np.zeros((b, num_heads, s, d), np.float32)
     for hh in range(num_heads):
         kv = hh // group
-        scores = np.einsum("bsd,btd->bst", qh[:, hh].astype(np.float64), pk[:, kv].astype(np.float64))
+        scores = np.matmul(qh[:, hh].astype(np.float64), pk[:, kv].astype(np.float64).transpose(0, 2, 1))
         scores = (scores.astype(np.float32).astype(np.float64) * sc)
         mask = np.arange(total)[None, :] > (p + np.arange(s))[:, None]
         scores = np.where(mask[None], -np.inf, scores)
         mx = scores.max(-1, keepdims=True)
         e = np.exp(scores - mx)
         probs = (e / e.sum(-1, keepdims=True)).astype(np.float32)
-        out[:, hh] = np.einsum("bst,btd->bsd", probs.astype(np.float64), pv[:, kv].astype(np.float64))
+        out[:, hh] = np.matmul(probs.astype(np.float64), pv[:, kv].astype(np.float64))
     return out.transpose(0, 2, 1, 3).reshape(b, s, hid), pk, pv
 
 
@@ -154,7 +154,7 @@ def mha(q, k, v, num_heads, kv_heads=None, mask=None, scale=None, causal=False, 
     out = np.zeros((b, num_heads, s, d), np.float32)
     for hh in range(num_heads):
         kv = hh // group
-        scores = np.einsum("bsd,btd->bst", qh[:, hh].astype(np.float64), kh[:, kv].astype(np.float64))
+        scores = np.matmul(qh[:, hh].astype(np.float64), kh[:, kv].astype(np.float64).transpose(0, 2, 1))
         val = scores.astype(np.float32).astype(np.float64) * sc
         if mask is not None:
             val = val + np.asarray(mask, np.float32).astype(np.float64).reshape(b, 1, t)
@@ -166,5 +166,5 @@ def mha(q, k, v, num_heads, kv_heads=None, mask=None, scale=None, causal=False, 
             val = np.where(np.arange(t)[None, None, :] > np.arange(s)[None, :, None], -np.inf, val)
         e = np.exp(val - val.max(-1, keepdims=True))
         probs = (e / e.sum(-1, keepdims=True)).astype(np.float32)
-        out[:, hh] = np.einsum("bst,btd->bsd", probs.astype(np.float64), vh[:, kv].astype(np.float64))
+        out[:, hh] = np.matmul(probs.astype(np.float64), vh[:, kv].astype(np.float64))
     return out.transpose(0, 2, 1, 3).reshape(b, s, hid)
