@@ -156,6 +156,14 @@ class Int4Decoder:
         self.graph = None
         self.stream = torch.cuda.Stream(device=dev)
 
+    def set_mode(self, mode: int) -> None:
+        """Switches the numerics mode (FAST, PRECISE or EXACT) of later calls;
+        the captured decode graph is dropped and captured again on next use."""
+        if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
+            raise N.ArgumentError("decoder: mode must be FAST, PRECISE or EXACT")
+        self.mode = mode
+        self.graph = None
+
     # -- one pass over the layers for `seq` new tokens per sequence -----------
     def _forward(self, seq: int):
         """Runs the chain for the B*seq token ids in self.ids (sequence-major)
