@@ -139,6 +139,127 @@ def cpu_decode_gbs(steps, warmup, layers_per_step, threads, seed=0):
     return steps * layers_per_step * launch_bytes(1) / dt / 1e9, dt
 
 
+def _best_time(fn, reps):
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        best = min(best, time.perf_counter() - t0)
+    return best
+
+
+def cpu_baselines(threads, seed=0):
+    """The oracle port (C restatement of the reference Dart kernels, compiled
+    -O2 -ffp-contract=off; not the Dart VM, which is not installed) timed per
+    BASELINE config on the host cores: 1 thread, and `threads` threads
+    column-splitting each MatMul the way the reference's GemmPool splits
+    float-initializer MatMuls (lib/src/parallel_pool.dart:236-260; the
+    reference itself pools only those, not MatMulInteger / MatMulNBits,
+    lib/src/onnx_graph.dart:856-872). Best of a few runs after a warm-up run.
+    Chains are truncated as stated in each entry."""
+    import platform
+
+    import oracle
+    from oracle import chains
+    from onnx_runtime_dart_b200.bert import BertConfig
+    from onnx_runtime_dart_b200.decoder import DecoderConfig
+
+    rng = np.random.default_rng(seed)
+    out = {"what": "oracle port of the reference Dart kernels (C, -O2 -ffp-contract=off), not the Dart VM",
+           "threads": threads, "cpu": platform.processor() or platform.machine()}
+    try:
+        with open("/proc/cpuinfo") as f:
+            names = [ln.split(":", 1)[1].strip() for ln in f if ln.startswith("model name")]
+        if names:
+            out["cpu"] = names[0]
+    except OSError:
+        pass
+
+    def both(fn, reps=3):
+        fn(1)
+        return _best_time(lambda: fn(1), reps), _best_time(lambda: fn(threads), reps)
+
+    a = rng.standard_normal((128, 384)).astype(np.float32)
+    b = (rng.standard_normal((384, 1536)) / np.sqrt(384)).astype(np.float32)
+    t1, tn = both(lambda th: oracle.matmul(a, b, nthreads=th), 5)
+    fl = 2 * 128 * 384 * 1536
+    out["config1_matmul_f32_gflops"] = {"1_thread": round(fl / t1 / 1e9, 3), f"{threads}_threads": round(fl / tn / 1e9, 3)}
+    bi = rng.integers(-127, 128, (1024, 3072)).astype(np.int8)
+    bz = rng.integers(-4, 5, 3072).astype(np.int8)
+    az = np.array(128, np.uint8)
+    c2 = {}
+    for m in (1, 64, 512):
+        ai = rng.integers(0, 256, (m, 1024)).astype(np.uint8)
+        t1, tn = both(lambda th: oracle.matmul_integer(ai, bi, az, bz, nthreads=th), 3 if m < 512 else 2)
+        ops = 2 * m * 1024 * 3072
+        c2[f"m{m}"] = {"1_thread_gops": round(ops / t1 / 1e9, 3), f"{threads}_threads_gops": round(ops / tn / 1e9, 3),
+                       "1_thread_ms": round(t1 * 1e3, 3)}
+    out["config2_matmulinteger"] = c2
+    bq = rng.integers(0, 256, (N_DIM, NB, BLOCK // 2), dtype=np.uint8)
+    sc = (np.abs(rng.normal(0, 0.02, (N_DIM, NB))) + 1e-3).astype(np.float32)
+    zp = rng.integers(0, 256, (N_DIM, (NB + 1) // 2), dtype=np.uint8)
+    c3 = {}
+    for m in (1, 8, 512):
+        x = rng.standard_normal((m, K_DIM)).astype(np.float32)
+        t1, tn = both(lambda th: oracle.matmul_nbits(x, bq, sc, zp, K_DIM, N_DIM, BLOCK, nthreads=th), 3 if m < 512 else 2)
+        e = {"1_thread_ms": round(t1 * 1e3, 3), f"{threads}_threads_ms": round(tn * 1e3, 3)}
+        if m < 512:
+            e["1_thread_gbs"] = round(launch_bytes(m) / t1 / 1e9, 3)
+            e[f"{threads}_threads_gbs"] = round(launch_bytes(m) / tn / 1e9, 3)
+        else:
+            fl = 2 * m * K_DIM * N_DIM
+            e["1_thread_gflops"] = round(fl / t1 / 1e9, 3)
+            e[f"{threads}_threads_gflops"] = round(fl / tn / 1e9, 3)
+        c3[f"m{m}"] = e
+    out["config3_matmulnbits"] = c3
+
+    # config 4: one sequence of 128 tokens (of the 32 x 128 batch); all 12
+    # layers on `threads` threads, the first 2 layers on 1 thread.
+    bc = BertConfig.base()
+    bh = chains.bert_host(bc, seed)
+    ids = rng.integers(0, bc.vocab, (1, 128)).astype(np.int64)
+    mask = np.ones((1, 128), np.int64)
+    tn = _best_time(lambda: chains.bert_forward(bc, bh, ids, mask, nthreads=threads), 1)
+    bc2 = BertConfig.base()
+    bc2.layers = 1
+    t1 = _best_time(lambda: chains.bert_forward(bc2, bh, ids, mask, nthreads=1), 1)
+    out["config4_bert"] = {"sample": "1 sequence x 128 tokens; 12 layers on all threads, 1 layer on 1 thread",
+                           f"{threads}_threads_tokens_per_s": round(128 / tn, 2),
+                           "1_thread_ms_per_layer": round(t1 * 1e3, 2),
+                           "1_thread_tokens_per_s_12_layers_derived": round(128 / (t1 * 12), 2)}
+    del bh
+
+    # config 5: one sequence, 32-token prefill then 2 greedy decode steps;
+    # all 28 layers on `threads` threads, 2 layers on 1 thread (the lm_head
+    # included in both).
+    dc = DecoderConfig.qwen3_0_6b()
+    dh = chains.decoder_host(dc, seed)
+    prompt = rng.integers(0, dc.vocab, (1, 32)).astype(np.int64)
+
+    def run_dec(cfg, th):
+        t0 = time.perf_counter()
+        lg, past = chains.decoder_forward(cfg, dh, 40, prompt, None, strict=True, nthreads=th)
+        t1_ = time.perf_counter()
+        tok = np.argmax(lg, axis=-1).reshape(1, 1)
+        for _ in range(2):
+            lg, past = chains.decoder_forward(cfg, dh, 40, tok, past, strict=True, nthreads=th)
+            tok = np.argmax(lg, axis=-1).reshape(1, 1)
+        return t1_ - t0, time.perf_counter() - t1_
+
+    pn, dn = run_dec(dc, threads)
+    dc2 = DecoderConfig.qwen3_0_6b()
+    dc2.layers = 2
+    p1, d1 = run_dec(dc2, 1)
+    out["config5_decoder"] = {"sample": "1 sequence, 32-token prefill + 2 greedy decode steps; 28 layers on all "
+                                        "threads, 2 layers on 1 thread (lm_head included in both)",
+                              f"{threads}_threads_prefill_tokens_per_s": round(32 / pn, 2),
+                              f"{threads}_threads_decode_tokens_per_s": round(2 / dn, 3),
+                              "1_thread_2_layers_prefill_ms": round(p1 * 1e3, 1),
+                              "1_thread_2_layers_decode_ms_per_step": round(d1 * 1e3 / 2, 1)}
+    del dh
+    return out
+
+
 def run_reference(args, rank):
     if rank != 0:
         return
@@ -426,7 +547,7 @@ def main():
                     help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--case", default="all",
-                    choices=["all", "decode1", "decode8", "prefill", "ops", "decoder", "bert", "conv"],
+                    choices=["all", "decode1", "decode8", "prefill", "ops", "decoder", "bert", "conv", "cpu"],
                     help="run one phase only (for profiler captures); prints its device time. "
                          "`ops` times BASELINE configs 1 and 2 (fp32 MatMul, MatMulInteger); `conv` the "
                          "convolutions through the GEMM cores")
@@ -444,6 +565,11 @@ def main():
 
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+
+    if args.case == "cpu":
+        if rank == 0:
+            print(json.dumps({"case": "cpu", **cpu_baselines(os.cpu_count() or 1)}), flush=True)
         return
 
     import torch
@@ -655,6 +781,10 @@ def main():
                "sample": f"oracle restatement of opMatMulNBits m==1 (double accumulation), {layers} config-3 "
                          f"layers ({dt_c:.1f} s), column split over {threads} threads"}
 
+    cpu_all = None
+    if rank == 0 and not args.no_cpu_baseline:
+        cpu_all = cpu_baselines(os.cpu_count() or 1)
+
     traffic = committed_traffic("nbits_decode_m1_k1024_n3072.md")
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -690,6 +820,8 @@ def main():
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if cpu_all is not None:
+        line["secondary"]["cpu_baselines_per_config"] = cpu_all
     if rank == 0:
         print(json.dumps(line), flush=True)
     for w in packed:

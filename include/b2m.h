@@ -260,7 +260,11 @@ B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m,
  * on a device and keeps the last call's contents, so calls that overlap on
  * the GPU race; serialise them (one stream, or host-side ordering). The first
  * call on a device resolves the array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream capture. */
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * That address is kept for the life of the process: a cudaDeviceReset after
+ * the first call is not supported. Every call copies the kernels' error word
+ * back and synchronises `stream`, so it blocks the host until the stream has
+ * drained (two calls cannot be queued back to back). */
 #define B2M_NOALLOC_SCRATCH_BYTES (8u << 20)
 B2M_API b2m_status b2m_matmul_nbits_noalloc(const b2m_weight *w, const float *a, int64_t m, const float *bias,
                                             float *y, void *stream);

@@ -46,6 +46,7 @@ def _check(have, want, what, max_rel, min_cos):
     rel, cos = rel_cos(have, want)
     assert np.all(np.isfinite(have)), f"{what}: non-finite output"
     assert rel <= max_rel and cos >= min_cos, f"{what}: max rel {rel:.3e} (bound {max_rel}), cos {cos:.9f}"
+    print(f"{what}: max rel {rel:.3e}, cos {cos:.10f}")
     return rel, cos
 
 
