@@ -384,7 +384,8 @@ def other_configs(ctx, lib, N, stream, dev, steps, warmup):
     return out
 
 
-def run_decoder(ctx, torch, stream, global_batch, prefill_len=512, steps=128, layers=None, seed=0, world=1, rank=0):
+def run_decoder(ctx, torch, stream, global_batch, prefill_len=512, steps=128, layers=None, seed=0, world=1, rank=0,
+                fused=True, mode=None):
     """Qwen3-0.6B-shaped int4 decoder (random weights,
     replicated on every rank). This rank runs its slice of the
     `global_batch` sequences (a seeded global prompt of `prefill_len` tokens
@@ -400,7 +401,10 @@ def run_decoder(ctx, torch, stream, global_batch, prefill_len=512, steps=128, la
     prompt_all = rng.integers(0, cfg.vocab, (global_batch, prefill_len)).astype(np.int64)
     prompt = sharding.local_slice(prompt_all, world, rank)
     batch = len(prompt)
-    dec = Int4Decoder(ctx, cfg, batch=batch, cap=prefill_len + steps + 8, max_prefill=prefill_len, seed=seed)
+    from onnx_runtime_dart_b200 import _native as N
+
+    dec = Int4Decoder(ctx, cfg, batch=batch, cap=prefill_len + steps + 8, max_prefill=prefill_len, seed=seed,
+                      fused=fused, mode=N.MODE_FAST if mode is None else mode)
     with torch.cuda.stream(stream):
         dec.prefill(prompt)  # warm-up (kernel attributes, scratch growth)
         dec.decode(2)        # captures the decode graph
@@ -415,6 +419,7 @@ def run_decoder(ctx, torch, stream, global_batch, prefill_len=512, steps=128, la
     ms_p, ms_d = e0.elapsed_time(e1), e1.elapsed_time(e2)
     ok = bool(((gen >= 0) & (gen < cfg.vocab)).all().item())
     out = {"batch_per_gpu": batch, "prefill_len": prefill_len, "decode_steps": steps, "layers": cfg.layers,
+           "projections": "fused q/k/v and gate/up" if fused else "separate (the exported graph's seven per layer)",
            "prefill_ms": round(ms_p, 3), "decode_ms": round(ms_d, 3),
            "prefill_tokens_per_s": round(batch * prefill_len / (ms_p / 1e3), 1),
            "decode_tokens_per_s": round(batch * steps / (ms_d / 1e3), 1),
@@ -553,6 +558,10 @@ def main():
                          "convolutions through the GEMM cores")
     ap.add_argument("--dec-layers", type=int, default=None, help="decoder case: layers (default 28)")
     ap.add_argument("--dec-steps", type=int, default=128, help="decoder case: greedy decode steps")
+    ap.add_argument("--dec-unfused", action="store_true",
+                    help="decoder case: separate q/k/v and gate/up MatMulNBits (the exported graph's projections)")
+    ap.add_argument("--dec-mode", default="fast", choices=["fast", "precise", "exact"],
+                    help="decoder case: MatMulNBits numerics mode")
     ap.add_argument("--dec-batch", type=int, default=None,
                     help="decoder case: sequences of the whole job, split over the ranks (default 64)")
     ap.add_argument("--bert-layers", type=int, default=None, help="bert case: layers (default 12)")
@@ -614,7 +623,8 @@ def main():
 
     if args.case == "decoder":
         r = run_decoder(ctx, torch, stream, args.dec_batch or 64, steps=args.dec_steps, world=world, rank=rank,
-                        layers=args.dec_layers)
+                        layers=args.dec_layers, fused=not args.dec_unfused,
+                        mode={"fast": N.MODE_FAST, "precise": N.MODE_PRECISE, "exact": N.MODE_EXACT}[args.dec_mode])
         t_p = max_over_ranks(r["prefill_ms"])
         t_d = max_over_ranks(r["decode_ms"])
         if rank == 0:
@@ -733,7 +743,15 @@ def main():
                 "decode_tokens_per_s": round(64 * dec["decode_steps"] / (dec_td / 1e3), 1),
                 "sequences": 64, "prefill_len": dec["prefill_len"],
                 "decode_steps": dec["decode_steps"], "decode_ms_per_step": dec["decode_ms_per_step"],
-                "tokens_valid": dec["tokens_valid"]}
+                "mode": "FAST", "projections": dec["projections"], "tokens_valid": dec["tokens_valid"]}
+    # The same decoder with the exported graph's separate projections, and in
+    # PRECISE mode (the chain-parity mode), fused.
+    for tag, kw in (("unfused_fast", dict(fused=False)), ("precise", dict(mode=N.MODE_PRECISE))):
+        d2 = run_decoder(ctx, torch, stream, 64, world=world, rank=rank, **kw)
+        tp2, td2 = max_over_ranks(d2["prefill_ms"]), max_over_ranks(d2["decode_ms"])
+        dec_line[tag] = {"prefill_tokens_per_s": round(64 * d2["prefill_len"] / (tp2 / 1e3), 1),
+                         "decode_tokens_per_s": round(64 * d2["decode_steps"] / (td2 / 1e3), 1),
+                         "decode_ms_per_step": d2["decode_ms_per_step"], "projections": d2["projections"]}
 
     # the BERT-base fp32 chain, sequences sharded over ranks.
     bert = run_bert(ctx, torch, stream, 32, steps=5, warmup=3, world=world, rank=rank)

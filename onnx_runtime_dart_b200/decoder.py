@@ -81,7 +81,7 @@ class Int4Decoder:
     cache of `cap` positions; prompts up to `max_prefill` tokens."""
 
     def __init__(self, ctx, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int, seed: int = 0,
-                 keep_host: bool = False, mode: int = N.MODE_FAST):
+                 keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True):
         import torch
 
         if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
@@ -90,6 +90,14 @@ class Int4Decoder:
         # EXACT in EXACT mode and FAST (bf16-split products) otherwise, and the
         # attention runs the fp32 CUDA-core kernels in EXACT mode.
         self.mode = mode
+        # fused: q/k/v as one MatMulNBits over the concatenated weight rows and
+        # gate/up likewise (a load-time rewrite of same-input siblings); not
+        # fused: the exported graph's seven MatMulNBits per layer, each
+        # dispatched on its own with its own output, as
+        # OnnxGraphExecutor._dispatch runs them (onnx_graph.dart:2918-2934).
+        # The weights are the same either way (the fused weight's rows are the
+        # separate weights stacked), so the two compute the same columns.
+        self.fused = fused
         self.torch = torch
         self.ctx, self.cfg, self.B, self.cap = ctx, cfg, batch, cap
         self.lib = ctx.lib
@@ -104,7 +112,16 @@ class Int4Decoder:
             for name, k, n in (("qkv", c.hidden, c.qkv_n), ("o", c.heads * c.head_dim, c.hidden),
                                ("gate_up", c.hidden, 2 * c.inter), ("down", c.inter, c.hidden)):
                 bq, sc, zp = random_nbits(rng, k, n, c.block)
-                lw[name] = ctx.prepack_nbits(bq, sc, zp, k, n, 4, c.block)
+                if fused or name in ("o", "down"):
+                    lw[name] = ctx.prepack_nbits(bq, sc, zp, k, n, 4, c.block)
+                else:
+                    splits = ({"q": (0, c.heads * c.head_dim),
+                               "k": (c.heads * c.head_dim, (c.heads + c.kv_heads) * c.head_dim),
+                               "v": ((c.heads + c.kv_heads) * c.head_dim, c.qkv_n)} if name == "qkv"
+                              else {"gate": (0, c.inter), "up": (c.inter, 2 * c.inter)})
+                    for part, (r0, r1) in splits.items():
+                        lw[part] = ctx.prepack_nbits(np.ascontiguousarray(bq[r0:r1]), np.ascontiguousarray(sc[r0:r1]),
+                                                     np.ascontiguousarray(zp[r0:r1]), k, r1 - r0, 4, c.block)
                 if keep_host:
                     self.host[(li, name)] = (bq, sc, zp)
             for name, d in (("attn_norm", c.hidden), ("mlp_norm", c.hidden), ("q_norm", c.head_dim),
@@ -141,6 +158,12 @@ class Int4Decoder:
         self.res = torch.empty((t, c.hidden), **f32)
         self.h = torch.empty((t, c.hidden), **f32)
         self.qkv = torch.empty((t, c.qkv_n), **f32)
+        if not fused:  # separate outputs, one per projection
+            self.q = torch.empty((t, c.heads * c.head_dim), **f32)
+            self.k = torch.empty((t, c.kv_heads * c.head_dim), **f32)
+            self.v = torch.empty((t, c.kv_heads * c.head_dim), **f32)
+            self.gate = torch.empty((t, c.inter), **f32)
+            self.up = torch.empty((t, c.inter), **f32)
         self.attn = torch.empty((t, c.heads * c.head_dim), **f32)
         self.o = torch.empty((t, c.hidden), **f32)
         self.gu = torch.empty((t, 2 * c.inter), **f32)
@@ -191,23 +214,38 @@ class Int4Decoder:
             else:  # residual of the previous layer's MLP, then the attention norm
                 chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(lw["attn_norm"]), _ptr(self.h),
                                         _ptr(self.res), T, H, c.eps))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["qkv"].handle, None, self.mode, _ptr(self.qkv)))
-            chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qkv + q_off), _ptr(lw["q_norm"]),
-                                          ctypes.c_void_p(qkv + q_off), T, c.heads, D, c.qkv_n, c.eps))
-            chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qkv + k_off), _ptr(lw["k_norm"]),
-                                          ctypes.c_void_p(qkv + k_off), T, c.kv_heads, D, c.qkv_n, c.eps))
-            chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qkv + q_off), ctypes.c_void_p(qkv + k_off),
-                                ctypes.c_void_p(qkv + v_off), c.qkv_n, c.qkv_n, _ptr(self.kcache[li]),
+            if self.fused:
+                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["qkv"].handle, None, self.mode, _ptr(self.qkv)))
+                qp, kp, vp = qkv + q_off, qkv + k_off, qkv + v_off
+                q_rs = kv_rs = c.qkv_n
+            else:
+                for part in ("q", "k", "v"):
+                    chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
+                                                 _ptr(getattr(self, part))))
+                qp, kp, vp = self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()
+                q_rs, kv_rs = c.heads * D, c.kv_heads * D
+            chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qp), _ptr(lw["q_norm"]), ctypes.c_void_p(qp), T,
+                                          c.heads, D, q_rs, c.eps))
+            chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(kp), _ptr(lw["k_norm"]), ctypes.c_void_p(kp), T,
+                                          c.kv_heads, D, kv_rs, c.eps))
+            chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
+                                _ptr(self.kcache[li]),
                                 _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D, 0,
                                 _ptr(self.attn), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
             chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, self.mode, _ptr(self.o)))
             chk(lib.b2m_rmsnorm_dev(h, _ptr(self.o), _ptr(self.res), _ptr(lw["mlp_norm"]), _ptr(self.h),
                                     _ptr(self.res), T, H, c.eps))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["gate_up"].handle, None, self.mode,
-                                         _ptr(self.gu)))
-            gu = self.gu.data_ptr()
-            chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gu), ctypes.c_void_p(gu + c.inter * 4), 2 * c.inter,
-                                     2 * c.inter, _ptr(self.act), T, c.inter))
+            if self.fused:
+                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["gate_up"].handle, None, self.mode,
+                                             _ptr(self.gu)))
+                gp, up_, g_rs = self.gu.data_ptr(), self.gu.data_ptr() + c.inter * 4, 2 * c.inter
+            else:
+                for part in ("gate", "up"):
+                    chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
+                                                 _ptr(getattr(self, part))))
+                gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
+            chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
+                                     c.inter))
             chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
                                          _ptr(self.down)))
         chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(self.final_norm), _ptr(self.h),

@@ -187,6 +187,36 @@ def test_decoder_sharded_batch_matches_full_batch(ctx):
     torch.cuda.empty_cache()
 
 
+def test_decoder_unfused_projections_match_fused(ctx):
+    """The exported graph's separate q / k / v and gate / up MatMulNBits
+    (each dispatched on its own, with its own output) against the fused
+    siblings the bench's headline decoder uses: the same weights, so EXACT
+    logits and tokens are bitwise equal and PRECISE logits agree within
+    1e-3 / 0.99999 (full width, 4 layers)."""
+    from onnx_runtime_dart_b200.decoder import DecoderConfig, Int4Decoder
+
+    cfg = DecoderConfig.qwen3_0_6b()
+    cfg.layers = 4
+    s, steps = 24, 3
+    prompt = _prompt(cfg, 4, s, 71)
+    decs = [Int4Decoder(ctx, cfg, batch=4, cap=s + steps + 2, max_prefill=s, seed=73, mode=N.MODE_EXACT, fused=f)
+            for f in (True, False)]
+    for d in decs:
+        d.prefill(prompt)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(decs[0].logits.cpu().numpy(), decs[1].logits.cpu().numpy())
+    gens = [d.decode(steps).cpu().numpy() for d in decs]
+    np.testing.assert_array_equal(gens[0], gens[1])
+    np.testing.assert_array_equal(decs[0].logits.cpu().numpy(), decs[1].logits.cpu().numpy())
+    for d in decs:
+        d.set_mode(N.MODE_PRECISE)
+        d.prefill(prompt)
+    torch.cuda.synchronize()
+    _check(decs[1].logits.cpu().numpy(), decs[0].logits.cpu().numpy(), "PRECISE unfused vs fused", 1e-3, 0.99999)
+    del decs
+    torch.cuda.empty_cache()
+
+
 # ---------------------------------------------------------------------------
 # config 4: BERT-base
 # ---------------------------------------------------------------------------
