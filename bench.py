@@ -551,6 +551,8 @@ def main():
     ap.add_argument("--passes", type=int, default=64,
                     help="passes over the weight sets per decode step (step = layers x passes launches)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-weight-links", action="store_true",
+                    help="do not declare each weight set's successor (no cross-call L2 prefetch)")
     ap.add_argument("--case", default="all",
                     choices=["all", "decode1", "decode8", "prefill", "ops", "decoder", "bert", "conv", "cpu"],
                     help="run one phase only (for profiler captures); prints its device time. "
@@ -650,6 +652,11 @@ def main():
     R = args.layers
     ws = make_weights(rng, R)
     packed = [ctx.prepack_nbits(bq, sc, zp, K_DIM, N_DIM, 4, BLOCK) for bq, sc, zp in ws]
+    # The stack's call order, declared as a session would at load time: each
+    # call's kernels prefetch the next call's weights into L2.
+    if not args.no_weight_links:
+        for i, w in enumerate(packed):
+            w.set_next(packed[(i + 1) % R])
 
     def run_graph(m, layers, steps, warmup, passes=1):
         a = torch.randn((m, K_DIM), device=dev, dtype=torch.float32)

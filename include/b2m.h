@@ -186,6 +186,18 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
                                             b2m_weight **out);
 B2M_API b2m_status b2m_weight_free(b2m_weight *w);
 
+/* Declares `next` (a MatMulNBits weight of the same context, or NULL to
+ * clear) as the weight of the call that follows each MatMulNBits call of `w`
+ * in the caller's op order — the next projection of a decoder layer, the
+ * first of the next layer. Kernels running `w` then prefetch the part of
+ * `next` its call will read into L2, so that call's weight prologue (which
+ * runs under programmatic dependent launch while `w`'s call finishes) reads
+ * L2 instead of HBM. A hint: results do not change. Freeing either weight
+ * drops the link; a CUDA graph captured with the link keeps prefetching
+ * `next`, so free `next` only after such graphs. No counterpart in the
+ * reference, whose kernels run on the host. */
+B2M_API b2m_status b2m_weight_set_next(b2m_weight *w, const b2m_weight *next);
+
 /* ---- operators --------------------------------------------------------- */
 
 /* MatMul (opMatMul, onnx_ops.dart:1710-1766): numpy-broadcast batched

@@ -6,6 +6,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <unordered_map>
 
 #include "../../include/b2m.h"
 
@@ -75,6 +76,9 @@ struct b2m_ctx {
   // Attention numerics (b2m_set_attention_mode): fp32 CUDA-core kernels and
   // no key splits when set.
   bool attn_exact = false;
+  // Declared successors (b2m_weight_set_next): the weight whose call follows
+  // each weight's call; its kernels prefetch the successor into L2.
+  std::unordered_map<const b2m_weight *, const b2m_weight *> next_of;
   // Pinned staging for the host-buffer helpers.
   void *pinned = nullptr;
   size_t pinned_bytes = 0;
@@ -131,7 +135,16 @@ struct NbitsWeight {
   // (s, 1024 + zp) of the chunk's two 32-k groups.
   uint8_t *tsq = nullptr;
   uint32_t *tss = nullptr;
+  // Decode records (block >= 32, integer or absent zero points; derived on
+  // the device from bq / scales / zero points, not exported): per (16-column
+  // tile, 64-k chunk) DREC_BYTES = the 512-byte fragment record of bq, then
+  // for each g in 0..7 the fp32 scales s(g, group 0), s(g, group 1),
+  // s(g+8, group 0), s(g+8, group 1), then for each g a 16-bit word of the four
+  // zero-point nibbles in the same order. One 16-byte load per lane for the
+  // nibbles, one for the scales and one 2-byte load for the zero points.
+  uint8_t *drec = nullptr;
 };
+constexpr int DREC_BYTES = 656;
 
 // Packed int8 / uint8 weights: bt[npad][kpad] (K-major), colsum[n] = sum_k b.
 // ts8: TMEM-operand / GEMV layout, per (128-column tile, 128-k chunk) eight
@@ -291,6 +304,19 @@ struct ConvRequant {
 void launch_conv_scatter(const int32_t *z, const ConvGeom &g, int64_t grp, int64_t b0, int64_t nb, int32_t *y32,
                          void *yq, const ConvRequant &rq, cudaStream_t s);
 
+// L2 prefetch of the next call's weight (its declared successor): CTA i of a
+// launch takes bytes [i * share[j], (i + 1) * share[j]) of segment j (share a
+// multiple of 16, set on the host for the launch's grid); empty when seg[0]
+// is null.
+struct PrefetchPlan {
+  const void *seg[2] = {nullptr, nullptr};
+  int64_t bytes[2] = {0, 0};
+  int64_t share[2] = {0, 0};
+  void set_grid(int64_t ctas) {
+    for (int j = 0; j < 2; j++) share[j] = seg[j] && ctas > 0 ? ((bytes[j] + ctas - 1) / ctas + 15) / 16 * 16 : 0;
+  }
+};
+
 // MatMulNBits
 struct NbitsArgs {
   const float *A = nullptr;  // [M][K]
@@ -299,8 +325,11 @@ struct NbitsArgs {
   float *Y = nullptr;           // [M][N]
   int64_t M = 0, K = 0, N = 0;
   int32_t *dev_err = nullptr;
+  PrefetchPlan pf;
 };
 bool nbits_smallm_supported(const NbitsWeight &w, int64_t M);
+// Builds w.drec from bq / scales / zero points when the weight qualifies.
+void nbits_build_drec(NbitsWeight &w, cudaStream_t s);
 void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl);
 void launch_nbits_simt(const NbitsArgs &a, cudaStream_t s);
 void launch_nbits_dequant_f32(const NbitsWeight &w, int64_t K, int64_t N, float *out, cudaStream_t s);

@@ -246,6 +246,123 @@ __global__ void __launch_bounds__(NW * 32) nbits_decode_kernel(const NbitsArgs p
   }
 }
 
+// Decode GEMV over the decode records (NbitsWeight::drec: block >= 32,
+// integer or absent zero points), the same arithmetic as nbits_decode_kernel
+// with every weight-side load of a chunk reduced to three per lane. The
+// post-wait path (activation loads, MMAs, the cross-warp sum) is the chain's
+// critical path, so its shape is fixed at compile time: VEC (16-byte aligned
+// activation rows, K % 4 == 0) and FIT (the warps' chunks cover exactly the
+// padded K, no chunk guard).
+template <int MT, int CPW, bool VEC, bool FIT>
+__global__ void __launch_bounds__(DEC_WARPS * 32) nbits_decode_rec_kernel(const NbitsArgs p, const uint8_t *drec,
+                                                                         int nchunks) {
+  constexpr int NW = DEC_WARPS;
+  __shared__ __align__(16) float s_red[NW * MT * 32 * 4];
+  const int tile = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+
+  // The declared next call's weights go to L2 first, so that its weight
+  // prologue (launched when this grid triggers) reads L2 instead of HBM.
+  if (threadIdx.x == 0 && p.pf.seg[0]) prefetch_share(p.pf, blockIdx.x);
+
+  uint4 v[CPW];
+  float4 s4[CPW];
+  uint32_t zw[CPW];
+#pragma unroll
+  for (int i = 0; i < CPW; i++) {
+    const int c = warp + i * NW;
+    v[i] = make_uint4(0u, 0u, 0u, 0u);
+    s4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    zw[i] = 0x8888u;
+    if (FIT || c < nchunks) {
+      const uint8_t *r = drec + ((size_t)tile * nchunks + c) * DREC_BYTES;
+      v[i] = __ldg(reinterpret_cast<const uint4 *>(r + lane * 16));
+      s4[i] = __ldg(reinterpret_cast<const float4 *>(r + 512 + g * 16));
+      zw[i] = __ldg(reinterpret_cast<const uint16_t *>(r + 640 + g * 2));
+    }
+  }
+  uint32_t af[CPW][2][2][4];  // [chunk][group][step][a0..a3]
+#pragma unroll
+  for (int i = 0; i < CPW; i++)
+#pragma unroll
+    for (int grp = 0; grp < 2; grp++) {
+      const float z0 = (float)((zw[i] >> (4 * grp)) & 15u), z1 = (float)((zw[i] >> (8 + 4 * grp)) & 15u);
+      const uint32_t x0 = grp ? v[i].z : v[i].x, x1 = grp ? v[i].w : v[i].y;
+#pragma unroll
+      for (int s = 0; s < 2; s++) {
+        const uint32_t sel = s == 0 ? 0x4140u : 0x4342u;
+        wfrag<1>(x0, sel, z0, af[i][grp][s][0], af[i][grp][s][2]);
+        wfrag<1>(x1, sel, z1, af[i][grp][s][1], af[i][grp][s][3]);
+      }
+    }
+
+  pdl_launch_dependents();  // after the weight prologue (earlier measured slower)
+  pdl_wait();               // the previous kernel's results (our activations) are visible
+
+  float acc[MT][4];
+#pragma unroll
+  for (int mt = 0; mt < MT; mt++)
+#pragma unroll
+    for (int e = 0; e < 4; e++) acc[mt][e] = 0.f;
+#pragma unroll
+  for (int i = 0; i < CPW; i++) {
+    const int c = warp + i * NW;
+    if (!FIT && c >= nchunks) break;
+    float4 av[2][2][MT];
+#pragma unroll
+    for (int grp = 0; grp < 2; grp++)
+#pragma unroll
+      for (int s = 0; s < 2; s++)
+#pragma unroll
+        for (int mt = 0; mt < MT; mt++)
+          av[grp][s][mt] = load_act4(p.A, p.M, p.K, mt * 8 + g, c * 64 + grp * 32 + s * 16 + 4 * t, VEC);
+#pragma unroll
+    for (int grp = 0; grp < 2; grp++) {
+      const float sa = grp ? s4[i].y : s4[i].x, sb = grp ? s4[i].w : s4[i].z;
+#pragma unroll
+      for (int mt = 0; mt < MT; mt++) {
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < 2; s++) {
+          const float4 a4 = av[grp][s][mt];
+          uint32_t h0, l0, h1, l1;
+          split_h2(a4.x, a4.z, h0, l0);
+          split_h2(a4.y, a4.w, h1, l1);
+          mma_16816(d, af[i][grp][s], h0, h1, d);
+          mma_16816(d, af[i][grp][s], l0, l1, d);
+        }
+        acc[mt][0] = fmaf(sa, d[0], acc[mt][0]);
+        acc[mt][1] = fmaf(sa, d[1], acc[mt][1]);
+        acc[mt][2] = fmaf(sb, d[2], acc[mt][2]);
+        acc[mt][3] = fmaf(sb, d[3], acc[mt][3]);
+      }
+    }
+  }
+
+  // Cross-warp reduction over the K split, in fixed warp order.
+#pragma unroll
+  for (int mt = 0; mt < MT; mt++)
+    *reinterpret_cast<float4 *>(&s_red[((warp * MT + mt) * 32 + lane) * 4]) =
+        make_float4(acc[mt][0], acc[mt][1], acc[mt][2], acc[mt][3]);
+  __syncthreads();
+  constexpr int OUTS = MT * 32 * 4;
+  static_assert(OUTS <= NW * 32, "one output per thread");
+  if (threadIdx.x < OUTS) {
+    const int o = threadIdx.x;
+    const int e = o & 3, ln = (o >> 2) & 31, mt = o >> 7;
+    float sum = 0.f;
+#pragma unroll
+    for (int wp = 0; wp < NW; wp++) sum += s_red[((wp * MT + mt) * 32 + ln) * 4 + e];
+    const int col = tile * 16 + (ln >> 2) + ((e & 2) ? 8 : 0);
+    const int row = mt * 8 + 2 * (ln & 3) + (e & 1);
+    if (row < p.M && col < p.N) {
+      if (p.bias) sum += __ldg(p.bias + col);
+      p.Y[(size_t)row * p.N + col] = sum;
+    }
+  }
+}
+
 // Generic fp32 tile kernel: Y[64 x 64] per CTA, K in steps of 32.
 __global__ void __launch_bounds__(256) nbits_simt_kernel(const NbitsArgs p, const NbitsWeight w) {
   __shared__ float As[32][64 + 4];
@@ -363,6 +480,43 @@ __global__ void nbits_split_planes_kernel(const NbitsWeight w, int64_t K, int64_
   lo[idx] = l;
 }
 
+// Decode records (see NbitsWeight::drec): one warp per (tile, chunk); lanes
+// copy the 512-byte fragment record, lanes 0-7 write the scales and
+// zero-point word of columns g / g+8. Scales of groups past the real blocks
+// are 0 (those nibbles are zero padding), as the bq path treats them.
+__global__ void nbits_drec_kernel(const NbitsWeight w, int64_t records) {
+  const int64_t rec = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (rec >= records) return;
+  const int64_t nchunks = w.kp >> 6;
+  const int64_t tile = rec / nchunks, c = rec - tile * nchunks;
+  uint8_t *r = w.drec + rec * DREC_BYTES;
+  reinterpret_cast<uint4 *>(r)[lane] = reinterpret_cast<const uint4 *>(w.bq + rec * 512)[lane];
+  if (lane < 8) {
+    const int64_t groups = (w.nblocks * w.block + 31) >> 5;
+    float sv[4];
+    uint32_t zw = 0;
+    for (int j = 0; j < 4; j++) {
+      const int64_t col = tile * 16 + lane + ((j & 2) ? 8 : 0);
+      const int grp = j & 1;
+      const int64_t G = 2 * c + grp;
+      const int64_t blk = (G * 32) / w.block;
+      const bool valid = G < groups && blk < w.nblocks;
+      sv[j] = valid ? w.scales[col * w.nblocks + blk] : 0.f;
+      uint32_t z = 8;
+      if (valid && w.zp_kind == 1) {
+        const uint8_t b = w.zp_u8[col * w.zstride + (blk >> 1)];
+        z = (blk & 1) ? (b >> 4) : (b & 15);
+      }
+      // word layout: (g, grp 0) | (g, grp 1) << 4 | (g+8, grp 0) << 8 | (g+8, grp 1) << 12
+      zw |= z << (4 * j);
+    }
+    float4 s4 = make_float4(sv[0], sv[1], sv[2], sv[3]);
+    *reinterpret_cast<float4 *>(r + 512 + lane * 16) = s4;
+    *reinterpret_cast<uint16_t *>(r + 640 + lane * 2) = (uint16_t)zw;
+  }
+}
+
 template <int MT, int ZPK, bool BS16, int CPW>
 void launch_decode_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   auto kern = nbits_decode_kernel<MT, ZPK, BS16, CPW, DEC_WARPS, DEC_LO>;
@@ -381,8 +535,41 @@ void launch_decode_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, a, *a.w));
 }
 
+template <int MT, int CPW, bool VEC, bool FIT>
+void launch_decode_rec_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
+  NbitsArgs p = a;
+  const unsigned grid = (unsigned)((a.N + 15) / 16);
+  p.pf.set_grid(grid);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(DEC_WARPS * 32);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, nbits_decode_rec_kernel<MT, CPW, VEC, FIT>, p, (const uint8_t *)a.w->drec,
+                              (int)(a.w->kp / 64)));
+}
+
+template <int MT, int CPW>
+void launch_decode_rec(const NbitsArgs &a, cudaStream_t s, bool pdl) {
+  const bool vec = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.A) & 15) == 0;
+  const bool fit = a.w->kp / 64 == (int64_t)CPW * DEC_WARPS;
+  if (vec) {
+    fit ? launch_decode_rec_t<MT, CPW, true, true>(a, s, pdl) : launch_decode_rec_t<MT, CPW, true, false>(a, s, pdl);
+  } else {
+    fit ? launch_decode_rec_t<MT, CPW, false, true>(a, s, pdl) : launch_decode_rec_t<MT, CPW, false, false>(a, s, pdl);
+  }
+}
+
 template <int MT, int CPW>
 void launch_decode_z(const NbitsArgs &a, cudaStream_t s, bool pdl) {
+  if (a.w->drec) {
+    launch_decode_rec<MT, CPW>(a, s, pdl);
+    return;
+  }
   const bool bs16 = a.w->block == 16;
   switch (a.w->zp_kind) {
     case 0: bs16 ? launch_decode_t<MT, 0, true, CPW>(a, s, pdl) : launch_decode_t<MT, 0, false, CPW>(a, s, pdl); break;
@@ -421,8 +608,23 @@ void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   } else if (cpw <= 2) {
     if (mt == 1) launch_decode_z<1, 2>(a, s, pdl);
     else launch_decode_z<2, 2>(a, s, pdl);
+  } else if (cpw == 3 && a.w->drec) {
+    launch_decode_rec<1, 3>(a, s, pdl);  // K = 3072: the warps' chunks cover K exactly
   } else {
     launch_decode_z<1, 4>(a, s, pdl);
+  }
+}
+
+void nbits_build_drec(NbitsWeight &w, cudaStream_t s) {
+  if (w.drec || w.block < 32 || w.zp_kind == 2 || !w.bq) return;
+  const int64_t records = (w.npad / 16) * (w.kp / 64);
+  B2M_CUDA(cudaMalloc(&w.drec, (size_t)(records * DREC_BYTES)));
+  nbits_drec_kernel<<<(unsigned)((records + 7) / 8), 256, 0, s>>>(w, records);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    cudaFree(w.drec);
+    w.drec = nullptr;
+    B2M_CUDA(e);
   }
 }
 

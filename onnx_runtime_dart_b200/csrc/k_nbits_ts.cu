@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     nbits_ts_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_y,
                     int use_tma_y, const uint4 *__restrict__ tsq, const uint2 *__restrict__ tss,
                     const float *__restrict__ bias, float *__restrict__ Y, int M, int N, int nchunks,
-                    int32_t *dev_err) {
+                    int32_t *dev_err, const PrefetchPlan pf) {
   using L = TsLayout<BT, STAGES, KSUB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -143,6 +143,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   auto chunks_of = [&](int rt) { return min(KSUB, nchunks - rt * KSUB); };
 
   if (threadIdx.x == 0) {
+    // The declared next call's weights go to L2 (this CTA's share).
+    if (pf.seg[0]) prefetch_share(pf, blockIdx.x + (int64_t)gridDim.x * (blockIdx.y + (int64_t)gridDim.y * blockIdx.z));
     for (int s = 0; s < STAGES; s++) {
       mbar_init(&full[s], 1 + 4);
       mbar_init(&empty[s], 1);
@@ -393,6 +395,8 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, 
   }
   auto kern = nbits_ts_kernel<BT, STAGES, KSUB>;
   set_smem_limit_once<nbits_ts_kernel<BT, STAGES, KSUB>>((int)L::BYTES);
+  PrefetchPlan pf = a.pf;
+  pf.set_grid((a.w->npad / 128) * ((a.M + BT - 1) / BT) * splits);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(a.w->npad / 128), (unsigned)((a.M + BT - 1) / BT), (unsigned)splits);
   cfg.blockDim = dim3(TS_THREADS);
@@ -409,7 +413,7 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, 
   cfg.numAttrs = splits > 1 ? 2 : 1;
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, ty, use_ty, reinterpret_cast<const uint4 *>(a.w->tsq),
                               reinterpret_cast<const uint2 *>(a.w->tss), a.bias, a.Y, (int)a.M, (int)a.N,
-                              (int)(a.w->kp / 64), a.dev_err));
+                              (int)(a.w->kp / 64), a.dev_err, pf));
 }
 
 // Token-tile width. Per CTA: MMA time (a readiness check per stage caps the

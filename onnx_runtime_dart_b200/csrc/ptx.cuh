@@ -111,6 +111,30 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// Hint: bring [src, src + bytes) into L2 (16-byte aligned address, size a
+// multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// This CTA's share of the segments of a prefetch plan: CTA `cta` takes bytes
+// [cta * share, (cta + 1) * share) of each segment (share a multiple of 16,
+// computed on the host), in pieces of at most 16 KB. Segment sizes are
+// multiples of 16.
+template <typename Plan>
+__device__ __forceinline__ void prefetch_share(const Plan &pl, int64_t cta) {
+#pragma unroll
+  for (int j = 0; j < 2; j++) {
+    if (!pl.seg[j] || pl.share[j] <= 0) continue;
+    int64_t off = cta * pl.share[j];
+    const int64_t end = off + pl.share[j] < pl.bytes[j] ? off + pl.share[j] : pl.bytes[j];
+    for (; off < end; off += 16384) {
+      const int64_t n = end - off < 16384 ? end - off : 16384;
+      bulk_prefetch_l2(static_cast<const uint8_t *>(pl.seg[j]) + off, (uint32_t)n);
+    }
+  }
+}
+
 __device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until the bulk stores committed by this thread have completed.
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }

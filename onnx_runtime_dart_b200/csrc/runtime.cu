@@ -571,6 +571,28 @@ static F32GemmArgs nbits_precise_args(const float *A, int64_t m, int64_t K, int6
   return p;
 }
 
+// The L2 prefetch plan of an m-row call of `w` in `mode`: the segments the
+// same route would read for w's declared successor (decode records for the
+// GEMV, the TMEM-operand layout for the tensor-core prefill); none without a
+// successor or for other routes.
+static void nbits_prefetch_plan(const b2m_ctx *ctx, const b2m_weight *w, int64_t m, int32_t mode, NbitsArgs &p) {
+  const auto it = ctx->next_of.find(w);
+  if (it == ctx->next_of.end() || !it->second || it->second->kind != W_NBITS) return;
+  const b2m_weight *nx = it->second;
+  const NbitsWeight &n = nx->nb;
+  const bool gemv = mode == B2M_MODE_PRECISE ? nbits_smallm_supported(n, m)
+                                             : mode == B2M_MODE_FAST && nbits_use_smallm(n, m, nx->k, nx->n);
+  if (gemv && n.drec) {
+    p.pf.seg[0] = n.drec;
+    p.pf.bytes[0] = (n.npad / 16) * (n.kp / 64) * DREC_BYTES;
+  } else if (!gemv && mode == B2M_MODE_FAST && n.tsq && nbits_tc_supported(n, m, nx->k, nx->n)) {
+    p.pf.seg[0] = n.tsq;
+    p.pf.bytes[0] = (n.npad / 128) * (n.kp / 64) * 4096;
+    p.pf.seg[1] = n.tss;
+    p.pf.bytes[1] = (n.npad / 128) * (n.kp / 64) * 128 * 8;
+  }
+}
+
 // Device scratch bytes nbits_run needs for an m-row call.
 size_t nbits_scratch_bytes(const b2m_weight *w, int64_t m, int32_t mode) {
   if (m == 0) return 0;
@@ -601,6 +623,7 @@ void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_w
       p.K = K;
       p.N = N;
       p.dev_err = ctx->dev_err;
+      nbits_prefetch_plan(ctx, w, m, mode, p);
       launch_nbits_smallm(p, ctx->stream, ctx->pdl);
       return;
     }
@@ -635,6 +658,7 @@ void nbits_run(b2m_ctx *ctx, Scratch &sc, const float *A, int64_t m, const b2m_w
     p.K = K;
     p.N = N;
     p.dev_err = ctx->dev_err;
+    nbits_prefetch_plan(ctx, w, m, mode, p);
     if (nbits_use_smallm(w->nb, m, K, N)) {
       launch_nbits_smallm(p, ctx->stream, ctx->pdl);
     } else if (nbits_tc_supported(w->nb, m, K, N)) {
@@ -1196,7 +1220,10 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
         w->seg_bytes[SEG_NB_ZP_F32] = z.size() * 4;
         B2M_CUDA(cudaMemcpy(W.zp_f32, z.data(), z.size() * 4, cudaMemcpyHostToDevice));
       }
+      nbits_build_drec(W, ctx->stream);
+      B2M_CUDA(cudaStreamSynchronize(ctx->stream));
     } catch (...) {
+      cudaFree(W.drec);
       cudaFree(W.bq);
       cudaFree(W.scales);
       cudaFree(W.zp_u8);
@@ -1211,11 +1238,26 @@ B2M_API b2m_status b2m_weight_prepack_nbits(b2m_ctx *ctx, const uint8_t *b_q, co
   });
 }
 
+B2M_API b2m_status b2m_weight_set_next(b2m_weight *w, const b2m_weight *next) {
+  return guarded([&] {
+    B2M_REQUIRE(w, B2M_ERR_INVALID_ARGUMENT, "null weight");
+    B2M_REQUIRE(!next || next->ctx == w->ctx, B2M_ERR_INVALID_ARGUMENT,
+                "weight set_next: both weights must belong to one context");
+    if (next)
+      w->ctx->next_of[w] = next;
+    else
+      w->ctx->next_of.erase(w);
+  });
+}
+
 B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
   return guarded([&] {
     if (!w) return;
     DeviceGuard dg(w->ctx->device);
     cudaStreamSynchronize(w->ctx->stream);
+    // No later launch may prefetch this weight, nor prefetch for it.
+    auto &nx = w->ctx->next_of;
+    for (auto it = nx.begin(); it != nx.end();) it = (it->first == w || it->second == w) ? nx.erase(it) : std::next(it);
     cudaFree(w->f32);
     cudaFree(w->bx_hi);
     cudaFree(w->bx_lo);
@@ -1232,6 +1274,7 @@ B2M_API b2m_status b2m_weight_free(b2m_weight *w) {
     cudaFree(w->nb.srec);
     cudaFree(w->nb.tsq);
     cudaFree(w->nb.tss);
+    cudaFree(w->nb.drec);
     delete w;
   });
 }
@@ -1367,7 +1410,12 @@ B2M_API b2m_status b2m_weight_import(b2m_ctx *ctx, const void *buf, size_t size,
         B2M_CUDA(cudaMemcpy(*slot, p, segb[i], cudaMemcpyHostToDevice));
         p += segb[i];
       }
+      if (w->kind == W_NBITS) {  // the decode records are derived, not stored
+        nbits_build_drec(w->nb, ctx->stream);
+        B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+      }
     } catch (...) {
+      cudaFree(w->nb.drec);
       for (int i = 0; i < SEG_COUNT; i++) cudaFree(*segment_slot(w, i));
       delete w;
       throw;

@@ -131,6 +131,13 @@ class Int4Decoder:
                 if keep_host:
                     self.host[(li, name)] = g
             self.layers.append(lw)
+        # The projections in call order, each declared as the successor of the
+        # one before (the last layer's down projection is followed by the
+        # first layer's q/k/v projection of the next step).
+        order = ("qkv", "o", "gate_up", "down") if fused else ("q", "k", "v", "o", "gate", "up", "down")
+        seq = [lw[nm] for lw in self.layers for nm in order]
+        for a, b in zip(seq, seq[1:] + seq[:1]):
+            a.set_next(b)
         gf = (1.0 + 0.1 * rng.standard_normal(c.hidden)).astype(np.float32)
         self.final_norm = torch.from_numpy(gf).to(dev)
         gen = torch.Generator(device=dev)

@@ -354,6 +354,7 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
                 w.shape = tuple(int(d) for d in arrays[0].shape)
             disp._packed[key] = w
 
+    nbits_order = []
     for nd in model.nodes:
         ins = nd.inputs
         if nd.op_type == "MatMul" and len(ins) > 1 and ins[1] in inits and inits[ins[1]].ndim == 2 \
@@ -389,6 +390,13 @@ def prepack_session(ctx, model: OnnxModel, cache_dir: str | None = None, f32_mod
             packed(key, "nbits", (k, n, bits, block), [bq, sc, zp],
                    lambda bq=bq, sc=sc, zp=zp, k=k, n=n, bits=bits, block=block: ops.prepack_nbits(
                        ctx, bq, sc, zp, k=k, n=n, bits=bits, blockSize=block))
+            nbits_order.append(key)
+    # The MatMulNBits calls in node order, each weight declared as the
+    # successor of the one before (b2m_weight_set_next): their kernels
+    # prefetch the next projection's weights into L2.
+    for a, b in zip(nbits_order, nbits_order[1:]):
+        if a != b:
+            disp._packed[a].set_next(disp._packed[b])
     stats = {"packed": len(disp._packed), "cache_hits": cache.hits if cache else 0,
              "cache_misses": cache.misses if cache else 0}
     return disp, stats

@@ -241,6 +241,12 @@ class PackedWeight:
         N.check(self.ctx.lib.b2m_weight_info(self.handle, ctypes.byref(k), ctypes.byref(n)))
         return int(k.value), int(n.value)
 
+    def set_next(self, nxt: "PackedWeight | None"):
+        """Declares the MatMulNBits weight of the call that follows this
+        weight's calls (b2m_weight_set_next): their kernels prefetch it into
+        L2. A hint; None clears it."""
+        N.check(self.ctx.lib.b2m_weight_set_next(self.handle, None if nxt is None else nxt.handle))
+
     def free(self):
         if self.handle:
             N.check(self.ctx.lib.b2m_weight_free(self.handle))
