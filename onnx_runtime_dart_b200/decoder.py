@@ -81,7 +81,7 @@ class Int4Decoder:
     cache of `cap` positions; prompts up to `max_prefill` tokens."""
 
     def __init__(self, ctx, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int, seed: int = 0,
-                 keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True):
+                 keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True, session=None):
         import torch
 
         if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
@@ -97,15 +97,184 @@ class Int4Decoder:
         # OnnxGraphExecutor._dispatch runs them (onnx_graph.dart:2918-2934).
         # The weights are the same either way (the fused weight's rows are the
         # separate weights stacked), so the two compute the same columns.
-        self.fused = fused
+        self.fused = fused if session is None else False
+        # session: an _OnnxSession (from_onnx) whose MatMulNBits nodes are run
+        # through GpuDispatch.dispatch; the weights are its prepacked
+        # initializers.
+        self.session = session
         self.torch = torch
         self.ctx, self.cfg, self.B, self.cap = ctx, cfg, batch, cap
         self.lib = ctx.lib
         c = cfg
         dev = torch.device("cuda", torch.cuda.current_device())
         self.dev = dev
-        rng = np.random.default_rng(seed)
         self.host = {} if keep_host else None
+        if session is None:
+            self._random_weights(ctx, seed, keep_host)
+        else:
+            self._session_weights(session)
+        half = c.head_dim // 2
+        inv = 1.0 / (c.theta ** (np.arange(half, dtype=np.float64) * 2.0 / c.head_dim))
+        ang = np.arange(cap, dtype=np.float64)[:, None] * inv[None, :]
+        self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
+        self.sin = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
+        kv_shape = (c.layers, batch, c.kv_heads, cap, c.head_dim)
+        self.kcache = torch.zeros(kv_shape, device=dev, dtype=torch.float32)
+        self.vcache = torch.zeros(kv_shape, device=dev, dtype=torch.float32)
+        self.past = torch.zeros(batch, device=dev, dtype=torch.int32)
+        t = batch * max_prefill
+        self.max_tokens = t
+        f32 = dict(device=dev, dtype=torch.float32)
+        self.res = torch.empty((t, c.hidden), **f32)
+        self.h = torch.empty((t, c.hidden), **f32)
+        self.qkv = torch.empty((t, c.qkv_n), **f32)
+        if not self.fused:  # separate outputs, one per projection
+            self.q = torch.empty((t, c.heads * c.head_dim), **f32)
+            self.k = torch.empty((t, c.kv_heads * c.head_dim), **f32)
+            self.v = torch.empty((t, c.kv_heads * c.head_dim), **f32)
+            self.gate = torch.empty((t, c.inter), **f32)
+            self.up = torch.empty((t, c.inter), **f32)
+        self.attn = torch.empty((t, c.heads * c.head_dim), **f32)
+        self.o = torch.empty((t, c.hidden), **f32)
+        self.gu = torch.empty((t, 2 * c.inter), **f32)
+        self.act = torch.empty((t, c.inter), **f32)
+        self.down = torch.empty((t, c.hidden), **f32)
+        self.last = torch.empty((batch, c.hidden), **f32)
+        self.logits = torch.empty((batch, c.vocab), **f32)
+        self.ids = torch.zeros(t, device=dev, dtype=torch.int64)
+        self.next_ids = torch.zeros(batch, device=dev, dtype=torch.int64)
+        self.last_idx = {}
+        self.t_last = ctx.wrap(self.last.data_ptr(), (batch, c.hidden), np.float32)
+        self.t_logits = ctx.wrap(self.logits.data_ptr(), (batch, c.vocab), np.float32)
+        self.graph = None
+        self.stream = torch.cuda.Stream(device=dev)
+        self._wraps = {}
+
+    def set_mode(self, mode: int) -> None:
+        """Switches the numerics mode (FAST, PRECISE or EXACT) of later calls;
+        the captured decode graph is dropped and captured again on next use."""
+        if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
+            raise N.ArgumentError("decoder: mode must be FAST, PRECISE or EXACT")
+        self.mode = mode
+        self.graph = None
+
+    # -- the exported graph ----------------------------------------------------
+    PROJ = (("q", "hidden", "q_n"), ("k", "hidden", "kv_n"), ("v", "hidden", "kv_n"), ("o", "q_n", "hidden"),
+            ("gate", "hidden", "inter"), ("up", "hidden", "inter"), ("down", "inter", "hidden"))
+
+    def export_onnx(self, path: str) -> None:
+        """Writes this decoder (built with keep_host=True) as an ONNX graph in
+        the node order of a decoder export run by OnnxGraphExecutor: per layer
+        (Skip)SimplifiedLayerNormalization, the q / k / v MatMulNBits, the
+        per-head q / k norms, GroupQueryAttention with rotary, the o
+        MatMulNBits, SkipSimplifiedLayerNormalization, the gate / up
+        MatMulNBits, Sigmoid and the two Muls of SwiGLU, the down MatMulNBits;
+        then the final norm and the fp32 lm_head MatMul. The projection
+        weights are the separate (unfused) initializers."""
+        from . import onnx_writer as W
+
+        if self.host is None or "lm_head" not in self.host:
+            raise N.ArgumentError("decoder export: build the decoder with keep_host=True")
+        c, hst = self.cfg, self.host
+        dims = {"hidden": c.hidden, "q_n": c.heads * c.head_dim, "kv_n": c.kv_heads * c.head_dim, "inter": c.inter}
+        rows = {"q": (0, dims["q_n"]), "k": (dims["q_n"], dims["q_n"] + dims["kv_n"]),
+                "v": (dims["q_n"] + dims["kv_n"], c.qkv_n), "gate": (0, c.inter), "up": (c.inter, 2 * c.inter)}
+        src = {"q": "qkv", "k": "qkv", "v": "qkv", "o": "o", "gate": "gate_up", "up": "gate_up", "down": "down"}
+        inits, nodes = [], []
+        ms = "com.microsoft"
+        inits.append(W.tensor("embed_tokens.weight", hst["emb"]))
+        nodes.append(W.node("Gather", ["embed_tokens.weight", "input_ids"], ["x0"]))
+        res = "x0"
+        prev = None
+        eps = W.attr_float("epsilon", c.eps)
+        for li in range(c.layers):
+            for nm in ("attn_norm", "mlp_norm", "q_norm", "k_norm"):
+                inits.append(W.tensor(f"layers.{li}.{nm}.weight", hst[(li, nm)]))
+            pre = f"l{li}."
+            if prev is None:
+                nodes.append(W.node("SimplifiedLayerNormalization", [res, f"layers.{li}.attn_norm.weight"],
+                                    [pre + "hn"], [eps]))
+            else:
+                nodes.append(W.node("SkipSimplifiedLayerNormalization", [prev, res, f"layers.{li}.attn_norm.weight"],
+                                    [pre + "hn", "", "", pre + "res0"], [eps], domain=ms))
+                res = pre + "res0"
+            for part, kd, nd in self.PROJ:
+                bq, sc, zp = hst[(li, src[part])]
+                r0, r1 = rows.get(part, (0, bq.shape[0]))
+                base = f"layers.{li}.{part}"
+                inits.append(W.tensor(base + ".qweight", np.ascontiguousarray(bq[r0:r1])))
+                inits.append(W.tensor(base + ".scales", np.ascontiguousarray(sc[r0:r1])))
+                inits.append(W.tensor(base + ".qzeros", np.ascontiguousarray(zp[r0:r1])))
+                x_in = {"q": pre + "hn", "k": pre + "hn", "v": pre + "hn", "o": pre + "attn", "gate": pre + "hn2",
+                        "up": pre + "hn2", "down": pre + "act"}[part]
+                attrs = [W.attr_int("K", dims[kd]), W.attr_int("N", dims[nd]), W.attr_int("bits", 4),
+                         W.attr_int("block_size", c.block)]
+                nodes.append(W.node("MatMulNBits", [x_in, base + ".qweight", base + ".scales", base + ".qzeros"],
+                                    [pre + part], attrs, domain=ms))
+                if part == "v":
+                    for h, nm in (("q", "q_norm"), ("k", "k_norm")):
+                        nodes.append(W.node("SimplifiedLayerNormalization", [pre + h, f"layers.{li}.{nm}.weight"],
+                                            [pre + h + "n"], [eps, W.attr_int("axis", -1)]))
+                    nodes.append(W.node("GroupQueryAttention",
+                                        [pre + "qn", pre + "kn", pre + "v", f"past_key.{li}", f"past_value.{li}",
+                                         "seqlens_k", "total_sequence_length", "cos_cache", "sin_cache"],
+                                        [pre + "attn", f"present_key.{li}", f"present_value.{li}"],
+                                        [W.attr_int("num_heads", c.heads), W.attr_int("kv_num_heads", c.kv_heads),
+                                         W.attr_int("do_rotary", 1)], domain=ms))
+                if part == "o":
+                    nodes.append(W.node("SkipSimplifiedLayerNormalization",
+                                        [pre + "o", res, f"layers.{li}.mlp_norm.weight"],
+                                        [pre + "hn2", "", "", pre + "res1"], [eps], domain=ms))
+                    res = pre + "res1"
+                if part == "up":
+                    nodes.append(W.node("Sigmoid", [pre + "gate"], [pre + "sig"]))
+                    nodes.append(W.node("Mul", [pre + "gate", pre + "sig"], [pre + "silu"]))
+                    nodes.append(W.node("Mul", [pre + "silu", pre + "up"], [pre + "act"]))
+            prev = pre + "down"
+        inits.append(W.tensor("norm.weight", hst["final_norm"]))
+        inits.append(W.tensor("lm_head.weight", hst["lm_head"]))
+        nodes.append(W.node("SkipSimplifiedLayerNormalization", [prev, res, "norm.weight"], ["hf"], [eps], domain=ms))
+        nodes.append(W.node("MatMul", ["hf", "lm_head.weight"], ["logits"]))
+        with open(path, "wb") as f:
+            f.write(W.model(nodes, inits, ["input_ids"], ["logits"]))
+
+    @classmethod
+    def from_onnx(cls, ctx, path: str, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int,
+                  mode: int = N.MODE_FAST, cache_dir: str | None = None) -> "Int4Decoder":
+        """A decoder over a model written by export_onnx: load_model reads it,
+        prepack_session packs every MatMulNBits / MatMul initializer under the
+        keys GpuDispatch looks up (and declares the projections' order for the
+        L2 prefetch), and every projection of the chain is run by
+        GpuDispatch.dispatch on the node's own inputs and attributes, writing
+        into the decoder's buffers. The glue between them (norms, attention,
+        SwiGLU) runs as the decoder's device ops."""
+        from .onnx_model import load_model, prepack_session
+
+        model = load_model(path)
+        disp, _ = prepack_session(ctx, model, cache_dir=cache_dir, nbits_mode=mode)
+        sess = _OnnxSession(model, disp, cfg)
+        return cls(ctx, cfg, batch, cap, max_prefill, mode=mode, session=sess)
+
+    def _dispatch_proj(self, part: str, lw, x, T: int, y):
+        """One MatMulNBits node through the dispatch, into buffer y."""
+        node = lw["nodes"][part]
+        k, n = int(node.attrs["K"]), int(node.attrs["N"])
+        key = (x.data_ptr(), y.data_ptr(), T, k, n)
+        pair = self._wraps.get(key)
+        if pair is None:
+            pair = (self.ctx.wrap(x.data_ptr(), (T, k), np.float32), self.ctx.wrap(y.data_ptr(), (T, n), np.float32))
+            self._wraps[key] = pair
+        inits = self.session.model.initializers
+        vals = [pair[0]] + [inits.get(nm) if nm else None for nm in node.inputs[1:]]
+        self.session.dispatch.nbits_mode = self.mode
+        self.session.dispatch.dispatch("MatMulNBits", node.inputs, vals, node.attrs, outputs=[pair[1]])
+
+    def _random_weights(self, ctx, seed: int, keep_host: bool):
+        """Random weights with config 3's distributions, prepacked."""
+        import torch
+
+        c, dev, fused = self.cfg, self.dev, self.fused
+        rng = np.random.default_rng(seed)
         self.layers = []
         for li in range(c.layers):
             lw = {}
@@ -150,49 +319,23 @@ class Int4Decoder:
             self.host["emb"] = self.emb.cpu().numpy()
             self.host["lm_head"] = lm
         del lm
-        half = c.head_dim // 2
-        inv = 1.0 / (c.theta ** (np.arange(half, dtype=np.float64) * 2.0 / c.head_dim))
-        ang = np.arange(cap, dtype=np.float64)[:, None] * inv[None, :]
-        self.cos = torch.from_numpy(np.cos(ang).astype(np.float32)).to(dev)
-        self.sin = torch.from_numpy(np.sin(ang).astype(np.float32)).to(dev)
-        kv_shape = (c.layers, batch, c.kv_heads, cap, c.head_dim)
-        self.kcache = torch.zeros(kv_shape, device=dev, dtype=torch.float32)
-        self.vcache = torch.zeros(kv_shape, device=dev, dtype=torch.float32)
-        self.past = torch.zeros(batch, device=dev, dtype=torch.int32)
-        t = batch * max_prefill
-        self.max_tokens = t
-        f32 = dict(device=dev, dtype=torch.float32)
-        self.res = torch.empty((t, c.hidden), **f32)
-        self.h = torch.empty((t, c.hidden), **f32)
-        self.qkv = torch.empty((t, c.qkv_n), **f32)
-        if not fused:  # separate outputs, one per projection
-            self.q = torch.empty((t, c.heads * c.head_dim), **f32)
-            self.k = torch.empty((t, c.kv_heads * c.head_dim), **f32)
-            self.v = torch.empty((t, c.kv_heads * c.head_dim), **f32)
-            self.gate = torch.empty((t, c.inter), **f32)
-            self.up = torch.empty((t, c.inter), **f32)
-        self.attn = torch.empty((t, c.heads * c.head_dim), **f32)
-        self.o = torch.empty((t, c.hidden), **f32)
-        self.gu = torch.empty((t, 2 * c.inter), **f32)
-        self.act = torch.empty((t, c.inter), **f32)
-        self.down = torch.empty((t, c.hidden), **f32)
-        self.last = torch.empty((batch, c.hidden), **f32)
-        self.logits = torch.empty((batch, c.vocab), **f32)
-        self.ids = torch.zeros(t, device=dev, dtype=torch.int64)
-        self.next_ids = torch.zeros(batch, device=dev, dtype=torch.int64)
-        self.last_idx = {}
-        self.t_last = ctx.wrap(self.last.data_ptr(), (batch, c.hidden), np.float32)
-        self.t_logits = ctx.wrap(self.logits.data_ptr(), (batch, c.vocab), np.float32)
-        self.graph = None
-        self.stream = torch.cuda.Stream(device=dev)
 
-    def set_mode(self, mode: int) -> None:
-        """Switches the numerics mode (FAST, PRECISE or EXACT) of later calls;
-        the captured decode graph is dropped and captured again on next use."""
-        if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
-            raise N.ArgumentError("decoder: mode must be FAST, PRECISE or EXACT")
-        self.mode = mode
-        self.graph = None
+    def _session_weights(self, sess):
+        """The weights of an exported model: the MatMulNBits initializers
+        packed by prepack_session (looked up under the dispatch's keys), the
+        norm gains, the embedding and the lm_head as initializers."""
+        import torch
+
+        c, dev, inits = self.cfg, self.dev, sess.model.initializers
+        t = lambda name: torch.from_numpy(np.ascontiguousarray(inits[name], np.float32)).to(dev)
+        self.layers = []
+        for li in range(c.layers):
+            lw = {name: t(f"layers.{li}.{name}.weight") for name in ("attn_norm", "mlp_norm", "q_norm", "k_norm")}
+            lw["nodes"] = sess.layer_nodes[li]
+            self.layers.append(lw)
+        self.final_norm = t("norm.weight")
+        self.emb = t("embed_tokens.weight")
+        self.lm_head = sess.dispatch._packed[("f32", "lm_head.weight")]
 
     # -- one pass over the layers for `seq` new tokens per sequence -----------
     def _forward(self, seq: int):
@@ -227,8 +370,11 @@ class Int4Decoder:
                 q_rs = kv_rs = c.qkv_n
             else:
                 for part in ("q", "k", "v"):
-                    chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
-                                                 _ptr(getattr(self, part))))
+                    if self.session is not None:
+                        self._dispatch_proj(part, lw, self.h, T, getattr(self, part))
+                    else:
+                        chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
+                                                     _ptr(getattr(self, part))))
                 qp, kp, vp = self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()
                 q_rs, kv_rs = c.heads * D, c.kv_heads * D
             chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qp), _ptr(lw["q_norm"]), ctypes.c_void_p(qp), T,
@@ -239,7 +385,10 @@ class Int4Decoder:
                                 _ptr(self.kcache[li]),
                                 _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D, 0,
                                 _ptr(self.attn), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, self.mode, _ptr(self.o)))
+            if self.session is not None:
+                self._dispatch_proj("o", lw, self.attn, T, self.o)
+            else:
+                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, self.mode, _ptr(self.o)))
             chk(lib.b2m_rmsnorm_dev(h, _ptr(self.o), _ptr(self.res), _ptr(lw["mlp_norm"]), _ptr(self.h),
                                     _ptr(self.res), T, H, c.eps))
             if self.fused:
@@ -248,13 +397,19 @@ class Int4Decoder:
                 gp, up_, g_rs = self.gu.data_ptr(), self.gu.data_ptr() + c.inter * 4, 2 * c.inter
             else:
                 for part in ("gate", "up"):
-                    chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
-                                                 _ptr(getattr(self, part))))
+                    if self.session is not None:
+                        self._dispatch_proj(part, lw, self.h, T, getattr(self, part))
+                    else:
+                        chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
+                                                     _ptr(getattr(self, part))))
                 gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
             chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
                                      c.inter))
-            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
-                                         _ptr(self.down)))
+            if self.session is not None:
+                self._dispatch_proj("down", lw, self.act, T, self.down)
+            else:
+                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
+                                             _ptr(self.down)))
         chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(self.final_norm), _ptr(self.h),
                                 _ptr(self.res), T, H, c.eps))
         idx = self.last_idx.get(seq)
@@ -316,3 +471,24 @@ class Int4Decoder:
                     self._decode_body()
                 out[i].copy_(self.next_ids)
         return out
+
+
+class _OnnxSession:
+    """An exported decoder model, its GpuDispatch, and each layer's
+    MatMulNBits nodes by projection name (read from the initializer names
+    export_onnx writes: layers.<i>.<proj>.qweight)."""
+
+    def __init__(self, model, dispatch, cfg: DecoderConfig):
+        self.model, self.dispatch = model, dispatch
+        self.layer_nodes = [dict() for _ in range(cfg.layers)]
+        for nd in model.nodes:
+            if nd.op_type != "MatMulNBits" or len(nd.inputs) < 2:
+                continue
+            parts = nd.inputs[1].split(".")
+            if len(parts) == 4 and parts[0] == "layers" and parts[3] == "qweight":
+                self.layer_nodes[int(parts[1])][parts[2]] = nd
+        for li, nodes in enumerate(self.layer_nodes):
+            missing = {p for p, _, _ in Int4Decoder.PROJ} - set(nodes)
+            if missing:
+                raise N.ArgumentError(f"decoder model: layer {li} lacks MatMulNBits nodes {sorted(missing)}")
+

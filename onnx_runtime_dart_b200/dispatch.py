@@ -49,7 +49,11 @@ class GpuDispatch:
             self._packed[key] = w
         return w
 
-    def dispatch(self, op_type: str, input_names: list, values: list, attrs: dict):
+    def dispatch(self, op_type: str, input_names: list, values: list, attrs: dict, outputs: list | None = None):
+        """Runs one node; returns its outputs (device tensors), or None for ops
+        outside the family. `outputs` optionally names caller-owned device
+        tensors the MatMulNBits output is written into (so a chain can keep
+        fixed buffers, e.g. inside a captured CUDA graph)."""
         if op_type not in self.HANDLED:
             return None
 
@@ -126,7 +130,7 @@ class GpuDispatch:
         else:
             w = ops.prepack_nbits(ctx, need(1), need(2), zp, k=k, n=n, bits=bits, blockSize=block)
         return [ops.opMatMulNBits(a, w, k=k, n=n, bits=bits, blockSize=block, bias=bias, mode=self.nbits_mode,
-                                  ctx=ctx)]
+                                  ctx=ctx, out=outputs[0] if outputs else None)]
 
     def _conv(self, op_type, input_names, need, opt, attrs):
         ctx = self.ctx

@@ -1,6 +1,7 @@
-"""A minimal ONNX protobuf writer for tests: builds ModelProto bytes with the
-field numbers of the ONNX schema (the reader under test is
-onnx_runtime_dart_b200/onnx_model.py)."""
+"""A minimal ONNX protobuf writer: ModelProto bytes with the field numbers of
+the ONNX schema (onnx_model.py reads them back). Used to export the drivers'
+random-weight models as ONNX graphs and by the loader tests; no onnx package
+is needed."""
 import struct
 
 import numpy as np

@@ -217,6 +217,35 @@ def test_decoder_unfused_projections_match_fused(ctx):
     torch.cuda.empty_cache()
 
 
+@pytest.mark.parametrize("mode", ["exact", "fast"])
+def test_decoder_exported_graph_through_dispatch(ctx, tmp_path, mode):
+    """The decoder written as an ONNX graph (the export's seven MatMulNBits
+    per layer, norms, GroupQueryAttention, SwiGLU, lm_head MatMul), read back
+    with load_model, packed by prepack_session, and every projection run by
+    GpuDispatch.dispatch on the node's own inputs and attributes: bitwise the
+    same logits and greedy tokens as the directly built decoder with the same
+    weights, prefill and graph-replayed decode."""
+    from onnx_runtime_dart_b200.decoder import DecoderConfig, Int4Decoder
+
+    cfg = DecoderConfig.tiny()
+    md = N.MODE_EXACT if mode == "exact" else N.MODE_FAST
+    b, s, steps = 2, 7, 3
+    direct = Int4Decoder(ctx, cfg, batch=b, cap=s + steps + 2, max_prefill=s, seed=79, keep_host=True, fused=False,
+                         mode=md)
+    path = str(tmp_path / "decoder.onnx")
+    direct.export_onnx(path)
+    loaded = Int4Decoder.from_onnx(ctx, path, cfg, batch=b, cap=s + steps + 2, max_prefill=s, mode=md)
+    prompt = _prompt(cfg, b, s, 83)
+    for d in (direct, loaded):
+        d.prefill(prompt)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(direct.logits.cpu().numpy(), loaded.logits.cpu().numpy())
+    gens = [d.decode(steps).cpu().numpy() for d in (direct, loaded)]
+    np.testing.assert_array_equal(gens[0], gens[1])
+    np.testing.assert_array_equal(direct.logits.cpu().numpy(), loaded.logits.cpu().numpy())
+    del direct, loaded
+
+
 # ---------------------------------------------------------------------------
 # config 4: BERT-base
 # ---------------------------------------------------------------------------

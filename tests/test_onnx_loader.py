@@ -1,5 +1,5 @@
 """Load-time prepack: the ONNX protobuf reader (onnx_runtime_dart_b200/
-onnx_model.py) on models written by tests/onnx_writer.py. CPU tests check the
+onnx_model.py) on models written by onnx_runtime_dart_b200/onnx_writer.py. CPU tests check the
 tensor decoding rules of the reference's tensorFromProto
 (lib/src/onnx_proto_loader.dart:171-299) and external data; the GPU tests
 check that load-time packing, with and without the on-disk cache, gives the
@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 
 from onnx_runtime_dart_b200 import onnx_model as om
-from tests import onnx_writer as W
+from onnx_runtime_dart_b200 import onnx_writer as W
 
 
 def _write(tmp_path, name, nodes, inits, inputs, outputs, extra=None):
