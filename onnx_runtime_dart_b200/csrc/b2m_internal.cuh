@@ -45,6 +45,7 @@ void b2m_set_last_error(const std::string &msg);
 #define B2M_DEVERR_INDEX 4       // gather id / rotary position outside its table
 #define B2M_DEVERR_CACHE_FULL 5  // KV-cache append past its capacity
 
+#define B2M_ATTN_COUNTERS 65536
 // Device state block of a context: error word, counters (runtime.cu).
 #define B2M_DEV_STATE_BYTES 256
 
@@ -76,6 +77,9 @@ struct b2m_ctx {
   // Attention numerics (b2m_set_attention_mode): fp32 CUDA-core kernels and
   // no key splits when set.
   bool attn_exact = false;
+  // Split-merge counters of the decode attention (launch_gqa), zeroed at
+  // allocation and re-armed by the kernel; B2M_ATTN_COUNTERS words.
+  uint32_t *attn_counters = nullptr;
   // Declared successors (b2m_weight_set_next): the weight whose call follows
   // each weight's call; its kernels prefetch the successor into L2.
   std::unordered_map<const b2m_weight *, const b2m_weight *> next_of;
@@ -326,7 +330,13 @@ struct NbitsArgs {
   int64_t M = 0, K = 0, N = 0;
   int32_t *dev_err = nullptr;
   PrefetchPlan pf;
+  // SwiGLU input (decode GEMV only): A is the gate and up the up projection,
+  // both with row stride gu_rs, and the activation is silu(gate) * up.
+  const float *up = nullptr;
+  int64_t gu_rs = 0;
 };
+// Whether the decode GEMV takes an m-row SwiGLU call of w directly.
+bool nbits_swiglu_gemv(const NbitsWeight &w, int64_t M);
 bool nbits_smallm_supported(const NbitsWeight &w, int64_t M);
 // Builds w.drec from bq / scales / zero points when the weight qualifies.
 void nbits_build_drec(NbitsWeight &w, cudaStream_t s);
@@ -346,8 +356,11 @@ void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s);
 void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s);
 
 // Transformer glue (k_glue.cu)
+// gamma_rs > 0: row i of a group of `per` rows uses gains gamma + i * gamma_rs
+// (per-head gains, e.g. the q and k norms of one packed projection in one
+// launch); 0: every row uses gamma.
 void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
-                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s);
+                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs = 0);
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                       float *sum_out, int64_t rows, int D, double eps, cudaStream_t s);
 void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
@@ -367,7 +380,10 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP);
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, bool exact, cudaStream_t s);
+                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s);
+// `counters` (B * KVH zeroed words, or null): the last split CTA of each (kv
+// head, sequence) merges the key splits itself, instead of a separate
+// combine launch; the words are zero again when the call completes.
 // `exact`: the fp32 CUDA-core attention kernels only (no bf16-split tensor-core
 // kernels); with nsplit = 1 every sequence's result is independent of the batch.
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
@@ -407,6 +423,8 @@ struct I8GemmArgs {
   void *Yq = nullptr;      // QLinearMatMul (uint8 or int8)
   int requant = 0;
   double mult = 0.0;
+  // L2 prefetch of the declared next call's weight (b2m_weight_set_next).
+  PrefetchPlan pf;
   int32_t y_zp = 0, lo = 0, hi = 0;
   int32_t *dev_err = nullptr;
   // Scratch for the tensor-core path's activation row sums (M int32), used

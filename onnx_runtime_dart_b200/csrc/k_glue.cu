@@ -53,11 +53,12 @@ __device__ __forceinline__ void norm_load(const float *xr, const float *sr, int 
 template <int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *skip, const float *__restrict__ gamma,
                                                       float *y, float *sum_out, int64_t rows, int D, double eps,
-                                                      int64_t per, int64_t gstride) {
+                                                      int64_t per, int64_t gstride, int64_t gamma_rs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
   const int64_t off = (r / per) * gstride + (r % per) * D;
+  const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
   float v[VPL];
   norm_load<VPL>(x + off, skip ? skip + off : nullptr, D, lane, v);
   float ss = 0.f;
@@ -70,7 +71,7 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const floa
     const int j = lane + 32 * i;
     if (j < D) {
       if (sum_out) sum_out[off + j] = v[i];
-      y[off + j] = v[i] * inv * gamma[j];
+      y[off + j] = v[i] * inv * gm[j];
     }
   }
 }
@@ -114,11 +115,12 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
                                                          const float *__restrict__ gamma,
                                                          const float *__restrict__ beta, float *y, float *sum_out,
                                                          int64_t rows, int D, double eps, int64_t per,
-                                                         int64_t gstride) {
+                                                         int64_t gstride, int64_t gamma_rs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
   const int64_t off = (r / per) * gstride + (r % per) * D;
+  const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
   const int d4 = D >> 2;
   const float4 *xr = reinterpret_cast<const float4 *>(x + off);
   const float4 *sr = skip ? reinterpret_cast<const float4 *>(skip + off) : nullptr;
@@ -150,7 +152,7 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
       s2 = fmaf(a, a, fmaf(b, b, fmaf(c, c, fmaf(d, d, s2))));
     }
   const float inv = (float)(1.0 / sqrt((double)warp_sum_f(s2) / D + eps));
-  const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+  const float4 *g4 = reinterpret_cast<const float4 *>(gm);
   const float4 *b4 = beta ? reinterpret_cast<const float4 *>(beta) : nullptr;
 #pragma unroll
   for (int i = 0; i < V4; i++) {
@@ -176,9 +178,10 @@ template <int NV4, bool LN>
 __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const float *skip,
                                                            const float *__restrict__ gamma,
                                                            const float *__restrict__ beta, float *y, float *sum_out,
-                                                           int D, double eps, int64_t per, int64_t gstride) {
+                                                           int D, double eps, int64_t per, int64_t gstride, int64_t gamma_rs) {
   const int64_t r = blockIdx.x;
   const int64_t off = (r / per) * gstride + (r % per) * D;
+  const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
   const int d4 = D >> 2, tid = threadIdx.x, nt = blockDim.x;
   const float4 *xr = reinterpret_cast<const float4 *>(x + off);
   const float4 *sr = skip ? reinterpret_cast<const float4 *>(skip + off) : nullptr;
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
       s2 = fmaf(a, a, fmaf(b, b, fmaf(c, c, fmaf(d, d, s2))));
     }
   const float inv = (float)(1.0 / sqrt((double)block_sum(s2) / D + eps));
-  const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+  const float4 *g4 = reinterpret_cast<const float4 *>(gm);
   const float4 *b4 = beta ? reinterpret_cast<const float4 *>(beta) : nullptr;
 #pragma unroll
   for (int i = 0; i < NV4; i++) {
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
 template <bool LN>
 bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                           float *sum_out, int64_t rows, int D, double eps, int64_t per, int64_t gstride,
-                          cudaStream_t s) {
+                          int64_t gamma_rs, cudaStream_t s) {
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (D % 4 || gstride % 4 || D > 4096 || !al(x) || !al(skip) || !al(gamma) || !al(beta) || !al(y) ||
       !al(sum_out))
@@ -251,7 +254,8 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
     const unsigned g = (unsigned)((rows + 7) / 8);
     const int v4 = (D / 4 + 31) / 32;
 #define B2M_NW4(N) \
-  norm_warp4_kernel<N, LN><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps, per, gstride)
+  norm_warp4_kernel<N, LN><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps, per, gstride, \
+                                              gamma_rs)
     if (v4 <= 1) B2M_NW4(1);
     else if (v4 <= 2) B2M_NW4(2);
     else if (v4 <= 4) B2M_NW4(4);
@@ -267,7 +271,8 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
   const int nt = std::min(256, (d4 + 31) / 32 * 32);
   const int nv4 = (d4 + nt - 1) / nt;
   const unsigned g = (unsigned)rows;
-#define B2M_NRC(N) norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride)
+#define B2M_NRC(N) \
+  norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride, gamma_rs)
   if (nv4 <= 1) B2M_NRC(1);
   else if (nv4 <= 2) B2M_NRC(2);
   else B2M_NRC(4);
@@ -280,11 +285,12 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
 __global__ void __launch_bounds__(256) rmsnorm_long_kernel(const float *x, const float *skip,
                                                            const float *__restrict__ gamma, float *y, float *sum_out,
                                                            int64_t rows, int D, double eps, int64_t per,
-                                                           int64_t gstride) {
+                                                           int64_t gstride, int64_t gamma_rs) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
   const int64_t off = (r / per) * gstride + (r % per) * D;
+  const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
   const float *xr = x + off;
   const float *sr = skip ? skip + off : nullptr;
   float ss = 0.f;
@@ -296,7 +302,7 @@ __global__ void __launch_bounds__(256) rmsnorm_long_kernel(const float *x, const
   for (int j = lane; j < D; j += 32) {
     const float v = sr ? xr[j] + sr[j] : xr[j];
     if (sum_out) sum_out[off + j] = v;
-    y[off + j] = v * inv * gamma[j];
+    y[off + j] = v * inv * gm[j];
   }
 }
 
@@ -327,7 +333,7 @@ __global__ void __launch_bounds__(256) layernorm_long_kernel(const float *x, con
 
 // y = silu(gate) * up, with gate / up either separate tensors or the two
 // halves of one [rows][2*D] tensor (a packed gate|up projection).
-__device__ __forceinline__ float silu_times(float g, float u) { return g / (1.f + expf(-g)) * u; }
+using b2m::silu_times;
 
 // Rows over blockIdx.y, columns over x (float4 when VEC: D, both row strides
 // and the three pointers 16-byte aligned); no per-element index division.
@@ -798,7 +804,8 @@ __device__ __forceinline__ void warp_allreduce8(float (&v)[8]) {
 // warp states merge in shared memory in fixed order; with key splits the
 // split states go to pm / pl / po and gqa_decode_combine_kernel merges them.
 template <int D, int G>
-__global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float *pm, float *pl, float *po) {
+__global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float *pm, float *pl, float *po,
+                                                         uint32_t *counters) {
   constexpr int VPD = D / 32, KB = 8 / G;
   static_assert(D % 32 == 0 && D <= 128 && KB * G == 8, "decode kernel shape");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -937,6 +944,35 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
         pl[slot] = L;
       }
       po[slot * D + d] = O;
+    }
+  }
+  if (nsplit > 1 && counters) {
+    // The last split CTA of this (kv head, sequence) to finish merges the
+    // split states in split order, exactly as gqa_decode_combine_kernel does,
+    // and re-arms the counter for the next call (calls are stream-ordered).
+    __shared__ int last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&counters[(int64_t)b * a.KVH + kvh], 1u) == (uint32_t)(nsplit - 1);
+    __syncthreads();
+    if (last) {
+      __threadfence();
+      for (int i = threadIdx.x; i < G * D; i += 256) {
+        const int g = i / D, d = i % D;
+        const int h = kvh * G + g;
+        const int64_t base = ((int64_t)b * a.H + h) * nsplit;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, __ldcg(pm + base + s2));
+        float L = 0.f, O = 0.f;
+        for (int s2 = 0; s2 < nsplit; s2++) {
+          const float mv = __ldcg(pm + base + s2);
+          const float f = mv == -INFINITY ? 0.f : __expf(mv - M);
+          L += __ldcg(pl + base + s2) * f;
+          O += __ldcg(po + (base + s2) * D + d) * f;
+        }
+        a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = O / L;
+      }
+      if (threadIdx.x == 0) counters[(int64_t)b * a.KVH + kvh] = 0u;
     }
   }
 }
@@ -1521,19 +1557,21 @@ unsigned grid_for(int64_t n, int block) {
 }  // namespace
 
 void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
-                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s) {
+                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs) {
   if (rows <= 0) return;
-  if (launch_norm_rows_cta<false>(x, skip, gamma, nullptr, y, sum_out, rows, D, eps, per, gstride, s)) return;
+  if (launch_norm_rows_cta<false>(x, skip, gamma, nullptr, y, sum_out, rows, D, eps, per, gstride, gamma_rs, s))
+    return;
   const unsigned g = (unsigned)((rows + 7) / 8);
   const int vpl = (D + 31) / 32;
-#define B2M_RMS(V) rmsnorm_kernel<V><<<g, 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride)
+#define B2M_RMS(V) \
+  rmsnorm_kernel<V><<<g, 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride, gamma_rs)
   if (vpl <= 4) B2M_RMS(4);
   else if (vpl <= 8) B2M_RMS(8);
   else if (vpl <= 16) B2M_RMS(16);
   else if (vpl <= 24) B2M_RMS(24);
   else if (vpl <= 32) B2M_RMS(32);
   else if (vpl <= 64) B2M_RMS(64);
-  else rmsnorm_long_kernel<<<g, 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride);
+  else rmsnorm_long_kernel<<<g, 256, 0, s>>>(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride, gamma_rs);
 #undef B2M_RMS
   B2M_CUDA(cudaGetLastError());
 }
@@ -1541,7 +1579,7 @@ void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                       float *sum_out, int64_t rows, int D, double eps, cudaStream_t s) {
   if (rows <= 0) return;
-  if (launch_norm_rows_cta<true>(x, skip, gamma, beta, y, sum_out, rows, D, eps, rows, 0, s)) return;
+  if (launch_norm_rows_cta<true>(x, skip, gamma, beta, y, sum_out, rows, D, eps, rows, 0, 0, s)) return;
   const unsigned g = (unsigned)((rows + 7) / 8);
   const int vpl = (D + 31) / 32;
 #define B2M_LN(V) layernorm_kernel<V><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps)
@@ -1631,7 +1669,8 @@ static bool fa_tc_shape(const GqaArgs &a) {
          al(a.q) && al(a.kcache) && al(a.vcache) && al(a.out) && (a.rot == 0 || !a.cos || a.rot <= a.D);
 }
 
-static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool exact, cudaStream_t s) {
+static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool exact, uint32_t *counters,
+                          cudaStream_t s) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
   if (decode_shape(a)) {
@@ -1640,14 +1679,14 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
     const int64_t slots = (int64_t)a.B * a.H * nsplit;
     float *pm = split_part, *pl = pm ? pm + slots : nullptr, *po = pm ? pl + slots : nullptr;
 #define B2M_DEC(DD, GG) \
-  if (D == DD && G == GG) gqa_decode_kernel<DD, GG><<<grid, 256, 0, s>>>(a, pm, pl, po);
+  if (D == DD && G == GG) gqa_decode_kernel<DD, GG><<<grid, 256, 0, s>>>(a, pm, pl, po, nsplit > 1 ? counters : nullptr);
     B2M_DEC(32, 1) B2M_DEC(32, 2) B2M_DEC(32, 4) B2M_DEC(32, 8)
     B2M_DEC(64, 1) B2M_DEC(64, 2) B2M_DEC(64, 4) B2M_DEC(64, 8)
     B2M_DEC(96, 1) B2M_DEC(96, 2) B2M_DEC(96, 4) B2M_DEC(96, 8)
     B2M_DEC(128, 1) B2M_DEC(128, 2) B2M_DEC(128, 4) B2M_DEC(128, 8)
 #undef B2M_DEC
     B2M_CUDA(cudaGetLastError());
-    if (nsplit > 1) {
+    if (nsplit > 1 && !counters) {
       gqa_decode_combine_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, 0, s>>>(pm, pl, po, a.out, a.H, D, nsplit);
     }
   } else if (!exact && fa_tc_shape(a)) {
@@ -1702,7 +1741,7 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP) {
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, bool exact, cudaStream_t s) {
+                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s) {
   GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
             B, S, H, KVH, D, CAP, scale, err};
   a.kc_rs = D;
@@ -1715,7 +1754,7 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
   const int64_t items = (int64_t)B * S * KVH;
   gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
   B2M_CUDA(cudaGetLastError());
-  launch_attend(a, split_part, nsplit, exact, s);
+  launch_attend(a, split_part, nsplit, exact, counters, s);
 }
 
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
@@ -1732,7 +1771,7 @@ void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, in
   a.mask_bs = mask_bs;
   a.mask_hs = mask_hs;
   a.mask_qs = mask_qs;
-  launch_attend(a, nullptr, 1, exact, s);
+  launch_attend(a, nullptr, 1, exact, nullptr, s);
 }
 
 void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,

@@ -334,17 +334,20 @@ __global__ void __launch_bounds__(256) i8_rowsum_kernel(const uint8_t *__restric
 // activation rows sit in shared memory (read as broadcast words).
 constexpr int GV_THREADS = 256;
 
-template <bool AS, bool WS, bool REQ>
+// MM: the largest row count this instantiation serves (1 for single-row
+// decode, I8_GEMV_MAX_M otherwise), so the per-row loops unroll exactly.
+template <bool AS, bool WS, bool REQ, int MM>
 __global__ void __launch_bounds__(GV_THREADS)
     i8_gemv_kernel(const uint4 *__restrict__ ts8, const int32_t *__restrict__ colsum, const uint8_t *__restrict__ A,
-                   const I8Epi e, int M, int N, int K, int K128, int nchunks) {
+                   const I8Epi e, int M, int N, int K, int K128, int nchunks, const PrefetchPlan pf) {
   extern __shared__ uint8_t gsm[];
   uint32_t *a_s = reinterpret_cast<uint32_t *>(gsm);                   // [M][K128/4]
   int *part = reinterpret_cast<int *>(gsm + (size_t)M * K128);         // [8 warps][M][32]
   int *rows = part + 8 * M * 32;                                      // [M]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile = blockIdx.x >> 2, qc = blockIdx.x & 3;
-  pdl_launch_dependents();
+  // The declared next call's weights go to L2 first.
+  if (threadIdx.x == 0 && pf.seg[0]) prefetch_share(pf, blockIdx.x);
   // Weight loads do not depend on earlier kernels: issue the first chunk now.
   const uint4 *wcol = ts8 + (size_t)tile * nchunks * 8 * 128 + qc * 32 + lane;
   uint4 wr[8];
@@ -352,6 +355,10 @@ __global__ void __launch_bounds__(GV_THREADS)
 #pragma unroll
     for (int pl = 0; pl < 8; pl++) wr[pl] = __ldg(wcol + (size_t)warp * 8 * 128 + pl * 128);
   }
+  // Trigger the next kernel once this warp's weights have arrived (as the int4
+  // decode GEMV does; triggering at entry lets later grids crowd the SMs).
+  asm volatile("" ::"r"(wr[0].x), "r"(wr[7].w));
+  pdl_launch_dependents();
   pdl_wait();
   const int kw = K128 >> 2;
   for (int i = threadIdx.x; i < M * kw; i += GV_THREADS) {
@@ -377,9 +384,9 @@ __global__ void __launch_bounds__(GV_THREADS)
       if (lane == 0) rows[m] = acc;
     }
   }
-  int acc[I8_GEMV_MAX_M];
+  int acc[MM];
 #pragma unroll
-  for (int m = 0; m < I8_GEMV_MAX_M; m++) acc[m] = 0;
+  for (int m = 0; m < MM; m++) acc[m] = 0;
   for (int ch = warp; ch < nchunks; ch += 8) {
     uint4 nx[8];
     const bool more = ch + 8 < nchunks;
@@ -389,7 +396,7 @@ __global__ void __launch_bounds__(GV_THREADS)
     }
     const uint32_t *wv = reinterpret_cast<const uint32_t *>(wr);
 #pragma unroll
-    for (int m = 0; m < I8_GEMV_MAX_M; m++) {
+    for (int m = 0; m < MM; m++) {
       if (m < M) {
         const uint32_t *ar = a_s + m * kw + ch * 32;
 #pragma unroll
@@ -402,7 +409,7 @@ __global__ void __launch_bounds__(GV_THREADS)
     }
   }
 #pragma unroll
-  for (int m = 0; m < I8_GEMV_MAX_M; m++)
+  for (int m = 0; m < MM; m++)
     if (m < M) part[(warp * M + m) * 32 + lane] = acc[m];
   __syncthreads();
   for (int i = threadIdx.x; i < M * 32; i += GV_THREADS) {
@@ -490,11 +497,13 @@ void launch_ts_bt(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaSt
   }
 }
 
-template <bool AS, bool WS, bool REQ>
-void launch_gemv(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaStream_t s) {
+template <bool AS, bool WS, bool REQ, int MM>
+void launch_gemv_m(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaStream_t s) {
   const size_t smem = (size_t)a.M * w.k128 + (size_t)8 * a.M * 32 * 4 + (size_t)a.M * 4;
-  auto kern = i8_gemv_kernel<AS, WS, REQ>;
-  set_smem_limit_once<i8_gemv_kernel<AS, WS, REQ>>(232448);
+  auto kern = i8_gemv_kernel<AS, WS, REQ, MM>;
+  set_smem_limit_once<i8_gemv_kernel<AS, WS, REQ, MM>>(232448);
+  PrefetchPlan pf = a.pf;
+  pf.set_grid(w.npad / 128 * 4);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(w.npad / 128 * 4));
   cfg.blockDim = dim3(GV_THREADS);
@@ -507,7 +516,15 @@ void launch_gemv(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaStr
   cfg.numAttrs = 1;
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, reinterpret_cast<const uint4 *>(w.ts8), (const int32_t *)w.colsum,
                               reinterpret_cast<const uint8_t *>(a.A), e, (int)a.M, (int)a.N, (int)a.K, (int)w.k128,
-                              (int)(w.k128 / 128)));
+                              (int)(w.k128 / 128), pf));
+}
+
+template <bool AS, bool WS, bool REQ>
+void launch_gemv(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaStream_t s) {
+  if (a.M == 1)
+    launch_gemv_m<AS, WS, REQ, 1>(a, w, e, s);
+  else
+    launch_gemv_m<AS, WS, REQ, I8_GEMV_MAX_M>(a, w, e, s);
 }
 
 template <bool REQ>

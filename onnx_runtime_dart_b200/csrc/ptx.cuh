@@ -111,6 +111,10 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// silu(g) * u in float, the arithmetic of the SiLU*Mul glue op; the decode
+// GEMV's fused SwiGLU load uses the same function, so both give the same bits.
+__device__ __forceinline__ float silu_times(float g, float u) { return g / (1.f + expf(-g)) * u; }
+
 // Hint: bring [src, src + bytes) into L2 (16-byte aligned address, size a
 // multiple of 16).
 __device__ __forceinline__ void bulk_prefetch_l2(const void *src, uint32_t bytes) {

@@ -525,6 +525,13 @@ void integer_impl(b2m_ctx *ctx, const b2m_tensor *a, const b2m_tensor *b, const 
   if (bw && batch == 1) {
     Scratch rs(ctx, (size_t)m * 4 + 256);
     p.rowsum = static_cast<int32_t *>(rs.take((size_t)m * 4));
+    // The declared next call's packed int8 weight goes to L2 (its ts8 layout,
+    // which both int8 kernels read).
+    const auto it = ctx->next_of.find(bw);
+    if (it != ctx->next_of.end() && it->second && it->second->kind == W_I8 && it->second->i8.ts8) {
+      p.pf.seg[0] = it->second->i8.ts8;
+      p.pf.bytes[0] = it->second->i8.npad * it->second->i8.k128;
+    }
     done = launch_i8_tc(p, bw->i8, ctx->stream);
   }
   if (!done) launch_i8_gemm(p, ctx->stream);
@@ -781,6 +788,7 @@ B2M_API b2m_status b2m_shutdown(b2m_ctx *ctx) {
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
     cudaFree(ctx->dev_err);
+    cudaFree(ctx->attn_counters);
     cudaEventDestroy(ctx->ev0);
     cudaEventDestroy(ctx->ev1);
     cudaStreamDestroy(ctx->own_stream);
@@ -1517,6 +1525,48 @@ B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m,
   });
 }
 
+B2M_API b2m_status b2m_matmul_nbits_swiglu_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gu_rs,
+                                               int64_t m, const b2m_weight *w, const float *bias, int32_t mode,
+                                               float *y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+    B2M_REQUIRE(m >= 0 && gu_rs >= w->k && (m == 0 || (gate && up && y)), B2M_ERR_INVALID_ARGUMENT,
+                "MatMulNBits SwiGLU: bad pointers or row stride");
+    B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST || mode == B2M_MODE_PRECISE,
+                B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad mode");
+    check_cancel(ctx);
+    if (m == 0) return;
+    OpTimer timer(ctx);
+    const bool gemv = mode == B2M_MODE_FAST ? nbits_use_smallm(w->nb, m, w->k, w->n)
+                                            : mode == B2M_MODE_PRECISE && nbits_precise_gemv(w->nb, m);
+    if (gemv && nbits_swiglu_gemv(w->nb, m)) {
+      // The GEMV forms silu(gate) * up in its activation load.
+      NbitsArgs p;
+      p.A = gate;
+      p.up = up;
+      p.gu_rs = gu_rs;
+      p.w = &w->nb;
+      p.bias = bias;
+      p.Y = y;
+      p.M = m;
+      p.K = w->k;
+      p.N = w->n;
+      p.dev_err = ctx->dev_err;
+      nbits_prefetch_plan(ctx, w, m, mode, p);
+      launch_nbits_smallm(p, ctx->stream, ctx->pdl);
+    } else {
+      const size_t abytes = (size_t)(m * w->k * 4);
+      Scratch sc(ctx, abytes + 256 + nbits_scratch_bytes(w, m, mode));
+      float *act = static_cast<float *>(sc.take(abytes));
+      launch_silu_mul(gate, up, gu_rs, gu_rs, act, m, w->k, ctx->stream);
+      nbits_run(ctx, sc, act, m, w, bias, mode, y);
+    }
+    timer.done();
+  });
+}
+
 B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int64_t m, const b2m_weight *w,
                                          const float *bias_host, int32_t mode, float *y_host) {
   return guarded([&] {
@@ -1571,6 +1621,20 @@ B2M_API b2m_status b2m_rmsnorm_heads_dev(b2m_ctx *ctx, const float *x, const flo
     DeviceGuard dg(ctx->device);
     launch_rmsnorm(x, nullptr, gamma, y, nullptr, tokens * heads, (int)head_dim, eps, heads, token_stride,
                    ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_rmsnorm_head_rows_dev(b2m_ctx *ctx, const float *x, const float *gamma_rows, float *y,
+                                             int64_t tokens, int64_t heads, int64_t head_dim, int64_t token_stride,
+                                             double eps) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(tokens >= 0 && heads > 0 && head_dim > 0 && head_dim <= (1 << 24) &&
+                    token_stride >= heads * head_dim && (tokens == 0 || (x && gamma_rows && y)),
+                B2M_ERR_INVALID_ARGUMENT, "RMSNorm head rows: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_rmsnorm(x, nullptr, gamma_rows, y, nullptr, tokens * heads, (int)head_dim, eps, heads, token_stride,
+                   ctx->stream, head_dim);
   });
 }
 
@@ -1666,9 +1730,23 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
     float *part = nullptr;
     Scratch scr(ctx, nsplit > 1 ? (size_t)b * h * nsplit * (2 + head_dim) * 4 + 256 : 0);
     if (nsplit > 1) part = static_cast<float *>(scr.take((size_t)b * h * nsplit * (2 + head_dim) * 4));
+    uint32_t *counters = nullptr;
+    if (nsplit > 1 && (int64_t)b * kvh <= B2M_ATTN_COUNTERS) {
+      if (!ctx->attn_counters) {
+        // Made once, outside any stream capture (a call under capture without
+        // them keeps the separate merge launch).
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        B2M_CUDA(cudaStreamIsCapturing(ctx->stream, &cs));
+        if (cs == cudaStreamCaptureStatusNone) {
+          B2M_CUDA(cudaMalloc(&ctx->attn_counters, B2M_ATTN_COUNTERS * sizeof(uint32_t)));
+          B2M_CUDA(cudaMemsetAsync(ctx->attn_counters, 0, B2M_ATTN_COUNTERS * sizeof(uint32_t), ctx->stream));
+        }
+      }
+      counters = ctx->attn_counters;
+    }
     launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
                interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit,
-               ctx->attn_exact, ctx->stream);
+               ctx->attn_exact, counters, ctx->stream);
   });
 }
 

@@ -299,6 +299,7 @@ class Int4Decoder:
                 lw[name] = torch.from_numpy(g).to(dev)
                 if keep_host:
                     self.host[(li, name)] = g
+            lw["qk_gain"] = self._qk_gain(lw)
             self.layers.append(lw)
         # The projections in call order, each declared as the successor of the
         # one before (the last layer's down projection is followed by the
@@ -320,6 +321,13 @@ class Int4Decoder:
             self.host["lm_head"] = lm
         del lm
 
+    def _qk_gain(self, lw):
+        """[heads + kv_heads][head_dim] gains: the q norm's for every query head,
+        then the k norm's for every kv head (one launch normalises both)."""
+        c = self.cfg
+        return self.torch.cat([lw["q_norm"].reshape(1, -1).repeat(c.heads, 1),
+                               lw["k_norm"].reshape(1, -1).repeat(c.kv_heads, 1)]).contiguous()
+
     def _session_weights(self, sess):
         """The weights of an exported model: the MatMulNBits initializers
         packed by prepack_session (looked up under the dispatch's keys), the
@@ -332,6 +340,7 @@ class Int4Decoder:
         for li in range(c.layers):
             lw = {name: t(f"layers.{li}.{name}.weight") for name in ("attn_norm", "mlp_norm", "q_norm", "k_norm")}
             lw["nodes"] = sess.layer_nodes[li]
+            lw["qk_gain"] = self._qk_gain(lw)
             self.layers.append(lw)
         self.final_norm = t("norm.weight")
         self.emb = t("embed_tokens.weight")
@@ -377,10 +386,14 @@ class Int4Decoder:
                                                      _ptr(getattr(self, part))))
                 qp, kp, vp = self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()
                 q_rs, kv_rs = c.heads * D, c.kv_heads * D
-            chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qp), _ptr(lw["q_norm"]), ctypes.c_void_p(qp), T,
-                                          c.heads, D, q_rs, c.eps))
-            chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(kp), _ptr(lw["k_norm"]), ctypes.c_void_p(kp), T,
-                                          c.kv_heads, D, kv_rs, c.eps))
+            if self.fused:  # q and k heads are adjacent in the packed rows: one launch
+                chk(lib.b2m_rmsnorm_head_rows_dev(h, ctypes.c_void_p(qp), _ptr(lw["qk_gain"]), ctypes.c_void_p(qp), T,
+                                                  c.heads + c.kv_heads, D, q_rs, c.eps))
+            else:
+                chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qp), _ptr(lw["q_norm"]), ctypes.c_void_p(qp), T,
+                                              c.heads, D, q_rs, c.eps))
+                chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(kp), _ptr(lw["k_norm"]), ctypes.c_void_p(kp), T,
+                                              c.kv_heads, D, kv_rs, c.eps))
             chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
                                 _ptr(self.kcache[li]),
                                 _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D, 0,
@@ -403,13 +416,13 @@ class Int4Decoder:
                         chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
                                                      _ptr(getattr(self, part))))
                 gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
-            chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
-                                     c.inter))
-            if self.session is not None:
+            if self.session is not None:  # the export's Sigmoid / Mul / Mul nodes, then its down MatMulNBits
+                chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
+                                         c.inter))
                 self._dispatch_proj("down", lw, self.act, T, self.down)
-            else:
-                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
-                                             _ptr(self.down)))
+            else:  # SwiGLU formed in the down projection's activation load where the GEMV serves it
+                chk(lib.b2m_matmul_nbits_swiglu_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, T,
+                                                    lw["down"].handle, None, self.mode, _ptr(self.down)))
         chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(self.final_norm), _ptr(self.h),
                                 _ptr(self.res), T, H, c.eps))
         idx = self.last_idx.get(seq)
