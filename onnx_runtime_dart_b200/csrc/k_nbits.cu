@@ -640,7 +640,10 @@ void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   }
 }
 
-bool nbits_swiglu_gemv(const NbitsWeight &w, int64_t M) { return w.drec && nbits_smallm_supported(w, M); }
+// The fused load reads gate and up rows: twice the activation bytes of every
+// CTA. Measured in the decode chain, that loses to a separate SiLU*Mul launch
+// from 8 rows on.
+bool nbits_swiglu_gemv(const NbitsWeight &w, int64_t M) { return w.drec && M <= 4 && nbits_smallm_supported(w, M); }
 
 void nbits_build_drec(NbitsWeight &w, cudaStream_t s) {
   if (w.drec || w.block < 32 || w.zp_kind == 2 || !w.bq) return;
