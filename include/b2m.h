@@ -256,18 +256,6 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
 B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m, const b2m_weight *w,
                                         const float *bias, int32_t mode, float *y);
 
-/* MatMulNBits of the SwiGLU activation: Y = (silu(gate) * up) . dequant(W)^T
- * (+ bias), gate and up m x K floats with row stride gu_rs (the two halves of
- * a packed gate|up projection, or two tensors), the decoder's down
- * projection. The reference runs Sigmoid, Mul, Mul and MatMulNBits as
- * separate nodes (onnx_ops.dart, onnx_qlinear_ops.dart:115-228); results are
- * the same bits as b2m_silu_mul_dev followed by b2m_matmul_nbits_dev. Where
- * the decode GEMV serves the call it forms the activation in its load (one
- * launch); otherwise the two steps run back to back. */
-B2M_API b2m_status b2m_matmul_nbits_swiglu_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gu_rs,
-                                               int64_t m, const b2m_weight *w, const float *bias, int32_t mode,
-                                               float *y);
-
 /* Allocation-free MatMulNBits. No counterpart in the reference: this entry
  * point exists for callers that must not allocate device memory while they
  * run an operator — a host application that has handed all device memory to

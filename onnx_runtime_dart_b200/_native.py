@@ -114,7 +114,6 @@ SIGNATURES = {
     "b2m_set_attention_mode": (_i32, [_c_ctx, _i32]),
     "b2m_weight_set_next": (_i32, [_c_weight, _c_weight]),
     "b2m_rmsnorm_head_rows_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_double]),
-    "b2m_matmul_nbits_swiglu_dev": (_i32, [_c_ctx, _vp, _vp, _i64, _i64, _c_weight, _vp, _i32, _vp]),
     "b2m_enable_timing": (_i32, [_c_ctx, _i32]),
     "b2m_last_kernel_ms": (_i32, [_c_ctx, ctypes.POINTER(_f32)]),
     "b2m_tensor_alloc": (_i32, [_c_ctx, _i32, _i64p, _i32, ctypes.POINTER(_c_tensor)]),

@@ -66,9 +66,13 @@ struct b2m_ctx {
   // operands). Stream-ordered: reused by the next op on the same stream.
   void *scratch = nullptr;
   size_t scratch_bytes = 0;
-  // Device word that kernels with bounded spin-waits set on timeout.
+  // The error word that kernels with bounded spin-waits (and index checks)
+  // set: mapped pinned host memory, so a synchronising call reads it with a
+  // plain load instead of a device-to-host copy. dev_err is its device
+  // address, err_host its host address.
   int32_t *dev_err = nullptr;
-  // Self-resetting device counter (zero between calls) in the same block,
+  int32_t *err_host = nullptr;
+  // Self-resetting device counters (zero between calls; B2M_DEV_STATE_BYTES),
   // used by DynamicQuantizeLinear.
   uint32_t *dev_counter = nullptr;
   // Programmatic dependent launch for the decode kernels (env
@@ -86,9 +90,6 @@ struct b2m_ctx {
   // Pinned staging for the host-buffer helpers.
   void *pinned = nullptr;
   size_t pinned_bytes = 0;
-  // Pinned copy of the device error word: a host-buffer call enqueues its
-  // read with the output copy and checks it after its one synchronisation.
-  int32_t *err_host = nullptr;
 };
 
 struct b2m_tensor {
@@ -330,13 +331,7 @@ struct NbitsArgs {
   int64_t M = 0, K = 0, N = 0;
   int32_t *dev_err = nullptr;
   PrefetchPlan pf;
-  // SwiGLU input (decode GEMV only): A is the gate and up the up projection,
-  // both with row stride gu_rs, and the activation is silu(gate) * up.
-  const float *up = nullptr;
-  int64_t gu_rs = 0;
 };
-// Whether the decode GEMV takes an m-row SwiGLU call of w directly.
-bool nbits_swiglu_gemv(const NbitsWeight &w, int64_t M);
 bool nbits_smallm_supported(const NbitsWeight &w, int64_t M);
 // Builds w.drec from bq / scales / zero points when the weight qualifies.
 void nbits_build_drec(NbitsWeight &w, cudaStream_t s);

@@ -379,7 +379,7 @@ __global__ void gather_rows_kernel(const float *__restrict__ table, const int64_
   if (r >= rows) return;
   const int64_t id = ids[r];
   const bool ok = id >= 0 && id < V;
-  if (!ok && threadIdx.x == 0 && err) atomicExch(err, B2M_DEVERR_INDEX);
+  if (!ok && threadIdx.x == 0 && err) b2m::set_dev_error(err, B2M_DEVERR_INDEX);
   for (int64_t j = threadIdx.x; j < D; j += blockDim.x) y[r * D + j] = ok ? table[id * D + j] : 0.f;
 }
 
@@ -510,7 +510,7 @@ __global__ void __launch_bounds__(256) rotary_kernel(const float *__restrict__ x
   if (p >= 0 && p < max_pos) {
     rotate_head(v, cos, sin, p, half, rot, interleaved, lane, 32);
   } else if (lane == 0 && err) {
-    atomicExch(err, B2M_DEVERR_INDEX);
+    b2m::set_dev_error(err, B2M_DEVERR_INDEX);
   }
   __syncwarp();
   float *dst = y + bs * y_rs + (int64_t)h * D;
@@ -554,7 +554,7 @@ __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
   const int past = a.past[b];
   const int pos = past + s;
   if (pos >= a.CAP) {
-    if (lane == 0 && a.err) atomicExch(a.err, B2M_DEVERR_CACHE_FULL);
+    if (lane == 0 && a.err) b2m::set_dev_error(a.err, B2M_DEVERR_CACHE_FULL);
     return;
   }
   __shared__ float kbuf[8][256];

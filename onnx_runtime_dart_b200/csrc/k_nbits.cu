@@ -70,17 +70,6 @@ __device__ __forceinline__ float4 load_act4(const float *A, int64_t M, int64_t K
   return v;
 }
 
-// The activation of a decode call: A's row r at k0..k0+3, or with SwiGLU
-// (p.up set) silu(gate) * up of the two rows of stride p.gu_rs.
-template <bool SWI, bool VEC>
-__device__ __forceinline__ float4 load_act(const NbitsArgs &p, int64_t r, int64_t k0) {
-  if (!SWI) return load_act4(p.A, p.M, p.K, r, k0, VEC);
-  const int64_t rs = p.gu_rs;
-  const float4 g = load_act4(p.A + (r < p.M ? r * (rs - p.K) : 0), p.M, p.K, r, k0, VEC);
-  const float4 u = load_act4(p.up + (r < p.M ? r * (rs - p.K) : 0), p.M, p.K, r, k0, VEC);
-  return make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z), silu_times(g.w, u.w));
-}
-
 // f16 hi + lo split of (x, y): hi = rn16(x), lo = rn16(x - hi).
 __device__ __forceinline__ void split_h2(float x, float y, uint32_t &hi, uint32_t &lo) {
   const __half2 h = __floats2half2_rn(x, y);
@@ -267,7 +256,7 @@ __global__ void __launch_bounds__(NW * 32) nbits_decode_kernel(const NbitsArgs p
 // (minBlocks 1 lets ptxas schedule the post-wait path with more registers:
 // 52 instead of 42 at MT = CPW = 1, 1.84 instead of 2.02 us per chained
 // launch; the occupancy itself measured the same either way.)
-template <int MT, int CPW, bool VEC, bool FIT, bool SWI>
+template <int MT, int CPW, bool VEC, bool FIT>
 __global__ void __launch_bounds__(DEC_WARPS * 32, 1) nbits_decode_rec_kernel(const NbitsArgs p, const uint8_t *drec,
                                                                             int nchunks) {
   constexpr int NW = DEC_WARPS;
@@ -330,7 +319,7 @@ __global__ void __launch_bounds__(DEC_WARPS * 32, 1) nbits_decode_rec_kernel(con
       for (int s = 0; s < 2; s++)
 #pragma unroll
         for (int mt = 0; mt < MT; mt++)
-          av[grp][s][mt] = load_act<SWI, VEC>(p, mt * 8 + g, c * 64 + grp * 32 + s * 16 + 4 * t);
+          av[grp][s][mt] = load_act4(p.A, p.M, p.K, mt * 8 + g, c * 64 + grp * 32 + s * 16 + 4 * t, VEC);
 #pragma unroll
     for (int grp = 0; grp < 2; grp++) {
       const float sa = grp ? s4[i].y : s4[i].x, sb = grp ? s4[i].w : s4[i].z;
@@ -549,7 +538,7 @@ void launch_decode_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, a, *a.w));
 }
 
-template <int MT, int CPW, bool VEC, bool FIT, bool SWI>
+template <int MT, int CPW, bool VEC, bool FIT>
 void launch_decode_rec_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   NbitsArgs p = a;
   const unsigned grid = (unsigned)((a.N + 15) / 16);
@@ -563,30 +552,19 @@ void launch_decode_rec_t(const NbitsArgs &a, cudaStream_t s, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  B2M_CUDA(cudaLaunchKernelEx(&cfg, nbits_decode_rec_kernel<MT, CPW, VEC, FIT, SWI>, p, (const uint8_t *)a.w->drec,
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, nbits_decode_rec_kernel<MT, CPW, VEC, FIT>, p, (const uint8_t *)a.w->drec,
                               (int)(a.w->kp / 64)));
-}
-
-template <int MT, int CPW, bool SWI>
-void launch_decode_rec_s(const NbitsArgs &a, cudaStream_t s, bool pdl) {
-  auto al = [](const void *q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  const bool vec = (a.K & 3) == 0 && al(a.A) && (!SWI || (al(a.up) && (a.gu_rs & 3) == 0));
-  const bool fit = a.w->kp / 64 == (int64_t)CPW * DEC_WARPS;
-  if (vec) {
-    fit ? launch_decode_rec_t<MT, CPW, true, true, SWI>(a, s, pdl)
-        : launch_decode_rec_t<MT, CPW, true, false, SWI>(a, s, pdl);
-  } else {
-    fit ? launch_decode_rec_t<MT, CPW, false, true, SWI>(a, s, pdl)
-        : launch_decode_rec_t<MT, CPW, false, false, SWI>(a, s, pdl);
-  }
 }
 
 template <int MT, int CPW>
 void launch_decode_rec(const NbitsArgs &a, cudaStream_t s, bool pdl) {
-  if (a.up)
-    launch_decode_rec_s<MT, CPW, true>(a, s, pdl);
-  else
-    launch_decode_rec_s<MT, CPW, false>(a, s, pdl);
+  const bool vec = (a.K & 3) == 0 && (reinterpret_cast<uintptr_t>(a.A) & 15) == 0;
+  const bool fit = a.w->kp / 64 == (int64_t)CPW * DEC_WARPS;
+  if (vec) {
+    fit ? launch_decode_rec_t<MT, CPW, true, true>(a, s, pdl) : launch_decode_rec_t<MT, CPW, true, false>(a, s, pdl);
+  } else {
+    fit ? launch_decode_rec_t<MT, CPW, false, true>(a, s, pdl) : launch_decode_rec_t<MT, CPW, false, false>(a, s, pdl);
+  }
 }
 
 template <int MT, int CPW>
@@ -639,11 +617,6 @@ void launch_nbits_smallm(const NbitsArgs &a, cudaStream_t s, bool pdl) {
     launch_decode_z<1, 4>(a, s, pdl);
   }
 }
-
-// The fused load reads gate and up rows: twice the activation bytes of every
-// CTA. Measured in the decode chain, that loses to a separate SiLU*Mul launch
-// from 8 rows on.
-bool nbits_swiglu_gemv(const NbitsWeight &w, int64_t M) { return w.drec && M <= 4 && nbits_smallm_supported(w, M); }
 
 void nbits_build_drec(NbitsWeight &w, cudaStream_t s) {
   if (w.drec || w.block < 32 || w.zp_kind == 2 || !w.bq) return;

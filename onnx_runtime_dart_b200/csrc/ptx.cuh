@@ -111,6 +111,14 @@ __device__ __forceinline__ void tma_store_2d(const void *tmap, const void *src, 
                "r"(smem_u32(src)), "r"(x), "r"(y)
                : "memory");
 }
+// Records `code` in the context's error word, which lives in mapped host
+// memory: a plain store, since device atomics on host memory are not
+// guaranteed across PCIe (every writer stores a nonzero code; any one of them
+// is enough for the host).
+__device__ __forceinline__ void set_dev_error(int32_t *err, int32_t code) {
+  *reinterpret_cast<volatile int32_t *>(err) = code;
+}
+
 // silu(g) * u in float, the arithmetic of the SiLU*Mul glue op; the decode
 // GEMV's fused SwiGLU load uses the same function, so both give the same bits.
 __device__ __forceinline__ float silu_times(float g, float u) { return g / (1.f + expf(-g)) * u; }

@@ -78,32 +78,35 @@ void check_cancel(b2m_ctx *ctx) {
   if (ctx->cancel_flag && *ctx->cancel_flag) b2m_throw(B2M_ERR_CANCELLED, "operation cancelled");
 }
 
-void check_device_error(b2m_ctx *ctx) {
-  // Bounded device waits report through ctx->dev_err; read it lazily when the
-  // host synchronises anyway.
-  int32_t e = 0;
-  B2M_CUDA(cudaMemcpyAsync(&e, ctx->dev_err, sizeof(e), cudaMemcpyDeviceToHost, ctx->stream));
-  B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+// Bounded device waits report through the mapped error word; a call that
+// has just synchronised the stream reads it with a plain host load.
+void raise_device_error(b2m_ctx *ctx) {
+  const int32_t e = *reinterpret_cast<volatile int32_t *>(ctx->err_host);
   if (e != B2M_DEVERR_NONE) {
+    *reinterpret_cast<volatile int32_t *>(ctx->err_host) = B2M_DEVERR_NONE;
     // An aborted kernel may leave counters mid-count: clear the whole block.
-    B2M_CUDA(cudaMemsetAsync(ctx->dev_err, 0, B2M_DEV_STATE_BYTES, ctx->stream));
+    B2M_CUDA(cudaMemsetAsync(ctx->dev_counter, 0, B2M_DEV_STATE_BYTES, ctx->stream));
+    if (e == B2M_DEVERR_INDEX)
+      b2m_throw(B2M_ERR_INVALID_ARGUMENT, "an index (a gather id or a rotary position) was outside its table");
+    if (e == B2M_DEVERR_CACHE_FULL) b2m_throw(B2M_ERR_INVALID_ARGUMENT, "a KV-cache append went past its capacity");
     b2m_throw(B2M_ERR_TIMEOUT, "a bounded device-side wait timed out (code " + std::to_string(e) + ")");
   }
 }
 
-// The same check for a caller that synchronises anyway: enqueue_error_read
-// before its cudaStreamSynchronize, raise_enqueued_error after it.
-void enqueue_error_read(b2m_ctx *ctx) {
-  B2M_CUDA(cudaMemcpyAsync(ctx->err_host, ctx->dev_err, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx->stream));
+void check_device_error(b2m_ctx *ctx) {
+  B2M_CUDA(cudaStreamSynchronize(ctx->stream));
+  raise_device_error(ctx);
 }
 
-void raise_enqueued_error(b2m_ctx *ctx) {
-  const int32_t e = *ctx->err_host;
-  if (e != B2M_DEVERR_NONE) {
-    B2M_CUDA(cudaMemsetAsync(ctx->dev_err, 0, B2M_DEV_STATE_BYTES, ctx->stream));
-    *ctx->err_host = B2M_DEVERR_NONE;
-    b2m_throw(B2M_ERR_TIMEOUT, "a bounded device-side wait timed out (code " + std::to_string(e) + ")");
+// The device address of a host buffer that kernels can write directly
+// (pinned or registered host memory), or nullptr for pageable memory.
+void *mapped_host_ptr(void *p) {
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, p) != cudaSuccess) {
+    (void)cudaGetLastError();
+    return nullptr;
   }
+  return at.type == cudaMemoryTypeHost ? at.devicePointer : nullptr;
 }
 
 b2m_tensor *new_tensor(b2m_ctx *ctx, int32_t dtype, const int64_t *shape, int32_t rank) {
@@ -763,13 +766,14 @@ B2M_API b2m_status b2m_init(int32_t device, b2m_ctx **out_ctx) {
     B2M_CUDA(cudaMemPoolSetAttribute(ctx->pool, cudaMemPoolAttrReleaseThreshold, &thr));
     B2M_CUDA(cudaEventCreate(&ctx->ev0));
     B2M_CUDA(cudaEventCreate(&ctx->ev1));
-    // One zeroed block: the error word, then counters that kernels reset
-    // themselves after use (the DynamicQuantizeLinear block counter).
-    B2M_CUDA(cudaMalloc(&ctx->dev_err, B2M_DEV_STATE_BYTES));
-    B2M_CUDA(cudaMemset(ctx->dev_err, 0, B2M_DEV_STATE_BYTES));
-    ctx->dev_counter = reinterpret_cast<uint32_t *>(reinterpret_cast<char *>(ctx->dev_err) + 128);
-    B2M_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&ctx->err_host), sizeof(int32_t), cudaHostAllocDefault));
+    // Counters that kernels reset themselves after use (the
+    // DynamicQuantizeLinear block counter), and the error word in mapped
+    // pinned host memory.
+    B2M_CUDA(cudaMalloc(&ctx->dev_counter, B2M_DEV_STATE_BYTES));
+    B2M_CUDA(cudaMemset(ctx->dev_counter, 0, B2M_DEV_STATE_BYTES));
+    B2M_CUDA(cudaHostAlloc(reinterpret_cast<void **>(&ctx->err_host), sizeof(int32_t), cudaHostAllocMapped));
     *ctx->err_host = B2M_DEVERR_NONE;
+    B2M_CUDA(cudaHostGetDevicePointer(reinterpret_cast<void **>(&ctx->dev_err), ctx->err_host, 0));
 
     const char *no_pdl = std::getenv("B2M_DISABLE_PDL");
     ctx->pdl = !(no_pdl && no_pdl[0] == '1');
@@ -787,7 +791,7 @@ B2M_API b2m_status b2m_shutdown(b2m_ctx *ctx) {
     cudaStreamSynchronize(ctx->own_stream);
     if (ctx->pinned) cudaFreeHost(ctx->pinned);
     if (ctx->err_host) cudaFreeHost(ctx->err_host);
-    cudaFree(ctx->dev_err);
+    cudaFree(ctx->dev_counter);
     cudaFree(ctx->attn_counters);
     cudaEventDestroy(ctx->ev0);
     cudaEventDestroy(ctx->ev1);
@@ -1525,48 +1529,6 @@ B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m,
   });
 }
 
-B2M_API b2m_status b2m_matmul_nbits_swiglu_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gu_rs,
-                                               int64_t m, const b2m_weight *w, const float *bias, int32_t mode,
-                                               float *y) {
-  return guarded([&] {
-    check_ctx(ctx);
-    DeviceGuard dg(ctx->device);
-    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
-    B2M_REQUIRE(m >= 0 && gu_rs >= w->k && (m == 0 || (gate && up && y)), B2M_ERR_INVALID_ARGUMENT,
-                "MatMulNBits SwiGLU: bad pointers or row stride");
-    B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST || mode == B2M_MODE_PRECISE,
-                B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: bad mode");
-    check_cancel(ctx);
-    if (m == 0) return;
-    OpTimer timer(ctx);
-    const bool gemv = mode == B2M_MODE_FAST ? nbits_use_smallm(w->nb, m, w->k, w->n)
-                                            : mode == B2M_MODE_PRECISE && nbits_precise_gemv(w->nb, m);
-    if (gemv && nbits_swiglu_gemv(w->nb, m)) {
-      // The GEMV forms silu(gate) * up in its activation load.
-      NbitsArgs p;
-      p.A = gate;
-      p.up = up;
-      p.gu_rs = gu_rs;
-      p.w = &w->nb;
-      p.bias = bias;
-      p.Y = y;
-      p.M = m;
-      p.K = w->k;
-      p.N = w->n;
-      p.dev_err = ctx->dev_err;
-      nbits_prefetch_plan(ctx, w, m, mode, p);
-      launch_nbits_smallm(p, ctx->stream, ctx->pdl);
-    } else {
-      const size_t abytes = (size_t)(m * w->k * 4);
-      Scratch sc(ctx, abytes + 256 + nbits_scratch_bytes(w, m, mode));
-      float *act = static_cast<float *>(sc.take(abytes));
-      launch_silu_mul(gate, up, gu_rs, gu_rs, act, m, w->k, ctx->stream);
-      nbits_run(ctx, sc, act, m, w, bias, mode, y);
-    }
-    timer.done();
-  });
-}
-
 B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int64_t m, const b2m_weight *w,
                                          const float *bias_host, int32_t mode, float *y_host) {
   return guarded([&] {
@@ -1580,17 +1542,23 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
     const size_t abytes = (size_t)(m * w->k * 4), ybytes = (size_t)(m * w->n * 4), bbytes = (size_t)(w->n * 4);
     Scratch sc(ctx, abytes + ybytes + bbytes + 1024 + nbits_scratch_bytes(w, m, mode));
     float *da = static_cast<float *>(sc.take(abytes));
-    float *dy = static_cast<float *>(sc.take(ybytes));
+    // The decode GEMV stores Y (one 64-byte segment per CTA and row) straight
+    // into a pinned y_host: no device-to-host copy to queue and wait for.
+    // Other routes, and pageable y_host, go through device memory.
+    const bool gemv = mode == B2M_MODE_FAST ? nbits_use_smallm(w->nb, m, w->k, w->n)
+                                            : mode == B2M_MODE_PRECISE && nbits_precise_gemv(w->nb, m);
+    float *dy = gemv ? static_cast<float *>(mapped_host_ptr(y_host)) : nullptr;
+    const bool direct_y = dy != nullptr;
+    if (!direct_y) dy = static_cast<float *>(sc.take(ybytes));
     float *db = bias_host ? static_cast<float *>(sc.take(bbytes)) : nullptr;
     B2M_CUDA(cudaMemcpyAsync(da, a_host, abytes, cudaMemcpyHostToDevice, ctx->stream));
     if (db) B2M_CUDA(cudaMemcpyAsync(db, bias_host, bbytes, cudaMemcpyHostToDevice, ctx->stream));
     OpTimer timer(ctx);
     nbits_run(ctx, sc, da, m, w, db, mode, dy);
     timer.done();
-    B2M_CUDA(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, ctx->stream));
-    enqueue_error_read(ctx);  // one synchronisation for Y and the error word
+    if (!direct_y) B2M_CUDA(cudaMemcpyAsync(y_host, dy, ybytes, cudaMemcpyDeviceToHost, ctx->stream));
     B2M_CUDA(cudaStreamSynchronize(ctx->stream));
-    raise_enqueued_error(ctx);
+    raise_device_error(ctx);
   });
 }
 

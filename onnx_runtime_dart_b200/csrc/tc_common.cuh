@@ -25,7 +25,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
     if (i > 256) __nanosleep(64);
   }
   *abort_flag = 1;
-  if (dev_err) atomicExch(dev_err, B2M_DEVERR_MBAR_TIMEOUT);
+  if (dev_err) set_dev_error(dev_err, B2M_DEVERR_MBAR_TIMEOUT);
   return false;
 }
 

@@ -416,13 +416,14 @@ class Int4Decoder:
                         chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
                                                      _ptr(getattr(self, part))))
                 gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
-            if self.session is not None:  # the export's Sigmoid / Mul / Mul nodes, then its down MatMulNBits
-                chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
-                                         c.inter))
+            # the export's Sigmoid / Mul / Mul nodes as one op, then its down MatMulNBits
+            chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
+                                     c.inter))
+            if self.session is not None:
                 self._dispatch_proj("down", lw, self.act, T, self.down)
-            else:  # SwiGLU formed in the down projection's activation load where the GEMV serves it
-                chk(lib.b2m_matmul_nbits_swiglu_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, T,
-                                                    lw["down"].handle, None, self.mode, _ptr(self.down)))
+            else:
+                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
+                                             _ptr(self.down)))
         chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(self.final_norm), _ptr(self.h),
                                 _ptr(self.res), T, H, c.eps))
         idx = self.last_idx.get(seq)

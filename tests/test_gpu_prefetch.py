@@ -75,34 +75,3 @@ def test_prefetch_hint_keeps_results_and_links_survive_free(m, k, n, block, zp):
         w.free()
     ctx.close()
 
-
-@pytest.mark.parametrize("m", [1, 8, 24, 96])
-def test_swiglu_matmul_nbits_matches_separate_ops(m):
-    """b2m_matmul_nbits_swiglu_dev (the decoder's down projection with the
-    SwiGLU formed in the GEMV's activation load where the GEMV serves the call)
-    against b2m_silu_mul_dev followed by b2m_matmul_nbits_dev: the same bits in
-    every mode, for gate|up as the two halves of one packed buffer."""
-    rng = np.random.default_rng(100 + m)
-    k, n = 3072, 1024
-    ctx = b2m.Context(0)
-    bq, sc, z = _weights(rng, k, n)
-    w = ctx.prepack_nbits(bq, sc, z, k, n, 4, 32)
-    gu = torch.from_numpy(rng.standard_normal((m, 2 * k)).astype(np.float32)).cuda()
-    bias = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
-    p = lambda t: ctypes.c_void_p(t.data_ptr())
-    act = torch.empty((m, k), device="cuda")
-    N.check(ctx.lib.b2m_silu_mul_dev(ctx.handle, p(gu), ctypes.c_void_p(gu.data_ptr() + k * 4), 2 * k, 2 * k, p(act),
-                                     m, k))
-    for mode in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
-        y_sep = torch.full((m, n), float("nan"), device="cuda")
-        y_fused = torch.full((m, n), float("nan"), device="cuda")
-        N.check(ctx.lib.b2m_matmul_nbits_dev(ctx.handle, p(act), m, w.handle, p(bias), mode, p(y_sep)))
-        N.check(ctx.lib.b2m_matmul_nbits_swiglu_dev(ctx.handle, p(gu), ctypes.c_void_p(gu.data_ptr() + k * 4), 2 * k,
-                                                    m, w.handle, p(bias), mode, p(y_fused)))
-        torch.cuda.synchronize()
-        np.testing.assert_array_equal(y_fused.cpu().numpy(), y_sep.cpu().numpy(), err_msg=f"m={m} mode={mode}")
-    assert ctx.lib.b2m_matmul_nbits_swiglu_dev(ctx.handle, p(gu), p(gu), k - 1, m, w.handle, None, N.MODE_FAST,
-                                               p(act)) == N.B2M_ERR_INVALID_ARGUMENT
-    w.free()
-    ctx.close()
-
