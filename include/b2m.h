@@ -153,6 +153,14 @@ B2M_API b2m_status b2m_tensor_wrap(b2m_ctx *ctx, void *device_ptr, int32_t dtype
 B2M_API b2m_status b2m_tensor_upload(b2m_ctx *ctx, b2m_tensor *t, const void *host, int64_t bytes);
 B2M_API b2m_status b2m_tensor_download(b2m_ctx *ctx, const b2m_tensor *t, void *host, int64_t bytes);
 B2M_API b2m_status b2m_tensor_free(b2m_tensor *t);
+
+/* Page-locked host buffers (no counterpart in the reference, whose FFI buffers
+ * come from package:ffi's malloc). Staging a host-buffer call's A and Y here
+ * lets b2m_matmul_nbits_host's decode GEMV store Y straight into host memory
+ * (no device-to-host copy) and makes the copy of A a direct DMA. bytes >= 0;
+ * free with b2m_host_free. */
+B2M_API b2m_status b2m_host_alloc(b2m_ctx *ctx, int64_t bytes, void **out);
+B2M_API b2m_status b2m_host_free(b2m_ctx *ctx, void *p);
 /* dtype, rank, shape (B2M_MAX_RANK entries) and device pointer of `t`. */
 B2M_API b2m_status b2m_tensor_info(const b2m_tensor *t, int32_t *dtype, int32_t *rank, int64_t *shape,
                                    void **device_ptr);

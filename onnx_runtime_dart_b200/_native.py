@@ -121,6 +121,8 @@ SIGNATURES = {
     "b2m_tensor_upload": (_i32, [_c_ctx, _c_tensor, _vp, _i64]),
     "b2m_tensor_download": (_i32, [_c_ctx, _c_tensor, _vp, _i64]),
     "b2m_tensor_free": (_i32, [_c_tensor]),
+    "b2m_host_alloc": (_i32, [_c_ctx, _i64, ctypes.POINTER(_vp)]),
+    "b2m_host_free": (_i32, [_c_ctx, _vp]),
     "b2m_tensor_info": (_i32, [_c_tensor, _i32p, _i32p, _i64p, ctypes.POINTER(_vp)]),
     "b2m_weight_prepack_f32": (_i32, [_c_ctx, _vp, _i64, _i64, _i32, ctypes.POINTER(_c_weight)]),
     "b2m_weight_prepack_i8": (_i32, [_c_ctx, _vp, _i32, _i64, _i64, ctypes.POINTER(_c_weight)]),

@@ -922,6 +922,31 @@ B2M_API b2m_status b2m_tensor_download(b2m_ctx *ctx, const b2m_tensor *t, void *
   });
 }
 
+B2M_API b2m_status b2m_host_alloc(b2m_ctx *ctx, int64_t bytes, void **out) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(out && bytes >= 0, B2M_ERR_INVALID_ARGUMENT, "host alloc: bad arguments");
+    *out = nullptr;
+    DeviceGuard dg(ctx->device);
+    const cudaError_t e = cudaHostAlloc(out, (size_t)std::max<int64_t>(bytes, 1), cudaHostAllocDefault);
+    if (e != cudaSuccess) {
+      (void)cudaGetLastError();
+      *out = nullptr;
+      b2m_throw(B2M_ERR_OUT_OF_MEMORY, "host alloc: cudaHostAlloc of " + std::to_string((long long)bytes) +
+                                           " bytes failed");
+    }
+  });
+}
+
+B2M_API b2m_status b2m_host_free(b2m_ctx *ctx, void *p) {
+  return guarded([&] {
+    check_ctx(ctx);
+    if (!p) return;
+    DeviceGuard dg(ctx->device);
+    B2M_CUDA(cudaFreeHost(p));
+  });
+}
+
 B2M_API b2m_status b2m_tensor_free(b2m_tensor *t) {
   return guarded([&] {
     if (!t) return;

@@ -90,3 +90,30 @@ def test_error_word_reports_gather_index_and_clears(ctx):
     N.check(lib.b2m_gather_rows_dev(h, _p(table), _p(ids_ok), _p(y), 3, v, d))
     N.check(lib.b2m_synchronize(h))
     assert torch.equal(y.cpu(), table[1:4].cpu())
+
+
+def test_host_call_with_library_pinned_buffers(ctx):
+    """A and Y staged in b2m_host_alloc buffers (what a Dart caller would
+    allocate through the ABI): the same bits as the device call."""
+    rng = np.random.default_rng(5)
+    k, n, m = 1024, 3072, 1
+    w = _weight(ctx, rng, k, n)
+    lib, h = ctx.lib, ctx.handle
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    pa, py = ctypes.c_void_p(), ctypes.c_void_p()
+    N.check(lib.b2m_host_alloc(h, a.nbytes, ctypes.byref(pa)))
+    N.check(lib.b2m_host_alloc(h, m * n * 4, ctypes.byref(py)))
+    try:
+        ctypes.memmove(pa, a.ctypes.data, a.nbytes)
+        N.check(lib.b2m_matmul_nbits_host(h, pa, m, w.handle, None, N.MODE_FAST, py))
+        got = np.ctypeslib.as_array(ctypes.cast(py, ctypes.POINTER(ctypes.c_float)), shape=(m, n)).copy()
+        a_d = torch.from_numpy(a).cuda()
+        y_d = torch.empty((m, n), device="cuda")
+        torch.cuda.synchronize()
+        N.check(lib.b2m_matmul_nbits_dev(h, _p(a_d), m, w.handle, None, N.MODE_FAST, _p(y_d)))
+        N.check(lib.b2m_synchronize(h))
+        np.testing.assert_array_equal(got, y_d.cpu().numpy())
+    finally:
+        N.check(lib.b2m_host_free(h, pa))
+        N.check(lib.b2m_host_free(h, py))
+        w.free()
