@@ -1022,8 +1022,11 @@ using b2m::tmem_alloc;
 using b2m::tmem_dealloc;
 using b2m::tmem_ld16;
 using b2m::tmem_ld_wait;
+using b2m::tmem_st8;
+using b2m::tmem_st_wait;
 using b2m::umma_commit;
 using b2m::umma_f16;
+using b2m::umma_f16_ts;
 using b2m::umma_idesc;
 using b2m::warp_wait_or_abort;
 
@@ -1254,20 +1257,21 @@ __global__ void __launch_bounds__(512) mha_tc_kernel(const GqaArgs a) {
 // Causal GroupQueryAttention prefill on the tensor cores (head_dim 64 or
 // 128, keys from the KV cache): flash-style, one CTA of 512 threads per
 // (128-query tile, query head, sequence), 64-key tiles with an online
-// softmax. Per key tile:
-//   * all threads stage K (64 x D) and V^T (D x 64) as bf16 hi / lo planes in
-//     128-byte swizzled shared memory;
-//   * one thread issues S = Q.K^T as three kind::f16 products (the bf16
-//     split Q0.K0 + Q0.K1 + Q1.K0, as the FAST GEMM) into TMEM columns 0-63;
+// softmax. Q (scaled, then rotated as the SIMT prefill kernel does) is split
+// into bf16 hi / lo planes once. Per key tile j:
+//   * Q.K_j^T, three kind::f16 products (the bf16 split Q0.K0 + Q0.K1 +
+//     Q1.K0, as the FAST GEMM) into TMEM columns 0-63, was issued at the end
+//     of tile j-1; meanwhile all threads split tile j+1's K and V^T (loaded
+//     into registers one tile earlier) into the other of two shared-memory
+//     buffers and load tile j+2;
 //   * warp w reads lane quarter w % 4 (query rows) and 16 of the 64 score
 //     columns, applies the causal limit (key j visible to query i when
-//     j <= past + i), and the four column warps of a row agree on the running
-//     max and sum through shared memory; P = exp(s - max) is split into
-//     bf16 hi / lo in shared memory;
-//   * one thread issues P.V (three products, fresh accumulator in TMEM
-//     columns 64 .. 64 + D); each thread adds its D / 4 output columns into
-//     registers as O = O * corr + PV.
-// Q (scaled, then rotated as the SIMT prefill kernel does) is staged once.
+//     j <= past + i); the four column warps of a row agree on the running max
+//     and sum through shared memory; P = exp(s - max), split into bf16 hi /
+//     lo, goes to TMEM with tcgen05.st;
+//   * one thread issues P.V with P as the TMEM (A) operand (three products
+//     into TMEM columns 64 .. 64 + D) and, behind it, Q.K_{j+1}^T; each thread
+//     folds its D / 4 output columns into registers as O = O * corr + PV.
 // Every wait is bounded; a timeout records the device error and the CTA
 // leaves the loop.
 // ---------------------------------------------------------------------------
@@ -1275,16 +1279,22 @@ template <int D>
 struct FaLayout {
   static constexpr int ND = D / 64;                       // 64-dim SW128 blocks of Q / K
   static constexpr uint32_t QH = 0, QL = ND * 16384;      // [128][64] blocks
-  static constexpr uint32_t R = 2 * ND * 16384;           // K / V / P region (Q staging scratch first)
-  static constexpr uint32_t KH = R, KL = KH + ND * 8192;  // [64][64] blocks
-  static constexpr uint32_t VH = KL + ND * 8192, VL = VH + D * 128;  // [D][64] blocks
-  static constexpr uint32_t PH = VL + D * 128, PL = PH + 16384;      // [128][64]
-  static constexpr uint32_t RED = PL + 16384;             // red_m[4][128], red_l[4][128]
+  static constexpr uint32_t R = 2 * ND * 16384;           // K / V buffers (Q staging scratch first)
+  // Two K / V buffers, KV_BUF apart: K hi / lo [64][64] blocks, then V^T
+  // hi / lo [D][64] blocks.
+  static constexpr uint32_t KH = R, KL = KH + ND * 8192;
+  static constexpr uint32_t VH = KL + ND * 8192, VL = VH + D * 128;
+  static constexpr uint32_t KV_BUF = 2 * ND * 8192 + 2 * D * 128;
+  static constexpr uint32_t RED = R + 2 * KV_BUF;         // red_m[4][128], red_l[4][128]
   static constexpr uint32_t BAR = RED + 2 * 4 * 128 * 4;  // bar_s, bar_o
   static constexpr uint32_t SLOT = BAR + 16;
   static constexpr uint32_t FLAG = SLOT + 8;
   static constexpr uint32_t BYTES = FLAG + 8 + 1024;      // + alignment slack
-  static_assert(128 * D * 4 <= PL + 16384 - R, "Q staging fits the K / V / P region");
+  // TMEM columns: S [0, 64), the P.V accumulator [64, 64 + D), P as bf16
+  // hi / lo pairs (32 columns each).
+  static constexpr uint32_t P_HI = 64 + D, P_LO = P_HI + 32;
+  static_assert(P_LO + 32 <= 256, "TMEM allocation");
+  static_assert(128 * D * 4 <= 2 * KV_BUF, "Q staging fits the K / V buffers");
   static_assert(BYTES <= 232448, "shared memory");
 };
 
@@ -1312,27 +1322,93 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
   if (warp == 0) tmem_alloc(slot, 256);
 
   // Q tile: scaled fp32 rows in the K / V / P region, rotated, then split.
+  // Every load of a phase is issued before its first use (the rotary pass
+  // read cos / sin one pair at a time and took ~20,000 cycles per CTA).
   float *qf = reinterpret_cast<float *>(smem + L::R);  // [128][D]
-  for (int it = tid; it < 128 * (D / 4); it += 512) {
-    const int r = it / (D / 4), c = it % (D / 4);
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (q0 + r < a.S)
-      v = *reinterpret_cast<const float4 *>(a.q + (int64_t)(b * a.S + q0 + r) * a.q_rs + h * D + 4 * c);
-    v.x *= a.scale, v.y *= a.scale, v.z *= a.scale, v.w *= a.scale;
-    *reinterpret_cast<float4 *>(qf + r * D + 4 * c) = v;
+  {
+    constexpr int QI = 128 * (D / 4) / 512;  // float4 items per thread
+    float4 qv[QI];
+#pragma unroll
+    for (int u = 0; u < QI; u++) {
+      const int e = tid + 512 * u, rr = e / (D / 4), c = e % (D / 4);
+      qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (q0 + rr < a.S)
+        qv[u] = *reinterpret_cast<const float4 *>(a.q + (int64_t)(b * a.S + q0 + rr) * a.q_rs + h * D + 4 * c);
+    }
+#pragma unroll
+    for (int u = 0; u < QI; u++) {
+      const int e = tid + 512 * u, rr = e / (D / 4), c = e % (D / 4);
+      float4 v = qv[u];
+      v.x *= a.scale, v.y *= a.scale, v.z *= a.scale, v.w *= a.scale;
+      *reinterpret_cast<float4 *>(qf + rr * D + 4 * c) = v;
+    }
   }
   __syncthreads();
   if (a.cos) {
     const int npair = a.rot / 2;
-    for (int i = tid; i < 128 * npair; i += 512) {
-      const int r = i / npair, pi = i % npair;
-      const int64_t pos = past + q0 + r;
-      if (q0 + r >= a.S || pos >= a.CAP) continue;
-      const float c = a.cos[pos * a.half + pi], sn = a.sin[pos * a.half + pi];
-      const int i0 = a.interleaved ? 2 * pi : pi, i1 = a.interleaved ? 2 * pi + 1 : pi + npair;
-      const float x0 = qf[r * D + i0], x1 = qf[r * D + i1];
-      qf[r * D + i0] = x0 * c - x1 * sn;
-      qf[r * D + i1] = x1 * c + x0 * sn;
+    auto al16 = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    if (npair % 4 == 0 && a.half % 4 == 0 && al16(a.cos) && al16(a.sin)) {
+      // Four pairs per item: cos / sin as float4, x0 / x1 as float4 from the
+      // staged rows (pairs (i, i + npair), or adjacent when interleaved).
+      const int ng = npair / 4;
+      constexpr int RI = (128 * (D / 8) + 511) / 512;  // items per thread at most (npair <= D / 2)
+      float4 cv[RI], snv[RI];
+      bool okv[RI];
+      int rv[RI], gv[RI];
+#pragma unroll
+      for (int u = 0; u < RI; u++) {
+        const int e = tid + 512 * u, rr = e / ng, g = e % ng;
+        const int64_t pos = past + q0 + rr;
+        okv[u] = e < 128 * ng && q0 + rr < a.S && pos < a.CAP;
+        rv[u] = rr, gv[u] = g;
+        cv[u] = snv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (okv[u]) {
+          cv[u] = *reinterpret_cast<const float4 *>(a.cos + pos * a.half + 4 * g);
+          snv[u] = *reinterpret_cast<const float4 *>(a.sin + pos * a.half + 4 * g);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < RI; u++) {
+        if (!okv[u]) continue;
+        float *row = qf + rv[u] * D;
+        const float c4[4] = {cv[u].x, cv[u].y, cv[u].z, cv[u].w}, s4[4] = {snv[u].x, snv[u].y, snv[u].z, snv[u].w};
+        float x0[4], x1[4];
+        if (a.interleaved) {
+          const float4 p0 = *reinterpret_cast<const float4 *>(row + 8 * gv[u]);
+          const float4 p1 = *reinterpret_cast<const float4 *>(row + 8 * gv[u] + 4);
+          x0[0] = p0.x, x1[0] = p0.y, x0[1] = p0.z, x1[1] = p0.w;
+          x0[2] = p1.x, x1[2] = p1.y, x0[3] = p1.z, x1[3] = p1.w;
+        } else {
+          const float4 p0 = *reinterpret_cast<const float4 *>(row + 4 * gv[u]);
+          const float4 p1 = *reinterpret_cast<const float4 *>(row + npair + 4 * gv[u]);
+          x0[0] = p0.x, x0[1] = p0.y, x0[2] = p0.z, x0[3] = p0.w;
+          x1[0] = p1.x, x1[1] = p1.y, x1[2] = p1.z, x1[3] = p1.w;
+        }
+        float y0[4], y1[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          y0[j] = x0[j] * c4[j] - x1[j] * s4[j];
+          y1[j] = x1[j] * c4[j] + x0[j] * s4[j];
+        }
+        if (a.interleaved) {
+          *reinterpret_cast<float4 *>(row + 8 * gv[u]) = make_float4(y0[0], y1[0], y0[1], y1[1]);
+          *reinterpret_cast<float4 *>(row + 8 * gv[u] + 4) = make_float4(y0[2], y1[2], y0[3], y1[3]);
+        } else {
+          *reinterpret_cast<float4 *>(row + 4 * gv[u]) = make_float4(y0[0], y0[1], y0[2], y0[3]);
+          *reinterpret_cast<float4 *>(row + npair + 4 * gv[u]) = make_float4(y1[0], y1[1], y1[2], y1[3]);
+        }
+      }
+    } else {
+      for (int i = tid; i < 128 * npair; i += 512) {
+        const int rr = i / npair, pi = i % npair;
+        const int64_t pos = past + q0 + rr;
+        if (q0 + rr >= a.S || pos >= a.CAP) continue;
+        const float c = a.cos[pos * a.half + pi], sn = a.sin[pos * a.half + pi];
+        const int i0 = a.interleaved ? 2 * pi : pi, i1 = a.interleaved ? 2 * pi + 1 : pi + npair;
+        const float x0 = qf[rr * D + i0], x1 = qf[rr * D + i1];
+        qf[rr * D + i0] = x0 * c - x1 * sn;
+        qf[rr * D + i1] = x1 * c + x0 * sn;
+      }
     }
   }
   __syncthreads();
@@ -1363,10 +1439,16 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
 #pragma unroll
   for (int c = 0; c < DW; c++) o[c] = 0.f;
   bool ok = true;
-  int it = 0;
-  // The next key tile's K / V values are loaded into registers while the
-  // current tile's MMAs and softmax run, and written to shared memory (split)
-  // once the tile's P.V has consumed the previous ones.
+  // Matrix descriptors of the operand planes, formed once; an MMA's operand
+  // is its plane's descriptor plus the 16-byte offset of its k slice (the
+  // start-address field does not overflow below 256 KB).
+  const uint32_t sbase = smem_u32(smem);
+  const uint64_t d_qh = sw128_kmajor_desc(sbase + L::QH), d_ql = sw128_kmajor_desc(sbase + L::QL);
+  const uint64_t d_kh = sw128_kmajor_desc(sbase + L::KH), d_kl = sw128_kmajor_desc(sbase + L::KL);
+  const uint64_t d_vh = sw128_kmajor_desc(sbase + L::VH), d_vl = sw128_kmajor_desc(sbase + L::VL);
+  // K / V values of a key tile are loaded into registers two tiles ahead and
+  // split into the bf16 planes of the other buffer one tile ahead, while the
+  // current tile's Q.K^T runs on the tensor cores.
   constexpr int KI = (64 * (D / 8) + 511) / 512;  // K items (key, 8-dim chunk) per thread
   float kx[KI][8], vx[2][8];
   auto load_tile = [&](int j0) {
@@ -1397,9 +1479,11 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
       }
     }
   };
-  if (kend > 0) load_tile(0);
-  for (int j0 = 0; j0 < kend; j0 += 64, it++) {
-    // K tile: (key t, 8-dim chunk) items, split into the hi / lo planes.
+  // The registers' tile as bf16 hi / lo planes in buffer `buf`, published to
+  // the tensor cores' proxy (the next barrier makes them visible to the
+  // issuing thread).
+  auto stage_tile = [&](int buf) {
+    uint8_t *kb = smem + buf * L::KV_BUF, *vb = smem + buf * L::KV_BUF;
 #pragma unroll
     for (int i = 0; i < KI; i++) {
       const int e = tid + 512 * i, t = e / (D / 8), c = e % (D / 8);
@@ -1410,49 +1494,57 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
         split_bf16x2(kx[i][4], kx[i][5], hv.z, lv.z);
         split_bf16x2(kx[i][6], kx[i][7], hv.w, lv.w);
         const uint32_t ob = (uint32_t)(c >> 3) * 8192u + sw128_elem(t, (8 * c) & 63);
-        *reinterpret_cast<uint4 *>(smem + L::KH + ob) = hv;
-        *reinterpret_cast<uint4 *>(smem + L::KL + ob) = lv;
+        *reinterpret_cast<uint4 *>(kb + L::KH + ob) = hv;
+        *reinterpret_cast<uint4 *>(kb + L::KL + ob) = lv;
       }
     }
     // V^T tile: keys 2p, 2p+1 of dims 8g .. 8g+7 as bf16 pairs.
-    {
-      const int pr = tid % 32, g = tid / 32, t0 = 2 * pr;
-      if (g < D / 8) {
+    const int pr = tid % 32, g = tid / 32, t0 = 2 * pr;
+    if (g < D / 8) {
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-          uint32_t hw, lw;
-          split_bf16x2(vx[0][j], vx[1][j], hw, lw);
-          const uint32_t ov = sw128_elem(8 * g + j, t0);
-          *reinterpret_cast<uint32_t *>(smem + L::VH + ov) = hw;
-          *reinterpret_cast<uint32_t *>(smem + L::VL + ov) = lw;
-        }
+      for (int j = 0; j < 8; j++) {
+        uint32_t hw, lw;
+        split_bf16x2(vx[0][j], vx[1][j], hw, lw);
+        const uint32_t ov = sw128_elem(8 * g + j, t0);
+        *reinterpret_cast<uint32_t *>(vb + L::VH + ov) = hw;
+        *reinterpret_cast<uint32_t *>(vb + L::VL + ov) = lw;
       }
     }
     fence_proxy_async_smem();
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    if (*abort_flag) {  // read by every thread after the same barrier: a uniform exit
-      ok = false;
-      break;
-    }
-    if (tid == 0) {
-      constexpr uint32_t idesc_s = umma_idesc(128, 64, 1u, 1u, 1u);
-      const uint32_t base = smem_u32(smem);
+  };
+  // S = Q.K^T of the tile in buffer `buf` (three bf16 products) into TMEM
+  // columns 0-63, issued by thread 0.
+  auto issue_s = [&](int buf) {
+    const uint64_t kvo = (uint64_t)((buf * L::KV_BUF) >> 4);
+    constexpr uint32_t idesc_s = umma_idesc(128, 64, 1u, 1u, 1u);
 #pragma unroll
-      for (int kk = 0; kk < D / 16; kk++) {
-        const uint32_t o16 = (uint32_t)(kk & 3) * 32u;
-        const uint64_t qh = sw128_kmajor_desc(base + L::QH + (kk >> 2) * 16384u + o16);
-        const uint64_t ql = sw128_kmajor_desc(base + L::QL + (kk >> 2) * 16384u + o16);
-        const uint64_t kh = sw128_kmajor_desc(base + L::KH + (kk >> 2) * 8192u + o16);
-        const uint64_t kl = sw128_kmajor_desc(base + L::KL + (kk >> 2) * 8192u + o16);
-        umma_f16(tmem, ql, kh, idesc_s, kk ? 1u : 0u);
-        umma_f16(tmem, qh, kl, idesc_s, 1u);
-        umma_f16(tmem, qh, kh, idesc_s, 1u);
-      }
-      umma_commit(bar_s);
+    for (int kk = 0; kk < D / 16; kk++) {
+      const uint64_t oq = (uint64_t)(((kk >> 2) * 16384u + (kk & 3) * 32u) >> 4);
+      const uint64_t ok16 = kvo + (uint64_t)(((kk >> 2) * 8192u + (kk & 3) * 32u) >> 4);
+      umma_f16(tmem, d_ql + oq, d_kh + ok16, idesc_s, kk ? 1u : 0u);
+      umma_f16(tmem, d_qh + oq, d_kl + ok16, idesc_s, 1u);
+      umma_f16(tmem, d_qh + oq, d_kh + ok16, idesc_s, 1u);
     }
-    if (j0 + 64 < kend) load_tile(j0 + 64);  // in flight under this tile's MMAs and softmax
+    umma_commit(bar_s);
+  };
+  if (kend > 0) {
+    load_tile(0);
+    stage_tile(0);
+  }
+  if (kend > 64) load_tile(64);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0 && kend > 0) issue_s(0);
+  int it = 0;
+  for (int j0 = 0; j0 < kend; j0 += 64, it++) {
+    const int buf = it & 1;
+    const uint64_t kvo = (uint64_t)((buf * L::KV_BUF) >> 4);
+    // While this tile's Q.K^T runs (issued at the end of the previous
+    // iteration): the next tile into the other buffer (its last readers, the
+    // previous tile's MMAs, have completed), and the loads of the one after.
+    if (j0 + 64 < kend) stage_tile(buf ^ 1);
+    if (j0 + 128 < kend) load_tile(j0 + 128);
     const bool ok_s = warp_wait_or_abort(bar_s, (uint32_t)(it & 1), abort_flag, a.err);
     tc_fence_after();
     float sv[16];
@@ -1471,9 +1563,16 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
     }
     red_m[cb * 128 + r] = tmax;
     __syncthreads();
+    if (*abort_flag) {  // read by every thread after the same barrier: a uniform exit
+      ok = false;
+      break;
+    }
     const float mnew = fmaxf(m, fmaxf(fmaxf(red_m[r], red_m[128 + r]), fmaxf(red_m[256 + r], red_m[384 + r])));
     float psum = 0.f;
     {
+      // P = exp(s - max) as bf16 hi / lo, straight into TMEM as the A operand
+      // of P.V (keys 2c, 2c+1 in column c): no shared-memory round trip and
+      // no proxy fence.
       uint32_t ph[8], pl[8];
 #pragma unroll
       for (int j = 0; j < 16; j += 2) {
@@ -1482,15 +1581,11 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
         psum += e0 + e1;
         split_bf16x2(e0, e1, ph[j / 2], pl[j / 2]);
       }
-#pragma unroll
-      for (int hh = 0; hh < 2; hh++) {
-        const uint32_t op = sw128_elem(r, cb * 16 + 8 * hh);
-        *reinterpret_cast<uint4 *>(smem + L::PH + op) = make_uint4(ph[4 * hh], ph[4 * hh + 1], ph[4 * hh + 2], ph[4 * hh + 3]);
-        *reinterpret_cast<uint4 *>(smem + L::PL + op) = make_uint4(pl[4 * hh], pl[4 * hh + 1], pl[4 * hh + 2], pl[4 * hh + 3]);
-      }
+      tmem_st8(trow + L::P_HI + (uint32_t)(cb * 8), ph);
+      tmem_st8(trow + L::P_LO + (uint32_t)(cb * 8), pl);
+      tmem_st_wait();
     }
     red_l[cb * 128 + r] = psum;
-    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -1500,18 +1595,20 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
     if (tid == 0) {
       if (ok_s) {
         constexpr uint32_t idesc_o = umma_idesc(128, D, 1u, 1u, 1u);
-        const uint32_t base = smem_u32(smem);
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {
-          const uint32_t o16 = (uint32_t)kk * 32u;
-          const uint64_t ph = sw128_kmajor_desc(base + L::PH + o16), pl = sw128_kmajor_desc(base + L::PL + o16);
-          const uint64_t vh = sw128_kmajor_desc(base + L::VH + o16), vl = sw128_kmajor_desc(base + L::VL + o16);
-          umma_f16(tmem + 64, pl, vh, idesc_o, kk ? 1u : 0u);
-          umma_f16(tmem + 64, ph, vl, idesc_o, 1u);
-          umma_f16(tmem + 64, ph, vh, idesc_o, 1u);
+          const uint64_t o16 = kvo + (uint64_t)((kk * 32u) >> 4);
+          const uint32_t pc = (uint32_t)(kk * 8);
+          umma_f16_ts(tmem + 64, tmem + L::P_LO + pc, d_vh + o16, idesc_o, kk ? 1u : 0u);
+          umma_f16_ts(tmem + 64, tmem + L::P_HI + pc, d_vl + o16, idesc_o, 1u);
+          umma_f16_ts(tmem + 64, tmem + L::P_HI + pc, d_vh + o16, idesc_o, 1u);
         }
       }
       umma_commit(bar_o);  // also when skipped, so every wait ends
+      // The next tile's Q.K^T right behind it: its K planes were staged and
+      // fenced before this tile's two barriers, S has been read, and P sits in
+      // other TMEM columns. It runs under the output update below.
+      if (j0 + 64 < kend) issue_s(buf ^ 1);
     }
     const bool ok_o = warp_wait_or_abort(bar_o, (uint32_t)(it & 1), abort_flag, a.err) && ok_s;
     tc_fence_after();
@@ -1525,9 +1622,9 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
         for (int j = 0; j < 16; j++) o[c0 + j] = fmaf(o[c0 + j], corr, __uint_as_float(v[j]));
       }
     }
-    // No barrier here: every thread has passed this tile's P.V completion
-    // (so K, V and P are free) and the next tile's first barrier orders the
-    // rest.
+    // No barrier here: the next tile's S issue needs its K / V planes, which
+    // every thread staged (and fenced) before this tile's two barriers; the
+    // P.V that read P and V has completed for every thread that goes on.
   }
   if (ok && q0 + r < a.S) {
     const float inv = 1.f / l;
