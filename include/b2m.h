@@ -264,6 +264,28 @@ B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int6
 B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m, const b2m_weight *w,
                                         const float *bias, int32_t mode, float *y);
 
+/* Which kernels b2m_matmul_nbits_dev runs for an m-row call of `w` in
+ * `mode`: B2M_ROUTE_GEMV (the decode GEMV, fp32 activations read as they
+ * are), B2M_ROUTE_TC_F16 (the tensor-core GEMM, which first rounds the
+ * activations to f16; b2m_matmul_nbits_f16_dev takes them already rounded)
+ * or B2M_ROUTE_OTHER. No counterpart in the reference: a chain driver uses it
+ * to have each projection's producer write the f16 operand. */
+#define B2M_ROUTE_GEMV 0
+#define B2M_ROUTE_TC_F16 1
+#define B2M_ROUTE_OTHER 2
+B2M_API b2m_status b2m_matmul_nbits_route(b2m_ctx *ctx, const b2m_weight *w, int64_t m, int32_t mode,
+                                          int32_t *route);
+
+/* FAST MatMulNBits on activations already rounded to f16 by their producer:
+ * a16 holds m rows of K f16 values (K % 8 == 0), round to nearest of the fp32
+ * activations, as b2m_rmsnorm_f16_dev and b2m_silu_mul_f16_dev write them. The
+ * result is bit for bit that of b2m_matmul_nbits_dev in FAST mode on the fp32
+ * rows; the call is accepted only where that call's route is
+ * B2M_ROUTE_TC_F16 (otherwise B2M_ERR_UNSUPPORTED). Saves the conversion
+ * launch in front of the GEMM. */
+B2M_API b2m_status b2m_matmul_nbits_f16_dev(b2m_ctx *ctx, const uint16_t *a16, int64_t m, const b2m_weight *w,
+                                            const float *bias, float *y);
+
 /* Allocation-free MatMulNBits. No counterpart in the reference: this entry
  * point exists for callers that must not allocate device memory while they
  * run an operator — a host application that has handed all device memory to
@@ -303,6 +325,11 @@ B2M_API b2m_status b2m_matmul_nbits_noalloc(const b2m_weight *w, const float *a,
 B2M_API b2m_status b2m_rmsnorm_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma, float *y,
                                    float *sum_out, int64_t rows, int64_t d, double eps);
 
+/* b2m_rmsnorm_dev that also writes y as f16 (round to nearest) into y16
+ * (rows x d, d % 8 == 0): the operand of b2m_matmul_nbits_f16_dev. */
+B2M_API b2m_status b2m_rmsnorm_f16_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma, float *y,
+                                       float *sum_out, uint16_t *y16, int64_t rows, int64_t d, double eps);
+
 /* RMSNorm of every head vector of [tokens][heads x head_dim] rows placed
  * token_stride floats apart (per-head q / k norms read from a packed
  * projection output; y may alias x, with the same layout). */
@@ -328,6 +355,11 @@ B2M_API b2m_status b2m_layernorm_dev(b2m_ctx *ctx, const float *x, const float *
  * packed projection). */
 B2M_API b2m_status b2m_silu_mul_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gate_rs,
                                     int64_t up_rs, float *y, int64_t rows, int64_t d);
+
+/* b2m_silu_mul_dev that also writes y as f16 (round to nearest) into y16
+ * (rows x d, d % 8 == 0). */
+B2M_API b2m_status b2m_silu_mul_f16_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gate_rs,
+                                        int64_t up_rs, float *y, uint16_t *y16, int64_t rows, int64_t d);
 
 /* erf GELU, y = 0.5 x (1 + erf(x / sqrt 2)) (opGelu, lib/src/onnx_ops.dart:706). */
 B2M_API b2m_status b2m_gelu_dev(b2m_ctx *ctx, const float *x, float *y, int64_t n);

@@ -35,6 +35,7 @@ B2M_FLOAT16 = 10
 MODE_EXACT = 0
 MODE_FAST = 1
 MODE_PRECISE = 2  # MatMulNBits: bf16-split products on exactly dequantized weights
+ROUTE_GEMV, ROUTE_TC_F16, ROUTE_OTHER = 0, 1, 2  # b2m_matmul_nbits_route
 
 MAX_RANK = 8
 NOALLOC_SCRATCH_BYTES = 8 << 20
@@ -154,6 +155,10 @@ SIGNATURES = {
     "b2m_rmsnorm_heads_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_double]),
     "b2m_layernorm_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_double]),
     "b2m_silu_mul_dev": (_i32, [_c_ctx, _vp, _vp, _i64, _i64, _vp, _i64, _i64]),
+    "b2m_silu_mul_f16_dev": (_i32, [_c_ctx, _vp, _vp, _i64, _i64, _vp, _vp, _i64, _i64]),
+    "b2m_rmsnorm_f16_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_double]),
+    "b2m_matmul_nbits_route": (_i32, [_c_ctx, _c_weight, _i64, _i32, ctypes.POINTER(_i32)]),
+    "b2m_matmul_nbits_f16_dev": (_i32, [_c_ctx, _vp, _i64, _c_weight, _vp, _vp]),
     "b2m_gelu_dev": (_i32, [_c_ctx, _vp, _vp, _i64]),
     "b2m_add_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i32]),
     "b2m_gather_rows_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i64]),

@@ -353,13 +353,16 @@ void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStre
 // Transformer glue (k_glue.cu)
 // gamma_rs > 0: row i of a group of `per` rows uses gains gamma + i * gamma_rs
 // (per-head gains, e.g. the q and k norms of one packed projection in one
-// launch); 0: every row uses gamma.
+// launch); 0: every row uses gamma. y16 (optional; D % 8 == 0 and per ==
+// rows): the output rows also as f16 (round to nearest), the operand a FAST
+// MatMulNBits prefill GEMM takes.
 void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
-                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs = 0);
+                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs = 0,
+                    __half *y16 = nullptr);
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                       float *sum_out, int64_t rows, int D, double eps, cudaStream_t s);
 void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
-                     int64_t D, cudaStream_t s);
+                     int64_t D, cudaStream_t s, __half *y16 = nullptr);
 void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s);
 void launch_add(const float *a, const float *b, float *y, int64_t rows, int64_t D, int b_bcast, cudaStream_t s);
 void launch_gather_rows(const float *table, const int64_t *ids, float *y, int64_t rows, int64_t V, int64_t D,

@@ -106,6 +106,16 @@ __global__ void __launch_bounds__(256) layernorm_kernel(const float *x, const fl
   }
 }
 
+// Four values as f16, round to nearest (the rounding of f32_to_f16_rows, so a
+// producer's f16 copy equals what the GEMM's own conversion would form).
+__device__ __forceinline__ void store_f16x4(__half *p, float4 v) {
+  const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+  uint2 u;
+  u.x = *reinterpret_cast<const uint32_t *>(&a);
+  u.y = *reinterpret_cast<const uint32_t *>(&b);
+  *reinterpret_cast<uint2 *>(p) = u;
+}
+
 // Warp per row with float4 loads (D % 4 == 0, 16-byte aligned rows): lane
 // takes float4 chunks lane + 32 i. Half the load instructions of the scalar
 // form and twice the bytes per request (BERT LayerNorm 4096 x 768: 6.5 us
@@ -115,7 +125,7 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
                                                          const float *__restrict__ gamma,
                                                          const float *__restrict__ beta, float *y, float *sum_out,
                                                          int64_t rows, int D, double eps, int64_t per,
-                                                         int64_t gstride, int64_t gamma_rs) {
+                                                         int64_t gstride, int64_t gamma_rs, __half *y16) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -161,9 +171,10 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
       if (sum_out) reinterpret_cast<float4 *>(sum_out + off)[j] = v[i];
       const float4 g = g4[j];
       const float4 bb = b4 ? b4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      reinterpret_cast<float4 *>(y + off)[j] =
-          make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
-                      (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
+      const float4 o = make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
+                                   (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
+      reinterpret_cast<float4 *>(y + off)[j] = o;
+      if (y16) store_f16x4(y16 + off + 4 * j, o);
     }
   }
 }
@@ -178,7 +189,8 @@ template <int NV4, bool LN>
 __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const float *skip,
                                                            const float *__restrict__ gamma,
                                                            const float *__restrict__ beta, float *y, float *sum_out,
-                                                           int D, double eps, int64_t per, int64_t gstride, int64_t gamma_rs) {
+                                                           int D, double eps, int64_t per, int64_t gstride, int64_t gamma_rs,
+                                                           __half *y16) {
   const int64_t r = blockIdx.x;
   const int64_t off = (r / per) * gstride + (r % per) * D;
   const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
@@ -232,9 +244,10 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
       if (sum_out) reinterpret_cast<float4 *>(sum_out + off)[j] = v[i];
       const float4 g = g4[j];
       const float4 bb = b4 ? b4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
-      reinterpret_cast<float4 *>(y + off)[j] =
-          make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
-                      (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
+      const float4 o = make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
+                                   (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
+      reinterpret_cast<float4 *>(y + off)[j] = o;
+      if (y16) store_f16x4(y16 + off + 4 * j, o);
     }
   }
 }
@@ -244,7 +257,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
 template <bool LN>
 bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                           float *sum_out, int64_t rows, int D, double eps, int64_t per, int64_t gstride,
-                          int64_t gamma_rs, cudaStream_t s) {
+                          int64_t gamma_rs, cudaStream_t s, __half *y16 = nullptr) {
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (D % 4 || gstride % 4 || D > 4096 || !al(x) || !al(skip) || !al(gamma) || !al(beta) || !al(y) ||
       !al(sum_out))
@@ -255,7 +268,7 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
     const int v4 = (D / 4 + 31) / 32;
 #define B2M_NW4(N) \
   norm_warp4_kernel<N, LN><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps, per, gstride, \
-                                              gamma_rs)
+                                              gamma_rs, y16)
     if (v4 <= 1) B2M_NW4(1);
     else if (v4 <= 2) B2M_NW4(2);
     else if (v4 <= 4) B2M_NW4(4);
@@ -272,7 +285,7 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
   const int nv4 = (d4 + nt - 1) / nt;
   const unsigned g = (unsigned)rows;
 #define B2M_NRC(N) \
-  norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride, gamma_rs)
+  norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride, gamma_rs, y16)
   if (nv4 <= 1) B2M_NRC(1);
   else if (nv4 <= 2) B2M_NRC(2);
   else B2M_NRC(4);
@@ -335,11 +348,12 @@ __global__ void __launch_bounds__(256) layernorm_long_kernel(const float *x, con
 // halves of one [rows][2*D] tensor (a packed gate|up projection).
 using b2m::silu_times;
 
+
 // Rows over blockIdx.y, columns over x (float4 when VEC: D, both row strides
 // and the three pointers 16-byte aligned); no per-element index division.
 template <bool VEC>
 __global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__restrict__ up, int64_t g_rs,
-                                int64_t u_rs, float *y, int64_t rows, int64_t D) {
+                                int64_t u_rs, float *y, int64_t rows, int64_t D, __half *y16) {
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
     const float *gr = gate + r * g_rs, *ur = up + r * u_rs;
@@ -347,8 +361,10 @@ __global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__r
     if (VEC) {
       for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < D / 4; c += step) {
         const float4 g = reinterpret_cast<const float4 *>(gr)[c], u = reinterpret_cast<const float4 *>(ur)[c];
-        reinterpret_cast<float4 *>(yr)[c] =
+        const float4 o =
             make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z), silu_times(g.w, u.w));
+        reinterpret_cast<float4 *>(yr)[c] = o;
+        if (y16) store_f16x4(y16 + r * D + 4 * c, o);
       }
     } else {
       for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < D; c += step) yr[c] = silu_times(gr[c], ur[c]);
@@ -1654,10 +1670,15 @@ unsigned grid_for(int64_t n, int block) {
 }  // namespace
 
 void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
-                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs) {
+                    int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs, __half *y16) {
   if (rows <= 0) return;
-  if (launch_norm_rows_cta<false>(x, skip, gamma, nullptr, y, sum_out, rows, D, eps, per, gstride, gamma_rs, s))
+  if (launch_norm_rows_cta<false>(x, skip, gamma, nullptr, y, sum_out, rows, D, eps, per, gstride, gamma_rs, s, y16))
     return;
+  if (y16) {  // the fallback kernels write fp32 only: round the rows after them
+    launch_rmsnorm(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride, s, gamma_rs, nullptr);
+    b2m::launch_f32_to_f16(y, y16, rows, D, D, 0, s);
+    return;
+  }
   const unsigned g = (unsigned)((rows + 7) / 8);
   const int vpl = (D + 31) / 32;
 #define B2M_RMS(V) \
@@ -1692,14 +1713,20 @@ void launch_layernorm(const float *x, const float *skip, const float *gamma, con
 }
 
 void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
-                     int64_t D, cudaStream_t s) {
+                     int64_t D, cudaStream_t s, __half *y16) {
   if (rows * D <= 0) return;
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  const bool vec = D % 4 == 0 && g_rs % 4 == 0 && u_rs % 4 == 0 && al(gate) && al(up) && al(y);
+  const bool vec = D % 4 == 0 && g_rs % 4 == 0 && u_rs % 4 == 0 && al(gate) && al(up) && al(y) &&
+                   (reinterpret_cast<uintptr_t>(y16) & 7) == 0;
+  if (y16 && !vec) {  // the scalar path writes fp32 only: round the rows after it
+    launch_silu_mul(gate, up, g_rs, u_rs, y, rows, D, s, nullptr);
+    b2m::launch_f32_to_f16(y, y16, rows, D, D, 0, s);
+    return;
+  }
   const int64_t cols = vec ? D / 4 : D;
   const dim3 grid((unsigned)std::min<int64_t>((cols + 255) / 256, 64), (unsigned)std::min<int64_t>(rows, 65535));
-  if (vec) silu_mul_kernel<true><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D);
-  else silu_mul_kernel<false><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D);
+  if (vec) silu_mul_kernel<true><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D, y16);
+  else silu_mul_kernel<false><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D, nullptr);
   B2M_CUDA(cudaGetLastError());
 }
 

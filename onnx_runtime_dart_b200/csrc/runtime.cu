@@ -1554,6 +1554,54 @@ B2M_API b2m_status b2m_matmul_nbits_dev(b2m_ctx *ctx, const float *a, int64_t m,
   });
 }
 
+static int32_t nbits_route(const b2m_weight *w, int64_t m, int32_t mode) {
+  if (mode == B2M_MODE_FAST) {
+    if (nbits_use_smallm(w->nb, m, w->k, w->n)) return B2M_ROUTE_GEMV;
+    if (w->nb.tsq && nbits_tc_supported(w->nb, m, w->k, w->n)) return B2M_ROUTE_TC_F16;
+    return B2M_ROUTE_OTHER;
+  }
+  if (mode == B2M_MODE_PRECISE && nbits_precise_gemv(w->nb, m)) return B2M_ROUTE_GEMV;
+  return B2M_ROUTE_OTHER;
+}
+
+B2M_API b2m_status b2m_matmul_nbits_route(b2m_ctx *ctx, const b2m_weight *w, int64_t m, int32_t mode,
+                                          int32_t *route) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(w && w->kind == W_NBITS && route && m >= 0, B2M_ERR_INVALID_ARGUMENT,
+                "MatMulNBits route: bad arguments");
+    *route = m == 0 ? B2M_ROUTE_OTHER : nbits_route(w, m, mode);
+  });
+}
+
+B2M_API b2m_status b2m_matmul_nbits_f16_dev(b2m_ctx *ctx, const uint16_t *a16, int64_t m, const b2m_weight *w,
+                                            const float *bias, float *y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+    B2M_REQUIRE(m >= 0 && (m == 0 || (a16 && y)), B2M_ERR_INVALID_ARGUMENT, "MatMulNBits f16: bad pointers");
+    check_cancel(ctx);
+    if (m == 0) return;
+    B2M_REQUIRE(w->k % 8 == 0 && (reinterpret_cast<uintptr_t>(a16) & 15) == 0 &&
+                    nbits_route(w, m, B2M_MODE_FAST) == B2M_ROUTE_TC_F16,
+                B2M_ERR_UNSUPPORTED, "MatMulNBits f16: the call's route does not take f16 activations");
+    OpTimer timer(ctx);
+    NbitsArgs p;
+    p.A = nullptr;
+    p.w = &w->nb;
+    p.bias = bias;
+    p.Y = y;
+    p.M = m;
+    p.K = w->k;
+    p.N = w->n;
+    p.dev_err = ctx->dev_err;
+    nbits_prefetch_plan(ctx, w, m, B2M_MODE_FAST, p);
+    launch_nbits_ts(p, reinterpret_cast<const __half *>(a16), w->k, ctx->stream);
+    timer.done();
+  });
+}
+
 B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int64_t m, const b2m_weight *w,
                                          const float *bias_host, int32_t mode, float *y_host) {
   return guarded([&] {
@@ -1604,6 +1652,18 @@ B2M_API b2m_status b2m_rmsnorm_dev(b2m_ctx *ctx, const float *x, const float *sk
   });
 }
 
+B2M_API b2m_status b2m_rmsnorm_f16_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma, float *y,
+                                       float *sum_out, uint16_t *y16, int64_t rows, int64_t d, double eps) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d > 0 && d % 8 == 0 && d <= (1 << 24) && (rows == 0 || (x && gamma && y && y16)),
+                B2M_ERR_INVALID_ARGUMENT, "RMSNorm f16: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_rmsnorm(x, skip, gamma, y, sum_out, rows, (int)d, eps, std::max<int64_t>(rows, 1), 0, ctx->stream, 0,
+                   reinterpret_cast<__half *>(y16));
+  });
+}
+
 B2M_API b2m_status b2m_rmsnorm_heads_dev(b2m_ctx *ctx, const float *x, const float *gamma, float *y, int64_t tokens,
                                          int64_t heads, int64_t head_dim, int64_t token_stride, double eps) {
   return guarded([&] {
@@ -1651,6 +1711,18 @@ B2M_API b2m_status b2m_silu_mul_dev(b2m_ctx *ctx, const float *gate, const float
                 B2M_ERR_INVALID_ARGUMENT, "SiLU*Mul: bad arguments");
     DeviceGuard dg(ctx->device);
     launch_silu_mul(gate, up, gate_rs, up_rs, y, rows, d, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_silu_mul_f16_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gate_rs,
+                                        int64_t up_rs, float *y, uint16_t *y16, int64_t rows, int64_t d) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d >= 0 && d % 8 == 0 && gate_rs >= d && up_rs >= d &&
+                    (rows * d == 0 || (gate && up && y && y16)),
+                B2M_ERR_INVALID_ARGUMENT, "SiLU*Mul f16: bad arguments");
+    DeviceGuard dg(ctx->device);
+    launch_silu_mul(gate, up, gate_rs, up_rs, y, rows, d, ctx->stream, reinterpret_cast<__half *>(y16));
   });
 }
 

@@ -81,7 +81,8 @@ class Int4Decoder:
     cache of `cap` positions; prompts up to `max_prefill` tokens."""
 
     def __init__(self, ctx, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int, seed: int = 0,
-                 keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True, session=None):
+                 keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True, session=None,
+                 producer_f16: bool = True):
         import torch
 
         if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
@@ -102,6 +103,12 @@ class Int4Decoder:
         # through GpuDispatch.dispatch; the weights are its prepacked
         # initializers.
         self.session = session
+        # producer_f16: where a fused projection takes the FAST tensor-core
+        # route, the RMSNorm / SiLU*Mul that produces its input also writes the
+        # f16 operand (the bits the GEMM's own conversion forms), so the
+        # projection runs without its conversion launch.
+        self.producer_f16 = producer_f16
+        self._routes = {}
         self.torch = torch
         self.ctx, self.cfg, self.B, self.cap = ctx, cfg, batch, cap
         self.lib = ctx.lib
@@ -138,6 +145,9 @@ class Int4Decoder:
         self.o = torch.empty((t, c.hidden), **f32)
         self.gu = torch.empty((t, 2 * c.inter), **f32)
         self.act = torch.empty((t, c.inter), **f32)
+        if self.fused and producer_f16:
+            self.h16 = torch.empty((t, c.hidden), device=dev, dtype=torch.float16)
+            self.act16 = torch.empty((t, c.inter), device=dev, dtype=torch.float16)
         self.down = torch.empty((t, c.hidden), **f32)
         self.last = torch.empty((batch, c.hidden), **f32)
         self.logits = torch.empty((batch, c.vocab), **f32)
@@ -359,6 +369,34 @@ class Int4Decoder:
         finally:
             self.ctx.set_attention_mode(N.MODE_FAST)
 
+    def _f16_input(self, w, T: int) -> bool:
+        """Whether the fused projection `w` at T rows takes its activations as
+        f16 from their producer (FAST mode, tensor-core route)."""
+        if not (self.fused and self.producer_f16 and self.session is None and self.mode == N.MODE_FAST):
+            return False
+        key = (w.handle.value, T)
+        r = self._routes.get(key)
+        if r is None:
+            out = ctypes.c_int32(-1)
+            N.check(self.lib.b2m_matmul_nbits_route(self.ctx.handle, w.handle, T, N.MODE_FAST, ctypes.byref(out)))
+            r = self._routes[key] = out.value == N.ROUTE_TC_F16 and w.kn[0] % 8 == 0
+        return r
+
+    def _norm(self, x, skip, gamma, sum_out, T: int, f16: bool):
+        c, lib, h = self.cfg, self.lib, self.ctx.handle
+        if f16:
+            N.check(lib.b2m_rmsnorm_f16_dev(h, _ptr(x), skip, _ptr(gamma), _ptr(self.h), sum_out, _ptr(self.h16), T,
+                                            c.hidden, c.eps))
+        else:
+            N.check(lib.b2m_rmsnorm_dev(h, _ptr(x), skip, _ptr(gamma), _ptr(self.h), sum_out, T, c.hidden, c.eps))
+
+    def _proj(self, w, T: int, f16: bool, x, x16, y):
+        h = self.ctx.handle
+        if f16:
+            N.check(self.lib.b2m_matmul_nbits_f16_dev(h, _ptr(x16), T, w.handle, None, _ptr(y)))
+        else:
+            N.check(self.lib.b2m_matmul_nbits_dev(h, _ptr(x), T, w.handle, None, self.mode, _ptr(y)))
+
     def _layers(self, seq: int, T: int):
         c, lib, h = self.cfg, self.lib, self.ctx.handle
         H, D = c.hidden, c.head_dim
@@ -367,14 +405,15 @@ class Int4Decoder:
         qkv = self.qkv.data_ptr()
         q_off, k_off, v_off = 0, c.heads * D * 4, (c.heads + c.kv_heads) * D * 4
         for li, lw in enumerate(self.layers):
+            qkv16 = self.fused and self._f16_input(lw["qkv"], T)
+            gu16 = self.fused and self._f16_input(lw["gate_up"], T)
+            dn16 = self.fused and self._f16_input(lw["down"], T)
             if li == 0:
-                chk(lib.b2m_rmsnorm_dev(h, _ptr(self.res), None, _ptr(lw["attn_norm"]), _ptr(self.h), None, T, H,
-                                        c.eps))
+                self._norm(self.res, None, lw["attn_norm"], None, T, qkv16)
             else:  # residual of the previous layer's MLP, then the attention norm
-                chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(lw["attn_norm"]), _ptr(self.h),
-                                        _ptr(self.res), T, H, c.eps))
+                self._norm(self.down, _ptr(self.res), lw["attn_norm"], _ptr(self.res), T, qkv16)
             if self.fused:
-                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["qkv"].handle, None, self.mode, _ptr(self.qkv)))
+                self._proj(lw["qkv"], T, qkv16, self.h, getattr(self, "h16", None), self.qkv)
                 qp, kp, vp = qkv + q_off, qkv + k_off, qkv + v_off
                 q_rs = kv_rs = c.qkv_n
             else:
@@ -402,11 +441,9 @@ class Int4Decoder:
                 self._dispatch_proj("o", lw, self.attn, T, self.o)
             else:
                 chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, self.mode, _ptr(self.o)))
-            chk(lib.b2m_rmsnorm_dev(h, _ptr(self.o), _ptr(self.res), _ptr(lw["mlp_norm"]), _ptr(self.h),
-                                    _ptr(self.res), T, H, c.eps))
+            self._norm(self.o, _ptr(self.res), lw["mlp_norm"], _ptr(self.res), T, gu16)
             if self.fused:
-                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw["gate_up"].handle, None, self.mode,
-                                             _ptr(self.gu)))
+                self._proj(lw["gate_up"], T, gu16, self.h, getattr(self, "h16", None), self.gu)
                 gp, up_, g_rs = self.gu.data_ptr(), self.gu.data_ptr() + c.inter * 4, 2 * c.inter
             else:
                 for part in ("gate", "up"):
@@ -417,13 +454,16 @@ class Int4Decoder:
                                                      _ptr(getattr(self, part))))
                 gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
             # the export's Sigmoid / Mul / Mul nodes as one op, then its down MatMulNBits
-            chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
-                                     c.inter))
+            if dn16:
+                chk(lib.b2m_silu_mul_f16_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act),
+                                             _ptr(self.act16), T, c.inter))
+            else:
+                chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
+                                         c.inter))
             if self.session is not None:
                 self._dispatch_proj("down", lw, self.act, T, self.down)
             else:
-                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.act), T, lw["down"].handle, None, self.mode,
-                                             _ptr(self.down)))
+                self._proj(lw["down"], T, dn16, self.act, getattr(self, "act16", None), self.down)
         chk(lib.b2m_rmsnorm_dev(h, _ptr(self.down), _ptr(self.res), _ptr(self.final_norm), _ptr(self.h),
                                 _ptr(self.res), T, H, c.eps))
         idx = self.last_idx.get(seq)

@@ -1,0 +1,140 @@
+"""GPU tests of the producer-written f16 operand of FAST MatMulNBits.
+
+Where a FAST MatMulNBits call takes the tensor-core route, the GEMM first
+rounds its fp32 activations to f16 in a conversion launch. In a chain the op
+that produces those activations (RMSNorm, SiLU*Mul) can write the f16 copy
+itself, and b2m_matmul_nbits_f16_dev takes it: one launch fewer per
+projection and the same bits. The tests hold every piece to bit equality with
+the path it replaces: the route query, the f16 entry against the fp32 entry,
+the producers' f16 copies against rounding their fp32 outputs, and a decoder
+(Qwen3-0.6B shapes, two layers) with and without producer-written operands.
+The reference runs these ops as separate Dart kernels in fp32
+(lib/src/onnx_qlinear_ops.dart:115-228, lib/src/onnx_ops.dart:1771); FAST mode
+is held to its tolerance contract elsewhere."""
+import ctypes
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import onnx_runtime_dart_b200 as b2m  # noqa: E402
+from onnx_runtime_dart_b200 import _native as N  # noqa: E402
+from onnx_runtime_dart_b200.decoder import DecoderConfig, Int4Decoder  # noqa: E402
+
+
+def _p(t):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = b2m.Context(0)
+    yield c
+    c.close()
+
+
+def _weight(ctx, rng, k, n):
+    nb = k // 32
+    bq = rng.integers(0, 256, (n, nb, 16), dtype=np.uint8)
+    sc = (np.abs(rng.normal(0, 0.02, (n, nb))) + 1e-3).astype(np.float32)
+    zp = rng.integers(0, 256, (n, (nb + 1) // 2), dtype=np.uint8)
+    return ctx.prepack_nbits(bq, sc, zp, k, n, 4, 32)
+
+
+def _route(ctx, w, m, mode):
+    r = ctypes.c_int32(-1)
+    N.check(ctx.lib.b2m_matmul_nbits_route(ctx.handle, w.handle, m, mode, ctypes.byref(r)))
+    return r.value
+
+
+def test_route_query(ctx):
+    w = _weight(ctx, np.random.default_rng(0), 1024, 3072)
+    assert _route(ctx, w, 1, N.MODE_FAST) == N.ROUTE_GEMV
+    assert _route(ctx, w, 8, N.MODE_FAST) == N.ROUTE_GEMV
+    assert _route(ctx, w, 512, N.MODE_FAST) == N.ROUTE_TC_F16
+    assert _route(ctx, w, 1, N.MODE_PRECISE) == N.ROUTE_GEMV
+    assert _route(ctx, w, 512, N.MODE_EXACT) == N.ROUTE_OTHER
+    assert _route(ctx, w, 0, N.MODE_FAST) == N.ROUTE_OTHER
+    w.free()
+
+
+@pytest.mark.parametrize("m,k,n", [(64, 1024, 4096), (512, 1024, 3072), (777, 3072, 1024)])
+def test_f16_entry_matches_fast_entry_bitwise(ctx, m, k, n):
+    rng = np.random.default_rng(m)
+    w = _weight(ctx, rng, k, n)
+    lib, h = ctx.lib, ctx.handle
+    a = torch.from_numpy(rng.standard_normal((m, k)).astype(np.float32)).cuda()
+    a16 = a.half()  # round to nearest, as the GEMM's conversion rounds
+    bias = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
+    y32 = torch.full((m, n), float("nan"), device="cuda")
+    y16 = torch.full((m, n), float("nan"), device="cuda")
+    torch.cuda.synchronize()
+    N.check(lib.b2m_matmul_nbits_dev(h, _p(a), m, w.handle, _p(bias), N.MODE_FAST, _p(y32)))
+    N.check(lib.b2m_matmul_nbits_f16_dev(h, _p(a16), m, w.handle, _p(bias), _p(y16)))
+    N.check(lib.b2m_synchronize(h))
+    np.testing.assert_array_equal(y16.cpu().numpy(), y32.cpu().numpy())
+    # a row count the GEMV serves is refused
+    assert lib.b2m_matmul_nbits_f16_dev(h, _p(a16), 1, w.handle, None, _p(y16)) == N.B2M_ERR_UNSUPPORTED
+    w.free()
+
+
+@pytest.mark.parametrize("rows,d,skip", [(64, 1024, True), (4096, 1024, False), (3, 3072, True)])
+def test_rmsnorm_f16_copy(ctx, rows, d, skip):
+    rng = np.random.default_rng(rows + d)
+    lib, h = ctx.lib, ctx.handle
+    x = torch.from_numpy(rng.standard_normal((rows, d)).astype(np.float32)).cuda()
+    s = torch.from_numpy(rng.standard_normal((rows, d)).astype(np.float32)).cuda() if skip else None
+    g = torch.from_numpy(rng.standard_normal(d).astype(np.float32)).cuda()
+    y_ref, y, sum_ref, sum_out = (torch.empty((rows, d), device="cuda") for _ in range(4))
+    y16 = torch.empty((rows, d), device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+    N.check(lib.b2m_rmsnorm_dev(h, _p(x), _p(s) if skip else None, _p(g), _p(y_ref), _p(sum_ref) if skip else None,
+                                rows, d, 1e-6))
+    N.check(lib.b2m_rmsnorm_f16_dev(h, _p(x), _p(s) if skip else None, _p(g), _p(y), _p(sum_out) if skip else None,
+                                    _p(y16), rows, d, 1e-6))
+    N.check(lib.b2m_synchronize(h))
+    assert torch.equal(y, y_ref)
+    assert torch.equal(y16, y_ref.half())
+    if skip:
+        assert torch.equal(sum_out, sum_ref)
+
+
+@pytest.mark.parametrize("rows,d", [(64, 3072), (2048, 3072)])
+def test_silu_mul_f16_copy(ctx, rows, d):
+    rng = np.random.default_rng(rows)
+    lib, h = ctx.lib, ctx.handle
+    gu = torch.from_numpy(rng.standard_normal((rows, 2 * d)).astype(np.float32)).cuda()
+    y_ref, y = torch.empty((rows, d), device="cuda"), torch.empty((rows, d), device="cuda")
+    y16 = torch.empty((rows, d), device="cuda", dtype=torch.float16)
+    up = ctypes.c_void_p(gu.data_ptr() + d * 4)
+    torch.cuda.synchronize()
+    N.check(lib.b2m_silu_mul_dev(h, _p(gu), up, 2 * d, 2 * d, _p(y_ref), rows, d))
+    N.check(lib.b2m_silu_mul_f16_dev(h, _p(gu), up, 2 * d, 2 * d, _p(y), _p(y16), rows, d))
+    N.check(lib.b2m_synchronize(h))
+    assert torch.equal(y, y_ref)
+    assert torch.equal(y16, y_ref.half())
+
+
+def test_decoder_producer_f16_same_bits(ctx):
+    """Qwen3-0.6B shapes, two layers, 64 sequences: a 32-token prefill (2048
+    rows) and two greedy decode steps (64 rows, the tensor-core route), with
+    and without the producer-written f16 operands: identical logits."""
+    cfg = DecoderConfig.qwen3_0_6b()
+    cfg.layers = 2
+    B, S = 64, 32
+    prompt = np.random.default_rng(3).integers(0, cfg.vocab, (B, S))
+    out = []
+    for pf in (False, True):
+        dec = Int4Decoder(ctx, cfg, batch=B, cap=S + 4, max_prefill=S, seed=11, producer_f16=pf)
+        dec.prefill(prompt)
+        torch.cuda.synchronize()
+        logits = [dec.logits.cpu().numpy().copy()]
+        dec.decode(2)
+        torch.cuda.synchronize()
+        logits.append(dec.logits.cpu().numpy().copy())
+        out.append(logits)
+        del dec
+    for a, b in zip(out[0], out[1]):
+        np.testing.assert_array_equal(a, b)
