@@ -350,6 +350,13 @@ B2M_API b2m_status b2m_layernorm_dev(b2m_ctx *ctx, const float *x, const float *
                                      const float *beta, float *y, float *sum_out, int64_t rows, int64_t d,
                                      double eps);
 
+/* b2m_layernorm_dev that also writes y as the bf16 hi / lo planes of the
+ * FAST fp32 Gemm's A operand into y_planes (rows x d hi values, then rows x d
+ * lo values; d % 64 == 0): the operand of b2m_gemm_f32_split_dev. */
+B2M_API b2m_status b2m_layernorm_split_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma,
+                                           const float *beta, float *y, float *sum_out, uint16_t *y_planes,
+                                           int64_t rows, int64_t d, double eps);
+
 /* y[r][c] = silu(gate[r*gate_rs + c]) * up[r*up_rs + c] for c < d (the
  * Sigmoid/Mul pair of a SwiGLU MLP; gate and up may be the two halves of one
  * packed projection). */
@@ -363,6 +370,21 @@ B2M_API b2m_status b2m_silu_mul_f16_dev(b2m_ctx *ctx, const float *gate, const f
 
 /* erf GELU, y = 0.5 x (1 + erf(x / sqrt 2)) (opGelu, lib/src/onnx_ops.dart:706). */
 B2M_API b2m_status b2m_gelu_dev(b2m_ctx *ctx, const float *x, float *y, int64_t n);
+
+/* erf GELU of rows x d values (d % 64 == 0) written as the bf16 hi / lo planes
+ * of a FAST Gemm's A operand (layout as b2m_layernorm_split_dev), and to y
+ * when y is not NULL; 16-byte aligned pointers. */
+B2M_API b2m_status b2m_gelu_split_dev(b2m_ctx *ctx, const float *x, float *y, uint16_t *y_planes, int64_t rows,
+                                      int64_t d);
+
+/* FAST Gemm y = A . B + bias (B prepacked by b2m_weight_prepack_f32, bias N
+ * floats or NULL) with A given as its bf16 hi / lo planes, as the _split_dev
+ * producers write them (m x roundup(K, 64) hi values, then as many lo values):
+ * bit for bit b2m_gemm_f32 in FAST mode (alpha = beta = 1, C = bias) on the
+ * fp32 rows, without the split pass in front of the GEMM. No counterpart in
+ * the reference (its Gemm reads fp32 rows, onnx_ops.dart:2152). */
+B2M_API b2m_status b2m_gemm_f32_split_dev(b2m_ctx *ctx, const uint16_t *a_planes, int64_t m, const b2m_weight *w,
+                                          const float *bias, float *y);
 
 /* y = a + b over rows x d; with b_broadcast, b is one row of d added to every
  * row (bias). */

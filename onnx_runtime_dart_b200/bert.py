@@ -70,13 +70,18 @@ class BertEncoder:
     the fp32 CUDA-core kernels)."""
 
     def __init__(self, ctx, cfg: BertConfig, batch: int, seq: int, seed: int = 0, mode: int = N.MODE_FAST,
-                 keep_host: bool = False):
+                 keep_host: bool = False, producer_split: bool = True):
         import torch
 
         if seq > cfg.max_pos:
             raise N.ArgumentError("BertEncoder: seq exceeds max_pos")
         self.torch = torch
         self.ctx, self.cfg, self.B, self.S, self.mode = ctx, cfg, batch, seq, mode
+        # producer_split (FAST mode): the LayerNorms and the GELU in front of
+        # the QKV, FFN-up and FFN-down Gemms also write the bf16 hi / lo planes
+        # those Gemms take (the bits of the GEMM's own split), so each runs
+        # without its split pass; the GELU then writes only the planes.
+        self.split = producer_split and mode == N.MODE_FAST and cfg.hidden % 64 == 0 and cfg.inter % 64 == 0
         self.lib = ctx.lib
         c = cfg
         dev = torch.device("cuda", torch.cuda.current_device())
@@ -133,6 +138,10 @@ class BertEncoder:
         self.f = torch.empty((T, I), **f32)
         self.ids = torch.zeros(T, device=dev, dtype=torch.int64)
         self.mask = torch.zeros((batch, seq), **f32)
+        if self.split:  # [2][rows][d] bf16: hi plane, then lo plane
+            self.xs = torch.empty((2, T, H), device=dev, dtype=torch.bfloat16)
+            self.h1s = torch.empty((2, T, H), device=dev, dtype=torch.bfloat16)
+            self.fs = torch.empty((2, T, I), device=dev, dtype=torch.bfloat16)
         w = ctx.wrap
         self.t = dict(x=w(self.x.data_ptr(), (T, H), np.float32), qkv=w(self.qkv.data_ptr(), (T, 3 * H), np.float32),
                       attn=w(self.attn.data_ptr(), (T, H), np.float32), o=w(self.o.data_ptr(), (T, H), np.float32),
@@ -160,26 +169,45 @@ class BertEncoder:
         finally:
             self.ctx.set_attention_mode(N.MODE_FAST)
 
+    def _gemm_split(self, planes, lw, name, y):
+        N.check(self.lib.b2m_gemm_f32_split_dev(self.ctx.handle, _ptr(planes), self.T, lw[name].handle,
+                                                _ptr(lw[name + "_b"]), _ptr(y)))
+
+    def _ln(self, x, skip, g, b, y, planes):
+        c, T = self.cfg, self.T
+        if planes is not None:
+            N.check(self.lib.b2m_layernorm_split_dev(self.ctx.handle, _ptr(x), _ptr(skip), _ptr(g), _ptr(b), _ptr(y),
+                                                     None, _ptr(planes), T, c.hidden, ctypes.c_double(c.eps)))
+        else:
+            N.check(self.lib.b2m_layernorm_dev(self.ctx.handle, _ptr(x), _ptr(skip), _ptr(g), _ptr(b), _ptr(y), None,
+                                               T, c.hidden, ctypes.c_double(c.eps)))
+
     def _layers(self):
         c, lib, h, chk = self.cfg, self.lib, self.ctx.handle, N.check
         T, H, I, D = self.T, c.hidden, c.inter, c.head_dim
+        sp = self.split
         chk(lib.b2m_gather_rows_dev(h, _ptr(self.word), _ptr(self.ids), _ptr(self.o), T, c.vocab, H))
-        chk(lib.b2m_layernorm_dev(h, _ptr(self.o), _ptr(self.pos_type), _ptr(self.emb_g), _ptr(self.emb_b),
-                                  _ptr(self.x), None, T, H, ctypes.c_double(c.eps)))
+        self._ln(self.o, self.pos_type, self.emb_g, self.emb_b, self.x, self.xs if sp else None)
         qkv = self.qkv.data_ptr()
         for lw in self.layers:
-            self._gemm("x", lw, "qkv", "qkv")
+            if sp:
+                self._gemm_split(self.xs, lw, "qkv", self.qkv)
+            else:
+                self._gemm("x", lw, "qkv", "qkv")
             chk(lib.b2m_mha_dev(h, ctypes.c_void_p(qkv), ctypes.c_void_p(qkv + H * 4), ctypes.c_void_p(qkv + 2 * H * 4),
                                 3 * H, 3 * H, _ptr(self.mask), self.S, 0, 0, _ptr(self.attn), self.B, self.S, self.S,
                                 c.heads, c.heads, D, ctypes.c_float(0.0), 0))
             self._gemm("attn", lw, "o", "o")
-            chk(lib.b2m_layernorm_dev(h, _ptr(self.o), _ptr(self.x), _ptr(lw["ln1_g"]), _ptr(lw["ln1_b"]),
-                                      _ptr(self.h1), None, T, H, ctypes.c_double(c.eps)))
-            self._gemm("h1", lw, "ff1", "f")
-            chk(lib.b2m_gelu_dev(h, _ptr(self.f), _ptr(self.f), T * I))
-            self._gemm("f", lw, "ff2", "o")
-            chk(lib.b2m_layernorm_dev(h, _ptr(self.o), _ptr(self.h1), _ptr(lw["ln2_g"]), _ptr(lw["ln2_b"]),
-                                      _ptr(self.x), None, T, H, ctypes.c_double(c.eps)))
+            self._ln(self.o, self.x, lw["ln1_g"], lw["ln1_b"], self.h1, self.h1s if sp else None)
+            if sp:
+                self._gemm_split(self.h1s, lw, "ff1", self.f)
+                chk(lib.b2m_gelu_split_dev(h, _ptr(self.f), None, _ptr(self.fs), T, I))
+                self._gemm_split(self.fs, lw, "ff2", self.o)
+            else:
+                self._gemm("h1", lw, "ff1", "f")
+                chk(lib.b2m_gelu_dev(h, _ptr(self.f), _ptr(self.f), T * I))
+                self._gemm("f", lw, "ff2", "o")
+            self._ln(self.o, self.h1, lw["ln2_g"], lw["ln2_b"], self.x, self.xs if sp else None)
 
     def forward_device(self, use_graph: bool = True):
         """One forward over the ids already in `self.ids`, ordered on torch's

@@ -238,6 +238,9 @@ void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cud
 void launch_f32_tc_b(const F32GemmArgs &p, const void *b_hi, const void *b_lo, int64_t b_rows, void *a_split,
                      cudaStream_t s);
 bool f32_tc_shape_ok(const F32GemmArgs &p);
+// A[M][K] (row stride lda) -> bf16 hi / lo planes [M][kp] (zero padded).
+void launch_f32_split(const float *A, int64_t lda, __nv_bfloat16 *p0, __nv_bfloat16 *p1, int64_t M, int64_t K,
+                      int64_t kp, cudaStream_t s);
 // The same GEMM on operands already split into bf16 planes: A planes (x0 then
 // x1, each [M][f32_tc_kp(K)]) and B planes [b_rows][f32_tc_kp(K)]; p.Y, p.ldy
 // and the Gemm epilogue fields as above. cm_P > 0 selects the channel-major
@@ -359,11 +362,16 @@ void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStre
 void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float *y, float *sum_out, int64_t rows,
                     int D, double eps, int64_t per, int64_t gstride, cudaStream_t s, int64_t gamma_rs = 0,
                     __half *y16 = nullptr);
+// p0 / p1 (optional; D % 64 == 0): the output rows also as the bf16 hi / lo
+// planes a FAST fp32 Gemm takes as its A operand.
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
-                      float *sum_out, int64_t rows, int D, double eps, cudaStream_t s);
+                      float *sum_out, int64_t rows, int D, double eps, cudaStream_t s,
+                      __nv_bfloat16 *p0 = nullptr, __nv_bfloat16 *p1 = nullptr);
 void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
                      int64_t D, cudaStream_t s, __half *y16 = nullptr);
 void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s);
+// GELU into bf16 hi / lo planes (and y when not null); n % 4 == 0, aligned.
+void launch_gelu_split(const float *x, float *y, __nv_bfloat16 *p0, __nv_bfloat16 *p1, int64_t n, cudaStream_t s);
 void launch_add(const float *a, const float *b, float *y, int64_t rows, int64_t D, int b_bcast, cudaStream_t s);
 void launch_gather_rows(const float *table, const int64_t *ids, float *y, int64_t rows, int64_t V, int64_t D,
                         int32_t *err, cudaStream_t s);

@@ -449,6 +449,21 @@ void launch_f32_tc_planes(const F32GemmArgs &p, const void *b_hi, const void *b_
   launch_ft_any(p, b, a0, a1, kp, s);
 }
 
+void launch_f32_split(const float *A, int64_t lda, __nv_bfloat16 *p0, __nv_bfloat16 *p1, int64_t M, int64_t K,
+                      int64_t kp, cudaStream_t s) {
+  const int64_t total = M * (kp / 8);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(device_sm_count() * 8, (total + 255) / 256)));
+  cfg.blockDim = dim3(256);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_split_rows, A, lda, p0, p1, M, K, kp));
+}
+
 void launch_f32_tc(const F32GemmArgs &p, const b2m_weight &w, void *a_split, cudaStream_t s) {
   launch_f32_tc_b(p, w.bx_hi, w.bx_lo, w.n, a_split, s);
 }
@@ -457,19 +472,7 @@ void launch_f32_tc_b(const F32GemmArgs &p, const void *b_hi, const void *b_lo, i
                      cudaStream_t s) {
   const int64_t kp = f32_tc_kp(p.K);
   __nv_bfloat16 *a0 = static_cast<__nv_bfloat16 *>(a_split), *a1 = a0 + p.M * kp;
-  {
-    const int64_t total = p.M * (kp / 8);
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)std::max<int64_t>(1, std::min<int64_t>(device_sm_count() * 8, (total + 255) / 256)));
-    cfg.blockDim = dim3(256);
-    cfg.stream = s;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    B2M_CUDA(cudaLaunchKernelEx(&cfg, f32_split_rows, p.A, p.sa_m, a0, a1, p.M, p.K, kp));
-  }
+  launch_f32_split(p.A, p.sa_m, a0, a1, p.M, p.K, kp, s);
   FtOperandB b;
   b.hi = b_hi;
   b.lo = b_lo;

@@ -116,6 +116,17 @@ __device__ __forceinline__ void store_f16x4(__half *p, float4 v) {
   *reinterpret_cast<uint2 *>(p) = u;
 }
 
+// Four values as bf16 hi / lo planes (split_bf16x2 pairs, the split of
+// f32_split_rows, so a producer's planes equal what the FAST GEMM's own split
+// forms).
+__device__ __forceinline__ void store_split4(__nv_bfloat16 *p0, __nv_bfloat16 *p1, int64_t i, float4 v) {
+  uint2 h, l;
+  b2m::split_bf16x2(v.x, v.y, h.x, l.x);
+  b2m::split_bf16x2(v.z, v.w, h.y, l.y);
+  *reinterpret_cast<uint2 *>(p0 + i) = h;
+  *reinterpret_cast<uint2 *>(p1 + i) = l;
+}
+
 // Warp per row with float4 loads (D % 4 == 0, 16-byte aligned rows): lane
 // takes float4 chunks lane + 32 i. Half the load instructions of the scalar
 // form and twice the bytes per request (BERT LayerNorm 4096 x 768: 6.5 us
@@ -125,7 +136,8 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
                                                          const float *__restrict__ gamma,
                                                          const float *__restrict__ beta, float *y, float *sum_out,
                                                          int64_t rows, int D, double eps, int64_t per,
-                                                         int64_t gstride, int64_t gamma_rs, __half *y16) {
+                                                         int64_t gstride, int64_t gamma_rs, __half *y16,
+                                                         __nv_bfloat16 *p0, __nv_bfloat16 *p1) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -175,6 +187,7 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
                                    (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
       reinterpret_cast<float4 *>(y + off)[j] = o;
       if (y16) store_f16x4(y16 + off + 4 * j, o);
+      if (p0) store_split4(p0, p1, off + 4 * j, o);
     }
   }
 }
@@ -190,7 +203,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
                                                            const float *__restrict__ gamma,
                                                            const float *__restrict__ beta, float *y, float *sum_out,
                                                            int D, double eps, int64_t per, int64_t gstride, int64_t gamma_rs,
-                                                           __half *y16) {
+                                                           __half *y16, __nv_bfloat16 *p0, __nv_bfloat16 *p1) {
   const int64_t r = blockIdx.x;
   const int64_t off = (r / per) * gstride + (r % per) * D;
   const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
@@ -248,6 +261,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
                                    (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
       reinterpret_cast<float4 *>(y + off)[j] = o;
       if (y16) store_f16x4(y16 + off + 4 * j, o);
+      if (p0) store_split4(p0, p1, off + 4 * j, o);
     }
   }
 }
@@ -257,7 +271,8 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
 template <bool LN>
 bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                           float *sum_out, int64_t rows, int D, double eps, int64_t per, int64_t gstride,
-                          int64_t gamma_rs, cudaStream_t s, __half *y16 = nullptr) {
+                          int64_t gamma_rs, cudaStream_t s, __half *y16 = nullptr, __nv_bfloat16 *p0 = nullptr,
+                          __nv_bfloat16 *p1 = nullptr) {
   auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (D % 4 || gstride % 4 || D > 4096 || !al(x) || !al(skip) || !al(gamma) || !al(beta) || !al(y) ||
       !al(sum_out))
@@ -268,7 +283,7 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
     const int v4 = (D / 4 + 31) / 32;
 #define B2M_NW4(N) \
   norm_warp4_kernel<N, LN><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps, per, gstride, \
-                                              gamma_rs, y16)
+                                              gamma_rs, y16, p0, p1)
     if (v4 <= 1) B2M_NW4(1);
     else if (v4 <= 2) B2M_NW4(2);
     else if (v4 <= 4) B2M_NW4(4);
@@ -285,7 +300,8 @@ bool launch_norm_rows_cta(const float *x, const float *skip, const float *gamma,
   const int nv4 = (d4 + nt - 1) / nt;
   const unsigned g = (unsigned)rows;
 #define B2M_NRC(N) \
-  norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride, gamma_rs, y16)
+  norm_row_cta_kernel<N, LN><<<g, nt, 0, s>>>(x, skip, gamma, beta, y, sum_out, D, eps, per, gstride, gamma_rs, y16, \
+                                               p0, p1)
   if (nv4 <= 1) B2M_NRC(1);
   else if (nv4 <= 2) B2M_NRC(2);
   else B2M_NRC(4);
@@ -376,6 +392,23 @@ __global__ void gelu_kernel(const float *__restrict__ x, float *y, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float v = x[i];
     y[i] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
+  }
+}
+
+// GELU of n values (n % 4 == 0, 16-byte aligned) written as bf16 hi / lo
+// planes (and to y when given): the FAST Gemm's A operand for rows of a
+// length that is a multiple of 64 (no padding then).
+__global__ void gelu_split_kernel(const float *__restrict__ x, float *y, __nv_bfloat16 *p0, __nv_bfloat16 *p1,
+                                  int64_t n4) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4 *>(x)[i];
+    float4 o;
+    o.x = 0.5f * v.x * (1.f + erff(v.x * 0.70710678118654752f));
+    o.y = 0.5f * v.y * (1.f + erff(v.y * 0.70710678118654752f));
+    o.z = 0.5f * v.z * (1.f + erff(v.z * 0.70710678118654752f));
+    o.w = 0.5f * v.w * (1.f + erff(v.w * 0.70710678118654752f));
+    if (y) reinterpret_cast<float4 *>(y)[i] = o;
+    store_split4(p0, p1, 4 * i, o);
   }
 }
 
@@ -1695,9 +1728,16 @@ void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float
 }
 
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
-                      float *sum_out, int64_t rows, int D, double eps, cudaStream_t s) {
+                      float *sum_out, int64_t rows, int D, double eps, cudaStream_t s, __nv_bfloat16 *p0,
+                      __nv_bfloat16 *p1) {
   if (rows <= 0) return;
-  if (launch_norm_rows_cta<true>(x, skip, gamma, beta, y, sum_out, rows, D, eps, rows, 0, 0, s)) return;
+  if (launch_norm_rows_cta<true>(x, skip, gamma, beta, y, sum_out, rows, D, eps, rows, 0, 0, s, nullptr, p0, p1))
+    return;
+  if (p0) {  // the fallback kernels write fp32 only: split the rows after them
+    launch_layernorm(x, skip, gamma, beta, y, sum_out, rows, D, eps, s, nullptr, nullptr);
+    ::launch_f32_split(y, D, p0, p1, rows, D, D, s);
+    return;
+  }
   const unsigned g = (unsigned)((rows + 7) / 8);
   const int vpl = (D + 31) / 32;
 #define B2M_LN(V) layernorm_kernel<V><<<g, 256, 0, s>>>(x, skip, gamma, beta, y, sum_out, rows, D, eps)
@@ -1733,6 +1773,12 @@ void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u
 void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s) {
   if (n <= 0) return;
   gelu_kernel<<<grid_for(n, 256), 256, 0, s>>>(x, y, n);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_gelu_split(const float *x, float *y, __nv_bfloat16 *p0, __nv_bfloat16 *p1, int64_t n, cudaStream_t s) {
+  if (n <= 0) return;
+  gelu_split_kernel<<<grid_for(n / 4, 256), 256, 0, s>>>(x, y, p0, p1, n / 4);
   B2M_CUDA(cudaGetLastError());
 }
 

@@ -7,6 +7,7 @@
 // opQLinearMatMul (lib/src/onnx_qlinear_ops.dart:32-108) and opMatMulNBits
 // (:115-228).
 #include <cuda.h>
+#include <cuda_bf16.h>
 
 #include <algorithm>
 #include <cmath>
@@ -1703,6 +1704,19 @@ B2M_API b2m_status b2m_layernorm_dev(b2m_ctx *ctx, const float *x, const float *
   });
 }
 
+B2M_API b2m_status b2m_layernorm_split_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma,
+                                           const float *beta, float *y, float *sum_out, uint16_t *y_planes,
+                                           int64_t rows, int64_t d, double eps) {
+  return guarded([&] {
+    check_ctx(ctx);
+    B2M_REQUIRE(rows >= 0 && d > 0 && d % 64 == 0 && d <= (1 << 24) && (rows == 0 || (x && gamma && y && y_planes)),
+                B2M_ERR_INVALID_ARGUMENT, "LayerNormalization split: bad arguments");
+    DeviceGuard dg(ctx->device);
+    __nv_bfloat16 *p0 = reinterpret_cast<__nv_bfloat16 *>(y_planes);
+    launch_layernorm(x, skip, gamma, beta, y, sum_out, rows, (int)d, eps, ctx->stream, p0, p0 + rows * d);
+  });
+}
+
 B2M_API b2m_status b2m_silu_mul_dev(b2m_ctx *ctx, const float *gate, const float *up, int64_t gate_rs,
                                     int64_t up_rs, float *y, int64_t rows, int64_t d) {
   return guarded([&] {
@@ -1732,6 +1746,59 @@ B2M_API b2m_status b2m_gelu_dev(b2m_ctx *ctx, const float *x, float *y, int64_t 
     B2M_REQUIRE(n >= 0 && (n == 0 || (x && y)), B2M_ERR_INVALID_ARGUMENT, "Gelu: bad arguments");
     DeviceGuard dg(ctx->device);
     launch_gelu(x, y, n, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_gelu_split_dev(b2m_ctx *ctx, const float *x, float *y, uint16_t *y_planes, int64_t rows,
+                                      int64_t d) {
+  return guarded([&] {
+    check_ctx(ctx);
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    B2M_REQUIRE(rows >= 0 && d > 0 && d % 64 == 0 &&
+                    (rows == 0 || (x && y_planes && al(x) && al(y) && al(y_planes))),
+                B2M_ERR_INVALID_ARGUMENT, "Gelu split: bad arguments");
+    DeviceGuard dg(ctx->device);
+    __nv_bfloat16 *p0 = reinterpret_cast<__nv_bfloat16 *>(y_planes);
+    launch_gelu_split(x, y, p0, p0 + rows * d, rows * d, ctx->stream);
+  });
+}
+
+B2M_API b2m_status b2m_gemm_f32_split_dev(b2m_ctx *ctx, const uint16_t *a_planes, int64_t m, const b2m_weight *w,
+                                          const float *bias, float *y) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(w && w->kind == W_F32 && w->bx_hi, B2M_ERR_INVALID_ARGUMENT,
+                "Gemm split: the weight is not an fp32 weight with FAST planes");
+    B2M_REQUIRE(m >= 0 && (m == 0 || (a_planes && y)), B2M_ERR_INVALID_ARGUMENT, "Gemm split: bad pointers");
+    check_cancel(ctx);
+    if (m == 0) return;
+    F32GemmArgs p;
+    p.A = nullptr;
+    p.B = w->f32;
+    p.Y = y;
+    p.M = m;
+    p.N = w->n;
+    p.K = w->k;
+    p.sa_m = w->k;
+    p.sa_k = 1;
+    p.sb_k = w->n;
+    p.sb_n = 1;
+    p.ldy = w->n;
+    p.m_eff = m;
+    p.tile_w = w->n;
+    p.batch = 1;
+    p.epi = EPI_GEMM;
+    if (bias) {
+      p.C = bias;
+      p.c_rs = 0;
+      p.c_cs = 1;
+    }
+    p.dev_err = ctx->dev_err;
+    B2M_REQUIRE(f32_tc_shape_ok(p), B2M_ERR_UNSUPPORTED, "Gemm split: shape not supported by the FAST GEMM");
+    OpTimer timer(ctx);
+    launch_f32_tc_planes(p, w->bx_hi, w->bx_lo, w->n, a_planes, 0, 0, ctx->stream);
+    timer.done();
   });
 }
 

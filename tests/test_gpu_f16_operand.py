@@ -138,3 +138,74 @@ def test_decoder_producer_f16_same_bits(ctx):
         del dec
     for a, b in zip(out[0], out[1]):
         np.testing.assert_array_equal(a, b)
+
+
+# --- the FAST fp32 Gemm's bf16 hi / lo planes written by their producer ---
+
+from onnx_runtime_dart_b200.bert import BertConfig, BertEncoder  # noqa: E402
+
+
+def _gemm_fast(ctx, a, m, k, w, bias, y):
+    """b2m_gemm_f32 FAST, alpha = beta = 1, C = bias (a BERT Gemm)."""
+    at = ctx.wrap(a.data_ptr(), (m, k), np.float32)
+    bt = ctx.wrap(bias.data_ptr(), (bias.numel(),), np.float32)
+    yt = ctx.wrap(y.data_ptr(), tuple(y.shape), np.float32)  # kept alive across the call
+    yh = ctypes.c_void_p(yt.handle.value)
+    N.check(ctx.lib.b2m_gemm_f32(ctx.handle, at.handle, None, w.handle, bt.handle, ctypes.c_float(1.0),
+                                 ctypes.c_float(1.0), 0, 0, N.MODE_FAST, ctypes.byref(yh)))
+    N.check(ctx.lib.b2m_synchronize(ctx.handle))
+
+
+@pytest.mark.parametrize("rows", [128, 4096])
+def test_layernorm_and_gelu_planes_feed_the_gemm_bitwise(ctx, rows):
+    rng = np.random.default_rng(rows)
+    lib, h = ctx.lib, ctx.handle
+    d, n, i = 768, 3072, 3072
+    x = torch.from_numpy(rng.standard_normal((rows, d)).astype(np.float32)).cuda()
+    s = torch.from_numpy(rng.standard_normal((rows, d)).astype(np.float32)).cuda()
+    g = torch.from_numpy((1 + 0.1 * rng.standard_normal(d)).astype(np.float32)).cuda()
+    b = torch.from_numpy((0.1 * rng.standard_normal(d)).astype(np.float32)).cuda()
+    w1 = ctx.prepack_f32((rng.standard_normal((d, n)) / np.sqrt(d)).astype(np.float32))
+    w2 = ctx.prepack_f32((rng.standard_normal((i, d)) / np.sqrt(i)).astype(np.float32))
+    b1 = torch.from_numpy(rng.standard_normal(n).astype(np.float32)).cuda()
+    b2 = torch.from_numpy(rng.standard_normal(d).astype(np.float32)).cuda()
+    y_ref, y = torch.empty((rows, d), device="cuda"), torch.empty((rows, d), device="cuda")
+    planes = torch.empty((2, rows, d), device="cuda", dtype=torch.bfloat16)
+    torch.cuda.synchronize()
+    N.check(lib.b2m_layernorm_dev(h, _p(x), _p(s), _p(g), _p(b), _p(y_ref), None, rows, d, ctypes.c_double(1e-12)))
+    N.check(lib.b2m_layernorm_split_dev(h, _p(x), _p(s), _p(g), _p(b), _p(y), None, _p(planes), rows, d,
+                                        ctypes.c_double(1e-12)))
+    f_ref, f = torch.empty((rows, n), device="cuda"), torch.empty((rows, n), device="cuda")
+    _gemm_fast(ctx, y_ref, rows, d, w1, b1, f_ref)
+    N.check(lib.b2m_gemm_f32_split_dev(h, _p(planes), rows, w1.handle, _p(b1), _p(f)))
+    N.check(lib.b2m_synchronize(h))
+    assert torch.equal(y, y_ref)
+    assert torch.equal(f, f_ref)
+    # GELU: planes only, then the FFN-down Gemm
+    g_ref = torch.empty_like(f_ref)
+    N.check(lib.b2m_gelu_dev(h, _p(f_ref), _p(g_ref), rows * n))
+    gplanes = torch.empty((2, rows, n), device="cuda", dtype=torch.bfloat16)
+    N.check(lib.b2m_gelu_split_dev(h, _p(f), None, _p(gplanes), rows, n))
+    o_ref, o = torch.empty((rows, d), device="cuda"), torch.empty((rows, d), device="cuda")
+    _gemm_fast(ctx, g_ref, rows, i, w2, b2, o_ref)
+    N.check(lib.b2m_gemm_f32_split_dev(h, _p(gplanes), rows, w2.handle, _p(b2), _p(o)))
+    N.check(lib.b2m_synchronize(h))
+    assert torch.equal(o, o_ref)
+    w1.free()
+    w2.free()
+
+
+def test_bert_producer_split_same_bits(ctx):
+    """BERT-base shapes, two layers, 4 x 128 tokens: the encoder with the
+    producer-written planes and with the Gemms' own split pass give the same
+    last hidden state."""
+    cfg = BertConfig.base()
+    cfg.layers = 2
+    ids = np.random.default_rng(9).integers(0, cfg.vocab, (4, 128))
+    outs = []
+    for ps in (False, True):
+        enc = BertEncoder(ctx, cfg, 4, 128, seed=21, producer_split=ps)
+        assert enc.split == ps
+        outs.append(enc.forward(ids, use_graph=False))
+        del enc
+    np.testing.assert_array_equal(outs[0], outs[1])
