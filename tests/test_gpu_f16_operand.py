@@ -209,3 +209,41 @@ def test_bert_producer_split_same_bits(ctx):
         outs.append(enc.forward(ids, use_graph=False))
         del enc
     np.testing.assert_array_equal(outs[0], outs[1])
+
+
+# --- 33..64 rows (the decode projections at 64 sequences) against the oracle ---
+
+import oracle  # noqa: E402
+from tests.conftest import assert_fast_close  # noqa: E402
+
+
+@pytest.mark.parametrize("m,k,n", [(33, 1024, 384), (48, 3072, 1000), (64, 1024, 6144), (64, 2048, 1024)])
+def test_33_to_64_rows_within_fast_contract(ctx, m, k, n):
+    """33..64 rows (the decoder's decode projections at 64 sequences) take
+    the tensor-core route: within the FAST contract of the oracle's
+    opMatMulNBits (onnx_qlinear_ops.dart:208-226) through the fp32 entry,
+    bit for bit the same through the f16 entry and on a second call."""
+    rng = np.random.default_rng(m * 7 + n)
+    nb = k // 32
+    bq = rng.integers(0, 256, (n, nb, 16), dtype=np.uint8)
+    sc = (np.abs(rng.normal(0, 0.02, (n, nb))) + 1e-3).astype(np.float32)
+    zp = rng.integers(0, 256, (n, (nb + 1) // 2), dtype=np.uint8)
+    w = ctx.prepack_nbits(bq, sc, zp, k, n, 4, 32)
+    assert _route(ctx, w, m, N.MODE_FAST) == N.ROUTE_TC_F16
+    lib, h = ctx.lib, ctx.handle
+    a_np = rng.standard_normal((m, k)).astype(np.float32)
+    bias_np = rng.standard_normal(n).astype(np.float32)
+    a = torch.from_numpy(a_np).cuda()
+    bias = torch.from_numpy(bias_np).cuda()
+    y1, y2, y3 = (torch.full((m, n), float("nan"), device="cuda") for _ in range(3))
+    torch.cuda.synchronize()
+    N.check(lib.b2m_matmul_nbits_dev(h, _p(a), m, w.handle, _p(bias), N.MODE_FAST, _p(y1)))
+    N.check(lib.b2m_matmul_nbits_dev(h, _p(a), m, w.handle, _p(bias), N.MODE_FAST, _p(y2)))
+    N.check(lib.b2m_matmul_nbits_f16_dev(h, _p(a.half()), m, w.handle, _p(bias), _p(y3)))
+    N.check(lib.b2m_synchronize(h))
+    got = y1.cpu().numpy()
+    np.testing.assert_array_equal(y2.cpu().numpy(), got)
+    np.testing.assert_array_equal(y3.cpu().numpy(), got)
+    want = oracle.matmul_nbits(a_np, bq, sc, zp, k, n, 32, bias=bias_np, nthreads=8)
+    assert_fast_close(got, want, f"m={m} k={k} n={n}")
+    w.free()
