@@ -22,6 +22,11 @@
 #include "b2m_internal.cuh"
 #include "tc_common.cuh"
 
+// Every glue kernel triggers programmatic dependent launch at entry: the
+// next kernel of the stream, when it is launched that way (the GEMMs and
+// GEMVs are), starts its weight-side prologue under this one and waits for
+// this grid (griddepcontrol.wait) before it reads or writes anything this
+// grid touches.
 namespace {
 
 __device__ __forceinline__ float warp_sum_f(float v) {
@@ -54,6 +59,7 @@ template <int VPL>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *x, const float *skip, const float *__restrict__ gamma,
                                                       float *y, float *sum_out, int64_t rows, int D, double eps,
                                                       int64_t per, int64_t gstride, int64_t gamma_rs) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -80,6 +86,7 @@ template <int VPL>
 __global__ void __launch_bounds__(256) layernorm_kernel(const float *x, const float *skip,
                                                         const float *__restrict__ gamma, const float *__restrict__ beta,
                                                         float *y, float *sum_out, int64_t rows, int D, double eps) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -138,6 +145,7 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
                                                          int64_t rows, int D, double eps, int64_t per,
                                                          int64_t gstride, int64_t gamma_rs, __half *y16,
                                                          __nv_bfloat16 *p0, __nv_bfloat16 *p1) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -204,6 +212,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
                                                            const float *__restrict__ beta, float *y, float *sum_out,
                                                            int D, double eps, int64_t per, int64_t gstride, int64_t gamma_rs,
                                                            __half *y16, __nv_bfloat16 *p0, __nv_bfloat16 *p1) {
+  b2m::pdl_launch_dependents();
   const int64_t r = blockIdx.x;
   const int64_t off = (r / per) * gstride + (r % per) * D;
   const float *gm = gamma + (r % per) * gamma_rs;  // per-row gains (gamma_rs = D) or one row (0)
@@ -315,6 +324,7 @@ __global__ void __launch_bounds__(256) rmsnorm_long_kernel(const float *x, const
                                                            const float *__restrict__ gamma, float *y, float *sum_out,
                                                            int64_t rows, int D, double eps, int64_t per,
                                                            int64_t gstride, int64_t gamma_rs) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -339,6 +349,7 @@ __global__ void __launch_bounds__(256) layernorm_long_kernel(const float *x, con
                                                              const float *__restrict__ gamma,
                                                              const float *__restrict__ beta, float *y, float *sum_out,
                                                              int64_t rows, int D, double eps) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + warp;
   if (r >= rows) return;
@@ -370,6 +381,7 @@ using b2m::silu_times;
 template <bool VEC>
 __global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__restrict__ up, int64_t g_rs,
                                 int64_t u_rs, float *y, int64_t rows, int64_t D, __half *y16) {
+  b2m::pdl_launch_dependents();
   const int64_t step = (int64_t)gridDim.x * blockDim.x;
   for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
     const float *gr = gate + r * g_rs, *ur = up + r * u_rs;
@@ -389,6 +401,7 @@ __global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__r
 }
 
 __global__ void gelu_kernel(const float *__restrict__ x, float *y, int64_t n) {
+  b2m::pdl_launch_dependents();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     const float v = x[i];
     y[i] = 0.5f * v * (1.f + erff(v * 0.70710678118654752f));
@@ -400,6 +413,7 @@ __global__ void gelu_kernel(const float *__restrict__ x, float *y, int64_t n) {
 // length that is a multiple of 64 (no padding then).
 __global__ void gelu_split_kernel(const float *__restrict__ x, float *y, __nv_bfloat16 *p0, __nv_bfloat16 *p1,
                                   int64_t n4) {
+  b2m::pdl_launch_dependents();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     const float4 v = reinterpret_cast<const float4 *>(x)[i];
     float4 o;
@@ -415,6 +429,7 @@ __global__ void gelu_split_kernel(const float *__restrict__ x, float *y, __nv_bf
 // y = a + b, b broadcast over rows when b_rows == 1.
 __global__ void add_kernel(const float *__restrict__ a, const float *__restrict__ b, float *y, int64_t rows, int64_t D,
                            int b_bcast) {
+  b2m::pdl_launch_dependents();
   const int64_t total = rows * D;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x)
     y[i] = a[i] + b[b_bcast ? i % D : i];
@@ -424,6 +439,7 @@ __global__ void add_kernel(const float *__restrict__ a, const float *__restrict_
 // raise the error word.
 __global__ void gather_rows_kernel(const float *__restrict__ table, const int64_t *__restrict__ ids, float *y,
                                    int64_t rows, int64_t V, int64_t D, int32_t *err) {
+  b2m::pdl_launch_dependents();
   const int64_t r = blockIdx.x;
   if (r >= rows) return;
   const int64_t id = ids[r];
@@ -544,6 +560,7 @@ __global__ void __launch_bounds__(256) rotary_kernel(const float *__restrict__ x
                                                      const float *cos, const float *sin, int half, int max_pos,
                                                      float *y, int64_t y_rs, int B, int S, int heads, int D, int rot,
                                                      int interleaved, int32_t *err) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * 8 + warp;
   if (item >= (int64_t)B * S * heads) return;
@@ -593,6 +610,7 @@ struct GqaArgs {
 // Appends this call's keys / values to the cache (rotary on K), one warp per
 // (token, kv head).
 __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t item = (int64_t)blockIdx.x * 8 + warp;
   const int64_t total = (int64_t)a.B * a.S * a.KVH;
@@ -626,6 +644,7 @@ __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
 // registers across lanes, online softmax over the keys, fp32 accumulation of
 // P.V in registers (D <= 256, 8 values per lane).
 __global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
+  b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int h = blockIdx.y, b = blockIdx.z;
   const int s = blockIdx.x * 8 + warp;
@@ -686,6 +705,7 @@ __global__ void __launch_bounds__(256) gqa_attend_kernel(const GqaArgs a) {
 // from the cache. Key tiles past the last visible key are skipped.
 template <int D>
 __global__ void __launch_bounds__(256) gqa_prefill_kernel(const GqaArgs a) {
+  b2m::pdl_launch_dependents();
   constexpr int QT = 64, KT = 64, LD = 68, CPT = D / 16;
   extern __shared__ __align__(16) float fsm[];
   float *Qt = fsm;            // [D][LD], Qt[d][r]
@@ -855,6 +875,7 @@ __device__ __forceinline__ void warp_allreduce8(float (&v)[8]) {
 template <int D, int G>
 __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float *pm, float *pl, float *po,
                                                          uint32_t *counters) {
+  b2m::pdl_launch_dependents();
   constexpr int VPD = D / 32, KB = 8 / G;
   static_assert(D % 32 == 0 && D <= 128 && KB * G == 8, "decode kernel shape");
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1029,6 +1050,7 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
 // Merges the key-split states of gqa_decode_kernel in split order.
 __global__ void gqa_decode_combine_kernel(const float *pm, const float *pl, const float *po, float *out, int H, int D,
                                           int nsplit) {
+  b2m::pdl_launch_dependents();
   const int h = blockIdx.x, b = blockIdx.y;
   const int64_t base = ((int64_t)b * H + h) * nsplit;
   float M = -INFINITY;
@@ -1133,6 +1155,7 @@ __device__ __forceinline__ void mtc_stage_rows(uint8_t *smem, uint32_t off_h, ui
 // column block w / 4: 32 of the 128 score columns, 16 of the 64 output
 // columns; row max and sum combine the four column blocks in shared memory.
 __global__ void __launch_bounds__(512) mha_tc_kernel(const GqaArgs a) {
+  b2m::pdl_launch_dependents();
   extern __shared__ uint8_t mtc_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(mtc_raw) + 1023) & ~(uintptr_t)1023);
   float *mrow = reinterpret_cast<float *>(smem + MTC_MASK);
@@ -1349,6 +1372,7 @@ struct FaLayout {
 
 template <int D>
 __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
+  b2m::pdl_launch_dependents();
   using L = FaLayout<D>;
   constexpr int DW = D / 4;  // output columns per thread
   extern __shared__ uint8_t fa_raw[];
