@@ -117,3 +117,35 @@ def test_host_call_with_library_pinned_buffers(ctx):
         N.check(lib.b2m_host_free(h, pa))
         N.check(lib.b2m_host_free(h, py))
         w.free()
+
+
+@pytest.mark.parametrize("m", [1, 96])
+def test_host_call_behind_queued_device_work(ctx, m):
+    """A host-buffer call enqueued right behind device work still in flight on
+    the same stream (a GEMV that lets the next kernel launch early) computes on
+    its own A: the copy of A is ordered before the kernel that reads it."""
+    rng = np.random.default_rng(77 + m)
+    k, n = 1024, 3072
+    w = _weight(ctx, rng, k, n)
+    lib, h = ctx.lib, ctx.handle
+    a_list = [rng.standard_normal((m, k)).astype(np.float32) for _ in range(2)]
+    want = []
+    for a in a_list:
+        a_d = torch.from_numpy(a).cuda()
+        y_d = torch.empty((m, n), device="cuda")
+        torch.cuda.synchronize()
+        N.check(lib.b2m_matmul_nbits_dev(h, _p(a_d), m, w.handle, None, N.MODE_FAST, _p(y_d)))
+        N.check(lib.b2m_synchronize(h))
+        want.append(y_d.cpu().numpy())
+    a0_d = torch.from_numpy(a_list[0]).cuda()
+    y0_d = torch.empty((m, n), device="cuda")
+    a1_pin = torch.from_numpy(a_list[1]).pin_memory()
+    y1_pin = torch.empty((m, n)).pin_memory()
+    torch.cuda.synchronize()
+    for _ in range(20):
+        for _ in range(8):  # queued work that triggers its successors early
+            N.check(lib.b2m_matmul_nbits_dev(h, _p(a0_d), m, w.handle, None, N.MODE_FAST, _p(y0_d)))
+        N.check(lib.b2m_matmul_nbits_host(h, _p(a1_pin), m, w.handle, None, N.MODE_FAST, _p(y1_pin)))
+        np.testing.assert_array_equal(y1_pin.numpy(), want[1])
+    np.testing.assert_array_equal(y0_d.cpu().numpy(), want[0])
+    w.free()
