@@ -416,6 +416,15 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
                                int32_t rotary_dim, int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h,
                                int32_t kvh, int32_t head_dim, int32_t cap, float scale);
 
+/* b2m_gqa_dev that also writes the attention output as f16 (round to
+ * nearest) into out16 ([b*s][h*head_dim], h*head_dim % 8 == 0): the operand of
+ * b2m_matmul_nbits_f16_dev for the output projection. */
+B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                                   int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
+                                   const float *cos_cache, const float *sin_cache, int32_t rotary_half,
+                                   int32_t rotary_dim, int32_t interleaved, float *out, uint16_t *out16, int32_t b,
+                                   int32_t s, int32_t h, int32_t kvh, int32_t head_dim, int32_t cap, float scale);
+
 /* MultiHeadAttention over projected rows (opMultiHeadAttention,
  * lib/src/onnx_ops.dart:2019; the scale + mask + softmax between the two
  * batched MatMuls of opFusedSDPA, :2106-2148). q: [b][s] rows of h*head_dim

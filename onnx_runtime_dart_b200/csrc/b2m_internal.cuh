@@ -386,7 +386,8 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP);
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s);
+                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s,
+                __half *out16 = nullptr);
 // `counters` (B * KVH zeroed words, or null): the last split CTA of each (kv
 // head, sequence) merges the key splits itself, instead of a separate
 // combine launch; the words are zero again when the call completes.

@@ -605,6 +605,9 @@ struct GqaArgs {
   // at mask[b*mask_bs + h*mask_hs + s*mask_qs + j] (0 strides broadcast).
   const float *mask;
   int64_t mask_bs, mask_hs, mask_qs;
+  // Optional f16 copy of `out` (round to nearest), the operand of the output
+  // projection's tensor-core GEMM.
+  __half *out16 = nullptr;
 };
 
 // Appends this call's keys / values to the cache (rotary on K), one warp per
@@ -1006,7 +1009,9 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
     }
     const int h = kvh * G + g;
     if (nsplit == 1) {
-      a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = O / L;
+      const float ov = O / L;
+      a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
+      if (a.out16) a.out16[(int64_t)b * (int64_t)a.H * D + h * D + d] = __float2half_rn(ov);
     } else {
       const int64_t slot = ((int64_t)b * a.H + h) * nsplit + sp;
       if (d == 0) {
@@ -1040,7 +1045,9 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
           L += __ldcg(pl + base + s2) * f;
           O += __ldcg(po + (base + s2) * D + d) * f;
         }
-        a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = O / L;
+        const float ov = O / L;
+      a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
+      if (a.out16) a.out16[(int64_t)b * (int64_t)a.H * D + h * D + d] = __float2half_rn(ov);
       }
       if (threadIdx.x == 0) counters[(int64_t)b * a.KVH + kvh] = 0u;
     }
@@ -1701,10 +1708,14 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
   }
   if (ok && q0 + r < a.S) {
     const float inv = 1.f / l;
-    float *dst = a.out + (int64_t)(b * a.S + q0 + r) * a.H * D + h * D + cb * DW;
+    const int64_t off = (int64_t)(b * a.S + q0 + r) * a.H * D + h * D + cb * DW;
+    float *dst = a.out + off;
 #pragma unroll
-    for (int c = 0; c < DW; c += 4)
-      *reinterpret_cast<float4 *>(dst + c) = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+    for (int c = 0; c < DW; c += 4) {
+      const float4 v4 = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
+      *reinterpret_cast<float4 *>(dst + c) = v4;
+      if (a.out16) store_f16x4(a.out16 + off + c, v4);
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -1867,6 +1878,7 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
                           cudaStream_t s) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
+  bool wrote16 = false;  // the kernel wrote a.out16 itself
   if (decode_shape(a)) {
     if (!split_part) nsplit = 1;
     dim3 grid((unsigned)a.KVH, (unsigned)a.B, (unsigned)nsplit);
@@ -1882,8 +1894,11 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
     B2M_CUDA(cudaGetLastError());
     if (nsplit > 1 && !counters) {
       gqa_decode_combine_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 128, 0, s>>>(pm, pl, po, a.out, a.H, D, nsplit);
+    } else {
+      wrote16 = true;
     }
   } else if (!exact && fa_tc_shape(a)) {
+    wrote16 = true;
     if (D == 128) {
       b2m::set_smem_limit_once<fa_tc_kernel<128>>((int)FaLayout<128>::BYTES);
       fa_tc_kernel<128><<<dim3((unsigned)((a.S + 127) / 128), (unsigned)a.H, (unsigned)a.B), 512,
@@ -1922,6 +1937,8 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
     gqa_attend_kernel<<<grid, 256, 0, s>>>(a);
   }
   B2M_CUDA(cudaGetLastError());
+  if (a.out16 && !wrote16)  // the other kernels write fp32 only: round after them
+    b2m::launch_f32_to_f16(a.out, a.out16, (int64_t)a.B * a.S, (int64_t)a.H * D, (int64_t)a.H * D, 0, s);
 }
 
 // Key splits of the decode kernel: enough CTAs for two per SM, at least 128
@@ -1935,9 +1952,10 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP) {
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s) {
+                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s, __half *out16) {
   GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
             B, S, H, KVH, D, CAP, scale, err};
+  a.out16 = out16;
   a.kc_rs = D;
   a.kc_hs = (int64_t)CAP * D;
   a.kc_bs = (int64_t)KVH * CAP * D;

@@ -1838,11 +1838,11 @@ B2M_API b2m_status b2m_argmax_dev(b2m_ctx *ctx, const float *x, int64_t *out, in
   });
 }
 
-B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
-                               int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
-                               const float *cos_cache, const float *sin_cache, int32_t rotary_half,
-                               int32_t rotary_dim, int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h,
-                               int32_t kvh, int32_t head_dim, int32_t cap, float scale) {
+static b2m_status gqa_impl(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                           int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
+                           const float *cos_cache, const float *sin_cache, int32_t rotary_half, int32_t rotary_dim,
+                           int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h, int32_t kvh,
+                           int32_t head_dim, int32_t cap, float scale, uint16_t *out16) {
   return guarded([&] {
     check_ctx(ctx);
     B2M_REQUIRE(b >= 0 && s >= 0 && h > 0 && kvh > 0 && h % kvh == 0 && head_dim > 0 && head_dim <= 256 && cap > 0,
@@ -1851,6 +1851,8 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
                 "GroupQueryAttention: row strides too small");
     B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && k_cache && v_cache && past && out), B2M_ERR_INVALID_ARGUMENT,
                 "GroupQueryAttention: null pointer");
+    B2M_REQUIRE(!out16 || ((int64_t)h * head_dim) % 8 == 0, B2M_ERR_INVALID_ARGUMENT,
+                "GroupQueryAttention f16: h * head_dim must be a multiple of 8");
     const bool rot = cos_cache != nullptr;
     B2M_REQUIRE(!rot || (sin_cache && rotary_half > 0 && rotary_dim > 0 && rotary_dim <= head_dim &&
                          rotary_dim % 2 == 0 && rotary_dim / 2 <= rotary_half),
@@ -1878,8 +1880,30 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
     }
     launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
                interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit,
-               ctx->attn_exact, counters, ctx->stream);
+               ctx->attn_exact, counters, ctx->stream, reinterpret_cast<__half *>(out16));
   });
+}
+
+B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                               int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
+                               const float *cos_cache, const float *sin_cache, int32_t rotary_half,
+                               int32_t rotary_dim, int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h,
+                               int32_t kvh, int32_t head_dim, int32_t cap, float scale) {
+  return gqa_impl(ctx, q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
+                  interleaved, out, b, s, h, kvh, head_dim, cap, scale, nullptr);
+}
+
+B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                                   int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
+                                   const float *cos_cache, const float *sin_cache, int32_t rotary_half,
+                                   int32_t rotary_dim, int32_t interleaved, float *out, uint16_t *out16, int32_t b,
+                                   int32_t s, int32_t h, int32_t kvh, int32_t head_dim, int32_t cap, float scale) {
+  if (!out16) {
+    b2m_set_last_error("GroupQueryAttention f16: out16 is null");
+    return B2M_ERR_INVALID_ARGUMENT;
+  }
+  return gqa_impl(ctx, q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
+                  interleaved, out, b, s, h, kvh, head_dim, cap, scale, out16);
 }
 
 B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,

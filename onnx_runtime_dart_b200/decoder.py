@@ -148,6 +148,7 @@ class Int4Decoder:
         if self.fused and producer_f16:
             self.h16 = torch.empty((t, c.hidden), device=dev, dtype=torch.float16)
             self.act16 = torch.empty((t, c.inter), device=dev, dtype=torch.float16)
+            self.attn16 = torch.empty((t, c.heads * c.head_dim), device=dev, dtype=torch.float16)
         self.down = torch.empty((t, c.hidden), **f32)
         self.last = torch.empty((batch, c.hidden), **f32)
         self.logits = torch.empty((batch, c.vocab), **f32)
@@ -406,6 +407,7 @@ class Int4Decoder:
         q_off, k_off, v_off = 0, c.heads * D * 4, (c.heads + c.kv_heads) * D * 4
         for li, lw in enumerate(self.layers):
             qkv16 = self.fused and self._f16_input(lw["qkv"], T)
+            o16 = self.fused and self._f16_input(lw["o"], T)
             gu16 = self.fused and self._f16_input(lw["gate_up"], T)
             dn16 = self.fused and self._f16_input(lw["down"], T)
             if li == 0:
@@ -433,14 +435,20 @@ class Int4Decoder:
                                               c.heads, D, q_rs, c.eps))
                 chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(kp), _ptr(lw["k_norm"]), ctypes.c_void_p(kp), T,
                                               c.kv_heads, D, kv_rs, c.eps))
-            chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
-                                _ptr(self.kcache[li]),
-                                _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D, 0,
-                                _ptr(self.attn), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
+            if o16:  # the attention also writes the o projection's f16 operand
+                chk(lib.b2m_gqa_f16_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
+                                        _ptr(self.kcache[li]), _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos),
+                                        _ptr(self.sin), D // 2, D, 0, _ptr(self.attn), _ptr(self.attn16), self.B, seq,
+                                        c.heads, c.kv_heads, D, self.cap, 0.0))
+            else:
+                chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
+                                    _ptr(self.kcache[li]),
+                                    _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D,
+                                    0, _ptr(self.attn), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
             if self.session is not None:
                 self._dispatch_proj("o", lw, self.attn, T, self.o)
             else:
-                chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.attn), T, lw["o"].handle, None, self.mode, _ptr(self.o)))
+                self._proj(lw["o"], T, o16, self.attn, getattr(self, "attn16", None), self.o)
             self._norm(self.o, _ptr(self.res), lw["mlp_norm"], _ptr(self.res), T, gu16)
             if self.fused:
                 self._proj(lw["gate_up"], T, gu16, self.h, getattr(self, "h16", None), self.gu)

@@ -247,3 +247,41 @@ def test_33_to_64_rows_within_fast_contract(ctx, m, k, n):
     want = oracle.matmul_nbits(a_np, bq, sc, zp, k, n, 32, bias=bias_np, nthreads=8)
     assert_fast_close(got, want, f"m={m} k={k} n={n}")
     w.free()
+
+
+@pytest.mark.parametrize("b,s,past,D", [(64, 1, 300, 128), (2, 512, 0, 128), (3, 5, 7, 96)])
+def test_gqa_f16_copy(ctx, b, s, past, D):
+    """b2m_gqa_f16_dev: the same fp32 output as b2m_gqa_dev and its f16 copy
+    equal to rounding it (decode with key splits, the tensor-core prefill, and
+    a head_dim the tensor-core kernel does not take: the CUDA-core kernel plus
+    a rounding pass)."""
+    rng = np.random.default_rng(b * 1000 + s)
+    lib, h = ctx.lib, ctx.handle
+    H, KVH, cap = 16, 8, 640
+    q = torch.from_numpy(rng.standard_normal((b * s, H * D)).astype(np.float32)).cuda()
+    k = torch.from_numpy(rng.standard_normal((b * s, KVH * D)).astype(np.float32)).cuda()
+    v = torch.from_numpy(rng.standard_normal((b * s, KVH * D)).astype(np.float32)).cuda()
+    cache0 = torch.from_numpy(rng.standard_normal((b, KVH, cap, D)).astype(np.float32)).cuda()
+    half = D // 2
+    inv = 1.0 / (10000.0 ** (np.arange(half) * 2.0 / D))
+    ang = np.arange(cap)[:, None] * inv[None, :]
+    cos = torch.from_numpy(np.cos(ang).astype(np.float32)).cuda()
+    sin = torch.from_numpy(np.sin(ang).astype(np.float32)).cuda()
+    outs = []
+    for f16 in (False, True):
+        kc, vc = cache0.clone(), cache0.clone()
+        past_t = torch.full((b,), past, dtype=torch.int32, device="cuda")
+        out = torch.full((b * s, H * D), float("nan"), device="cuda")
+        out16 = torch.empty((b * s, H * D), device="cuda", dtype=torch.float16)
+        torch.cuda.synchronize()
+        args = [h, _p(q), _p(k), _p(v), H * D, KVH * D, _p(kc), _p(vc), _p(past_t), _p(cos), _p(sin), half, D, 0,
+                _p(out)]
+        tail = [b, s, H, KVH, D, cap, ctypes.c_float(0.0)]
+        if f16:
+            N.check(lib.b2m_gqa_f16_dev(*args, _p(out16), *tail))
+        else:
+            N.check(lib.b2m_gqa_dev(*args, *tail))
+        N.check(lib.b2m_synchronize(h))
+        outs.append((out, out16))
+    assert torch.equal(outs[1][0], outs[0][0])
+    assert torch.equal(outs[1][1], outs[0][0].half())
