@@ -442,6 +442,16 @@ B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, con
                                float *out, int32_t b, int32_t s, int32_t t, int32_t h, int32_t kvh, int32_t head_dim,
                                float scale, int32_t causal);
 
+/* b2m_mha_dev that also writes the attention output as the bf16 hi / lo
+ * planes of a FAST Gemm's A operand into out_planes ([b*s][h*head_dim] hi
+ * values, then as many lo values; h*head_dim % 64 == 0): the operand of
+ * b2m_gemm_f32_split_dev for the output projection. */
+B2M_API b2m_status b2m_mha_split_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                                     int64_t kv_rs, const float *mask, int64_t mask_bs, int64_t mask_hs,
+                                     int64_t mask_qs, float *out, uint16_t *out_planes, int32_t b, int32_t s,
+                                     int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale,
+                                     int32_t causal);
+
 /* DynamicQuantizeLinear (opDynamicQuantizeLinear, lib/src/onnx_ops.dart:3556):
  * uint8 y[n] from float x[n] with the range's scale (float, written to
  * *scale) and zero point (uint8, *zero_point), all device memory, bit-exact

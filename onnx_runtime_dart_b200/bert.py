@@ -142,6 +142,7 @@ class BertEncoder:
             self.xs = torch.empty((2, T, H), device=dev, dtype=torch.bfloat16)
             self.h1s = torch.empty((2, T, H), device=dev, dtype=torch.bfloat16)
             self.fs = torch.empty((2, T, I), device=dev, dtype=torch.bfloat16)
+            self.attns = torch.empty((2, T, H), device=dev, dtype=torch.bfloat16)
         w = ctx.wrap
         self.t = dict(x=w(self.x.data_ptr(), (T, H), np.float32), qkv=w(self.qkv.data_ptr(), (T, 3 * H), np.float32),
                       attn=w(self.attn.data_ptr(), (T, H), np.float32), o=w(self.o.data_ptr(), (T, H), np.float32),
@@ -194,10 +195,16 @@ class BertEncoder:
                 self._gemm_split(self.xs, lw, "qkv", self.qkv)
             else:
                 self._gemm("x", lw, "qkv", "qkv")
-            chk(lib.b2m_mha_dev(h, ctypes.c_void_p(qkv), ctypes.c_void_p(qkv + H * 4), ctypes.c_void_p(qkv + 2 * H * 4),
-                                3 * H, 3 * H, _ptr(self.mask), self.S, 0, 0, _ptr(self.attn), self.B, self.S, self.S,
-                                c.heads, c.heads, D, ctypes.c_float(0.0), 0))
-            self._gemm("attn", lw, "o", "o")
+            q_, k_, v_ = ctypes.c_void_p(qkv), ctypes.c_void_p(qkv + H * 4), ctypes.c_void_p(qkv + 2 * H * 4)
+            if sp:  # the attention also writes the O Gemm's planes
+                chk(lib.b2m_mha_split_dev(h, q_, k_, v_, 3 * H, 3 * H, _ptr(self.mask), self.S, 0, 0, _ptr(self.attn),
+                                          _ptr(self.attns), self.B, self.S, self.S, c.heads, c.heads, D,
+                                          ctypes.c_float(0.0), 0))
+                self._gemm_split(self.attns, lw, "o", self.o)
+            else:
+                chk(lib.b2m_mha_dev(h, q_, k_, v_, 3 * H, 3 * H, _ptr(self.mask), self.S, 0, 0, _ptr(self.attn), self.B,
+                                    self.S, self.S, c.heads, c.heads, D, ctypes.c_float(0.0), 0))
+                self._gemm("attn", lw, "o", "o")
             self._ln(self.o, self.x, lw["ln1_g"], lw["ln1_b"], self.h1, self.h1s if sp else None)
             if sp:
                 self._gemm_split(self.h1s, lw, "ff1", self.f)

@@ -395,7 +395,8 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
 // kernels); with nsplit = 1 every sequence's result is independent of the batch.
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
                 int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
-                int D, float scale, int causal, int32_t *err, bool exact, cudaStream_t s);
+                int D, float scale, int causal, int32_t *err, bool exact, cudaStream_t s,
+                __nv_bfloat16 *planes = nullptr);
 void launch_advance_positions(int32_t *past, int n, int delta, cudaStream_t s);
 void launch_rotary(const float *x, int64_t x_rs, const int64_t *pos, int pos_per_batch, const float *cos,
                    const float *sin, int half, int max_pos, float *y, int64_t y_rs, int B, int S, int heads, int D,

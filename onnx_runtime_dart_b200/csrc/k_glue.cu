@@ -606,8 +606,10 @@ struct GqaArgs {
   const float *mask;
   int64_t mask_bs, mask_hs, mask_qs;
   // Optional f16 copy of `out` (round to nearest), the operand of the output
-  // projection's tensor-core GEMM.
+  // projection's tensor-core GEMM, and optional bf16 hi / lo planes of `out`
+  // (row stride H*D), the A operand of a FAST fp32 Gemm.
   __half *out16 = nullptr;
+  __nv_bfloat16 *p0 = nullptr, *p1 = nullptr;
 };
 
 // Appends this call's keys / values to the cache (rotary on K), one warp per
@@ -1321,7 +1323,12 @@ __global__ void __launch_bounds__(512) mha_tc_kernel(const GqaArgs a) {
   if (ok_o) {
     for (int it = tid; it < 128 * MTC_D; it += 512) {
       const int q = it >> 6, d = it & 63;
-      if (q < S) a.out[((int64_t)b * S + q) * (int64_t)a.H * MTC_D + h * MTC_D + d] = st[q * 65 + d];
+      if (q < S) {
+        const int64_t idx = ((int64_t)b * S + q) * (int64_t)a.H * MTC_D + h * MTC_D + d;
+        const float x = st[q * 65 + d];
+        a.out[idx] = x;
+        if (a.p0) b2m::split_bf16(x, a.p0[idx], a.p1[idx]);
+      }
     }
   }
   tc_fence_before();
@@ -1878,7 +1885,7 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
                           cudaStream_t s) {
   const int D = a.D, G = a.H / a.KVH;
   const bool dok = D == 32 || D == 64 || D == 96 || D == 128;
-  bool wrote16 = false;  // the kernel wrote a.out16 itself
+  bool wrote16 = false, wrote_planes = false;  // the kernel wrote a.out16 / a.p0, a.p1 itself
   if (decode_shape(a)) {
     if (!split_part) nsplit = 1;
     dim3 grid((unsigned)a.KVH, (unsigned)a.B, (unsigned)nsplit);
@@ -1909,6 +1916,7 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
                          FaLayout<64>::BYTES, s>>>(a);
     }
   } else if (!exact && mha_tc_shape(a)) {
+    wrote_planes = true;
     b2m::set_smem_limit_once<mha_tc_kernel>((int)MTC_BYTES);
     mha_tc_kernel<<<dim3((unsigned)a.H, (unsigned)a.B), 512, MTC_BYTES, s>>>(a);
   } else if (dok) {
@@ -1939,6 +1947,8 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
   B2M_CUDA(cudaGetLastError());
   if (a.out16 && !wrote16)  // the other kernels write fp32 only: round after them
     b2m::launch_f32_to_f16(a.out, a.out16, (int64_t)a.B * a.S, (int64_t)a.H * D, (int64_t)a.H * D, 0, s);
+  if (a.p0 && !wrote_planes)
+    ::launch_f32_split(a.out, (int64_t)a.H * D, a.p0, a.p1, (int64_t)a.B * a.S, (int64_t)a.H * D, (int64_t)a.H * D, s);
 }
 
 // Key splits of the decode kernel: enough CTAs for two per SM, at least 128
@@ -1971,9 +1981,13 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
 
 void launch_mha(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, const float *mask,
                 int64_t mask_bs, int64_t mask_hs, int64_t mask_qs, float *out, int B, int S, int T, int H, int KVH,
-                int D, float scale, int causal, int32_t *err, bool exact, cudaStream_t s) {
+                int D, float scale, int causal, int32_t *err, bool exact, cudaStream_t s, __nv_bfloat16 *planes) {
   GqaArgs a{q, k, v, q_rs, kv_rs, const_cast<float *>(k), const_cast<float *>(v), nullptr, nullptr, nullptr, 0, 0,
             0, out, B, S, H, KVH, D, T, scale, err};
+  if (planes) {
+    a.p0 = planes;
+    a.p1 = planes + (int64_t)B * S * H * D;
+  }
   a.kc_rs = kv_rs;
   a.kc_hs = D;
   a.kc_bs = (int64_t)T * kv_rs;

@@ -1906,10 +1906,10 @@ B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k,
                   interleaved, out, b, s, h, kvh, head_dim, cap, scale, out16);
 }
 
-B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+static b2m_status mha_impl(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
                                int64_t kv_rs, const float *mask, int64_t mask_bs, int64_t mask_hs, int64_t mask_qs,
                                float *out, int32_t b, int32_t s, int32_t t, int32_t h, int32_t kvh, int32_t head_dim,
-                               float scale, int32_t causal) {
+                               float scale, int32_t causal, uint16_t *planes) {
   return guarded([&] {
     check_ctx(ctx);
     B2M_REQUIRE(b >= 0 && s >= 0 && t > 0 && h > 0 && kvh > 0 && h % kvh == 0 && head_dim > 0 && head_dim <= 256,
@@ -1921,12 +1921,35 @@ B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, con
     B2M_REQUIRE(!causal || s <= t, B2M_ERR_INVALID_ARGUMENT, "MultiHeadAttention: causal needs s <= t");
     B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && out), B2M_ERR_INVALID_ARGUMENT,
                 "MultiHeadAttention: null pointer");
+    B2M_REQUIRE(!planes || ((int64_t)h * head_dim) % 64 == 0, B2M_ERR_INVALID_ARGUMENT,
+                "MultiHeadAttention split: h * head_dim must be a multiple of 64");
     DeviceGuard dg(ctx->device);
     if ((int64_t)b * s == 0) return;
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
     launch_mha(q, k, v, q_rs, kv_rs, mask, mask_bs, mask_hs, mask_qs, out, b, s, t, h, kvh, head_dim, sc,
-               causal ? 1 : 0, ctx->dev_err, ctx->attn_exact, ctx->stream);
+               causal ? 1 : 0, ctx->dev_err, ctx->attn_exact, ctx->stream, reinterpret_cast<__nv_bfloat16 *>(planes));
   });
+}
+
+B2M_API b2m_status b2m_mha_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                               int64_t kv_rs, const float *mask, int64_t mask_bs, int64_t mask_hs, int64_t mask_qs,
+                               float *out, int32_t b, int32_t s, int32_t t, int32_t h, int32_t kvh, int32_t head_dim,
+                               float scale, int32_t causal) {
+  return mha_impl(ctx, q, k, v, q_rs, kv_rs, mask, mask_bs, mask_hs, mask_qs, out, b, s, t, h, kvh, head_dim, scale,
+                  causal, nullptr);
+}
+
+B2M_API b2m_status b2m_mha_split_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
+                                     int64_t kv_rs, const float *mask, int64_t mask_bs, int64_t mask_hs,
+                                     int64_t mask_qs, float *out, uint16_t *out_planes, int32_t b, int32_t s,
+                                     int32_t t, int32_t h, int32_t kvh, int32_t head_dim, float scale,
+                                     int32_t causal) {
+  if (!out_planes) {
+    b2m_set_last_error("MultiHeadAttention split: out_planes is null");
+    return B2M_ERR_INVALID_ARGUMENT;
+  }
+  return mha_impl(ctx, q, k, v, q_rs, kv_rs, mask, mask_bs, mask_hs, mask_qs, out, b, s, t, h, kvh, head_dim, scale,
+                  causal, out_planes);
 }
 
 B2M_API b2m_status b2m_dynamic_quantize_linear_dev(b2m_ctx *ctx, const float *x, int64_t n, uint8_t *y,

@@ -285,3 +285,34 @@ def test_gqa_f16_copy(ctx, b, s, past, D):
         outs.append((out, out16))
     assert torch.equal(outs[1][0], outs[0][0])
     assert torch.equal(outs[1][1], outs[0][0].half())
+
+
+@pytest.mark.parametrize("b,s,heads,D", [(4, 128, 12, 64), (2, 40, 8, 96)])
+def test_mha_split_planes(ctx, b, s, heads, D):
+    """b2m_mha_split_dev: the same fp32 output as b2m_mha_dev and planes that
+    feed the FAST Gemm to the bits of the Gemm's own split (the tensor-core MHA
+    at BERT's shape, and a head_dim it does not take: a split pass after)."""
+    rng = np.random.default_rng(s + heads)
+    lib, h = ctx.lib, ctx.handle
+    H = heads * D
+    qkv = torch.from_numpy(rng.standard_normal((b * s, 3 * H)).astype(np.float32)).cuda()
+    mask = torch.zeros((b, s), device="cuda")
+    mask[0, s - 3:] = -10000.0
+    w = ctx.prepack_f32((rng.standard_normal((H, 256)) / np.sqrt(H)).astype(np.float32))
+    bias = torch.from_numpy(rng.standard_normal(256).astype(np.float32)).cuda()
+    out_ref, out = torch.empty((b * s, H), device="cuda"), torch.empty((b * s, H), device="cuda")
+    planes = torch.empty((2, b * s, H), device="cuda", dtype=torch.bfloat16)
+    base = qkv.data_ptr()
+    q_, k_, v_ = ctypes.c_void_p(base), ctypes.c_void_p(base + H * 4), ctypes.c_void_p(base + 2 * H * 4)
+    torch.cuda.synchronize()
+    N.check(lib.b2m_mha_dev(h, q_, k_, v_, 3 * H, 3 * H, _p(mask), s, 0, 0, _p(out_ref), b, s, s, heads, heads, D,
+                            ctypes.c_float(0.0), 0))
+    N.check(lib.b2m_mha_split_dev(h, q_, k_, v_, 3 * H, 3 * H, _p(mask), s, 0, 0, _p(out), _p(planes), b, s, s, heads,
+                                  heads, D, ctypes.c_float(0.0), 0))
+    y_ref, y = torch.empty((b * s, 256), device="cuda"), torch.empty((b * s, 256), device="cuda")
+    _gemm_fast(ctx, out_ref, b * s, H, w, bias, y_ref)
+    N.check(lib.b2m_gemm_f32_split_dev(h, _p(planes), b * s, w.handle, _p(bias), _p(y)))
+    N.check(lib.b2m_synchronize(h))
+    assert torch.equal(out, out_ref)
+    assert torch.equal(y, y_ref)
+    w.free()
