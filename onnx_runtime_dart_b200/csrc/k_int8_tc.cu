@@ -428,6 +428,7 @@ __global__ void __launch_bounds__(GV_THREADS)
 }
 
 int i8_pick_bt(int64_t M, int64_t N, int sms) {
+  if (M <= 64) return 64;  // up to 64 rows: the smallest tile that covers them
   static const int cand[] = {256, 192, 128, 96};
   const int64_t ntile = (N + 127) / 128;
   int best = 128;
@@ -493,6 +494,7 @@ void launch_ts_bt(const I8GemmArgs &a, const I8Weight &w, const I8Epi &e, cudaSt
     case 256: launch_ts<256, 3, AS, WS, REQ>(a, w, e, s); break;
     case 192: launch_ts<192, 4, AS, WS, REQ>(a, w, e, s); break;
     case 128: launch_ts<128, 6, AS, WS, REQ>(a, w, e, s); break;
+    case 64: launch_ts<64, 6, AS, WS, REQ>(a, w, e, s); break;
     default: launch_ts<96, 6, AS, WS, REQ>(a, w, e, s); break;
   }
 }
