@@ -425,6 +425,23 @@ B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k,
                                    int32_t rotary_dim, int32_t interleaved, float *out, uint16_t *out16, int32_t b,
                                    int32_t s, int32_t h, int32_t kvh, int32_t head_dim, int32_t cap, float scale);
 
+/* b2m_gqa_dev preceded by the per-head RMSNorm of q and k (the q_norm /
+ * k_norm SimplifiedLayerNormalization nodes of a Qwen3 layer, each head of
+ * head_dim values normalised with its gain row): qk_gain is [h + kvh][head_dim],
+ * the gain rows of the h query heads, then those of the kvh key heads; eps the
+ * norm's epsilon. out16: NULL, or the f16 copy of out as b2m_gqa_f16_dev
+ * writes it. Results equal b2m_rmsnorm_head_rows_dev on q and k followed by
+ * b2m_gqa_dev / b2m_gqa_f16_dev. A single-token call (s == 1) normalises
+ * inside the decode attention kernel, which also appends the token's key and
+ * value (one launch); other calls normalise q and k IN PLACE first, so both
+ * buffers may hold their normalised values afterwards. */
+B2M_API b2m_status b2m_gqa_qknorm_dev(b2m_ctx *ctx, float *q, float *k, const float *v, int64_t q_rs, int64_t kv_rs,
+                                      const float *qk_gain, double eps, float *k_cache, float *v_cache,
+                                      const int32_t *past, const float *cos_cache, const float *sin_cache,
+                                      int32_t rotary_half, int32_t rotary_dim, int32_t interleaved, float *out,
+                                      uint16_t *out16, int32_t b, int32_t s, int32_t h, int32_t kvh, int32_t head_dim,
+                                      int32_t cap, float scale);
+
 /* MultiHeadAttention over projected rows (opMultiHeadAttention,
  * lib/src/onnx_ops.dart:2019; the scale + mask + softmax between the two
  * batched MatMuls of opFusedSDPA, :2106-2148). q: [b][s] rows of h*head_dim

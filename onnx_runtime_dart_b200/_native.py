@@ -170,6 +170,8 @@ SIGNATURES = {
                            _i32, _i32, _i32, _i32, _i32, _f32]),
     "b2m_gqa_f16_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp,
                                _i32, _i32, _i32, _i32, _i32, _i32, _f32]),
+    "b2m_gqa_qknorm_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _vp, ctypes.c_double, _vp, _vp, _vp, _vp, _vp,
+                                  _i32, _i32, _i32, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _i32, _f32]),
     "b2m_mha_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _i32, _i32, _i32, _i32,
                            _i32, _i32, _f32, _i32]),
     "b2m_mha_split_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _i64, _vp, _vp, _i32, _i32,

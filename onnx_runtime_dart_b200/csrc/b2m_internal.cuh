@@ -387,7 +387,11 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
                 float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s,
-                __half *out16 = nullptr);
+                __half *out16 = nullptr, const float *qk_gain = nullptr, double qk_eps = 0.0);
+// `qk_gain` ([H + KVH][D] gain rows, or null): q and k are first RMS-normalised
+// per head (eps `qk_eps`), inside the decode kernel for S == 1 (which then
+// also appends the token's key and value), else in place by the head-rows
+// norm before the append.
 // `counters` (B * KVH zeroed words, or null): the last split CTA of each (kv
 // head, sequence) merges the key splits itself, instead of a separate
 // combine launch; the words are zero again when the call completes.

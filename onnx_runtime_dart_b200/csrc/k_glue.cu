@@ -610,10 +610,56 @@ struct GqaArgs {
   // (row stride H*D), the A operand of a FAST fp32 Gemm.
   __half *out16 = nullptr;
   __nv_bfloat16 *p0 = nullptr, *p1 = nullptr;
+  // Decode kernel only: per-head RMSNorm gains of q and k ([H + KVH][D]: the
+  // query heads' rows, then the kv heads'), or null when q and k arrive
+  // normalised; with them the kernel also appends the token's key and value.
+  const float *qk_gain = nullptr;
+  double qk_eps = 0.0;
 };
 
+// RMSNorm of one head of D <= 128 values held as one float4 per lane (lanes
+// at or past D / 4 hold zeros), gain row g: the arithmetic of
+// norm_warp4_kernel<1, false> (and of norm_row_cta_kernel with one warp), so
+// the result equals the head-rows norm launch bit for bit.
+__device__ __forceinline__ float4 rms_head4(float4 v, const float *__restrict__ g, int D, double eps, int lane) {
+  const int d4 = D >> 2;
+  const float mean = 0.f;
+  float s2 = 0.f;
+  if (lane < d4) {
+    const float a = v.x - mean, b = v.y - mean, c = v.z - mean, d = v.w - mean;
+    s2 = fmaf(a, a, fmaf(b, b, fmaf(c, c, fmaf(d, d, s2))));
+  }
+  const float inv = (float)(1.0 / sqrt((double)warp_sum_f(s2) / D + eps));
+  if (lane >= d4) return make_float4(0.f, 0.f, 0.f, 0.f);
+  const float4 gg = reinterpret_cast<const float4 *>(g)[lane];
+  const float bb = 0.f;
+  return make_float4((v.x - mean) * inv * gg.x + bb, (v.y - mean) * inv * gg.y + bb, (v.z - mean) * inv * gg.z + bb,
+                     (v.w - mean) * inv * gg.w + bb);
+}
+
+// rms_head4 for rows of D = 64 or 128 held by D / 4 consecutive lanes (two
+// rows per warp at D = 64), c the lane's float4 within its row. At D = 64 the
+// butterfly skips the step that would add the other half's zeros in
+// rms_head4, which changes no bit.
+template <int D>
+__device__ __forceinline__ float4 rms_row4(float4 v, const float *__restrict__ g, double eps, int c) {
+  static_assert(D == 64 || D == 128, "rows of 16 or 32 lanes");
+  const float mean = 0.f;
+  const float a = v.x - mean, b = v.y - mean, cc = v.z - mean, d = v.w - mean;
+  float t = fmaf(a, a, fmaf(b, b, fmaf(cc, cc, fmaf(d, d, 0.f))));
+  if (D == 128) t += __shfl_xor_sync(0xffffffffu, t, 16);
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  const float inv = (float)(1.0 / sqrt((double)t / D + eps));
+  const float4 gg = reinterpret_cast<const float4 *>(g)[c];
+  const float bb = 0.f;
+  return make_float4((v.x - mean) * inv * gg.x + bb, (v.y - mean) * inv * gg.y + bb, (v.z - mean) * inv * gg.z + bb,
+                     (v.w - mean) * inv * gg.w + bb);
+}
+
 // Appends this call's keys / values to the cache (rotary on K), one warp per
-// (token, kv head).
+// (token, kv head). With a.qk_gain (D <= 128, float4-aligned rows) each key
+// head is RMS-normalised first.
 __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
   b2m::pdl_launch_dependents();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -629,11 +675,18 @@ __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
     if (lane == 0 && a.err) b2m::set_dev_error(a.err, B2M_DEVERR_CACHE_FULL);
     return;
   }
-  __shared__ float kbuf[8][256];
+  __shared__ __align__(16) float kbuf[8][256];
   float *kv = kbuf[warp];
   const float *ksrc = a.k + (int64_t)(b * a.S + s) * a.kv_rs + kvh * a.D;
   const float *vsrc = a.v + (int64_t)(b * a.S + s) * a.kv_rs + kvh * a.D;
-  for (int d = lane; d < a.D; d += 32) kv[d] = ksrc[d];
+  if (a.qk_gain) {
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lane < (a.D >> 2)) x = *reinterpret_cast<const float4 *>(ksrc + 4 * lane);
+    const float4 o = rms_head4(x, a.qk_gain + (int64_t)(a.H + kvh) * a.D, a.D, a.qk_eps, lane);
+    if (lane < (a.D >> 2)) *reinterpret_cast<float4 *>(kv + 4 * lane) = o;
+  } else {
+    for (int d = lane; d < a.D; d += 32) kv[d] = ksrc[d];
+  }
   __syncwarp();
   if (a.cos) rotate_head(kv, a.cos, a.sin, pos, a.half, a.rot, a.interleaved, lane, 32);
   __syncwarp();
@@ -892,9 +945,50 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
   __shared__ __align__(16) float qs[G][D];
   __shared__ float wm[8][G], wl[8][G];
   __shared__ float wo[8][G][D];
-  for (int i = threadIdx.x; i < G * D; i += 256) {
-    const int g = i / D, d = i % D;
-    qs[g][d] = a.q[(int64_t)b * a.q_rs + (kvh * G + g) * D + d] * a.scale;
+  if (a.qk_gain) {
+    // Head RMSNorm folded in: warp g normalises query head kvh*G + g; warp
+    // G % 8 normalises this kv head's new key, rotates it and appends it and
+    // the value at position past, in the CTA whose key range holds past (it
+    // reads them back below; __syncthreads makes the stores visible).
+    constexpr int D4 = D / 4;
+    if (warp < G) {
+      const int h = kvh * G + warp;
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane < D4) x = *reinterpret_cast<const float4 *>(a.q + (int64_t)b * a.q_rs + (int64_t)h * D + 4 * lane);
+      const float4 o = rms_head4(x, a.qk_gain + (int64_t)h * D, D, a.qk_eps, lane);
+      if (lane < D4) {
+        qs[warp][4 * lane + 0] = o.x * a.scale;
+        qs[warp][4 * lane + 1] = o.y * a.scale;
+        qs[warp][4 * lane + 2] = o.z * a.scale;
+        qs[warp][4 * lane + 3] = o.w * a.scale;
+      }
+    }
+    if (warp == (G & 7)) {
+      __shared__ __align__(16) float kb[D];
+      if (past >= a.CAP) {
+        if (lane == 0 && sp == 0 && a.err) b2m::set_dev_error(a.err, B2M_DEVERR_CACHE_FULL);
+      } else if (jbeg <= past && past < jend) {
+        const float *ksrc = a.k + (int64_t)b * a.kv_rs + (int64_t)kvh * D;
+        const float *vsrc = a.v + (int64_t)b * a.kv_rs + (int64_t)kvh * D;
+        float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (lane < D4) x = *reinterpret_cast<const float4 *>(ksrc + 4 * lane);
+        const float4 o = rms_head4(x, a.qk_gain + (int64_t)(a.H + kvh) * D, D, a.qk_eps, lane);
+        if (lane < D4) *reinterpret_cast<float4 *>(&kb[4 * lane]) = o;
+        __syncwarp();
+        if (a.cos) rotate_head(kb, a.cos, a.sin, past, a.half, a.rot, a.interleaved, lane, 32);
+        __syncwarp();
+        const int64_t dst = (((int64_t)b * a.KVH + kvh) * a.CAP + past) * D;
+        for (int d = lane; d < D; d += 32) {
+          a.kcache[dst + d] = kb[d];
+          a.vcache[dst + d] = vsrc[d];
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < G * D; i += 256) {
+      const int g = i / D, d = i % D;
+      qs[g][d] = a.q[(int64_t)b * a.q_rs + (kvh * G + g) * D + d] * a.scale;
+    }
   }
   __syncthreads();
   if (a.cos && past < a.CAP) {
@@ -1047,9 +1141,9 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
           L += __ldcg(pl + base + s2) * f;
           O += __ldcg(po + (base + s2) * D + d) * f;
         }
-        const float ov = O / L;
-      a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
-      if (a.out16) a.out16[(int64_t)b * (int64_t)a.H * D + h * D + d] = __float2half_rn(ov);
+          const float ov = O / L;
+        a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
+        if (a.out16) a.out16[(int64_t)b * (int64_t)a.H * D + h * D + d] = __float2half_rn(ov);
       }
       if (threadIdx.x == 0) counters[(int64_t)b * a.KVH + kvh] = 0u;
     }
@@ -1426,6 +1520,10 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
     for (int u = 0; u < QI; u++) {
       const int e = tid + 512 * u, rr = e / (D / 4), c = e % (D / 4);
       float4 v = qv[u];
+      if (a.qk_gain) {  // the head's RMSNorm folded in (rows of D / 4 lanes; padding rows stay zero)
+        const float4 o = rms_row4<D>(v, a.qk_gain + (int64_t)h * D, a.qk_eps, c);
+        if (q0 + rr < a.S) v = o;
+      }
       v.x *= a.scale, v.y *= a.scale, v.z *= a.scale, v.w *= a.scale;
       *reinterpret_cast<float4 *>(qf + rr * D + 4 * c) = v;
     }
@@ -1962,7 +2060,8 @@ int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP) {
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,
-                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s, __half *out16) {
+                float *split_part, int nsplit, bool exact, uint32_t *counters, cudaStream_t s, __half *out16,
+                const float *qk_gain, double qk_eps) {
   GqaArgs a{q, k, v, q_rs, kv_rs, kcache, vcache, past, cos, sin, half, rot, interleaved, out,
             B, S, H, KVH, D, CAP, scale, err};
   a.out16 = out16;
@@ -1973,6 +2072,37 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
   a.kv_len = CAP;
   a.mask = nullptr;
   a.mask_bs = a.mask_hs = a.mask_qs = 0;
+  if (qk_gain) {
+    // Folded where the head-rows norm would take its float4 form (the
+    // arithmetic the kernels reproduce): the decode kernel normalises q and
+    // k in its prologue and appends; for the flash prefill kernel the append
+    // kernel normalises k and the flash kernel q.
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const bool f4 = D % 4 == 0 && D <= 128 && q_rs % 4 == 0 && kv_rs % 4 == 0 && al(q) && al(k) && al(qk_gain);
+    if (f4 && decode_shape(a)) {
+      a.qk_gain = qk_gain;
+      a.qk_eps = qk_eps;
+      launch_attend(a, split_part, nsplit, exact, counters, s);
+      return;
+    }
+    if (f4 && !exact && fa_tc_shape(a)) {
+      a.qk_gain = qk_gain;
+      a.qk_eps = qk_eps;
+      const int64_t items = (int64_t)B * S * KVH;
+      gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
+      B2M_CUDA(cudaGetLastError());
+      launch_attend(a, split_part, nsplit, exact, counters, s);
+      return;
+    }
+    float *qw = const_cast<float *>(q), *kw = const_cast<float *>(k);
+    if (k == q + (int64_t)H * D && kv_rs == q_rs) {  // q and k heads adjacent in the rows: one launch
+      launch_rmsnorm(qw, nullptr, qk_gain, qw, nullptr, (int64_t)B * S * (H + KVH), D, qk_eps, H + KVH, q_rs, s, D);
+    } else {
+      launch_rmsnorm(qw, nullptr, qk_gain, qw, nullptr, (int64_t)B * S * H, D, qk_eps, H, q_rs, s, D);
+      launch_rmsnorm(kw, nullptr, qk_gain + (int64_t)H * D, kw, nullptr, (int64_t)B * S * KVH, D, qk_eps, KVH, kv_rs,
+                     s, D);
+    }
+  }
   const int64_t items = (int64_t)B * S * KVH;
   gqa_append_kernel<<<(unsigned)((items + 7) / 8), 256, 0, s>>>(a);
   B2M_CUDA(cudaGetLastError());

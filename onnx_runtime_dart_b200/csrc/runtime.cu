@@ -1842,7 +1842,8 @@ static b2m_status gqa_impl(b2m_ctx *ctx, const float *q, const float *k, const f
                            int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
                            const float *cos_cache, const float *sin_cache, int32_t rotary_half, int32_t rotary_dim,
                            int32_t interleaved, float *out, int32_t b, int32_t s, int32_t h, int32_t kvh,
-                           int32_t head_dim, int32_t cap, float scale, uint16_t *out16) {
+                           int32_t head_dim, int32_t cap, float scale, uint16_t *out16,
+                           const float *qk_gain = nullptr, double qk_eps = 0.0) {
   return guarded([&] {
     check_ctx(ctx);
     B2M_REQUIRE(b >= 0 && s >= 0 && h > 0 && kvh > 0 && h % kvh == 0 && head_dim > 0 && head_dim <= 256 && cap > 0,
@@ -1880,7 +1881,7 @@ static b2m_status gqa_impl(b2m_ctx *ctx, const float *q, const float *k, const f
     }
     launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
                interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit,
-               ctx->attn_exact, counters, ctx->stream, reinterpret_cast<__half *>(out16));
+               ctx->attn_exact, counters, ctx->stream, reinterpret_cast<__half *>(out16), qk_gain, qk_eps);
   });
 }
 
@@ -1904,6 +1905,24 @@ B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k,
   }
   return gqa_impl(ctx, q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
                   interleaved, out, b, s, h, kvh, head_dim, cap, scale, out16);
+}
+
+B2M_API b2m_status b2m_gqa_qknorm_dev(b2m_ctx *ctx, float *q, float *k, const float *v, int64_t q_rs, int64_t kv_rs,
+                                      const float *qk_gain, double eps, float *k_cache, float *v_cache,
+                                      const int32_t *past, const float *cos_cache, const float *sin_cache,
+                                      int32_t rotary_half, int32_t rotary_dim, int32_t interleaved, float *out,
+                                      uint16_t *out16, int32_t b, int32_t s, int32_t h, int32_t kvh, int32_t head_dim,
+                                      int32_t cap, float scale) {
+  if ((int64_t)b * s > 0 && !qk_gain) {
+    b2m_set_last_error("GroupQueryAttention q/k norm: qk_gain is null");
+    return B2M_ERR_INVALID_ARGUMENT;
+  }
+  if (!(eps >= 0.0)) {
+    b2m_set_last_error("GroupQueryAttention q/k norm: eps must be >= 0");
+    return B2M_ERR_INVALID_ARGUMENT;
+  }
+  return gqa_impl(ctx, q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
+                  interleaved, out, b, s, h, kvh, head_dim, cap, scale, out16, qk_gain, eps);
 }
 
 static b2m_status mha_impl(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,

@@ -82,7 +82,7 @@ class Int4Decoder:
 
     def __init__(self, ctx, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int, seed: int = 0,
                  keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True, session=None,
-                 producer_f16: bool = True):
+                 producer_f16: bool = True, fold_qk_norm: bool = True):
         import torch
 
         if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
@@ -108,6 +108,11 @@ class Int4Decoder:
         # f16 operand (the bits the GEMM's own conversion forms), so the
         # projection runs without its conversion launch.
         self.producer_f16 = producer_f16
+        # fold_qk_norm (fused chains): the q / k head norms go into the
+        # attention call (b2m_gqa_qknorm_dev), which at one token per sequence
+        # normalises, rotates and appends inside the decode kernel: two
+        # launches fewer per layer and step, the same results.
+        self.fold_qk_norm = fold_qk_norm
         self._routes = {}
         self.torch = torch
         self.ctx, self.cfg, self.B, self.cap = ctx, cfg, batch, cap
@@ -427,24 +432,31 @@ class Int4Decoder:
                                                      _ptr(getattr(self, part))))
                 qp, kp, vp = self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr()
                 q_rs, kv_rs = c.heads * D, c.kv_heads * D
-            if self.fused:  # q and k heads are adjacent in the packed rows: one launch
-                chk(lib.b2m_rmsnorm_head_rows_dev(h, ctypes.c_void_p(qp), _ptr(lw["qk_gain"]), ctypes.c_void_p(qp), T,
-                                                  c.heads + c.kv_heads, D, q_rs, c.eps))
+            if self.fused and self.fold_qk_norm:  # head norms inside the attention call
+                chk(lib.b2m_gqa_qknorm_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs,
+                                           kv_rs, _ptr(lw["qk_gain"]), c.eps, _ptr(self.kcache[li]),
+                                           _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin),
+                                           D // 2, D, 0, _ptr(self.attn), _ptr(self.attn16) if o16 else None, self.B,
+                                           seq, c.heads, c.kv_heads, D, self.cap, 0.0))
             else:
-                chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qp), _ptr(lw["q_norm"]), ctypes.c_void_p(qp), T,
-                                              c.heads, D, q_rs, c.eps))
-                chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(kp), _ptr(lw["k_norm"]), ctypes.c_void_p(kp), T,
-                                              c.kv_heads, D, kv_rs, c.eps))
-            if o16:  # the attention also writes the o projection's f16 operand
-                chk(lib.b2m_gqa_f16_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
+                if self.fused:  # q and k heads are adjacent in the packed rows: one launch
+                    chk(lib.b2m_rmsnorm_head_rows_dev(h, ctypes.c_void_p(qp), _ptr(lw["qk_gain"]), ctypes.c_void_p(qp),
+                                                      T, c.heads + c.kv_heads, D, q_rs, c.eps))
+                else:
+                    chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(qp), _ptr(lw["q_norm"]), ctypes.c_void_p(qp), T,
+                                                  c.heads, D, q_rs, c.eps))
+                    chk(lib.b2m_rmsnorm_heads_dev(h, ctypes.c_void_p(kp), _ptr(lw["k_norm"]), ctypes.c_void_p(kp), T,
+                                                  c.kv_heads, D, kv_rs, c.eps))
+                if o16:  # the attention also writes the o projection's f16 operand
+                    chk(lib.b2m_gqa_f16_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs,
+                                            kv_rs, _ptr(self.kcache[li]), _ptr(self.vcache[li]), _ptr(self.past),
+                                            _ptr(self.cos), _ptr(self.sin), D // 2, D, 0, _ptr(self.attn),
+                                            _ptr(self.attn16), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
+                else:
+                    chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
                                         _ptr(self.kcache[li]), _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos),
-                                        _ptr(self.sin), D // 2, D, 0, _ptr(self.attn), _ptr(self.attn16), self.B, seq,
-                                        c.heads, c.kv_heads, D, self.cap, 0.0))
-            else:
-                chk(lib.b2m_gqa_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs, kv_rs,
-                                    _ptr(self.kcache[li]),
-                                    _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin), D // 2, D,
-                                    0, _ptr(self.attn), self.B, seq, c.heads, c.kv_heads, D, self.cap, 0.0))
+                                        _ptr(self.sin), D // 2, D, 0, _ptr(self.attn), self.B, seq, c.heads,
+                                        c.kv_heads, D, self.cap, 0.0))
             if self.session is not None:
                 self._dispatch_proj("o", lw, self.attn, T, self.o)
             else:
