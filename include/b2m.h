@@ -286,6 +286,26 @@ B2M_API b2m_status b2m_matmul_nbits_route(b2m_ctx *ctx, const b2m_weight *w, int
 B2M_API b2m_status b2m_matmul_nbits_f16_dev(b2m_ctx *ctx, const uint16_t *a16, int64_t m, const b2m_weight *w,
                                             const float *bias, float *y);
 
+/* The SwiGLU front half of an MLP in one call: the gate and up MatMulNBits
+ * of a layer (one weight of N = 2I output rows) followed by silu(gate) * up,
+ * the Sigmoid / Mul / Mul nodes between them and the down MatMulNBits
+ * (lib/src/onnx_qlinear_ops.dart:115-228 for each MatMulNBits, then the
+ * elementwise nodes). The weight's rows are TILE-INTERLEAVED: for t in
+ * [0, I/64) its rows 128t .. 128t+63 are the gate rows 64t .. 64t+63 and rows
+ * 128t+64 .. 128t+127 the matching up rows (N % 128 == 0). act: [m][I] fp32
+ * and / or act16: the same rounded to f16 (the operand of
+ * b2m_matmul_nbits_f16_dev for the down projection); either may be NULL,
+ * both 16-byte aligned. a: the fp32 activations [m][K]; a16: NULL or their
+ * f16 copy (as b2m_rmsnorm_f16_dev writes it), used where the call's route
+ * is B2M_ROUTE_TC_F16, where the tensor-core GEMM forms the products in its
+ * epilogue (no fp32 gate / up rows in memory). On other routes a is required
+ * and the result is b2m_matmul_nbits_dev followed by the elementwise pass.
+ * Results are bit for bit those of b2m_matmul_nbits_dev on the same weight
+ * (mode as given) followed by b2m_silu_mul_dev / b2m_silu_mul_f16_dev on the
+ * gate and up columns. */
+B2M_API b2m_status b2m_matmul_nbits_swiglu_dev(b2m_ctx *ctx, const float *a, const uint16_t *a16, int64_t m,
+                                               const b2m_weight *w, int32_t mode, float *act, uint16_t *act16);
+
 /* Allocation-free MatMulNBits. No counterpart in the reference: this entry
  * point exists for callers that must not allocate device memory while they
  * run an operator — a host application that has handed all device memory to

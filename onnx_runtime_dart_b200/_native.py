@@ -162,6 +162,7 @@ SIGNATURES = {
     "b2m_rmsnorm_f16_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, ctypes.c_double]),
     "b2m_matmul_nbits_route": (_i32, [_c_ctx, _c_weight, _i64, _i32, ctypes.POINTER(_i32)]),
     "b2m_matmul_nbits_f16_dev": (_i32, [_c_ctx, _vp, _i64, _c_weight, _vp, _vp]),
+    "b2m_matmul_nbits_swiglu_dev": (_i32, [_c_ctx, _vp, _vp, _i64, _c_weight, _i32, _vp, _vp]),
     "b2m_gelu_dev": (_i32, [_c_ctx, _vp, _vp, _i64]),
     "b2m_add_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i32]),
     "b2m_gather_rows_dev": (_i32, [_c_ctx, _vp, _vp, _vp, _i64, _i64, _i64]),

@@ -351,7 +351,17 @@ bool nbits_tc_supported(const NbitsWeight &w, int64_t M, int64_t K, int64_t N);
 void launch_nbits_tc(const NbitsArgs &a, __half *a16, cudaStream_t s);
 // The TMEM-operand variant (weights with tsq/tss), called by launch_nbits_tc
 // after the activation conversion.
-void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s);
+namespace b2m {
+// fp32 rows -> f16 rows of K8 columns (zero padded; k permuted in groups of
+// four when perm), the conversion in front of the tensor-core GEMMs.
+void launch_f32_to_f16(const float *A, __half *A16, int64_t M, int64_t K, int64_t K8, int perm, cudaStream_t s);
+}  // namespace b2m
+// act / act16 (optional, 16-byte aligned): the SwiGLU epilogue. The weight's
+// N = 2I rows are tile-interleaved (rows 128t .. 128t+63 the gate rows 64t ..,
+// rows 128t+64 .. the matching up rows; N % 128 == 0) and the kernel writes
+// act[M][I] = silu(gate) * up (fp32 and / or f16) instead of Y.
+void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s, float *act = nullptr,
+                     __half *act16 = nullptr);
 
 // Transformer glue (k_glue.cu)
 // gamma_rs > 0: row i of a group of `per` rows uses gains gamma + i * gamma_rs
@@ -367,6 +377,10 @@ void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float
 void launch_layernorm(const float *x, const float *skip, const float *gamma, const float *beta, float *y,
                       float *sum_out, int64_t rows, int D, double eps, cudaStream_t s,
                       __nv_bfloat16 *p0 = nullptr, __nv_bfloat16 *p1 = nullptr);
+// SwiGLU over a tile-interleaved gate / up output y [rows][2I] (the layout
+// of launch_nbits_ts's SwiGLU epilogue): act / act16 [rows][I], either may be
+// null; I % 64 == 0, 16-byte aligned buffers.
+void launch_silu_mul_tiles(const float *y, int64_t rows, int64_t I, float *act, __half *act16, cudaStream_t s);
 void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u_rs, float *y, int64_t rows,
                      int64_t D, cudaStream_t s, __half *y16 = nullptr);
 void launch_gelu(const float *x, float *y, int64_t n, cudaStream_t s);

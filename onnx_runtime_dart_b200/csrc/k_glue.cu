@@ -400,6 +400,25 @@ __global__ void silu_mul_kernel(const float *__restrict__ gate, const float *__r
   }
 }
 
+// SwiGLU over the tile-interleaved output of a gate / up projection: row r
+// of y holds, per 128-column tile t, the gate columns 64t .. 64t+63 and then
+// the matching up columns; act[r][j] = silu(gate j) * up j (fp32 and / or the
+// f16 copy). Four columns per thread (I % 64 == 0, 16-byte aligned rows).
+__global__ void silu_mul_tiles_kernel(const float *__restrict__ y, int64_t rows, int64_t I, float *act,
+                                      __half *act16) {
+  b2m::pdl_launch_dependents();
+  const int64_t q = I >> 2, n = rows * q;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = e / q, c4 = (e - r * q) * 4;
+    const float *yr = y + r * 2 * I + (c4 >> 6) * 128 + (c4 & 63);
+    const float4 g = *reinterpret_cast<const float4 *>(yr), u = *reinterpret_cast<const float4 *>(yr + 64);
+    const float4 o =
+        make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z), silu_times(g.w, u.w));
+    if (act) reinterpret_cast<float4 *>(act + r * I)[c4 >> 2] = o;
+    if (act16) store_f16x4(act16 + r * I + c4, o);
+  }
+}
+
 __global__ void gelu_kernel(const float *__restrict__ x, float *y, int64_t n) {
   b2m::pdl_launch_dependents();
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
@@ -1907,6 +1926,12 @@ void launch_silu_mul(const float *gate, const float *up, int64_t g_rs, int64_t u
   const dim3 grid((unsigned)std::min<int64_t>((cols + 255) / 256, 64), (unsigned)std::min<int64_t>(rows, 65535));
   if (vec) silu_mul_kernel<true><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D, y16);
   else silu_mul_kernel<false><<<grid, 256, 0, s>>>(gate, up, g_rs, u_rs, y, rows, D, nullptr);
+  B2M_CUDA(cudaGetLastError());
+}
+
+void launch_silu_mul_tiles(const float *y, int64_t rows, int64_t I, float *act, __half *act16, cudaStream_t s) {
+  if (rows * I <= 0) return;
+  silu_mul_tiles_kernel<<<grid_for(rows * (I / 4), 256), 256, 0, s>>>(y, rows, I, act, act16);
   B2M_CUDA(cudaGetLastError());
 }
 

@@ -20,6 +20,10 @@
 //               of the accumulator (lane = weight column, column = token), add
 //               bias, stage the half tile in shared memory, one TMA store
 //               (or, for unaligned outputs, coalesced stores of Y rows).
+// SwiGLU epilogue (act / act16 given): the weight's rows are tile-interleaved,
+// each 128-column tile holding 64 gate columns and then the 64 matching up
+// columns, and the CTA writes act = silu(gate) * up for its 64 columns (fp32
+// and / or f16) from the staged tile instead of Y.
 // Accumulator in TMEM columns [0, BT); A stages from column A_COL0 on, 64
 // columns per 128-k stage (two f16 per 32-bit column, k order).
 // Every mbarrier wait is bounded; a timeout sets the context's device error
@@ -107,13 +111,28 @@ __device__ __forceinline__ void ts_dequant(const TsRec &r, uint32_t (&out)[32]) 
   }
 }
 
+// act[i .. i+3] = silu(g) * u (silu_mul_kernel's arithmetic), and / or its
+// f16 copy rounded to nearest (i a multiple of 4, 16-byte aligned outputs).
+__device__ __forceinline__ void swiglu_store4(float *act, __half *act16, size_t i, float4 g, float4 u) {
+  const float4 o = make_float4(silu_times(g.x, u.x), silu_times(g.y, u.y), silu_times(g.z, u.z), silu_times(g.w, u.w));
+  if (act) *reinterpret_cast<float4 *>(act + i) = o;
+  if (act16) {
+    const __half2 a = __floats2half2_rn(o.x, o.y), b = __floats2half2_rn(o.z, o.w);
+    uint2 w;
+    w.x = h2_as_u32(a);
+    w.y = h2_as_u32(b);
+    *reinterpret_cast<uint2 *>(act16 + i) = w;
+  }
+}
+
 template <int BT, int STAGES, int KSUB>
 __global__ void __launch_bounds__(TS_THREADS, 1)
     nbits_ts_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_y,
                     int use_tma_y, const uint4 *__restrict__ tsq, const uint2 *__restrict__ tss,
                     const float *__restrict__ bias, float *__restrict__ Y, int M, int N, int nchunks,
-                    int32_t *dev_err, const PrefetchPlan pf) {
+                    int32_t *dev_err, const PrefetchPlan pf, float *__restrict__ act, __half *__restrict__ act16) {
   using L = TsLayout<BT, STAGES, KSUB>;
+  const bool swiglu = act != nullptr || act16 != nullptr;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
   // full[s]: the stage's activation bytes landed (TMA, one arrival + tx) and
@@ -273,7 +292,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       const bool colok = col < N;
       // With K split, the raw partial tile is staged (no bias) for the
       // cluster reduction below.
-      const bool stage = use_tma_y || splits > 1;
+      const bool stage = use_tma_y || splits > 1 || swiglu;
       const float b = (bias && colok && splits == 1) ? __ldg(bias + col) : 0.f;
       // All TMEM loads of a group of up to 64 tokens go out before one wait;
       // a wait per 16 columns serializes the load latency.
@@ -308,7 +327,24 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         }
       }
     }
-    if (use_tma_y && splits == 1) {
+    if (swiglu && splits == 1) {
+      // Every epilogue warp takes the group barrier, aborted or not; then the
+      // group pairs gate column j with up column 64 + j of its staged rows.
+      named_barrier_sync(2 + gq, 128);
+      if (go) {
+        constexpr int HALF = BT / 2;
+        const float *so = reinterpret_cast<const float *>(smem) + (size_t)gq * HALF * 128;
+        const int gt = (warp - 2 - 4 * gq) * 32 + lane;
+        for (int it = gt; it < HALF * 16; it += 128) {
+          const int row = it >> 4, c4 = (it & 15) * 4;
+          const int t = t0 + gq * HALF + row;
+          if (t >= M) continue;
+          const float4 g = *reinterpret_cast<const float4 *>(so + row * 128 + c4);
+          const float4 u = *reinterpret_cast<const float4 *>(so + row * 128 + 64 + c4);
+          swiglu_store4(act, act16, (size_t)t * (size_t)(N >> 1) + (size_t)tile * 64 + c4, g, u);
+        }
+      }
+    } else if (use_tma_y && splits == 1) {
       // Every epilogue warp takes the group barrier, aborted or not.
       fence_proxy_async_smem();
       named_barrier_sync(2 + gq, 128);
@@ -330,7 +366,34 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
     const int rb = zr * per, re = min(BT, rb + per);
     const uint32_t sbase = smem_u32(smem);
     const bool vec = (N & 3) == 0 && (reinterpret_cast<uintptr_t>(Y) & 15) == 0;
-    if (!*abort_flag) {
+    if (!*abort_flag && swiglu) {
+      // Gate columns [c4, c4 + 4) and the matching up columns 64 + c4 ..,
+      // each summed over the ranks in rank order (the plain path's order).
+      for (int it = threadIdx.x; it < (re - rb) * 16; it += TS_THREADS) {
+        const int row = rb + (it >> 4), c4 = (it & 15) * 4;
+        const int t = t0 + row;
+        if (t >= M) continue;
+        const uint32_t og = (uint32_t)(row * 128 + c4) * 4u, ou = og + 64u * 4u;
+        float4 g = make_float4(0.f, 0.f, 0.f, 0.f), u = g;
+        for (int rk = 0; rk < splits; rk++) {
+          const float4 p = dsmem_ld4(dsmem_map(sbase + og, (uint32_t)rk));
+          g.x += p.x, g.y += p.y, g.z += p.z, g.w += p.w;
+          const float4 q4 = dsmem_ld4(dsmem_map(sbase + ou, (uint32_t)rk));
+          u.x += q4.x, u.y += q4.y, u.z += q4.z, u.w += q4.w;
+        }
+        if (bias) {
+          const int cg = n0 + c4, cu = n0 + 64 + c4;
+          g.x = g.x + __ldg(bias + cg), g.y = g.y + __ldg(bias + cg + 1);
+          g.z = g.z + __ldg(bias + cg + 2), g.w = g.w + __ldg(bias + cg + 3);
+          u.x = u.x + __ldg(bias + cu), u.y = u.y + __ldg(bias + cu + 1);
+          u.z = u.z + __ldg(bias + cu + 2), u.w = u.w + __ldg(bias + cu + 3);
+        } else {
+          g.x = g.x + 0.f, g.y = g.y + 0.f, g.z = g.z + 0.f, g.w = g.w + 0.f;
+          u.x = u.x + 0.f, u.y = u.y + 0.f, u.z = u.z + 0.f, u.w = u.w + 0.f;
+        }
+        swiglu_store4(act, act16, (size_t)t * (size_t)(N >> 1) + (size_t)tile * 64 + c4, g, u);
+      }
+    } else if (!*abort_flag) {
       for (int it = threadIdx.x; it < (re - rb) * 32; it += TS_THREADS) {
         const int row = rb + (it >> 5), c4 = (it & 31) * 4;
         const int t = t0 + row, col = n0 + c4;
@@ -368,7 +431,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
 }
 
 template <int BT, int STAGES, int KSUB>
-void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, cudaStream_t s) {
+void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, cudaStream_t s, float *act,
+                 __half *act16) {
   using L = TsLayout<BT, STAGES, KSUB>;
   CUtensorMap tm;
   const cuuint64_t dims[2] = {(cuuint64_t)K8, (cuuint64_t)a.M};
@@ -383,7 +447,7 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, 
   // columns x BT/2 tokens (needs 16-byte aligned rows; otherwise direct stores).
   CUtensorMap ty = tm;
   int use_ty = 0;
-  if ((a.N % 4) == 0 && (reinterpret_cast<uintptr_t>(a.Y) & 15) == 0) {
+  if (!act && !act16 && (a.N % 4) == 0 && (reinterpret_cast<uintptr_t>(a.Y) & 15) == 0) {
     const cuuint64_t ydims[2] = {(cuuint64_t)a.N, (cuuint64_t)a.M};
     const cuuint64_t ystr[1] = {(cuuint64_t)(a.N * 4)};
     const cuuint32_t ybox[2] = {128u, (cuuint32_t)(BT / 2)};
@@ -413,7 +477,7 @@ void launch_ts_t(const NbitsArgs &a, const __half *a16, int64_t K8, int splits, 
   cfg.numAttrs = splits > 1 ? 2 : 1;
   B2M_CUDA(cudaLaunchKernelEx(&cfg, kern, tm, ty, use_ty, reinterpret_cast<const uint4 *>(a.w->tsq),
                               reinterpret_cast<const uint2 *>(a.w->tss), a.bias, a.Y, (int)a.M, (int)a.N,
-                              (int)(a.w->kp / 64), a.dev_err, pf));
+                              (int)(a.w->kp / 64), a.dev_err, pf, act, act16));
 }
 
 // Token-tile width. Per CTA: MMA time (a readiness check per stage caps the
@@ -490,19 +554,20 @@ int ts_splits(const NbitsArgs &a, int sms) {
 }
 
 template <int BT, int STAGES, int KSUB>
-void launch_ts_split(const NbitsArgs &a, const __half *a16, int64_t K8, int sms, cudaStream_t s) {
-  launch_ts_t<BT, STAGES, KSUB>(a, a16, K8, ts_splits<BT, STAGES, KSUB>(a, sms), s);
+void launch_ts_split(const NbitsArgs &a, const __half *a16, int64_t K8, int sms, cudaStream_t s, float *act,
+                     __half *act16) {
+  launch_ts_t<BT, STAGES, KSUB>(a, a16, K8, ts_splits<BT, STAGES, KSUB>(a, sms), s, act, act16);
 }
 
 }  // namespace
 
-void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s) {
+void launch_nbits_ts(const NbitsArgs &a, const __half *a16, int64_t K8, cudaStream_t s, float *act, __half *act16) {
   const int sms = device_sm_count();
   switch (nbits_ts_pick_bt(a.M, a.N, sms)) {
-    case 256: launch_ts_split<256, 3, 2>(a, a16, K8, sms, s); break;
-    case 192: launch_ts_split<192, 4, 2>(a, a16, K8, sms, s); break;
-    case 128: launch_ts_split<128, 3, 4>(a, a16, K8, sms, s); break;
-    case 64: launch_ts_split<64, 3, 4>(a, a16, K8, sms, s); break;
-    default: launch_ts_split<96, 3, 4>(a, a16, K8, sms, s); break;
+    case 256: launch_ts_split<256, 3, 2>(a, a16, K8, sms, s, act, act16); break;
+    case 192: launch_ts_split<192, 4, 2>(a, a16, K8, sms, s, act, act16); break;
+    case 128: launch_ts_split<128, 3, 4>(a, a16, K8, sms, s, act, act16); break;
+    case 64: launch_ts_split<64, 3, 4>(a, a16, K8, sms, s, act, act16); break;
+    default: launch_ts_split<96, 3, 4>(a, a16, K8, sms, s, act, act16); break;
   }
 }

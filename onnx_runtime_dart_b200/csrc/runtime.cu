@@ -1603,6 +1603,56 @@ B2M_API b2m_status b2m_matmul_nbits_f16_dev(b2m_ctx *ctx, const uint16_t *a16, i
   });
 }
 
+B2M_API b2m_status b2m_matmul_nbits_swiglu_dev(b2m_ctx *ctx, const float *a, const uint16_t *a16, int64_t m,
+                                               const b2m_weight *w, int32_t mode, float *act, uint16_t *act16) {
+  return guarded([&] {
+    check_ctx(ctx);
+    DeviceGuard dg(ctx->device);
+    B2M_REQUIRE(w && w->kind == W_NBITS, B2M_ERR_INVALID_ARGUMENT, "MatMulNBits: weight is not a MatMulNBits weight");
+    B2M_REQUIRE(mode == B2M_MODE_EXACT || mode == B2M_MODE_FAST || mode == B2M_MODE_PRECISE,
+                B2M_ERR_INVALID_ARGUMENT, "MatMulNBits SwiGLU: bad mode");
+    B2M_REQUIRE(w->n % 128 == 0, B2M_ERR_INVALID_ARGUMENT,
+                "MatMulNBits SwiGLU: N must be a multiple of 128 (tile-interleaved gate / up rows)");
+    auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    B2M_REQUIRE(m >= 0 && (m == 0 || ((a || a16) && (act || act16))) && al(act) && al(act16),
+                B2M_ERR_INVALID_ARGUMENT, "MatMulNBits SwiGLU: bad pointers (act / act16 16-byte aligned)");
+    check_cancel(ctx);
+    if (m == 0) return;
+    const int64_t I = w->n / 2;
+    OpTimer timer(ctx);
+    const bool tc = mode == B2M_MODE_FAST && nbits_route(w, m, mode) == B2M_ROUTE_TC_F16;
+    if (tc && (a16 ? (w->k % 8 == 0 && al(a16)) : true)) {
+      NbitsArgs p;
+      p.A = a;
+      p.w = &w->nb;
+      p.bias = nullptr;
+      p.Y = nullptr;
+      p.M = m;
+      p.K = w->k;
+      p.N = w->n;
+      p.dev_err = ctx->dev_err;
+      nbits_prefetch_plan(ctx, w, m, mode, p);
+      const int64_t K8 = nbits_tc_k8(w->k);
+      Scratch sc(ctx, a16 ? 0 : (size_t)(m * K8 * 2) + 256);
+      const __half *x16 = reinterpret_cast<const __half *>(a16);
+      if (!a16) {
+        __half *c16 = static_cast<__half *>(sc.take((size_t)(m * K8 * 2)));
+        b2m::launch_f32_to_f16(a, c16, m, w->k, K8, 0, ctx->stream);
+        x16 = c16;
+      }
+      launch_nbits_ts(p, x16, a16 ? w->k : K8, ctx->stream, act, reinterpret_cast<__half *>(act16));
+    } else {
+      B2M_REQUIRE(a, B2M_ERR_UNSUPPORTED, "MatMulNBits SwiGLU: this call's route takes fp32 activations (a is null)");
+      const size_t ybytes = (size_t)(m * w->n * 4);
+      Scratch sc(ctx, ybytes + 256 + nbits_scratch_bytes(w, m, mode));
+      float *y = static_cast<float *>(sc.take(ybytes));
+      nbits_run(ctx, sc, a, m, w, nullptr, mode, y);
+      launch_silu_mul_tiles(y, m, I, act, reinterpret_cast<__half *>(act16), ctx->stream);
+    }
+    timer.done();
+  });
+}
+
 B2M_API b2m_status b2m_matmul_nbits_host(b2m_ctx *ctx, const float *a_host, int64_t m, const b2m_weight *w,
                                          const float *bias_host, int32_t mode, float *y_host) {
   return guarded([&] {

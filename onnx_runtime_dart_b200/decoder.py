@@ -72,6 +72,14 @@ def random_nbits(rng, k: int, n: int, block: int):
     return bq, scales, zp
 
 
+def swiglu_row_order(inter: int) -> np.ndarray:
+    """Row order of a stacked [gate; up] weight (2 * inter rows) in the
+    tile-interleaved layout b2m_matmul_nbits_swiglu_dev takes: per 128-row
+    tile t, gate rows 64t .. 64t+63, then up rows 64t .. 64t+63."""
+    t = np.arange(inter // 64)[:, None] * 64 + np.arange(64)[None, :]
+    return np.concatenate([t, t + inter], axis=1).reshape(-1)
+
+
 def _ptr(t) -> ctypes.c_void_p:
     return ctypes.c_void_p(t.data_ptr())
 
@@ -82,7 +90,7 @@ class Int4Decoder:
 
     def __init__(self, ctx, cfg: DecoderConfig, batch: int, cap: int, max_prefill: int, seed: int = 0,
                  keep_host: bool = False, mode: int = N.MODE_FAST, fused: bool = True, session=None,
-                 producer_f16: bool = True, fold_qk_norm: bool = True):
+                 producer_f16: bool = True, fold_qk_norm: bool = True, swiglu_epilogue: bool = True):
         import torch
 
         if mode not in (N.MODE_FAST, N.MODE_PRECISE, N.MODE_EXACT):
@@ -113,6 +121,12 @@ class Int4Decoder:
         # normalises, rotates and appends inside the decode kernel: two
         # launches fewer per layer and step, the same results.
         self.fold_qk_norm = fold_qk_norm
+        # swiglu_epilogue (fused chains with random weights): the gate / up
+        # weight is packed with tile-interleaved rows and one call
+        # (b2m_matmul_nbits_swiglu_dev) writes silu(gate) * up, on the
+        # tensor-core route from the GEMM's epilogue: no gate / up rows in
+        # memory and no SiLU*Mul launch, the same results.
+        self.swiglu = bool(swiglu_epilogue and self.fused and session is None and cfg.inter % 64 == 0)
         self._routes = {}
         self.torch = torch
         self.ctx, self.cfg, self.B, self.cap = ctx, cfg, batch, cap
@@ -148,7 +162,8 @@ class Int4Decoder:
             self.up = torch.empty((t, c.inter), **f32)
         self.attn = torch.empty((t, c.heads * c.head_dim), **f32)
         self.o = torch.empty((t, c.hidden), **f32)
-        self.gu = torch.empty((t, 2 * c.inter), **f32)
+        if not self.swiglu:
+            self.gu = torch.empty((t, 2 * c.inter), **f32)
         self.act = torch.empty((t, c.inter), **f32)
         if self.fused and producer_f16:
             self.h16 = torch.empty((t, c.hidden), device=dev, dtype=torch.float16)
@@ -297,7 +312,11 @@ class Int4Decoder:
             for name, k, n in (("qkv", c.hidden, c.qkv_n), ("o", c.heads * c.head_dim, c.hidden),
                                ("gate_up", c.hidden, 2 * c.inter), ("down", c.inter, c.hidden)):
                 bq, sc, zp = random_nbits(rng, k, n, c.block)
-                if fused or name in ("o", "down"):
+                if name == "gate_up" and self.swiglu:
+                    r = swiglu_row_order(c.inter)
+                    lw[name] = ctx.prepack_nbits(np.ascontiguousarray(bq[r]), np.ascontiguousarray(sc[r]),
+                                                 np.ascontiguousarray(zp[r]), k, n, 4, c.block)
+                elif fused or name in ("o", "down"):
                     lw[name] = ctx.prepack_nbits(bq, sc, zp, k, n, 4, c.block)
                 else:
                     splits = ({"q": (0, c.heads * c.head_dim),
@@ -396,6 +415,14 @@ class Int4Decoder:
         else:
             N.check(lib.b2m_rmsnorm_dev(h, _ptr(x), skip, _ptr(gamma), _ptr(self.h), sum_out, T, c.hidden, c.eps))
 
+    def down_input(self, rows: int):
+        """fp32 view of the first `rows` rows the last call's down projection
+        read: its f16 operand widened where it took one, else the fp32 SiLU*Mul
+        output."""
+        if getattr(self, "_down_f16", False):
+            return self.act16[:rows].float()
+        return self.act[:rows]
+
     def _proj(self, w, T: int, f16: bool, x, x16, y):
         h = self.ctx.handle
         if f16:
@@ -415,6 +442,7 @@ class Int4Decoder:
             o16 = self.fused and self._f16_input(lw["o"], T)
             gu16 = self.fused and self._f16_input(lw["gate_up"], T)
             dn16 = self.fused and self._f16_input(lw["down"], T)
+            self._down_f16 = dn16
             if li == 0:
                 self._norm(self.res, None, lw["attn_norm"], None, T, qkv16)
             else:  # residual of the previous layer's MLP, then the attention norm
@@ -462,24 +490,29 @@ class Int4Decoder:
             else:
                 self._proj(lw["o"], T, o16, self.attn, getattr(self, "attn16", None), self.o)
             self._norm(self.o, _ptr(self.res), lw["mlp_norm"], _ptr(self.res), T, gu16)
-            if self.fused:
-                self._proj(lw["gate_up"], T, gu16, self.h, getattr(self, "h16", None), self.gu)
-                gp, up_, g_rs = self.gu.data_ptr(), self.gu.data_ptr() + c.inter * 4, 2 * c.inter
+            if self.swiglu:  # gate / up and SiLU*Mul in one call (tile-interleaved weight rows)
+                chk(lib.b2m_matmul_nbits_swiglu_dev(h, _ptr(self.h), _ptr(self.h16) if gu16 else None, T,
+                                                    lw["gate_up"].handle, self.mode, None if dn16 else _ptr(self.act),
+                                                    _ptr(self.act16) if dn16 else None))
             else:
-                for part in ("gate", "up"):
-                    if self.session is not None:
-                        self._dispatch_proj(part, lw, self.h, T, getattr(self, part))
-                    else:
-                        chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
-                                                     _ptr(getattr(self, part))))
-                gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
-            # the export's Sigmoid / Mul / Mul nodes as one op, then its down MatMulNBits
-            if dn16:
-                chk(lib.b2m_silu_mul_f16_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act),
-                                             _ptr(self.act16), T, c.inter))
-            else:
-                chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act), T,
-                                         c.inter))
+                if self.fused:
+                    self._proj(lw["gate_up"], T, gu16, self.h, getattr(self, "h16", None), self.gu)
+                    gp, up_, g_rs = self.gu.data_ptr(), self.gu.data_ptr() + c.inter * 4, 2 * c.inter
+                else:
+                    for part in ("gate", "up"):
+                        if self.session is not None:
+                            self._dispatch_proj(part, lw, self.h, T, getattr(self, part))
+                        else:
+                            chk(lib.b2m_matmul_nbits_dev(h, _ptr(self.h), T, lw[part].handle, None, self.mode,
+                                                         _ptr(getattr(self, part))))
+                    gp, up_, g_rs = self.gate.data_ptr(), self.up.data_ptr(), c.inter
+                # the export's Sigmoid / Mul / Mul nodes as one op, then its down MatMulNBits
+                if dn16:
+                    chk(lib.b2m_silu_mul_f16_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs,
+                                                 _ptr(self.act), _ptr(self.act16), T, c.inter))
+                else:
+                    chk(lib.b2m_silu_mul_dev(h, ctypes.c_void_p(gp), ctypes.c_void_p(up_), g_rs, g_rs, _ptr(self.act),
+                                             T, c.inter))
             if self.session is not None:
                 self._dispatch_proj("down", lw, self.act, T, self.down)
             else:

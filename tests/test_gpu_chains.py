@@ -120,7 +120,7 @@ def test_decoder_config5_fast_ops_within_contract_and_chain_bound(ctx, dec1):
     c = dec1.cfg
     last = c.layers - 1
     attn = dec1.attn[:PREFILL].cpu().numpy()
-    act = dec1.act[:PREFILL].cpu().numpy()  # the down projection's input (SiLU*Mul of the last layer)
+    act = dec1.down_input(PREFILL).cpu().numpy()  # the down projection's input (SiLU*Mul of the last layer)
     for x, name, y in ((attn, "o", dec1.o), (act, "down", dec1.down)):
         bq, sc, zp = dec1.host[(last, name)]
         want = oracle.matmul_nbits(x, bq, sc, zp, x.shape[1], bq.shape[0], c.block, nthreads=chain_refs.THREADS)
