@@ -656,12 +656,13 @@ __device__ __forceinline__ float4 rms_head4(float4 v, const float *__restrict__ 
                      (v.w - mean) * inv * gg.w + bb);
 }
 
-// rms_head4 for rows of D = 64 or 128 held by D / 4 consecutive lanes (two
-// rows per warp at D = 64), c the lane's float4 within its row. At D = 64 the
+// Sum of squares of a row of D = 64 or 128 values held as one float4 per
+// lane by D / 4 consecutive lanes (two rows per warp at D = 64), as
+// rms_head4 forms it; every lane of the row gets the sum. At D = 64 the
 // butterfly skips the step that would add the other half's zeros in
 // rms_head4, which changes no bit.
 template <int D>
-__device__ __forceinline__ float4 rms_row4(float4 v, const float *__restrict__ g, double eps, int c) {
+__device__ __forceinline__ float row_sumsq4(float4 v) {
   static_assert(D == 64 || D == 128, "rows of 16 or 32 lanes");
   const float mean = 0.f;
   const float a = v.x - mean, b = v.y - mean, cc = v.z - mean, d = v.w - mean;
@@ -669,9 +670,13 @@ __device__ __forceinline__ float4 rms_row4(float4 v, const float *__restrict__ g
   if (D == 128) t += __shfl_xor_sync(0xffffffffu, t, 16);
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-  const float inv = (float)(1.0 / sqrt((double)t / D + eps));
+  return t;
+}
+
+// rms_head4's output arithmetic for float4 c of a row with factor inv.
+__device__ __forceinline__ float4 rms_scale4(float4 v, float inv, const float *__restrict__ g, int c) {
+  const float mean = 0.f, bb = 0.f;
   const float4 gg = reinterpret_cast<const float4 *>(g)[c];
-  const float bb = 0.f;
   return make_float4((v.x - mean) * inv * gg.x + bb, (v.y - mean) * inv * gg.y + bb, (v.z - mean) * inv * gg.z + bb,
                      (v.w - mean) * inv * gg.w + bb);
 }
@@ -1535,12 +1540,39 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
       if (q0 + rr < a.S)
         qv[u] = *reinterpret_cast<const float4 *>(a.q + (int64_t)(b * a.S + q0 + rr) * a.q_rs + h * D + 4 * c);
     }
+    float inv[QI];
+    if (a.qk_gain) {
+      // The head's RMSNorm folded in. A warp holds eight rows over its items
+      // (one per item at D = 128, two at D = 64, half a warp each); lane l
+      // forms the double-precision factor of row l % 8 alone and the factors
+      // come back by shuffle: an eighth of the FP64 work of every lane
+      // forming every factor, the same bits.
+      static_assert(QI * 32 / (D / 4) == 8, "eight rows per warp");
+      float ts[QI];
+#pragma unroll
+      for (int u = 0; u < QI; u++) ts[u] = row_sumsq4<D>(qv[u]);
+      const int myrow = lane & 7;
+      float mine = 0.f;
+#pragma unroll
+      for (int u = 0; u < QI; u++) {
+        if (D == 128) {
+          if (myrow == u) mine = ts[u];
+        } else {
+          const float t0 = __shfl_sync(0xffffffffu, ts[u], 0), t1 = __shfl_sync(0xffffffffu, ts[u], 16);
+          if (myrow == 2 * u) mine = t0;
+          if (myrow == 2 * u + 1) mine = t1;
+        }
+      }
+      const float inv_l = (float)(1.0 / sqrt((double)mine / D + a.qk_eps));
+#pragma unroll
+      for (int u = 0; u < QI; u++) inv[u] = __shfl_sync(0xffffffffu, inv_l, D == 128 ? u : 2 * u + (lane >> 4));
+    }
 #pragma unroll
     for (int u = 0; u < QI; u++) {
       const int e = tid + 512 * u, rr = e / (D / 4), c = e % (D / 4);
       float4 v = qv[u];
-      if (a.qk_gain) {  // the head's RMSNorm folded in (rows of D / 4 lanes; padding rows stay zero)
-        const float4 o = rms_row4<D>(v, a.qk_gain + (int64_t)h * D, a.qk_eps, c);
+      if (a.qk_gain) {  // padding rows stay zero
+        const float4 o = rms_scale4(v, inv[u], a.qk_gain + (int64_t)h * D, c);
         if (q0 + rr < a.S) v = o;
       }
       v.x *= a.scale, v.y *= a.scale, v.z *= a.scale, v.w *= a.scale;
