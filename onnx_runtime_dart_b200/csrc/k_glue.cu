@@ -703,18 +703,41 @@ __global__ void __launch_bounds__(256) gqa_append_kernel(const GqaArgs a) {
   float *kv = kbuf[warp];
   const float *ksrc = a.k + (int64_t)(b * a.S + s) * a.kv_rs + kvh * a.D;
   const float *vsrc = a.v + (int64_t)(b * a.S + s) * a.kv_rs + kvh * a.D;
-  if (a.qk_gain) {
-    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (lane < (a.D >> 2)) x = *reinterpret_cast<const float4 *>(ksrc + 4 * lane);
-    const float4 o = rms_head4(x, a.qk_gain + (int64_t)(a.H + kvh) * a.D, a.D, a.qk_eps, lane);
-    if (lane < (a.D >> 2)) *reinterpret_cast<float4 *>(kv + 4 * lane) = o;
-  } else {
-    for (int d = lane; d < a.D; d += 32) kv[d] = ksrc[d];
+  const int64_t dst = (((int64_t)b * a.KVH + kvh) * a.CAP + pos) * a.D;
+  auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  const int d4 = a.D >> 2;
+  if ((a.D & 3) == 0 && (a.kv_rs & 3) == 0 && al(a.k) && al(a.v) && al(a.kcache) && al(a.vcache)) {
+    // float4 rows (D <= 256: at most two per lane); V's loads go out first.
+    float4 vv[2];
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+      if (lane + 32 * i < d4) vv[i] = reinterpret_cast<const float4 *>(vsrc)[lane + 32 * i];
+    if (a.qk_gain) {
+      float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (lane < d4) x = *reinterpret_cast<const float4 *>(ksrc + 4 * lane);
+      const float4 o = rms_head4(x, a.qk_gain + (int64_t)(a.H + kvh) * a.D, a.D, a.qk_eps, lane);
+      if (lane < d4) *reinterpret_cast<float4 *>(kv + 4 * lane) = o;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 2; i++)
+        if (lane + 32 * i < d4)
+          reinterpret_cast<float4 *>(kv)[lane + 32 * i] = reinterpret_cast<const float4 *>(ksrc)[lane + 32 * i];
+    }
+    __syncwarp();
+    if (a.cos) rotate_head(kv, a.cos, a.sin, pos, a.half, a.rot, a.interleaved, lane, 32);
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 2; i++)
+      if (lane + 32 * i < d4) {
+        reinterpret_cast<float4 *>(a.kcache + dst)[lane + 32 * i] = reinterpret_cast<const float4 *>(kv)[lane + 32 * i];
+        reinterpret_cast<float4 *>(a.vcache + dst)[lane + 32 * i] = vv[i];
+      }
+    return;
   }
+  for (int d = lane; d < a.D; d += 32) kv[d] = ksrc[d];  // (qk_gain is only set on the float4 layout)
   __syncwarp();
   if (a.cos) rotate_head(kv, a.cos, a.sin, pos, a.half, a.rot, a.interleaved, lane, 32);
   __syncwarp();
-  const int64_t dst = (((int64_t)b * a.KVH + kvh) * a.CAP + pos) * a.D;
   for (int d = lane; d < a.D; d += 32) {
     a.kcache[dst + d] = kv[d];
     a.vcache[dst + d] = vsrc[d];
@@ -2135,7 +2158,8 @@ void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, in
     // k in its prologue and appends; for the flash prefill kernel the append
     // kernel normalises k and the flash kernel q.
     auto al = [](const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-    const bool f4 = D % 4 == 0 && D <= 128 && q_rs % 4 == 0 && kv_rs % 4 == 0 && al(q) && al(k) && al(qk_gain);
+    const bool f4 = D % 4 == 0 && D <= 128 && q_rs % 4 == 0 && kv_rs % 4 == 0 && al(q) && al(k) && al(v) &&
+                    al(qk_gain);
     if (f4 && decode_shape(a)) {
       a.qk_gain = qk_gain;
       a.qk_eps = qk_eps;
