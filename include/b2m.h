@@ -346,7 +346,9 @@ B2M_API b2m_status b2m_rmsnorm_dev(b2m_ctx *ctx, const float *x, const float *sk
                                    float *sum_out, int64_t rows, int64_t d, double eps);
 
 /* b2m_rmsnorm_dev that also writes y as f16 (round to nearest) into y16
- * (rows x d, d % 8 == 0): the operand of b2m_matmul_nbits_f16_dev. */
+ * (rows x d, d % 8 == 0): the operand of b2m_matmul_nbits_f16_dev. y may be
+ * NULL when only the f16 rows are consumed (16-byte aligned operands; other
+ * layouts need y). */
 B2M_API b2m_status b2m_rmsnorm_f16_dev(b2m_ctx *ctx, const float *x, const float *skip, const float *gamma, float *y,
                                        float *sum_out, uint16_t *y16, int64_t rows, int64_t d, double eps);
 

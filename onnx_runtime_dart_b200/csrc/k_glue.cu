@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(256) norm_warp4_kernel(const float *x, const f
       const float4 bb = b4 ? b4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
       const float4 o = make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
                                    (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
-      reinterpret_cast<float4 *>(y + off)[j] = o;
+      if (y) reinterpret_cast<float4 *>(y + off)[j] = o;
       if (y16) store_f16x4(y16 + off + 4 * j, o);
       if (p0) store_split4(p0, p1, off + 4 * j, o);
     }
@@ -268,7 +268,7 @@ __global__ void __launch_bounds__(256) norm_row_cta_kernel(const float *x, const
       const float4 bb = b4 ? b4[j] : make_float4(0.f, 0.f, 0.f, 0.f);
       const float4 o = make_float4((v[i].x - mean) * inv * g.x + bb.x, (v[i].y - mean) * inv * g.y + bb.y,
                                    (v[i].z - mean) * inv * g.z + bb.z, (v[i].w - mean) * inv * g.w + bb.w);
-      reinterpret_cast<float4 *>(y + off)[j] = o;
+      if (y) reinterpret_cast<float4 *>(y + off)[j] = o;
       if (y16) store_f16x4(y16 + off + 4 * j, o);
       if (p0) store_split4(p0, p1, off + 4 * j, o);
     }
@@ -1921,6 +1921,8 @@ void launch_rmsnorm(const float *x, const float *skip, const float *gamma, float
   if (rows <= 0) return;
   if (launch_norm_rows_cta<false>(x, skip, gamma, nullptr, y, sum_out, rows, D, eps, per, gstride, gamma_rs, s, y16))
     return;
+  B2M_REQUIRE(y, B2M_ERR_INVALID_ARGUMENT,
+              "RMSNorm f16: y may be NULL only for rows of d % 4 == 0 floats with 16-byte aligned operands");
   if (y16) {  // the fallback kernels write fp32 only: round the rows after them
     launch_rmsnorm(x, skip, gamma, y, sum_out, rows, D, eps, per, gstride, s, gamma_rs, nullptr);
     b2m::launch_f32_to_f16(y, y16, rows, D, D, 0, s);

@@ -1707,7 +1707,7 @@ B2M_API b2m_status b2m_rmsnorm_f16_dev(b2m_ctx *ctx, const float *x, const float
                                        float *sum_out, uint16_t *y16, int64_t rows, int64_t d, double eps) {
   return guarded([&] {
     check_ctx(ctx);
-    B2M_REQUIRE(rows >= 0 && d > 0 && d % 8 == 0 && d <= (1 << 24) && (rows == 0 || (x && gamma && y && y16)),
+    B2M_REQUIRE(rows >= 0 && d > 0 && d % 8 == 0 && d <= (1 << 24) && (rows == 0 || (x && gamma && y16)),
                 B2M_ERR_INVALID_ARGUMENT, "RMSNorm f16: bad arguments");
     DeviceGuard dg(ctx->device);
     launch_rmsnorm(x, skip, gamma, y, sum_out, rows, (int)d, eps, std::max<int64_t>(rows, 1), 0, ctx->stream, 0,

@@ -409,8 +409,8 @@ class Int4Decoder:
 
     def _norm(self, x, skip, gamma, sum_out, T: int, f16: bool):
         c, lib, h = self.cfg, self.lib, self.ctx.handle
-        if f16:
-            N.check(lib.b2m_rmsnorm_f16_dev(h, _ptr(x), skip, _ptr(gamma), _ptr(self.h), sum_out, _ptr(self.h16), T,
+        if f16:  # the projection reads only the f16 rows: no fp32 copy
+            N.check(lib.b2m_rmsnorm_f16_dev(h, _ptr(x), skip, _ptr(gamma), None, sum_out, _ptr(self.h16), T,
                                             c.hidden, c.eps))
         else:
             N.check(lib.b2m_rmsnorm_dev(h, _ptr(x), skip, _ptr(gamma), _ptr(self.h), sum_out, T, c.hidden, c.eps))

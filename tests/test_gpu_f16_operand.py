@@ -99,6 +99,28 @@ def test_rmsnorm_f16_copy(ctx, rows, d, skip):
     assert torch.equal(y16, y_ref.half())
     if skip:
         assert torch.equal(sum_out, sum_ref)
+    # Only the f16 rows (the projection's operand): the same bits, the same sum.
+    y16b = torch.zeros((rows, d), device="cuda", dtype=torch.float16)
+    sum_b = torch.zeros((rows, d), device="cuda")
+    torch.cuda.synchronize()
+    N.check(lib.b2m_rmsnorm_f16_dev(h, _p(x), _p(s) if skip else None, _p(g), None, _p(sum_b) if skip else None,
+                                    _p(y16b), rows, d, 1e-6))
+    N.check(lib.b2m_synchronize(h))
+    assert torch.equal(y16b, y16)
+    if skip:
+        assert torch.equal(sum_b, sum_ref)
+
+
+def test_rmsnorm_f16_without_fp32_rows_needs_aligned_rows(ctx):
+    """y = NULL is refused where only the scalar kernel serves the layout."""
+    lib, h = ctx.lib, ctx.handle
+    x = torch.zeros((4, 1026), device="cuda")  # rows of 1024 from offset 2: 8-byte aligned only
+    g = torch.ones(1024, device="cuda")
+    y16 = torch.zeros((4, 1024), device="cuda", dtype=torch.float16)
+    torch.cuda.synchronize()
+    with pytest.raises(N.ArgumentError, match="y may be NULL only"):
+        N.check(lib.b2m_rmsnorm_f16_dev(h, ctypes.c_void_p(x.data_ptr() + 8), None, _p(g), None, None, _p(y16), 4,
+                                        1024, 1e-6))
 
 
 @pytest.mark.parametrize("rows,d", [(64, 3072), (2048, 3072)])
