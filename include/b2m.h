@@ -440,7 +440,9 @@ B2M_API b2m_status b2m_gqa_dev(b2m_ctx *ctx, const float *q, const float *k, con
 
 /* b2m_gqa_dev that also writes the attention output as f16 (round to
  * nearest) into out16 ([b*s][h*head_dim], h*head_dim % 8 == 0): the operand of
- * b2m_matmul_nbits_f16_dev for the output projection. */
+ * b2m_matmul_nbits_f16_dev for the output projection. out may be NULL when
+ * only the f16 copy is consumed: the decode and flash prefill kernels then
+ * skip the fp32 rows, other kernels write them to scratch. */
 B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k, const float *v, int64_t q_rs,
                                    int64_t kv_rs, float *k_cache, float *v_cache, const int32_t *past,
                                    const float *cos_cache, const float *sin_cache, int32_t rotary_half,
@@ -452,7 +454,7 @@ B2M_API b2m_status b2m_gqa_f16_dev(b2m_ctx *ctx, const float *q, const float *k,
  * head_dim values normalised with its gain row): qk_gain is [h + kvh][head_dim],
  * the gain rows of the h query heads, then those of the kvh key heads; eps the
  * norm's epsilon. out16: NULL, or the f16 copy of out as b2m_gqa_f16_dev
- * writes it. Results equal b2m_rmsnorm_head_rows_dev on q and k followed by
+ * writes it (with out16 given, out may be NULL as there). Results equal b2m_rmsnorm_head_rows_dev on q and k followed by
  * b2m_gqa_dev / b2m_gqa_f16_dev. A single-token call (s == 1) normalises
  * inside the decode attention kernel, which also appends the token's key and
  * value (one launch); other calls normalise q and k IN PLACE first, so both

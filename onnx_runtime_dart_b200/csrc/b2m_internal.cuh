@@ -397,6 +397,11 @@ void launch_argmax(const float *x, int64_t *out, int64_t rows, int64_t V, float 
 // CTAs per (kv head, sequence); split_part holds B*H*nsplit*(2 + D) floats
 // (null: no split).
 int gqa_decode_splits(int B, int S, int H, int KVH, int D, int CAP);
+// Whether launch_gqa (same arguments) writes out16 from the attention kernel
+// itself; then `out` may be null (only the f16 output is written).
+bool gqa_writes_f16(const float *q, int64_t q_rs, const float *kcache, const float *vcache, const int32_t *past,
+                    const float *cos, int rot, int B, int S, int H, int KVH, int D, int CAP, int nsplit, bool exact,
+                    bool counters);
 void launch_gqa(const float *q, const float *k, const float *v, int64_t q_rs, int64_t kv_rs, float *kcache,
                 float *vcache, const int32_t *past, const float *cos, const float *sin, int half, int rot,
                 int interleaved, float *out, int B, int S, int H, int KVH, int D, int CAP, float scale, int32_t *err,

@@ -1153,7 +1153,7 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
     const int h = kvh * G + g;
     if (nsplit == 1) {
       const float ov = O / L;
-      a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
+      if (a.out) a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
       if (a.out16) a.out16[(int64_t)b * (int64_t)a.H * D + h * D + d] = __float2half_rn(ov);
     } else {
       const int64_t slot = ((int64_t)b * a.H + h) * nsplit + sp;
@@ -1189,7 +1189,7 @@ __global__ void __launch_bounds__(256) gqa_decode_kernel(const GqaArgs a, float 
           O += __ldcg(po + (base + s2) * D + d) * f;
         }
           const float ov = O / L;
-        a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
+        if (a.out) a.out[(int64_t)b * (int64_t)a.H * D + h * D + d] = ov;
         if (a.out16) a.out16[(int64_t)b * (int64_t)a.H * D + h * D + d] = __float2half_rn(ov);
       }
       if (threadIdx.x == 0) counters[(int64_t)b * a.KVH + kvh] = 0u;
@@ -1888,11 +1888,10 @@ __global__ void __launch_bounds__(512, 1) fa_tc_kernel(const GqaArgs a) {
   if (ok && q0 + r < a.S) {
     const float inv = 1.f / l;
     const int64_t off = (int64_t)(b * a.S + q0 + r) * a.H * D + h * D + cb * DW;
-    float *dst = a.out + off;
 #pragma unroll
     for (int c = 0; c < DW; c += 4) {
       const float4 v4 = make_float4(o[c] * inv, o[c + 1] * inv, o[c + 2] * inv, o[c + 3] * inv);
-      *reinterpret_cast<float4 *>(dst + c) = v4;
+      if (a.out) *reinterpret_cast<float4 *>(a.out + off + c) = v4;
       if (a.out16) store_f16x4(a.out16 + off + c, v4);
     }
   }
@@ -2129,6 +2128,25 @@ static void launch_attend(const GqaArgs &a, float *split_part, int nsplit, bool 
     b2m::launch_f32_to_f16(a.out, a.out16, (int64_t)a.B * a.S, (int64_t)a.H * D, (int64_t)a.H * D, 0, s);
   if (a.p0 && !wrote_planes)
     ::launch_f32_split(a.out, (int64_t)a.H * D, a.p0, a.p1, (int64_t)a.B * a.S, (int64_t)a.H * D, (int64_t)a.H * D, s);
+}
+
+// Whether launch_gqa's attention kernel for these arguments writes the f16
+// output itself (the decode kernel when its key splits merge in the kernel,
+// the flash prefill kernel), so that the fp32 output may be omitted.
+bool gqa_writes_f16(const float *q, int64_t q_rs, const float *kcache, const float *vcache, const int32_t *past,
+                    const float *cos, int rot, int B, int S, int H, int KVH, int D, int CAP, int nsplit, bool exact,
+                    bool counters) {
+  GqaArgs a{q, nullptr, nullptr, q_rs, 0, const_cast<float *>(kcache), const_cast<float *>(vcache), past, cos,
+            nullptr, 0, rot, 0, nullptr, B, S, H, KVH, D, CAP, 1.f, nullptr};
+  a.kc_rs = D;
+  a.kc_hs = (int64_t)CAP * D;
+  a.kc_bs = (int64_t)KVH * CAP * D;
+  a.causal = 1;
+  a.kv_len = CAP;
+  a.mask = nullptr;
+  a.mask_bs = a.mask_hs = a.mask_qs = 0;
+  if (decode_shape(a)) return nsplit <= 1 || counters;
+  return !exact && fa_tc_shape(a);
 }
 
 // Key splits of the decode kernel: enough CTAs for two per SM, at least 128

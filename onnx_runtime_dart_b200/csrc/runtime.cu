@@ -1900,8 +1900,8 @@ static b2m_status gqa_impl(b2m_ctx *ctx, const float *q, const float *k, const f
                 B2M_ERR_INVALID_ARGUMENT, "GroupQueryAttention: bad shape arguments");
     B2M_REQUIRE(q_rs >= (int64_t)h * head_dim && kv_rs >= (int64_t)kvh * head_dim, B2M_ERR_INVALID_ARGUMENT,
                 "GroupQueryAttention: row strides too small");
-    B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && k_cache && v_cache && past && out), B2M_ERR_INVALID_ARGUMENT,
-                "GroupQueryAttention: null pointer");
+    B2M_REQUIRE((int64_t)b * s == 0 || (q && k && v && k_cache && v_cache && past && (out || out16)),
+                B2M_ERR_INVALID_ARGUMENT, "GroupQueryAttention: null pointer");
     B2M_REQUIRE(!out16 || ((int64_t)h * head_dim) % 8 == 0, B2M_ERR_INVALID_ARGUMENT,
                 "GroupQueryAttention f16: h * head_dim must be a multiple of 8");
     const bool rot = cos_cache != nullptr;
@@ -1913,8 +1913,6 @@ static b2m_status gqa_impl(b2m_ctx *ctx, const float *q, const float *k, const f
     const float sc = scale > 0.f ? scale : 1.f / std::sqrt((float)head_dim);
     const int nsplit = ctx->attn_exact ? 1 : gqa_decode_splits(b, s, h, kvh, head_dim, cap);
     float *part = nullptr;
-    Scratch scr(ctx, nsplit > 1 ? (size_t)b * h * nsplit * (2 + head_dim) * 4 + 256 : 0);
-    if (nsplit > 1) part = static_cast<float *>(scr.take((size_t)b * h * nsplit * (2 + head_dim) * 4));
     uint32_t *counters = nullptr;
     if (nsplit > 1 && (int64_t)b * kvh <= B2M_ATTN_COUNTERS) {
       if (!ctx->attn_counters) {
@@ -1929,6 +1927,16 @@ static b2m_status gqa_impl(b2m_ctx *ctx, const float *q, const float *k, const f
       }
       counters = ctx->attn_counters;
     }
+    // Without `out` (only the f16 copy wanted), kernels that form the f16
+    // output themselves skip the fp32 rows; the others write them to scratch.
+    const size_t out_bytes = (size_t)b * s * h * head_dim * 4;
+    const bool out_scratch =
+        !out && !gqa_writes_f16(q, q_rs, k_cache, v_cache, past, cos_cache, rotary_dim, b, s, h, kvh, head_dim, cap,
+                                nsplit, ctx->attn_exact, counters != nullptr);
+    const size_t part_bytes = nsplit > 1 ? (size_t)b * h * nsplit * (2 + head_dim) * 4 : 0;
+    Scratch scr(ctx, (part_bytes || out_scratch) ? part_bytes + (out_scratch ? out_bytes : 0) + 512 : 0);
+    if (nsplit > 1) part = static_cast<float *>(scr.take(part_bytes));
+    if (out_scratch) out = static_cast<float *>(scr.take(out_bytes));
     launch_gqa(q, k, v, q_rs, kv_rs, k_cache, v_cache, past, cos_cache, sin_cache, rotary_half, rotary_dim,
                interleaved ? 1 : 0, out, b, s, h, kvh, head_dim, cap, sc, ctx->dev_err, part, nsplit,
                ctx->attn_exact, counters, ctx->stream, reinterpret_cast<__half *>(out16), qk_gain, qk_eps);

@@ -415,6 +415,14 @@ class Int4Decoder:
         else:
             N.check(lib.b2m_rmsnorm_dev(h, _ptr(x), skip, _ptr(gamma), _ptr(self.h), sum_out, T, c.hidden, c.eps))
 
+    def o_input(self, rows: int):
+        """fp32 view of the first `rows` rows the last call's o projection read
+        (the attention output, widened from its f16 copy where only that was
+        written)."""
+        if getattr(self, "_o_f16", False):
+            return self.attn16[:rows].float()
+        return self.attn[:rows]
+
     def down_input(self, rows: int):
         """fp32 view of the first `rows` rows the last call's down projection
         read: its f16 operand widened where it took one, else the fp32 SiLU*Mul
@@ -443,6 +451,9 @@ class Int4Decoder:
             gu16 = self.fused and self._f16_input(lw["gate_up"], T)
             dn16 = self.fused and self._f16_input(lw["down"], T)
             self._down_f16 = dn16
+            # (with the folded head norms the attention writes only the o
+            # projection's f16 operand when that is what it reads)
+            self._o_f16 = o16 and self.fold_qk_norm
             if li == 0:
                 self._norm(self.res, None, lw["attn_norm"], None, T, qkv16)
             else:  # residual of the previous layer's MLP, then the attention norm
@@ -464,8 +475,9 @@ class Int4Decoder:
                 chk(lib.b2m_gqa_qknorm_dev(h, ctypes.c_void_p(qp), ctypes.c_void_p(kp), ctypes.c_void_p(vp), q_rs,
                                            kv_rs, _ptr(lw["qk_gain"]), c.eps, _ptr(self.kcache[li]),
                                            _ptr(self.vcache[li]), _ptr(self.past), _ptr(self.cos), _ptr(self.sin),
-                                           D // 2, D, 0, _ptr(self.attn), _ptr(self.attn16) if o16 else None, self.B,
-                                           seq, c.heads, c.kv_heads, D, self.cap, 0.0))
+                                           D // 2, D, 0, None if o16 else _ptr(self.attn),
+                                           _ptr(self.attn16) if o16 else None, self.B, seq, c.heads, c.kv_heads, D,
+                                           self.cap, 0.0))
             else:
                 if self.fused:  # q and k heads are adjacent in the packed rows: one launch
                     chk(lib.b2m_rmsnorm_head_rows_dev(h, ctypes.c_void_p(qp), _ptr(lw["qk_gain"]), ctypes.c_void_p(qp),

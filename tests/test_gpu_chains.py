@@ -119,7 +119,7 @@ def test_decoder_config5_fast_ops_within_contract_and_chain_bound(ctx, dec1):
     torch.cuda.synchronize()
     c = dec1.cfg
     last = c.layers - 1
-    attn = dec1.attn[:PREFILL].cpu().numpy()
+    attn = dec1.o_input(PREFILL).cpu().numpy()  # the o projection's input (the last layer's attention)
     act = dec1.down_input(PREFILL).cpu().numpy()  # the down projection's input (SiLU*Mul of the last layer)
     for x, name, y in ((attn, "o", dec1.o), (act, "down", dec1.down)):
         bq, sc, zp = dec1.host[(last, name)]

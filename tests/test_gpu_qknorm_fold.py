@@ -139,6 +139,41 @@ def test_prefill_fold_same_bits(ctx, b, s, D, packed):
         assert torch.equal(r, g)
 
 
+@pytest.mark.parametrize("b,s,D", [(64, 1, 128), (3, 1, 128), (4, 40, 128), (2, 9, 96)])
+def test_fold_f16_only_output(ctx, b, s, D):
+    """out = NULL with out16 given: the f16 output and the caches are the
+    same bits as with the fp32 output requested (the decode kernel with and
+    without key splits and the flash prefill skip the fp32 rows; at head_dim
+    96 the CUDA-core kernel writes them to scratch first)."""
+    rng = np.random.default_rng(b * 100 + s)
+    lib, h = ctx.lib, ctx.handle
+    H, KVH, cap = 16, 8, 256
+    T = b * s
+    rs = (H + 2 * KVH) * D
+    rows0 = torch.from_numpy((3 * rng.standard_normal((T, rs))).astype(np.float32)).cuda()
+    gain = torch.from_numpy((1 + 0.2 * rng.standard_normal((H + KVH, D))).astype(np.float32)).cuda()
+    cache0 = torch.from_numpy(rng.standard_normal((b, KVH, cap, D)).astype(np.float32)).cuda()
+    cos, sin = _rope(cap, D)
+    pasts = rng.integers(0, cap - s, b).tolist()
+    res = []
+    for with_out in (True, False):
+        rows = rows0.clone()
+        base = rows.data_ptr()
+        kc, vc = cache0.clone(), cache0.clone()
+        past = torch.tensor(pasts, dtype=torch.int32, device="cuda")
+        out = torch.empty((T, H * D), device="cuda")
+        out16 = torch.zeros((T, H * D), device="cuda", dtype=torch.float16)
+        torch.cuda.synchronize()
+        N.check(lib.b2m_gqa_qknorm_dev(h, _vp(base), _vp(base + H * D * 4), _vp(base + (H + KVH) * D * 4), rs, rs,
+                                       _p(gain), 1e-6, _p(kc), _p(vc), _p(past), _p(cos), _p(sin), D // 2, D, 0,
+                                       _p(out) if with_out else None, _p(out16), b, s, H, KVH, D, cap,
+                                       ctypes.c_float(0.0)))
+        N.check(lib.b2m_synchronize(h))
+        res.append((out16, kc, vc))
+    for r, g in zip(res[0], res[1]):
+        assert torch.equal(r, g)
+
+
 def test_decode_fold_cache_full(ctx):
     """A sequence whose cache is full reports the capacity error, as the
     separate append kernel does, and leaves the cache alone."""
