@@ -157,3 +157,36 @@ def test_conv_spatial_attributes_are_length_checked():
     with pytest.raises(N.ArgumentError, match="rank"):
         ops._check_conv_rank(np.zeros((1, 4, 5)), pw, 3, 5)
     assert ops.AUTO_PAD == {"NOTSET": 0, "SAME_UPPER": 1, "SAME_LOWER": 2, "VALID": 3}
+
+
+def test_swiglu_row_order_is_the_tile_interleave():
+    """The gate / up row order b2m_matmul_nbits_swiglu_dev takes: per 128-row
+    tile t, gate rows 64t .. 64t+63, then the matching up rows."""
+    from onnx_runtime_dart_b200.decoder import swiglu_row_order
+
+    inter = 3072
+    r = swiglu_row_order(inter)
+    assert sorted(r.tolist()) == list(range(2 * inter))
+    t = r.reshape(inter // 64, 2, 64)
+    base = np.arange(inter // 64)[:, None] * 64 + np.arange(64)[None, :]
+    np.testing.assert_array_equal(t[:, 0, :], base)
+    np.testing.assert_array_equal(t[:, 1, :], base + inter)
+
+
+def test_fused_entries_reject_bad_arguments_without_a_device(lib):
+    """The fused attention and SwiGLU entries validate before touching a
+    device: a null context, a null gain table, a negative epsilon."""
+    from onnx_runtime_dart_b200 import _native
+
+    bad = _native.B2M_ERR_INVALID_ARGUMENT
+    assert lib.b2m_matmul_nbits_swiglu_dev(None, None, None, 4, None, 1, None, None) == bad
+
+    def qknorm(gain, eps, b, s):  # a null context and null buffers; h 16, kvh 8, head_dim 128, cap 64
+        return lib.b2m_gqa_qknorm_dev(None, None, None, None, 0, 0, gain, eps, None, None, None, None, None, 0, 0, 0,
+                                      None, None, b, s, 16, 8, 128, 64, ctypes.c_float(0.0))
+    assert qknorm(None, 1e-6, 1, 1) == bad
+    assert b"qk_gain" in lib.b2m_last_error()
+    g = np.ones((24, 128), np.float32)
+    assert qknorm(g.ctypes.data_as(ctypes.c_void_p), -1.0, 1, 1) == bad
+    assert b"eps" in lib.b2m_last_error()
+    assert qknorm(None, 1e-6, 0, 0) == bad  # nothing to do, but the context is still checked
