@@ -419,7 +419,9 @@ def run_decoder(ctx, torch, stream, global_batch, prefill_len=512, steps=128, la
     ms_p, ms_d = e0.elapsed_time(e1), e1.elapsed_time(e2)
     ok = bool(((gen >= 0) & (gen < cfg.vocab)).all().item())
     out = {"batch_per_gpu": batch, "prefill_len": prefill_len, "decode_steps": steps, "layers": cfg.layers,
-           "projections": "fused q/k/v and gate/up" if fused else "separate (the exported graph's seven per layer)",
+           "projections": ("fused q/k/v and gate/up (SwiGLU in the gate/up epilogue; q/k head norms, rotary and "
+                           "cache append in the attention)" if fused
+                           else "separate (the exported graph's seven per layer)"),
            "prefill_ms": round(ms_p, 3), "decode_ms": round(ms_d, 3),
            "prefill_tokens_per_s": round(batch * prefill_len / (ms_p / 1e3), 1),
            "decode_tokens_per_s": round(batch * steps / (ms_d / 1e3), 1),
