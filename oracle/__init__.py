@@ -85,6 +85,8 @@ def _load():
     lib.orc_conv_transpose_f32.argtypes = [_f32p, _i64p, ctypes.c_int, _f32p, _i64p, _i64, _i64, _f32p, _i64p,
                                            _i64p, _i64p, _i64p, _i64p, _f32p, _i64p]
     lib.orc_conv_transpose_f32.restype = ctypes.c_int
+    lib.orc_conv_winograd_f2x2.argtypes = [_f32p, _i64, _i64, _i64, _i64, _f32p, _i64, _f32p, _i64, _f32p]
+    lib.orc_conv_winograd_f2x2.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -278,6 +280,48 @@ def resolve_pads(in_sp, kernel, strides, dilations, auto_pad="NOTSET", pads=None
             p[nd + k] = 0 if pads is None else int(pads[nd + k])
             out[k] = (in_sp[k] + p[k] + p[nd + k] - window) // strides[k] + 1
     return p, out
+
+
+def conv_winograd_eligible(w_shape, in_shape, strides=None, pads=None, dilations=None, group=1,
+                           auto_pad="NOTSET", min_out_pixels=1024):
+    """``convWinogradEligible`` (lib/src/onnx_nn_ops.dart:779-812): whether the
+    executor takes opConv's Winograd F(2x2, 3x3) branch for an initializer
+    weight of this shape (the executor also requires the weight to be an
+    initializer, onnx_graph.dart:2450-2454)."""
+    if group != 1 or len(w_shape) != 4 or len(in_shape) != 4:
+        return False
+    if w_shape[2] != 3 or w_shape[3] != 3:
+        return False
+    if auto_pad != "NOTSET" or pads is None or len(pads) != 4:
+        return False
+    if not (all(v == 0 for v in pads) or all(v == 1 for v in pads)):
+        return False
+    s = list(strides) if strides is not None else [1, 1]
+    d = list(dilations) if dilations is not None else [1, 1]
+    if len(s) != 2 or len(d) != 2 or s != [1, 1] or d != [1, 1]:
+        return False
+    _, osp = resolve_pads(list(in_shape[2:]), [3, 3], s, d, auto_pad, list(pads))
+    return osp[0] * osp[1] >= min_out_pixels
+
+
+def conv_winograd_f32(x, w, bias=None, pad=1):
+    """opConv's Winograd F(2x2, 3x3) branch (lib/src/onnx_nn_ops.dart:271-293
+    with pretransformWinogradF2x2 :584-628 and _convWinogradF2x2 :630-748), a
+    standalone call: x [N, C, H, W], w [M, C, 3, 3], pads all `pad` (0 or 1),
+    stride and dilation 1."""
+    x = _c(x, np.float32)
+    w = _c(w, np.float32)
+    bias = _c(bias, np.float32)
+    n, c, h, wd = x.shape
+    m = w.shape[0]
+    if w.shape != (m, c, 3, 3):
+        raise ValueError("oracle winograd conv: weight must be [M, C, 3, 3]")
+    out = np.zeros((n, m, h + 2 * pad - 2, wd + 2 * pad - 2), np.float32)
+    rc = _load().orc_conv_winograd_f2x2(_p(x, _f32p), n, c, h, wd, _p(w, _f32p), m, _p(bias, _f32p), int(pad),
+                                        _p(out, _f32p))
+    if rc:
+        raise ValueError(f"oracle winograd conv: bad arguments ({rc})")
+    return out
 
 
 def conv_f32(x, w, bias=None, strides=None, pads=None, dilations=None, group=1, auto_pad="NOTSET"):

@@ -13,6 +13,8 @@
  *   - opMatMulInteger         lib/src/onnx_qlinear_ops.dart:32-81
  *   - opQLinearMatMul         lib/src/onnx_qlinear_ops.dart:85-108 (+ _roundEven :19-26)
  *   - opMatMulNBits           lib/src/onnx_qlinear_ops.dart:115-228
+ *   - opConv (im2col, depthwise, 3-D and the Winograd F(2x2,3x3) branch),
+ *     ConvInteger / QLinearConv, ConvTranspose, DynamicQuantizeLinear
  *
  * Numerics. Dart's Float32x4 lanes multiply and add with separate float32
  * rounding (SSE mulps/addps, no FMA), and scalar Dart `double` code rounds in
@@ -654,6 +656,132 @@ ORC_API int orc_conv_f32(const float *x, const int64_t *xshape, int nd, const fl
       }
     }
   }
+  return 0;
+}
+
+/* ------------------------------------------------------------------------- */
+/* Conv, Winograd F(2x2, 3x3) branch (lib/src/onnx_nn_ops.dart:271-293,       */
+/* 584-786)                                                                   */
+/* ------------------------------------------------------------------------- */
+
+/*
+ * The executor takes this branch for an initializer weight [M, C, 3, 3],
+ * group 1, stride 1, dilation 1, symmetric pads all 0 or all 1, with at least
+ * 1024 output pixels (convWinogradEligible :779-812, onnx_graph.dart:2450).
+ * A standalone call (no isolate pool band), with its arithmetic:
+ *   - weights (pretransformWinogradF2x2 :584-628): U[y*4+x][om*C+ic] =
+ *     f32(sum over ky, kx of (g[y][ky] * w) * g[x][kx]) in double, ky outer;
+ *   - tile rows in bands of max(1, (16 << 20) / (16 (C + M) tw)) rows, tw =
+ *     ceil(outW / 2) (:652-660); per band the input rows go into a zeroed
+ *     padded buffer of rows*2 + 2 rows by tw*2 + 2 columns, padLeft in;
+ *   - input transform (:683-704) in double from the float inputs, each of the
+ *     16 planes stored as float: V = Bᵀ d B with the row pass first;
+ *   - 16 products: matmulKernel(U[q] [M x C], V[q] [C x band tiles]);
+ *   - output transform (:717-746) in double from the float products, the row
+ *     pass first (a0 + a1 + a2, a1 - a2 - a3), then the column pass plus the
+ *     bias in double, one float rounding per output.
+ * Returns 0, or a negative code for shapes the branch does not take.
+ */
+ORC_API int orc_conv_winograd_f2x2(const float *x, int64_t n, int64_t c, int64_t in_h, int64_t in_w,
+                                   const float *w, int64_t m, const float *bias, int64_t pad, float *out) {
+  if (pad != 0 && pad != 1) return -1;
+  const int64_t out_h = in_h + 2 * pad - 2, out_w = in_w + 2 * pad - 2;
+  if (out_h < 1 || out_w < 1 || n < 1 || c < 1 || m < 1) return -2;
+  static const double g[4][3] = {{1, 0, 0}, {0.5, 0.5, 0.5}, {0.5, -0.5, 0.5}, {0, 0, 1}};
+  float *u = (float *)malloc(sizeof(float) * (size_t)(16 * m * c));
+  for (int64_t om = 0; om < m; om++)
+    for (int64_t ic = 0; ic < c; ic++) {
+      const float *wk = w + (om * c + ic) * 9;
+      for (int y = 0; y < 4; y++)
+        for (int xx = 0; xx < 4; xx++) {
+          double sum = 0;
+          for (int ky = 0; ky < 3; ky++)
+            for (int kx = 0; kx < 3; kx++) sum += g[y][ky] * (double)wk[ky * 3 + kx] * g[xx][kx];
+          u[(size_t)(y * 4 + xx) * (size_t)(m * c) + (size_t)(om * c + ic)] = (float)sum;
+        }
+    }
+  const int64_t tw = (out_w + 1) >> 1, gy1 = (out_h + 1) >> 1;
+  int64_t band_rows = ((int64_t)16 << 20) / (16 * (c + m) * tw);
+  if (band_rows < 1) band_rows = 1;
+  if (band_rows > gy1) band_rows = gy1;
+  const int64_t pw = tw * 2 + 2;
+  const int64_t max_tiles = band_rows * tw;
+  float *padded = (float *)malloc(sizeof(float) * (size_t)(c * (band_rows * 2 + 2) * pw));
+  float *v = (float *)malloc(sizeof(float) * (size_t)(16 * c * max_tiles));
+  float *prod = (float *)malloc(sizeof(float) * (size_t)(16 * m * max_tiles));
+  double tmp[16];
+  for (int64_t b = 0; b < n; b++) {
+    for (int64_t cy0 = 0; cy0 < gy1; cy0 += band_rows) {
+      const int64_t rows = cy0 + band_rows <= gy1 ? band_rows : gy1 - cy0;
+      const int64_t tiles = rows * tw, pad_rows = rows * 2 + 2;
+      memset(padded, 0, sizeof(float) * (size_t)(c * pad_rows * pw));
+      const int64_t row0 = cy0 * 2 - pad;
+      for (int64_t ic = 0; ic < c; ic++)
+        for (int64_t py = 0; py < pad_rows; py++) {
+          const int64_t yy = row0 + py;
+          if (yy < 0 || yy >= in_h) continue;
+          memcpy(padded + (ic * pad_rows + py) * pw + pad, x + ((b * c + ic) * in_h + yy) * in_w,
+                 sizeof(float) * (size_t)in_w);
+        }
+      for (int64_t ic = 0; ic < c; ic++)
+        for (int64_t ty = 0; ty < rows; ty++)
+          for (int64_t tx = 0; tx < tw; tx++) {
+            for (int r = 0; r < 4; r++) {
+              const float *d = padded + (ic * pad_rows + ty * 2 + r) * pw + tx * 2;
+              const double d0 = d[0], d1 = d[1], d2 = d[2], d3 = d[3];
+              tmp[r * 4 + 0] = d0 - d2;
+              tmp[r * 4 + 1] = d1 + d2;
+              tmp[r * 4 + 2] = -d1 + d2;
+              tmp[r * 4 + 3] = d1 - d3;
+            }
+            const int64_t tile = ty * tw + tx;
+            for (int col = 0; col < 4; col++) {
+              const double a0 = tmp[col], a1 = tmp[4 + col], a2 = tmp[8 + col], a3 = tmp[12 + col];
+              v[(size_t)col * (size_t)(c * tiles) + (size_t)(ic * tiles + tile)] = (float)(a0 - a2);
+              v[(size_t)(4 + col) * (size_t)(c * tiles) + (size_t)(ic * tiles + tile)] = (float)(a1 + a2);
+              v[(size_t)(8 + col) * (size_t)(c * tiles) + (size_t)(ic * tiles + tile)] = (float)(-a1 + a2);
+              v[(size_t)(12 + col) * (size_t)(c * tiles) + (size_t)(ic * tiles + tile)] = (float)(a1 - a3);
+            }
+          }
+      for (int q = 0; q < 16; q++) {
+        const float *uq = u + (size_t)q * (size_t)(m * c);
+        const float *vq = v + (size_t)q * (size_t)(c * tiles);
+        float *pq = prod + (size_t)q * (size_t)(m * tiles);
+        for (int64_t j = 0; j < tiles; j++) gemm_column(uq, c, vq, tiles, pq, tiles, m, c, tiles, j);
+      }
+      for (int64_t om = 0; om < m; om++) {
+        float *ob = out + (b * m + om) * out_h * out_w;
+        const double bias0 = bias ? (double)bias[om] : 0.0;
+        for (int64_t ty = 0; ty < rows; ty++) {
+          const int64_t oy = (cy0 + ty) * 2;
+          for (int64_t tx = 0; tx < tw; tx++) {
+            const int64_t tile = ty * tw + tx;
+            for (int col = 0; col < 4; col++) {
+              const double a0 = prod[(size_t)col * (size_t)(m * tiles) + (size_t)(om * tiles + tile)];
+              const double a1 = prod[(size_t)(4 + col) * (size_t)(m * tiles) + (size_t)(om * tiles + tile)];
+              const double a2 = prod[(size_t)(8 + col) * (size_t)(m * tiles) + (size_t)(om * tiles + tile)];
+              const double a3 = prod[(size_t)(12 + col) * (size_t)(m * tiles) + (size_t)(om * tiles + tile)];
+              tmp[col] = a0 + a1 + a2;
+              tmp[4 + col] = a1 - a2 - a3;
+            }
+            const int64_t ox = tx * 2;
+            if (oy < out_h) {
+              if (ox < out_w) ob[oy * out_w + ox] = (float)(tmp[0] + tmp[1] + tmp[2] + bias0);
+              if (ox + 1 < out_w) ob[oy * out_w + ox + 1] = (float)(tmp[1] - tmp[2] - tmp[3] + bias0);
+            }
+            if (oy + 1 < out_h) {
+              if (ox < out_w) ob[(oy + 1) * out_w + ox] = (float)(tmp[4] + tmp[5] + tmp[6] + bias0);
+              if (ox + 1 < out_w) ob[(oy + 1) * out_w + ox + 1] = (float)(tmp[5] - tmp[6] - tmp[7] + bias0);
+            }
+          }
+        }
+      }
+    }
+  }
+  free(u);
+  free(padded);
+  free(v);
+  free(prod);
   return 0;
 }
 

@@ -309,3 +309,63 @@ def test_conv_transpose_oracle_vs_float64(cfg):
     want = _conv_transpose_f64(x, w, b, s, p, d, op, grp)
     assert got.shape == want.shape
     assert np.max(np.abs(got - want)) <= 1e-5 * max(1.0, np.max(np.abs(want)))
+
+
+# --- opConv's Winograd F(2x2, 3x3) branch -----------------------------------
+
+def _conv3x3_f64(x, w, b, pad):
+    x, w = x.astype(np.float64), w.astype(np.float64)
+    oh, ow = x.shape[2] + 2 * pad - 2, x.shape[3] + 2 * pad - 2
+    xp = np.pad(x, ((0, 0), (0, 0), (pad, pad), (pad, pad)))
+    out = np.zeros((x.shape[0], w.shape[0], oh, ow))
+    for ky in range(3):
+        for kx in range(3):
+            out += np.einsum("nchw,mc->nmhw", xp[:, :, ky:ky + oh, kx:kx + ow], w[:, :, ky, kx])
+    return out + (0 if b is None else b.astype(np.float64)[None, :, None, None])
+
+
+@pytest.mark.parametrize("case,pad", [("conv2d_basic", 0), ("conv2d_bias", 0), ("conv2d_pads", 1)])
+def test_winograd_restatement_matches_eligible_shaped_fixtures(case, pad):
+    """The reference's 3x3 stride-1 group-1 fixtures with all-0 / all-1 pads
+    (the branch's shapes; the executor itself takes it from 1024 output
+    pixels on) through the Winograd restatement, at the fixture tolerance."""
+    g = load_golden(case)
+    x = g["arrays"]
+    got = oracle.conv_winograd_f32(x[0], x[1], x[2] if len(x) > 2 else None, pad=pad)
+    assert_fixture_close(got, g["expected_arrays"][g["outputs"][0]], case + " (Winograd)")
+
+
+@pytest.mark.parametrize("n,c,h,w,m,pad", [
+    (2, 16, 34, 34, 8, 1),      # one band
+    (1, 3, 40, 33, 2, 0),       # two output channels: double tail columns in the products
+    (1, 1024, 256, 16, 4, 1),   # two bands of tile rows (127 + 1)
+    (1, 1024, 230, 18, 2, 1),   # two bands with tail columns of different widths
+])
+def test_winograd_restatement_against_float64(n, c, h, w, m, pad):
+    """Eligible shapes, banding included, against a float64 convolution at
+    the fixture tolerance; the im2col restatement (what the device EXACT
+    kernels reproduce) meets the same bound, so the two branches differ by
+    float32 rounding only."""
+    rng = np.random.default_rng(c + h)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((m, c, 3, 3)) / np.sqrt(9 * c)).astype(np.float32)
+    b = rng.standard_normal(m).astype(np.float32)
+    assert oracle.conv_winograd_eligible(wt.shape, x.shape, pads=[pad] * 4)
+    ref = _conv3x3_f64(x, wt, b, pad)
+    assert_fixture_close(oracle.conv_winograd_f32(x, wt, b, pad=pad), ref, "Winograd vs float64")
+    assert_fixture_close(oracle.conv_f32(x, wt, b, pads=[pad] * 4), ref, "im2col vs float64")
+
+
+def test_winograd_eligibility_mirrors_the_reference():
+    """convWinogradEligible (lib/src/onnx_nn_ops.dart:779-812)."""
+    e = oracle.conv_winograd_eligible
+    assert e((8, 4, 3, 3), (1, 4, 32, 32), pads=[1, 1, 1, 1])          # 32 x 32 = 1024 outputs
+    assert not e((8, 4, 3, 3), (1, 4, 31, 32), pads=[1, 1, 1, 1])      # 992
+    assert e((8, 4, 3, 3), (1, 4, 34, 34), pads=[0, 0, 0, 0])
+    assert not e((8, 4, 3, 3), (1, 4, 64, 64), pads=[1, 0, 1, 0])      # mixed pads
+    assert not e((8, 4, 3, 3), (1, 4, 64, 64), pads=None)              # pads must be given
+    assert not e((8, 4, 3, 3), (1, 4, 64, 64), pads=[1] * 4, strides=[2, 2])
+    assert not e((8, 4, 3, 3), (1, 4, 64, 64), pads=[1] * 4, dilations=[2, 2])
+    assert not e((8, 2, 3, 3), (1, 4, 64, 64), pads=[1] * 4, group=2)
+    assert not e((8, 4, 5, 5), (1, 4, 64, 64), pads=[1] * 4)
+    assert not e((8, 4, 3, 3), (1, 4, 64, 64), pads=[1] * 4, auto_pad="SAME_UPPER")
